@@ -1,0 +1,247 @@
+"""Generate the golden fixtures in tests/golden/*.npz by running the REFERENCE
+implementation (Carbo-hub/Clifford-Space-Network, mounted read-only at
+/root/reference) in float64 on seeded inputs.
+
+Run in the development container only (the reference does not exist on the GPU
+machines):
+
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py
+
+Each fixture stores the inputs, the reference outputs and the reference
+gradients of loss = sum(W * out) for a seeded weight W (so dOut = W).  Reference
+functions called (paths relative to the reference root):
+
+* python/clifford_scan.py:41  parallel_rotor_scan (two-sided tree, and one-sided tree)
+* csn_toolkit/csn/scan.py:96  parallel_rotor_scan(backend="pytorch") -> CliffordScanFunction
+* python/clifford_cl6.py:57   cayley_rotor_8x8
+* python/clifford_cl8.py:29   cayley_rotor_16x16(use_schulz=False), :65 cayley_rotor_4x4
+* csn_toolkit/csn/rotors.py:54-115 cayley_rotor_* (transposed convention)
+* python/clifford_cl6.py:150-171 the block's scan section, composed from the calls above
+* python/clifford_layer.py:14 CliffordTENNCell
+* python/clifford_cl6.py:71 CliffordCL6Block, python/clifford_cl8.py:92 CliffordCL8Block
+"""
+from __future__ import annotations
+
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+REF = Path("/root/reference")
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parent.parent
+sys.path.insert(0, str(REF))
+sys.path.insert(0, str(REF / "csn_toolkit"))
+sys.dont_write_bytecode = True
+
+from python.clifford_scan import parallel_rotor_scan as ref_tree_scan  # noqa: E402
+from python.clifford_cl6 import cayley_rotor_8x8, CliffordCL6Block  # noqa: E402
+from python.clifford_cl8 import cayley_rotor_16x16, cayley_rotor_4x4, CliffordCL8Block  # noqa: E402
+from python.clifford_layer import CliffordTENNCell  # noqa: E402
+import csn.scan as ref_csn_scan  # noqa: E402
+import csn.rotors as ref_csn_rotors  # noqa: E402
+
+import importlib.util  # noqa: E402
+
+# rho tables (the blade data format) are loaded straight from their file so that this
+# build's own `python`/`csn` drop-in packages never shadow the reference's on sys.path.
+_spec = importlib.util.spec_from_file_location(
+    "csn_algebra", REPO / "clifford-space-network_b200" / "csn_b200" / "algebra.py")
+algebra = importlib.util.module_from_spec(_spec)
+sys.modules["csn_algebra"] = algebra
+_spec.loader.exec_module(algebra)
+
+torch.set_default_dtype(torch.float64)
+F64 = torch.float64
+
+
+def t(a):
+    return torch.as_tensor(np.asarray(a), dtype=F64)
+
+
+def save(name, **arrays):
+    out = {}
+    for k, v in arrays.items():
+        if v is None:  # autograd leaves .grad None for an unused input (M_0 when T == 1)
+            like = arrays[k[1:]] if k.startswith("d") and k[1:] in arrays else None
+            v = torch.zeros_like(like) if like is not None else np.zeros(0)
+        out[k] = v.detach().cpu().numpy() if torch.is_tensor(v) else np.asarray(v)
+    np.savez_compressed(HERE / f"{name}.npz", **out)
+    print(f"  {name}.npz  " + ", ".join(f"{k}{tuple(v.shape)}" for k, v in out.items()))
+
+
+def random_transitions(rng, B, T, N, D, spread=0.05):
+    """Contractive, non-orthogonal transition matrices: s * Cayley(skew) + noise."""
+    A = rng.standard_normal((B, T, N, D, D)) * 0.4
+    skew = 0.5 * (A - np.swapaxes(A, -1, -2))
+    eye = np.eye(D)
+    Q = np.linalg.solve(eye - skew, eye + skew)
+    s = rng.uniform(0.6, 1.0, size=(B, T, N, 1, 1))
+    return s * Q + spread * rng.standard_normal((B, T, N, D, D))
+
+
+def scans(rng):
+    for D, shape in ((4, (2, 37, 3)), (8, (2, 23, 2)), (16, (1, 19, 2))):
+        for (B, T, N) in (shape, (1, 1, 2)):
+            M = t(random_transitions(rng, B, T, N, D)).requires_grad_(True)
+            C = t(rng.standard_normal((B, T, N, D, D))).requires_grad_(True)
+            W = t(rng.standard_normal((B, T, N, D, D)))
+            # two-sided tree (python/clifford_scan.py:41, default is_spinor_bundle=False)
+            X = ref_tree_scan(M, C)
+            (X * W).sum().backward()
+            save(f"scan_two_d{D}_T{T}", M=M, C=C, W=W, X=X, dM=M.grad, dC=C.grad)
+            # one-sided: csn sequential analytic adjoint and the python tree
+            M1 = M.detach().clone().requires_grad_(True)
+            C1 = C.detach().clone().requires_grad_(True)
+            X1 = ref_csn_scan.parallel_rotor_scan(M1, C1, backend="pytorch")
+            (X1 * W).sum().backward()
+            M2 = M.detach().clone().requires_grad_(True)
+            C2 = C.detach().clone().requires_grad_(True)
+            X2 = ref_tree_scan(M2, C2, is_spinor_bundle=True)
+            (X2 * W).sum().backward()
+            save(f"scan_one_d{D}_T{T}", M=M1, C=C1, W=W, X=X1, dM=M1.grad, dC=C1.grad,
+                 X_tree=X2, dM_tree=M2.grad if M2.grad is not None else torch.zeros_like(M2), dC_tree=C2.grad)
+
+
+def cayleys(rng):
+    fns = {4: lambda o: cayley_rotor_4x4(o, use_schulz=False),
+           8: cayley_rotor_8x8,
+           16: lambda o: cayley_rotor_16x16(o, use_schulz=False)}
+    csn_fns = {4: ref_csn_rotors.cayley_rotor_4x4, 8: ref_csn_rotors.cayley_rotor_8x8,
+               16: ref_csn_rotors.cayley_rotor_16x16}
+    for D, fn in fns.items():
+        A = rng.standard_normal((2, 4, D, D)) * 0.7
+        Om = t(0.5 * (A - np.swapaxes(A, -1, -2))).requires_grad_(True)
+        W = t(rng.standard_normal((2, 4, D, D)))
+        Q = fn(Om)
+        (Q * W).sum().backward()
+        Qc = csn_fns[D](Om.detach(), use_schulz=False)
+        save(f"cayley_d{D}", Om=Om, W=W, Q=Q, dOm=Om.grad, Q_csn_transposed=Qc)
+
+
+def rotor_section(gens, dt, gamma, S, basis, D, spinor=False):
+    """python/clifford_cl6.py:150-171 (and python/clifford_cl8.py:160-179) with the
+    projections already applied: gens = biv_proj(x) * omega_scale, dt = time_head(x),
+    gamma = softplus(gamma_proj(x))."""
+    B, T, N = S.shape[:3]
+    dt5 = dt.view(B, T, 1, 1, 1)
+    if basis is None:
+        u, v = torch.triu_indices(D, D, offset=1)
+        skew = torch.zeros(B, T, N, D, D)
+        skew[..., u, v] = gens
+        skew[..., v, u] = -gens
+    else:
+        skew = torch.einsum("btnk,kij->btnij", gens, t(basis))
+    Omega = skew * (0.5 * dt5)
+    if D == 8:
+        Q = cayley_rotor_8x8(Omega)
+    elif D == 16:
+        Q = cayley_rotor_16x16(Omega, use_schulz=False)
+    else:
+        Q = cayley_rotor_4x4(Omega, use_schulz=False)
+    if gamma is not None:
+        decay = torch.sigmoid(-gamma.view(B, T, N, 1, 1) * dt5)
+        M = torch.sqrt(decay) * Q
+        C = (1.0 - decay) * S
+    else:
+        M, C = Q, S
+    return ref_tree_scan(M, C, is_spinor_bundle=spinor)
+
+
+def rotor_scans(rng):
+    cases = [
+        ("rotor_d8_damped", 8, None, True, False, (2, 21, 3), 1.0),
+        ("rotor_d8_undamped", 8, None, False, False, (2, 21, 3), 1.0),
+        ("rotor_d4_damped", 4, None, True, False, (2, 21, 3), 1.0),
+        ("rotor_d16_damped", 16, None, True, False, (1, 13, 2), 1.0),
+        ("rotor_d16_spinor", 16, None, True, True, (1, 13, 2), 1.0),
+        ("rotor_cl8ga_undamped", 16, algebra.bivector_basis(algebra.CL8), False, False, (1, 13, 2), 1.0),
+        ("rotor_cl8ga_damped", 16, algebra.bivector_basis(algebra.CL8), True, False, (1, 13, 2), 1.0),
+    ]
+    for name, D, basis, damped, spinor, (B, T, N), _ in cases:
+        K = D * (D - 1) // 2 if basis is None else basis.shape[0]
+        # block-like magnitudes: omega_scale 10, biv ~ N(0, 1) -> g ~ N(0, 10^2)
+        gens = t(rng.standard_normal((B, T, N, K)) * 10.0).requires_grad_(True)
+        dt = t(rng.uniform(0.01, 0.1, size=(B, T))).requires_grad_(True)
+        gamma = t(np.log1p(np.exp(rng.standard_normal((B, T, N))))).requires_grad_(True) if damped else None
+        S = t(rng.standard_normal((B, T, N, D, D))).requires_grad_(True)
+        W = t(rng.standard_normal((B, T, N, D, D)))
+        X = rotor_section(gens, dt, gamma, S, basis, D, spinor=spinor)
+        (X * W).sum().backward()
+        extra = {"basis": basis if basis is not None else algebra.triu_basis(D)}
+        if damped:
+            extra.update(gamma=gamma, dgamma=gamma.grad)
+        save(name, gens=gens, dt=dt, S=S, W=W, X=X, dgens=gens.grad, ddt=dt.grad, dS=S.grad,
+             spinor=np.array(spinor), **extra)
+
+
+def ga3(rng):
+    """Cl(3,0) recurrence h_t = R_t h_{t-1} R~_t + x_t, evaluated by the reference's
+    two-sided matrix scan on rho-embedded 4x4 matrices (the reference has no Cl(3) code)."""
+    rep = algebra.real_rep(algebra.CL3)
+    E = t(algebra.bivector_basis(algebra.CL3))
+    for name, gscale in (("ga3_config1", 0.1), ("ga3_large", 8.0)):
+        B, T, N = 2, 40, 3
+        gens = t(rng.standard_normal((B, T, N, 3)) * gscale).requires_grad_(True)
+        dt = t(rng.uniform(0.01, 0.1, size=(B, T))).requires_grad_(True)
+        x = t(rng.standard_normal((B, T, N, 8))).requires_grad_(True)
+        W = t(rng.standard_normal((B, T, N, 8)))
+        Om = torch.einsum("btnk,kij->btnij", gens, E) * (0.5 * dt.view(B, T, 1, 1, 1))
+        M = cayley_rotor_4x4(Om, use_schulz=False)
+        C = torch.einsum("btni,ijk->btnjk", x, t(rep))
+        X = ref_tree_scan(M, C)
+        h = torch.einsum("btnjk,ijk->btni", X, t(rep)) / 4.0
+        (h * W).sum().backward()
+        save(name, gens=gens, dt=dt, x=x, W=W, h=h, dgens=gens.grad, ddt=dt.grad, dx=x.grad)
+
+
+def cells(rng):
+    for name, (Bt, N, in_dim, dt) in (("cell_a", (3, 5, 4, 0.02)), ("cell_b", (2, 8, 3, 0.3))):
+        torch.manual_seed(int(rng.integers(1 << 30)))
+        cell = CliffordTENNCell(num_neurons=N, in_dim=in_dim).double()
+        with torch.no_grad():
+            cell.gamma_bias.copy_(t(rng.standard_normal(N) * 0.5))
+            cell.W_rec.mul_(20.0)  # larger than init so the rotation is not negligible
+        x = t(rng.standard_normal((Bt, in_dim))).requires_grad_(True)
+        prev = t(rng.standard_normal((Bt, N, 16))).requires_grad_(True)
+        W = t(rng.standard_normal((Bt, N, 16)))
+        out, nxt = cell(x, prev, dt=dt)
+        (out * W).sum().backward()
+        save(name, x=x, prev=prev, W_rec=cell.W_rec, W_in=cell.W_in, gamma_bias=cell.gamma_bias,
+             dt=np.array(dt), W=W, out=out, dx=x.grad, dprev=prev.grad, dW_rec=cell.W_rec.grad,
+             dW_in=cell.W_in.grad, dgamma_bias=cell.gamma_bias.grad)
+
+
+def blocks(rng):
+    for name, cls, kw, (B, T, d_model) in (
+        ("cl6_block", CliffordCL6Block, dict(num_neurons=4), (2, 24, 32)),
+        ("cl8_block", CliffordCL8Block, dict(num_neurons=2, use_schulz=False), (2, 12, 32)),
+    ):
+        torch.manual_seed(int(rng.integers(1 << 30)))
+        blk = cls(d_model=d_model, **kw).double()
+        with torch.no_grad():  # non-trivial time head so dt varies per token
+            blk.time_head.proj.weight.normal_(0.0, 0.1)
+        x = t(rng.standard_normal((B, T, d_model))).requires_grad_(True)
+        W = t(rng.standard_normal((B, T, d_model)))
+        out, Omega, dt = blk(x)
+        (out * W).sum().backward()
+        sd = {f"param.{k}": v for k, v in blk.state_dict().items()}
+        grads = {f"grad.{k}": p.grad for k, p in blk.named_parameters()}
+        save(name, x=x, W=W, out=out, Omega=Omega, dt=dt, dx=x.grad, **sd, **grads)
+
+
+def main():
+    os.environ.setdefault("PYTHONDONTWRITEBYTECODE", "1")
+    rng = np.random.default_rng(20260101)
+    print("scans");  scans(rng)
+    print("cayley"); cayleys(rng)
+    print("rotor");  rotor_scans(rng)
+    print("ga3");    ga3(rng)
+    print("cells");  cells(rng)
+    print("blocks"); blocks(rng)
+
+
+if __name__ == "__main__":
+    main()

@@ -310,18 +310,21 @@ def emit_header(path: Path) -> str:
                 assert len(nzc) == 1, "rho(bivector) must be a signed permutation"
                 cols[k, u] = nzc[0]
                 sgns[k, u] = int(E[k, u, nzc[0]])
-        lines.append(f"// rho(bivector_k) of {tag} as signed permutations: row u has its one")
-        lines.append(f"// nonzero at column {tag}_BIV_COL[k][u] with sign {tag}_BIV_SGN[k][u].")
+        lines.append(f"// rho(bivector_k) of {tag} as signed permutations: row u of rho(bivector_k)")
+        lines.append("// has its one nonzero at column col[k][u] with sign sgn[k][u].  Use as a local")
+        lines.append(f"// `constexpr auto t = {tag.lower()}_biv_tab();` so the tables fold into device code.")
         lines.append(f"#define CSN_{tag}_NBIV {K}")
         lines.append(f"#define CSN_{tag}_REPD {D}")
-        lines.append(f"static constexpr unsigned char {tag}_BIV_COL[{K}][{D}] = {{")
+        lines.append(f"struct {tag.capitalize()}BivTab {{ unsigned char col[{K}][{D}]; signed char sgn[{K}][{D}]; }};")
+        lines.append(f"__host__ __device__ constexpr {tag.capitalize()}BivTab {tag.lower()}_biv_tab() {{")
+        lines.append(f"  return {tag.capitalize()}BivTab{{{{")
         for k in range(K):
-            lines.append("  {" + ", ".join(str(int(c)) for c in cols[k]) + "},")
-        lines.append("};")
-        lines.append(f"static constexpr signed char {tag}_BIV_SGN[{K}][{D}] = {{")
+            lines.append("    {" + ", ".join(str(int(c)) for c in cols[k]) + "},")
+        lines.append("  }, {")
         for k in range(K):
-            lines.append("  {" + ", ".join(str(int(s)) for s in sgns[k]) + "},")
-        lines.append("};")
+            lines.append("    {" + ", ".join(str(int(x)) for x in sgns[k]) + "},")
+        lines.append("  }};")
+        lines.append("}")
         lines.append("")
     lines += ["}  // namespace csn", ""]
     text = "\n".join(lines)

@@ -1,0 +1,199 @@
+"""PyTorch front end of the CUDA rotor-scan library (autograd + shape handling).
+
+Every op runs on the current CUDA stream through the C ABI (``_lib``).  Inputs
+must be CUDA tensors; there is no CPU path and no silent fallback.  Computation
+is float32: float64/float16/bfloat16 inputs are computed in float32 and the
+result is returned in the input dtype.
+
+Ops (reference functions they replace, paths relative to the reference root):
+
+* :func:`rotor_scan`        -- python/clifford_scan.py:41 parallel_rotor_scan (two-sided),
+                               csn_toolkit/csn/scan.py:16-72 CliffordScanFunction (one-sided)
+* :func:`fused_rotor_scan`  -- python/clifford_cl6.py:150-171 / python/clifford_cl8.py:160-179
+                               (Cayley rotor + decay + scan in one pass)
+* :func:`cayley`            -- python/clifford_cl6.py:57, python/clifford_cl8.py:29,65
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+__all__ = ["rotor_scan", "fused_rotor_scan", "cayley", "BASIS"]
+
+BASIS = {"triu": 0, "ga": 1}
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+
+
+def _stream(device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _require_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("csn_b200 ops need CUDA tensors: the library has no CPU path")
+
+
+def _f32(t):
+    """Contiguous float32 copy (or the tensor itself when it already is one), 16-byte aligned."""
+    if t is None:
+        return None
+    t = t.detach()
+    if t.dtype != torch.float32:
+        t = t.float()
+    t = t.contiguous()
+    if t.data_ptr() % 16:
+        t = t.clone()
+    return t
+
+
+def _workspace(nbytes, device):
+    return torch.empty(int(nbytes), dtype=torch.uint8, device=device)
+
+
+# --------------------------------------------------------------------- plain scan
+def _scan_fwd(M, C, h0, two_sided):
+    B, T, N, D, _ = M.shape
+    X = torch.empty_like(C)
+    ws_bytes = _lib.load().csn_scan_workspace_bytes(B, T, N, D)
+    ws = _workspace(ws_bytes, M.device)
+    _lib.call("csn_scan_fwd", _ptr(M), _ptr(C), _ptr(h0), _ptr(X), B, T, N, D, int(two_sided),
+              _ptr(ws), ws_bytes, _stream(M.device))
+    return X
+
+
+def _scan_bwd(M, X, dX, h0, two_sided, need_dh0):
+    B, T, N, D, _ = M.shape
+    dM = torch.empty_like(M)
+    dC = torch.empty_like(M)
+    dh0 = torch.empty_like(h0) if (need_dh0 and h0 is not None) else None
+    ws_bytes = _lib.load().csn_scan_workspace_bytes(B, T, N, D)
+    ws = _workspace(ws_bytes, M.device)
+    _lib.call("csn_scan_bwd", _ptr(M), _ptr(X), _ptr(dX), _ptr(h0), _ptr(dM), _ptr(dC), _ptr(dh0),
+              B, T, N, D, int(two_sided), _ptr(ws), ws_bytes, _stream(M.device))
+    return dM, dC, dh0
+
+
+class ScanFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, M, C, h0, two_sided):
+        _require_cuda(M, C, h0)
+        Mf, Cf, hf = _f32(M), _f32(C), _f32(h0)
+        X = _scan_fwd(Mf, Cf, hf, two_sided)
+        ctx.save_for_backward(Mf, X, hf)
+        ctx.two_sided = two_sided
+        ctx.dtypes = (M.dtype, C.dtype, None if h0 is None else h0.dtype)
+        return X.to(C.dtype)
+
+    @staticmethod
+    def backward(ctx, dX):
+        Mf, X, hf = ctx.saved_tensors
+        dM, dC, dh0 = _scan_bwd(Mf, X, _f32(dX), hf, ctx.two_sided, ctx.needs_input_grad[2])
+        dM = dM.to(ctx.dtypes[0])
+        dC = dC.to(ctx.dtypes[1])
+        if dh0 is not None:
+            dh0 = dh0.to(ctx.dtypes[2])
+        return dM, dC, dh0, None
+
+
+def rotor_scan(M, C, two_sided: bool = True, h0=None):
+    """Inclusive scan X_t = M_t X_{t-1} M_t^T + C_t (two-sided) or M_t X_{t-1} + C_t.
+
+    M, C: [B, T, N, D, D] with D in {4, 8, 16}; h0: optional [B, N, D, D] (X_{-1}).
+    """
+    if M.dim() != 5 or C.shape != M.shape or M.shape[-1] != M.shape[-2]:
+        raise ValueError(f"rotor_scan expects M, C of shape [B, T, N, D, D], got {tuple(M.shape)}, "
+                         f"{tuple(C.shape)}")
+    return ScanFunction.apply(M, C, h0, bool(two_sided))
+
+
+# ---------------------------------------------------------------- fused rotor scan
+class RotorScanFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, gens, dt, gamma, S, h0, basis, two_sided):
+        _require_cuda(gens, dt, gamma, S, h0)
+        g, d, ga, s, hf = _f32(gens), _f32(dt), _f32(gamma), _f32(S), _f32(h0)
+        B, T, N, D, _ = s.shape
+        X = torch.empty_like(s)
+        lib = _lib.load()
+        ws_bytes = lib.csn_rotor_scan_workspace_bytes(B, T, N, D)
+        ws = _workspace(ws_bytes, s.device)
+        _lib.call("csn_rotor_scan_fwd", _ptr(g), _ptr(d), _ptr(ga), _ptr(s), _ptr(hf), _ptr(X),
+                  B, T, N, D, basis, int(two_sided), _ptr(ws), ws_bytes, _stream(s.device))
+        ctx.save_for_backward(g, d, ga, s, hf, X)
+        ctx.basis, ctx.two_sided = basis, two_sided
+        ctx.dtypes = tuple(None if t is None else t.dtype for t in (gens, dt, gamma, S, h0))
+        return X.to(S.dtype)
+
+    @staticmethod
+    def backward(ctx, dX):
+        g, d, ga, s, hf, X = ctx.saved_tensors
+        B, T, N, D, _ = s.shape
+        dXf = _f32(dX)
+        dg = torch.empty_like(g)
+        ddt = torch.empty_like(d)
+        dga = torch.empty_like(ga) if ga is not None else None
+        dS = torch.empty_like(s)
+        dh0 = torch.empty_like(hf) if (hf is not None and ctx.needs_input_grad[4]) else None
+        lib = _lib.load()
+        ws_bytes = lib.csn_rotor_scan_workspace_bytes(B, T, N, D)
+        ws = _workspace(ws_bytes, s.device)
+        _lib.call("csn_rotor_scan_bwd", _ptr(g), _ptr(d), _ptr(ga), _ptr(s), _ptr(hf), _ptr(X),
+                  _ptr(dXf), _ptr(dg), _ptr(ddt), _ptr(dga), _ptr(dS), _ptr(dh0), B, T, N, D,
+                  ctx.basis, int(ctx.two_sided), _ptr(ws), ws_bytes, _stream(s.device))
+        outs = [dg, ddt, dga, dS, dh0]
+        outs = [None if o is None else o.to(dt_) for o, dt_ in zip(outs, ctx.dtypes)]
+        return outs[0], outs[1], outs[2], outs[3], outs[4], None, None
+
+
+def fused_rotor_scan(gens, dt, gamma, S, basis: str = "triu", two_sided: bool = True, h0=None):
+    """Cayley rotor + decay + scan in one pass (M and C are never materialised).
+
+    gens [B, T, N, K], dt [B, T] (or [B, T, 1, 1, 1]), gamma [B, T, N] (post-softplus;
+    None = undamped, M = Q and C = S), S [B, T, N, D, D].  ``basis`` "triu" is the
+    reference generator layout (K = D(D-1)/2); "ga" takes GA bivector blades (Cl(3,0)
+    for D = 4, Cl(8,0) for D = 16).
+    """
+    if S.dim() != 5:
+        raise ValueError("S must be [B, T, N, D, D]")
+    B, T, N, D, _ = S.shape
+    dt = dt.reshape(B, T)
+    if gamma is not None:
+        gamma = gamma.reshape(B, T, N)
+    if basis not in BASIS:
+        raise ValueError(f"basis must be one of {sorted(BASIS)}")
+    return RotorScanFunction.apply(gens, dt, gamma, S, h0, BASIS[basis], bool(two_sided))
+
+
+# ------------------------------------------------------------------------ Cayley
+class CayleyFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, Om):
+        _require_cuda(Om)
+        O = _f32(Om)
+        D = O.shape[-1]
+        Q = torch.empty_like(O)
+        _lib.call("csn_cayley_fwd", _ptr(O), _ptr(Q), O.numel() // (D * D), D, _stream(O.device))
+        ctx.save_for_backward(Q)
+        ctx.dtype = Om.dtype
+        return Q.to(Om.dtype)
+
+    @staticmethod
+    def backward(ctx, dQ):
+        (Q,) = ctx.saved_tensors
+        D = Q.shape[-1]
+        dO = torch.empty_like(Q)
+        _lib.call("csn_cayley_bwd", _ptr(Q), _ptr(_f32(dQ)), _ptr(dO), Q.numel() // (D * D), D,
+                  _stream(Q.device))
+        return dO.to(ctx.dtype)
+
+
+def cayley(Omega):
+    """Q = (I - Omega)^{-1} (I + Omega) for skew Omega[..., D, D], D in {4, 8, 16}."""
+    return CayleyFunction.apply(Omega)

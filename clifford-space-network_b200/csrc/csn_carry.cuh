@@ -1,0 +1,187 @@
+// csn_carry.cuh -- per-sequence carry propagation between time chunks, shared by
+// the D = 4/8 and D = 16 scan families.
+#pragma once
+
+#include "csn_common.cuh"
+#include "csn_scan_args.cuh"
+
+namespace csn {
+
+// ------------------------------------------------------------ forward: carry
+// One warp per sequence; lane l owns D*D/32 entries (D = 8: 2, D = 16: 8) of the
+// running carry.  D = 4 uses one thread per sequence.
+template <int D, bool TWO>
+__global__ void __launch_bounds__(128) fwd_carry_kernel(ScanArgs a) {
+  const int64_t S = a.B * a.N;
+  if constexpr (D == 4) {
+    const int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (s >= S) return;
+    Mat<4> h, P;
+    if (a.h0) load_mat(h, a.h0 + s * 16); else mat_zero(h);
+    store_mat(a.carry + (s * a.nchunks) * 16, h);
+    for (int64_t j = 0; j + 1 < a.nchunks; ++j) {
+      load_mat(P, a.aggP + (s * a.nchunks + j) * 16);
+      lmul(P, h);
+      if constexpr (TWO) rmulT(h, P);
+      add_scaled_mat(h, a.aggC + (s * a.nchunks + j) * 16, 1.0f);
+      store_mat(a.carry + (s * a.nchunks + j + 1) * 16, h);
+    }
+  } else {
+    constexpr int DD = D * D;
+    constexpr int PER = DD / 32;
+    __shared__ float sh_h[4][DD];
+    __shared__ float sh_P[4][DD];
+    __shared__ float sh_y[4][DD];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t s = blockIdx.x * 4 + w;
+    if (s >= S) return;  // whole warp exits together
+    float* h = sh_h[w];
+    float* P = sh_P[w];
+    float* y = sh_y[w];
+#pragma unroll
+    for (int q = 0; q < PER; ++q) {
+      const int idx = lane + 32 * q;
+      h[idx] = a.h0 ? a.h0[s * DD + idx] : 0.0f;
+      a.carry[(s * a.nchunks) * DD + idx] = h[idx];
+    }
+    __syncwarp();
+    for (int64_t j = 0; j + 1 < a.nchunks; ++j) {
+      const float* Pg = a.aggP + (s * a.nchunks + j) * DD;
+      const float* cg = a.aggC + (s * a.nchunks + j) * DD;
+      float cv[PER];
+#pragma unroll
+      for (int q = 0; q < PER; ++q) {
+        P[lane + 32 * q] = Pg[lane + 32 * q];
+        cv[q] = cg[lane + 32 * q];
+      }
+      __syncwarp();
+      // y = P h
+#pragma unroll
+      for (int q = 0; q < PER; ++q) {
+        const int idx = lane + 32 * q, i = idx / D, jj = idx % D;
+        float acc = 0.0f;
+#pragma unroll
+        for (int k = 0; k < D; ++k) acc = fmaf(P[i * D + k], h[k * D + jj], acc);
+        y[idx] = acc;
+      }
+      __syncwarp();
+      float nv[PER];
+#pragma unroll
+      for (int q = 0; q < PER; ++q) {
+        const int idx = lane + 32 * q, i = idx / D, l = idx % D;
+        float acc;
+        if constexpr (TWO) {
+          acc = 0.0f;
+#pragma unroll
+          for (int k = 0; k < D; ++k) acc = fmaf(y[i * D + k], P[l * D + k], acc);
+        } else {
+          acc = y[idx];
+        }
+        nv[q] = acc + cv[q];
+      }
+      __syncwarp();
+#pragma unroll
+      for (int q = 0; q < PER; ++q) {
+        const int idx = lane + 32 * q;
+        h[idx] = nv[q];
+        a.carry[(s * a.nchunks + j + 1) * DD + idx] = nv[q];
+      }
+      __syncwarp();
+    }
+  }
+}
+
+// ------------------------------------------------------------ backward: carry
+// H_{nchunks-1} = 0;  H_{j-1} = P_j^T H_j P_j + c'_j  (one-sided: P_j^T H_j + c'_j)
+template <int D, bool TWO>
+__global__ void __launch_bounds__(128) bwd_carry_kernel(ScanArgs a) {
+  const int64_t S = a.B * a.N;
+  if constexpr (D == 4) {
+    const int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (s >= S) return;
+    Mat<4> H, P;
+    mat_zero(H);
+    store_mat(a.carry + (s * a.nchunks + a.nchunks - 1) * 16, H);
+    for (int64_t j = a.nchunks - 1; j >= 1; --j) {
+      load_mat(P, a.aggP + (s * a.nchunks + j) * 16);
+      lmulT(P, H);
+      if constexpr (TWO) rmul(H, P);
+      add_scaled_mat(H, a.aggC + (s * a.nchunks + j) * 16, 1.0f);
+      store_mat(a.carry + (s * a.nchunks + j - 1) * 16, H);
+    }
+  } else {
+    constexpr int DD = D * D;
+    constexpr int PER = DD / 32;
+    __shared__ float sh_h[4][DD];
+    __shared__ float sh_P[4][DD];
+    __shared__ float sh_y[4][DD];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t s = blockIdx.x * 4 + w;
+    if (s >= S) return;
+    float* h = sh_h[w];
+    float* P = sh_P[w];
+    float* y = sh_y[w];
+#pragma unroll
+    for (int q = 0; q < PER; ++q) {
+      const int idx = lane + 32 * q;
+      h[idx] = 0.0f;
+      a.carry[(s * a.nchunks + a.nchunks - 1) * DD + idx] = 0.0f;
+    }
+    __syncwarp();
+    for (int64_t j = a.nchunks - 1; j >= 1; --j) {
+      const float* Pg = a.aggP + (s * a.nchunks + j) * DD;
+      const float* cg = a.aggC + (s * a.nchunks + j) * DD;
+      float cv[PER];
+#pragma unroll
+      for (int q = 0; q < PER; ++q) {
+        P[lane + 32 * q] = Pg[lane + 32 * q];
+        cv[q] = cg[lane + 32 * q];
+      }
+      __syncwarp();
+      // y = P^T h
+#pragma unroll
+      for (int q = 0; q < PER; ++q) {
+        const int idx = lane + 32 * q, i = idx / D, jj = idx % D;
+        float acc = 0.0f;
+#pragma unroll
+        for (int k = 0; k < D; ++k) acc = fmaf(P[k * D + i], h[k * D + jj], acc);
+        y[idx] = acc;
+      }
+      __syncwarp();
+      float nv[PER];
+#pragma unroll
+      for (int q = 0; q < PER; ++q) {
+        const int idx = lane + 32 * q, i = idx / D, l = idx % D;
+        float acc;
+        if constexpr (TWO) {  // (P^T h) P
+          acc = 0.0f;
+#pragma unroll
+          for (int k = 0; k < D; ++k) acc = fmaf(y[i * D + k], P[k * D + l], acc);
+        } else {
+          acc = y[idx];
+        }
+        nv[q] = acc + cv[q];
+      }
+      __syncwarp();
+#pragma unroll
+      for (int q = 0; q < PER; ++q) {
+        const int idx = lane + 32 * q;
+        h[idx] = nv[q];
+        a.carry[(s * a.nchunks + j - 1) * DD + idx] = nv[q];
+      }
+      __syncwarp();
+    }
+  }
+}
+
+// ddt[b, t] = sum_n ddt_part[b, t, n]
+static __global__ void reduce_channels_kernel(const float* __restrict__ part, float* __restrict__ out,
+                                       int64_t BT, int64_t N) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= BT) return;
+  float s = 0.0f;
+  for (int64_t n = 0; n < N; ++n) s += part[i * N + n];
+  out[i] = s;
+}
+
+}  // namespace csn

@@ -1,0 +1,317 @@
+// csn_common.cuh -- shared device primitives for the rotor-scan kernels (sm_100a).
+//
+// Small D x D matrices (D = 4, 8) live in registers as Mat<D>; every loop is fully
+// unrolled so the compiler keeps them in registers.  The in-place products below
+// never need a second D x D buffer: a left product X <- M X is done column by
+// column and a right product X <- X M^T row by row, each column/row depending
+// only on itself.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "ga_tables.h"
+
+namespace csn {
+
+template <int D>
+struct Mat {
+  float a[D][D];
+};
+
+template <int D>
+__device__ __forceinline__ void mat_zero(Mat<D>& X) {
+#pragma unroll
+  for (int i = 0; i < D; ++i)
+#pragma unroll
+    for (int j = 0; j < D; ++j) X.a[i][j] = 0.0f;
+}
+
+template <int D>
+__device__ __forceinline__ void mat_identity(Mat<D>& X) {
+#pragma unroll
+  for (int i = 0; i < D; ++i)
+#pragma unroll
+    for (int j = 0; j < D; ++j) X.a[i][j] = (i == j) ? 1.0f : 0.0f;
+}
+
+// X <- M X
+template <int D>
+__device__ __forceinline__ void lmul(const Mat<D>& M, Mat<D>& X) {
+#pragma unroll
+  for (int j = 0; j < D; ++j) {
+    float col[D];
+#pragma unroll
+    for (int i = 0; i < D; ++i) {
+      float s = 0.0f;
+#pragma unroll
+      for (int k = 0; k < D; ++k) s = fmaf(M.a[i][k], X.a[k][j], s);
+      col[i] = s;
+    }
+#pragma unroll
+    for (int i = 0; i < D; ++i) X.a[i][j] = col[i];
+  }
+}
+
+// X <- M^T X
+template <int D>
+__device__ __forceinline__ void lmulT(const Mat<D>& M, Mat<D>& X) {
+#pragma unroll
+  for (int j = 0; j < D; ++j) {
+    float col[D];
+#pragma unroll
+    for (int i = 0; i < D; ++i) {
+      float s = 0.0f;
+#pragma unroll
+      for (int k = 0; k < D; ++k) s = fmaf(M.a[k][i], X.a[k][j], s);
+      col[i] = s;
+    }
+#pragma unroll
+    for (int i = 0; i < D; ++i) X.a[i][j] = col[i];
+  }
+}
+
+// X <- X M^T
+template <int D>
+__device__ __forceinline__ void rmulT(Mat<D>& X, const Mat<D>& M) {
+#pragma unroll
+  for (int i = 0; i < D; ++i) {
+    float row[D];
+#pragma unroll
+    for (int l = 0; l < D; ++l) {
+      float s = 0.0f;
+#pragma unroll
+      for (int j = 0; j < D; ++j) s = fmaf(X.a[i][j], M.a[l][j], s);
+      row[l] = s;
+    }
+#pragma unroll
+    for (int l = 0; l < D; ++l) X.a[i][l] = row[l];
+  }
+}
+
+// X <- X M
+template <int D>
+__device__ __forceinline__ void rmul(Mat<D>& X, const Mat<D>& M) {
+#pragma unroll
+  for (int i = 0; i < D; ++i) {
+    float row[D];
+#pragma unroll
+    for (int l = 0; l < D; ++l) {
+      float s = 0.0f;
+#pragma unroll
+      for (int j = 0; j < D; ++j) s = fmaf(X.a[i][j], M.a[j][l], s);
+      row[l] = s;
+    }
+#pragma unroll
+    for (int l = 0; l < D; ++l) X.a[i][l] = row[l];
+  }
+}
+
+// In-place Gauss-Jordan inverse without pivoting.  Only used on A = I - Omega with
+// Omega skew: the symmetric part of A and of every Schur complement of A is the
+// identity or larger, so every pivot is >= 1 and no pivoting is needed.
+template <int D>
+__device__ __forceinline__ void gj_inverse(Mat<D>& A) {
+#pragma unroll
+  for (int k = 0; k < D; ++k) {
+    const float inv = 1.0f / A.a[k][k];
+    A.a[k][k] = 1.0f;
+#pragma unroll
+    for (int j = 0; j < D; ++j) A.a[k][j] *= inv;
+#pragma unroll
+    for (int i = 0; i < D; ++i) {
+      if (i == k) continue;
+      const float f = A.a[i][k];
+      A.a[i][k] = 0.0f;
+#pragma unroll
+      for (int j = 0; j < D; ++j) A.a[i][j] = fmaf(-f, A.a[k][j], A.a[i][j]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- global loads
+template <int D>
+__device__ __forceinline__ void load_mat(Mat<D>& X, const float* __restrict__ p) {
+  static_assert((D * D) % 4 == 0, "vector loads need D*D % 4 == 0");
+  const float4* q = reinterpret_cast<const float4*>(p);
+#pragma unroll
+  for (int v = 0; v < D * D / 4; ++v) {
+    const float4 f = __ldg(q + v);
+    const int e = 4 * v;
+    X.a[e / D][e % D] = f.x;
+    X.a[(e + 1) / D][(e + 1) % D] = f.y;
+    X.a[(e + 2) / D][(e + 2) % D] = f.z;
+    X.a[(e + 3) / D][(e + 3) % D] = f.w;
+  }
+}
+
+template <int D>
+__device__ __forceinline__ void store_mat(float* __restrict__ p, const Mat<D>& X) {
+  float4* q = reinterpret_cast<float4*>(p);
+#pragma unroll
+  for (int v = 0; v < D * D / 4; ++v) {
+    const int e = 4 * v;
+    float4 f;
+    f.x = X.a[e / D][e % D];
+    f.y = X.a[(e + 1) / D][(e + 1) % D];
+    f.z = X.a[(e + 2) / D][(e + 2) % D];
+    f.w = X.a[(e + 3) / D][(e + 3) % D];
+    q[v] = f;
+  }
+}
+
+// Streaming store (evict-first): outputs are not re-read by this kernel, so keep
+// L2 for the inputs that the apply pass reads a second time.
+template <int D>
+__device__ __forceinline__ void store_mat_cs(float* __restrict__ p, const Mat<D>& X) {
+  float4* q = reinterpret_cast<float4*>(p);
+#pragma unroll
+  for (int v = 0; v < D * D / 4; ++v) {
+    const int e = 4 * v;
+    float4 f;
+    f.x = X.a[e / D][e % D];
+    f.y = X.a[(e + 1) / D][(e + 1) % D];
+    f.z = X.a[(e + 2) / D][(e + 2) % D];
+    f.w = X.a[(e + 3) / D][(e + 3) % D];
+    __stcs(q + v, f);
+  }
+}
+
+// X += s * (matrix at p)
+template <int D>
+__device__ __forceinline__ void add_scaled_mat(Mat<D>& X, const float* __restrict__ p, float s) {
+  const float4* q = reinterpret_cast<const float4*>(p);
+#pragma unroll
+  for (int v = 0; v < D * D / 4; ++v) {
+    const float4 f = __ldg(q + v);
+    const int e = 4 * v;
+    X.a[e / D][e % D] = fmaf(s, f.x, X.a[e / D][e % D]);
+    X.a[(e + 1) / D][(e + 1) % D] = fmaf(s, f.y, X.a[(e + 1) / D][(e + 1) % D]);
+    X.a[(e + 2) / D][(e + 2) % D] = fmaf(s, f.z, X.a[(e + 2) / D][(e + 2) % D]);
+    X.a[(e + 3) / D][(e + 3) % D] = fmaf(s, f.w, X.a[(e + 3) / D][(e + 3) % D]);
+  }
+}
+
+template <int D>
+__device__ __forceinline__ float mat_dot_global(const Mat<D>& X, const float* __restrict__ p) {
+  const float4* q = reinterpret_cast<const float4*>(p);
+  float s = 0.0f;
+#pragma unroll
+  for (int v = 0; v < D * D / 4; ++v) {
+    const float4 f = __ldg(q + v);
+    const int e = 4 * v;
+    s = fmaf(X.a[e / D][e % D], f.x, s);
+    s = fmaf(X.a[(e + 1) / D][(e + 1) % D], f.y, s);
+    s = fmaf(X.a[(e + 2) / D][(e + 2) % D], f.z, s);
+    s = fmaf(X.a[(e + 3) / D][(e + 3) % D], f.w, s);
+  }
+  return s;
+}
+
+// Generator layouts accepted by the fused rotor kernels.
+enum Basis : int {
+  BASIS_TRIU = 0,  // reference layout: g_k at torch.triu_indices(D, D, 1)[:, k]
+  BASIS_GA = 1,    // GA bivector blades through rho: Cl(3,0) for D = 4, Cl(8,0) for D = 16
+};
+
+template <int D, int BASIS>
+struct GenCount {
+  static constexpr int K = D * (D - 1) / 2;
+};
+template <>
+struct GenCount<4, BASIS_GA> {
+  static constexpr int K = CSN_CL3_NBIV;
+};
+template <>
+struct GenCount<16, BASIS_GA> {
+  static constexpr int K = CSN_CL8_NBIV;
+};
+
+// Load the K generators of one element (K*4 bytes, 8-byte aligned at least).
+template <int K>
+__device__ __forceinline__ void load_gens(float (&g)[K], const float* __restrict__ p) {
+  if constexpr (K % 4 == 0) {
+    const float4* q = reinterpret_cast<const float4*>(p);
+#pragma unroll
+    for (int v = 0; v < K / 4; ++v) {
+      const float4 f = __ldg(q + v);
+      g[4 * v] = f.x; g[4 * v + 1] = f.y; g[4 * v + 2] = f.z; g[4 * v + 3] = f.w;
+    }
+  } else if constexpr (K % 2 == 0) {
+    const float2* q = reinterpret_cast<const float2*>(p);
+#pragma unroll
+    for (int v = 0; v < K / 2; ++v) {
+      const float2 f = __ldg(q + v);
+      g[2 * v] = f.x; g[2 * v + 1] = f.y;
+    }
+  } else {
+#pragma unroll
+    for (int v = 0; v < K; ++v) g[v] = __ldg(p + v);
+  }
+}
+
+// rho(bivector) tables of the GA layout: Cl(3,0) on R^4, Cl(8,0) on R^16.
+template <int D>
+__host__ __device__ constexpr auto rho_biv_tab() {
+  if constexpr (D == 4) return cl3_biv_tab();
+  else return cl8_biv_tab();
+}
+
+// A <- I - h * sum_k g_k E_k  (h = dt / 2), for the generator layout BASIS.
+template <int D, int BASIS, int K>
+__device__ __forceinline__ void build_I_minus_omega(Mat<D>& A, const float (&g)[K], float h) {
+  if constexpr (BASIS == BASIS_TRIU) {
+    int k = 0;
+#pragma unroll
+    for (int u = 0; u < D; ++u) {
+      A.a[u][u] = 1.0f;
+#pragma unroll
+      for (int v = u + 1; v < D; ++v) {
+        const float w = h * g[k];
+        A.a[u][v] = -w;
+        A.a[v][u] = w;
+        ++k;
+      }
+    }
+  } else {
+    mat_identity(A);
+    constexpr auto tab = rho_biv_tab<D>();
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const float w = h * g[k];
+#pragma unroll
+      for (int u = 0; u < D; ++u) {
+        const int col = tab.col[k][u];
+        const float sg = tab.sgn[k][u];
+        A.a[u][col] = fmaf(-sg, w, A.a[u][col]);
+      }
+    }
+  }
+}
+
+// Projection of a D x D gradient G_Omega onto the generators:
+// out_k = <G_Omega, E_k>.
+template <int D, int BASIS, int K>
+__device__ __forceinline__ void project_generators(const Mat<D>& Gom, float (&out)[K]) {
+  if constexpr (BASIS == BASIS_TRIU) {
+    int k = 0;
+#pragma unroll
+    for (int u = 0; u < D; ++u)
+#pragma unroll
+      for (int v = u + 1; v < D; ++v) {
+        out[k] = Gom.a[u][v] - Gom.a[v][u];
+        ++k;
+      }
+  } else {
+    constexpr auto tab = rho_biv_tab<D>();
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      float s = 0.0f;
+#pragma unroll
+      for (int u = 0; u < D; ++u) s = fmaf((float)tab.sgn[k][u], Gom.a[u][tab.col[k][u]], s);
+      out[k] = s;
+    }
+  }
+}
+
+}  // namespace csn

@@ -1,0 +1,570 @@
+// csn_scan.cu -- chunked rotor scans for sm_100a (D = 4, 8).
+//
+// Recurrence (per sequence s = (b, n), X_{-1} = h0 or 0):
+//   two-sided  X_t = M_t X_{t-1} M_t^T + C_t     (python/clifford_scan.py:19-85)
+//   one-sided  X_t = M_t X_{t-1} + C_t           (csn_toolkit/csn/scan.py:16-41)
+// with (M_t, C_t) either given (plain scan) or built on the fly from generators,
+// dt, gamma and S (fused rotor scan, python/clifford_cl6.py:150-171):
+//   Omega = 0.5 dt sum_k g_k E_k, Q = (I - Omega)^{-1}(I + Omega) = 2 (I - Omega)^{-1} - I,
+//   damped:   a = sigmoid(-gamma dt), M = sqrt(a) Q, C = (1 - a) S
+//   undamped: M = Q, C = S.
+//
+// Parallel structure (work-efficient reduce-then-scan over time chunks; one thread
+// owns one (sequence, chunk) and keeps its D x D matrices in registers):
+//   1. reduce: each chunk j computes its aggregate (P_j, c_j): P_j = M_end ... M_start,
+//      c_j = chunk-local scan result with zero carry-in;
+//   2. carry:  per sequence, h_{j+1} = P_j h_j P_j^T + c_j (one-sided: P_j h_j + c_j),
+//      h_0 = h0;
+//   3. apply:  each chunk rescans from its carry h_j and writes X.
+// The backward pass is the mirror image in reverse time with transitions M^T
+// (G_t = dX_t + M_{t+1}^T G_{t+1} M_{t+1}), chunk aggregates (P_j, c'_j) where
+// H_{j-1} = P_j^T H_j P_j + c'_j, and an apply pass that emits the gradients.
+#include "csn_common.cuh"
+#include "csn_internal.h"
+#include "csn_scan_args.cuh"
+#include "csn_carry.cuh"
+
+namespace csn {
+
+// Build M_t of the fused rotor scan.  Writes M and the rotor scalars.
+template <int D, int BASIS, bool DAMPED, int K>
+__device__ __forceinline__ void rotor_transition(const ScanArgs& a, int64_t b, int64_t t,
+                                                 int64_t e, Mat<D>& M, RotorStep<D, K>& r) {
+  load_gens<K>(r.g, a.gens + e * K);
+  r.dt = __ldg(a.dt + b * a.T + t);
+  build_I_minus_omega<D, BASIS, K>(M, r.g, 0.5f * r.dt);
+  gj_inverse(M);  // M = A^{-1}
+  if constexpr (DAMPED) {
+    r.gamma = __ldg(a.gamma + e);
+    r.alpha = 1.0f / (1.0f + expf(r.gamma * r.dt));
+    r.sa = sqrtf(r.alpha);
+  } else {
+    r.gamma = 0.0f;
+    r.alpha = 1.0f;
+    r.sa = 1.0f;
+  }
+  // M = sa * (2 A^{-1} - I)
+#pragma unroll
+  for (int i = 0; i < D; ++i)
+#pragma unroll
+    for (int j = 0; j < D; ++j) M.a[i][j] = r.sa * (2.0f * M.a[i][j] - ((i == j) ? 1.0f : 0.0f));
+}
+
+// Load/build the transition M_t; returns the scale applied to the injected matrix
+// (C_t = cscale * S_t for the rotor source, C_t itself for the plain source).
+template <int D, int SRC, int BASIS, bool DAMPED, int K>
+__device__ __forceinline__ float transition(const ScanArgs& a, int64_t b, int64_t t, int64_t e,
+                                            Mat<D>& M, RotorStep<D, K>& r) {
+  if constexpr (SRC == SRC_MC) {
+    load_mat(M, a.M + e * (D * D));
+    return 1.0f;
+  } else {
+    rotor_transition<D, BASIS, DAMPED, K>(a, b, t, e, M, r);
+    return DAMPED ? (1.0f - r.alpha) : 1.0f;
+  }
+}
+
+template <int D, int SRC>
+__device__ __forceinline__ const float* injected(const ScanArgs& a, int64_t e) {
+  return (SRC == SRC_MC) ? (a.C + e * (D * D)) : (a.S + e * (D * D));
+}
+
+// ------------------------------------------------------------ forward: reduce
+template <int D, int SRC, int BASIS, bool DAMPED, bool TWO>
+__global__ void __launch_bounds__(128) fwd_reduce_kernel(ScanArgs a) {
+  constexpr int K = GenCount<D, BASIS>::K;
+  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t total = a.B * a.N * a.nchunks;
+  if (tid >= total) return;
+  const int64_t n = tid % a.N;
+  const int64_t j = (tid / a.N) % a.nchunks;
+  const int64_t b = tid / (a.N * a.nchunks);
+  const int64_t t0 = j * a.chunk;
+  const int64_t t1 = min(a.T, t0 + a.chunk);
+
+  Mat<D> P, c, M;
+  mat_identity(P);
+  mat_zero(c);
+  RotorStep<D, K> r;
+  for (int64_t t = t0; t < t1; ++t) {
+    const int64_t e = elem(a, b, t, n);
+    const float cs = transition<D, SRC, BASIS, DAMPED, K>(a, b, t, e, M, r);
+    lmul(M, c);
+    if constexpr (TWO) rmulT(c, M);
+    add_scaled_mat(c, injected<D, SRC>(a, e), cs);
+    lmul(M, P);
+  }
+  const int64_t s = b * a.N + n;
+  store_mat(a.aggP + (s * a.nchunks + j) * (D * D), P);
+  store_mat(a.aggC + (s * a.nchunks + j) * (D * D), c);
+}
+
+// ------------------------------------------------------------ forward: apply
+template <int D, int SRC, int BASIS, bool DAMPED, bool TWO>
+__global__ void __launch_bounds__(128) fwd_apply_kernel(ScanArgs a) {
+  constexpr int K = GenCount<D, BASIS>::K;
+  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t total = a.B * a.N * a.nchunks;
+  if (tid >= total) return;
+  const int64_t n = tid % a.N;
+  const int64_t j = (tid / a.N) % a.nchunks;
+  const int64_t b = tid / (a.N * a.nchunks);
+  const int64_t s = b * a.N + n;
+  const int64_t t0 = j * a.chunk;
+  const int64_t t1 = min(a.T, t0 + a.chunk);
+
+  Mat<D> X, M;
+  if (a.nchunks > 1) load_mat(X, a.carry + (s * a.nchunks + j) * (D * D));
+  else if (a.h0) load_mat(X, a.h0 + s * (D * D));
+  else mat_zero(X);
+  RotorStep<D, K> r;
+  for (int64_t t = t0; t < t1; ++t) {
+    const int64_t e = elem(a, b, t, n);
+    const float cs = transition<D, SRC, BASIS, DAMPED, K>(a, b, t, e, M, r);
+    lmul(M, X);
+    if constexpr (TWO) rmulT(X, M);
+    add_scaled_mat(X, injected<D, SRC>(a, e), cs);
+    store_mat_cs(a.out + e * (D * D), X);
+  }
+}
+
+// ------------------------------------------------------------ backward: reduce
+// Chunk aggregate of the reverse recurrence with zero carry from the right:
+//   g <- 0; for t = end..start: G = dX_t + g; g = M_t^T G M_t (one-sided M_t^T G)
+//   P = M_end ... M_start.
+template <int D, int SRC, int BASIS, bool DAMPED, bool TWO>
+__global__ void __launch_bounds__(128) bwd_reduce_kernel(ScanArgs a) {
+  constexpr int K = GenCount<D, BASIS>::K;
+  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t total = a.B * a.N * a.nchunks;
+  if (tid >= total) return;
+  const int64_t n = tid % a.N;
+  const int64_t j = (tid / a.N) % a.nchunks;
+  const int64_t b = tid / (a.N * a.nchunks);
+  if (j == 0) return;  // chunk 0's aggregate is never needed (dh0 comes from the apply pass)
+  const int64_t t0 = j * a.chunk;
+  const int64_t t1 = min(a.T, t0 + a.chunk);
+
+  Mat<D> P, g, M;
+  mat_identity(P);
+  mat_zero(g);
+  RotorStep<D, K> r;
+  for (int64_t t = t1 - 1; t >= t0; --t) {
+    const int64_t e = elem(a, b, t, n);
+    transition<D, SRC, BASIS, DAMPED, K>(a, b, t, e, M, r);
+    add_scaled_mat(g, a.dX + e * (D * D), 1.0f);
+    lmulT(M, g);
+    if constexpr (TWO) rmul(g, M);
+    rmul(P, M);
+  }
+  const int64_t s = b * a.N + n;
+  store_mat(a.aggP + (s * a.nchunks + j) * (D * D), P);
+  store_mat(a.aggC + (s * a.nchunks + j) * (D * D), g);
+}
+
+// ------------------------------------------------------------ backward: apply
+template <int D, int SRC, int BASIS, bool DAMPED, bool TWO>
+__global__ void __launch_bounds__(128) bwd_apply_kernel(ScanArgs a) {
+  constexpr int K = GenCount<D, BASIS>::K;
+  constexpr int DD = D * D;
+  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t total = a.B * a.N * a.nchunks;
+  if (tid >= total) return;
+  const int64_t n = tid % a.N;
+  const int64_t j = (tid / a.N) % a.nchunks;
+  const int64_t b = tid / (a.N * a.nchunks);
+  const int64_t s = b * a.N + n;
+  const int64_t t0 = j * a.chunk;
+  const int64_t t1 = min(a.T, t0 + a.chunk);
+
+  Mat<D> H, M;
+  if (a.nchunks > 1) load_mat(H, a.carry + (s * a.nchunks + j) * DD);
+  else mat_zero(H);
+  RotorStep<D, K> r;
+  for (int64_t t = t1 - 1; t >= t0; --t) {
+    const int64_t e = elem(a, b, t, n);
+    transition<D, SRC, BASIS, DAMPED, K>(a, b, t, e, M, r);
+    // G = dX_t + H (held in H)
+    add_scaled_mat(H, a.dX + e * DD, 1.0f);
+    const float* xprev = (t > 0) ? (a.X + elem(a, b, t - 1, n) * DD) : a.h0 ? (a.h0 + s * DD) : nullptr;
+
+    // dM = G M Xp^T + G^T M Xp (two-sided) | G Xp^T (one-sided)
+    Mat<D> dM;
+    if (xprev) {
+      Mat<D> Xp;
+      load_mat(Xp, xprev);
+      if constexpr (TWO) {
+        Mat<D> W = H;
+        rmul(W, M);    // G M
+        rmulT(W, Xp);  // G M Xp^T
+        lmul(M, Xp);   // M Xp
+        // dM = W + G^T (M Xp)
+#pragma unroll
+        for (int jj = 0; jj < D; ++jj)
+#pragma unroll
+          for (int i = 0; i < D; ++i) {
+            float acc = W.a[i][jj];
+#pragma unroll
+            for (int k = 0; k < D; ++k) acc = fmaf(H.a[k][i], Xp.a[k][jj], acc);
+            dM.a[i][jj] = acc;
+          }
+      } else {
+        dM = H;
+        rmulT(dM, Xp);
+      }
+    } else {
+      mat_zero(dM);
+    }
+
+    if constexpr (SRC == SRC_MC) {
+      store_mat_cs(a.dM + e * DD, dM);
+      store_mat_cs(a.dC + e * DD, H);
+    } else {
+      // dS = (1 - a) G  (undamped: G)
+      const float cs = DAMPED ? (1.0f - r.alpha) : 1.0f;
+      {
+        Mat<D> dS;
+#pragma unroll
+        for (int i = 0; i < D; ++i)
+#pragma unroll
+          for (int jj = 0; jj < D; ++jj) dS.a[i][jj] = cs * H.a[i][jj];
+        store_mat_cs(a.dC + e * DD, dS);
+      }
+      float da = 0.0f;
+      if constexpr (DAMPED) {
+        // da = -<G, S> + <dM, M> / (2 a)
+        float dmm = 0.0f;
+#pragma unroll
+        for (int i = 0; i < D; ++i)
+#pragma unroll
+          for (int jj = 0; jj < D; ++jj) dmm = fmaf(dM.a[i][jj], M.a[i][jj], dmm);
+        da = -mat_dot_global(H, a.S + e * DD) + dmm / (2.0f * r.alpha);
+      }
+      // dQ = sa dM;  dOm = 2 Bt dQ Bt with Bt = A^{-T} = 0.5 (Q^T + I), Q = M / sa
+      const float inv_sa = 1.0f / r.sa;
+      Mat<D> Bt;
+#pragma unroll
+      for (int i = 0; i < D; ++i)
+#pragma unroll
+        for (int jj = 0; jj < D; ++jj)
+          Bt.a[i][jj] = 0.5f * (M.a[jj][i] * inv_sa + ((i == jj) ? 1.0f : 0.0f));
+#pragma unroll
+      for (int i = 0; i < D; ++i)
+#pragma unroll
+        for (int jj = 0; jj < D; ++jj) dM.a[i][jj] *= 2.0f * r.sa;
+      lmul(Bt, dM);  // Bt dQ
+      rmul(dM, Bt);  // Bt dQ Bt
+      float proj[K];
+      project_generators<D, BASIS, K>(dM, proj);
+      const float hdt = 0.5f * r.dt;
+      float ddt = 0.0f;
+      float outg[K];
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        outg[k] = proj[k] * hdt;
+        ddt = fmaf(proj[k], 0.5f * r.g[k], ddt);
+      }
+      float* dg = a.dgens + e * K;
+      if constexpr (K % 4 == 0) {
+#pragma unroll
+        for (int v = 0; v < K / 4; ++v)
+          __stcs(reinterpret_cast<float4*>(dg) + v,
+                 make_float4(outg[4 * v], outg[4 * v + 1], outg[4 * v + 2], outg[4 * v + 3]));
+      } else {
+#pragma unroll
+        for (int k = 0; k < K; ++k) dg[k] = outg[k];
+      }
+      if constexpr (DAMPED) {
+        const float dz = da * r.alpha * (1.0f - r.alpha);
+        a.dgamma[e] = -dz * r.dt;
+        ddt = fmaf(-dz, r.gamma, ddt);
+      }
+      a.ddt_part[e] = ddt;
+    }
+    // H <- M^T G M (one-sided: M^T G)
+    lmulT(M, H);
+    if constexpr (TWO) rmul(H, M);
+  }
+  if (j == 0 && a.dh0) store_mat(a.dh0 + s * DD, H);
+}
+
+// ================================================================= host side
+namespace {
+
+int64_t pick_chunk(int64_t S, int64_t T, int D) {
+  // Enough (sequence, chunk) work items to fill 148 SMs at the residency each
+  // family allows: D = 4 ~1024 threads / SM, D = 8 ~256 threads / SM (register
+  // bound), D = 16 ~16 warps / SM (one warp per chunk, shared-memory bound).
+  const int64_t target = (D == 16) ? 148 * 16 : (D == 8) ? 148 * 256 : 148 * 1024;
+  int64_t chunk = (S * T + target - 1) / target;
+  if (chunk < 8) chunk = 8;
+  if (chunk > T) chunk = T > 0 ? T : 1;
+  return chunk;
+}
+
+struct Plan {
+  int64_t nchunks, chunk;
+  size_t agg_floats;   // aggP + aggC + carry
+  size_t part_floats;  // ddt partials (rotor backward)
+};
+
+Plan make_plan(int64_t B, int64_t T, int64_t N, int D, bool rotor_bwd) {
+  Plan p;
+  const int64_t S = B * N;
+  p.chunk = pick_chunk(S, T, D);
+  p.nchunks = T > 0 ? (T + p.chunk - 1) / p.chunk : 0;
+  p.agg_floats = p.nchunks > 1 ? (size_t)3 * S * p.nchunks * D * D : 0;
+  p.part_floats = rotor_bwd ? (size_t)B * T * N : 0;
+  return p;
+}
+
+size_t plan_bytes(const Plan& p) { return (p.agg_floats + p.part_floats) * sizeof(float) + 256; }
+
+struct Workspace {
+  float* base = nullptr;
+  bool owned = false;
+  cudaStream_t stream = nullptr;
+  ~Workspace() {
+    if (owned && base) cudaFreeAsync(base, stream);
+  }
+};
+
+int get_ws(Workspace& w, void* user, size_t user_bytes, size_t need, cudaStream_t st) {
+  w.stream = st;
+  if (user) {
+    if (user_bytes < need) return set_error(CSN_ERR_INVALID, "workspace smaller than *_workspace_bytes()");
+    w.base = static_cast<float*>(user);
+    return CSN_OK;
+  }
+  cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&w.base), need, st);
+  if (e != cudaSuccess) return set_cuda_error(e, "cudaMallocAsync(workspace)");
+  w.owned = true;
+  return CSN_OK;
+}
+
+void bind_ws(ScanArgs& a, const Plan& p, float* base, int D) {
+  const int64_t S = a.B * a.N;
+  const size_t one = (size_t)S * p.nchunks * D * D;
+  float* aligned = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(base) + 255) & ~uintptr_t(255));
+  a.aggP = aligned;
+  a.aggC = aligned + one;
+  a.carry = aligned + 2 * one;
+  a.ddt_part = aligned + p.agg_floats;
+  a.nchunks = p.nchunks;
+  a.chunk = p.chunk;
+}
+
+unsigned blocks_for(int64_t n, int threads) { return (unsigned)((n + threads - 1) / threads); }
+
+template <int D, int SRC, int BASIS, bool DAMPED, bool TWO>
+int run_fwd(ScanArgs a, cudaStream_t st) {
+  const int64_t S = a.B * a.N;
+  const int64_t total = S * a.nchunks;
+  if (total == 0) return CSN_OK;
+  if (a.nchunks > 1) {
+    {
+      KernelTimer kt("fwd_reduce", st);
+      fwd_reduce_kernel<D, SRC, BASIS, DAMPED, TWO><<<blocks_for(total, 128), 128, 0, st>>>(a);
+    }
+    KernelTimer kt("fwd_carry", st);
+    if (D == 4) fwd_carry_kernel<D, TWO><<<blocks_for(S, 128), 128, 0, st>>>(a);
+    else fwd_carry_kernel<D, TWO><<<blocks_for(S, 4), 128, 0, st>>>(a);
+  }
+  {
+    KernelTimer kt("fwd_apply", st);
+    fwd_apply_kernel<D, SRC, BASIS, DAMPED, TWO><<<blocks_for(total, 128), 128, 0, st>>>(a);
+  }
+  return check_launch("scan forward");
+}
+
+template <int D, int SRC, int BASIS, bool DAMPED, bool TWO>
+int run_bwd(ScanArgs a, cudaStream_t st) {
+  const int64_t S = a.B * a.N;
+  const int64_t total = S * a.nchunks;
+  if (total > 0) {
+    if (a.nchunks > 1) {
+      {
+        KernelTimer kt("bwd_reduce", st);
+        bwd_reduce_kernel<D, SRC, BASIS, DAMPED, TWO><<<blocks_for(total, 128), 128, 0, st>>>(a);
+      }
+      KernelTimer kt("bwd_carry", st);
+      if (D == 4) bwd_carry_kernel<D, TWO><<<blocks_for(S, 128), 128, 0, st>>>(a);
+      else bwd_carry_kernel<D, TWO><<<blocks_for(S, 4), 128, 0, st>>>(a);
+    }
+    KernelTimer kt("bwd_apply", st);
+    bwd_apply_kernel<D, SRC, BASIS, DAMPED, TWO><<<blocks_for(total, 128), 128, 0, st>>>(a);
+  }
+  if (SRC == SRC_ROTOR && a.B * a.T > 0) {
+    const int64_t BT = a.B * a.T;
+    KernelTimer kt("reduce_channels", st);
+    reduce_channels_kernel<<<blocks_for(BT, 256), 256, 0, st>>>(a.ddt_part, a.ddt, BT, a.N);
+  }
+  return check_launch("scan backward");
+}
+
+template <int D, int SRC, int BASIS, bool DAMPED>
+int run_sided(ScanArgs a, bool two, bool bwd, cudaStream_t st) {
+  if (bwd) return two ? run_bwd<D, SRC, BASIS, DAMPED, true>(a, st) : run_bwd<D, SRC, BASIS, DAMPED, false>(a, st);
+  return two ? run_fwd<D, SRC, BASIS, DAMPED, true>(a, st) : run_fwd<D, SRC, BASIS, DAMPED, false>(a, st);
+}
+
+int dispatch(ScanArgs a, int D, int src, int basis, bool damped, bool two, bool bwd, cudaStream_t st) {
+  if (src == SRC_MC) {
+    switch (D) {
+      case 4: return run_sided<4, SRC_MC, BASIS_TRIU, false>(a, two, bwd, st);
+      case 8: return run_sided<8, SRC_MC, BASIS_TRIU, false>(a, two, bwd, st);
+      default: break;
+    }
+    return set_error(CSN_ERR_UNSUPPORTED, "plain scan: D must be 4 or 8 in this kernel family");
+  }
+  if (D == 4 && basis == BASIS_TRIU)
+    return damped ? run_sided<4, SRC_ROTOR, BASIS_TRIU, true>(a, two, bwd, st)
+                  : run_sided<4, SRC_ROTOR, BASIS_TRIU, false>(a, two, bwd, st);
+  if (D == 4 && basis == BASIS_GA)
+    return damped ? run_sided<4, SRC_ROTOR, BASIS_GA, true>(a, two, bwd, st)
+                  : run_sided<4, SRC_ROTOR, BASIS_GA, false>(a, two, bwd, st);
+  if (D == 8 && basis == BASIS_TRIU)
+    return damped ? run_sided<8, SRC_ROTOR, BASIS_TRIU, true>(a, two, bwd, st)
+                  : run_sided<8, SRC_ROTOR, BASIS_TRIU, false>(a, two, bwd, st);
+  return set_error(CSN_ERR_UNSUPPORTED, "rotor scan: unsupported (D, basis) for this kernel family");
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+bool aligned8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7u) == 0; }
+
+int check_shape(int64_t B, int64_t T, int64_t N, int D) {
+  if (B < 0 || T < 0 || N < 0) return set_error(CSN_ERR_INVALID, "negative dimension");
+  if (D != 4 && D != 8 && D != 16) return set_error(CSN_ERR_INVALID, "D must be 4, 8 or 16");
+  return CSN_OK;
+}
+
+}  // namespace
+
+// Implemented in csn_scan16.cu (D = 16 kernel family).
+int scan16_dispatch(const ScanArgs& a, int src, int basis, bool damped, bool two, bool bwd,
+                    cudaStream_t st);
+
+}  // namespace csn
+
+using namespace csn;
+
+extern "C" size_t csn_scan_workspace_bytes(int64_t B, int64_t T, int64_t N, int D) {
+  if (B < 0 || T < 0 || N < 0 || D < 1) return 0;
+  return plan_bytes(make_plan(B, T, N, D, false));
+}
+
+extern "C" size_t csn_rotor_scan_workspace_bytes(int64_t B, int64_t T, int64_t N, int D) {
+  if (B < 0 || T < 0 || N < 0 || D < 1) return 0;
+  return plan_bytes(make_plan(B, T, N, D, true));
+}
+
+extern "C" int csn_scan_fwd(const float* M, const float* C, const float* h0, float* X, int64_t B,
+                            int64_t T, int64_t N, int D, int two_sided, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  if (int rc = check_shape(B, T, N, D)) return rc;
+  if (B * T * N == 0) return CSN_OK;
+  if (!M || !C || !X) return set_error(CSN_ERR_INVALID, "csn_scan_fwd: M, C and X are required");
+  if (!aligned16(M) || !aligned16(C) || !aligned16(X) || (h0 && !aligned16(h0)))
+    return set_error(CSN_ERR_INVALID, "csn_scan_fwd: pointers must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Plan p = make_plan(B, T, N, D, false);
+  Workspace ws;
+  if (int rc = get_ws(ws, workspace, workspace_bytes, plan_bytes(p), st)) return rc;
+  ScanArgs a{};
+  a.M = M; a.C = C; a.h0 = h0; a.out = X; a.B = B; a.T = T; a.N = N;
+  bind_ws(a, p, ws.base, D);
+  if (D == 16) return scan16_dispatch(a, SRC_MC, BASIS_TRIU, false, two_sided != 0, false, st);
+  return dispatch(a, D, SRC_MC, BASIS_TRIU, false, two_sided != 0, false, st);
+}
+
+extern "C" int csn_scan_bwd(const float* M, const float* X, const float* dX, const float* h0,
+                            float* dM, float* dC, float* dh0, int64_t B, int64_t T, int64_t N,
+                            int D, int two_sided, void* workspace, size_t workspace_bytes,
+                            void* stream) {
+  if (int rc = check_shape(B, T, N, D)) return rc;
+  if (B * T * N == 0) return CSN_OK;
+  if (!M || !X || !dX || !dM || !dC)
+    return set_error(CSN_ERR_INVALID, "csn_scan_bwd: M, X, dX, dM and dC are required");
+  if (!aligned16(M) || !aligned16(X) || !aligned16(dX) || !aligned16(dM) || !aligned16(dC) ||
+      (h0 && !aligned16(h0)) || (dh0 && !aligned16(dh0)))
+    return set_error(CSN_ERR_INVALID, "csn_scan_bwd: pointers must be 16-byte aligned");
+  if (dh0 && !h0) return set_error(CSN_ERR_INVALID, "csn_scan_bwd: dh0 needs h0");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Plan p = make_plan(B, T, N, D, false);
+  Workspace ws;
+  if (int rc = get_ws(ws, workspace, workspace_bytes, plan_bytes(p), st)) return rc;
+  ScanArgs a{};
+  a.M = M; a.X = X; a.dX = dX; a.h0 = h0; a.dM = dM; a.dC = dC; a.dh0 = dh0;
+  a.B = B; a.T = T; a.N = N;
+  bind_ws(a, p, ws.base, D);
+  if (D == 16) return scan16_dispatch(a, SRC_MC, BASIS_TRIU, false, two_sided != 0, true, st);
+  return dispatch(a, D, SRC_MC, BASIS_TRIU, false, two_sided != 0, true, st);
+}
+
+static int rotor_common_checks(const float* gens, const float* dt, const float* S, int64_t B,
+                               int64_t T, int64_t N, int D, int basis) {
+  if (int rc = check_shape(B, T, N, D)) return rc;
+  if (basis != BASIS_TRIU && basis != BASIS_GA) return set_error(CSN_ERR_INVALID, "unknown basis");
+  if (basis == BASIS_GA && D == 8)
+    return set_error(CSN_ERR_UNSUPPORTED, "GA basis is provided for D = 4 (Cl(3,0)) and D = 16 (Cl(8,0))");
+  if (B * T * N == 0) return CSN_OK;
+  if (!gens || !dt || !S) return set_error(CSN_ERR_INVALID, "rotor scan: gens, dt and S are required");
+  const int K = (basis == BASIS_GA) ? (D == 4 ? CSN_CL3_NBIV : CSN_CL8_NBIV) : D * (D - 1) / 2;
+  if (K % 4 == 0 ? !aligned16(gens) : !aligned8(gens))
+    return set_error(CSN_ERR_INVALID, "rotor scan: gens misaligned");
+  if (!aligned16(S)) return set_error(CSN_ERR_INVALID, "rotor scan: S must be 16-byte aligned");
+  return CSN_OK;
+}
+
+extern "C" int csn_rotor_scan_fwd(const float* gens, const float* dt, const float* gamma,
+                                  const float* S, const float* h0, float* X, int64_t B, int64_t T,
+                                  int64_t N, int D, int basis, int two_sided, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  if (int rc = rotor_common_checks(gens, dt, S, B, T, N, D, basis)) return rc;
+  if (B * T * N == 0) return CSN_OK;
+  if (!X || !aligned16(X) || (h0 && !aligned16(h0)))
+    return set_error(CSN_ERR_INVALID, "csn_rotor_scan_fwd: X missing or misaligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Plan p = make_plan(B, T, N, D, false);
+  Workspace ws;
+  if (int rc = get_ws(ws, workspace, workspace_bytes, plan_bytes(p), st)) return rc;
+  ScanArgs a{};
+  a.gens = gens; a.dt = dt; a.gamma = gamma; a.S = S; a.h0 = h0; a.out = X;
+  a.B = B; a.T = T; a.N = N;
+  bind_ws(a, p, ws.base, D);
+  if (D == 16) return scan16_dispatch(a, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, false, st);
+  return dispatch(a, D, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, false, st);
+}
+
+extern "C" int csn_rotor_scan_bwd(const float* gens, const float* dt, const float* gamma,
+                                  const float* S, const float* h0, const float* X,
+                                  const float* dX, float* dgens, float* ddt, float* dgamma,
+                                  float* dS, float* dh0, int64_t B, int64_t T, int64_t N, int D,
+                                  int basis, int two_sided, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  if (int rc = rotor_common_checks(gens, dt, S, B, T, N, D, basis)) return rc;
+  if (B * T * N == 0) {
+    if (B * T > 0 && ddt) {
+      cudaError_t e = cudaMemsetAsync(ddt, 0, sizeof(float) * B * T, static_cast<cudaStream_t>(stream));
+      if (e != cudaSuccess) return set_cuda_error(e, "cudaMemsetAsync(ddt)");
+    }
+    return CSN_OK;
+  }
+  if (!X || !dX || !dgens || !ddt || !dS || (gamma && !dgamma))
+    return set_error(CSN_ERR_INVALID, "csn_rotor_scan_bwd: missing X, dX or a gradient output");
+  if (!aligned16(X) || !aligned16(dX) || !aligned16(dS) || (h0 && !aligned16(h0)) ||
+      (dh0 && !aligned16(dh0)))
+    return set_error(CSN_ERR_INVALID, "csn_rotor_scan_bwd: pointers must be 16-byte aligned");
+  if (dh0 && !h0) return set_error(CSN_ERR_INVALID, "csn_rotor_scan_bwd: dh0 needs h0");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Plan p = make_plan(B, T, N, D, true);
+  Workspace ws;
+  if (int rc = get_ws(ws, workspace, workspace_bytes, plan_bytes(p), st)) return rc;
+  ScanArgs a{};
+  a.gens = gens; a.dt = dt; a.gamma = gamma; a.S = S; a.h0 = h0; a.X = X; a.dX = dX;
+  a.dgens = dgens; a.ddt = ddt; a.dgamma = dgamma; a.dC = dS; a.dh0 = dh0;
+  a.B = B; a.T = T; a.N = N;
+  bind_ws(a, p, ws.base, D);
+  if (D == 16) return scan16_dispatch(a, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, true, st);
+  return dispatch(a, D, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, true, st);
+}

@@ -1,0 +1,56 @@
+// csn_scan_args.cuh -- argument block shared by the scan kernel families.
+#pragma once
+
+#include <stdint.h>
+
+namespace csn {
+
+// ----------------------------------------------------------------- arguments
+struct ScanArgs {
+  // plain scan inputs
+  const float* M;
+  const float* C;
+  // fused rotor inputs
+  const float* gens;
+  const float* dt;
+  const float* gamma;  // nullptr = undamped
+  const float* S;
+  // common
+  const float* h0;  // [B, N, D, D] or nullptr
+  const float* X;   // forward output (backward only)
+  const float* dX;  // incoming gradient (backward only)
+  float* out;       // forward X
+  // backward outputs
+  float* dM;      // plain: dM     | rotor: unused
+  float* dC;      // plain: dC     | rotor: dS
+  float* dgens;   // rotor
+  float* dgamma;  // rotor (damped)
+  float* ddt_part;  // rotor: per (b, t, n) partial of ddt, reduced over n afterwards
+  float* ddt;       // rotor: [B, T]
+  float* dh0;       // [B, N, D, D] or nullptr
+  // workspace
+  float* aggP;   // [S, nchunks, D, D]
+  float* aggC;   // [S, nchunks, D, D]
+  float* carry;  // [S, nchunks, D, D]
+  int64_t B, T, N;
+  int64_t nchunks, chunk;
+};
+
+__device__ __forceinline__ int64_t elem(const ScanArgs& a, int64_t b, int64_t t, int64_t n) {
+  return (b * a.T + t) * a.N + n;
+}
+
+// ----------------------------------------------------------------- step sources
+enum Src : int { SRC_MC = 0, SRC_ROTOR = 1 };
+
+// Per-step rotor quantities kept for the backward pass.
+template <int D, int K>
+struct RotorStep {
+  float g[K];
+  float dt;
+  float gamma;
+  float alpha;
+  float sa;  // sqrt(alpha)
+};
+
+}  // namespace csn

@@ -1,0 +1,127 @@
+/*
+ * csn_b200.h -- C ABI of the B200 (sm_100a) rotor-scan library libcsn_b200.so.
+ *
+ * Plain C: raw device pointers, sizes and a cudaStream_t passed as void*.  No torch
+ * types cross this boundary.  Every entry point returns a status code (CSN_OK = 0)
+ * and records a message retrievable with csn_last_error() on the calling thread.
+ * Launches are asynchronous on `stream` (NULL = legacy default stream); a status of
+ * CSN_OK means the launches were queued, not that they finished.
+ *
+ * Tensor layout is the reference's: float32, row-major, contiguous,
+ *   M, C, S, X, dX, dM, dC, dS : [B, T, N, D, D]     element (b,t,n) at ((b*T+t)*N+n)*D*D
+ *   gens, dgens                : [B, T, N, K]        K = D(D-1)/2 (basis TRIU) or the
+ *                                                    GA bivector count (basis GA)
+ *   dt, ddt                    : [B, T]              one time step per token, shared by channels
+ *   gamma, dgamma              : [B, T, N]           post-softplus decay rate
+ *   h0, dh0                    : [B, N, D, D]        optional initial state (NULL = zero)
+ * Device pointers must be 16-byte aligned (8-byte for gens/dgens when K % 4 != 0).
+ *
+ * Workspace: entry points that take (workspace, workspace_bytes) use scratch device
+ * memory of at least the size the matching *_workspace_bytes() query returns.  Pass
+ * workspace = NULL to let the library allocate it stream-ordered (cudaMallocAsync /
+ * cudaFreeAsync on `stream`).
+ *
+ * Each declaration names the reference interface it replaces (paths relative to the
+ * reference project root).
+ */
+#ifndef CSN_B200_H
+#define CSN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum csn_status {
+  CSN_OK = 0,
+  CSN_ERR_INVALID = 1,     /* bad shape, pointer, alignment or size */
+  CSN_ERR_UNSUPPORTED = 2, /* a D / basis / mode this build does not provide */
+  CSN_ERR_CUDA = 3,        /* a CUDA runtime call or launch failed */
+  CSN_ERR_TIMEOUT = 4      /* a bounded device-side wait gave up */
+};
+
+enum csn_basis {
+  CSN_BASIS_TRIU = 0, /* g_k at torch.triu_indices(D, D, 1)[:, k] (python/clifford_cl6.py:124-125) */
+  CSN_BASIS_GA = 1    /* GA bivector blades e_ij (i<j, lexicographic) mapped through a real
+                         representation: Cl(3,0) on R^4 (D = 4), Cl(8,0) on R^16 (D = 16) */
+};
+
+/* Library version string and the message of the last failing call on this thread. */
+const char* csn_version(void);
+const char* csn_last_error(void);
+
+/* ------------------------------------------------------------------ plain scan */
+size_t csn_scan_workspace_bytes(int64_t B, int64_t T, int64_t N, int D);
+
+/* X_t = M_t X_{t-1} M_t^T + C_t (two_sided != 0) or M_t X_{t-1} + C_t, X_{-1} = h0 or 0.
+ * Replaces python/clifford_scan.py:41 parallel_rotor_scan (two-sided default),
+ * csn_toolkit/csn/scan.py:24 CliffordScanFunction.forward, and the pybind entry
+ * scan_fwd_cuda_d4(M, C) -> X of csn_toolkit/csn/cuda/scan_cuda.cpp:6 ([S,T,4,4] is
+ * B = S, N = 1, D = 4, two_sided = 0).  D in {4, 8, 16}. */
+int csn_scan_fwd(const float* M, const float* C, const float* h0, float* X,
+                 int64_t B, int64_t T, int64_t N, int D, int two_sided,
+                 void* workspace, size_t workspace_bytes, void* stream);
+
+/* Reverse-time adjoint of csn_scan_fwd: dM, dC (and dh0 when h0 and dh0 are given).
+ * Replaces csn_toolkit/csn/scan.py:44 CliffordScanFunction.backward, autograd through
+ * python/clifford_scan.py:41, and scan_bwd_cuda_d4(M, X, grad_X) -> [grad_M, grad_C]
+ * of csn_toolkit/csn/cuda/scan_cuda.cpp:7.  dM_0 = 0 when h0 is NULL, as in the
+ * reference. */
+int csn_scan_bwd(const float* M, const float* X, const float* dX, const float* h0,
+                 float* dM, float* dC, float* dh0,
+                 int64_t B, int64_t T, int64_t N, int D, int two_sided,
+                 void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------ fused rotor scan */
+size_t csn_rotor_scan_workspace_bytes(int64_t B, int64_t T, int64_t N, int D);
+
+/* Generators + dt + gamma + S -> X in one pass, never materialising M or C:
+ *   Omega = 0.5 dt sum_k g_k E_k,  Q = (I - Omega)^{-1} (I + Omega),
+ *   gamma != NULL: a = sigmoid(-gamma dt), M = sqrt(a) Q, C = (1 - a) S
+ *   gamma == NULL: M = Q, C = S     (h_t = R_t h_{t-1} R~_t + x_t)
+ *   X = scan(M, C).
+ * Replaces the scan section of CliffordCL6Block.forward (python/clifford_cl6.py:150-171)
+ * and CliffordCL8Block.forward (python/clifford_cl8.py:160-179): cayley_rotor_8x8 /
+ * cayley_rotor_16x16 + parallel_rotor_scan. */
+int csn_rotor_scan_fwd(const float* gens, const float* dt, const float* gamma, const float* S,
+                       const float* h0, float* X,
+                       int64_t B, int64_t T, int64_t N, int D, int basis, int two_sided,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* Adjoint of csn_rotor_scan_fwd (what autograd computes through the same reference
+ * lines): dgens, ddt [B,T] (summed over channels), dgamma (damped only), dS, dh0. */
+int csn_rotor_scan_bwd(const float* gens, const float* dt, const float* gamma, const float* S,
+                       const float* h0, const float* X, const float* dX,
+                       float* dgens, float* ddt, float* dgamma, float* dS, float* dh0,
+                       int64_t B, int64_t T, int64_t N, int D, int basis, int two_sided,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* -------------------------------------------------------------------- Cayley */
+/* Q = (I - Omega)^{-1} (I + Omega) for `count` skew D x D matrices.
+ * Replaces cayley_rotor_8x8 (python/clifford_cl6.py:57) and cayley_rotor_16x16 /
+ * cayley_rotor_4x4 with use_schulz=False (python/clifford_cl8.py:29,65). */
+int csn_cayley_fwd(const float* Omega, float* Q, int64_t count, int D, void* stream);
+
+/* dOmega = (I - Omega)^{-T} dQ (I + Q)^T = 0.5 (I + Q)^T dQ (I + Q)^T (needs only Q):
+ * the autograd of torch.linalg.solve in the same reference functions. */
+int csn_cayley_bwd(const float* Q, const float* dQ, float* dOmega, int64_t count, int D,
+                   void* stream);
+
+/* -------------------------------------------------------------- kernel timing */
+/* Measurement hook with no counterpart in the reference (which times with wall clock,
+ * tests/profile_performance.py:41-71).  While enabled, every kernel the library
+ * launches is bracketed by a pair of CUDA events recorded on its own stream.
+ * csn_timing_read() waits for those events and returns the summed elapsed time and
+ * the launch count of kernels named `name` ("fwd_reduce", "fwd_carry", "fwd_apply",
+ * "bwd_reduce", "bwd_carry", "bwd_apply", "reduce_channels"; NULL = all). */
+int csn_timing_enable(int on);
+int csn_timing_reset(void);
+int csn_timing_read(const char* name, double* total_ms, int64_t* count);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CSN_B200_H */

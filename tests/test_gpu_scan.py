@@ -1,0 +1,202 @@
+"""GPU parity of the CUDA scans (through the C ABI) against the float64 oracle and
+the reference's golden vectors.
+
+Tolerances (reference metric max|a - ref| / max|ref|,
+csn_toolkit/examples/benchmark_cuda_kernels.py:60-62):
+  forward outputs  <= 1e-4   (BASELINE: fp32 over L = 8192 vs the fp64 oracle)
+  gradients        <= 1e-3   (the reference's own gradient tolerance, same file :75-77)
+"""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+FWD_TOL = 1e-4
+BWD_TOL = 1e-3
+DEV = "cuda:0"
+
+
+def rel(a, ref):
+    a = a.detach().double().cpu().numpy() if torch.is_tensor(a) else np.asarray(a, dtype=np.float64)
+    den = np.max(np.abs(ref))
+    return float(np.max(np.abs(a - ref)) / den) if den > 0 else float(np.max(np.abs(a - ref)))
+
+
+def cuda(a, grad=False):
+    t = torch.as_tensor(np.asarray(a), dtype=torch.float32, device=DEV)
+    return t.requires_grad_(grad)
+
+
+def transitions(rng, B, T, N, D):
+    A = rng.standard_normal((B, T, N, D, D)) * 0.4
+    skew = 0.5 * (A - np.swapaxes(A, -1, -2))
+    eye = np.eye(D)
+    Q = np.linalg.solve(eye - skew, eye + skew)
+    return rng.uniform(0.6, 1.0, (B, T, N, 1, 1)) * Q + 0.05 * rng.standard_normal((B, T, N, D, D))
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from csn_b200 import _build, ops as o
+    _build.build()
+    assert torch.cuda.is_available()
+    return o
+
+
+# ----------------------------------------------------------------- plain scan
+SHAPES = [(2, 37, 3), (1, 1, 2), (1, 300, 2), (3, 129, 5)]
+
+
+@pytest.mark.parametrize("D", [4, 8, 16])
+@pytest.mark.parametrize("two", [True, False], ids=["two", "one"])
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("with_h0", [False, True], ids=["zero", "h0"])
+def test_scan_matches_oracle(ops, oracle, D, two, shape, with_h0):
+    rng = np.random.default_rng(hash((D, two, shape, with_h0)) % 2**32)
+    B, T, N = shape
+    M = transitions(rng, B, T, N, D)
+    C = rng.standard_normal((B, T, N, D, D))
+    W = rng.standard_normal((B, T, N, D, D))
+    h0 = rng.standard_normal((B, N, D, D)) if with_h0 else None
+    Xr = oracle.scan_fwd(M, C, h0=h0, two_sided=two)
+    dMr, dCr, dh0r = oracle.scan_bwd(M, Xr, W, h0=h0, two_sided=two)
+
+    Mt, Ct = cuda(M, True), cuda(C, True)
+    ht = cuda(h0, True) if with_h0 else None
+    X = ops.rotor_scan(Mt, Ct, two_sided=two, h0=ht)
+    assert rel(X, Xr) < FWD_TOL
+    (X * cuda(W)).sum().backward()
+    assert rel(Ct.grad, dCr) < BWD_TOL
+    assert rel(Mt.grad, dMr) < BWD_TOL
+    if with_h0:
+        assert rel(ht.grad, dh0r) < BWD_TOL
+
+
+@pytest.mark.parametrize("name", ["two_d4_T37", "two_d8_T23", "two_d16_T19", "one_d4_T37",
+                                  "one_d8_T23", "one_d16_T19", "two_d8_T1", "one_d4_T1"])
+def test_scan_matches_reference_golden(ops, golden, name):
+    g = golden(f"scan_{name}")
+    two = name.startswith("two")
+    M, C = cuda(g["M"], True), cuda(g["C"], True)
+    X = ops.rotor_scan(M, C, two_sided=two)
+    assert rel(X, g["X"]) < FWD_TOL
+    (X * cuda(g["W"])).sum().backward()
+    assert rel(C.grad, g["dC"]) < BWD_TOL
+    ref_dM = g["dM"] if g["dM"].shape == tuple(M.shape) else np.zeros(M.shape)
+    assert rel(M.grad, ref_dM) < BWD_TOL
+
+
+# ------------------------------------------------------------------ Cayley
+@pytest.mark.parametrize("D", [4, 8, 16])
+def test_cayley_matches_reference_golden(ops, golden, D):
+    g = golden(f"cayley_d{D}")
+    Om = cuda(g["Om"], True)
+    Q = ops.cayley(Om)
+    assert rel(Q, g["Q"]) < FWD_TOL
+    eye = torch.eye(D, device=DEV)
+    assert (Q.transpose(-1, -2) @ Q - eye).abs().max().item() < 1e-5  # |R R~ - 1| <= 1e-5
+    (Q * cuda(g["W"])).sum().backward()
+    assert rel(Om.grad, g["dOm"]) < BWD_TOL
+
+
+# -------------------------------------------------------------- fused rotor scan
+ROTOR_GOLDEN = ["rotor_d8_damped", "rotor_d8_undamped", "rotor_d4_damped", "rotor_d16_damped",
+                "rotor_d16_spinor", "rotor_cl8ga_undamped", "rotor_cl8ga_damped"]
+
+
+@pytest.mark.parametrize("case", ROTOR_GOLDEN)
+def test_fused_rotor_scan_matches_reference_golden(ops, golden, case):
+    g = golden(case)
+    basis = "ga" if "cl8ga" in case else "triu"
+    gens, dt, S = cuda(g["gens"], True), cuda(g["dt"], True), cuda(g["S"], True)
+    gamma = cuda(g["gamma"], True) if "gamma" in g else None
+    X = ops.fused_rotor_scan(gens, dt, gamma, S, basis=basis, two_sided=not bool(g["spinor"]))
+    assert rel(X, g["X"]) < FWD_TOL
+    (X * cuda(g["W"])).sum().backward()
+    assert rel(S.grad, g["dS"]) < BWD_TOL
+    assert rel(gens.grad, g["dgens"]) < BWD_TOL
+    assert rel(dt.grad, g["ddt"]) < BWD_TOL
+    if gamma is not None:
+        assert rel(gamma.grad, g["dgamma"]) < BWD_TOL
+
+
+def _rotor_case(rng, B, T, N, D, basis, damped, gscale=1.0):
+    from csn_b200 import algebra
+    if basis == "triu":
+        E = algebra.triu_basis(D)
+    else:
+        E = algebra.bivector_basis(algebra.CL3 if D == 4 else algebra.CL8)
+    K = E.shape[0]
+    gens = rng.standard_normal((B, T, N, K)) * gscale
+    dt = rng.uniform(0.01, 0.1, (B, T))
+    gamma = np.log1p(np.exp(rng.standard_normal((B, T, N)))) if damped else None
+    S = rng.standard_normal((B, T, N, D, D))
+    return E, gens, dt, gamma, S
+
+
+@pytest.mark.parametrize("D,basis", [(4, "triu"), (4, "ga"), (8, "triu"), (16, "triu"), (16, "ga")])
+@pytest.mark.parametrize("damped", [True, False], ids=["damped", "undamped"])
+@pytest.mark.parametrize("two", [True, False], ids=["two", "one"])
+def test_fused_rotor_scan_matches_oracle(ops, oracle, D, basis, damped, two):
+    rng = np.random.default_rng(hash((D, basis, damped, two)) % 2**32)
+    B, T, N = (2, 150, 3) if D < 16 else (1, 70, 2)
+    E, gens, dt, gamma, S = _rotor_case(rng, B, T, N, D, basis, damped, gscale=8.0)
+    h0 = rng.standard_normal((B, N, D, D))
+    W = rng.standard_normal((B, T, N, D, D))
+    Xr = oracle.rotor_scan_fwd(gens, dt, gamma, S, E, h0=h0, two_sided=two)
+    dg, ddt, dgam, dS, dh0 = oracle.rotor_scan_bwd(gens, dt, gamma, S, E, Xr, W, h0=h0, two_sided=two)
+    tg, tdt, tS, th0 = cuda(gens, True), cuda(dt, True), cuda(S, True), cuda(h0, True)
+    tgam = cuda(gamma, True) if damped else None
+    X = ops.fused_rotor_scan(tg, tdt, tgam, tS, basis=basis, two_sided=two, h0=th0)
+    assert rel(X, Xr) < FWD_TOL
+    (X * cuda(W)).sum().backward()
+    assert rel(tS.grad, dS) < BWD_TOL
+    assert rel(tg.grad, dg) < BWD_TOL
+    assert rel(tdt.grad, ddt) < BWD_TOL
+    assert rel(th0.grad, dh0) < BWD_TOL
+    if damped:
+        assert rel(tgam.grad, dgam) < BWD_TOL
+
+
+def test_fused_matches_materialised_transitions(ops, oracle):
+    """The fused kernel equals Cayley + decay + plain scan run separately."""
+    rng = np.random.default_rng(7)
+    E, gens, dt, gamma, S = _rotor_case(rng, 2, 64, 3, 8, "triu", True, gscale=5.0)
+    M, C = oracle.rotor_build(gens, dt, gamma, S, E)
+    X1 = ops.rotor_scan(cuda(M), cuda(C))
+    X2 = ops.fused_rotor_scan(cuda(gens), cuda(dt), cuda(gamma), cuda(S))
+    assert (X1 - X2).abs().max().item() / X1.abs().max().item() < 1e-5
+
+
+# --------------------------------------------------------- long sequences (L = 8192)
+@pytest.mark.parametrize("D,shape", [(8, (1, 8192, 2)), (16, (1, 8192, 1)), (4, (2, 8192, 2))])
+def test_long_sequence_tolerance_L8192(ops, oracle, D, shape):
+    """BASELINE tolerance: max-rel <= 1e-4 at fp32 over L = 8192 against fp64."""
+    rng = np.random.default_rng(D)
+    B, T, N = shape
+    E, gens, dt, gamma, S = _rotor_case(rng, B, T, N, D, "triu", True, gscale=1.0)
+    W = rng.standard_normal((B, T, N, D, D))
+    Xr = oracle.rotor_scan_fwd(gens, dt, gamma, S, E)
+    dg, ddt, dgam, dS, _ = oracle.rotor_scan_bwd(gens, dt, gamma, S, E, Xr, W)
+    tg, tdt, tgam, tS = cuda(gens, True), cuda(dt, True), cuda(gamma, True), cuda(S, True)
+    X = ops.fused_rotor_scan(tg, tdt, tgam, tS)
+    assert rel(X, Xr) < FWD_TOL
+    (X * cuda(W)).sum().backward()
+    for got, ref in ((tS.grad, dS), (tg.grad, dg), (tdt.grad, ddt), (tgam.grad, dgam)):
+        assert rel(got, ref) < FWD_TOL
+
+
+def test_undamped_orthogonal_scan_preserves_norm_L8192(ops):
+    """Undamped two-sided scan with zero injection after t = 0 is a pure rotation:
+    |X_t|_F stays |C_0|_F (orthogonal Cayley rotors), a size-independent invariant."""
+    B, T, N, D = 2, 8192, 4, 8
+    g = torch.Generator(device="cpu").manual_seed(0)
+    gens = torch.randn(B, T, N, 28, generator=g).to(DEV)
+    dt = torch.rand(B, T, generator=g).mul(0.09).add(0.01).to(DEV)
+    S = torch.zeros(B, T, N, D, D, device=DEV)
+    S[:, 0] = torch.randn(B, N, D, D, generator=g).to(DEV)
+    X = ops.fused_rotor_scan(gens, dt, None, S)
+    n0 = S[:, 0].flatten(2).norm(dim=-1)
+    nT = X[:, -1].flatten(2).norm(dim=-1)
+    assert ((nT - n0).abs() / n0).max().item() < 1e-4

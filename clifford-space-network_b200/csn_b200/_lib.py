@@ -33,6 +33,8 @@ SIGNATURES = {
                            _int),
     "csn_rotor_scan_bwd": ([_f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _i64, _i64, _i64, _int,
                             _int, _int, _f, _sz, _f], _int),
+    "csn_rotor_scan_fwd_noalloc": ([_f, _f, _f, _f, _f, _f, _i64, _i64, _i64, _int, _int, _int,
+                                    _f], _int),
     "csn_cayley_fwd": ([_f, _f, _i64, _int, _f], _int),
     "csn_cayley_bwd": ([_f, _f, _f, _i64, _int, _f], _int),
     "csn_timing_enable": ([_int], _int),

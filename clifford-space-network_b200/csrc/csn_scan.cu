@@ -19,6 +19,8 @@
 // The backward pass is the mirror image in reverse time with transitions M^T
 // (G_t = dX_t + M_{t+1}^T G_{t+1} M_{t+1}), chunk aggregates (P_j, c'_j) where
 // H_{j-1} = P_j^T H_j P_j + c'_j, and an apply pass that emits the gradients.
+#include <mutex>
+
 #include "csn_common.cuh"
 #include "csn_internal.h"
 #include "csn_scan_args.cuh"
@@ -567,4 +569,76 @@ extern "C" int csn_rotor_scan_bwd(const float* gens, const float* dt, const floa
   bind_ws(a, p, ws.base, D);
   if (D == 16) return scan16_dispatch(a, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, true, st);
   return dispatch(a, D, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, true, st);
+}
+
+// ======================================================= no-allocation forward variant
+//
+// csn_rotor_scan_fwd_noalloc is csn_rotor_scan_fwd for callers that must not allocate
+// device memory: hosts that reserve the whole GPU through their own pool (so a library
+// cudaMalloc either fails or eats their budget) and serving loops where allocating
+// after start-up is forbidden.  The scratch that the chunked scan needs (chunk
+// aggregates and carries) lives in the file-scope array below instead of a
+// caller-provided or cudaMallocAsync'd workspace.  Every GPU that loads this library
+// holds the array until the process exits.
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;  // 32 MiB per device
+constexpr int kNoAllocMaxDevices = 64;
+
+}  // namespace
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device.  In host code the
+// symbol name is only a host-side stand-in, so the address is looked up once per
+// device (with that device current) and cached.
+int noalloc_scratch(float** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_cuda_error(e, "csn_rotor_scan_fwd_noalloc: cudaGetDevice");
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return set_error(CSN_ERR_UNSUPPORTED, "csn_rotor_scan_fwd_noalloc: device ordinal above 63");
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess)
+      return set_cuda_error(e, "csn_rotor_scan_fwd_noalloc: cudaGetSymbolAddress(scratch)");
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = static_cast<float*>(g_noalloc_ptr[dev]);
+  return CSN_OK;
+}
+
+}  // namespace
+
+extern "C" int csn_rotor_scan_fwd_noalloc(const float* gens, const float* dt, const float* gamma,
+                                          const float* S, const float* h0, float* X, int64_t B,
+                                          int64_t T, int64_t N, int D, int basis, int two_sided,
+                                          void* stream) {
+  if (int rc = rotor_common_checks(gens, dt, S, B, T, N, D, basis)) return rc;
+  if (B * T * N == 0) return CSN_OK;
+  if (!X || !aligned16(X) || (h0 && !aligned16(h0)))
+    return set_error(CSN_ERR_INVALID, "csn_rotor_scan_fwd_noalloc: X missing or misaligned");
+  // Same chunking as csn_rotor_scan_fwd, so both entry points give identical results.
+  Plan p = make_plan(B, T, N, D, false);
+  if (plan_bytes(p) > kNoAllocScratchBytes)
+    return set_error(CSN_ERR_INVALID,
+                     "csn_rotor_scan_fwd_noalloc: problem needs more than the 32 MiB static scratch "
+                     "(csn_scan_workspace_bytes(B, T, N, D) must be <= 33554432); use "
+                     "csn_rotor_scan_fwd with a workspace instead");
+  float* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  ScanArgs a{};
+  a.gens = gens; a.dt = dt; a.gamma = gamma; a.S = S; a.h0 = h0; a.out = X;
+  a.B = B; a.T = T; a.N = N;
+  bind_ws(a, p, scratch, D);
+  if (D == 16) return scan16_dispatch(a, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, false, st);
+  return dispatch(a, D, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, false, st);
 }

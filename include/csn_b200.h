@@ -98,6 +98,23 @@ int csn_rotor_scan_bwd(const float* gens, const float* dt, const float* gamma, c
                        int64_t B, int64_t T, int64_t N, int D, int basis, int two_sided,
                        void* workspace, size_t workspace_bytes, void* stream);
 
+/* Same computation and chunking as csn_rotor_scan_fwd (bit-identical results), for
+ * callers that cannot allocate device memory: hosts that hand the whole GPU to their
+ * own memory pool, or loops that must not allocate once running.  No counterpart in
+ * the reference (whose extension allocates every output with torch::empty_like,
+ * csn_toolkit/csn/cuda/scan_cuda.cu:237).  The caller still passes every input and X.
+ * Scratch comes from a static 32 MiB device array that the library holds on every GPU
+ * that loads it, until process exit; problems whose csn_scan_workspace_bytes(B, T, N, D)
+ * exceeds 33554432 bytes are rejected with CSN_ERR_INVALID.  The first call on a device
+ * looks up that array's device address (cudaGetSymbolAddress), so make it before any
+ * stream capture.  All calls share the one array: calls that overlap on the GPU (other
+ * streams, other threads) race and must be serialised by the caller.  No scratch word
+ * needs to start at zero: every word a call reads is written earlier in that call. */
+int csn_rotor_scan_fwd_noalloc(const float* gens, const float* dt, const float* gamma,
+                               const float* S, const float* h0, float* X,
+                               int64_t B, int64_t T, int64_t N, int D, int basis, int two_sided,
+                               void* stream);
+
 /* -------------------------------------------------------------------- Cayley */
 /* Q = (I - Omega)^{-1} (I + Omega) for `count` skew D x D matrices.
  * Replaces cayley_rotor_8x8 (python/clifford_cl6.py:57) and cayley_rotor_16x16 /

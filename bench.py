@@ -21,7 +21,6 @@ import ctypes
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -34,7 +33,6 @@ sys.path.insert(0, str(REPO))
 METRIC = "rotor-scan fwd+bwd Gelem/s (B*L*C)"
 UNIT = "Gelem/s"
 B, T, N, D, K_GEN, LAYERS = 32, 2048, 8, 8, 28, 4
-ELEMS_PER_LAYER = B * T * N
 # compulsory HBM bytes per element (float32), n = D*D, k = K_GEN, dt amortised over N
 _n, _k = D * D, K_GEN
 OP_BYTES = 4.0 * (5 * _n + 3 * _k + 3 + 3.0 / N)          # whole fused fwd+bwd op
@@ -56,11 +54,11 @@ def dist_env():
     return ws, rank, local
 
 
-def make_inputs(seed, device, batch=B):
+def make_inputs(seed, device, batch=B, nlayers=LAYERS):
     import torch
     g = torch.Generator(device="cpu").manual_seed(seed)
     layers = []
-    for _ in range(LAYERS):
+    for _ in range(nlayers):
         gens = torch.randn(batch, T, N, K_GEN, generator=g)
         dt = torch.rand(batch, T, generator=g) * 0.02 + 0.04
         gamma = torch.nn.functional.softplus(torch.randn(batch, T, N, generator=g) * 0.5)
@@ -72,57 +70,51 @@ def make_inputs(seed, device, batch=B):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """SM clocks and throttle reasons sampled through NVML (read-only) every 100 ms
+    during the timed region."""
+
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "sw_power_cap": 0x4}
 
     def __init__(self, index):
         self.index = index
-        self.rows = []
-        self.proc = None
+        self.sm, self.mx, self.reasons = [], [], set()
+        self._stop = threading.Event()
         self.thread = None
+        self.err = None
+
+    def _run(self):
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByIndex(self.index)
+            mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            while not self._stop.is_set():
+                self.sm.append(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                self.mx.append(mx)
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                for name, bit in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+                self._stop.wait(0.1)
+            nv.nvmlShutdown()
+        except Exception as e:  # NVML missing: record why, never fail the bench
+            self.err = repr(e)
 
     def __enter__(self):
-        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "200",
-                 "-i", str(self.index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-        except OSError:
-            self.proc = None
+        self.thread = threading.Thread(target=self._run, daemon=True)
+        self.thread.start()
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.rows.append([c.strip() for c in line.split(",")])
-
     def __exit__(self, *exc):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-            self.thread.join(timeout=5)
+        self._stop.set()
+        self.thread.join(timeout=5)
 
     def summary(self):
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in self.rows:
-            try:
-                sm.append(float(r[0]))
-                mx.append(float(r[1]))
-            except (ValueError, IndexError):
-                continue
-            for name, v in zip(names, r[4:8]):
-                if v.lower() == "active":
-                    reasons.add(name)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if not self.sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "error": self.err}
+        return {"sm_mhz": statistics.median(self.sm), "sm_max_mhz": max(self.mx),
+                "reasons": sorted(self.reasons), "samples": len(self.sm)}
 
 
 def peaks():
@@ -168,7 +160,11 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=B, help="per-rank batch (profiling: smaller)")
+    ap.add_argument("--layers", type=int, default=LAYERS, help="layers per step (profiling: 1)")
     args = ap.parse_args()
+    bsz, nlay = args.batch, args.layers
+    ELEMS_PER_LAYER = bsz * T * N
     ws, rank, local = dist_env()
     cores = os.cpu_count() or 1
 
@@ -202,9 +198,9 @@ def main():
     torch.cuda.set_device(dev)
     lib = _lib.load()
 
-    layers = make_inputs(1234 + rank, dev)
+    layers = make_inputs(1234 + rank, dev, bsz, nlay)
     basis = ops.BASIS["triu"]
-    ws_bytes = lib.csn_rotor_scan_workspace_bytes(B, T, N, D)
+    ws_bytes = lib.csn_rotor_scan_workspace_bytes(bsz, T, N, D)
     work = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     outs = [dict(X=torch.empty_like(L["S"]), dgens=torch.empty_like(L["gens"]),
                  ddt=torch.empty_like(L["dt"]), dgamma=torch.empty_like(L["gamma"]),
@@ -216,10 +212,10 @@ def main():
     def step():
         for L, O in zip(layers, outs):
             _lib.call("csn_rotor_scan_fwd", P(L["gens"]), P(L["dt"]), P(L["gamma"]), P(L["S"]),
-                      P(None), P(O["X"]), B, T, N, D, basis, 1, P(work), ws_bytes, sp)
+                      P(None), P(O["X"]), bsz, T, N, D, basis, 1, P(work), ws_bytes, sp)
             _lib.call("csn_rotor_scan_bwd", P(L["gens"]), P(L["dt"]), P(L["gamma"]), P(L["S"]),
                       P(None), P(O["X"]), P(L["dX"]), P(O["dgens"]), P(O["ddt"]), P(O["dgamma"]),
-                      P(O["dS"]), P(None), B, T, N, D, basis, 1, P(work), ws_bytes, sp)
+                      P(O["dS"]), P(None), bsz, T, N, D, basis, 1, P(work), ws_bytes, sp)
 
     def barrier():
         if ws > 1:
@@ -248,7 +244,7 @@ def main():
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms = t.item()
     ms_per_step = ms / args.steps
-    elems_step = ELEMS_PER_LAYER * LAYERS
+    elems_step = ELEMS_PER_LAYER * nlay
     value = elems_step * ws / (ms_per_step * 1e-3) / 1e9
 
     # per-kernel device times over the timed region
@@ -309,7 +305,8 @@ def main():
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
                 "warmup": max(3, args.warmup), "ms_per_step": ms_per_step, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-                "config": dict(CONFIG, parallelism=f"replicas{ws}" if ws > 1 else "single"),
+                "config": dict(CONFIG, batch=bsz, layers=nlay,
+                               parallelism=f"replicas{ws}" if ws > 1 else "single"),
                 "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm,
                              "unit": "GB/s", "frac": achieved / hbm, "traffic": None,
                              "peak_kind": peak_kind,

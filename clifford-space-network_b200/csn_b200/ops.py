@@ -12,6 +12,7 @@ Ops (reference functions they replace, paths relative to the reference root):
 * :func:`fused_rotor_scan`  -- python/clifford_cl6.py:150-171 / python/clifford_cl8.py:160-179
                                (Cayley rotor + decay + scan in one pass)
 * :func:`cayley`            -- python/clifford_cl6.py:57, python/clifford_cl8.py:29,65
+* :func:`cell_step`         -- python/clifford_layer.py:50-115 CliffordTENNCell.forward
 """
 from __future__ import annotations
 
@@ -21,7 +22,7 @@ import torch
 
 from . import _lib
 
-__all__ = ["rotor_scan", "fused_rotor_scan", "cayley", "BASIS"]
+__all__ = ["rotor_scan", "fused_rotor_scan", "cayley", "cell_step", "BASIS"]
 
 BASIS = {"triu": 0, "ga": 1}
 
@@ -94,7 +95,8 @@ class ScanFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dX):
         Mf, X, hf = ctx.saved_tensors
-        dM, dC, dh0 = _scan_bwd(Mf, X, _f32(dX), hf, ctx.two_sided, ctx.needs_input_grad[2])
+        need_dh0 = len(ctx.needs_input_grad) > 2 and ctx.needs_input_grad[2]
+        dM, dC, dh0 = _scan_bwd(Mf, X, _f32(dX), hf, ctx.two_sided, need_dh0)
         dM = dM.to(ctx.dtypes[0])
         dC = dC.to(ctx.dtypes[1])
         if dh0 is not None:
@@ -197,3 +199,46 @@ class CayleyFunction(torch.autograd.Function):
 def cayley(Omega):
     """Q = (I - Omega)^{-1} (I + Omega) for skew Omega[..., D, D], D in {4, 8, 16}."""
     return CayleyFunction.apply(Omega)
+
+
+# ----------------------------------------------------------------- Clifford cell
+class CellFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, prev, W_rec, W_in, gamma_bias, dt):
+        _require_cuda(x, prev, W_rec, W_in, gamma_bias)
+        xf, pf, wr, wi, gb = (_f32(t) for t in (x, prev, W_rec, W_in, gamma_bias))
+        Bt, N, A = pf.shape
+        if A != 16:
+            raise ValueError("the Clifford cell works on 16-component (4 x 4) states")
+        in_dim = xf.shape[1]
+        nxt = torch.empty_like(pf)
+        _lib.call("csn_cell_fwd", _ptr(pf), _ptr(xf), _ptr(wr), _ptr(wi), _ptr(gb), float(dt),
+                  _ptr(nxt), Bt, N, in_dim, _stream(pf.device))
+        ctx.save_for_backward(xf, pf, wr, wi, gb)
+        ctx.dt = float(dt)
+        ctx.dtypes = (x.dtype, prev.dtype, W_rec.dtype, W_in.dtype, gamma_bias.dtype)
+        return nxt.to(prev.dtype)
+
+    @staticmethod
+    def backward(ctx, dnext):
+        xf, pf, wr, wi, gb = ctx.saved_tensors
+        Bt, N, _ = pf.shape
+        in_dim = xf.shape[1]
+        dprev = torch.empty_like(pf)
+        dx = torch.empty_like(xf)
+        dwr = torch.empty_like(wr)
+        dwi = torch.empty_like(wi)
+        dgb = torch.empty_like(gb)
+        nbytes = _lib.load().csn_cell_workspace_bytes(Bt, N)
+        ws = _workspace(nbytes, pf.device)
+        _lib.call("csn_cell_bwd", _ptr(pf), _ptr(xf), _ptr(wr), _ptr(wi), _ptr(gb), ctx.dt,
+                  _ptr(_f32(dnext)), _ptr(dprev), _ptr(dx), _ptr(dwr), _ptr(dwi), _ptr(dgb),
+                  Bt, N, in_dim, _ptr(ws), nbytes, _stream(pf.device))
+        outs = [dx, dprev, dwr, dwi, dgb]
+        outs = [o.to(d) for o, d in zip(outs, ctx.dtypes)]
+        return outs[0], outs[1], outs[2], outs[3], outs[4], None
+
+
+def cell_step(x, prev, W_rec, W_in, gamma_bias, dt: float = 0.02):
+    """One CliffordTENNCell step: x [Bt, in_dim], prev [Bt, N, 16] -> next [Bt, N, 16]."""
+    return CellFunction.apply(x, prev, W_rec, W_in, gamma_bias, dt)

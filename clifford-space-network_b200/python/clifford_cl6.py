@@ -1,0 +1,138 @@
+"""Cl(6,0) ~ M_8(R) block with adaptive dt, drop-in for python/clifford_cl6.py.
+
+``CliffordCL6Block.forward`` keeps the reference's parameters, inputs and outputs
+(python/clifford_cl6.py:71-186) but runs lines 150-171 -- skew generator, Omega,
+exact Cayley rotor, decay, M/C construction and the scan -- as ONE fused CUDA op
+(csn_b200.ops.fused_rotor_scan): M and C are never materialised.  Omega is still
+returned for the action regulariser of the LM.
+"""
+import math
+from typing import Dict, Optional, Tuple
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from csn_b200 import ops
+from python.clifford_model import GeometricGatedLinearUnit, RiemannianGeodesicHead
+from python.clifford_scan import parallel_rotor_scan, surrogate_spike  # noqa: F401 (re-export)
+
+
+class AdaptiveTimeHead(nn.Module):
+    """dt_t = softplus(W x_t + b) * dt_base, initialised at dt_base (python/clifford_cl6.py:27-54)."""
+
+    def __init__(self, d_model: int, dt_base: float = 0.05):
+        super().__init__()
+        self.dt_base = dt_base
+        self.proj = nn.Linear(d_model, 1)
+        nn.init.zeros_(self.proj.weight)
+        nn.init.constant_(self.proj.bias, math.log(math.e - 1.0))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        dt = F.softplus(self.proj(x)) * self.dt_base
+        return dt.unsqueeze(-1).unsqueeze(-1)  # [B, T, 1, 1, 1]
+
+
+def cayley_rotor_8x8(Omega: torch.Tensor) -> torch.Tensor:
+    """Exact Q = (I - Omega)^{-1} (I + Omega) for skew 8 x 8 Omega (python/clifford_cl6.py:57-68)."""
+    return ops.cayley(Omega)
+
+
+def skew_from_generators(biv: torch.Tensor, D: int, triu_u: torch.Tensor, triu_v: torch.Tensor):
+    skew = torch.zeros(*biv.shape[:-1], D, D, device=biv.device, dtype=biv.dtype)
+    skew[..., triu_u, triu_v] = biv
+    skew[..., triu_v, triu_u] = -biv
+    return skew
+
+
+class CliffordCL6Block(nn.Module):
+    def __init__(self, d_model: int, num_neurons: int = 6, kernel_size: int = 4, dt_base: float = 0.05,
+                 spike_threshold: float = 0.1, spike_beta: float = 10.0):
+        super().__init__()
+        self.d_model = d_model
+        self.num_neurons = num_neurons
+        self.dt_base = dt_base
+        self.spike_threshold = spike_threshold
+        self.spike_beta = spike_beta
+        self.ln_1 = nn.LayerNorm(d_model)
+        self.conv1d = nn.Conv1d(d_model, d_model, kernel_size=kernel_size, padding=kernel_size - 1,
+                                groups=d_model)
+        self.time_head = AdaptiveTimeHead(d_model, dt_base=dt_base)
+        self.in_proj = nn.Linear(d_model, num_neurons * 64)
+        self.gamma_proj = nn.Linear(d_model, num_neurons)
+        self.biv_proj = nn.Linear(d_model, num_neurons * 28)
+        self.omega_scale = nn.Parameter(torch.ones(num_neurons, 1) * 10.0)
+        self.W_mix = nn.Parameter(torch.randn(num_neurons, num_neurons) / math.sqrt(num_neurons))
+        self.out_proj = nn.Linear(num_neurons * 64, d_model)
+        self.ln_2 = nn.LayerNorm(d_model)
+        self.gglu = GeometricGatedLinearUnit(d_model, d_ffn=2 * d_model)
+        self.register_buffer("triu_u", torch.triu_indices(8, 8, offset=1)[0], persistent=False)
+        self.register_buffer("triu_v", torch.triu_indices(8, 8, offset=1)[1], persistent=False)
+
+    def forward(self, x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        B, T, _ = x.shape
+        N = self.num_neurons
+        residual = x
+        x_conv = F.silu(self.conv1d(self.ln_1(x).transpose(1, 2))[:, :, :T].transpose(1, 2))
+        dt = self.time_head(x_conv)                                   # [B, T, 1, 1, 1]
+        S = self.in_proj(x_conv).view(B, T, N, 8, 8)
+        gamma = F.softplus(self.gamma_proj(x_conv))                   # [B, T, N]
+        biv = self.biv_proj(x_conv).view(B, T, N, 28) * self.omega_scale
+        X_all = ops.fused_rotor_scan(biv, dt.view(B, T), gamma, S)     # lines 150-171 fused
+        Omega = skew_from_generators(biv, 8, self.triu_u, self.triu_v) * (0.5 * dt)
+        energy = torch.norm(X_all, dim=(-1, -2), keepdim=True)
+        X_spiked = X_all * surrogate_spike(energy, threshold=self.spike_threshold, beta=self.spike_beta)
+        feat = torch.einsum("ij,btjrc->btirc", self.W_mix, X_spiked).reshape(B, T, N * 64)
+        h = residual + self.out_proj(feat)
+        out = h + self.gglu(self.ln_2(h))
+        return out, Omega, dt.view(B, T)
+
+
+class CliffordCL6ForCausalLM(nn.Module):
+    def __init__(self, vocab_size: int, d_model: int = 48, num_layers: int = 2, num_neurons: int = 6,
+                 dt_base: float = 0.05, kernel_size: int = 4, spike_threshold: float = 0.1,
+                 lambda_kin: float = 0.01, lambda_smooth: float = 0.005, lambda_time: float = 0.01):
+        super().__init__()
+        self.vocab_size = vocab_size
+        self.d_model = d_model
+        self.num_layers = num_layers
+        self.dt_base = dt_base
+        self.lambda_kin = lambda_kin
+        self.lambda_smooth = lambda_smooth
+        self.lambda_time = lambda_time
+        self.tok_emb = nn.Embedding(vocab_size, d_model)
+        self.blocks = nn.ModuleList([
+            CliffordCL6Block(d_model=d_model, num_neurons=num_neurons, kernel_size=kernel_size,
+                             dt_base=dt_base, spike_threshold=spike_threshold)
+            for _ in range(num_layers)])
+        self.ln_f = nn.LayerNorm(d_model)
+        self.head = RiemannianGeodesicHead(vocab_size=vocab_size, d_model=d_model)
+
+    def forward(self, idx: torch.Tensor, targets: Optional[torch.Tensor] = None):
+        B, T = idx.shape
+        x = self.tok_emb(idx)
+        e_kin = 0.0
+        e_smooth = 0.0
+        t_loss = 0.0
+        dts = []
+        for block in self.blocks:
+            x, Omega, dt_t = block(x)
+            dts.append(dt_t)
+            e_kin = e_kin + (Omega ** 2).mean()
+            if T > 1:
+                e_smooth = e_smooth + ((Omega[:, 1:] - Omega[:, :-1]) ** 2).mean()
+                t_loss = t_loss + (((dt_t[:, 1:] - dt_t[:, :-1]) / self.dt_base) ** 2).mean()
+        logits = self.head(self.ln_f(x))
+        stacked = torch.stack(dts)
+        diagnostics: Dict[str, float] = {"mean_dt": stacked.mean().item(), "min_dt": stacked.min().item(),
+                                         "max_dt": stacked.max().item()}
+        loss = None
+        if targets is not None:
+            ce = F.cross_entropy(logits.view(-1, self.vocab_size), targets.view(-1))
+            action = self.lambda_kin * e_kin + self.lambda_smooth * e_smooth
+            time_pen = self.lambda_time * t_loss
+            loss = ce + action + time_pen
+            diagnostics["ce_loss"] = ce.item()
+            diagnostics["action_loss"] = float(action)
+            diagnostics["time_loss"] = float(time_pen)
+        return logits, loss, diagnostics

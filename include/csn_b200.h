@@ -126,6 +126,30 @@ int csn_cayley_fwd(const float* Omega, float* Q, int64_t count, int D, void* str
 int csn_cayley_bwd(const float* Q, const float* dQ, float* dOmega, int64_t count, int D,
                    void* stream);
 
+/* ------------------------------------------------------------- Clifford cell */
+/* One step of the Clifford-LTC cell, python/clifford_layer.py:50-115 (CliffordTENNCell.
+ * forward, 4 x 4 matrix form with the symmetric rational rotor of that file):
+ *   S_i = sum_j W_rec[i,j] X_j + sum_k W_in[i,k] x_k;  gamma = softplus(gamma_bias_i + tr S_i / 4)
+ *   Om = (S - S^T) dt / 4;  Q = (I + Om)(I - Om) / (1 + |Om|_F^2 / 8)
+ *   next = sig(-gamma dt) Q X_i Q^T + (1 - sig(-gamma dt)) S_i
+ * prev/next [Bt, N, 16], x [Bt, in_dim], W_rec [N, N, 16], W_in [N, in_dim, 16], gamma_bias [N].
+ * Replaces launch_clifford_cfc_forward (include/clifford_tenn_cell.cuh:50-55) with the
+ * semantics of the Python module, which is the one the reference's models call. */
+int csn_cell_fwd(const float* prev, const float* x, const float* W_rec, const float* W_in,
+                 const float* gamma_bias, float dt, float* next, int64_t Bt, int64_t N,
+                 int64_t in_dim, void* stream);
+
+size_t csn_cell_workspace_bytes(int64_t Bt, int64_t N);
+
+/* Exact adjoint of csn_cell_fwd (what autograd computes through the same lines): dprev,
+ * dx, dW_rec, dW_in, dgamma_bias.  Outputs are written, not accumulated (the reference's
+ * launch_clifford_cfc_backward, include/clifford_tenn_cell.cuh:57-63, accumulates with
+ * atomics into caller-zeroed buffers).  dx, dW_rec, dW_in, dgamma_bias may be NULL. */
+int csn_cell_bwd(const float* prev, const float* x, const float* W_rec, const float* W_in,
+                 const float* gamma_bias, float dt, const float* dnext, float* dprev, float* dx,
+                 float* dW_rec, float* dW_in, float* dgamma_bias, int64_t Bt, int64_t N,
+                 int64_t in_dim, void* workspace, size_t workspace_bytes, void* stream);
+
 /* -------------------------------------------------------------- kernel timing */
 /* Measurement hook with no counterpart in the reference (which times with wall clock,
  * tests/profile_performance.py:41-71).  While enabled, every kernel the library

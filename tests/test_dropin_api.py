@@ -1,0 +1,72 @@
+"""CPU checks of the reference-compatible module API: names, signatures and
+state_dict keys match the reference (paths relative to the reference root)."""
+import inspect
+
+import numpy as np
+import pytest
+import torch
+
+
+def params(fn):
+    return list(inspect.signature(fn).parameters)
+
+
+def test_scan_signatures_match_reference():
+    import csn.scan as cs
+    import python.clifford_scan as ps
+    # python/clifford_scan.py:19, :41
+    assert params(ps.parallel_rotor_scan) == ["M", "C", "is_spinor_bundle"]
+    assert inspect.signature(ps.parallel_rotor_scan).parameters["is_spinor_bundle"].default is False
+    assert params(ps.rotor_binary_op) == ["M_b", "C_b", "M_a", "C_a", "is_spinor_bundle"]
+    # csn_toolkit/csn/scan.py:96-102 (toolkit default is the one-sided scan)
+    assert params(cs.parallel_rotor_scan) == ["M", "C", "is_spinor_bundle", "force_tree", "backend"]
+    assert inspect.signature(cs.parallel_rotor_scan).parameters["is_spinor_bundle"].default is True
+    assert params(cs.rotor_binary_op) == ["M_right", "C_right", "M_left", "C_left", "is_spinor_bundle"]
+
+
+def test_rotor_and_cell_signatures_match_reference():
+    from python import clifford_cl6, clifford_cl8, clifford_layer
+    from csn import rotors
+    assert params(clifford_cl6.cayley_rotor_8x8) == ["Omega"]
+    assert params(clifford_cl8.cayley_rotor_16x16) == ["Omega", "use_schulz"]
+    assert params(clifford_cl8.cayley_rotor_4x4) == ["Omega", "use_schulz"]
+    for fn in (rotors.cayley_rotor_4x4, rotors.cayley_rotor_8x8, rotors.cayley_rotor_16x16):
+        assert params(fn) == ["Omega", "use_schulz"]
+    assert params(clifford_layer.CliffordTENNCell.forward) == ["self", "x_t", "prev_state", "dt"]
+    assert params(clifford_layer.CliffordTENNCell.__init__) == ["self", "num_neurons", "in_dim",
+                                                                 "algebra_dim"]
+
+
+@pytest.mark.parametrize("name,ctor", [
+    ("cl6_block", lambda: __import__("python.clifford_cl6", fromlist=["x"]).CliffordCL6Block(32, num_neurons=4)),
+    ("cl8_block", lambda: __import__("python.clifford_cl8", fromlist=["x"]).CliffordCL8Block(32, num_neurons=2)),
+])
+def test_block_state_dict_matches_reference(golden, name, ctor):
+    g = golden(name)
+    ref_keys = {k[len("param."):]: v.shape for k, v in g.items() if k.startswith("param.")}
+    blk = ctor()
+    mine = {k: tuple(v.shape) for k, v in blk.state_dict().items()}
+    assert mine == {k: tuple(s) for k, s in ref_keys.items()}
+    blk.load_state_dict({k: torch.as_tensor(g["param." + k]) for k in ref_keys})
+
+
+def test_cell_parameters_match_reference():
+    from python.clifford_layer import CliffordTENNCell
+    cell = CliffordTENNCell(num_neurons=5, in_dim=4)
+    assert {k: tuple(v.shape) for k, v in cell.state_dict().items()} == {
+        "W_rec": (5, 5, 16), "W_in": (5, 4, 16), "gamma_bias": (5,), "bivector_bias": (5, 6)}
+
+
+def test_rotor_binary_op_composes_like_the_reference():
+    from python.clifford_scan import rotor_binary_op
+    rng = np.random.default_rng(0)
+    Mb, Cb, Ma, Ca = (torch.tensor(rng.standard_normal((2, 4, 4))) for _ in range(4))
+    M, C = rotor_binary_op(Mb, Cb, Ma, Ca)
+    assert torch.allclose(M, Mb @ Ma) and torch.allclose(C, Mb @ Ca @ Mb.transpose(-1, -2) + Cb)
+
+
+def test_dropin_modules_refuse_cpu_tensors():
+    from python.clifford_scan import parallel_rotor_scan
+    M = torch.zeros(1, 3, 1, 4, 4)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        parallel_rotor_scan(M, M)

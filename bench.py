@@ -70,7 +70,7 @@ def make_inputs(seed, device, batch=B, nlayers=LAYERS):
 
 
 class ClockSampler:
-    """SM clocks and throttle reasons sampled through NVML (read-only) every 100 ms
+    """SM clocks and throttle reasons sampled through NVML (read-only) every 10 ms
     during the timed region."""
 
     REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
@@ -85,9 +85,7 @@ class ClockSampler:
 
     def _run(self):
         try:
-            import pynvml as nv
-            nv.nvmlInit()
-            h = nv.nvmlDeviceGetHandleByIndex(self.index)
+            nv, h = self._nv, self._h
             mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
             while not self._stop.is_set():
                 self.sm.append(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
@@ -96,19 +94,27 @@ class ClockSampler:
                 for name, bit in self.REASONS.items():
                     if r & bit:
                         self.reasons.add(name)
-                self._stop.wait(0.1)
+                self._stop.wait(0.01)
             nv.nvmlShutdown()
         except Exception as e:  # NVML missing: record why, never fail the bench
             self.err = repr(e)
 
     def __enter__(self):
+        try:  # NVML initialised before the timed region starts
+            import pynvml as nv
+            nv.nvmlInit()
+            self._nv, self._h = nv, nv.nvmlDeviceGetHandleByIndex(self.index)
+        except Exception as e:
+            self.err = repr(e)
+            return self
         self.thread = threading.Thread(target=self._run, daemon=True)
         self.thread.start()
         return self
 
     def __exit__(self, *exc):
         self._stop.set()
-        self.thread.join(timeout=5)
+        if self.thread is not None:
+            self.thread.join(timeout=5)
 
     def summary(self):
         if not self.sm:

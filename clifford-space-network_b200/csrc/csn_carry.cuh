@@ -45,14 +45,27 @@ __global__ void __launch_bounds__(128) fwd_carry_kernel(ScanArgs a) {
       a.carry[(s * a.nchunks) * DD + idx] = h[idx];
     }
     __syncwarp();
+    // the aggregate of chunk j + 1 is loaded while chunk j's link is computed, so the
+    // serial chain never waits on global memory
+    float pn[PER], cn[PER];
+#pragma unroll
+    for (int q = 0; q < PER; ++q) {
+      pn[q] = (a.nchunks > 1) ? a.aggP[(s * a.nchunks) * DD + lane + 32 * q] : 0.0f;
+      cn[q] = (a.nchunks > 1) ? a.aggC[(s * a.nchunks) * DD + lane + 32 * q] : 0.0f;
+    }
     for (int64_t j = 0; j + 1 < a.nchunks; ++j) {
-      const float* Pg = a.aggP + (s * a.nchunks + j) * DD;
-      const float* cg = a.aggC + (s * a.nchunks + j) * DD;
       float cv[PER];
 #pragma unroll
       for (int q = 0; q < PER; ++q) {
-        P[lane + 32 * q] = Pg[lane + 32 * q];
-        cv[q] = cg[lane + 32 * q];
+        P[lane + 32 * q] = pn[q];
+        cv[q] = cn[q];
+      }
+      if (j + 2 < a.nchunks) {
+#pragma unroll
+        for (int q = 0; q < PER; ++q) {
+          pn[q] = a.aggP[(s * a.nchunks + j + 1) * DD + lane + 32 * q];
+          cn[q] = a.aggC[(s * a.nchunks + j + 1) * DD + lane + 32 * q];
+        }
       }
       __syncwarp();
       // y = P h
@@ -128,14 +141,25 @@ __global__ void __launch_bounds__(128) bwd_carry_kernel(ScanArgs a) {
       a.carry[(s * a.nchunks + a.nchunks - 1) * DD + idx] = 0.0f;
     }
     __syncwarp();
+    float pn[PER], cn[PER];
+#pragma unroll
+    for (int q = 0; q < PER; ++q) {
+      pn[q] = a.aggP[(s * a.nchunks + a.nchunks - 1) * DD + lane + 32 * q];
+      cn[q] = a.aggC[(s * a.nchunks + a.nchunks - 1) * DD + lane + 32 * q];
+    }
     for (int64_t j = a.nchunks - 1; j >= 1; --j) {
-      const float* Pg = a.aggP + (s * a.nchunks + j) * DD;
-      const float* cg = a.aggC + (s * a.nchunks + j) * DD;
       float cv[PER];
 #pragma unroll
       for (int q = 0; q < PER; ++q) {
-        P[lane + 32 * q] = Pg[lane + 32 * q];
-        cv[q] = cg[lane + 32 * q];
+        P[lane + 32 * q] = pn[q];
+        cv[q] = cn[q];
+      }
+      if (j >= 2) {
+#pragma unroll
+        for (int q = 0; q < PER; ++q) {
+          pn[q] = a.aggP[(s * a.nchunks + j - 1) * DD + lane + 32 * q];
+          cn[q] = a.aggC[(s * a.nchunks + j - 1) * DD + lane + 32 * q];
+        }
       }
       __syncwarp();
       // y = P^T h

@@ -208,6 +208,31 @@ __device__ __forceinline__ float mat_dot_global(const Mat<D>& X, const float* __
   return s;
 }
 
+// ------------------------------------------------------------ async staging
+// Per-thread global -> shared copies (cp.async).  Each thread stages its own inputs
+// into a private shared-memory slot one step ahead of use; cp.async.wait_group makes
+// the thread's own copies visible to itself, so no block barrier is needed.
+__device__ __forceinline__ void cp_async16(float* smem, const float* gmem) {
+  const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async4(float* smem, const float* gmem) {
+  const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+// n floats (n % 4 == 0, both pointers 16-byte aligned)
+template <int NF>
+__device__ __forceinline__ void cp_async_floats(float* smem, const float* gmem) {
+  static_assert(NF % 4 == 0, "16-byte granules");
+#pragma unroll
+  for (int v = 0; v < NF / 4; ++v) cp_async16(smem + 4 * v, gmem + 4 * v);
+}
+
 // Generator layouts accepted by the fused rotor kernels.
 enum Basis : int {
   BASIS_TRIU = 0,  // reference layout: g_k at torch.triu_indices(D, D, 1)[:, k]

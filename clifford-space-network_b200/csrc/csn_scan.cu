@@ -291,6 +291,12 @@ __global__ void __launch_bounds__(128) bwd_apply_kernel(ScanArgs a) {
 }
 
 // ================================================================= host side
+// Implemented in csn_scan16.cu (D = 16 kernel family).
+int scan16_dispatch(const ScanArgs& a, int src, int basis, bool damped, bool two, bool bwd,
+                    cudaStream_t st);
+// Implemented in csn_scan8.cu (staged D = 8 fused rotor kernels).
+int scan8_rotor_dispatch(const ScanArgs& a, bool damped, bool two, bool bwd, cudaStream_t st);
+
 namespace {
 
 int64_t pick_chunk(int64_t S, int64_t T, int D) {
@@ -425,9 +431,7 @@ int dispatch(ScanArgs a, int D, int src, int basis, bool damped, bool two, bool 
   if (D == 4 && basis == BASIS_GA)
     return damped ? run_sided<4, SRC_ROTOR, BASIS_GA, true>(a, two, bwd, st)
                   : run_sided<4, SRC_ROTOR, BASIS_GA, false>(a, two, bwd, st);
-  if (D == 8 && basis == BASIS_TRIU)
-    return damped ? run_sided<8, SRC_ROTOR, BASIS_TRIU, true>(a, two, bwd, st)
-                  : run_sided<8, SRC_ROTOR, BASIS_TRIU, false>(a, two, bwd, st);
+  if (D == 8 && basis == BASIS_TRIU) return scan8_rotor_dispatch(a, damped, two, bwd, st);
   return set_error(CSN_ERR_UNSUPPORTED, "rotor scan: unsupported (D, basis) for this kernel family");
 }
 
@@ -442,9 +446,6 @@ int check_shape(int64_t B, int64_t T, int64_t N, int D) {
 
 }  // namespace
 
-// Implemented in csn_scan16.cu (D = 16 kernel family).
-int scan16_dispatch(const ScanArgs& a, int src, int basis, bool damped, bool two, bool bwd,
-                    cudaStream_t st);
 
 }  // namespace csn
 

@@ -1,0 +1,744 @@
+// csn_scan8.cu -- D = 8 (Cl(6,0) ~ M_8(R)) fused rotor scan, staged kernels.
+//
+// Same reduce -> carry -> apply algorithm as csn_scan.cu (one thread per (sequence,
+// chunk)), specialised for the LM hot path:
+//  * every step's inputs (generators, S or dX, X_{t-1}, gamma, dt) are staged with
+//    cp.async into a private shared-memory slot of the thread; each slot is refilled
+//    for the next step right after its last read in the current step, so the copy
+//    overlaps (at least) the rest of the step's arithmetic;
+//  * slot strides are = 4 (mod 32) words apart for every 128-bit access pattern used
+//    here, so the 8 lanes of a quarter warp hit 8 different bank groups;
+//  * matrices that would not fit in the 255-register budget next to the live state
+//    (the running product P in the reduce passes, M in the backward apply pass) live in
+//    the slot too, and products with them are written as row-broadcast outer products
+//    (one 128-bit load of a row feeds 32 FMAs), so they cost no register spills.
+// Chunks, carries and results are identical to the generic kernels.
+#include "csn_common.cuh"
+#include "csn_internal.h"
+#include "csn_scan_args.cuh"
+#include "csn_carry.cuh"
+
+namespace csn {
+namespace s8 {
+
+constexpr int D = 8;
+constexpr int DD = 64;
+constexpr int K = 28;  // so(8) generators, reference triu layout
+constexpr int THREADS = 128;
+
+// slot layouts (floats)
+struct FwdSlot {  // reduce / apply forward
+  static constexpr int G = 0, S = 28, GAM = 92, DT = 93, P = 96, STRIDE = 164;
+};
+struct BwdRedSlot {  // backward reduce
+  static constexpr int G = 0, DX = 28, GAM = 92, DT = 93, P = 96, STRIDE = 164;
+};
+struct BwdAppSlot {  // backward apply: M/S share a buffer
+  static constexpr int MS = 0, XP = 64, DX = 128, G = 192, STRIDE = 220;
+};
+static_assert(FwdSlot::STRIDE % 32 == 4 && BwdRedSlot::STRIDE % 32 == 4, "bank spread");
+static_assert(BwdAppSlot::STRIDE % 32 == 28, "bank spread");
+
+extern __shared__ __align__(16) float s8_smem[];
+
+__device__ __forceinline__ void lds_row(float (&r)[8], const float* p) {
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  const float4 b = *reinterpret_cast<const float4*>(p + 4);
+  r[0] = a.x; r[1] = a.y; r[2] = a.z; r[3] = a.w; r[4] = b.x; r[5] = b.y; r[6] = b.z; r[7] = b.w;
+}
+__device__ __forceinline__ void sts_row(float* p, const float (&r)[8]) {
+  *reinterpret_cast<float4*>(p) = make_float4(r[0], r[1], r[2], r[3]);
+  *reinterpret_cast<float4*>(p + 4) = make_float4(r[4], r[5], r[6], r[7]);
+}
+
+// ------------------------------------------------- warp-cooperative row transfers
+// A lane's per-step rows (S, dX, X, dS: 64 floats = 256 B) are contiguous in memory but
+// 256 B away from its neighbours' rows.  Instead of each lane moving its own row 16 B at
+// a time (every warp instruction then touches 32 rows), 16 lanes move one whole row
+// together: instruction v handles rows 2v and 2v+1 of the warp, one contiguous 256 B
+// run per half warp.  The owner's row index comes from a shuffle.
+struct LaneRows {
+  int64_t first;  // element index (b*T + t)*N + n of the lane's first step (forward order)
+  int len;        // steps in the lane's chunk (0 for lanes past the end of the grid)
+  int t0;         // time index of the first step
+};
+constexpr unsigned FULL = 0xffffffffu;
+
+// Row of lane r at `step` (reverse order counts from the chunk's last step), shifted by
+// `back` rows (1 = the previous time step).  Returns -1 when that time is before 0.
+template <bool REVERSE>
+__device__ __forceinline__ int64_t lane_row(int64_t first, int len, int t0, int step, int back,
+                                            int64_t row_step) {
+  const int k = REVERSE ? (len - 1 - step) : step;
+  if (t0 + k - back < 0) return -1;
+  return first + (int64_t)(k - back) * row_step;
+}
+
+// g -> smem.  RF floats per row (RF/4 16-byte vectors), 16 lanes per row for RF = 64
+// (two rows per instruction), 8 lanes per row for RF = 28 (four rows per instruction).
+template <int RF, bool REVERSE>
+__device__ __forceinline__ void coop_load_rows(float* warp_slots, int stride, int off,
+                                               const float* __restrict__ g, const LaneRows& me,
+                                               int step, int64_t row_step, int back = 0) {
+  constexpr int RV = RF / 4, LPR = RV > 8 ? 16 : 8, RPI = 32 / LPR;
+  const int lane = threadIdx.x & 31, c = lane % LPR;
+#pragma unroll
+  for (int v = 0; v < 32 / RPI; ++v) {
+    const int r = v * RPI + lane / LPR;
+    const int64_t first = __shfl_sync(FULL, me.first, r);
+    const int len = __shfl_sync(FULL, me.len, r);
+    const int t0 = __shfl_sync(FULL, me.t0, r);
+    if (c < RV && step < len) {
+      const int64_t row = lane_row<REVERSE>(first, len, t0, step, back, row_step);
+      if (row >= 0) cp_async16(warp_slots + r * stride + off + 4 * c, g + row * RF + 4 * c);
+    }
+  }
+}
+
+// smem -> g, each row scaled by its owner's `scale`.
+template <int RF, bool REVERSE>
+__device__ __forceinline__ void coop_store_rows(const float* warp_slots, int stride, int off,
+                                                float* __restrict__ g, const LaneRows& me,
+                                                int step, int64_t row_step, float scale) {
+  constexpr int RV = RF / 4, LPR = RV > 8 ? 16 : 8, RPI = 32 / LPR;
+  const int lane = threadIdx.x & 31, c = lane % LPR;
+#pragma unroll
+  for (int v = 0; v < 32 / RPI; ++v) {
+    const int r = v * RPI + lane / LPR;
+    const int64_t first = __shfl_sync(FULL, me.first, r);
+    const int len = __shfl_sync(FULL, me.len, r);
+    const int t0 = __shfl_sync(FULL, me.t0, r);
+    const float sc = __shfl_sync(FULL, scale, r);
+    if (c < RV && step < len) {
+      const int64_t row = lane_row<REVERSE>(first, len, t0, step, 0, row_step);
+      float4 f = *reinterpret_cast<const float4*>(warp_slots + r * stride + off + 4 * c);
+      f.x *= sc; f.y *= sc; f.z *= sc; f.w *= sc;
+      __stcs(reinterpret_cast<float4*>(g + row * RF + 4 * c), f);
+    }
+  }
+}
+
+// M = sa (2 (I - Omega)^{-1} - I) from the staged generators.
+template <bool DAMPED>
+__device__ __forceinline__ void cayley_from_slot(const float* gslot, float dtv, float gam,
+                                                 Mat<8>& M, float& alpha, float& sa) {
+  float g[K];
+#pragma unroll
+  for (int v = 0; v < K / 4; ++v) {
+    const float4 f = *reinterpret_cast<const float4*>(gslot + 4 * v);
+    g[4 * v] = f.x; g[4 * v + 1] = f.y; g[4 * v + 2] = f.z; g[4 * v + 3] = f.w;
+  }
+  build_I_minus_omega<8, BASIS_TRIU, K>(M, g, 0.5f * dtv);
+  gj_inverse(M);
+  if constexpr (DAMPED) {
+    alpha = 1.0f / (1.0f + expf(gam * dtv));
+    sa = sqrtf(alpha);
+  } else {
+    alpha = 1.0f;
+    sa = 1.0f;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) M.a[i][j] = sa * (2.0f * M.a[i][j] - ((i == j) ? 1.0f : 0.0f));
+}
+
+__device__ __forceinline__ void thread_coords(const ScanArgs& a, int64_t tid, int64_t& b, int64_t& n,
+                                              int64_t& j) {
+  n = tid % a.N;
+  j = (tid / a.N) % a.nchunks;
+  b = tid / (a.N * a.nchunks);
+}
+
+// ------------------------------------------------------------------ forward
+// REDUCE = true: chunk aggregate (P, c) with zero carry.  REDUCE = false: rescan from
+// the chunk's carry and write X.  The step loop is warp-uniform (it runs to the longest
+// chunk in the warp) because the S loads and X stores are warp-cooperative.
+template <bool REDUCE, bool DAMPED, bool TWO>
+__global__ void __launch_bounds__(THREADS, 2) fwd8_kernel(ScanArgs a) {
+  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t total = a.B * a.N * a.nchunks;
+  const bool active = tid < total;
+  int64_t b = 0, n = 0, j = 0;
+  if (active) thread_coords(a, tid, b, n, j);
+  const int64_t s = b * a.N + n;
+  const int64_t t0 = j * a.chunk, t1 = active ? min(a.T, t0 + a.chunk) : t0;
+  LaneRows me{(b * a.T + t0) * a.N + n, (int)(t1 - t0), (int)t0};
+  const int nsteps = __reduce_max_sync(FULL, me.len);
+  if (nsteps == 0) return;  // whole warp idle
+  float* warp_slots = s8_smem + (threadIdx.x & ~31) * FwdSlot::STRIDE;
+  float* slot = s8_smem + threadIdx.x * FwdSlot::STRIDE;
+
+  auto issue_a = [&](int st) {  // generators, gamma, dt of step st (own lane)
+    if (st < me.len) {
+      const int64_t t = t0 + st;
+      const int64_t e = (b * a.T + t) * a.N + n;
+      cp_async_floats<K>(slot + FwdSlot::G, a.gens + e * K);
+      if (DAMPED) cp_async4(slot + FwdSlot::GAM, a.gamma + e);
+      cp_async4(slot + FwdSlot::DT, a.dt + b * a.T + t);
+    }
+  };
+
+  // S of step st: the apply pass loads it warp-cooperatively (coalesced); the reduce pass,
+  // which is arithmetic-bound, lets each lane copy its own row (no shuffles)
+  auto issue_s = [&](int st) {
+    if constexpr (REDUCE) {
+      if (st < me.len) {
+        const int64_t e = (b * a.T + t0 + st) * a.N + n;
+        cp_async_floats<DD>(slot + FwdSlot::S, a.S + e * DD);
+      }
+    } else {
+      coop_load_rows<DD, false>(warp_slots, FwdSlot::STRIDE, FwdSlot::S, a.S, me, st, a.N);
+    }
+  };
+  issue_a(0);
+  cp_async_commit();
+  issue_s(0);
+  cp_async_commit();
+
+  Mat<8> X, M;
+  if constexpr (REDUCE) {
+    mat_zero(X);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {  // P^T = I, stored transposed: row j of P^T = column j of P
+      float r[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) r[c] = (i == c) ? 1.0f : 0.0f;
+      sts_row(slot + FwdSlot::P + 8 * i, r);
+    }
+  } else {
+    if (!active) mat_zero(X);
+    else if (a.nchunks > 1) load_mat(X, a.carry + (s * a.nchunks + j) * DD);
+    else if (a.h0) load_mat(X, a.h0 + s * DD);
+    else mat_zero(X);
+  }
+
+  for (int st = 0; st < nsteps; ++st) {
+    const bool live = st < me.len;
+    cp_async_wait<1>();  // own generators / gamma / dt of this step
+    float alpha = 1.0f, sa = 1.0f;
+    if (live) {
+      const float dtv = slot[FwdSlot::DT];
+      const float gam = DAMPED ? slot[FwdSlot::GAM] : 0.0f;
+      cayley_from_slot<DAMPED>(slot + FwdSlot::G, dtv, gam, M, alpha, sa);
+    }
+    issue_a(st + 1);
+    cp_async_commit();
+    if (live) {
+      lmul(M, X);
+      if constexpr (TWO) rmulT(X, M);
+    }
+    cp_async_wait<1>();  // S rows of this step
+    if constexpr (!REDUCE) __syncwarp();  // rows were copied by other lanes
+    const float cs = DAMPED ? (1.0f - alpha) : 1.0f;
+    if (live) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float r[8];
+        lds_row(r, slot + FwdSlot::S + 8 * i);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) X.a[i][c] = fmaf(cs, r[c], X.a[i][c]);
+      }
+    }
+    if constexpr (REDUCE) {
+      issue_s(st + 1);
+      cp_async_commit();
+      if (live) {
+        // P <- M P; column j of the new P = M * (column j of P) = M * (row j of P^T)
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+          float v[8], o[8];
+          lds_row(v, slot + FwdSlot::P + 8 * jj);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            float acc = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) acc = fmaf(M.a[i][k], v[k], acc);
+            o[i] = acc;
+          }
+          sts_row(slot + FwdSlot::P + 8 * jj, o);
+        }
+      }
+    } else {
+      // X goes out through the S buffer: own row into the slot, then a coalesced store
+      if (live) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float r[8];
+#pragma unroll
+          for (int c = 0; c < 8; ++c) r[c] = X.a[i][c];
+          sts_row(slot + FwdSlot::S + 8 * i, r);
+        }
+      }
+      __syncwarp();
+      coop_store_rows<DD, false>(warp_slots, FwdSlot::STRIDE, FwdSlot::S, a.out, me, st, a.N, 1.0f);
+      __syncwarp();  // the S buffer is free again
+      issue_s(st + 1);
+      cp_async_commit();
+    }
+  }
+  cp_async_wait<0>();
+  if (!active) return;
+  if constexpr (REDUCE) {
+    store_mat(a.aggC + (s * a.nchunks + j) * DD, X);
+    Mat<8> P;
+#pragma unroll
+    for (int jj = 0; jj < 8; ++jj) {
+      float v[8];
+      lds_row(v, slot + FwdSlot::P + 8 * jj);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) P.a[i][jj] = v[i];
+    }
+    store_mat(a.aggP + (s * a.nchunks + j) * DD, P);
+  }
+}
+
+// --------------------------------------------------------------- backward reduce
+// g <- 0; for t = end .. start: G = dX_t + g; g = M^T G M (one-sided M^T G); P <- P M
+template <bool DAMPED, bool TWO>
+__global__ void __launch_bounds__(THREADS, 2) bwd8_reduce_kernel(ScanArgs a) {
+  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (tid >= a.B * a.N * a.nchunks) return;
+  int64_t b, n, j;
+  thread_coords(a, tid, b, n, j);
+  if (j == 0) return;
+  const int64_t s = b * a.N + n;
+  const int64_t t0 = j * a.chunk, t1 = min(a.T, t0 + a.chunk);
+  float* slot = s8_smem + threadIdx.x * BwdRedSlot::STRIDE;
+
+  auto issue_a = [&](int64_t t) {
+    const int64_t e = (b * a.T + t) * a.N + n;
+    cp_async_floats<K>(slot + BwdRedSlot::G, a.gens + e * K);
+    if (DAMPED) cp_async4(slot + BwdRedSlot::GAM, a.gamma + e);
+    cp_async4(slot + BwdRedSlot::DT, a.dt + b * a.T + t);
+  };
+  auto issue_b = [&](int64_t t) {
+    const int64_t e = (b * a.T + t) * a.N + n;
+    cp_async_floats<DD>(slot + BwdRedSlot::DX, a.dX + e * DD);
+  };
+  issue_a(t1 - 1);
+  cp_async_commit();
+  issue_b(t1 - 1);
+  cp_async_commit();
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float r[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) r[c] = (i == c) ? 1.0f : 0.0f;
+    sts_row(slot + BwdRedSlot::P + 8 * i, r);
+  }
+  Mat<8> g, M;
+  mat_zero(g);
+  for (int64_t t = t1 - 1; t >= t0; --t) {
+    cp_async_wait<1>();
+    const float dtv = slot[BwdRedSlot::DT];
+    const float gam = DAMPED ? slot[BwdRedSlot::GAM] : 0.0f;
+    float alpha, sa;
+    cayley_from_slot<DAMPED>(slot + BwdRedSlot::G, dtv, gam, M, alpha, sa);
+    if (t - 1 >= t0) issue_a(t - 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float r[8];
+      lds_row(r, slot + BwdRedSlot::DX + 8 * i);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) g.a[i][c] += r[c];
+    }
+    if (t - 1 >= t0) issue_b(t - 1);
+    cp_async_commit();
+    lmulT(M, g);
+    if constexpr (TWO) rmul(g, M);
+    // P <- P M, row by row in place
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float v[8], o[8];
+      lds_row(v, slot + BwdRedSlot::P + 8 * i);
+#pragma unroll
+      for (int l = 0; l < 8; ++l) {
+        float acc = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc = fmaf(v[k], M.a[k][l], acc);
+        o[l] = acc;
+      }
+      sts_row(slot + BwdRedSlot::P + 8 * i, o);
+    }
+  }
+  cp_async_wait<0>();
+  store_mat(a.aggC + (s * a.nchunks + j) * DD, g);
+  Mat<8> P;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float v[8];
+    lds_row(v, slot + BwdRedSlot::P + 8 * i);
+#pragma unroll
+    for (int l = 0; l < 8; ++l) P.a[i][l] = v[l];
+  }
+  store_mat(a.aggP + (s * a.nchunks + j) * DD, P);
+}
+
+// ---------------------------------------------------------------- backward apply
+// Per step t (reverse):  G = dX_t + H
+//   dS_t = (1 - a) G,  dM = G M Xp^T + G^T M Xp  (one-sided: G Xp^T),  Xp = X_{t-1}
+//   da = -<G, S> + <dM, M> / (2 a)
+//   V = (M^T dM + sa dM) / 2,  dOm = V M^T / sa + V,  dg_k = <dOm, E_k> dt / 2
+//   H <- M^T G M  (one-sided: M^T G)
+// Slot: [M or S | Xp | dX or G | gens or dgens].  S_t is staged into the M buffer and
+// read before M_t overwrites it; G is parked in the dX buffer right after it is formed;
+// dgens leaves through the generator buffer.  Every row moves warp-cooperatively
+// (coalesced), so the step loop is warp-uniform.  Group order per step: Xp, gens, S+dX.
+template <bool DAMPED, bool TWO>
+__global__ void __launch_bounds__(THREADS, 2) bwd8_apply_kernel(ScanArgs a) {
+  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t total = a.B * a.N * a.nchunks;
+  const bool active = tid < total;
+  int64_t b = 0, n = 0, j = 0;
+  if (active) thread_coords(a, tid, b, n, j);
+  const int64_t s = b * a.N + n;
+  const int64_t t0 = j * a.chunk, t1 = active ? min(a.T, t0 + a.chunk) : t0;
+  const LaneRows me{(b * a.T + t0) * a.N + n, (int)(t1 - t0), (int)t0};
+  const int nsteps = __reduce_max_sync(FULL, me.len);
+  if (nsteps == 0) return;
+  constexpr int ST = BwdAppSlot::STRIDE;
+  float* warp_slots = s8_smem + (threadIdx.x & ~31) * ST;
+  float* slot = s8_smem + threadIdx.x * ST;
+  float* sM = slot + BwdAppSlot::MS;
+  float* sXp = slot + BwdAppSlot::XP;
+  float* sDX = slot + BwdAppSlot::DX;
+  float* sG = slot + BwdAppSlot::G;
+
+  // step st of this lane is time t = t1 - 1 - st
+  auto issue_xp = [&](int st) {  // X_{t-1}; rows before t = 0 come from h0 (or zeros) below
+    coop_load_rows<DD, true>(warp_slots, ST, BwdAppSlot::XP, a.X, me, st, a.N, 1);
+  };
+  auto fix_xp = [&](int st) {  // own lane: X_{-1} = h0 or 0 when this step is t = 0
+    if (st < me.len && t1 - 1 - st == 0) {
+      if (a.h0) {
+#pragma unroll
+        for (int v = 0; v < 16; ++v)
+          *reinterpret_cast<float4*>(sXp + 4 * v) = __ldg(reinterpret_cast<const float4*>(a.h0 + s * DD) + v);
+      } else {
+        float z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sts_row(sXp + 8 * i, z);
+      }
+    }
+  };
+  auto issue_gens = [&](int st) {
+    coop_load_rows<K, true>(warp_slots, ST, BwdAppSlot::G, a.gens, me, st, a.N);
+  };
+  auto issue_sdx = [&](int st) {
+    if (DAMPED) coop_load_rows<DD, true>(warp_slots, ST, BwdAppSlot::MS, a.S, me, st, a.N);
+    coop_load_rows<DD, true>(warp_slots, ST, BwdAppSlot::DX, a.dX, me, st, a.N);
+  };
+  issue_xp(0);
+  cp_async_commit();
+  issue_gens(0);
+  cp_async_commit();
+  issue_sdx(0);
+  cp_async_commit();
+  fix_xp(0);
+  float gam_n = 0.0f, dt_n = 0.0f;
+  if (me.len > 0) {
+    const int64_t e = (b * a.T + t1 - 1) * a.N + n;
+    if (DAMPED) gam_n = __ldg(a.gamma + e);
+    dt_n = __ldg(a.dt + b * a.T + t1 - 1);
+  }
+
+  Mat<8> H;
+  if (active && a.nchunks > 1) load_mat(H, a.carry + (s * a.nchunks + j) * DD);
+  else mat_zero(H);
+
+  for (int st = 0; st < nsteps; ++st) {
+    const bool live = st < me.len;
+    const int64_t t = t1 - 1 - st;
+    const int64_t e = (b * a.T + t) * a.N + n;
+    const float dtv = dt_n, gam = gam_n;
+    if (st + 1 < me.len) {  // scalars of the next step, a full step ahead
+      const int64_t e1 = (b * a.T + t - 1) * a.N + n;
+      if (DAMPED) gam_n = __ldg(a.gamma + e1);
+      dt_n = __ldg(a.dt + b * a.T + t - 1);
+    }
+    // ---- 1. Cayley in registers (Xp, gens landed; S, dX may still be in flight)
+    cp_async_wait<1>();
+    __syncwarp();
+    Mat<8> Mr;
+    float alpha = 1.0f, sa = 1.0f;
+    if (live) cayley_from_slot<DAMPED>(sG, dtv, gam, Mr, alpha, sa);
+    // ---- 2. G = H + dX;  <G, S>;  G parks in the dX buffer;  M into its buffer
+    cp_async_wait<0>();
+    __syncwarp();
+    float gS = 0.0f;
+    const float cs = DAMPED ? (1.0f - alpha) : 1.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float r[8], sr[8];
+      lds_row(r, sDX + 8 * i);
+      if (DAMPED) lds_row(sr, sM + 8 * i);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        H.a[i][c] += r[c];
+        if (DAMPED) gS = fmaf(H.a[i][c], sr[c], gS);
+      }
+#pragma unroll
+      for (int c = 0; c < 8; ++c) r[c] = H.a[i][c];
+      sts_row(sDX + 8 * i, r);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float r[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) r[c] = Mr.a[i][c];
+      sts_row(sM + 8 * i, r);
+    }
+    __syncwarp();
+    coop_store_rows<DD, true>(warp_slots, ST, BwdAppSlot::DX, a.dC, me, st, a.N, cs);  // dS = (1-a) G
+    // ---- 3. dM, with G read back from the dX buffer
+    Mat<8> dM;
+    if constexpr (TWO) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        // keeps the scheduler from overlapping the two halves (which would hold both
+        // halves' temporaries at once and spill)
+        __syncwarp();
+        float W[4][8], U[4][8];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+          for (int l = 0; l < 8; ++l) W[r][l] = U[r][l] = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {  // W = G[rows] M,  U = (G^T)[rows] M
+          float mr[8];
+          lds_row(mr, sM + 8 * k);
+          const float4 gu4 = *reinterpret_cast<const float4*>(sDX + 8 * k + 4 * h);  // G[k][rows]
+          const float guv[4] = {gu4.x, gu4.y, gu4.z, gu4.w};
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const float gw = sDX[8 * (4 * h + r) + k], gu = guv[r];
+#pragma unroll
+            for (int l = 0; l < 8; ++l) {
+              W[r][l] = fmaf(gw, mr[l], W[r][l]);
+              U[r][l] = fmaf(gu, mr[l], U[r][l]);
+            }
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {  // dM[rows] = W Xp^T + U Xp
+          float xr[8];
+          lds_row(xr, sXp + 8 * k);
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            float acc = 0.0f;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) acc = fmaf(W[r][c], xr[c], acc);
+            if (k == 0) {
+#pragma unroll
+              for (int l = 0; l < 8; ++l) dM.a[4 * h + r][l] = U[r][0] * xr[l];
+            } else {
+#pragma unroll
+              for (int l = 0; l < 8; ++l) dM.a[4 * h + r][l] = fmaf(U[r][k], xr[l], dM.a[4 * h + r][l]);
+            }
+            dM.a[4 * h + r][k] += acc;
+          }
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {  // dM = G Xp^T, row i from row i of G
+        float gr[8];
+        lds_row(gr, sDX + 8 * i);
+#pragma unroll
+        for (int l = 0; l < 8; ++l) {
+          float xr[8];
+          lds_row(xr, sXp + 8 * l);
+          float acc = 0.0f;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) acc = fmaf(gr[k], xr[k], acc);
+          dM.a[i][l] = acc;
+        }
+      }
+    }
+    __syncwarp();  // every lane is done with its Xp
+    issue_xp(st + 1);
+    cp_async_commit();
+    fix_xp(st + 1);
+    // ---- 4. decay gradient
+    float da = 0.0f;
+    if constexpr (DAMPED) {
+      float dmm = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float mr[8];
+        lds_row(mr, sM + 8 * i);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) dmm = fmaf(dM.a[i][c], mr[c], dmm);
+      }
+      da = -gS + dmm / (2.0f * alpha);
+    }
+    // ---- 5. generator gradient: V = (M^T dM + sa dM)/2, dOm = V M^T / sa + V
+    float proj[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) proj[k] = 0.0f;
+    {
+      const float inv_sa = 1.0f / sa;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {  // rows 4h .. 4h+3 of V and dOm
+        __syncwarp();
+        float V[4][8];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+          for (int l = 0; l < 8; ++l) V[r][l] = 0.5f * sa * dM.a[4 * h + r][l];
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {  // V += (M^T dM)[rows] / 2
+          float mr[8];
+          lds_row(mr, sM + 8 * jj);
+#pragma unroll
+          for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int l = 0; l < 8; ++l) V[r][l] = fmaf(0.5f * mr[4 * h + r], dM.a[jj][l], V[r][l]);
+        }
+#pragma unroll
+        for (int l = 0; l < 8; ++l) {  // dOm[rows][l] = (V M^T)[rows][l] / sa + V[rows][l]
+          float mr[8];
+          lds_row(mr, sM + 8 * l);
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const int i = 4 * h + r;
+            if (i == l) continue;
+            float acc = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) acc = fmaf(V[r][k], mr[k], acc);
+            const float dom = fmaf(acc, inv_sa, V[r][l]);
+            if (i < l) proj[i * (15 - i) / 2 + (l - i - 1)] += dom;
+            else proj[l * (15 - l) / 2 + (i - l - 1)] -= dom;
+          }
+        }
+      }
+    }
+    {
+      const float hdt = 0.5f * dtv;
+      float ddt = 0.0f;
+#pragma unroll
+      for (int v = 0; v < K / 4; ++v) {  // g_t is still in the generator buffer
+        float4 f = *reinterpret_cast<const float4*>(sG + 4 * v);
+        ddt = fmaf(proj[4 * v], 0.5f * f.x, ddt);
+        ddt = fmaf(proj[4 * v + 1], 0.5f * f.y, ddt);
+        ddt = fmaf(proj[4 * v + 2], 0.5f * f.z, ddt);
+        ddt = fmaf(proj[4 * v + 3], 0.5f * f.w, ddt);
+        f = make_float4(proj[4 * v] * hdt, proj[4 * v + 1] * hdt, proj[4 * v + 2] * hdt,
+                        proj[4 * v + 3] * hdt);
+        *reinterpret_cast<float4*>(sG + 4 * v) = f;  // dgens leave through the same buffer
+      }
+      if (live) {
+        if constexpr (DAMPED) {
+          const float dz = da * alpha * (1.0f - alpha);
+          a.dgamma[e] = -dz * dtv;
+          ddt = fmaf(-dz, gam, ddt);
+        }
+        a.ddt_part[e] = ddt;
+      }
+    }
+    __syncwarp();
+    coop_store_rows<K, true>(warp_slots, ST, BwdAppSlot::G, a.dgens, me, st, a.N, 1.0f);
+    __syncwarp();
+    issue_gens(st + 1);
+    cp_async_commit();
+    // ---- 6. H <- M^T G M (one-sided: M^T G), G read back by rows from the dX buffer
+    {
+      Mat<8> Tm;  // M^T G
+      mat_zero(Tm);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        float mr[8], gr[8];
+        lds_row(mr, sM + 8 * k);
+        lds_row(gr, sDX + 8 * k);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+          for (int l = 0; l < 8; ++l) Tm.a[i][l] = fmaf(mr[i], gr[l], Tm.a[i][l]);
+      }
+      if constexpr (TWO) {
+        mat_zero(H);
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+          float mr[8];
+          lds_row(mr, sM + 8 * jj);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int l = 0; l < 8; ++l) H.a[i][l] = fmaf(Tm.a[i][jj], mr[l], H.a[i][l]);
+        }
+      } else {
+        H = Tm;
+      }
+    }
+    __syncwarp();  // M and G buffers are free
+    issue_sdx(st + 1);
+    cp_async_commit();
+  }
+  cp_async_wait<0>();
+  if (active && j == 0 && a.dh0) store_mat(a.dh0 + s * DD, H);
+}
+
+template <typename Kern>
+void set_smem(Kern k, int bytes) {
+  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
+unsigned nblk(int64_t n) { return (unsigned)((n + THREADS - 1) / THREADS); }
+
+template <bool DAMPED, bool TWO>
+int run8(const ScanArgs& a, bool bwd, cudaStream_t st) {
+  const int64_t S = a.B * a.N;
+  const int64_t total = S * a.nchunks;
+  const int fwd_bytes = THREADS * FwdSlot::STRIDE * 4;
+  const int red_bytes = THREADS * BwdRedSlot::STRIDE * 4;
+  const int app_bytes = THREADS * BwdAppSlot::STRIDE * 4;
+  if (!bwd) {
+    if (total == 0) return CSN_OK;
+    if (a.nchunks > 1) {
+      {
+        KernelTimer kt("fwd_reduce", st);
+        set_smem(fwd8_kernel<true, DAMPED, TWO>, fwd_bytes);
+        fwd8_kernel<true, DAMPED, TWO><<<nblk(total), THREADS, fwd_bytes, st>>>(a);
+      }
+      KernelTimer kt("fwd_carry", st);
+      fwd_carry_kernel<8, TWO><<<(unsigned)((S + 3) / 4), 128, 0, st>>>(a);
+    }
+    KernelTimer kt("fwd_apply", st);
+    set_smem(fwd8_kernel<false, DAMPED, TWO>, fwd_bytes);
+    fwd8_kernel<false, DAMPED, TWO><<<nblk(total), THREADS, fwd_bytes, st>>>(a);
+    return check_launch("rotor scan forward (D=8)");
+  }
+  if (total > 0) {
+    if (a.nchunks > 1) {
+      {
+        KernelTimer kt("bwd_reduce", st);
+        set_smem(bwd8_reduce_kernel<DAMPED, TWO>, red_bytes);
+        bwd8_reduce_kernel<DAMPED, TWO><<<nblk(total), THREADS, red_bytes, st>>>(a);
+      }
+      KernelTimer kt("bwd_carry", st);
+      bwd_carry_kernel<8, TWO><<<(unsigned)((S + 3) / 4), 128, 0, st>>>(a);
+    }
+    KernelTimer kt("bwd_apply", st);
+    set_smem(bwd8_apply_kernel<DAMPED, TWO>, app_bytes);
+    bwd8_apply_kernel<DAMPED, TWO><<<nblk(total), THREADS, app_bytes, st>>>(a);
+  }
+  if (a.B * a.T > 0) {
+    const int64_t BT = a.B * a.T;
+    KernelTimer kt("reduce_channels", st);
+    reduce_channels_kernel<<<(unsigned)((BT + 255) / 256), 256, 0, st>>>(a.ddt_part, a.ddt, BT, a.N);
+  }
+  return check_launch("rotor scan backward (D=8)");
+}
+
+}  // namespace s8
+
+int scan8_rotor_dispatch(const ScanArgs& a, bool damped, bool two, bool bwd, cudaStream_t st) {
+  using namespace s8;
+  if (damped) return two ? run8<true, true>(a, bwd, st) : run8<true, false>(a, bwd, st);
+  return two ? run8<false, true>(a, bwd, st) : run8<false, false>(a, bwd, st);
+}
+
+}  // namespace csn

@@ -1,18 +1,25 @@
 #!/usr/bin/env python
-"""Throughput benchmark of the fused rotor scan (forward + backward).
-
-Workload (one "step"): the Cl(6,0) LM scan section, forward and backward, for 4 layers
-at batch 32, L = 2048, 8 channels of 8 x 8 real matrices (Cl(6,0) ~ M_8(R)), 28 so(8)
-generators per channel, adaptive dt per token and decay gamma per channel.  Synthetic
-seeded inputs shaped like the block's projections (python/clifford_cl6.py:144-168):
-gens ~ N(0, 1), dt ~ U(0.04, 0.06), gamma = softplus(N(0, 0.5^2)), S ~ N(0, 1), dX ~ N(0, 1).
+"""Throughput benchmark of the rotor-scan hot path (forward + backward).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload cl6_lm|cl3]
+
+Workloads (one "step" = one forward + backward pass over one batch of synthetic input,
+seeded, float32, shaped like the reference's configurations):
+
+* ``cl6_lm`` (default) -- the Cl(6,0) LM scan section of 4 layers: batch 32, L 2048,
+  8 channels of 8 x 8 matrices (Cl(6,0) ~ M_8(R)), 28 so(8) generators, adaptive dt per
+  token, decay gamma per channel.  Inputs shaped like the block's projections
+  (python/clifford_cl6.py:144-168): gens ~ N(0,1), dt ~ U(0.04,0.06),
+  gamma = softplus(N(0,0.5^2)), S ~ N(0,1), dX ~ N(0,1).
+* ``cl3`` -- Cl(3,0) blade-basis scan h_t = R_t h R~_t + x_t at the bandwidth scale of
+  the Cl(3) configuration: batch 64, L 65536, 16 channels, gens ~ N(0, 0.1^2) on the 3
+  bivectors, dt ~ U(0.01, 0.1), x ~ N(0, 1), dh ~ N(0, 1).
 
 N > 1 runs under torchrun: every rank owns its own batch (independent sequences, no
 data-path collective: weak scaling); time is the max over ranks.  ``--impl reference``
 times the float64 CPU restatement of the reference algorithm (the oracle) on the host
-cores instead, on a bounded sample.
+cores instead, on a bounded sample of the same workload.
 """
 from __future__ import annotations
 
@@ -32,19 +39,6 @@ sys.path.insert(0, str(REPO))
 
 METRIC = "rotor-scan fwd+bwd Gelem/s (B*L*C)"
 UNIT = "Gelem/s"
-B, T, N, D, K_GEN, LAYERS = 32, 2048, 8, 8, 28, 4
-# compulsory HBM bytes per element (float32), n = D*D, k = K_GEN, dt amortised over N
-_n, _k = D * D, K_GEN
-OP_BYTES = 4.0 * (5 * _n + 3 * _k + 3 + 3.0 / N)          # whole fused fwd+bwd op
-KERNEL_BYTES = {                                           # per kernel, per element
-    "fwd_apply": 4.0 * (_k + 2 * _n + 1 + 1.0 / N),        # gens, S, gamma, dt -> X
-    "fwd_reduce": 4.0 * (_k + _n + 1 + 1.0 / N),           # gens, S, gamma, dt
-    "bwd_reduce": 4.0 * (_n + _k + 1 + 1.0 / N),           # dX, gens, gamma, dt
-    "bwd_apply": 4.0 * (3 * _n + 2 * _k + 2 + 2.0 / N),    # dX, X, gens, gamma, dt -> dS, dgens, dgamma, ddt
-}
-CONFIG = {"workload": "cl6_lm_scan_fwd_bwd", "batch": B, "seq_len": T, "channels": N,
-          "matrix_dim": D, "generators": K_GEN, "layers": LAYERS, "algebra": "Cl(6,0)",
-          "sided": "two", "damped": True, "l2": "inputs larger than L2 (195 MB per layer forward)"}
 
 
 def dist_env():
@@ -52,21 +46,6 @@ def dist_env():
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     return ws, rank, local
-
-
-def make_inputs(seed, device, batch=B, nlayers=LAYERS):
-    import torch
-    g = torch.Generator(device="cpu").manual_seed(seed)
-    layers = []
-    for _ in range(nlayers):
-        gens = torch.randn(batch, T, N, K_GEN, generator=g)
-        dt = torch.rand(batch, T, generator=g) * 0.02 + 0.04
-        gamma = torch.nn.functional.softplus(torch.randn(batch, T, N, generator=g) * 0.5)
-        S = torch.randn(batch, T, N, D, D, generator=g)
-        dX = torch.randn(batch, T, N, D, D, generator=g)
-        layers.append({k: v.to(device) if device != "cpu" else v
-                       for k, v in dict(gens=gens, dt=dt, gamma=gamma, S=S, dX=dX).items()})
-    return layers
 
 
 class ClockSampler:
@@ -95,7 +74,6 @@ class ClockSampler:
                     if r & bit:
                         self.reasons.add(name)
                 self._stop.wait(0.01)
-            nv.nvmlShutdown()
         except Exception as e:  # NVML missing: record why, never fail the bench
             self.err = repr(e)
 
@@ -131,68 +109,249 @@ def peaks():
     return 6650.0, "fallback"
 
 
-def run_cpu_reference(sample_batch, reps, warmup):
-    """The float64 oracle (CPU restatement of the reference algorithm) on host cores."""
-    import numpy as np
-    from oracle import oracle as orc
-    from csn_b200 import algebra
-    E = algebra.triu_basis(D)
-    rng = np.random.default_rng(0)
-    gens = rng.standard_normal((sample_batch, T, N, K_GEN))
-    dt = rng.uniform(0.04, 0.06, (sample_batch, T))
-    gamma = np.log1p(np.exp(rng.standard_normal((sample_batch, T, N)) * 0.5))
-    S = rng.standard_normal((sample_batch, T, N, D, D))
-    dX = rng.standard_normal((sample_batch, T, N, D, D))
+def _p(t):
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
 
-    def one():
-        X = orc.rotor_scan_fwd(gens, dt, gamma, S, E)
-        orc.rotor_scan_bwd(gens, dt, gamma, S, E, X, dX)
 
+def _time_cpu(one, reps, warmup):
     for _ in range(warmup):
         one()
     t0 = time.perf_counter()
     for _ in range(reps):
         one()
-    el = time.perf_counter() - t0
-    elems = sample_batch * T * N * reps
-    return elems / el / 1e9, el
+    return time.perf_counter() - t0
 
 
+# =============================================================================== workloads
+class Cl6LM:
+    """4 layers of the Cl(6,0) LM scan section, forward + backward."""
+    name = "cl6_lm_scan_fwd_bwd"
+    T, N, D, K = 2048, 8, 8, 28
+
+    def __init__(self, batch=32, layers=4):
+        self.B, self.layers = batch, layers
+        n, k, N = self.D * self.D, self.K, self.N
+        # compulsory HBM bytes per element (float32), dt amortised over the channels
+        self.op_bytes = 4.0 * (5 * n + 3 * k + 3 + 3.0 / N)
+        self.kernel_bytes = {
+            "fwd_apply": 4.0 * (k + 2 * n + 1 + 1.0 / N),      # gens, S, gamma, dt -> X
+            "fwd_reduce": 4.0 * (k + n + 1 + 1.0 / N),         # gens, S, gamma, dt
+            "bwd_reduce": 4.0 * (n + k + 1 + 1.0 / N),         # dX, gens, gamma, dt
+            "bwd_apply": 4.0 * (3 * n + 2 * k + 2 + 2.0 / N),  # dX, X, gens, gamma, dt -> dS, dgens, dgamma, ddt
+        }
+        self.kernel_names = ["fwd_reduce", "fwd_carry", "fwd_apply", "bwd_reduce", "bwd_carry",
+                             "bwd_apply", "reduce_channels"]
+        self.elems_per_step = self.B * self.T * N * layers
+        self.config = {"workload": self.name, "batch": self.B, "seq_len": self.T, "channels": N,
+                       "matrix_dim": self.D, "generators": k, "layers": layers, "algebra": "Cl(6,0)",
+                       "sided": "two", "damped": True,
+                       "l2": "inputs larger than L2 (195 MB per layer forward)"}
+
+    def _host_inputs(self, seed, batch):
+        import torch
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        out = []
+        for _ in range(self.layers):
+            out.append(dict(
+                gens=torch.randn(batch, self.T, self.N, self.K, generator=g),
+                dt=torch.rand(batch, self.T, generator=g) * 0.02 + 0.04,
+                gamma=torch.nn.functional.softplus(torch.randn(batch, self.T, self.N, generator=g) * 0.5),
+                S=torch.randn(batch, self.T, self.N, self.D, self.D, generator=g),
+                dX=torch.randn(batch, self.T, self.N, self.D, self.D, generator=g)))
+        return out
+
+    def setup(self, dev, rank, lib):
+        import torch
+        self.dev = dev
+        self.inputs = [{k: v.to(dev) for k, v in L.items()} for L in self._host_inputs(1234 + rank, self.B)]
+        self.outs = [dict(X=torch.empty_like(L["S"]), dgens=torch.empty_like(L["gens"]),
+                          ddt=torch.empty_like(L["dt"]), dgamma=torch.empty_like(L["gamma"]),
+                          dS=torch.empty_like(L["S"])) for L in self.inputs]
+        self.ws_bytes = lib.csn_rotor_scan_workspace_bytes(self.B, self.T, self.N, self.D)
+        self.work = torch.empty(self.ws_bytes, dtype=torch.uint8, device=dev)
+
+    def step(self, stream):
+        from csn_b200 import _lib
+        sp = ctypes.c_void_p(stream.cuda_stream)
+        B, T, N, D = self.B, self.T, self.N, self.D
+        for L, O in zip(self.inputs, self.outs):
+            _lib.call("csn_rotor_scan_fwd", _p(L["gens"]), _p(L["dt"]), _p(L["gamma"]), _p(L["S"]),
+                      _p(None), _p(O["X"]), B, T, N, D, 0, 1, _p(self.work), self.ws_bytes, sp)
+            _lib.call("csn_rotor_scan_bwd", _p(L["gens"]), _p(L["dt"]), _p(L["gamma"]), _p(L["S"]),
+                      _p(None), _p(O["X"]), _p(L["dX"]), _p(O["dgens"]), _p(O["ddt"]), _p(O["dgamma"]),
+                      _p(O["dS"]), _p(None), B, T, N, D, 0, 1, _p(self.work), self.ws_bytes, sp)
+
+    def e2e_setup(self):
+        import torch
+        self.host = [{k: v.cpu().pin_memory() for k, v in L.items()} for L in self.inputs]
+        self.hout = [{k: torch.empty_like(v, device="cpu").pin_memory() for k, v in O.items()}
+                     for O in self.outs]
+        h2d = sum(v.numel() * v.element_size() for Lh in self.host for v in Lh.values())
+        d2h = sum(v.numel() * v.element_size() for Ho in self.hout for v in Ho.values())
+        return h2d, d2h
+
+    def e2e_step(self):
+        from csn_b200 import ops
+        for Lh, Ho in zip(self.host, self.hout):
+            gens = Lh["gens"].to(self.dev, non_blocking=True).requires_grad_(True)
+            dt = Lh["dt"].to(self.dev, non_blocking=True).requires_grad_(True)
+            gamma = Lh["gamma"].to(self.dev, non_blocking=True).requires_grad_(True)
+            S = Lh["S"].to(self.dev, non_blocking=True).requires_grad_(True)
+            dX = Lh["dX"].to(self.dev, non_blocking=True)
+            X = ops.fused_rotor_scan(gens, dt, gamma, S)
+            X.backward(dX)
+            for k, src in (("X", X.detach()), ("dgens", gens.grad), ("ddt", dt.grad),
+                           ("dgamma", gamma.grad), ("dS", S.grad)):
+                Ho[k].copy_(src, non_blocking=True)
+
+    def cpu_reference(self, reps, warmup, sample_batch=8):
+        import numpy as np
+        from csn_b200 import algebra
+        from oracle import oracle as orc
+        E = algebra.triu_basis(self.D)
+        rng = np.random.default_rng(0)
+        gens = rng.standard_normal((sample_batch, self.T, self.N, self.K))
+        dt = rng.uniform(0.04, 0.06, (sample_batch, self.T))
+        gamma = np.log1p(np.exp(rng.standard_normal((sample_batch, self.T, self.N)) * 0.5))
+        S = rng.standard_normal((sample_batch, self.T, self.N, self.D, self.D))
+        dX = rng.standard_normal((sample_batch, self.T, self.N, self.D, self.D))
+
+        def one():
+            X = orc.rotor_scan_fwd(gens, dt, gamma, S, E)
+            orc.rotor_scan_bwd(gens, dt, gamma, S, E, X, dX)
+
+        el = _time_cpu(one, reps, warmup)
+        return (sample_batch * self.T * self.N * reps, el,
+                f"one layer at batch {sample_batch} of {self.B} (B{sample_batch} L{self.T} C{self.N} "
+                f"D{self.D}) per step, fwd+bwd, float64 C oracle, OpenMP")
+
+
+class Cl3:
+    """Cl(3,0) blade-basis scan at the bandwidth scale (B64 L65536 C16), fwd + bwd."""
+    name = "cl3_ga_scan_fwd_bwd"
+    T, N = 65536, 16
+
+    def __init__(self, batch=64, layers=1):
+        self.B = batch
+        N = self.N
+        # fwd reads gens (3) + x (8) + dt, writes h (8); bwd reads dh, h_{t-1}, gens, dt and
+        # writes dx, dgens, ddt
+        self.op_bytes = 4.0 * ((3 + 16 + 1.0 / N) + (8 + 8 + 3 + 8 + 3 + 2.0 / N))
+        self.kernel_bytes = {
+            "ga3_fwd_apply": 4.0 * (3 + 8 + 8 + 1.0 / N),
+            "ga3_fwd_reduce": 4.0 * (3 + 8 + 1.0 / N),
+            "ga3_bwd_reduce": 4.0 * (8 + 3 + 1.0 / N),
+            "ga3_bwd_apply": 4.0 * (8 + 8 + 3 + 1.0 / N + 8 + 3 + 1),
+        }
+        self.kernel_names = ["ga3_fwd_reduce", "ga3_fwd_carry", "ga3_fwd_apply", "ga3_bwd_reduce",
+                             "ga3_bwd_carry", "ga3_bwd_apply", "ga3_reduce_channels"]
+        self.elems_per_step = self.B * self.T * N
+        self.config = {"workload": self.name, "batch": self.B, "seq_len": self.T, "channels": N,
+                       "multivector": 8, "rotor": 4, "algebra": "Cl(3,0)", "sided": "two",
+                       "l2": "inputs larger than L2 (2.9 GB forward)"}
+
+    def _host(self, seed, batch):
+        import torch
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        return dict(gens=torch.randn(batch, self.T, self.N, 3, generator=g) * 0.1,
+                    dt=torch.rand(batch, self.T, generator=g) * 0.09 + 0.01,
+                    x=torch.randn(batch, self.T, self.N, 8, generator=g),
+                    dh=torch.randn(batch, self.T, self.N, 8, generator=g))
+
+    def setup(self, dev, rank, lib):
+        import torch
+        self.dev = dev
+        self.inp = {k: v.to(dev) for k, v in self._host(99 + rank, self.B).items()}
+        self.out = dict(h=torch.empty_like(self.inp["x"]), dx=torch.empty_like(self.inp["x"]),
+                        dgens=torch.empty_like(self.inp["gens"]), ddt=torch.empty_like(self.inp["dt"]))
+        self.ws_bytes = lib.csn_ga3_workspace_bytes(self.B, self.T, self.N)
+        self.work = torch.empty(self.ws_bytes, dtype=torch.uint8, device=dev)
+
+    def step(self, stream):
+        from csn_b200 import _lib
+        sp = ctypes.c_void_p(stream.cuda_stream)
+        I, O = self.inp, self.out
+        _lib.call("csn_ga3_scan_fwd", _p(I["gens"]), _p(I["dt"]), _p(I["x"]), _p(None), _p(O["h"]),
+                  self.B, self.T, self.N, _p(self.work), self.ws_bytes, sp)
+        _lib.call("csn_ga3_scan_bwd", _p(I["gens"]), _p(I["dt"]), _p(None), _p(O["h"]), _p(I["dh"]),
+                  _p(O["dgens"]), _p(O["ddt"]), _p(O["dx"]), _p(None), self.B, self.T, self.N,
+                  _p(self.work), self.ws_bytes, sp)
+
+    def e2e_setup(self):
+        import torch
+        self.host = {k: v.cpu().pin_memory() for k, v in self.inp.items()}
+        self.hout = {k: torch.empty_like(v, device="cpu").pin_memory() for k, v in self.out.items()}
+        return (sum(v.numel() * v.element_size() for v in self.host.values()),
+                sum(v.numel() * v.element_size() for v in self.hout.values()))
+
+    def e2e_step(self):
+        from csn_b200 import ops
+        H = self.host
+        gens = H["gens"].to(self.dev, non_blocking=True).requires_grad_(True)
+        dt = H["dt"].to(self.dev, non_blocking=True).requires_grad_(True)
+        x = H["x"].to(self.dev, non_blocking=True).requires_grad_(True)
+        dh = H["dh"].to(self.dev, non_blocking=True)
+        h = ops.ga3_rotor_scan(gens, dt, x)
+        h.backward(dh)
+        for k, src in (("h", h.detach()), ("dx", x.grad), ("dgens", gens.grad), ("ddt", dt.grad)):
+            self.hout[k].copy_(src, non_blocking=True)
+
+    def cpu_reference(self, reps, warmup, sample_batch=4):
+        from oracle import oracle as orc
+        a = {k: v.double().numpy() for k, v in self._host(5, sample_batch).items()}
+
+        def one():
+            hh = orc.ga3_scan_fwd(a["gens"], a["dt"], a["x"])
+            orc.ga3_scan_bwd(a["gens"], a["dt"], hh, a["dh"])
+
+        el = _time_cpu(one, reps, warmup)
+        return (sample_batch * self.T * self.N * reps, el,
+                f"batch {sample_batch} of {self.B} (B{sample_batch} L{self.T} C{self.N}) per step, "
+                f"fwd+bwd, float64 C oracle, OpenMP")
+
+
+WORKLOADS = {"cl6_lm": Cl6LM, "cl3": Cl3}
+
+
+# ==================================================================================== main
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="cl6_lm", choices=sorted(WORKLOADS))
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--batch", type=int, default=B, help="per-rank batch (profiling: smaller)")
-    ap.add_argument("--layers", type=int, default=LAYERS, help="layers per step (profiling: 1)")
+    ap.add_argument("--batch", type=int, default=None, help="per-rank batch (profiling: smaller)")
+    ap.add_argument("--layers", type=int, default=None, help="layers per step (cl6_lm; profiling: 1)")
     args = ap.parse_args()
-    bsz, nlay = args.batch, args.layers
-    ELEMS_PER_LAYER = bsz * T * N
     ws, rank, local = dist_env()
     cores = os.cpu_count() or 1
+    kw = {}
+    if args.batch is not None:
+        kw["batch"] = args.batch
+    if args.layers is not None:
+        kw["layers"] = args.layers
+    wl = WORKLOADS[args.workload](**kw)
 
     if args.impl == "reference":
         if rank != 0:
             return 0
         os.environ.setdefault("OMP_NUM_THREADS", str(cores))
-        sample_batch = 8
-        v, el = run_cpu_reference(sample_batch, reps=max(1, args.steps), warmup=max(0, min(args.warmup, 1)))
+        elems, el, sample = wl.cpu_reference(reps=max(1, args.steps), warmup=min(args.warmup, 1))
+        v = elems / el / 1e9
         line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": el / max(1, args.steps) * 1e3,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
-                "data": "synthetic", "config": CONFIG, "impl": "reference",
-                "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
-                                 "sample": f"one layer at batch {sample_batch} of {B} (B{sample_batch} L{T} "
-                                           f"C{N} D{D}) per step, float64 C oracle, OpenMP"},
+                "data": "synthetic", "config": wl.config, "impl": "reference",
+                "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
                 "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return 0
 
     import torch
-    from csn_b200 import _lib, ops
+    from csn_b200 import _lib
 
     if ws > 1:
         import torch.distributed as dist
@@ -203,32 +362,15 @@ def main():
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     lib = _lib.load()
-
-    layers = make_inputs(1234 + rank, dev, bsz, nlay)
-    basis = ops.BASIS["triu"]
-    ws_bytes = lib.csn_rotor_scan_workspace_bytes(bsz, T, N, D)
-    work = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
-    outs = [dict(X=torch.empty_like(L["S"]), dgens=torch.empty_like(L["gens"]),
-                 ddt=torch.empty_like(L["dt"]), dgamma=torch.empty_like(L["gamma"]),
-                 dS=torch.empty_like(L["S"])) for L in layers]
-    P = ops._ptr
+    wl.setup(dev, rank, lib)
     stream = torch.cuda.current_stream(dev)
-    sp = ctypes.c_void_p(stream.cuda_stream)
-
-    def step():
-        for L, O in zip(layers, outs):
-            _lib.call("csn_rotor_scan_fwd", P(L["gens"]), P(L["dt"]), P(L["gamma"]), P(L["S"]),
-                      P(None), P(O["X"]), bsz, T, N, D, basis, 1, P(work), ws_bytes, sp)
-            _lib.call("csn_rotor_scan_bwd", P(L["gens"]), P(L["dt"]), P(L["gamma"]), P(L["S"]),
-                      P(None), P(O["X"]), P(L["dX"]), P(O["dgens"]), P(O["ddt"]), P(O["dgamma"]),
-                      P(O["dS"]), P(None), bsz, T, N, D, basis, 1, P(work), ws_bytes, sp)
 
     def barrier():
         if ws > 1:
             torch.distributed.barrier()
 
     for _ in range(max(3, args.warmup)):
-        step()
+        wl.step(stream)
     torch.cuda.synchronize()
 
     _lib.timing_reset()
@@ -239,7 +381,7 @@ def main():
         _lib.timing_enable(True)
         e0.record(stream)
         for _ in range(args.steps):
-            step()
+            wl.step(stream)
         e1.record(stream)
         torch.cuda.synchronize()
         _lib.timing_enable(False)
@@ -250,77 +392,57 @@ def main():
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms = t.item()
     ms_per_step = ms / args.steps
-    elems_step = ELEMS_PER_LAYER * nlay
-    value = elems_step * ws / (ms_per_step * 1e-3) / 1e9
+    value = wl.elems_per_step * ws / (ms_per_step * 1e-3) / 1e9
 
-    # per-kernel device times over the timed region
-    names = ["fwd_reduce", "fwd_carry", "fwd_apply", "bwd_reduce", "bwd_carry", "bwd_apply",
-             "reduce_channels"]
-    ktimes = {n: _lib.timing_read(n) for n in names}
+    # per-kernel device times over the timed region (CUDA events on the launch stream)
+    ktimes = {n: _lib.timing_read(n) for n in wl.kernel_names}
     launches = sum(c for _, c in ktimes.values())
-    dom = max((n for n in KERNEL_BYTES), key=lambda n: ktimes[n][0])
-    dom_ms = ktimes[dom][0] / max(1, ktimes[dom][1])
+    dom = max(wl.kernel_bytes, key=lambda n: ktimes[n][0])
+    dom_launches = max(1, ktimes[dom][1])
+    dom_ms = ktimes[dom][0] / dom_launches
+    elems_per_launch = wl.elems_per_step * args.steps / dom_launches
     hbm, peak_kind = peaks()
-    achieved = KERNEL_BYTES[dom] * ELEMS_PER_LAYER / (dom_ms * 1e-3) / 1e9
+    achieved = wl.kernel_bytes[dom] * elems_per_launch / (dom_ms * 1e-3) / 1e9
     _lib.timing_reset()
 
-    # end to end through the public op API with host buffers (pinned), copies inside
     e2e = None
     if args.e2e_steps > 0:
-        host = [{k: v.cpu().pin_memory() for k, v in L.items()} for L in layers]
-        h2d = sum(v.numel() * v.element_size() for Lh in host for v in Lh.values())
-        d2h = sum(v.numel() * v.element_size() for O in outs for v in O.values())
-        hout = [{k: torch.empty_like(v, device="cpu").pin_memory() for k, v in O.items()} for O in outs]
-
-        def e2e_step():
-            for Lh, Ho in zip(host, hout):
-                gens = Lh["gens"].to(dev, non_blocking=True).requires_grad_(True)
-                dt = Lh["dt"].to(dev, non_blocking=True).requires_grad_(True)
-                gamma = Lh["gamma"].to(dev, non_blocking=True).requires_grad_(True)
-                S = Lh["S"].to(dev, non_blocking=True).requires_grad_(True)
-                dX = Lh["dX"].to(dev, non_blocking=True)
-                X = ops.fused_rotor_scan(gens, dt, gamma, S)
-                X.backward(dX)
-                for k, src in (("X", X.detach()), ("dgens", gens.grad), ("ddt", dt.grad),
-                               ("dgamma", gamma.grad), ("dS", S.grad)):
-                    Ho[k].copy_(src, non_blocking=True)
-            torch.cuda.current_stream(dev).synchronize()
-
-        e2e_step()
+        h2d, d2h = wl.e2e_setup()
+        wl.e2e_step()
+        torch.cuda.synchronize()
         barrier()
         t0 = time.perf_counter()
         for _ in range(args.e2e_steps):
-            e2e_step()
+            wl.e2e_step()
+        torch.cuda.current_stream(dev).synchronize()
         el = time.perf_counter() - t0
         if ws > 1:
             t = torch.tensor([el], device=dev)
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
             el = t.item()
-        e2e = {"value": elems_step * ws * args.e2e_steps / el / 1e9, "unit": UNIT,
+        e2e = {"value": wl.elems_per_step * ws * args.e2e_steps / el / 1e9, "unit": UNIT,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "timing": "wall clock around K steps ending in a stream synchronize, max over ranks"}
+               "timing": "wall clock around K steps (pinned host -> device, op forward + backward, "
+                         "device -> pinned host) ending in a stream synchronize, max over ranks"}
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         os.environ.setdefault("OMP_NUM_THREADS", str(cores))
-        v, el = run_cpu_reference(8, reps=2, warmup=0)
-        cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
-               "sample": f"B8 L{T} C{N} D{D}, one layer fwd+bwd x2, float64 C oracle (OpenMP)"}
+        elems, el, sample = wl.cpu_reference(reps=2, warmup=0)
+        cpu = {"value": elems / el / 1e9, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
 
     if rank == 0:
+        op_ach = wl.op_bytes * wl.elems_per_step / (ms_per_step * 1e-3) / 1e9
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
                 "warmup": max(3, args.warmup), "ms_per_step": ms_per_step, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-                "config": dict(CONFIG, batch=bsz, layers=nlay,
-                               parallelism=f"replicas{ws}" if ws > 1 else "single"),
+                "config": dict(wl.config, parallelism=f"replicas{ws}" if ws > 1 else "single"),
                 "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm,
                              "unit": "GB/s", "frac": achieved / hbm, "traffic": None,
-                             "peak_kind": peak_kind,
-                             "bytes_per_elem": KERNEL_BYTES[dom], "avg_launch_ms": dom_ms},
-                "op_roofline": {"achieved": OP_BYTES * elems_step / (ms_per_step * 1e-3) / 1e9,
-                                "peak": hbm, "unit": "GB/s",
-                                "frac": OP_BYTES * elems_step / (ms_per_step * 1e-3) / 1e9 / hbm,
-                                "bytes_per_elem": OP_BYTES},
+                             "peak_kind": peak_kind, "bytes_per_elem": wl.kernel_bytes[dom],
+                             "avg_launch_ms": dom_ms},
+                "op_roofline": {"achieved": op_ach, "peak": hbm, "unit": "GB/s", "frac": op_ach / hbm,
+                                "bytes_per_elem": wl.op_bytes},
                 "kernel_ms": {n: {"total_ms": t, "launches": c} for n, (t, c) in ktimes.items()},
                 "gpu_launches": launches, "clocks": clk.summary(), "e2e": e2e, "cpu_baseline": cpu}
         print(json.dumps(line), flush=True)

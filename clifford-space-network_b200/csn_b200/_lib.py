@@ -37,6 +37,9 @@ SIGNATURES = {
                                     _f], _int),
     "csn_cayley_fwd": ([_f, _f, _i64, _int, _f], _int),
     "csn_cayley_bwd": ([_f, _f, _f, _i64, _int, _f], _int),
+    "csn_ga3_workspace_bytes": ([_i64, _i64, _i64], _sz),
+    "csn_ga3_scan_fwd": ([_f, _f, _f, _f, _f, _i64, _i64, _i64, _f, _sz, _f], _int),
+    "csn_ga3_scan_bwd": ([_f, _f, _f, _f, _f, _f, _f, _f, _f, _i64, _i64, _i64, _f, _sz, _f], _int),
     "csn_cell_fwd": ([_f, _f, _f, _f, _f, ctypes.c_float, _f, _i64, _i64, _i64, _f], _int),
     "csn_cell_workspace_bytes": ([_i64, _i64], _sz),
     "csn_cell_bwd": ([_f, _f, _f, _f, _f, ctypes.c_float, _f, _f, _f, _f, _f, _f, _i64, _i64, _i64,

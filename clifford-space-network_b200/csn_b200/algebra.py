@@ -276,6 +276,33 @@ def emit_header(path: Path) -> str:
         lines.append(f"  L.m[{i}][{j}] = {_fmt_poly(ent)};")
         nz.append((i, j))
     lines += ["}", ""]
+    # vector-Jacobian product of (R h R~) with respect to the rotor components:
+    # dr_m = sum_ij G_i h_j dL_ij / dr_m, with L_ij a quadratic form in r
+    lines += [
+        "// dr[m] = sum_ij G[i] h[j] d(L[i][j]) / d r_m  (gradient of <G, R h R~> w.r.t. r)",
+        "__host__ __device__ __forceinline__ void ga3_sandwich_vjp(float r0, float r1, float r2, float r3,",
+        "                                                           const float h[8], const float G[8],",
+        "                                                           float dr[4]) {",
+        "  const float r[4] = {r0, r1, r2, r3};",
+        "  float d0 = 0.0f, d1 = 0.0f, d2 = 0.0f, d3 = 0.0f;",
+    ]
+    acc = {m: [] for m in range(4)}
+    for (i, j), ent in sorted(poly.items()):
+        for a_, b_, c in ent:
+            # d(c r_a r_b)/d r_m = c (delta_am r_b + delta_bm r_a)
+            for m in range(4):
+                k = (1 if a_ == m else 0) * 1 + (1 if b_ == m else 0) * 1
+                if a_ == m and b_ == m:
+                    acc[m].append((2 * c, a_, i, j))
+                elif a_ == m:
+                    acc[m].append((c, b_, i, j))
+                elif b_ == m:
+                    acc[m].append((c, a_, i, j))
+    for m in range(4):
+        for c, o, i, j in acc[m]:
+            coef = f"{float(c)}f * " if abs(c) != 1 else ("-" if c < 0 else "")
+            lines.append(f"  d{m} += {coef}r[{o}] * G[{i}] * h[{j}];")
+    lines += ["  dr[0] = d0; dr[1] = d1; dr[2] = d2; dr[3] = d3;", "}", ""]
     lines.append("// nonzero pattern of the Cl(3,0) sandwich map (block diagonal by grade)")
     lines.append(f"#define CSN_GA3_NNZ {len(nz)}")
     lines.append("")

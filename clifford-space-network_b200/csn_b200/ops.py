@@ -13,6 +13,8 @@ Ops (reference functions they replace, paths relative to the reference root):
                                (Cayley rotor + decay + scan in one pass)
 * :func:`cayley`            -- python/clifford_cl6.py:57, python/clifford_cl8.py:29,65
 * :func:`cell_step`         -- python/clifford_layer.py:50-115 CliffordTENNCell.forward
+* :func:`ga3_rotor_scan`    -- Cl(3,0) blade-basis form of the two-sided scan
+                               (layout include/clifford_configs.cuh:38-51)
 """
 from __future__ import annotations
 
@@ -22,7 +24,7 @@ import torch
 
 from . import _lib
 
-__all__ = ["rotor_scan", "fused_rotor_scan", "cayley", "cell_step", "BASIS"]
+__all__ = ["rotor_scan", "fused_rotor_scan", "cayley", "cell_step", "ga3_rotor_scan", "BASIS"]
 
 BASIS = {"triu": 0, "ga": 1}
 
@@ -242,3 +244,43 @@ class CellFunction(torch.autograd.Function):
 def cell_step(x, prev, W_rec, W_in, gamma_bias, dt: float = 0.02):
     """One CliffordTENNCell step: x [Bt, in_dim], prev [Bt, N, 16] -> next [Bt, N, 16]."""
     return CellFunction.apply(x, prev, W_rec, W_in, gamma_bias, dt)
+
+
+# ----------------------------------------------------------- Cl(3,0) blade scan
+class Ga3ScanFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, gens, dt, x, h0):
+        _require_cuda(gens, dt, x, h0)
+        g, d, xf, hf = _f32(gens), _f32(dt), _f32(x), _f32(h0)
+        B, T, N, _ = xf.shape
+        h = torch.empty_like(xf)
+        nbytes = _lib.load().csn_ga3_workspace_bytes(B, T, N)
+        ws = _workspace(nbytes, xf.device)
+        _lib.call("csn_ga3_scan_fwd", _ptr(g), _ptr(d), _ptr(xf), _ptr(hf), _ptr(h), B, T, N,
+                  _ptr(ws), nbytes, _stream(xf.device))
+        ctx.save_for_backward(g, d, hf, h)
+        ctx.dtypes = tuple(None if t is None else t.dtype for t in (gens, dt, x, h0))
+        return h.to(x.dtype)
+
+    @staticmethod
+    def backward(ctx, dh):
+        g, d, hf, h = ctx.saved_tensors
+        B, T, N, _ = h.shape
+        dg, ddt, dx = torch.empty_like(g), torch.empty_like(d), torch.empty_like(h)
+        dh0 = torch.empty_like(hf) if (hf is not None and ctx.needs_input_grad[3]) else None
+        nbytes = _lib.load().csn_ga3_workspace_bytes(B, T, N)
+        ws = _workspace(nbytes, h.device)
+        _lib.call("csn_ga3_scan_bwd", _ptr(g), _ptr(d), _ptr(hf), _ptr(h), _ptr(_f32(dh)), _ptr(dg),
+                  _ptr(ddt), _ptr(dx), _ptr(dh0), B, T, N, _ptr(ws), nbytes, _stream(h.device))
+        outs = [dg, ddt, dx, dh0]
+        return tuple(None if o is None else o.to(t) for o, t in zip(outs, ctx.dtypes))
+
+
+def ga3_rotor_scan(gens, dt, x, h0=None):
+    """Cl(3,0) affine rotor scan h_t = R_t h_{t-1} R~_t + x_t in the blade basis.
+
+    gens [B, T, N, 3] on (e12, e23, e31), dt [B, T], x [B, T, N, 8] on
+    [1, e1, e2, e3, e12, e23, e31, e123], h0 optional [B, N, 8].
+    """
+    B, T, N, _ = x.shape
+    return Ga3ScanFunction.apply(gens, dt.reshape(B, T), x, h0)

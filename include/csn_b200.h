@@ -126,6 +126,21 @@ int csn_cayley_fwd(const float* Omega, float* Q, int64_t count, int D, void* str
 int csn_cayley_bwd(const float* Q, const float* dQ, float* dOmega, int64_t count, int D,
                    void* stream);
 
+/* ---------------------------------------------------- Cl(3,0) blade-basis scan */
+/* h_t = R_t h_{t-1} R~_t + x_t with R_t = (1 - Om)^{-1}(1 + Om), Om = dt/2 (g12 e12 + g23 e23 +
+ * g31 e31), h_{-1} = h0 or 0.  Multivectors [B,T,N,8] in the layout [1,e1,e2,e3,e12,e23,e31,e123]
+ * of include/clifford_configs.cuh:38-51; gens [B,T,N,3]; dt [B,T].  The reference has no
+ * Cl(3) scan: this is the blade-basis form of python/clifford_scan.py:41 (two-sided) with
+ * the generated product tables of include/clifford_algebra.cuh:60-74. */
+size_t csn_ga3_workspace_bytes(int64_t B, int64_t T, int64_t N);
+int csn_ga3_scan_fwd(const float* gens, const float* dt, const float* x, const float* h0, float* h,
+                     int64_t B, int64_t T, int64_t N, void* workspace, size_t workspace_bytes,
+                     void* stream);
+/* Adjoint: dx, dgens, ddt [B,T] (summed over channels), dh0 (when h0 and dh0 are given). */
+int csn_ga3_scan_bwd(const float* gens, const float* dt, const float* h0, const float* h,
+                     const float* dh, float* dgens, float* ddt, float* dx, float* dh0, int64_t B,
+                     int64_t T, int64_t N, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------- Clifford cell */
 /* One step of the Clifford-LTC cell, python/clifford_layer.py:50-115 (CliffordTENNCell.
  * forward, 4 x 4 matrix form with the symmetric rational rotor of that file):

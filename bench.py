@@ -15,6 +15,8 @@ seeded, float32, shaped like the reference's configurations):
 * ``cl3`` -- Cl(3,0) blade-basis scan h_t = R_t h R~_t + x_t at the bandwidth scale of
   the Cl(3) configuration: batch 64, L 65536, 16 channels, gens ~ N(0, 0.1^2) on the 3
   bivectors, dt ~ U(0.01, 0.1), x ~ N(0, 1), dh ~ N(0, 1).
+* ``gen`` -- autoregressive O(1)-state generation, Cl(6,0), 256 streams x 8 channels:
+  p50 latency of one rotor step (graph-replayed) and tokens/s.
 
 N > 1 runs under torchrun: every rank owns its own batch (independent sequences, no
 data-path collective: weak scaling); time is the max over ranks.  ``--impl reference``
@@ -313,6 +315,119 @@ class Cl3:
 WORKLOADS = {"cl6_lm": Cl6LM, "cl3": Cl3}
 
 
+def run_generation(args, ws, rank, local, cores):
+    """Autoregressive O(1)-state generation, Cl(6,0): 256 streams x 8 channels, 8 x 8 state,
+    one rotor step per token (gens ~ N(0, 0.1^2), dt ~ U(0.01, 0.1), damped).  Reports the
+    p50 per-step latency of graph-replayed steps and tokens/s = streams / latency."""
+    import numpy as np
+    B, N, D, chunk, total = 256, 8, 8, 128, 2048
+    config = {"workload": "cl6_generation_step", "streams": B, "channels": N, "matrix_dim": D,
+              "steps": total, "graph_steps": chunk, "algebra": "Cl(6,0)", "damped": True}
+    metric = "rotor-step p50 latency (us), 256 streams x 8 channels Cl(6,0)"
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        from csn_b200 import algebra
+        from oracle import oracle as orc
+        E = algebra.triu_basis(D)
+        rng = np.random.default_rng(0)
+        h = np.zeros((B, N, D, D))
+        lat = []
+        for _ in range(max(1, args.steps)):
+            g = rng.standard_normal((B, 1, N, 28)) * 0.1
+            dt = rng.uniform(0.01, 0.1, (B, 1))
+            gam = np.log1p(np.exp(rng.standard_normal((B, 1, N))))
+            S = rng.standard_normal((B, 1, N, D, D))
+            t0 = time.perf_counter()
+            h = orc.rotor_scan_fwd(g, dt, gam, S, E, h0=h)[:, 0]
+            lat.append((time.perf_counter() - t0) * 1e6)
+        p50 = float(np.median(lat))
+        print(json.dumps({"metric": metric, "value": p50, "unit": "us", "n_gpus": 1, "steps": args.steps,
+                          "warmup": 0, "ms_per_step": p50 / 1e3, "higher_is_better": False,
+                          "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+                          "config": config, "impl": "reference", "tok_per_s": B / (p50 * 1e-6),
+                          "cpu_baseline": {"value": p50, "unit": "us", "cores": cores, "kind": "port",
+                                           "sample": "one step of 256 x 8 streams per sample, float64 C oracle"},
+                          "e2e": {"value": p50, "unit": "us", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}), flush=True)
+        return 0
+    import torch
+    from csn_b200 import _lib, ops
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    _lib.load()
+    g = ops.RotorStepGraph(B, N, D, steps=chunk, damped=True, device=dev)
+    gen = torch.Generator(device="cpu").manual_seed(0)
+    g.gens.copy_(torch.randn(chunk, B, N, 28, generator=gen) * 0.1)
+    g.dt.copy_(torch.rand(chunk, B, generator=gen) * 0.09 + 0.01)
+    g.gamma.copy_(torch.nn.functional.softplus(torch.randn(chunk, B, N, generator=gen)))
+    g.S.copy_(torch.randn(chunk, B, N, D, D, generator=gen))
+    for _ in range(max(3, args.warmup)):
+        g.replay()
+    torch.cuda.synchronize()
+    reps = total // chunk
+    lat = []
+    with ClockSampler(local) as clk:
+        for _ in range(max(reps, args.steps)):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            g.replay()
+            e1.record()
+            e1.synchronize()
+            lat.append(e0.elapsed_time(e1) * 1e3 / chunk)
+    p50 = float(np.median(lat))
+    # eager: one launch per step from the host (includes the host launch path)
+    eager = []
+    h = torch.zeros(B, N, D, D, device=dev)
+    for t in range(64):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        ops.rotor_step(g.gens[t % chunk], g.dt[t % chunk], g.gamma[t % chunk], g.S[t % chunk], h)
+        e1.record()
+        e1.synchronize()
+        eager.append(e0.elapsed_time(e1) * 1e3)
+    # end to end: pinned host inputs -> device, step, state back to host, per token
+    hin = {k: v[0].cpu().pin_memory() for k, v in (("gens", g.gens), ("dt", g.dt), ("gamma", g.gamma),
+                                                  ("S", g.S))}
+    hout = torch.empty(B, N, D, D).pin_memory()
+    e2e_lat = []
+    for _ in range(32):
+        t0 = time.perf_counter()
+        d = {k: v.to(dev, non_blocking=True) for k, v in hin.items()}
+        ops.rotor_step(d["gens"], d["dt"], d["gamma"], d["S"], h)
+        hout.copy_(h, non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+        e2e_lat.append((time.perf_counter() - t0) * 1e6)
+    h2d = sum(v.numel() * 4 for v in hin.values())
+    cpu = None
+    if not args.no_cpu_baseline:
+        from csn_b200 import algebra
+        from oracle import oracle as orc
+        E = algebra.triu_basis(D)
+        rng = np.random.default_rng(0)
+        hh = np.zeros((B, N, D, D))
+        cl = []
+        for _ in range(5):
+            a = (rng.standard_normal((B, 1, N, 28)) * 0.1, rng.uniform(0.01, 0.1, (B, 1)),
+                 np.log1p(np.exp(rng.standard_normal((B, 1, N)))), rng.standard_normal((B, 1, N, D, D)))
+            t0 = time.perf_counter()
+            hh = orc.rotor_scan_fwd(*a, E, h0=hh)[:, 0]
+            cl.append((time.perf_counter() - t0) * 1e6)
+        cpu = {"value": float(np.median(cl)), "unit": "us", "cores": cores, "kind": "port",
+               "sample": "5 steps of 256 x 8 streams, float64 C oracle"}
+    print(json.dumps({
+        "metric": metric, "value": p50, "unit": "us", "n_gpus": 1, "steps": len(lat) * chunk,
+        "warmup": max(3, args.warmup), "ms_per_step": p50 / 1e3, "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
+        "tok_per_s": B / (p50 * 1e-6), "p50_eager_us": float(np.median(eager)),
+        "gpu_launches": len(lat) * chunk, "clocks": clk.summary(),
+        "e2e": {"value": float(np.median(e2e_lat)), "unit": "us", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": hout.numel() * 4,
+                "timing": "wall clock per token: pinned inputs to device, step, state to host"},
+        "cpu_baseline": cpu}), flush=True)
+    return 0
+
+
 # ==================================================================================== main
 def main():
     ap = argparse.ArgumentParser()
@@ -320,7 +435,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="cl6_lm", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="cl6_lm", choices=sorted(WORKLOADS) + ["gen"])
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=None, help="per-rank batch (profiling: smaller)")
@@ -328,6 +443,8 @@ def main():
     args = ap.parse_args()
     ws, rank, local = dist_env()
     cores = os.cpu_count() or 1
+    if args.workload == "gen":
+        return run_generation(args, ws, rank, local, cores)
     kw = {}
     if args.batch is not None:
         kw["batch"] = args.batch

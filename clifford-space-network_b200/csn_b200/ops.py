@@ -24,7 +24,8 @@ import torch
 
 from . import _lib
 
-__all__ = ["rotor_scan", "fused_rotor_scan", "cayley", "cell_step", "ga3_rotor_scan", "BASIS"]
+__all__ = ["rotor_scan", "fused_rotor_scan", "cayley", "cell_step", "ga3_rotor_scan", "rotor_step",
+           "RotorStepGraph", "BASIS"]
 
 BASIS = {"triu": 0, "ga": 1}
 
@@ -284,3 +285,57 @@ def ga3_rotor_scan(gens, dt, x, h0=None):
     """
     B, T, N, _ = x.shape
     return Ga3ScanFunction.apply(gens, dt.reshape(B, T), x, h0)
+
+
+# ------------------------------------------------------------ O(1) generation step
+def rotor_step(gens, dt, gamma, S, h, basis: str = "triu", two_sided: bool = True):
+    """Advance the carried state one token, in place: h <- M h M^T + C.
+
+    gens [B, N, K], dt [B], gamma [B, N] (None = undamped), S [B, N, D, D], h [B, N, D, D]
+    (float32, contiguous, CUDA).  Inference only (no autograd).  Returns h.
+    """
+    _require_cuda(gens, dt, gamma, S, h)
+    if h.dtype != torch.float32 or not h.is_contiguous() or h.data_ptr() % 16:
+        raise ValueError("rotor_step updates h in place: h must be contiguous, aligned float32")
+    B, N, D, _ = h.shape
+    g, d, ga, s = _f32(gens), _f32(dt), _f32(gamma), _f32(S)
+    _lib.call("csn_rotor_step", _ptr(g), _ptr(d), _ptr(ga), _ptr(s), _ptr(h), B, N, D,
+              BASIS[basis], int(two_sided), _stream(h.device))
+    return h
+
+
+class RotorStepGraph:
+    """A CUDA graph of `steps` consecutive rotor steps on static buffers.
+
+    Fill ``gens[t], dt[t], gamma[t], S[t]`` (leading step axis) and call ``replay()``: the
+    state ``h`` advances `steps` tokens with one graph launch, i.e. without a host round
+    trip per token.  Capture happens once, at construction.
+    """
+
+    def __init__(self, B, N, D, steps=1, damped=True, basis="triu", two_sided=True, device="cuda"):
+        K = D * (D - 1) // 2 if basis == "triu" else (3 if D == 4 else 28)
+        dev = torch.device(device)
+        self.h = torch.zeros(B, N, D, D, device=dev)
+        self.gens = torch.zeros(steps, B, N, K, device=dev)
+        self.dt = torch.full((steps, B), 0.05, device=dev)
+        self.gamma = torch.ones(steps, B, N, device=dev) if damped else None
+        self.S = torch.zeros(steps, B, N, D, D, device=dev)
+        self.steps = steps
+        args = (BASIS[basis], int(two_sided))
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):  # warm-up launch outside the graph (lazy module load)
+            rotor_step(self.gens[0], self.dt[0], None if self.gamma is None else self.gamma[0],
+                       self.S[0], self.h, basis, two_sided)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        self.h.zero_()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=s):
+            for t in range(steps):
+                _lib.call("csn_rotor_step", _ptr(self.gens[t]), _ptr(self.dt[t]),
+                          _ptr(None if self.gamma is None else self.gamma[t]), _ptr(self.S[t]),
+                          _ptr(self.h), B, N, D, *args, ctypes.c_void_p(s.cuda_stream))
+
+    def replay(self):
+        self.graph.replay()
+        return self.h

@@ -339,6 +339,7 @@ struct Workspace {
 
 int get_ws(Workspace& w, void* user, size_t user_bytes, size_t need, cudaStream_t st) {
   w.stream = st;
+  if (need <= 256) return CSN_OK;  // single-chunk plan: no scratch at all
   if (user) {
     if (user_bytes < need) return set_error(CSN_ERR_INVALID, "workspace smaller than *_workspace_bytes()");
     w.base = static_cast<float*>(user);
@@ -640,6 +641,27 @@ extern "C" int csn_rotor_scan_fwd_noalloc(const float* gens, const float* dt, co
   a.gens = gens; a.dt = dt; a.gamma = gamma; a.S = S; a.h0 = h0; a.out = X;
   a.B = B; a.T = T; a.N = N;
   bind_ws(a, p, scratch, D);
+  if (D == 16) return scan16_dispatch(a, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, false, st);
+  return dispatch(a, D, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, false, st);
+}
+
+// ================================================================ O(1) state step
+// One recurrence step applied in place to a carried state: h <- M h M^T + C
+// (one-sided: M h + C), with (M, C) built from this step's generators, dt, gamma and S.
+// This is the T = 1 case of the fused scan with h0 = h; a single-chunk plan needs no
+// scratch, so the call allocates nothing and launches one kernel.
+extern "C" int csn_rotor_step(const float* gens, const float* dt, const float* gamma,
+                              const float* S, float* h, int64_t B, int64_t N, int D, int basis,
+                              int two_sided, void* stream) {
+  if (int rc = rotor_common_checks(gens, dt, S, B, 1, N, D, basis)) return rc;
+  if (B * N == 0) return CSN_OK;
+  if (!h || !aligned16(h)) return set_error(CSN_ERR_INVALID, "csn_rotor_step: h missing or misaligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Plan p = make_plan(B, 1, N, D, false);
+  ScanArgs a{};
+  a.gens = gens; a.dt = dt; a.gamma = gamma; a.S = S; a.h0 = h; a.out = h;
+  a.B = B; a.T = 1; a.N = N;
+  bind_ws(a, p, nullptr, D);
   if (D == 16) return scan16_dispatch(a, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, false, st);
   return dispatch(a, D, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, false, st);
 }

@@ -87,6 +87,39 @@ class CliffordCL6Block(nn.Module):
         out = h + self.gglu(self.ln_2(h))
         return out, Omega, dt.view(B, T)
 
+    # ------------------------------------------------ O(1)-state generation (extension)
+    def init_state(self, batch_size: int, device=None):
+        """Zero decoding state: (causal-conv window [B, d_model, k-1], rotor state [B, N, 8, 8]).
+
+        The reference has no step API (its generation re-runs the prefix,
+        tests/profile_performance.py:58-66); step() advances this state one token at O(1)
+        cost and produces the same outputs as forward() on the whole prefix."""
+        device = device if device is not None else self.in_proj.weight.device
+        k = self.conv1d.kernel_size[0]
+        return (torch.zeros(batch_size, self.d_model, k - 1, device=device),
+                torch.zeros(batch_size, self.num_neurons, 8, 8, device=device))
+
+    @torch.no_grad()
+    def step(self, x_t: torch.Tensor, state):
+        """One token: x_t [B, d_model] -> (out [B, d_model], new state).  The rotor state is
+        updated in place by the CUDA step kernel (csn_rotor_step)."""
+        conv_buf, X = state
+        B = x_t.shape[0]
+        N = self.num_neurons
+        window = torch.cat([conv_buf, self.ln_1(x_t).unsqueeze(-1)], dim=-1)       # oldest first
+        xc = F.silu((window * self.conv1d.weight[:, 0, :]).sum(-1) + self.conv1d.bias)
+        dt = F.softplus(self.time_head.proj(xc)) * self.time_head.dt_base          # [B, 1]
+        S = self.in_proj(xc).view(B, N, 8, 8)
+        gamma = F.softplus(self.gamma_proj(xc))
+        biv = self.biv_proj(xc).view(B, N, 28) * self.omega_scale
+        ops.rotor_step(biv, dt.view(B), gamma, S, X)
+        energy = torch.norm(X, dim=(-1, -2), keepdim=True)
+        X_spiked = X * surrogate_spike(energy, threshold=self.spike_threshold, beta=self.spike_beta)
+        feat = torch.einsum("ij,bjrc->birc", self.W_mix, X_spiked).reshape(B, N * 64)
+        h = x_t + self.out_proj(feat)
+        out = h + self.gglu(self.ln_2(h))
+        return out, (window[:, :, 1:].contiguous(), X)
+
 
 class CliffordCL6ForCausalLM(nn.Module):
     def __init__(self, vocab_size: int, d_model: int = 48, num_layers: int = 2, num_neurons: int = 6,

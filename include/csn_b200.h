@@ -115,6 +115,15 @@ int csn_rotor_scan_fwd_noalloc(const float* gens, const float* dt, const float* 
                                int64_t B, int64_t T, int64_t N, int D, int basis, int two_sided,
                                void* stream);
 
+/* O(1)-state generation step, in place: h <- M h M^T + C (one-sided: M h + C) with M, C built
+ * from this step's gens [B,N,K], dt [B], gamma [B,N] (NULL = undamped) and S [B,N,D,D];
+ * h [B,N,D,D].  Allocates nothing and launches one kernel, so a decode loop can capture it
+ * in a CUDA graph.  The reference has no step API: its generation re-runs the whole model
+ * on the growing prefix (tests/profile_performance.py:58-66); this is the recurrence of
+ * python/clifford_cl6.py:150-171 advanced by one token. */
+int csn_rotor_step(const float* gens, const float* dt, const float* gamma, const float* S, float* h,
+                   int64_t B, int64_t N, int D, int basis, int two_sided, void* stream);
+
 /* -------------------------------------------------------------------- Cayley */
 /* Q = (I - Omega)^{-1} (I + Omega) for `count` skew D x D matrices.
  * Replaces cayley_rotor_8x8 (python/clifford_cl6.py:57) and cayley_rotor_16x16 /

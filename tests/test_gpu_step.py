@@ -1,0 +1,85 @@
+"""O(1)-state generation (config 4): stepping the recurrence one token at a time equals
+the full scan, and the Cl(6) block's step() equals its forward() on the whole prefix."""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+def rel(a, ref):
+    a = a.detach().double().cpu().numpy() if torch.is_tensor(a) else a
+    ref = ref.detach().double().cpu().numpy() if torch.is_tensor(ref) else ref
+    return float(np.max(np.abs(a - ref)) / np.max(np.abs(ref)))
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from csn_b200 import _build, ops as o
+    _build.build()
+    return o
+
+
+@pytest.mark.parametrize("D,basis,damped", [(8, "triu", True), (8, "triu", False), (4, "ga", False),
+                                            (16, "triu", True)])
+def test_stepping_equals_scan_and_oracle(ops, oracle, D, basis, damped):
+    """256 streams x 8 channels (config 4 shape) for D = 8; fewer steps for the others."""
+    from csn_b200 import algebra
+    B, N, T = (256, 8, 2048) if D == 8 else (8, 2, 300)
+    E = algebra.triu_basis(D) if basis == "triu" else algebra.bivector_basis(algebra.CL3)
+    rng = np.random.default_rng(D + damped)
+    gens = rng.standard_normal((B, T, N, E.shape[0])) * 0.1 * (10 if D == 4 else 1)
+    dt = rng.uniform(0.01, 0.1, (B, T))
+    gamma = np.log1p(np.exp(rng.standard_normal((B, T, N)))) if damped else None
+    S = rng.standard_normal((B, T, N, D, D))
+    tg = torch.tensor(gens, dtype=torch.float32, device=DEV)
+    tdt = torch.tensor(dt, dtype=torch.float32, device=DEV)
+    tga = torch.tensor(gamma, dtype=torch.float32, device=DEV) if damped else None
+    tS = torch.tensor(S, dtype=torch.float32, device=DEV)
+    h = torch.zeros(B, N, D, D, device=DEV)
+    traj = []
+    for t in range(T):
+        ops.rotor_step(tg[:, t].contiguous(), tdt[:, t].contiguous(),
+                       None if tga is None else tga[:, t].contiguous(), tS[:, t].contiguous(), h, basis)
+        if t % 97 == 0 or t == T - 1:
+            traj.append((t, h.clone()))
+    X = ops.fused_rotor_scan(tg, tdt, tga, tS, basis=basis)
+    for t, ht in traj:
+        assert rel(ht, X[:, t]) < 1e-4
+    if D == 8:  # oracle on a slice of the streams (sequences are independent)
+        Xr = oracle.rotor_scan_fwd(gens[:16], dt[:16], None if gamma is None else gamma[:16], S[:16], E)
+        assert rel(traj[-1][1][:16], Xr[:, -1]) < 1e-4
+
+
+def test_step_graph_matches_step_loop(ops):
+    B, N, D, steps = 256, 8, 8, 64
+    g = ops.RotorStepGraph(B, N, D, steps=steps, damped=True)
+    gen = torch.Generator(device="cpu").manual_seed(0)
+    g.gens.copy_(torch.randn(steps, B, N, 28, generator=gen) * 0.1)
+    g.dt.copy_(torch.rand(steps, B, generator=gen) * 0.09 + 0.01)
+    g.gamma.copy_(torch.rand(steps, B, N, generator=gen))
+    g.S.copy_(torch.randn(steps, B, N, D, D, generator=gen))
+    g.h.zero_()
+    hg = g.replay().clone()
+    h = torch.zeros(B, N, D, D, device=DEV)
+    for t in range(steps):
+        ops.rotor_step(g.gens[t], g.dt[t], g.gamma[t], g.S[t], h)
+    assert torch.equal(hg, h)
+
+
+def test_cl6_block_step_equals_forward(ops):
+    from python.clifford_cl6 import CliffordCL6Block
+    torch.manual_seed(0)
+    blk = CliffordCL6Block(32, num_neurons=4).to(DEV).eval()
+    with torch.no_grad():
+        blk.time_head.proj.weight.normal_(0, 0.1)
+    x = torch.randn(3, 40, 32, device=DEV)
+    with torch.no_grad():
+        out_full, _, _ = blk(x)
+        state = blk.init_state(3)
+        outs = []
+        for t in range(40):
+            o, state = blk.step(x[:, t], state)
+            outs.append(o)
+    assert rel(torch.stack(outs, 1), out_full) < 1e-4

@@ -2,7 +2,7 @@
 """Throughput benchmark of the rotor-scan hot path (forward + backward).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload cl6_lm|cl3]
+                    [--workload cl6_lm|cl3|cl8|gen]
 
 Workloads (one "step" = one forward + backward pass over one batch of synthetic input,
 seeded, float32, shaped like the reference's configurations):
@@ -15,6 +15,9 @@ seeded, float32, shaped like the reference's configurations):
 * ``cl3`` -- Cl(3,0) blade-basis scan h_t = R_t h R~_t + x_t at the bandwidth scale of
   the Cl(3) configuration: batch 64, L 65536, 16 channels, gens ~ N(0, 0.1^2) on the 3
   bivectors, dt ~ U(0.01, 0.1), x ~ N(0, 1), dh ~ N(0, 1).
+* ``cl8`` -- Cl(8,0) ~ M_16(R) scan: batch 16, L 8192, 32 channels of 16 x 16 matrices,
+  28 GA bivector-blade generators ~ N(0, 0.05^2) mapped through rho, dt ~ U(0.005, 0.05),
+  x ~ N(0, 1), undamped.
 * ``gen`` -- autoregressive O(1)-state generation, Cl(6,0), 256 streams x 8 channels:
   p50 latency of one rotor step (graph-replayed) and tokens/s.
 
@@ -312,7 +315,96 @@ class Cl3:
                 f"fwd+bwd, float64 C oracle, OpenMP")
 
 
-WORKLOADS = {"cl6_lm": Cl6LM, "cl3": Cl3}
+class Cl8:
+    """Cl(8,0) ~ M_16(R) rotor scan (B16 L8192 C32), fwd + bwd: 28 GA bivector-blade
+    generators mapped through rho, undamped (h_t = R h R~ + x_t)."""
+    name = "cl8_rotor_scan_fwd_bwd"
+    T, N, D, K = 8192, 32, 16, 28
+
+    def __init__(self, batch=16, layers=1):
+        self.B = batch
+        n, k, N = self.D * self.D, self.K, self.N
+        self.op_bytes = 4.0 * ((k + 2 * n + 1.0 / N) + (n + n + k + 1.0 / N + n + k + 1.0 / N))
+        self.kernel_bytes = {
+            "fwd_apply": 4.0 * (k + 2 * n + 1.0 / N),
+            "fwd_reduce": 4.0 * (k + n + 1.0 / N),
+            "bwd_reduce": 4.0 * (n + k + 1.0 / N),
+            "bwd_apply": 4.0 * (3 * n + 2 * k + 2.0 / N + 1),
+        }
+        self.kernel_names = ["fwd_reduce", "fwd_carry", "fwd_apply", "bwd_reduce", "bwd_carry",
+                             "bwd_apply", "reduce_channels"]
+        self.elems_per_step = self.B * self.T * N
+        self.config = {"workload": self.name, "batch": self.B, "seq_len": self.T, "channels": N,
+                       "matrix_dim": self.D, "generators": k, "basis": "GA bivector blades via rho",
+                       "algebra": "Cl(8,0)", "sided": "two", "damped": False,
+                       "l2": "inputs larger than L2 (4.3 GB per tensor)"}
+
+    def _host(self, seed, batch):
+        import torch
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        return dict(gens=torch.randn(batch, self.T, self.N, self.K, generator=g) * 0.05,
+                    dt=torch.rand(batch, self.T, generator=g) * 0.045 + 0.005,
+                    S=torch.randn(batch, self.T, self.N, self.D, self.D, generator=g),
+                    dX=torch.randn(batch, self.T, self.N, self.D, self.D, generator=g))
+
+    def setup(self, dev, rank, lib):
+        import torch
+        self.dev = dev
+        self.inp = {k: v.to(dev) for k, v in self._host(7 + rank, self.B).items()}
+        self.out = dict(X=torch.empty_like(self.inp["S"]), dS=torch.empty_like(self.inp["S"]),
+                        dgens=torch.empty_like(self.inp["gens"]), ddt=torch.empty_like(self.inp["dt"]))
+        self.ws_bytes = lib.csn_rotor_scan_workspace_bytes(self.B, self.T, self.N, self.D)
+        self.work = torch.empty(self.ws_bytes, dtype=torch.uint8, device=dev)
+
+    def step(self, stream):
+        from csn_b200 import _lib
+        sp = ctypes.c_void_p(stream.cuda_stream)
+        I, O = self.inp, self.out
+        B, T, N, D = self.B, self.T, self.N, self.D
+        _lib.call("csn_rotor_scan_fwd", _p(I["gens"]), _p(I["dt"]), _p(None), _p(I["S"]), _p(None),
+                  _p(O["X"]), B, T, N, D, 1, 1, _p(self.work), self.ws_bytes, sp)
+        _lib.call("csn_rotor_scan_bwd", _p(I["gens"]), _p(I["dt"]), _p(None), _p(I["S"]), _p(None),
+                  _p(O["X"]), _p(I["dX"]), _p(O["dgens"]), _p(O["ddt"]), _p(None), _p(O["dS"]),
+                  _p(None), B, T, N, D, 1, 1, _p(self.work), self.ws_bytes, sp)
+
+    def e2e_setup(self):
+        import torch
+        self.host = {k: v.cpu().pin_memory() for k, v in self.inp.items()}
+        self.hout = {k: torch.empty_like(v, device="cpu").pin_memory() for k, v in self.out.items()}
+        return (sum(v.numel() * v.element_size() for v in self.host.values()),
+                sum(v.numel() * v.element_size() for v in self.hout.values()))
+
+    def e2e_step(self):
+        from csn_b200 import ops
+        H = self.host
+        gens = H["gens"].to(self.dev, non_blocking=True).requires_grad_(True)
+        dt = H["dt"].to(self.dev, non_blocking=True).requires_grad_(True)
+        S = H["S"].to(self.dev, non_blocking=True).requires_grad_(True)
+        dX = H["dX"].to(self.dev, non_blocking=True)
+        X = ops.fused_rotor_scan(gens, dt, None, S, basis="ga")
+        X.backward(dX)
+        for k, src in (("X", X.detach()), ("dS", S.grad), ("dgens", gens.grad), ("ddt", dt.grad)):
+            self.hout[k].copy_(src, non_blocking=True)
+
+    def cpu_reference(self, reps, warmup, sample_batch=1):
+        import numpy as np
+        from csn_b200 import algebra
+        from oracle import oracle as orc
+        E = algebra.bivector_basis(algebra.CL8)
+        h = self._host(3, sample_batch)
+        a = {k: v.double().numpy()[:, :, :4] if v.dim() > 2 else v.double().numpy() for k, v in h.items()}
+
+        def one():
+            X = orc.rotor_scan_fwd(a["gens"], a["dt"], None, a["S"], E)
+            orc.rotor_scan_bwd(a["gens"], a["dt"], None, a["S"], E, X, a["dX"])
+
+        el = _time_cpu(one, reps, warmup)
+        return (sample_batch * self.T * 4 * reps, el,
+                f"full-L slice B{sample_batch} L{self.T} C4 (of C{self.N}) per step, fwd+bwd, "
+                f"float64 C oracle, OpenMP")
+
+
+WORKLOADS = {"cl6_lm": Cl6LM, "cl3": Cl3, "cl8": Cl8}
 
 
 def run_generation(args, ws, rank, local, cores):

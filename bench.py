@@ -2,7 +2,7 @@
 """Throughput benchmark of the rotor-scan hot path (forward + backward).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload cl6_lm|cl3|cl8|gen]
+                    [--workload cl6_lm|cl3|cl8|gen|sp]
 
 Workloads (one "step" = one forward + backward pass over one batch of synthetic input,
 seeded, float32, shaped like the reference's configurations):
@@ -20,6 +20,8 @@ seeded, float32, shaped like the reference's configurations):
   x ~ N(0, 1), undamped.
 * ``gen`` -- autoregressive O(1)-state generation, Cl(6,0), 256 streams x 8 channels:
   p50 latency of one rotor step (graph-replayed) and tokens/s.
+* ``sp`` -- sequence-parallel long scan, Cl(6,0): B 8, L 2^20, C 64, time axis split over
+  the torchrun ranks (strong scaling), forward.
 
 N > 1 runs under torchrun: every rank owns its own batch (independent sequences, no
 data-path collective: weak scaling); time is the max over ranks.  ``--impl reference``
@@ -32,6 +34,8 @@ import argparse
 import ctypes
 import json
 import os
+
+import numpy as np
 import statistics
 import sys
 import threading
@@ -407,6 +411,107 @@ class Cl8:
 WORKLOADS = {"cl6_lm": Cl6LM, "cl3": Cl3, "cl8": Cl8}
 
 
+def run_sequence_parallel(args, ws, rank, local, cores):
+    """Config 5: one L = 2^20 sequence per (b, c), B 8, C 64, Cl(6,0) 8 x 8, undamped
+    (gens ~ N(0, 0.02^2), dt ~ U(0.001, 0.01), x ~ N(0, 1)), time axis split over the ranks
+    (strong scaling).  Forward with the shard-aggregate all-gather and carried-in rescan.
+    Channels run in slabs of min(64, 8 * ranks) so every rank holds ~42 GB; the slabs reuse
+    one set of input buffers."""
+    B, L, C, D, K = 8, 1 << 20, 64, 8, 28
+    Tl = L // ws
+    cs = min(C, 8 * ws)
+    nslab = C // cs
+    config = {"workload": "cl6_sequence_parallel_fwd", "batch": B, "seq_len": L, "channels": C,
+              "matrix_dim": D, "algebra": "Cl(6,0)", "damped": False, "ranks": ws,
+              "shard_len": Tl, "channel_slab": cs, "partition": "time axis, one shard per rank",
+              "exchange": "one all-gather of (P, c) per slab (NCCL)"}
+    elems = B * L * C
+    n = D * D
+    op_bytes = 4.0 * (K + 2 * n + 1.0 / C)  # gens, x -> h
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        from csn_b200 import algebra
+        from oracle import oracle as orc
+        E = algebra.triu_basis(D)
+        rng = np.random.default_rng(0)
+        Ts = 16384
+        a = (rng.standard_normal((1, Ts, 4, K)) * 0.02, rng.uniform(0.001, 0.01, (1, Ts)), None,
+             rng.standard_normal((1, Ts, 4, D, D)))
+        el = _time_cpu(lambda: orc.rotor_scan_fwd(*a, E), max(1, args.steps), 0)
+        v = Ts * 4 * max(1, args.steps) / el / 1e9
+        print(json.dumps({"metric": METRIC.replace("fwd+bwd", "fwd"), "value": v, "unit": UNIT,
+                          "n_gpus": args.gpus, "steps": args.steps, "warmup": 0,
+                          "ms_per_step": el / max(1, args.steps) * 1e3, "higher_is_better": True,
+                          "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+                          "config": config, "impl": "reference",
+                          "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
+                                           "sample": f"B1 L{Ts} C4 slice, forward, float64 C oracle"},
+                          "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}), flush=True)
+        return 0
+    import torch
+    from csn_b200 import _lib, ops
+    from csn_b200.sequence_parallel import sp_forward
+    if ws > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    _lib.load()
+    g = torch.Generator(device=dev).manual_seed(17 + rank)
+    gens = torch.randn(B, Tl, cs, K, device=dev, generator=g) * 0.02
+    dt = torch.rand(B, Tl, device=dev, generator=g) * 0.009 + 0.001
+    S = torch.randn(B, Tl, cs, D, D, device=dev, generator=g)
+
+    def step():
+        for _ in range(nslab):
+            if ws > 1:
+                sp_forward(gens, dt, None, S, None, None, "triu", True)
+            else:
+                ops.fused_rotor_scan(gens, dt, None, S)
+
+    def barrier():
+        if ws > 1:
+            torch.distributed.barrier()
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps = max(1, args.steps)
+    with ClockSampler(local) as clk:
+        e0.record()
+        for _ in range(steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1)
+    if ws > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = t.item()
+    ms_step = ms / steps
+    value = elems / (ms_step * 1e-3) / 1e9
+    hbm, peak_kind = peaks()
+    if rank == 0:
+        ach = op_bytes * elems / ws / (ms_step * 1e-3) / 1e9
+        print(json.dumps({"metric": METRIC.replace("fwd+bwd", "fwd"), "value": value, "unit": UNIT,
+                          "n_gpus": ws, "steps": steps, "warmup": max(3, args.warmup),
+                          "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+                          "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
+                          "op_roofline": {"achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
+                                          "bytes_per_elem": op_bytes, "note": "per rank"},
+                          "clocks": clk.summary()}), flush=True)
+    if ws > 1:
+        torch.distributed.destroy_process_group()
+    return 0
+
+
 def run_generation(args, ws, rank, local, cores):
     """Autoregressive O(1)-state generation, Cl(6,0): 256 streams x 8 channels, 8 x 8 state,
     one rotor step per token (gens ~ N(0, 0.1^2), dt ~ U(0.01, 0.1), damped).  Reports the
@@ -527,7 +632,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="cl6_lm", choices=sorted(WORKLOADS) + ["gen"])
+    ap.add_argument("--workload", default="cl6_lm", choices=sorted(WORKLOADS) + ["gen", "sp"])
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=None, help="per-rank batch (profiling: smaller)")
@@ -537,6 +642,8 @@ def main():
     cores = os.cpu_count() or 1
     if args.workload == "gen":
         return run_generation(args, ws, rank, local, cores)
+    if args.workload == "sp":
+        return run_sequence_parallel(args, ws, rank, local, cores)
     kw = {}
     if args.batch is not None:
         kw["batch"] = args.batch

@@ -35,6 +35,11 @@ SIGNATURES = {
                             _int, _int, _f, _sz, _f], _int),
     "csn_rotor_scan_fwd_noalloc": ([_f, _f, _f, _f, _f, _f, _i64, _i64, _i64, _int, _int, _int,
                                     _f], _int),
+    "csn_rotor_scan_aggregate_workspace_bytes": ([_i64, _i64, _i64, _int], _sz),
+    "csn_rotor_scan_aggregate": ([_f, _f, _f, _f, _f, _f, _i64, _i64, _i64, _int, _int, _int, _f,
+                                  _sz, _f], _int),
+    "csn_rotor_scan_bwd_aggregate": ([_f, _f, _f, _f, _f, _i64, _i64, _i64, _int, _int, _int, _f,
+                                      _sz, _f], _int),
     "csn_rotor_step": ([_f, _f, _f, _f, _f, _i64, _i64, _int, _int, _int, _f], _int),
     "csn_cayley_fwd": ([_f, _f, _i64, _int, _f], _int),
     "csn_cayley_bwd": ([_f, _f, _f, _i64, _int, _f], _int),

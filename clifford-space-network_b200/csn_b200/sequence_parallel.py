@@ -1,0 +1,189 @@
+"""Sequence-parallel rotor scan: one long sequence split over the ranks of a process group.
+
+Rank g holds time steps [g*T, (g+1)*T) of every (batch, channel) sequence.  The scan is
+associative, so each shard is summarised by its aggregate and only those summaries
+cross GPUs (one all-gather of B*N pairs of D x D matrices per pass):
+
+forward
+  1. (P_g, c_g) = shard aggregate: P = M_last ... M_first, c = shard scanned from zero
+  2. all-gather (P, c)
+  3. carry-in h_g = scan of (P_r, c_r), r < g            (plain scan kernel, X_0 = c_0)
+  4. rescan the shard from h_g                          (fused rotor scan with h0 = h_g)
+backward (mirror image in reverse time)
+  1. c'_g = gradient leaving the shard at its first step with zero gradient from the right
+  2. all-gather c'
+  3. H_g = reverse scan of (P_r^T, c'_r), r > g           (gradient entering from the right)
+  4. local adjoint with h0 = h_g and dX[:, -1] += H_g
+
+The cross-shard compositions run on the same CUDA kernels as everything else.  Before
+each exchange the ranks all-gather a small header (shapes, flags) so that a rank with a
+mismatched shard is reported on every rank instead of deadlocking the collective, and
+the gathered carries are checked for non-finite values on every rank alike.
+
+The kernel calls go through a backend object (``CudaBackend`` here); tests substitute a
+CPU backend to exercise the exchange logic with the gloo backend.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from .ops import BASIS, _f32, _ptr, _require_cuda, _stream, _workspace
+
+
+class ShardMismatchError(RuntimeError):
+    """Ranks disagree on the shard layout, or a gathered carry is not finite."""
+
+
+class CudaBackend:
+    """Shard primitives on the CUDA library (float32, current stream)."""
+
+    def fwd_aggregate(self, gens, dt, gamma, S, basis, two_sided):
+        B, T, N, D, _ = S.shape
+        P = torch.empty(B, N, D, D, device=S.device)
+        c = torch.empty_like(P)
+        n = _lib.load().csn_rotor_scan_aggregate_workspace_bytes(B, T, N, D)
+        ws = _workspace(n, S.device)
+        _lib.call("csn_rotor_scan_aggregate", _ptr(gens), _ptr(dt), _ptr(gamma), _ptr(S), _ptr(P), _ptr(c),
+                  B, T, N, D, BASIS[basis], int(two_sided), _ptr(ws), n, _stream(S.device))
+        return P, c
+
+    def bwd_aggregate(self, gens, dt, gamma, dX, basis, two_sided):
+        B, T, N, D, _ = dX.shape
+        c = torch.empty(B, N, D, D, device=dX.device)
+        n = _lib.load().csn_rotor_scan_aggregate_workspace_bytes(B, T, N, D)
+        ws = _workspace(n, dX.device)
+        _lib.call("csn_rotor_scan_bwd_aggregate", _ptr(gens), _ptr(dt), _ptr(gamma), _ptr(dX), _ptr(c),
+                  B, T, N, D, BASIS[basis], int(two_sided), _ptr(ws), n, _stream(dX.device))
+        return c
+
+    def scan_mc(self, M, C, two_sided):
+        from .ops import _scan_fwd
+        return _scan_fwd(_f32(M), _f32(C), None, two_sided)
+
+    def rotor_fwd(self, gens, dt, gamma, S, h0, basis, two_sided):
+        B, T, N, D, _ = S.shape
+        X = torch.empty_like(S)
+        n = _lib.load().csn_rotor_scan_workspace_bytes(B, T, N, D)
+        ws = _workspace(n, S.device)
+        _lib.call("csn_rotor_scan_fwd", _ptr(gens), _ptr(dt), _ptr(gamma), _ptr(S), _ptr(h0), _ptr(X),
+                  B, T, N, D, BASIS[basis], int(two_sided), _ptr(ws), n, _stream(S.device))
+        return X
+
+    def rotor_bwd(self, gens, dt, gamma, S, h0, X, dX, basis, two_sided):
+        B, T, N, D, _ = S.shape
+        dg, ddt, dS = torch.empty_like(gens), torch.empty_like(dt), torch.empty_like(S)
+        dga = torch.empty_like(gamma) if gamma is not None else None
+        n = _lib.load().csn_rotor_scan_workspace_bytes(B, T, N, D)
+        ws = _workspace(n, S.device)
+        _lib.call("csn_rotor_scan_bwd", _ptr(gens), _ptr(dt), _ptr(gamma), _ptr(S), _ptr(h0), _ptr(X),
+                  _ptr(dX), _ptr(dg), _ptr(ddt), _ptr(dga), _ptr(dS), _ptr(None), B, T, N, D,
+                  BASIS[basis], int(two_sided), _ptr(ws), n, _stream(S.device))
+        return dg, ddt, dga, dS
+
+
+def _world(group):
+    return dist.get_world_size(group), dist.get_rank(group)
+
+
+def _check_header(local: torch.Tensor, group, what: str):
+    """All-gather a small int64 header; raise the same error on every rank on mismatch."""
+    ws, _ = _world(group)
+    hdr = [torch.empty_like(local) for _ in range(ws)]
+    dist.all_gather(hdr, local, group=group)
+    ref = hdr[0]
+    for r, h in enumerate(hdr):
+        if not torch.equal(h, ref):
+            raise ShardMismatchError(f"{what}: rank {r} shard header {h.tolist()} != rank 0 {ref.tolist()}")
+
+
+def _gather(t: torch.Tensor, group):
+    ws, _ = _world(group)
+    out = [torch.empty_like(t) for _ in range(ws)]
+    dist.all_gather(out, t.contiguous(), group=group)
+    return out
+
+
+def _check_finite(ts, what):
+    for r, t in enumerate(ts):
+        if not bool(torch.isfinite(t).all()):
+            raise ShardMismatchError(f"{what}: carry from rank {r} is not finite")
+
+
+def sp_forward(gens, dt, gamma, S, group=None, backend=None, basis="triu", two_sided=True):
+    """Forward of the sequence-parallel scan on this rank's shard.
+
+    Returns (X_local, h_in, Ps): the shard trajectory, the carry-in (None on rank 0) and the
+    gathered shard products (kept for the backward pass)."""
+    backend = backend or CudaBackend()
+    ws, g = _world(group)
+    B, T, N, D, _ = S.shape
+    dev = S.device
+    flags = int(gamma is not None) * 1 + int(two_sided) * 2 + (BASIS[basis] << 2)
+    _check_header(torch.tensor([B, T, N, D, gens.shape[-1], flags], dtype=torch.int64, device=dev),
+                  group, "sequence-parallel forward")
+    P, c = backend.fwd_aggregate(gens, dt, gamma, S, basis, two_sided)
+    Ps, cs = _gather(P, group), _gather(c, group)
+    _check_finite(Ps + cs, "sequence-parallel forward")
+    h_in = None
+    if g > 0:
+        Mseq = torch.stack(Ps[:g], dim=1)        # [B, g, N, D, D]
+        Cseq = torch.stack(cs[:g], dim=1)
+        h_in = backend.scan_mc(Mseq, Cseq, two_sided)[:, -1].contiguous()
+    X = backend.rotor_fwd(gens, dt, gamma, S, h_in, basis, two_sided)
+    return X, h_in, Ps
+
+
+def sp_backward(gens, dt, gamma, S, X, dX, h_in, Ps, group=None, backend=None, basis="triu",
+                two_sided=True):
+    """Backward of the sequence-parallel scan: (dgens, ddt, dgamma, dS) of this shard."""
+    backend = backend or CudaBackend()
+    ws, g = _world(group)
+    B, T, N, D, _ = S.shape
+    _check_header(torch.tensor([B, T, N, D, int(dX.shape == S.shape)], dtype=torch.int64,
+                               device=S.device), group, "sequence-parallel backward")
+    cb = backend.bwd_aggregate(gens, dt, gamma, dX, basis, two_sided)
+    cbs = _gather(cb, group)
+    _check_finite(cbs, "sequence-parallel backward")
+    dXl = dX
+    if g < ws - 1:
+        later = list(range(ws - 1, g, -1))         # r = G-1 .. g+1
+        Mseq = torch.stack([Ps[r].transpose(-1, -2) for r in later], dim=1)
+        Cseq = torch.stack([cbs[r] for r in later], dim=1)
+        H = backend.scan_mc(Mseq, Cseq, two_sided)[:, -1]
+        dXl = dX.clone()
+        dXl[:, -1] += H
+    return backend.rotor_bwd(gens, dt, gamma, S, h_in, X, dXl.contiguous(), basis, two_sided)
+
+
+class SequenceParallelRotorScan(torch.autograd.Function):
+    """Autograd wrapper: every rank calls it with its own time shard (same B, N, D, K)."""
+
+    @staticmethod
+    def forward(ctx, gens, dt, gamma, S, group, basis, two_sided):
+        _require_cuda(gens, dt, gamma, S)
+        g, d, ga, s = _f32(gens), _f32(dt), _f32(gamma), _f32(S)
+        X, h_in, Ps = sp_forward(g, d, ga, s, group, None, basis, two_sided)
+        ctx.save_for_backward(g, d, ga, s, X, h_in, *Ps)
+        ctx.group, ctx.basis, ctx.two_sided = group, basis, two_sided
+        return X
+
+    @staticmethod
+    def backward(ctx, dX):
+        g, d, ga, s, X, h_in, *Ps = ctx.saved_tensors
+        dg, ddt, dga, dS = sp_backward(g, d, ga, s, X, _f32(dX), h_in, list(Ps), ctx.group, None,
+                                       ctx.basis, ctx.two_sided)
+        return dg, ddt, dga, dS, None, None, None
+
+
+def sequence_parallel_rotor_scan(gens, dt, gamma, S, group=None, basis="triu", two_sided=True):
+    """Rotor scan of a sequence whose time axis is sharded over the ranks of `group`.
+
+    Each rank passes its own shard ([B, T_local, N, ...]); ranks must be ordered by time.
+    """
+    B, T, N = S.shape[:3]
+    return SequenceParallelRotorScan.apply(gens, dt.reshape(B, T), None if gamma is None else
+                                           gamma.reshape(B, T, N), S, group, basis, bool(two_sided))

@@ -208,4 +208,99 @@ static __global__ void reduce_channels_kernel(const float* __restrict__ part, fl
   out[i] = s;
 }
 
+// ------------------------------------------------------------ shard aggregates
+// Forward: fold the chunk aggregates of one sequence into the shard aggregate
+//   (P, c) <- (P_j P, P_j c P_j^T + c_j)   (one-sided: P_j c + c_j),  j = 0 .. nchunks-1
+// Backward (REVERSE): H <- P_j^T H P_j + c'_j for j = nchunks-1 .. 0, output H.
+// One warp per sequence, lane l owns D*D/32 entries (D = 4: lanes 0..15 own one each).
+template <int D, bool TWO, bool REVERSE>
+__global__ void __launch_bounds__(128) compose_kernel(ScanArgs a) {
+  constexpr int DD = D * D;
+  constexpr int PER = DD >= 32 ? DD / 32 : 1;
+  __shared__ float sh_h[4][DD];
+  __shared__ float sh_P[4][DD];
+  __shared__ float sh_acc[4][DD];
+  __shared__ float sh_y[4][DD];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t s = blockIdx.x * 4 + w;
+  if (s >= a.B * a.N) return;
+  float* h = sh_h[w];
+  float* P = sh_P[w];
+  float* acc = sh_acc[w];  // running product (forward only)
+  float* y = sh_y[w];
+#pragma unroll
+  for (int q = 0; q < PER; ++q) {
+    const int idx = lane + 32 * q;
+    if (idx < DD) {
+      h[idx] = 0.0f;
+      acc[idx] = (idx / D == idx % D) ? 1.0f : 0.0f;
+    }
+  }
+  __syncwarp();
+  for (int64_t k = 0; k < a.nchunks; ++k) {
+    const int64_t j = REVERSE ? (a.nchunks - 1 - k) : k;
+    float cv[PER];
+#pragma unroll
+    for (int q = 0; q < PER; ++q) {
+      const int idx = lane + 32 * q;
+      if (idx < DD) {
+        P[idx] = a.aggP[(s * a.nchunks + j) * DD + idx];
+        cv[q] = a.aggC[(s * a.nchunks + j) * DD + idx];
+      }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < PER; ++q) {  // y = P h (forward) | P^T h (reverse)
+      const int idx = lane + 32 * q, i = idx / D, jj = idx % D;
+      if (idx < DD) {
+        float v = 0.0f;
+#pragma unroll
+        for (int kk = 0; kk < D; ++kk) v = fmaf(REVERSE ? P[kk * D + i] : P[i * D + kk], h[kk * D + jj], v);
+        y[idx] = v;
+      }
+    }
+    __syncwarp();
+    float nv[PER], na[PER];
+#pragma unroll
+    for (int q = 0; q < PER; ++q) {
+      const int idx = lane + 32 * q, i = idx / D, l = idx % D;
+      if (idx < DD) {
+        float v;
+        if (TWO) {  // y P^T (forward) | y P (reverse)
+          v = 0.0f;
+#pragma unroll
+          for (int kk = 0; kk < D; ++kk) v = fmaf(y[i * D + kk], REVERSE ? P[kk * D + l] : P[l * D + kk], v);
+        } else {
+          v = y[idx];
+        }
+        nv[q] = v + cv[q];
+        if (!REVERSE) {  // running product P_j acc
+          float p = 0.0f;
+#pragma unroll
+          for (int kk = 0; kk < D; ++kk) p = fmaf(P[i * D + kk], acc[kk * D + l], p);
+          na[q] = p;
+        }
+      }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < PER; ++q) {
+      const int idx = lane + 32 * q;
+      if (idx < DD) {
+        h[idx] = nv[q];
+        if (!REVERSE) acc[idx] = na[q];
+      }
+    }
+    __syncwarp();
+  }
+#pragma unroll
+  for (int q = 0; q < PER; ++q) {
+    const int idx = lane + 32 * q;
+    if (idx < DD) {
+      a.c_out[s * DD + idx] = h[idx];
+      if (!REVERSE && a.P_out) a.P_out[s * DD + idx] = acc[idx];
+    }
+  }
+}
+
 }  // namespace csn

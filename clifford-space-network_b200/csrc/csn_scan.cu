@@ -143,7 +143,7 @@ __global__ void __launch_bounds__(128) bwd_reduce_kernel(ScanArgs a) {
   const int64_t n = tid % a.N;
   const int64_t j = (tid / a.N) % a.nchunks;
   const int64_t b = tid / (a.N * a.nchunks);
-  if (j == 0) return;  // chunk 0's aggregate is never needed (dh0 comes from the apply pass)
+  if (j == 0 && !a.agg_mode) return;  // chunk 0's aggregate only matters for shard aggregates
   const int64_t t0 = j * a.chunk;
   const int64_t t1 = min(a.T, t0 + a.chunk);
 
@@ -370,6 +370,11 @@ int run_fwd(ScanArgs a, cudaStream_t st) {
   const int64_t S = a.B * a.N;
   const int64_t total = S * a.nchunks;
   if (total == 0) return CSN_OK;
+  if (a.agg_mode) {
+    fwd_reduce_kernel<D, SRC, BASIS, DAMPED, TWO><<<blocks_for(total, 128), 128, 0, st>>>(a);
+    compose_kernel<D, TWO, false><<<blocks_for(S, 4), 128, 0, st>>>(a);
+    return check_launch("shard aggregate (forward)");
+  }
   if (a.nchunks > 1) {
     {
       KernelTimer kt("fwd_reduce", st);
@@ -390,6 +395,12 @@ template <int D, int SRC, int BASIS, bool DAMPED, bool TWO>
 int run_bwd(ScanArgs a, cudaStream_t st) {
   const int64_t S = a.B * a.N;
   const int64_t total = S * a.nchunks;
+  if (a.agg_mode) {
+    if (total == 0) return CSN_OK;
+    bwd_reduce_kernel<D, SRC, BASIS, DAMPED, TWO><<<blocks_for(total, 128), 128, 0, st>>>(a);
+    compose_kernel<D, TWO, true><<<blocks_for(S, 4), 128, 0, st>>>(a);
+    return check_launch("shard aggregate (backward)");
+  }
   if (total > 0) {
     if (a.nchunks > 1) {
       {
@@ -664,4 +675,63 @@ extern "C" int csn_rotor_step(const float* gens, const float* dt, const float* g
   bind_ws(a, p, nullptr, D);
   if (D == 16) return scan16_dispatch(a, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, false, st);
   return dispatch(a, D, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, false, st);
+}
+
+// ======================================================= sequence-parallel shard aggregates
+// A time shard [t0, t1) of every sequence, summarised for the cross-shard carry exchange:
+//   forward:  P = M_{t1-1} ... M_{t0},  c = final state of the shard scanned from zero
+//   backward: c' = gradient that leaves the shard at its first step when no gradient
+//             enters from the right (the shard's dh0 with zero right carry)
+// A shard's carry-in is then the scan of the earlier shards' (P, c) pairs, and its
+// gradient carry-in the reverse scan of the later shards' (P^T, c') pairs.
+static size_t agg_bytes(int64_t B, int64_t T, int64_t N, int D) {
+  Plan p = make_plan(B, T, N, D, false);
+  const int64_t nch = p.nchunks > 0 ? p.nchunks : 1;
+  return (size_t)3 * B * N * nch * D * D * sizeof(float) + 256;
+}
+
+extern "C" size_t csn_rotor_scan_aggregate_workspace_bytes(int64_t B, int64_t T, int64_t N, int D) {
+  if (B < 0 || T < 0 || N < 0 || D < 1) return 0;
+  return agg_bytes(B, T, N, D);
+}
+
+static int run_aggregate(bool bwd, const float* gens, const float* dt, const float* gamma,
+                         const float* S, const float* dX, float* P_out, float* c_out, int64_t B,
+                         int64_t T, int64_t N, int D, int basis, int two_sided, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+  if (int rc = rotor_common_checks(gens, dt, bwd ? dX : S, B, T, N, D, basis)) return rc;
+  if (B * N == 0) return CSN_OK;
+  if (T == 0) return set_error(CSN_ERR_INVALID, "shard aggregate: empty shard (T = 0)");
+  if (!c_out || !aligned16(c_out) || (P_out && !aligned16(P_out)))
+    return set_error(CSN_ERR_INVALID, "shard aggregate: outputs missing or misaligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Plan p = make_plan(B, T, N, D, false);
+  if (p.nchunks < 1) p.nchunks = 1;
+  p.agg_floats = (size_t)3 * B * N * p.nchunks * D * D;
+  Workspace ws;
+  if (int rc = get_ws(ws, workspace, workspace_bytes, agg_bytes(B, T, N, D), st)) return rc;
+  ScanArgs a{};
+  a.gens = gens; a.dt = dt; a.gamma = gamma; a.S = S; a.dX = dX;
+  a.B = B; a.T = T; a.N = N;
+  a.agg_mode = 1; a.P_out = P_out; a.c_out = c_out;
+  bind_ws(a, p, ws.base, D);
+  if (D == 16) return scan16_dispatch(a, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, bwd, st);
+  return dispatch(a, D, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, bwd, st);
+}
+
+extern "C" int csn_rotor_scan_aggregate(const float* gens, const float* dt, const float* gamma,
+                                        const float* S, float* P_out, float* c_out, int64_t B,
+                                        int64_t T, int64_t N, int D, int basis, int two_sided,
+                                        void* workspace, size_t workspace_bytes, void* stream) {
+  if (!P_out) return set_error(CSN_ERR_INVALID, "csn_rotor_scan_aggregate: P_out is required");
+  return run_aggregate(false, gens, dt, gamma, S, nullptr, P_out, c_out, B, T, N, D, basis,
+                       two_sided, workspace, workspace_bytes, stream);
+}
+
+extern "C" int csn_rotor_scan_bwd_aggregate(const float* gens, const float* dt, const float* gamma,
+                                            const float* dX, float* c_out, int64_t B, int64_t T,
+                                            int64_t N, int D, int basis, int two_sided,
+                                            void* workspace, size_t workspace_bytes, void* stream) {
+  return run_aggregate(true, gens, dt, gamma, nullptr, dX, nullptr, c_out, B, T, N, D, basis,
+                       two_sided, workspace, workspace_bytes, stream);
 }

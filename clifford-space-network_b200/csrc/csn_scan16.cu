@@ -312,7 +312,7 @@ template <int SRC, int BASIS, bool DAMPED, bool TWO>
 __global__ void __launch_bounds__(128) bwd_reduce16(ScanArgs a) {
   constexpr int K = GenCount<16, BASIS>::K;
   S16_SETUP();
-  if (j == 0) return;
+  if (j == 0 && !a.agg_mode) return;
   float o[8];
 #pragma unroll
   for (int q = 0; q < 8; ++q) {
@@ -515,6 +515,17 @@ template <int SRC, int BASIS, bool DAMPED, bool TWO>
 int run16(const ScanArgs& a, bool bwd, cudaStream_t st) {
   const int64_t S = a.B * a.N;
   const int64_t total = S * a.nchunks;
+  if (a.agg_mode) {
+    if (total == 0) return CSN_OK;
+    if (!bwd) {
+      fwd_reduce16<SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(a);
+      compose_kernel<16, TWO, false><<<nblk(S), 128, 0, st>>>(a);
+    } else {
+      bwd_reduce16<SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(a);
+      compose_kernel<16, TWO, true><<<nblk(S), 128, 0, st>>>(a);
+    }
+    return check_launch("shard aggregate (D=16)");
+  }
   if (!bwd) {
     if (total == 0) return CSN_OK;
     if (a.nchunks > 1) {

@@ -301,7 +301,7 @@ __global__ void __launch_bounds__(THREADS, 2) bwd8_reduce_kernel(ScanArgs a) {
   if (tid >= a.B * a.N * a.nchunks) return;
   int64_t b, n, j;
   thread_coords(a, tid, b, n, j);
-  if (j == 0) return;
+  if (j == 0 && !a.agg_mode) return;
   const int64_t s = b * a.N + n;
   const int64_t t0 = j * a.chunk, t1 = min(a.T, t0 + a.chunk);
   float* slot = s8_smem + threadIdx.x * BwdRedSlot::STRIDE;
@@ -695,6 +695,19 @@ int run8(const ScanArgs& a, bool bwd, cudaStream_t st) {
   const int fwd_bytes = THREADS * FwdSlot::STRIDE * 4;
   const int red_bytes = THREADS * BwdRedSlot::STRIDE * 4;
   const int app_bytes = THREADS * BwdAppSlot::STRIDE * 4;
+  if (a.agg_mode) {
+    if (total == 0) return CSN_OK;
+    if (!bwd) {
+      set_smem(fwd8_kernel<true, DAMPED, TWO>, fwd_bytes);
+      fwd8_kernel<true, DAMPED, TWO><<<nblk(total), THREADS, fwd_bytes, st>>>(a);
+      compose_kernel<8, TWO, false><<<(unsigned)((S + 3) / 4), 128, 0, st>>>(a);
+    } else {
+      set_smem(bwd8_reduce_kernel<DAMPED, TWO>, red_bytes);
+      bwd8_reduce_kernel<DAMPED, TWO><<<nblk(total), THREADS, red_bytes, st>>>(a);
+      compose_kernel<8, TWO, true><<<(unsigned)((S + 3) / 4), 128, 0, st>>>(a);
+    }
+    return check_launch("shard aggregate (D=8)");
+  }
   if (!bwd) {
     if (total == 0) return CSN_OK;
     if (a.nchunks > 1) {

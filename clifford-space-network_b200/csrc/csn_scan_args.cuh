@@ -34,6 +34,12 @@ struct ScanArgs {
   float* carry;  // [S, nchunks, D, D]
   int64_t B, T, N;
   int64_t nchunks, chunk;
+  // aggregate-only mode (sequence-parallel shards): reduce + compose, no apply pass.
+  //   forward:  P_out = M_{T-1} ... M_0, c_out = final state of a zero-carry scan
+  //   backward: c_out = gradient leaving the shard at t = 0 with zero carry from t = T
+  int agg_mode;
+  float* P_out;  // [B, N, D, D]
+  float* c_out;  // [B, N, D, D]
 };
 
 __device__ __forceinline__ int64_t elem(const ScanArgs& a, int64_t b, int64_t t, int64_t n) {

@@ -115,6 +115,25 @@ int csn_rotor_scan_fwd_noalloc(const float* gens, const float* dt, const float* 
                                int64_t B, int64_t T, int64_t N, int D, int basis, int two_sided,
                                void* stream);
 
+/* ------------------------------------------------ sequence-parallel shard aggregates */
+/* Summaries of one time shard (the local [B, T, N, ...] slice of a longer sequence) for the
+ * cross-GPU carry exchange of the sequence-parallel scan.  The reference has no distributed
+ * code; these are the chunk aggregates of its associative operator (python/clifford_scan.py:19-38)
+ * taken over a whole shard:
+ *   csn_rotor_scan_aggregate:     P_out = M_{T-1} ... M_0, c_out = final state of the shard's
+ *                                 scan from zero (both [B, N, D, D]);
+ *   csn_rotor_scan_bwd_aggregate: c_out = gradient leaving the shard at its first step when
+ *                                 no gradient enters from its right end. */
+size_t csn_rotor_scan_aggregate_workspace_bytes(int64_t B, int64_t T, int64_t N, int D);
+int csn_rotor_scan_aggregate(const float* gens, const float* dt, const float* gamma, const float* S,
+                             float* P_out, float* c_out, int64_t B, int64_t T, int64_t N, int D,
+                             int basis, int two_sided, void* workspace, size_t workspace_bytes,
+                             void* stream);
+int csn_rotor_scan_bwd_aggregate(const float* gens, const float* dt, const float* gamma,
+                                 const float* dX, float* c_out, int64_t B, int64_t T, int64_t N,
+                                 int D, int basis, int two_sided, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
 /* O(1)-state generation step, in place: h <- M h M^T + C (one-sided: M h + C) with M, C built
  * from this step's gens [B,N,K], dt [B], gamma [B,N] (NULL = undamped) and S [B,N,D,D];
  * h [B,N,D,D].  Allocates nothing and launches one kernel, so a decode loop can capture it

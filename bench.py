@@ -21,7 +21,7 @@ seeded, float32, shaped like the reference's configurations):
 * ``gen`` -- autoregressive O(1)-state generation, Cl(6,0), 256 streams x 8 channels:
   p50 latency of one rotor step (graph-replayed) and tokens/s.
 * ``sp`` -- sequence-parallel long scan, Cl(6,0): B 8, L 2^20, C 64, time axis split over
-  the torchrun ranks (strong scaling), forward.
+  the torchrun ranks (strong scaling), forward + backward.
 
 N > 1 runs under torchrun: every rank owns its own batch (independent sequences, no
 data-path collective: weak scaling); time is the max over ranks.  ``--impl reference``
@@ -411,23 +411,30 @@ class Cl8:
 WORKLOADS = {"cl6_lm": Cl6LM, "cl3": Cl3, "cl8": Cl8}
 
 
+SP_KERNELS = ("agg_fwd_reduce", "agg_bwd_reduce", "agg_compose", "fwd_reduce", "fwd_carry", "fwd_apply",
+              "bwd_reduce", "bwd_carry", "bwd_apply", "reduce_channels")
+
+
 def run_sequence_parallel(args, ws, rank, local, cores):
-    """Config 5: one L = 2^20 sequence per (b, c), B 8, C 64, Cl(6,0) 8 x 8, undamped
-    (gens ~ N(0, 0.02^2), dt ~ U(0.001, 0.01), x ~ N(0, 1)), time axis split over the ranks
-    (strong scaling).  Forward with the shard-aggregate all-gather and carried-in rescan.
-    Channels run in slabs of min(64, 8 * ranks) so every rank holds ~42 GB; the slabs reuse
-    one set of input buffers."""
+    """Sequence-parallel long scan, Cl(6,0) 8 x 8, undamped: B 8, L 2^20, C 64
+    (gens ~ N(0, 0.02^2), dt ~ U(0.001, 0.01), x ~ N(0, 1)), forward + backward.  The time
+    axis is split over the ranks (strong scaling): each rank aggregates its shard, the
+    (P, c) pairs are all-gathered over NCCL, and the shard resumes from its carry-in; the
+    backward mirrors it with the gradient carries.  Channels run in slabs of min(64, 8 * ranks)
+    so that every rank holds ~84 GB (inputs, trajectory, incoming and outgoing gradients);
+    the slabs reuse one set of buffers."""
     B, L, C, D, K = 8, 1 << 20, 64, 8, 28
     Tl = L // ws
     cs = min(C, 8 * ws)
     nslab = C // cs
-    config = {"workload": "cl6_sequence_parallel_fwd", "batch": B, "seq_len": L, "channels": C,
+    config = {"workload": "cl6_sequence_parallel_fwd_bwd", "batch": B, "seq_len": L, "channels": C,
               "matrix_dim": D, "algebra": "Cl(6,0)", "damped": False, "ranks": ws,
               "shard_len": Tl, "channel_slab": cs, "partition": "time axis, one shard per rank",
-              "exchange": "one all-gather of (P, c) per slab (NCCL)"}
+              "exchange": "all-gather of (P, c) forward and of c' backward per slab (NCCL)",
+              "l2": "inputs larger than L2"}
     elems = B * L * C
     n = D * D
-    op_bytes = 4.0 * (K + 2 * n + 1.0 / C)  # gens, x -> h
+    op_bytes = 4.0 * (5 * n + 3 * K + 3.0 / C)  # fwd: gens, S -> X; bwd: gens, X, dX -> dS, dgens
     if args.impl == "reference":
         if rank != 0:
             return 0
@@ -435,24 +442,30 @@ def run_sequence_parallel(args, ws, rank, local, cores):
         from oracle import oracle as orc
         E = algebra.triu_basis(D)
         rng = np.random.default_rng(0)
-        Ts = 16384
-        a = (rng.standard_normal((1, Ts, 4, K)) * 0.02, rng.uniform(0.001, 0.01, (1, Ts)), None,
-             rng.standard_normal((1, Ts, 4, D, D)))
-        el = _time_cpu(lambda: orc.rotor_scan_fwd(*a, E), max(1, args.steps), 0)
-        v = Ts * 4 * max(1, args.steps) / el / 1e9
-        print(json.dumps({"metric": METRIC.replace("fwd+bwd", "fwd"), "value": v, "unit": UNIT,
-                          "n_gpus": args.gpus, "steps": args.steps, "warmup": 0,
-                          "ms_per_step": el / max(1, args.steps) * 1e3, "higher_is_better": True,
+        Ts, Cs = 8192, 4
+        gs, dts, Ss = (rng.standard_normal((1, Ts, Cs, K)) * 0.02, rng.uniform(0.001, 0.01, (1, Ts)),
+                       rng.standard_normal((1, Ts, Cs, D, D)))
+        dXs = rng.standard_normal((1, Ts, Cs, D, D))
+
+        def ref_step():
+            X = orc.rotor_scan_fwd(gs, dts, None, Ss, E)
+            orc.rotor_scan_bwd(gs, dts, None, Ss, E, X, dXs)
+
+        steps = max(1, args.steps)
+        el = _time_cpu(ref_step, steps, 0)
+        v = Ts * Cs * steps / el / 1e9
+        print(json.dumps({"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": steps,
+                          "warmup": 0, "ms_per_step": el / steps * 1e3, "higher_is_better": True,
                           "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
                           "config": config, "impl": "reference",
                           "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
-                                           "sample": f"B1 L{Ts} C4 slice, forward, float64 C oracle"},
+                                           "sample": f"B1 L{Ts} C{Cs} slice, fwd+bwd, float64 C oracle"},
                           "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0,
                                   "d2h_bytes_per_step": 0}}), flush=True)
         return 0
     import torch
-    from csn_b200 import _lib, ops
-    from csn_b200.sequence_parallel import sp_forward
+    from csn_b200 import _lib
+    from csn_b200.sequence_parallel import CudaBackend, sp_backward, sp_forward
     if ws > 1:
         import torch.distributed as dist
         from datetime import timedelta
@@ -465,13 +478,19 @@ def run_sequence_parallel(args, ws, rank, local, cores):
     gens = torch.randn(B, Tl, cs, K, device=dev, generator=g) * 0.02
     dt = torch.rand(B, Tl, device=dev, generator=g) * 0.009 + 0.001
     S = torch.randn(B, Tl, cs, D, D, device=dev, generator=g)
+    dX = torch.randn(B, Tl, cs, D, D, device=dev, generator=g)
+    be = CudaBackend()
+    launches = [0]
 
     def step():
         for _ in range(nslab):
             if ws > 1:
-                sp_forward(gens, dt, None, S, None, None, "triu", True)
+                X, h_in, Ps = sp_forward(gens, dt, None, S, None, be, "triu", True)
+                sp_backward(gens, dt, None, S, X, dX, h_in, Ps, None, be, "triu", True)
             else:
-                ops.fused_rotor_scan(gens, dt, None, S)
+                X = be.rotor_fwd(gens, dt, None, S, None, "triu", True)
+                be.rotor_bwd(gens, dt, None, S, None, X, dX, "triu", True)
+            del X
 
     def barrier():
         if ws > 1:
@@ -483,12 +502,16 @@ def run_sequence_parallel(args, ws, rank, local, cores):
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     steps = max(1, args.steps)
+    _lib.timing_reset()
+    _lib.timing_enable(True)
     with ClockSampler(local) as clk:
         e0.record()
         for _ in range(steps):
             step()
         e1.record()
         torch.cuda.synchronize()
+    _lib.timing_enable(False)
+    kt = {k: _lib.timing_read(k) for k in SP_KERNELS}
     barrier()
     ms = e0.elapsed_time(e1)
     if ws > 1:
@@ -500,12 +523,14 @@ def run_sequence_parallel(args, ws, rank, local, cores):
     hbm, peak_kind = peaks()
     if rank == 0:
         ach = op_bytes * elems / ws / (ms_step * 1e-3) / 1e9
-        print(json.dumps({"metric": METRIC.replace("fwd+bwd", "fwd"), "value": value, "unit": UNIT,
+        print(json.dumps({"metric": METRIC, "value": value, "unit": UNIT,
                           "n_gpus": ws, "steps": steps, "warmup": max(3, args.warmup),
                           "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
                           "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
                           "op_roofline": {"achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
                                           "bytes_per_elem": op_bytes, "note": "per rank"},
+                          "kernel_ms_per_step": {k: v[0] / steps for k, v in kt.items() if v[1]},
+                          "gpu_launches": sum(v[1] for v in kt.values()),
                           "clocks": clk.summary()}), flush=True)
     if ws > 1:
         torch.distributed.destroy_process_group()

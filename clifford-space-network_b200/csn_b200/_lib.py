@@ -40,6 +40,10 @@ SIGNATURES = {
                                   _sz, _f], _int),
     "csn_rotor_scan_bwd_aggregate": ([_f, _f, _f, _f, _f, _i64, _i64, _i64, _int, _int, _int, _f,
                                       _sz, _f], _int),
+    "csn_rotor_scan_fwd_resume": ([_f, _f, _f, _f, _f, _f, _i64, _i64, _i64, _int, _int, _int, _f,
+                                   _sz, _f], _int),
+    "csn_rotor_scan_bwd_resume": ([_f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _i64, _i64,
+                                   _i64, _int, _int, _int, _f, _sz, _f], _int),
     "csn_rotor_step": ([_f, _f, _f, _f, _f, _i64, _i64, _int, _int, _int, _f], _int),
     "csn_cayley_fwd": ([_f, _f, _i64, _int, _f], _int),
     "csn_cayley_bwd": ([_f, _f, _f, _i64, _int, _f], _int),

@@ -8,12 +8,12 @@ forward
   1. (P_g, c_g) = shard aggregate: P = M_last ... M_first, c = shard scanned from zero
   2. all-gather (P, c)
   3. carry-in h_g = scan of (P_r, c_r), r < g            (plain scan kernel, X_0 = c_0)
-  4. rescan the shard from h_g                          (fused rotor scan with h0 = h_g)
+  4. resume the shard from h_g: carry + apply passes over the chunk aggregates of step 1
 backward (mirror image in reverse time)
   1. c'_g = gradient leaving the shard at its first step with zero gradient from the right
   2. all-gather c'
   3. H_g = reverse scan of (P_r^T, c'_r), r > g           (gradient entering from the right)
-  4. local adjoint with h0 = h_g and dX[:, -1] += H_g
+  4. resume the local adjoint with h0 = h_g and H_g entering after the last step
 
 The cross-shard compositions run on the same CUDA kernels as everything else.  Before
 each exchange the ranks all-gather a small header (shapes, flags) so that a rank with a
@@ -39,49 +39,70 @@ class ShardMismatchError(RuntimeError):
 
 
 class CudaBackend:
-    """Shard primitives on the CUDA library (float32, current stream)."""
+    """Shard primitives on the CUDA library (float32, current stream).
+
+    The aggregate calls return their workspace: it holds the chunk aggregates that the
+    matching resume call (``rotor_fwd`` / ``rotor_bwd`` with ``ws``) reuses, so each
+    shard's inputs are reduced once per direction."""
+
+    @staticmethod
+    def _agg_ws(B, T, N, D, device):
+        n = _lib.load().csn_rotor_scan_aggregate_workspace_bytes(B, T, N, D)
+        return torch.empty(n, dtype=torch.uint8, device=device)
 
     def fwd_aggregate(self, gens, dt, gamma, S, basis, two_sided):
         B, T, N, D, _ = S.shape
         P = torch.empty(B, N, D, D, device=S.device)
         c = torch.empty_like(P)
-        n = _lib.load().csn_rotor_scan_aggregate_workspace_bytes(B, T, N, D)
-        ws = _workspace(n, S.device)
+        ws = self._agg_ws(B, T, N, D, S.device)
         _lib.call("csn_rotor_scan_aggregate", _ptr(gens), _ptr(dt), _ptr(gamma), _ptr(S), _ptr(P), _ptr(c),
-                  B, T, N, D, BASIS[basis], int(two_sided), _ptr(ws), n, _stream(S.device))
-        return P, c
+                  B, T, N, D, BASIS[basis], int(two_sided), _ptr(ws), ws.numel(), _stream(S.device))
+        return P, c, ws
 
     def bwd_aggregate(self, gens, dt, gamma, dX, basis, two_sided):
         B, T, N, D, _ = dX.shape
         c = torch.empty(B, N, D, D, device=dX.device)
-        n = _lib.load().csn_rotor_scan_aggregate_workspace_bytes(B, T, N, D)
-        ws = _workspace(n, dX.device)
+        ws = self._agg_ws(B, T, N, D, dX.device)
         _lib.call("csn_rotor_scan_bwd_aggregate", _ptr(gens), _ptr(dt), _ptr(gamma), _ptr(dX), _ptr(c),
-                  B, T, N, D, BASIS[basis], int(two_sided), _ptr(ws), n, _stream(dX.device))
-        return c
+                  B, T, N, D, BASIS[basis], int(two_sided), _ptr(ws), ws.numel(), _stream(dX.device))
+        return c, ws
 
     def scan_mc(self, M, C, two_sided):
         from .ops import _scan_fwd
         return _scan_fwd(_f32(M), _f32(C), None, two_sided)
 
-    def rotor_fwd(self, gens, dt, gamma, S, h0, basis, two_sided):
+    def rotor_fwd(self, gens, dt, gamma, S, h0, basis, two_sided, ws=None):
         B, T, N, D, _ = S.shape
         X = torch.empty_like(S)
+        if ws is not None:
+            _lib.call("csn_rotor_scan_fwd_resume", _ptr(gens), _ptr(dt), _ptr(gamma), _ptr(S), _ptr(h0),
+                      _ptr(X), B, T, N, D, BASIS[basis], int(two_sided), _ptr(ws), ws.numel(),
+                      _stream(S.device))
+            return X
         n = _lib.load().csn_rotor_scan_workspace_bytes(B, T, N, D)
-        ws = _workspace(n, S.device)
+        w = _workspace(n, S.device)
         _lib.call("csn_rotor_scan_fwd", _ptr(gens), _ptr(dt), _ptr(gamma), _ptr(S), _ptr(h0), _ptr(X),
-                  B, T, N, D, BASIS[basis], int(two_sided), _ptr(ws), n, _stream(S.device))
+                  B, T, N, D, BASIS[basis], int(two_sided), _ptr(w), n, _stream(S.device))
         return X
 
-    def rotor_bwd(self, gens, dt, gamma, S, h0, X, dX, basis, two_sided):
+    def rotor_bwd(self, gens, dt, gamma, S, h0, X, dX, basis, two_sided, dh_right=None, ws=None):
         B, T, N, D, _ = S.shape
         dg, ddt, dS = torch.empty_like(gens), torch.empty_like(dt), torch.empty_like(S)
         dga = torch.empty_like(gamma) if gamma is not None else None
+        if ws is not None:
+            _lib.call("csn_rotor_scan_bwd_resume", _ptr(gens), _ptr(dt), _ptr(gamma), _ptr(S), _ptr(h0),
+                      _ptr(X), _ptr(dX), _ptr(dh_right), _ptr(dg), _ptr(ddt), _ptr(dga), _ptr(dS),
+                      _ptr(None), B, T, N, D, BASIS[basis], int(two_sided), _ptr(ws), ws.numel(),
+                      _stream(S.device))
+            return dg, ddt, dga, dS
+        if dh_right is not None:
+            dX = dX.clone()
+            dX[:, -1] += dh_right
         n = _lib.load().csn_rotor_scan_workspace_bytes(B, T, N, D)
-        ws = _workspace(n, S.device)
+        w = _workspace(n, S.device)
         _lib.call("csn_rotor_scan_bwd", _ptr(gens), _ptr(dt), _ptr(gamma), _ptr(S), _ptr(h0), _ptr(X),
                   _ptr(dX), _ptr(dg), _ptr(ddt), _ptr(dga), _ptr(dS), _ptr(None), B, T, N, D,
-                  BASIS[basis], int(two_sided), _ptr(ws), n, _stream(S.device))
+                  BASIS[basis], int(two_sided), _ptr(w), n, _stream(S.device))
         return dg, ddt, dga, dS
 
 
@@ -125,7 +146,7 @@ def sp_forward(gens, dt, gamma, S, group=None, backend=None, basis="triu", two_s
     flags = int(gamma is not None) * 1 + int(two_sided) * 2 + (BASIS[basis] << 2)
     _check_header(torch.tensor([B, T, N, D, gens.shape[-1], flags], dtype=torch.int64, device=dev),
                   group, "sequence-parallel forward")
-    P, c = backend.fwd_aggregate(gens, dt, gamma, S, basis, two_sided)
+    P, c, ws_fwd = backend.fwd_aggregate(gens, dt, gamma, S, basis, two_sided)
     Ps, cs = _gather(P, group), _gather(c, group)
     _check_finite(Ps + cs, "sequence-parallel forward")
     h_in = None
@@ -133,7 +154,7 @@ def sp_forward(gens, dt, gamma, S, group=None, backend=None, basis="triu", two_s
         Mseq = torch.stack(Ps[:g], dim=1)        # [B, g, N, D, D]
         Cseq = torch.stack(cs[:g], dim=1)
         h_in = backend.scan_mc(Mseq, Cseq, two_sided)[:, -1].contiguous()
-    X = backend.rotor_fwd(gens, dt, gamma, S, h_in, basis, two_sided)
+    X = backend.rotor_fwd(gens, dt, gamma, S, h_in, basis, two_sided, ws=ws_fwd)
     return X, h_in, Ps
 
 
@@ -145,18 +166,16 @@ def sp_backward(gens, dt, gamma, S, X, dX, h_in, Ps, group=None, backend=None, b
     B, T, N, D, _ = S.shape
     _check_header(torch.tensor([B, T, N, D, int(dX.shape == S.shape)], dtype=torch.int64,
                                device=S.device), group, "sequence-parallel backward")
-    cb = backend.bwd_aggregate(gens, dt, gamma, dX, basis, two_sided)
+    cb, ws_bwd = backend.bwd_aggregate(gens, dt, gamma, dX, basis, two_sided)
     cbs = _gather(cb, group)
     _check_finite(cbs, "sequence-parallel backward")
-    dXl = dX
+    H = None
     if g < ws - 1:
         later = list(range(ws - 1, g, -1))         # r = G-1 .. g+1
         Mseq = torch.stack([Ps[r].transpose(-1, -2) for r in later], dim=1)
         Cseq = torch.stack([cbs[r] for r in later], dim=1)
-        H = backend.scan_mc(Mseq, Cseq, two_sided)[:, -1]
-        dXl = dX.clone()
-        dXl[:, -1] += H
-    return backend.rotor_bwd(gens, dt, gamma, S, h_in, X, dXl.contiguous(), basis, two_sided)
+        H = backend.scan_mc(Mseq, Cseq, two_sided)[:, -1].contiguous()
+    return backend.rotor_bwd(gens, dt, gamma, S, h_in, X, dX, basis, two_sided, dh_right=H, ws=ws_bwd)
 
 
 class SequenceParallelRotorScan(torch.autograd.Function):

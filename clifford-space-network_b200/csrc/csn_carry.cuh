@@ -113,7 +113,7 @@ __global__ void __launch_bounds__(128) bwd_carry_kernel(ScanArgs a) {
     const int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     if (s >= S) return;
     Mat<4> H, P;
-    mat_zero(H);
+    if (a.hT) load_mat(H, a.hT + s * 16); else mat_zero(H);
     store_mat(a.carry + (s * a.nchunks + a.nchunks - 1) * 16, H);
     for (int64_t j = a.nchunks - 1; j >= 1; --j) {
       load_mat(P, a.aggP + (s * a.nchunks + j) * 16);
@@ -137,8 +137,8 @@ __global__ void __launch_bounds__(128) bwd_carry_kernel(ScanArgs a) {
 #pragma unroll
     for (int q = 0; q < PER; ++q) {
       const int idx = lane + 32 * q;
-      h[idx] = 0.0f;
-      a.carry[(s * a.nchunks + a.nchunks - 1) * DD + idx] = 0.0f;
+      h[idx] = a.hT ? a.hT[s * DD + idx] : 0.0f;
+      a.carry[(s * a.nchunks + a.nchunks - 1) * DD + idx] = h[idx];
     }
     __syncwarp();
     float pn[PER], cn[PER];

@@ -181,6 +181,7 @@ __global__ void __launch_bounds__(128) bwd_apply_kernel(ScanArgs a) {
 
   Mat<D> H, M;
   if (a.nchunks > 1) load_mat(H, a.carry + (s * a.nchunks + j) * DD);
+  else if (a.hT) load_mat(H, a.hT + s * DD);
   else mat_zero(H);
   RotorStep<D, K> r;
   for (int64_t t = t1 - 1; t >= t0; --t) {
@@ -370,13 +371,17 @@ int run_fwd(ScanArgs a, cudaStream_t st) {
   const int64_t S = a.B * a.N;
   const int64_t total = S * a.nchunks;
   if (total == 0) return CSN_OK;
-  if (a.agg_mode) {
-    fwd_reduce_kernel<D, SRC, BASIS, DAMPED, TWO><<<blocks_for(total, 128), 128, 0, st>>>(a);
+  if (a.agg_mode == 1) {
+    {
+      KernelTimer kt("agg_fwd_reduce", st);
+      fwd_reduce_kernel<D, SRC, BASIS, DAMPED, TWO><<<blocks_for(total, 128), 128, 0, st>>>(a);
+    }
+    KernelTimer kt("agg_compose", st);
     compose_kernel<D, TWO, false><<<blocks_for(S, 4), 128, 0, st>>>(a);
     return check_launch("shard aggregate (forward)");
   }
   if (a.nchunks > 1) {
-    {
+    if (a.agg_mode != 2) {
       KernelTimer kt("fwd_reduce", st);
       fwd_reduce_kernel<D, SRC, BASIS, DAMPED, TWO><<<blocks_for(total, 128), 128, 0, st>>>(a);
     }
@@ -395,15 +400,19 @@ template <int D, int SRC, int BASIS, bool DAMPED, bool TWO>
 int run_bwd(ScanArgs a, cudaStream_t st) {
   const int64_t S = a.B * a.N;
   const int64_t total = S * a.nchunks;
-  if (a.agg_mode) {
+  if (a.agg_mode == 1) {
     if (total == 0) return CSN_OK;
-    bwd_reduce_kernel<D, SRC, BASIS, DAMPED, TWO><<<blocks_for(total, 128), 128, 0, st>>>(a);
+    {
+      KernelTimer kt("agg_bwd_reduce", st);
+      bwd_reduce_kernel<D, SRC, BASIS, DAMPED, TWO><<<blocks_for(total, 128), 128, 0, st>>>(a);
+    }
+    KernelTimer kt("agg_compose", st);
     compose_kernel<D, TWO, true><<<blocks_for(S, 4), 128, 0, st>>>(a);
     return check_launch("shard aggregate (backward)");
   }
   if (total > 0) {
     if (a.nchunks > 1) {
-      {
+      if (a.agg_mode != 2) {
         KernelTimer kt("bwd_reduce", st);
         bwd_reduce_kernel<D, SRC, BASIS, DAMPED, TWO><<<blocks_for(total, 128), 128, 0, st>>>(a);
       }
@@ -684,11 +693,17 @@ extern "C" int csn_rotor_step(const float* gens, const float* dt, const float* g
 //             enters from the right (the shard's dh0 with zero right carry)
 // A shard's carry-in is then the scan of the earlier shards' (P, c) pairs, and its
 // gradient carry-in the reverse scan of the later shards' (P^T, c') pairs.
-static size_t agg_bytes(int64_t B, int64_t T, int64_t N, int D) {
-  Plan p = make_plan(B, T, N, D, false);
-  const int64_t nch = p.nchunks > 0 ? p.nchunks : 1;
-  return (size_t)3 * B * N * nch * D * D * sizeof(float) + 256;
+// The aggregate calls keep every chunk's aggregate in the workspace, so that the
+// *_resume calls on the same inputs run only the carry and apply passes afterwards.
+// The workspace also holds the per-(b, t, n) ddt partials of the backward resume.
+static Plan agg_plan(int64_t B, int64_t T, int64_t N, int D) {
+  Plan p = make_plan(B, T, N, D, true);
+  if (p.nchunks < 1) p.nchunks = 1;
+  p.agg_floats = (size_t)3 * B * N * p.nchunks * D * D;
+  return p;
 }
+
+static size_t agg_bytes(int64_t B, int64_t T, int64_t N, int D) { return plan_bytes(agg_plan(B, T, N, D)); }
 
 extern "C" size_t csn_rotor_scan_aggregate_workspace_bytes(int64_t B, int64_t T, int64_t N, int D) {
   if (B < 0 || T < 0 || N < 0 || D < 1) return 0;
@@ -705,11 +720,9 @@ static int run_aggregate(bool bwd, const float* gens, const float* dt, const flo
   if (!c_out || !aligned16(c_out) || (P_out && !aligned16(P_out)))
     return set_error(CSN_ERR_INVALID, "shard aggregate: outputs missing or misaligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  Plan p = make_plan(B, T, N, D, false);
-  if (p.nchunks < 1) p.nchunks = 1;
-  p.agg_floats = (size_t)3 * B * N * p.nchunks * D * D;
+  Plan p = agg_plan(B, T, N, D);
   Workspace ws;
-  if (int rc = get_ws(ws, workspace, workspace_bytes, agg_bytes(B, T, N, D), st)) return rc;
+  if (int rc = get_ws(ws, workspace, workspace_bytes, plan_bytes(p), st)) return rc;
   ScanArgs a{};
   a.gens = gens; a.dt = dt; a.gamma = gamma; a.S = S; a.dX = dX;
   a.B = B; a.T = T; a.N = N;
@@ -734,4 +747,70 @@ extern "C" int csn_rotor_scan_bwd_aggregate(const float* gens, const float* dt, 
                                             void* workspace, size_t workspace_bytes, void* stream) {
   return run_aggregate(true, gens, dt, gamma, nullptr, dX, nullptr, c_out, B, T, N, D, basis,
                        two_sided, workspace, workspace_bytes, stream);
+}
+
+// Resume: the shard's carry and apply passes from the chunk aggregates that the
+// matching aggregate call left in `workspace` (same inputs, same shape, same stream
+// order).  The workspace is required: it is where those aggregates live.
+static int resume_ws(void* workspace, size_t workspace_bytes, int64_t B, int64_t T, int64_t N, int D) {
+  if (!workspace || workspace_bytes < agg_bytes(B, T, N, D))
+    return set_error(CSN_ERR_INVALID,
+                     "resume: needs the workspace of the matching aggregate call "
+                     "(csn_rotor_scan_aggregate_workspace_bytes)");
+  return CSN_OK;
+}
+
+extern "C" int csn_rotor_scan_fwd_resume(const float* gens, const float* dt, const float* gamma,
+                                         const float* S, const float* h0, float* X, int64_t B,
+                                         int64_t T, int64_t N, int D, int basis, int two_sided,
+                                         void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = rotor_common_checks(gens, dt, S, B, T, N, D, basis)) return rc;
+  if (B * T * N == 0) return CSN_OK;
+  if (!X || !aligned16(X) || (h0 && !aligned16(h0)))
+    return set_error(CSN_ERR_INVALID, "csn_rotor_scan_fwd_resume: X missing or misaligned");
+  if (int rc = resume_ws(workspace, workspace_bytes, B, T, N, D)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Plan p = agg_plan(B, T, N, D);
+  ScanArgs a{};
+  a.gens = gens; a.dt = dt; a.gamma = gamma; a.S = S; a.h0 = h0; a.out = X;
+  a.B = B; a.T = T; a.N = N;
+  a.agg_mode = 2;
+  bind_ws(a, p, static_cast<float*>(workspace), D);
+  if (D == 16) return scan16_dispatch(a, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, false, st);
+  return dispatch(a, D, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, false, st);
+}
+
+extern "C" int csn_rotor_scan_bwd_resume(const float* gens, const float* dt, const float* gamma,
+                                         const float* S, const float* h0, const float* X,
+                                         const float* dX, const float* dh_right, float* dgens,
+                                         float* ddt, float* dgamma, float* dS, float* dh0,
+                                         int64_t B, int64_t T, int64_t N, int D, int basis,
+                                         int two_sided, void* workspace, size_t workspace_bytes,
+                                         void* stream) {
+  if (int rc = rotor_common_checks(gens, dt, S, B, T, N, D, basis)) return rc;
+  if (B * T * N == 0) {
+    if (B * T > 0 && ddt) {
+      cudaError_t e = cudaMemsetAsync(ddt, 0, sizeof(float) * B * T, static_cast<cudaStream_t>(stream));
+      if (e != cudaSuccess) return set_cuda_error(e, "cudaMemsetAsync(ddt)");
+    }
+    return CSN_OK;
+  }
+  if (!X || !dX || !dgens || !ddt || !dS || (gamma && !dgamma))
+    return set_error(CSN_ERR_INVALID, "csn_rotor_scan_bwd_resume: missing X, dX or a gradient output");
+  if (!aligned16(X) || !aligned16(dX) || !aligned16(dS) || (h0 && !aligned16(h0)) ||
+      (dh0 && !aligned16(dh0)) || (dh_right && !aligned16(dh_right)))
+    return set_error(CSN_ERR_INVALID, "csn_rotor_scan_bwd_resume: pointers must be 16-byte aligned");
+  if (dh0 && !h0) return set_error(CSN_ERR_INVALID, "csn_rotor_scan_bwd_resume: dh0 needs h0");
+  if (int rc = resume_ws(workspace, workspace_bytes, B, T, N, D)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Plan p = agg_plan(B, T, N, D);
+  ScanArgs a{};
+  a.gens = gens; a.dt = dt; a.gamma = gamma; a.S = S; a.h0 = h0; a.X = X; a.dX = dX;
+  a.hT = dh_right;
+  a.dgens = dgens; a.ddt = ddt; a.dgamma = dgamma; a.dC = dS; a.dh0 = dh0;
+  a.B = B; a.T = T; a.N = N;
+  a.agg_mode = 2;
+  bind_ws(a, p, static_cast<float*>(workspace), D);
+  if (D == 16) return scan16_dispatch(a, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, true, st);
+  return dispatch(a, D, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, true, st);
 }

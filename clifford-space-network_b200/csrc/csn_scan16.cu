@@ -369,7 +369,7 @@ __global__ void __launch_bounds__(128) bwd_apply16(ScanArgs a) {
 #pragma unroll
   for (int q = 0; q < 8; ++q) {
     const int idx = ent(lane, q);
-    w.A[idx] = (a.nchunks > 1) ? a.carry[(s * a.nchunks + j) * DD + idx] : 0.0f;
+    w.A[idx] = (a.nchunks > 1) ? a.carry[(s * a.nchunks + j) * DD + idx] : a.hT ? a.hT[s * DD + idx] : 0.0f;
   }
   __syncwarp();
   float* Xp = w.U;
@@ -515,13 +515,21 @@ template <int SRC, int BASIS, bool DAMPED, bool TWO>
 int run16(const ScanArgs& a, bool bwd, cudaStream_t st) {
   const int64_t S = a.B * a.N;
   const int64_t total = S * a.nchunks;
-  if (a.agg_mode) {
+  if (a.agg_mode == 1) {
     if (total == 0) return CSN_OK;
     if (!bwd) {
-      fwd_reduce16<SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(a);
+      {
+        KernelTimer kt("agg_fwd_reduce", st);
+        fwd_reduce16<SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(a);
+      }
+      KernelTimer kt("agg_compose", st);
       compose_kernel<16, TWO, false><<<nblk(S), 128, 0, st>>>(a);
     } else {
-      bwd_reduce16<SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(a);
+      {
+        KernelTimer kt("agg_bwd_reduce", st);
+        bwd_reduce16<SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(a);
+      }
+      KernelTimer kt("agg_compose", st);
       compose_kernel<16, TWO, true><<<nblk(S), 128, 0, st>>>(a);
     }
     return check_launch("shard aggregate (D=16)");
@@ -529,7 +537,7 @@ int run16(const ScanArgs& a, bool bwd, cudaStream_t st) {
   if (!bwd) {
     if (total == 0) return CSN_OK;
     if (a.nchunks > 1) {
-      {
+      if (a.agg_mode != 2) {
         KernelTimer kt("fwd_reduce", st);
         fwd_reduce16<SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(a);
       }
@@ -542,7 +550,7 @@ int run16(const ScanArgs& a, bool bwd, cudaStream_t st) {
   }
   if (total > 0) {
     if (a.nchunks > 1) {
-      {
+      if (a.agg_mode != 2) {
         KernelTimer kt("bwd_reduce", st);
         bwd_reduce16<SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(a);
       }

@@ -447,6 +447,7 @@ __global__ void __launch_bounds__(THREADS, 2) bwd8_apply_kernel(ScanArgs a) {
 
   Mat<8> H;
   if (active && a.nchunks > 1) load_mat(H, a.carry + (s * a.nchunks + j) * DD);
+  else if (active && a.hT) load_mat(H, a.hT + s * DD);
   else mat_zero(H);
 
   for (int st = 0; st < nsteps; ++st) {
@@ -695,15 +696,23 @@ int run8(const ScanArgs& a, bool bwd, cudaStream_t st) {
   const int fwd_bytes = THREADS * FwdSlot::STRIDE * 4;
   const int red_bytes = THREADS * BwdRedSlot::STRIDE * 4;
   const int app_bytes = THREADS * BwdAppSlot::STRIDE * 4;
-  if (a.agg_mode) {
+  if (a.agg_mode == 1) {
     if (total == 0) return CSN_OK;
     if (!bwd) {
-      set_smem(fwd8_kernel<true, DAMPED, TWO>, fwd_bytes);
-      fwd8_kernel<true, DAMPED, TWO><<<nblk(total), THREADS, fwd_bytes, st>>>(a);
+      {
+        KernelTimer kt("agg_fwd_reduce", st);
+        set_smem(fwd8_kernel<true, DAMPED, TWO>, fwd_bytes);
+        fwd8_kernel<true, DAMPED, TWO><<<nblk(total), THREADS, fwd_bytes, st>>>(a);
+      }
+      KernelTimer kt("agg_compose", st);
       compose_kernel<8, TWO, false><<<(unsigned)((S + 3) / 4), 128, 0, st>>>(a);
     } else {
-      set_smem(bwd8_reduce_kernel<DAMPED, TWO>, red_bytes);
-      bwd8_reduce_kernel<DAMPED, TWO><<<nblk(total), THREADS, red_bytes, st>>>(a);
+      {
+        KernelTimer kt("agg_bwd_reduce", st);
+        set_smem(bwd8_reduce_kernel<DAMPED, TWO>, red_bytes);
+        bwd8_reduce_kernel<DAMPED, TWO><<<nblk(total), THREADS, red_bytes, st>>>(a);
+      }
+      KernelTimer kt("agg_compose", st);
       compose_kernel<8, TWO, true><<<(unsigned)((S + 3) / 4), 128, 0, st>>>(a);
     }
     return check_launch("shard aggregate (D=8)");
@@ -711,7 +720,7 @@ int run8(const ScanArgs& a, bool bwd, cudaStream_t st) {
   if (!bwd) {
     if (total == 0) return CSN_OK;
     if (a.nchunks > 1) {
-      {
+      if (a.agg_mode != 2) {
         KernelTimer kt("fwd_reduce", st);
         set_smem(fwd8_kernel<true, DAMPED, TWO>, fwd_bytes);
         fwd8_kernel<true, DAMPED, TWO><<<nblk(total), THREADS, fwd_bytes, st>>>(a);
@@ -726,7 +735,7 @@ int run8(const ScanArgs& a, bool bwd, cudaStream_t st) {
   }
   if (total > 0) {
     if (a.nchunks > 1) {
-      {
+      if (a.agg_mode != 2) {
         KernelTimer kt("bwd_reduce", st);
         set_smem(bwd8_reduce_kernel<DAMPED, TWO>, red_bytes);
         bwd8_reduce_kernel<DAMPED, TWO><<<nblk(total), THREADS, red_bytes, st>>>(a);

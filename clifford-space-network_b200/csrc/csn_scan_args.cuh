@@ -17,6 +17,7 @@ struct ScanArgs {
   const float* S;
   // common
   const float* h0;  // [B, N, D, D] or nullptr
+  const float* hT;  // backward: gradient entering after the last step, [B, N, D, D] or nullptr
   const float* X;   // forward output (backward only)
   const float* dX;  // incoming gradient (backward only)
   float* out;       // forward X
@@ -34,9 +35,12 @@ struct ScanArgs {
   float* carry;  // [S, nchunks, D, D]
   int64_t B, T, N;
   int64_t nchunks, chunk;
-  // aggregate-only mode (sequence-parallel shards): reduce + compose, no apply pass.
-  //   forward:  P_out = M_{T-1} ... M_0, c_out = final state of a zero-carry scan
-  //   backward: c_out = gradient leaving the shard at t = 0 with zero carry from t = T
+  // Sequence-parallel shard modes.
+  //   agg_mode 1: reduce + compose, no apply pass; the chunk aggregates stay in aggP/aggC.
+  //     forward:  P_out = M_{T-1} ... M_0, c_out = final state of a zero-carry scan
+  //     backward: c_out = gradient leaving the shard at t = 0 with zero carry from t = T
+  //   agg_mode 2: resume -- the chunk aggregates left by mode 1 on the same inputs are
+  //     reused, so only the carry and apply passes run (carry-in h0; backward: hT).
   int agg_mode;
   float* P_out;  // [B, N, D, D]
   float* c_out;  // [B, N, D, D]

@@ -134,6 +134,25 @@ int csn_rotor_scan_bwd_aggregate(const float* gens, const float* dt, const float
                                  int D, int basis, int two_sided, void* workspace,
                                  size_t workspace_bytes, void* stream);
 
+/* Resume the shard after its aggregate: the aggregate calls leave every chunk's aggregate in
+ * `workspace`, and these calls (same inputs, same workspace, later on the same stream) run only
+ * the carry and apply passes from them, so a shard's inputs are reduced once per direction.
+ *   csn_rotor_scan_fwd_resume: csn_rotor_scan_fwd with carry-in h0 (NULL = zero);
+ *   csn_rotor_scan_bwd_resume: csn_rotor_scan_bwd with dh_right [B,N,D,D] (NULL = zero), the
+ *                              gradient entering after the shard's last step.
+ * The workspace is required (>= csn_rotor_scan_aggregate_workspace_bytes).  The reference has
+ * no sequence-parallel scan; these follow the scan of python/clifford_cl6.py:150-171. */
+int csn_rotor_scan_fwd_resume(const float* gens, const float* dt, const float* gamma,
+                              const float* S, const float* h0, float* X, int64_t B, int64_t T,
+                              int64_t N, int D, int basis, int two_sided, void* workspace,
+                              size_t workspace_bytes, void* stream);
+int csn_rotor_scan_bwd_resume(const float* gens, const float* dt, const float* gamma,
+                              const float* S, const float* h0, const float* X, const float* dX,
+                              const float* dh_right, float* dgens, float* ddt, float* dgamma,
+                              float* dS, float* dh0, int64_t B, int64_t T, int64_t N, int D,
+                              int basis, int two_sided, void* workspace, size_t workspace_bytes,
+                              void* stream);
+
 /* O(1)-state generation step, in place: h <- M h M^T + C (one-sided: M h + C) with M, C built
  * from this step's gens [B,N,K], dt [B], gamma [B,N] (NULL = undamped) and S [B,N,D,D];
  * h [B,N,D,D].  Allocates nothing and launches one kernel, so a decode loop can capture it

@@ -1,7 +1,8 @@
 """Sequence-parallel scan on the GPU.
 
 * Shard emulation on one GPU: the CUDA shard aggregates, the cross-shard composition
-  (plain scan kernel over the shard summaries) and the carried-in rescans, exactly as
+  (plain scan kernel over the shard summaries) and the carried-in passes -- resumed from
+  the aggregate's workspace, or rescanned in one piece -- exactly as
   csn_b200.sequence_parallel runs them per rank, equal the one-piece fused scan.
 * Multi-GPU (runs when >= 2 GPUs are visible): real NCCL ranks, one shard each, through
   sequence_parallel_rotor_scan (autograd) -- forward and gradients equal the one-piece scan.
@@ -37,16 +38,18 @@ def problem(B, T, N, D, damped, seed=0, device=DEV, gscale=1.0):
     return mv(gens), mv(dt), mv(gamma), mv(S), mv(dX)
 
 
-@pytest.mark.parametrize("D,damped,G", [(8, False, 4), (8, True, 3), (4, True, 5), (16, False, 2)])
-def test_shard_emulation_equals_full_scan(D, damped, G):
+@pytest.mark.parametrize("D,damped,G,Tl", [(8, False, 4, 96), (8, True, 3, 96), (4, True, 5, 96), (16, False, 2, 40),
+                                            (8, True, 3, 8), (16, True, 2, 8), (4, False, 3, 8), (8, False, 2, 5)])
+def test_shard_emulation_equals_full_scan(D, damped, G, Tl):
+    """Tl = 8 and 5 give single-chunk shards (the resume starts the apply pass from h0 / dh_right
+    directly); the others give many chunks per shard."""
     from csn_b200 import _build, ops
     from csn_b200.sequence_parallel import CudaBackend
     _build.build()
     B, N = 2, 3
-    T = 96 * G if D < 16 else 40 * G
+    T = Tl * G
     gens, dt, gamma, S, dX = problem(B, T, N, D, damped, gscale=0.3)
     be = CudaBackend()
-    Tl = T // G
     sh = lambda t, g: None if t is None else t[:, g * Tl:(g + 1) * Tl].contiguous()
     aggs = [be.fwd_aggregate(sh(gens, g), sh(dt, g), sh(gamma, g), sh(S, g), "triu", True) for g in range(G)]
     Xs, h_ins = [], []
@@ -56,7 +59,9 @@ def test_shard_emulation_equals_full_scan(D, damped, G):
             h_in = be.scan_mc(torch.stack([a[0] for a in aggs[:g]], 1), torch.stack([a[1] for a in aggs[:g]], 1),
                               True)[:, -1].contiguous()
         h_ins.append(h_in)
-        Xs.append(be.rotor_fwd(sh(gens, g), sh(dt, g), sh(gamma, g), sh(S, g), h_in, "triu", True))
+        # even shards resume from the aggregate's workspace, odd shards rescan in one piece
+        Xs.append(be.rotor_fwd(sh(gens, g), sh(dt, g), sh(gamma, g), sh(S, g), h_in, "triu", True,
+                               ws=aggs[g][2] if g % 2 == 0 else None))
     X = torch.cat(Xs, 1)
     Xref = ops.fused_rotor_scan(gens, dt, gamma, S)
     assert rel(X, Xref) < 1e-4
@@ -64,14 +69,14 @@ def test_shard_emulation_equals_full_scan(D, damped, G):
     cbs = [be.bwd_aggregate(sh(gens, g), sh(dt, g), sh(gamma, g), sh(dX, g), "triu", True) for g in range(G)]
     grads = []
     for g in range(G):
-        dXl = sh(dX, g).clone()
+        H = None
         if g < G - 1:
             later = list(range(G - 1, g, -1))
             H = be.scan_mc(torch.stack([aggs[r][0].transpose(-1, -2) for r in later], 1),
-                           torch.stack([cbs[r] for r in later], 1), True)[:, -1]
-            dXl[:, -1] += H
+                           torch.stack([cbs[r][0] for r in later], 1), True)[:, -1].contiguous()
         grads.append(be.rotor_bwd(sh(gens, g), sh(dt, g), sh(gamma, g), sh(S, g), h_ins[g], Xs[g],
-                                  dXl.contiguous(), "triu", True))
+                                  sh(dX, g), "triu", True, dh_right=H,
+                                  ws=cbs[g][1] if g % 2 == 0 else None))
     tg, tdt, tS = gens.clone().requires_grad_(True), dt.clone().requires_grad_(True), S.clone().requires_grad_(True)
     tga = gamma.clone().requires_grad_(True) if damped else None
     ops.fused_rotor_scan(tg, tdt, tga, tS).backward(dX)

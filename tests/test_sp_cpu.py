@@ -38,7 +38,7 @@ class OracleBackend:
         c = o.rotor_scan_fwd(n(gens), n(dt), n(gamma), n(S), self.E, two_sided=two_sided)[:, -1]
         if self.poison:
             c = c * np.nan
-        return torch.from_numpy(P), torch.from_numpy(np.ascontiguousarray(c))
+        return torch.from_numpy(P), torch.from_numpy(np.ascontiguousarray(c)), None
 
     def bwd_aggregate(self, gens, dt, gamma, dX, basis, two_sided):
         o, n = self.orc, self._n
@@ -48,18 +48,21 @@ class OracleBackend:
                              two_sided=two_sided)
         *_, dh0 = o.rotor_scan_bwd(n(gens), n(dt), n(gamma), S, self.E, X, n(dX),
                                    h0=np.zeros((B, N, D, D)), two_sided=two_sided)
-        return torch.from_numpy(dh0)
+        return torch.from_numpy(dh0), None
 
     def scan_mc(self, M, C, two_sided):
         return torch.from_numpy(self.orc.scan_fwd(self._n(M), self._n(C), two_sided=two_sided))
 
-    def rotor_fwd(self, gens, dt, gamma, S, h0, basis, two_sided):
+    def rotor_fwd(self, gens, dt, gamma, S, h0, basis, two_sided, ws=None):
         n = self._n
         return torch.from_numpy(self.orc.rotor_scan_fwd(n(gens), n(dt), n(gamma), n(S), self.E, h0=n(h0),
                                                         two_sided=two_sided))
 
-    def rotor_bwd(self, gens, dt, gamma, S, h0, X, dX, basis, two_sided):
+    def rotor_bwd(self, gens, dt, gamma, S, h0, X, dX, basis, two_sided, dh_right=None, ws=None):
         n = self._n
+        if dh_right is not None:
+            dX = dX.clone()
+            dX[:, -1] += dh_right
         h0n = n(h0) if h0 is not None else np.zeros((S.shape[0], S.shape[2], S.shape[3], S.shape[4]))
         dg, ddt, dga, dS, _ = self.orc.rotor_scan_bwd(n(gens), n(dt), n(gamma), n(S), self.E, n(X), n(dX),
                                                       h0=h0n, two_sided=two_sided)

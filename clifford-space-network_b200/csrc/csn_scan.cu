@@ -386,8 +386,8 @@ int run_fwd(ScanArgs a, cudaStream_t st) {
       fwd_reduce_kernel<D, SRC, BASIS, DAMPED, TWO><<<blocks_for(total, 128), 128, 0, st>>>(a);
     }
     KernelTimer kt("fwd_carry", st);
-    if (D == 4) fwd_carry_kernel<D, TWO><<<blocks_for(S, 128), 128, 0, st>>>(a);
-    else fwd_carry_kernel<D, TWO><<<blocks_for(S, 4), 128, 0, st>>>(a);
+    if constexpr (D == 4) fwd_carry_kernel<D, TWO><<<blocks_for(S, 128), 128, 0, st>>>(a);
+    else launch_grouped_carry<D, TWO, false>(a, st);
   }
   {
     KernelTimer kt("fwd_apply", st);
@@ -417,8 +417,8 @@ int run_bwd(ScanArgs a, cudaStream_t st) {
         bwd_reduce_kernel<D, SRC, BASIS, DAMPED, TWO><<<blocks_for(total, 128), 128, 0, st>>>(a);
       }
       KernelTimer kt("bwd_carry", st);
-      if (D == 4) bwd_carry_kernel<D, TWO><<<blocks_for(S, 128), 128, 0, st>>>(a);
-      else bwd_carry_kernel<D, TWO><<<blocks_for(S, 4), 128, 0, st>>>(a);
+      if constexpr (D == 4) bwd_carry_kernel<D, TWO><<<blocks_for(S, 128), 128, 0, st>>>(a);
+      else launch_grouped_carry<D, TWO, true>(a, st);
     }
     KernelTimer kt("bwd_apply", st);
     bwd_apply_kernel<D, SRC, BASIS, DAMPED, TWO><<<blocks_for(total, 128), 128, 0, st>>>(a);

@@ -542,7 +542,7 @@ int run16(const ScanArgs& a, bool bwd, cudaStream_t st) {
         fwd_reduce16<SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(a);
       }
       KernelTimer kt("fwd_carry", st);
-      fwd_carry_kernel<16, TWO><<<nblk(S), 128, 0, st>>>(a);
+      launch_grouped_carry<16, TWO, false>(a, st);
     }
     KernelTimer kt("fwd_apply", st);
     fwd_apply16<SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(a);
@@ -555,7 +555,7 @@ int run16(const ScanArgs& a, bool bwd, cudaStream_t st) {
         bwd_reduce16<SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(a);
       }
       KernelTimer kt("bwd_carry", st);
-      bwd_carry_kernel<16, TWO><<<nblk(S), 128, 0, st>>>(a);
+      launch_grouped_carry<16, TWO, true>(a, st);
     }
     KernelTimer kt("bwd_apply", st);
     bwd_apply16<SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(a);

@@ -726,7 +726,7 @@ int run8(const ScanArgs& a, bool bwd, cudaStream_t st) {
         fwd8_kernel<true, DAMPED, TWO><<<nblk(total), THREADS, fwd_bytes, st>>>(a);
       }
       KernelTimer kt("fwd_carry", st);
-      fwd_carry_kernel<8, TWO><<<(unsigned)((S + 3) / 4), 128, 0, st>>>(a);
+      launch_grouped_carry<8, TWO, false>(a, st);
     }
     KernelTimer kt("fwd_apply", st);
     set_smem(fwd8_kernel<false, DAMPED, TWO>, fwd_bytes);
@@ -741,7 +741,7 @@ int run8(const ScanArgs& a, bool bwd, cudaStream_t st) {
         bwd8_reduce_kernel<DAMPED, TWO><<<nblk(total), THREADS, red_bytes, st>>>(a);
       }
       KernelTimer kt("bwd_carry", st);
-      bwd_carry_kernel<8, TWO><<<(unsigned)((S + 3) / 4), 128, 0, st>>>(a);
+      launch_grouped_carry<8, TWO, true>(a, st);
     }
     KernelTimer kt("bwd_apply", st);
     set_smem(bwd8_apply_kernel<DAMPED, TWO>, app_bytes);

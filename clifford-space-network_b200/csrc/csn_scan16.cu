@@ -1,10 +1,25 @@
-// csn_scan16.cu -- D = 16 (Cl(8,0) ~ M_16(R)) rotor scans.
+// csn_scan16.cu -- D = 16 (Cl(8,0) ~ M_16(R)) scans on warp-level tensor-core MMA.
 //
-// Same three-phase chunked algorithm as csn_scan.cu (reduce -> carry -> apply, and
-// the reverse-time mirror for the adjoint), but a 16 x 16 matrix is too large for
-// one thread's registers, so one warp owns one (sequence, chunk).  The warp keeps
-// its matrices in shared memory; lane l owns the 8 entries (i, j) with
-// j = l % 16 and i = l / 16 + 2q (q = 0..7).
+// Same chunked reduce -> carry -> apply algorithm as the other families, one warp per
+// (sequence, chunk).  A 16 x 16 matrix lives in registers as an mma.m16n8k8 accumulator
+// fragment ("F16", 8 floats per lane): lane (g = lane / 4, t = lane % 4) holds rows g and
+// g + 8 at columns 8 nt + 2 t and 8 nt + 2 t + 1 of each 8-column half nt.  Those same
+// registers are the row-major A operand of mma.m16n8k8.tf32 when the k index inside each
+// k-step is permuted as (slot t, slot t + 4) <-> (column 2 t, column 2 t + 1), and the
+// B operand of the TRANSPOSED matrix under the same permutation.  So a product of the
+// form Z = A B^T takes two fragments and yields a fragment with no data movement, and
+// every product of the scan is written that way:
+//   forward      X' = M (M X^T)^T + C            (two products)
+//   chunk product P^T <- P^T M^T
+//   adjoint      H' = M^T (M^T G^T)^T,  dM = (G M) Xp^T + G^T (Xp^T M^T)^T, ...
+// Transposes are products with the identity.  Products run as 3xTF32: each fp32 operand
+// is split into a TF32 head and a TF32 tail and hi*hi + hi*lo + lo*hi is accumulated in
+// fp32, which keeps fp32-level accuracy.  The Cayley inverse (I - Omega)^{-1} is a short
+// matrix series when |h Omega|_F <= 0.1 (four more products, accurate to 1e-8) and
+// otherwise a Gauss-Jordan elimination on the fragment, whose pivot rows and columns
+// reach the lanes that need them by shuffles; either way the step stays in registers.
+#include <stdint.h>
+
 #include "csn_common.cuh"
 #include "csn_internal.h"
 #include "csn_scan_args.cuh"
@@ -15,470 +30,654 @@ namespace s16 {
 
 constexpr int D = 16;
 constexpr int DD = 256;
-constexpr int WARPS = 4;  // warps per block
+constexpr int WARPS = 4;   // warps per block
+constexpr int ZST = 20;    // row stride of the dOmega scratch (20 = 8t + g spreads banks)
+constexpr unsigned FULL = 0xffffffffu;
 
-// out(i,j) for the lane's 8 entries of A * B (A, B row-major 16 x 16 in smem).
-__device__ __forceinline__ void prod_nn(const float* __restrict__ A, const float* __restrict__ B,
-                                        float (&o)[8], int lane) {
-  const int j = lane & 15, i0 = lane >> 4;
-  float bc[16];
+// ------------------------------------------------------------------- fragments
+struct F16 {
+  float v[2][4];  // v[nt][e]: row g + 8 (e >> 1), column 8 nt + 2 t + (e & 1)
+};
+struct F16S {      // 3xTF32 operand: head and tail of every element
+  uint32_t hi[2][4], lo[2][4];
+};
+
+__device__ __forceinline__ int frow(int lane, int e) { return (lane >> 2) + 8 * (e >> 1); }
+__device__ __forceinline__ int fcol(int lane, int nt, int e) { return 8 * nt + 2 * (lane & 3) + (e & 1); }
+
+__device__ __forceinline__ uint32_t to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+__device__ __forceinline__ void split(F16S& o, const F16& x) {
 #pragma unroll
-  for (int k = 0; k < 16; ++k) bc[k] = B[k * 16 + j];
+  for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    const float4* ar = reinterpret_cast<const float4*>(A + (i0 + 2 * q) * 16);
-    float acc = 0.0f;
-#pragma unroll
-    for (int v = 0; v < 4; ++v) {
-      const float4 a = ar[v];
-      acc = fmaf(a.x, bc[4 * v], acc);
-      acc = fmaf(a.y, bc[4 * v + 1], acc);
-      acc = fmaf(a.z, bc[4 * v + 2], acc);
-      acc = fmaf(a.w, bc[4 * v + 3], acc);
+    for (int e = 0; e < 4; ++e) {
+      const uint32_t h = to_tf32(x.v[nt][e]);
+      o.hi[nt][e] = h;
+      o.lo[nt][e] = to_tf32(x.v[nt][e] - __uint_as_float(h));
     }
-    o[q] = acc;
-  }
 }
 
-// out = A * B^T
-__device__ __forceinline__ void prod_nt(const float* __restrict__ A, const float* __restrict__ B,
-                                        float (&o)[8], int lane) {
-  const int j = lane & 15, i0 = lane >> 4;
-  float bc[16];
-  const float4* br = reinterpret_cast<const float4*>(B + j * 16);
+// d (16 x 8) += A (16 x 8) * B (8 x 8), TF32 inputs, fp32 accumulation.
+__device__ __forceinline__ void mma_tf32(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// z = A B^T (3xTF32).  A fragment of k-step ks: (v[ks][0], v[ks][2], v[ks][1], v[ks][3]);
+// B fragment of (k-step ks, output half nz): (v[ks][2 nz], v[ks][2 nz + 1]).
+__device__ __forceinline__ void nt(F16& z, const F16S& A, const F16S& B) {
 #pragma unroll
-  for (int v = 0; v < 4; ++v) {
-    const float4 b = br[v];
-    bc[4 * v] = b.x; bc[4 * v + 1] = b.y; bc[4 * v + 2] = b.z; bc[4 * v + 3] = b.w;
-  }
+  for (int nz = 0; nz < 2; ++nz) {
+    float d0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, d1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    const float4* ar = reinterpret_cast<const float4*>(A + (i0 + 2 * q) * 16);
-    float acc = 0.0f;
-#pragma unroll
-    for (int v = 0; v < 4; ++v) {
-      const float4 a = ar[v];
-      acc = fmaf(a.x, bc[4 * v], acc);
-      acc = fmaf(a.y, bc[4 * v + 1], acc);
-      acc = fmaf(a.z, bc[4 * v + 2], acc);
-      acc = fmaf(a.w, bc[4 * v + 3], acc);
+    for (int ks = 0; ks < 2; ++ks) {
+      const uint32_t bh0 = B.hi[ks][2 * nz], bh1 = B.hi[ks][2 * nz + 1];
+      const uint32_t bl0 = B.lo[ks][2 * nz], bl1 = B.lo[ks][2 * nz + 1];
+      mma_tf32(d0, A.hi[ks][0], A.hi[ks][2], A.hi[ks][1], A.hi[ks][3], bh0, bh1);
+      mma_tf32(d1, A.hi[ks][0], A.hi[ks][2], A.hi[ks][1], A.hi[ks][3], bl0, bl1);
+      mma_tf32(d1, A.lo[ks][0], A.lo[ks][2], A.lo[ks][1], A.lo[ks][3], bh0, bh1);
     }
-    o[q] = acc;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) z.v[nz][e] = d0[e] + d1[e];
   }
 }
 
-__device__ __forceinline__ int ent(int lane, int q) { return ((lane >> 4) + 2 * q) * 16 + (lane & 15); }
-__device__ __forceinline__ int entT(int lane, int q) { return (lane & 15) * 16 + (lane >> 4) + 2 * q; }
-
-__device__ __forceinline__ void put(float* dst, const float (&o)[8], int lane) {
+// z = X^T, as the product I X^T (the identity is exact in TF32: head and tail of X only).
+__device__ __forceinline__ void transpose(F16& z, const F16S& X, int lane) {
+  const int g = lane >> 2, t = lane & 3;
+  constexpr uint32_t ONE = 0x3f800000u;
 #pragma unroll
-  for (int q = 0; q < 8; ++q) dst[ent(lane, q)] = o[q];
-}
-__device__ __forceinline__ void put2(float* dst, float* dstT, const float (&o)[8], int lane) {
+  for (int nz = 0; nz < 2; ++nz) {
+    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    dst[ent(lane, q)] = o[q];
-    dstT[entT(lane, q)] = o[q];
+    for (int ks = 0; ks < 2; ++ks) {
+      const int c = 8 * ks + 2 * t;  // k columns of slots t and t + 4: c and c + 1
+      const uint32_t a0 = (g == c) ? ONE : 0u, a1 = (g + 8 == c) ? ONE : 0u;
+      const uint32_t a2 = (g == c + 1) ? ONE : 0u, a3 = (g + 8 == c + 1) ? ONE : 0u;
+      mma_tf32(d, a0, a1, a2, a3, X.hi[ks][2 * nz], X.hi[ks][2 * nz + 1]);
+      mma_tf32(d, a0, a1, a2, a3, X.lo[ks][2 * nz], X.lo[ks][2 * nz + 1]);
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) z.v[nz][e] = d[e];
   }
 }
-__device__ __forceinline__ void load_lane(float (&o)[8], const float* __restrict__ g, int lane) {
+
+__device__ __forceinline__ void f_zero(F16& x) {
 #pragma unroll
-  for (int q = 0; q < 8; ++q) o[q] = __ldg(g + ent(lane, q));
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) x.v[nt][e] = 0.0f;
+}
+__device__ __forceinline__ void f_identity(F16& x, int lane) {
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) x.v[nt][e] = (frow(lane, e) == fcol(lane, nt, e)) ? 1.0f : 0.0f;
+}
+// row-major 16 x 16 at p (8-byte aligned)
+__device__ __forceinline__ void f_load(F16& x, const float* __restrict__ p, int lane) {
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float2 v = __ldg(reinterpret_cast<const float2*>(p + (g + 8 * h) * 16 + 8 * nt + 2 * t));
+      x.v[nt][2 * h] = v.x;
+      x.v[nt][2 * h + 1] = v.y;
+    }
+}
+__device__ __forceinline__ void f_load_plain(F16& x, const float* p, int lane) {
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float2 v = *reinterpret_cast<const float2*>(p + (g + 8 * h) * 16 + 8 * nt + 2 * t);
+      x.v[nt][2 * h] = v.x;
+      x.v[nt][2 * h + 1] = v.y;
+    }
+}
+template <bool STREAM>
+__device__ __forceinline__ void f_store(float* p, const F16& x, int lane, float scale = 1.0f) {
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float2 v = make_float2(scale * x.v[nt][2 * h], scale * x.v[nt][2 * h + 1]);
+      float2* q = reinterpret_cast<float2*>(p + (g + 8 * h) * 16 + 8 * nt + 2 * t);
+      if (STREAM) __stcs(q, v);
+      else *q = v;
+    }
+}
+// p[c][r] = x[r][c]
+__device__ __forceinline__ void f_store_t(float* p, const F16& x, int lane) {
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) p[fcol(lane, nt, e) * 16 + frow(lane, e)] = x.v[nt][e];
+}
+__device__ __forceinline__ void f_axpy(F16& y, float a, const F16& x) {
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) y.v[nt][e] = fmaf(a, x.v[nt][e], y.v[nt][e]);
+}
+__device__ __forceinline__ float f_dot(const F16& x, const F16& y) {
+  float s = 0.0f;
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) s = fmaf(x.v[nt][e], y.v[nt][e], s);
+  return s;
 }
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(FULL, v, off);
   return v;
 }
 
-struct Warp {
-  float* M;
-  float* Mt;
-  float* A;  // state / G
-  float* At;
-  float* T;
-  float* U;
-  float* V;
-  float* g;  // generators (<= 120)
-};
+// In-place Gauss-Jordan inverse of the fragment (no pivoting: the matrices inverted
+// here are I - Omega with Omega skew, whose pivots are >= 1).  Pivot k: row k lives in
+// the quad g = k % 8, column k in the lanes t = (k % 8) / 2.  With d = a_kk, u = column k
+// except u_k = d - 1, and v = row k except v_k = d + 1, the whole in-place step
+//   a_ij - a_ik a_kj / d,  a_kj / d (row k),  -a_ik / d (column k),  1 / d (pivot)
+// is the single rank-1 update A <- A - u v^T / d.
+__device__ __forceinline__ void gj_inverse(F16& A, int lane) {
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const int kh = k >> 3, kg = k & 7;                   // row k = kg + 8 kh
+    const int kn = k >> 3, kt = (k & 7) >> 1, ke = k & 1;  // col k = 8 kn + 2 kt + ke
+    float v[2][2], u[2];
+#pragma unroll
+    for (int n2 = 0; n2 < 2; ++n2)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) v[n2][c] = __shfl_sync(FULL, A.v[n2][2 * kh + c], 4 * kg + t);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) u[h] = __shfl_sync(FULL, A.v[kn][2 * h + ke], 4 * g + kt);
+    const float piv = __shfl_sync(FULL, A.v[kn][2 * kh + ke], 4 * kg + kt);
+    const float inv = __frcp_rn(piv);
+    if (g == kg) u[kh] -= 1.0f;   // this lane holds row k
+    if (t == kt) v[kn][ke] += 1.0f;  // this lane holds column k
+    const float p0 = u[0] * inv, p1 = u[1] * inv;
+#pragma unroll
+    for (int n2 = 0; n2 < 2; ++n2)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) A.v[n2][e] = fmaf(-((e >> 1) ? p1 : p0), v[n2][e & 1], A.v[n2][e]);
+  }
+}
 
+// ------------------------------------------------------------- rotor generators
+// Each lane's 8 entries of Omega are sums of up to NTERM signed generators; the terms
+// are packed once per kernel as bytes (bits 0-6 generator index, bit 7 negative; index
+// K points at a zero slot).
 struct BlockTab {
   unsigned char col[CSN_CL8_NBIV][16];
   signed char sgn[CSN_CL8_NBIV][16];
 };
 
-// Build M = sa (2 (I - Omega)^{-1} - I) and M^T into w.M / w.Mt.
-template <int BASIS, bool DAMPED, int K>
-__device__ __forceinline__ void build_M(const ScanArgs& a, const BlockTab& tab, Warp& w, int lane,
-                                        int64_t b, int64_t t, int64_t e, float& alpha, float& sa,
-                                        float& dtv, float& gam) {
-  for (int k = lane; k < K; k += 32) w.g[k] = __ldg(a.gens + e * K + k);
-  dtv = __ldg(a.dt + b * a.T + t);
-  const float h = 0.5f * dtv;
-  __syncwarp();
-  float* A = w.T;  // GJ work buffer
-  if constexpr (BASIS == BASIS_TRIU) {
+template <int BASIS>
+struct NTerms {
+  static constexpr int value = (BASIS == BASIS_TRIU) ? 1 : 3;
+};
+
+__device__ __forceinline__ int triu_index(int i, int j) { return i * (2 * D - i - 1) / 2 + (j - i - 1); }
+
+template <int BASIS, int K>
+__device__ __forceinline__ void make_terms(uint32_t (&terms)[2][4], const BlockTab& tab, int lane) {
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const int idx = ent(lane, q), i = idx >> 4, j = idx & 15;
-      float v = (i == j) ? 1.0f : 0.0f;
-      if (i < j) v = -h * w.g[i * (2 * D - i - 1) / 2 + (j - i - 1)];
-      else if (i > j) v = h * w.g[j * (2 * D - j - 1) / 2 + (i - j - 1)];
-      A[idx] = v;
-    }
-  } else {
-    if (lane < 16) {
-      float row[16];
+  for (int n2 = 0; n2 < 2; ++n2)
 #pragma unroll
-      for (int c = 0; c < 16; ++c) row[c] = (c == lane) ? 1.0f : 0.0f;
-      for (int k = 0; k < K; ++k) {
-        const float wk = h * w.g[k];
-        const int c = tab.col[k][lane];
-        const float sg = tab.sgn[k][lane];
-#pragma unroll
-        for (int cc = 0; cc < 16; ++cc)
-          if (cc == c) row[cc] = fmaf(-sg, wk, row[cc]);
+    for (int e = 0; e < 4; ++e) {
+      const int r = frow(lane, e), c = fcol(lane, n2, e);
+      uint32_t packed = (uint32_t)K | ((uint32_t)K << 8) | ((uint32_t)K << 16);
+      if constexpr (BASIS == BASIS_TRIU) {
+        if (r < c) packed = (packed & ~0xffu) | (uint32_t)triu_index(r, c);
+        else if (r > c) packed = (packed & ~0xffu) | (uint32_t)triu_index(c, r) | 0x80u;
+      } else {
+        int m = 0;
+        for (int k = 0; k < K; ++k) {
+          if (tab.col[k][r] == c && m < 3) {
+            const uint32_t byte = (uint32_t)k | (tab.sgn[k][r] < 0 ? 0x80u : 0u);
+            packed = (packed & ~(0xffu << (8 * m))) | (byte << (8 * m));
+            ++m;
+          }
+        }
       }
-#pragma unroll
-      for (int c = 0; c < 16; ++c) A[lane * 16 + c] = row[c];
+      terms[n2][e] = packed;
     }
-  }
-  __syncwarp();
-  // Gauss-Jordan inverse in place (pivots >= 1 for I - skew, no pivoting needed)
-  for (int k = 0; k < 16; ++k) {
-    const float inv = 1.0f / A[k * 16 + k];
-    float nv[8];
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const int idx = ent(lane, q), i = idx >> 4, j = idx & 15;
-      const float aij = A[idx];
-      if (i == k && j == k) nv[q] = inv;
-      else if (i == k) nv[q] = aij * inv;
-      else if (j == k) nv[q] = -aij * inv;
-      else nv[q] = aij - A[i * 16 + k] * A[k * 16 + j] * inv;
-    }
-    __syncwarp();
-#pragma unroll
-    for (int q = 0; q < 8; ++q) A[ent(lane, q)] = nv[q];
-    __syncwarp();
-  }
-  if constexpr (DAMPED) {
-    gam = __ldg(a.gamma + e);
-    alpha = 1.0f / (1.0f + expf(gam * dtv));
-    sa = sqrtf(alpha);
-  } else {
-    gam = 0.0f;
-    alpha = 1.0f;
-    sa = 1.0f;
-  }
-  float m[8];
-#pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    const int idx = ent(lane, q);
-    m[q] = sa * (2.0f * A[idx] - (((idx >> 4) == (idx & 15)) ? 1.0f : 0.0f));
-  }
-  put2(w.M, w.Mt, m, lane);
-  __syncwarp();
 }
+
+// Om = h Omega from the generators in shared memory (gs[K] == 0).
+template <int NTERM>
+__device__ __forceinline__ void build_Om(F16& Om, const float* gs, const uint32_t (&terms)[2][4], float h) {
+#pragma unroll
+  for (int n2 = 0; n2 < 2; ++n2)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float om = 0.0f;
+#pragma unroll
+      for (int m = 0; m < NTERM; ++m) {
+        const uint32_t byte = (terms[n2][e] >> (8 * m)) & 0xffu;
+        const float v = gs[byte & 0x7fu];
+        om += (byte & 0x80u) ? -v : v;
+      }
+      Om.v[n2][e] = h * om;
+    }
+}
+
+// |Om|_F^2 at or below this takes the series inverse (|Om|_2 <= |Om|_F <= 0.1).
+constexpr float kSeriesFro2 = 0.01f;
+
+// M = sa (2 (I - Om)^{-1} - I), in place on Om.
+// (I - Om)^{-1} = (I + Om) (I - W)^{-1} with W = Om^2 (Om skew, so W is symmetric and
+// |W|_2 <= |Om|_F^2).  For |Om|_F <= 0.1 the inverse is the series
+//   (I + Om) (I + W) (I + W^2)          (truncation sum_{k>=4} W^k <= 1.01e-8)
+// -- four products whose operands are symmetric or skew, so each is a plain A B^T with
+// no transposes; larger Om takes the Gauss-Jordan elimination.  The choice is uniform
+// across the warp (one matrix per warp).
+__device__ __forceinline__ void cayley(F16& M, float sa, int lane) {
+  const float fro2 = warp_sum(f_dot(M, M));
+  if (fro2 <= kSeriesFro2) {
+    F16S Os;
+    split(Os, M);
+    F16 W;
+    nt(W, Os, Os);  // Om Om^T = -Om^2
+    F16 P, U;       // I + W = I - Om Om^T ;  I + Om
+#pragma unroll
+    for (int n2 = 0; n2 < 2; ++n2)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float id = (frow(lane, e) == fcol(lane, n2, e)) ? 1.0f : 0.0f;
+        W.v[n2][e] = -W.v[n2][e];
+        P.v[n2][e] = id + W.v[n2][e];
+        U.v[n2][e] = id + M.v[n2][e];
+      }
+    F16S Ws;
+    split(Ws, W);
+    F16 Q;
+    nt(Q, Ws, Ws);  // W W^T = W^2
+#pragma unroll
+    for (int n2 = 0; n2 < 2; ++n2)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) Q.v[n2][e] += (frow(lane, e) == fcol(lane, n2, e)) ? 1.0f : 0.0f;
+    F16S Ps, Qs;
+    split(Ps, P);
+    split(Qs, Q);
+    F16 E;
+    nt(E, Ps, Qs);  // (I + W) (I + W^2), symmetric
+    F16S Us, Es;
+    split(Us, U);
+    split(Es, E);
+    nt(M, Us, Es);  // (I + Om) E
+  } else {
+#pragma unroll
+    for (int n2 = 0; n2 < 2; ++n2)
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        M.v[n2][e] = ((frow(lane, e) == fcol(lane, n2, e)) ? 1.0f : 0.0f) - M.v[n2][e];
+    gj_inverse(M, lane);
+  }
+#pragma unroll
+  for (int n2 = 0; n2 < 2; ++n2)
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      M.v[n2][e] = sa * (2.0f * M.v[n2][e] - ((frow(lane, e) == fcol(lane, n2, e)) ? 1.0f : 0.0f));
+}
+
+__device__ const Cl8BivTab g_cl8_tab = cl8_biv_tab();
 
 __device__ __forceinline__ void load_tab(BlockTab& tab) {
-  constexpr auto t = cl8_biv_tab();
   for (int i = threadIdx.x; i < CSN_CL8_NBIV * 16; i += blockDim.x) {
-    tab.col[i / 16][i % 16] = t.col[i / 16][i % 16];
-    tab.sgn[i / 16][i % 16] = t.sgn[i / 16][i % 16];
+    tab.col[i / 16][i % 16] = g_cl8_tab.col[i / 16][i % 16];
+    tab.sgn[i / 16][i % 16] = g_cl8_tab.sgn[i / 16][i % 16];
   }
 }
 
-#define S16_SETUP()                                                               \
-  __shared__ __align__(16) float sm[WARPS][7][DD];                                \
-  __shared__ __align__(16) float sg[WARPS][128];                                  \
-  __shared__ BlockTab tab;                                                        \
-  if (BASIS == BASIS_GA) load_tab(tab);                                           \
-  __syncthreads();                                                                \
-  const int wi = threadIdx.x >> 5, lane = threadIdx.x & 31;                       \
-  const int64_t wid = blockIdx.x * (int64_t)WARPS + wi;                           \
-  const int64_t total = a.B * a.N * a.nchunks;                                    \
-  if (wid >= total) return;                                                       \
-  const int64_t n = wid % a.N;                                                    \
-  const int64_t j = (wid / a.N) % a.nchunks;                                      \
-  const int64_t b = wid / (a.N * a.nchunks);                                      \
-  const int64_t s = b * a.N + n;                                                  \
-  const int64_t t0 = j * a.chunk;                                                 \
-  const int64_t t1 = min(a.T, t0 + a.chunk);                                      \
-  Warp w{sm[wi][0], sm[wi][1], sm[wi][2], sm[wi][3], sm[wi][4], sm[wi][5], sm[wi][6], sg[wi]}; \
-  (void)s; (void)t1;
+// Per-warp step context: coordinates, the generator slot and the packed Omega terms.
+struct Warp {
+  int lane;
+  int64_t b, n, j, s, t0, t1;
+  float* gs;  // K + 1 floats of this warp (gs[K] = 0)
+  float* zs;  // 16 x ZST dOmega scratch (backward apply)
+};
 
-template <int SRC, int BASIS, bool DAMPED, bool TWO>
-__global__ void __launch_bounds__(128) fwd_reduce16(ScanArgs a) {
-  constexpr int K = GenCount<16, BASIS>::K;
-  S16_SETUP();
-  // w.A = c (state), w.U = P
-  float o[8];
+#define S16_PROLOGUE(BASIS, K)                                                   \
+  __shared__ __align__(16) float sm_g[WARPS][128];                               \
+  __shared__ __align__(16) float sm_z[WARPS][16 * ZST];                          \
+  __shared__ BlockTab tab;                                                       \
+  if (BASIS == BASIS_GA) load_tab(tab);                                          \
+  __syncthreads();                                                               \
+  const int wi = threadIdx.x >> 5;                                               \
+  const int64_t wid = blockIdx.x * (int64_t)WARPS + wi;                          \
+  if (wid >= a.B * a.N * a.nchunks) return;                                      \
+  Warp w;                                                                        \
+  w.lane = threadIdx.x & 31;                                                     \
+  w.n = wid % a.N;                                                               \
+  w.j = (wid / a.N) % a.nchunks;                                                 \
+  w.b = wid / (a.N * a.nchunks);                                                 \
+  w.s = w.b * a.N + w.n;                                                         \
+  w.t0 = w.j * a.chunk;                                                          \
+  w.t1 = min(a.T, w.t0 + a.chunk);                                               \
+  w.gs = sm_g[wi];                                                               \
+  w.zs = sm_z[wi];                                                               \
+  uint32_t terms[2][4] = {{0u, 0u, 0u, 0u}, {0u, 0u, 0u, 0u}};                   \
+  if (SRC == SRC_ROTOR) {                                                        \
+    make_terms<BASIS, K>(terms, tab, w.lane);                                    \
+    if (w.lane == 0) w.gs[K] = 0.0f;                                             \
+  }
+
+// Generators of element e into registers (lane holds k = lane + 32 m).
+template <int K>
+__device__ __forceinline__ void fetch_gens(float (&gr)[(K + 31) / 32], const float* __restrict__ gens,
+                                           int64_t e, int lane) {
 #pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    const int idx = ent(lane, q);
-    w.A[idx] = 0.0f;
-    w.U[idx] = ((idx >> 4) == (idx & 15)) ? 1.0f : 0.0f;
+  for (int m = 0; m < (K + 31) / 32; ++m) {
+    const int k = lane + 32 * m;
+    gr[m] = (k < K) ? __ldg(gens + e * K + k) : 0.0f;
+  }
+}
+template <int K>
+__device__ __forceinline__ void stage_gens(float* gs, const float (&gr)[(K + 31) / 32], int lane) {
+  __syncwarp();  // previous step's readers are done
+#pragma unroll
+  for (int m = 0; m < (K + 31) / 32; ++m) {
+    const int k = lane + 32 * m;
+    if (k < K) gs[k] = gr[m];
   }
   __syncwarp();
-  for (int64_t t = t0; t < t1; ++t) {
-    const int64_t e = (b * a.T + t) * a.N + n;
-    float alpha = 1.0f, sa = 1.0f, dtv = 0.0f, gam = 0.0f, cs = 1.0f;
-    if constexpr (SRC == SRC_MC) {
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const float v = __ldg(a.M + e * DD + ent(lane, q));
-        w.M[ent(lane, q)] = v;
-        w.Mt[entT(lane, q)] = v;
-      }
-      __syncwarp();
+}
+
+// The step matrix M (Cayley rotor or a given M) of element e at time t.
+template <int SRC, int BASIS, bool DAMPED, int K>
+__device__ __forceinline__ void step_matrix(const ScanArgs& a, const Warp& w, const uint32_t (&terms)[2][4],
+                                            int64_t e, int64_t t, F16& M, float& alpha, float& sa,
+                                            float& dtv, float& gam) {
+  if constexpr (SRC == SRC_MC) {
+    f_load(M, a.M + e * DD, w.lane);
+    alpha = sa = 1.0f;
+    dtv = gam = 0.0f;
+  } else {
+    dtv = __ldg(a.dt + w.b * a.T + t);
+    if constexpr (DAMPED) {
+      gam = __ldg(a.gamma + e);
+      alpha = 1.0f / (1.0f + expf(gam * dtv));
+      sa = sqrtf(alpha);
     } else {
-      build_M<BASIS, DAMPED, K>(a, tab, w, lane, b, t, e, alpha, sa, dtv, gam);
-      cs = DAMPED ? (1.0f - alpha) : 1.0f;
+      gam = 0.0f;
+      alpha = sa = 1.0f;
     }
-    const float* inj = (SRC == SRC_MC) ? (a.C + e * DD) : (a.S + e * DD);
-    prod_nn(w.M, w.A, o, lane);  // M c
-    __syncwarp();
-    if constexpr (TWO) {
-      put(w.V, o, lane);
-      __syncwarp();
-      prod_nt(w.V, w.M, o, lane);  // (M c) M^T
-    }
-#pragma unroll
-    for (int q = 0; q < 8; ++q) o[q] = fmaf(cs, __ldg(inj + ent(lane, q)), o[q]);
-    __syncwarp();
-    put(w.A, o, lane);
-    prod_nn(w.M, w.U, o, lane);  // M P
-    __syncwarp();
-    put(w.U, o, lane);
-    __syncwarp();
-  }
-#pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    a.aggP[(s * a.nchunks + j) * DD + ent(lane, q)] = w.U[ent(lane, q)];
-    a.aggC[(s * a.nchunks + j) * DD + ent(lane, q)] = w.A[ent(lane, q)];
+    build_Om<NTerms<BASIS>::value>(M, w.gs, terms, 0.5f * dtv);
+    cayley(M, sa, w.lane);
   }
 }
 
-template <int SRC, int BASIS, bool DAMPED, bool TWO>
-__global__ void __launch_bounds__(128) fwd_apply16(ScanArgs a) {
+// ---------------------------------------------------------------------- forward
+// REDUCE: chunk aggregate (P = M_last ... M_first, c = chunk scanned from zero);
+// otherwise the apply pass from the chunk's carry.
+template <bool REDUCE, int SRC, int BASIS, bool DAMPED, bool TWO>
+__global__ void __launch_bounds__(128) fwd16_kernel(ScanArgs a) {
   constexpr int K = GenCount<16, BASIS>::K;
-  S16_SETUP();
-  float o[8];
-#pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    const int idx = ent(lane, q);
-    float v = 0.0f;
-    if (a.nchunks > 1) v = a.carry[(s * a.nchunks + j) * DD + idx];
-    else if (a.h0) v = a.h0[s * DD + idx];
-    w.A[idx] = v;
+  constexpr int KR = (K + 31) / 32;
+  S16_PROLOGUE(BASIS, K);
+  const int lane = w.lane;
+  F16 X, Pt;
+  if (REDUCE) {
+    f_zero(X);
+    f_identity(Pt, lane);
+  } else if (a.nchunks > 1) {
+    f_load_plain(X, a.carry + (w.s * a.nchunks + w.j) * DD, lane);
+  } else if (a.h0) {
+    f_load(X, a.h0 + w.s * DD, lane);
+  } else {
+    f_zero(X);
   }
-  __syncwarp();
-  for (int64_t t = t0; t < t1; ++t) {
-    const int64_t e = (b * a.T + t) * a.N + n;
-    float alpha = 1.0f, sa = 1.0f, dtv = 0.0f, gam = 0.0f, cs = 1.0f;
-    if constexpr (SRC == SRC_MC) {
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const float v = __ldg(a.M + e * DD + ent(lane, q));
-        w.M[ent(lane, q)] = v;
-        w.Mt[entT(lane, q)] = v;
-      }
-      __syncwarp();
-    } else {
-      build_M<BASIS, DAMPED, K>(a, tab, w, lane, b, t, e, alpha, sa, dtv, gam);
-      cs = DAMPED ? (1.0f - alpha) : 1.0f;
+  float gr[KR];
+  if (SRC == SRC_ROTOR && w.t0 < w.t1) fetch_gens<K>(gr, a.gens, (w.b * a.T + w.t0) * a.N + w.n, lane);
+  for (int64_t t = w.t0; t < w.t1; ++t) {
+    const int64_t e = (w.b * a.T + t) * a.N + w.n;
+    F16 Cin;
+    f_load(Cin, (SRC == SRC_MC ? a.C : a.S) + e * DD, lane);
+    if constexpr (SRC == SRC_ROTOR) {
+      stage_gens<K>(w.gs, gr, lane);
+      if (t + 1 < w.t1) fetch_gens<K>(gr, a.gens, e + a.N, lane);
     }
-    const float* inj = (SRC == SRC_MC) ? (a.C + e * DD) : (a.S + e * DD);
-    prod_nn(w.M, w.A, o, lane);
-    __syncwarp();
-    if constexpr (TWO) {
-      put(w.V, o, lane);
-      __syncwarp();
-      prod_nt(w.V, w.M, o, lane);
-    }
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      o[q] = fmaf(cs, __ldg(inj + ent(lane, q)), o[q]);
-      __stcs(a.out + e * DD + ent(lane, q), o[q]);
-    }
-    __syncwarp();
-    put(w.A, o, lane);
-    __syncwarp();
-  }
-}
-
-template <int SRC, int BASIS, bool DAMPED, bool TWO>
-__global__ void __launch_bounds__(128) bwd_reduce16(ScanArgs a) {
-  constexpr int K = GenCount<16, BASIS>::K;
-  S16_SETUP();
-  if (j == 0 && !a.agg_mode) return;
-  float o[8];
-#pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    const int idx = ent(lane, q);
-    w.A[idx] = 0.0f;
-    w.U[idx] = ((idx >> 4) == (idx & 15)) ? 1.0f : 0.0f;
-  }
-  __syncwarp();
-  for (int64_t t = t1 - 1; t >= t0; --t) {
-    const int64_t e = (b * a.T + t) * a.N + n;
+    F16 M;
     float alpha, sa, dtv, gam;
-    if constexpr (SRC == SRC_MC) {
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const float v = __ldg(a.M + e * DD + ent(lane, q));
-        w.M[ent(lane, q)] = v;
-        w.Mt[entT(lane, q)] = v;
-      }
-      __syncwarp();
-    } else {
-      build_M<BASIS, DAMPED, K>(a, tab, w, lane, b, t, e, alpha, sa, dtv, gam);
-    }
-    // G = g + dX
-#pragma unroll
-    for (int q = 0; q < 8; ++q) w.A[ent(lane, q)] += __ldg(a.dX + e * DD + ent(lane, q));
-    __syncwarp();
-    prod_nn(w.Mt, w.A, o, lane);  // M^T G
-    __syncwarp();
+    step_matrix<SRC, BASIS, DAMPED, K>(a, w, terms, e, t, M, alpha, sa, dtv, gam);
+    const float cs = (SRC == SRC_ROTOR && DAMPED) ? (1.0f - alpha) : 1.0f;
+    F16S Ms, Xs;
+    split(Ms, M);
+    split(Xs, X);
+    F16 V;
     if constexpr (TWO) {
-      put(w.V, o, lane);
-      __syncwarp();
-      prod_nn(w.V, w.M, o, lane);  // (M^T G) M
-      __syncwarp();
+      nt(V, Ms, Xs);  // M X^T
+    } else {
+      transpose(V, Xs, lane);  // X^T
     }
-    put(w.A, o, lane);
-    prod_nn(w.U, w.M, o, lane);  // P M
-    __syncwarp();
-    put(w.U, o, lane);
-    __syncwarp();
+    F16S Vs;
+    split(Vs, V);
+    nt(X, Ms, Vs);  // M V^T:  M X M^T  |  M X
+    f_axpy(X, cs, Cin);
+    if constexpr (REDUCE) {
+      F16S Ps;
+      split(Ps, Pt);
+      nt(Pt, Ps, Ms);  // P^T M^T = (M P)^T
+    } else {
+      f_store<true>(a.out + e * DD, X, lane);
+    }
   }
-#pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    a.aggP[(s * a.nchunks + j) * DD + ent(lane, q)] = w.U[ent(lane, q)];
-    a.aggC[(s * a.nchunks + j) * DD + ent(lane, q)] = w.A[ent(lane, q)];
+  if constexpr (REDUCE) {
+    f_store<false>(a.aggC + (w.s * a.nchunks + w.j) * DD, X, lane);
+    f_store_t(a.aggP + (w.s * a.nchunks + w.j) * DD, Pt, lane);
   }
 }
 
+// ------------------------------------------------------------- backward: reduce
+// c' = gradient leaving the chunk at its first step with zero gradient from the right,
+// P = M_last ... M_first (built as P <- P M walking backwards).
 template <int SRC, int BASIS, bool DAMPED, bool TWO>
-__global__ void __launch_bounds__(128) bwd_apply16(ScanArgs a) {
+__global__ void __launch_bounds__(128) bwd16_reduce_kernel(ScanArgs a) {
   constexpr int K = GenCount<16, BASIS>::K;
-  S16_SETUP();
-  float o[8], gq[8];
-  // w.A = H (carry from the right), later G;  w.At = G^T
-#pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    const int idx = ent(lane, q);
-    w.A[idx] = (a.nchunks > 1) ? a.carry[(s * a.nchunks + j) * DD + idx] : a.hT ? a.hT[s * DD + idx] : 0.0f;
+  constexpr int KR = (K + 31) / 32;
+  S16_PROLOGUE(BASIS, K);
+  if (w.j == 0 && !a.agg_mode) return;  // chunk 0's aggregate is only used by shard aggregates
+  const int lane = w.lane;
+  F16 Gc, P;
+  f_zero(Gc);
+  f_identity(P, lane);
+  float gr[KR];
+  if (SRC == SRC_ROTOR && w.t0 < w.t1) fetch_gens<K>(gr, a.gens, (w.b * a.T + w.t1 - 1) * a.N + w.n, lane);
+  for (int64_t t = w.t1 - 1; t >= w.t0; --t) {
+    const int64_t e = (w.b * a.T + t) * a.N + w.n;
+    F16 dX;
+    f_load(dX, a.dX + e * DD, lane);
+    if constexpr (SRC == SRC_ROTOR) {
+      stage_gens<K>(w.gs, gr, lane);
+      if (t - 1 >= w.t0) fetch_gens<K>(gr, a.gens, e - a.N, lane);
+    }
+    F16 M;
+    float alpha, sa, dtv, gam;
+    step_matrix<SRC, BASIS, DAMPED, K>(a, w, terms, e, t, M, alpha, sa, dtv, gam);
+    F16S Ms, Mts;
+    split(Ms, M);
+    F16 Mt;
+    transpose(Mt, Ms, lane);
+    split(Mts, Mt);
+    f_axpy(Gc, 1.0f, dX);  // G = g + dX
+    F16S Gs;
+    split(Gs, Gc);
+    F16 W;
+    if constexpr (TWO) {
+      nt(W, Mts, Gs);  // M^T G^T
+    } else {
+      transpose(W, Gs, lane);  // G^T
+    }
+    F16S Ws;
+    split(Ws, W);
+    nt(Gc, Mts, Ws);  // M^T G M  |  M^T G
+    F16S Ps;
+    split(Ps, P);
+    nt(P, Ps, Mts);  // P M
   }
-  __syncwarp();
-  float* Xp = w.U;
-  for (int64_t t = t1 - 1; t >= t0; --t) {
-    const int64_t e = (b * a.T + t) * a.N + n;
-    float alpha = 1.0f, sa = 1.0f, dtv = 0.0f, gam = 0.0f;
-    if constexpr (SRC == SRC_MC) {
+  f_store<false>(a.aggC + (w.s * a.nchunks + w.j) * DD, Gc, lane);
+  f_store<false>(a.aggP + (w.s * a.nchunks + w.j) * DD, P, lane);
+}
+
+// -------------------------------------------------------------- backward: apply
+// Per step t (reverse):  G = H + dX_t,  dC = G (rotor: dS = (1 - a) G)
+//   dM = G M Xp^T + G^T M Xp  (one-sided: G Xp^T),  Xp = X_{t-1}
+//   rotor: da = -<G, S> + <dM, M> / (2 a);  dOmega = 0.5 sa B dM B with B = I + M^T / sa;
+//          dg_k = <dOmega, E_k> dt / 2
+//   H <- M^T G M  (one-sided: M^T G)
+template <int SRC, int BASIS, bool DAMPED, bool TWO>
+__global__ void __launch_bounds__(128) bwd16_apply_kernel(ScanArgs a) {
+  constexpr int K = GenCount<16, BASIS>::K;
+  constexpr int KR = (K + 31) / 32;
+  S16_PROLOGUE(BASIS, K);
+  const int lane = w.lane;
+  F16 H;
+  if (a.nchunks > 1) f_load_plain(H, a.carry + (w.s * a.nchunks + w.j) * DD, lane);
+  else if (a.hT) f_load(H, a.hT + w.s * DD, lane);
+  else f_zero(H);
+  // triu generator k = lane + 32 m  ->  (i, j) packed as i * 16 + j
+  int kpair[KR];
+  if constexpr (SRC == SRC_ROTOR && BASIS == BASIS_TRIU) {
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const float v = __ldg(a.M + e * DD + ent(lane, q));
-        w.M[ent(lane, q)] = v;
-        w.Mt[entT(lane, q)] = v;
-      }
-      __syncwarp();
-    } else {
-      build_M<BASIS, DAMPED, K>(a, tab, w, lane, b, t, e, alpha, sa, dtv, gam);
-    }
-    // G = H + dX_t
-#pragma unroll
-    for (int q = 0; q < 8; ++q) gq[q] = w.A[ent(lane, q)] + __ldg(a.dX + e * DD + ent(lane, q));
-    __syncwarp();
-    put2(w.A, w.At, gq, lane);
-    const float* xprev = (t > 0) ? (a.X + ((b * a.T + t - 1) * a.N + n) * DD)
-                                 : (a.h0 ? a.h0 + s * DD : nullptr);
-    float dm[8];
-    if (xprev) {
-#pragma unroll
-      for (int q = 0; q < 8; ++q) Xp[ent(lane, q)] = __ldg(xprev + ent(lane, q));
-      __syncwarp();
-      if constexpr (TWO) {
-        prod_nn(w.A, w.M, o, lane);  // G M
-        put(w.T, o, lane);
-        __syncwarp();
-        prod_nt(w.T, Xp, dm, lane);  // G M Xp^T
-        prod_nn(w.M, Xp, o, lane);   // M Xp
-        __syncwarp();
-        put(w.V, o, lane);
-        __syncwarp();
-        prod_nn(w.At, w.V, o, lane);  // G^T M Xp
-#pragma unroll
-        for (int q = 0; q < 8; ++q) dm[q] += o[q];
+    for (int m = 0; m < KR; ++m) {
+      int k = lane + 32 * m, u = 0;
+      if (k < K) {
+        while (k >= D - 1 - u) { k -= D - 1 - u; ++u; }
+        kpair[m] = u * 16 + (u + 1 + k);
       } else {
-        prod_nt(w.A, Xp, dm, lane);  // G Xp^T
+        kpair[m] = 0;
       }
-    } else {
-#pragma unroll
-      for (int q = 0; q < 8; ++q) dm[q] = 0.0f;
     }
-    __syncwarp();
-    if constexpr (SRC == SRC_MC) {
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        __stcs(a.dM + e * DD + ent(lane, q), dm[q]);
-        __stcs(a.dC + e * DD + ent(lane, q), gq[q]);
+  }
+  float gr[KR];
+  if (SRC == SRC_ROTOR && w.t0 < w.t1) fetch_gens<K>(gr, a.gens, (w.b * a.T + w.t1 - 1) * a.N + w.n, lane);
+  for (int64_t t = w.t1 - 1; t >= w.t0; --t) {
+    const int64_t e = (w.b * a.T + t) * a.N + w.n;
+    F16 dX, Xp, Sx;
+    f_load(dX, a.dX + e * DD, lane);
+    const float* xprev = (t > 0) ? (a.X + (e - a.N) * DD) : (a.h0 ? a.h0 + w.s * DD : nullptr);
+    if (xprev) f_load(Xp, xprev, lane);
+    if (SRC == SRC_ROTOR && DAMPED) f_load(Sx, a.S + e * DD, lane);
+    if constexpr (SRC == SRC_ROTOR) {
+      stage_gens<K>(w.gs, gr, lane);
+      if (t - 1 >= w.t0) fetch_gens<K>(gr, a.gens, e - a.N, lane);
+    }
+    F16 M;
+    float alpha, sa, dtv, gam;
+    step_matrix<SRC, BASIS, DAMPED, K>(a, w, terms, e, t, M, alpha, sa, dtv, gam);
+    F16S Ms, Mts;
+    split(Ms, M);
+    F16 Mt;
+    transpose(Mt, Ms, lane);
+    split(Mts, Mt);
+    F16 G = H;
+    f_axpy(G, 1.0f, dX);
+    F16S Gs;
+    split(Gs, G);
+    const float cs = (SRC == SRC_ROTOR && DAMPED) ? (1.0f - alpha) : 1.0f;
+    f_store<true>(a.dC + e * DD, G, lane, cs);  // dC | dS
+    // ---- dM
+    F16 dM;
+    F16 Gt;  // G^T (two-sided dM, one-sided carry)
+    transpose(Gt, Gs, lane);
+    F16S Gts;
+    split(Gts, Gt);
+    if (xprev) {
+      F16S Xps;
+      split(Xps, Xp);
+      if constexpr (TWO) {
+        F16 GM;
+        nt(GM, Gs, Mts);  // G M
+        F16S GMs;
+        split(GMs, GM);
+        nt(dM, GMs, Xps);  // G M Xp^T
+        F16 Xpt;
+        transpose(Xpt, Xps, lane);
+        F16S Xpts;
+        split(Xpts, Xpt);
+        F16 XM;
+        nt(XM, Xpts, Ms);  // Xp^T M^T
+        F16S XMs;
+        split(XMs, XM);
+        F16 T2;
+        nt(T2, Gts, XMs);  // G^T M Xp
+        f_axpy(dM, 1.0f, T2);
+      } else {
+        nt(dM, Gs, Xps);  // G Xp^T
       }
     } else {
-      const float cs = DAMPED ? (1.0f - alpha) : 1.0f;
-#pragma unroll
-      for (int q = 0; q < 8; ++q) __stcs(a.dC + e * DD + ent(lane, q), cs * gq[q]);
+      f_zero(dM);
+    }
+    if constexpr (SRC == SRC_MC) {
+      f_store<true>(a.dM + e * DD, dM, lane);
+    } else {
       float da = 0.0f;
       if constexpr (DAMPED) {
-        float p1 = 0.0f, p2 = 0.0f;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          p1 = fmaf(dm[q], w.M[ent(lane, q)], p1);
-          p2 = fmaf(gq[q], __ldg(a.S + e * DD + ent(lane, q)), p2);
-        }
-        p1 = warp_sum(p1);
-        p2 = warp_sum(p2);
+        const float p1 = warp_sum(f_dot(dM, M));
+        const float p2 = warp_sum(f_dot(G, Sx));
         da = -p2 + p1 / (2.0f * alpha);
       }
-      // dQ = sa dM;  V = Bt dQ with Bt = 0.5 (Mt / sa + I);  dOm = 2 V Bt = V (Mt / sa + I)
+      // dOmega^T = 0.5 sa Bt dM^T Bt,  Bt = B^T = I + M / sa
       const float inv_sa = 1.0f / sa;
+      F16 Bt, Bm;
 #pragma unroll
-      for (int q = 0; q < 8; ++q) dm[q] *= sa;
-      put(w.T, dm, lane);
-      __syncwarp();
-      prod_nn(w.Mt, w.T, o, lane);
+      for (int n2 = 0; n2 < 2; ++n2)
 #pragma unroll
-      for (int q = 0; q < 8; ++q) o[q] = 0.5f * (o[q] * inv_sa + dm[q]);
+        for (int q = 0; q < 4; ++q) {
+          const float id = (frow(lane, q) == fcol(lane, n2, q)) ? 1.0f : 0.0f;
+          Bt.v[n2][q] = fmaf(M.v[n2][q], inv_sa, id);
+          Bm.v[n2][q] = fmaf(Mt.v[n2][q], inv_sa, id);
+        }
+      F16S Bts, Bms, dMs;
+      split(Bts, Bt);
+      split(Bms, Bm);
+      split(dMs, dM);
+      F16 Y;
+      nt(Y, Bts, dMs);  // Bt dM^T
+      F16S Ys;
+      split(Ys, Y);
+      F16 Zt;
+      nt(Zt, Ys, Bms);  // Bt dM^T Bt = (B dM B)^T
+      // dOmega[u][v] = 0.5 sa Zt[v][u] -> zs[u * ZST + v]
       __syncwarp();
-      put(w.V, o, lane);
-      __syncwarp();
-      float vq[8];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) vq[q] = o[q];
-      prod_nn(w.V, w.Mt, o, lane);
+      for (int n2 = 0; n2 < 2; ++n2)
 #pragma unroll
-      for (int q = 0; q < 8; ++q) o[q] = o[q] * inv_sa + vq[q];
-      __syncwarp();
-      put(w.T, o, lane);  // dOmega
+        for (int q = 0; q < 4; ++q)
+          w.zs[fcol(lane, n2, q) * ZST + frow(lane, q)] = 0.5f * sa * Zt.v[n2][q];
       __syncwarp();
       float ddt = 0.0f;
       const float hdt = 0.5f * dtv;
-      for (int k = lane; k < K; k += 32) {
-        float pk;
-        if constexpr (BASIS == BASIS_TRIU) {
-          // k -> (u, v) in triu order
-          int u = 0, rem = k;
-          while (rem >= D - 1 - u) { rem -= D - 1 - u; ++u; }
-          const int v = u + 1 + rem;
-          pk = w.T[u * 16 + v] - w.T[v * 16 + u];
-        } else {
-          pk = 0.0f;
 #pragma unroll
-          for (int u = 0; u < 16; ++u) pk = fmaf((float)tab.sgn[k][u], w.T[u * 16 + tab.col[k][u]], pk);
+      for (int m = 0; m < KR; ++m) {
+        const int k = lane + 32 * m;
+        if (k < K) {
+          float pk;
+          if constexpr (BASIS == BASIS_TRIU) {
+            const int u = kpair[m] >> 4, v = kpair[m] & 15;
+            pk = w.zs[u * ZST + v] - w.zs[v * ZST + u];
+          } else {
+            pk = 0.0f;
+#pragma unroll
+            for (int u = 0; u < 16; ++u) pk = fmaf((float)tab.sgn[k][u], w.zs[u * ZST + tab.col[k][u]], pk);
+          }
+          a.dgens[e * K + k] = pk * hdt;
+          ddt = fmaf(pk, 0.5f * w.gs[k], ddt);
         }
-        a.dgens[e * K + k] = pk * hdt;
-        ddt = fmaf(pk, 0.5f * w.g[k], ddt);
       }
       ddt = warp_sum(ddt);
       if (lane == 0) {
@@ -490,23 +689,18 @@ __global__ void __launch_bounds__(128) bwd_apply16(ScanArgs a) {
         a.ddt_part[e] = ddt;
       }
     }
-    __syncwarp();
-    // H <- M^T G M (one-sided M^T G)
-    prod_nn(w.Mt, w.A, o, lane);
-    __syncwarp();
+    // ---- H <- M^T G M  |  M^T G
     if constexpr (TWO) {
-      put(w.V, o, lane);
-      __syncwarp();
-      prod_nn(w.V, w.M, o, lane);
-      __syncwarp();
+      F16 W;
+      nt(W, Mts, Gs);  // M^T G^T
+      F16S Ws;
+      split(Ws, W);
+      nt(H, Mts, Ws);  // M^T G M
+    } else {
+      nt(H, Mts, Gts);  // M^T G
     }
-    put(w.A, o, lane);
-    __syncwarp();
   }
-  if (j == 0 && a.dh0) {
-#pragma unroll
-    for (int q = 0; q < 8; ++q) a.dh0[s * DD + ent(lane, q)] = w.A[ent(lane, q)];
-  }
+  if (w.j == 0 && a.dh0) f_store<false>(a.dh0 + w.s * DD, H, lane);
 }
 
 unsigned nblk(int64_t warps) { return (unsigned)((warps + WARPS - 1) / WARPS); }
@@ -520,14 +714,14 @@ int run16(const ScanArgs& a, bool bwd, cudaStream_t st) {
     if (!bwd) {
       {
         KernelTimer kt("agg_fwd_reduce", st);
-        fwd_reduce16<SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(a);
+        fwd16_kernel<true, SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(a);
       }
       KernelTimer kt("agg_compose", st);
       compose_kernel<16, TWO, false><<<nblk(S), 128, 0, st>>>(a);
     } else {
       {
         KernelTimer kt("agg_bwd_reduce", st);
-        bwd_reduce16<SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(a);
+        bwd16_reduce_kernel<SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(a);
       }
       KernelTimer kt("agg_compose", st);
       compose_kernel<16, TWO, true><<<nblk(S), 128, 0, st>>>(a);
@@ -539,26 +733,26 @@ int run16(const ScanArgs& a, bool bwd, cudaStream_t st) {
     if (a.nchunks > 1) {
       if (a.agg_mode != 2) {
         KernelTimer kt("fwd_reduce", st);
-        fwd_reduce16<SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(a);
+        fwd16_kernel<true, SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(a);
       }
       KernelTimer kt("fwd_carry", st);
       launch_grouped_carry<16, TWO, false>(a, st);
     }
     KernelTimer kt("fwd_apply", st);
-    fwd_apply16<SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(a);
+    fwd16_kernel<false, SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(a);
     return check_launch("scan forward (D=16)");
   }
   if (total > 0) {
     if (a.nchunks > 1) {
       if (a.agg_mode != 2) {
         KernelTimer kt("bwd_reduce", st);
-        bwd_reduce16<SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(a);
+        bwd16_reduce_kernel<SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(a);
       }
       KernelTimer kt("bwd_carry", st);
       launch_grouped_carry<16, TWO, true>(a, st);
     }
     KernelTimer kt("bwd_apply", st);
-    bwd_apply16<SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(a);
+    bwd16_apply_kernel<SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(a);
   }
   if (SRC == SRC_ROTOR && a.B * a.T > 0) {
     const int64_t BT = a.B * a.T;

@@ -159,6 +159,35 @@ def test_fused_rotor_scan_matches_oracle(ops, oracle, D, basis, damped, two):
         assert rel(tgam.grad, dgam) < BWD_TOL
 
 
+@pytest.mark.parametrize("basis", ["triu", "ga"])
+@pytest.mark.parametrize("damped", [True, False], ids=["damped", "undamped"])
+@pytest.mark.parametrize("two", [True, False], ids=["two", "one"])
+def test_d16_series_and_elimination_inverse_paths(ops, oracle, basis, damped, two):
+    """D = 16 Cayley inverse: steps with |h Omega|_F <= 0.1 take the matrix series, larger
+    ones Gauss-Jordan.  Generator scales alternate per step (0.02 / 4), so both paths run
+    inside every chunk of the forward and backward passes."""
+    rng = np.random.default_rng(11 + 2 * (basis == "ga") + 4 * damped + 8 * two)
+    B, T, N = 1, 96, 2
+    E, gens, dt, gamma, S = _rotor_case(rng, B, T, N, 16, basis, damped, gscale=1.0)
+    gens = gens * np.where(np.arange(T) % 3 == 0, 4.0, 0.02)[None, :, None, None]
+    h = 0.5 * dt[0]
+    fro = [np.linalg.norm(h[t] * np.einsum("k,kij->ij", gens[0, t, 0], E)) for t in range(T)]
+    assert min(fro) < 0.05 and max(fro) > 0.5  # both sides of the 0.1 switch
+    W = rng.standard_normal((B, T, N, 16, 16))
+    Xr = oracle.rotor_scan_fwd(gens, dt, gamma, S, E, two_sided=two)
+    dg, ddt, dgam, dS, _ = oracle.rotor_scan_bwd(gens, dt, gamma, S, E, Xr, W, two_sided=two)
+    tg, tdt, tS = cuda(gens, True), cuda(dt, True), cuda(S, True)
+    tgam = cuda(gamma, True) if damped else None
+    X = ops.fused_rotor_scan(tg, tdt, tgam, tS, basis=basis, two_sided=two)
+    assert rel(X, Xr) < FWD_TOL
+    (X * cuda(W)).sum().backward()
+    assert rel(tS.grad, dS) < BWD_TOL
+    assert rel(tg.grad, dg) < BWD_TOL
+    assert rel(tdt.grad, ddt) < BWD_TOL
+    if damped:
+        assert rel(tgam.grad, dgam) < BWD_TOL
+
+
 def test_fused_matches_materialised_transitions(ops, oracle):
     """The fused kernel equals Cayley + decay + plain scan run separately."""
     rng = np.random.default_rng(7)

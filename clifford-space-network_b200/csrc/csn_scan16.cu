@@ -15,7 +15,7 @@
 // Transposes are products with the identity.  Products run as 3xTF32: each fp32 operand
 // is split into a TF32 head and a TF32 tail and hi*hi + hi*lo + lo*hi is accumulated in
 // fp32, which keeps fp32-level accuracy.  The Cayley inverse (I - Omega)^{-1} is a short
-// matrix series when |h Omega|_F <= 0.1 (four more products, accurate to 1e-8) and
+// matrix series when |h Omega|_F <= 0.1 (three or four products, accurate to 2e-8) and
 // otherwise a Gauss-Jordan elimination on the fragment, whose pivot rows and columns
 // reach the lanes that need them by shuffles; either way the step stays in registers.
 #include <stdint.h>
@@ -45,20 +45,17 @@ struct F16S {      // 3xTF32 operand: head and tail of every element
 __device__ __forceinline__ int frow(int lane, int e) { return (lane >> 2) + 8 * (e >> 1); }
 __device__ __forceinline__ int fcol(int lane, int nt, int e) { return 8 * nt + 2 * (lane & 3) + (e & 1); }
 
-__device__ __forceinline__ uint32_t to_tf32(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return r;
-}
-
+// Head = x rounded to TF32 (nearest, ties away from zero: add half a TF32 unit to the
+// magnitude bits and clear the 13 bits below the TF32 mantissa); tail = x - head, which
+// is exact in fp32 and is read by the MMA at TF32 precision.
 __device__ __forceinline__ void split(F16S& o, const F16& x) {
 #pragma unroll
   for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const uint32_t h = to_tf32(x.v[nt][e]);
+      const uint32_t h = (__float_as_uint(x.v[nt][e]) + 0x1000u) & 0xffffe000u;
       o.hi[nt][e] = h;
-      o.lo[nt][e] = to_tf32(x.v[nt][e] - __uint_as_float(h));
+      o.lo[nt][e] = __float_as_uint(x.v[nt][e] - __uint_as_float(h));
     }
 }
 
@@ -275,16 +272,18 @@ __device__ __forceinline__ void build_Om(F16& Om, const float* gs, const uint32_
     }
 }
 
-// |Om|_F^2 at or below this takes the series inverse (|Om|_2 <= |Om|_F <= 0.1).
+// |Om|_F^2 at or below these takes a series inverse (|Om|_2 <= |Om|_F <= 0.1 or 0.05).
 constexpr float kSeriesFro2 = 0.01f;
+constexpr float kShortSeriesFro2 = 0.0025f;
 
 // M = sa (2 (I - Om)^{-1} - I), in place on Om.
 // (I - Om)^{-1} = (I + Om) (I - W)^{-1} with W = Om^2 (Om skew, so W is symmetric and
-// |W|_2 <= |Om|_F^2).  For |Om|_F <= 0.1 the inverse is the series
-//   (I + Om) (I + W) (I + W^2)          (truncation sum_{k>=4} W^k <= 1.01e-8)
-// -- four products whose operands are symmetric or skew, so each is a plain A B^T with
-// no transposes; larger Om takes the Gauss-Jordan elimination.  The choice is uniform
-// across the warp (one matrix per warp).
+// |W|_2 <= |Om|_F^2 = eps^2), and (I - W)^{-1} = sum_k W^k:
+//   eps <= 0.05:  (I + Om) (I + W + W^2)       truncation <= eps^6 / (1 - eps^2) <= 1.6e-8
+//   eps <= 0.1:   (I + Om) (I + W) (I + W^2)   truncation <= eps^8 / (1 - eps^2) <= 1.01e-8
+// -- three or four products whose operands are symmetric or skew, so each is a plain
+// A B^T with no transposes; larger Om takes the Gauss-Jordan elimination.  The choice is
+// uniform across the warp (one matrix per warp).
 __device__ __forceinline__ void cayley(F16& M, float sa, int lane) {
   const float fro2 = warp_sum(f_dot(M, M));
   if (fro2 <= kSeriesFro2) {
@@ -292,29 +291,40 @@ __device__ __forceinline__ void cayley(F16& M, float sa, int lane) {
     split(Os, M);
     F16 W;
     nt(W, Os, Os);  // Om Om^T = -Om^2
-    F16 P, U;       // I + W = I - Om Om^T ;  I + Om
+    F16 U;          // I + Om
 #pragma unroll
     for (int n2 = 0; n2 < 2; ++n2)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float id = (frow(lane, e) == fcol(lane, n2, e)) ? 1.0f : 0.0f;
         W.v[n2][e] = -W.v[n2][e];
-        P.v[n2][e] = id + W.v[n2][e];
-        U.v[n2][e] = id + M.v[n2][e];
+        U.v[n2][e] = ((frow(lane, e) == fcol(lane, n2, e)) ? 1.0f : 0.0f) + M.v[n2][e];
       }
     F16S Ws;
     split(Ws, W);
     F16 Q;
     nt(Q, Ws, Ws);  // W W^T = W^2
+    F16 E;          // symmetric
+    if (fro2 <= kShortSeriesFro2) {
 #pragma unroll
-    for (int n2 = 0; n2 < 2; ++n2)
+      for (int n2 = 0; n2 < 2; ++n2)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) Q.v[n2][e] += (frow(lane, e) == fcol(lane, n2, e)) ? 1.0f : 0.0f;
-    F16S Ps, Qs;
-    split(Ps, P);
-    split(Qs, Q);
-    F16 E;
-    nt(E, Ps, Qs);  // (I + W) (I + W^2), symmetric
+        for (int e = 0; e < 4; ++e)
+          E.v[n2][e] = ((frow(lane, e) == fcol(lane, n2, e)) ? 1.0f : 0.0f) + W.v[n2][e] + Q.v[n2][e];
+    } else {
+      F16 P;
+#pragma unroll
+      for (int n2 = 0; n2 < 2; ++n2)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float id = (frow(lane, e) == fcol(lane, n2, e)) ? 1.0f : 0.0f;
+          P.v[n2][e] = id + W.v[n2][e];
+          Q.v[n2][e] += id;
+        }
+      F16S Ps, Qs;
+      split(Ps, P);
+      split(Qs, Q);
+      nt(E, Ps, Qs);  // (I + W) (I + W^2)
+    }
     F16S Us, Es;
     split(Us, U);
     split(Es, E);
@@ -540,7 +550,7 @@ __global__ void __launch_bounds__(128) bwd16_reduce_kernel(ScanArgs a) {
 //          dg_k = <dOmega, E_k> dt / 2
 //   H <- M^T G M  (one-sided: M^T G)
 template <int SRC, int BASIS, bool DAMPED, bool TWO>
-__global__ void __launch_bounds__(128) bwd16_apply_kernel(ScanArgs a) {
+__global__ void __launch_bounds__(128, 3) bwd16_apply_kernel(ScanArgs a) {
   constexpr int K = GenCount<16, BASIS>::K;
   constexpr int KR = (K + 31) / 32;
   S16_PROLOGUE(BASIS, K);
@@ -605,8 +615,11 @@ __global__ void __launch_bounds__(128) bwd16_apply_kernel(ScanArgs a) {
         F16S GMs;
         split(GMs, GM);
         nt(dM, GMs, Xps);  // G M Xp^T
-        F16 Xpt;
-        transpose(Xpt, Xps, lane);
+        F16 Xpt;  // X_{t-1}^T straight from memory (the rows were just loaded: L1 hits)
+#pragma unroll
+        for (int n2 = 0; n2 < 2; ++n2)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) Xpt.v[n2][q] = __ldg(xprev + fcol(lane, n2, q) * 16 + frow(lane, q));
         F16S Xpts;
         split(Xpts, Xpt);
         F16 XM;

@@ -163,16 +163,20 @@ def test_fused_rotor_scan_matches_oracle(ops, oracle, D, basis, damped, two):
 @pytest.mark.parametrize("damped", [True, False], ids=["damped", "undamped"])
 @pytest.mark.parametrize("two", [True, False], ids=["two", "one"])
 def test_d16_series_and_elimination_inverse_paths(ops, oracle, basis, damped, two):
-    """D = 16 Cayley inverse: steps with |h Omega|_F <= 0.1 take the matrix series, larger
-    ones Gauss-Jordan.  Generator scales alternate per step (0.02 / 4), so both paths run
-    inside every chunk of the forward and backward passes."""
+    """D = 16 Cayley inverse: |h Omega|_F <= 0.05 takes the short matrix series, <= 0.1 the
+    long one, larger Gauss-Jordan.  Every (step, channel) generator is scaled to a target
+    norm cycling through 0.02 / 0.07 / 2.0, so all three paths run inside every chunk of
+    the forward and backward passes."""
     rng = np.random.default_rng(11 + 2 * (basis == "ga") + 4 * damped + 8 * two)
     B, T, N = 1, 96, 2
     E, gens, dt, gamma, S = _rotor_case(rng, B, T, N, 16, basis, damped, gscale=1.0)
-    gens = gens * np.where(np.arange(T) % 3 == 0, 4.0, 0.02)[None, :, None, None]
-    h = 0.5 * dt[0]
-    fro = [np.linalg.norm(h[t] * np.einsum("k,kij->ij", gens[0, t, 0], E)) for t in range(T)]
-    assert min(fro) < 0.05 and max(fro) > 0.5  # both sides of the 0.1 switch
+    fro = lambda t, n: np.linalg.norm(0.5 * dt[0, t] * np.einsum("k,kij->ij", gens[0, t, n], E))
+    target = np.array([0.02, 0.07, 2.0])
+    for t in range(T):
+        for n in range(N):
+            gens[0, t, n] *= target[(t + n) % 3] / fro(t, n)
+    got = np.array([[fro(t, n) for n in range(N)] for t in range(T)])
+    assert np.allclose(got, target[(np.arange(T)[:, None] + np.arange(N)[None, :]) % 3], rtol=1e-6)
     W = rng.standard_normal((B, T, N, 16, 16))
     Xr = oracle.rotor_scan_fwd(gens, dt, gamma, S, E, two_sided=two)
     dg, ddt, dgam, dS, _ = oracle.rotor_scan_bwd(gens, dt, gamma, S, E, Xr, W, two_sided=two)

@@ -132,6 +132,61 @@ def _time_cpu(one, reps, warmup):
 
 
 # =============================================================================== workloads
+class E2EPipeline:
+    """End-to-end step through the public op API, pipelined over pieces of the step.
+
+    Each piece (a layer and/or a slice of the batch) is copied host -> device on one
+    stream, run forward + backward on a second, and its outputs copied device -> host on
+    a third, so the PCIe transfers of neighbouring pieces (full duplex) overlap each other
+    and the compute.  Device input buffers form a ring of `depth` slots; a slot is
+    refilled only after the compute that read it has finished.  The op's output tensors
+    stay referenced until the step's copies have reached the host (one synchronize per
+    step: the step's results are then on the host), so no block is handed across
+    streams to the caching allocator."""
+
+    def __init__(self, pieces, run, dev, depth=2):
+        import torch
+        self.pieces, self.run, self.dev = pieces, run, dev
+        self.s_in, self.s_comp, self.s_out = (torch.cuda.Stream(dev) for _ in range(3))
+        shapes = pieces[0][0]
+        self.ring = [{k: torch.empty_like(v, device=dev) for k, v in shapes.items()} for _ in range(depth)]
+        self.ready = [torch.cuda.Event() for _ in range(depth)]
+        self.done = [torch.cuda.Event() for _ in range(depth)]
+        for ev in self.done:
+            ev.record(torch.cuda.current_stream(dev))
+
+    def step(self):
+        import torch
+        keep = []
+        for i, (hin, hout) in enumerate(self.pieces):
+            slot = i % len(self.ring)
+            buf = self.ring[slot]
+            with torch.cuda.stream(self.s_in):
+                self.s_in.wait_event(self.done[slot])
+                for k, v in hin.items():
+                    buf[k].copy_(v, non_blocking=True)
+                self.ready[slot].record(self.s_in)
+            with torch.cuda.stream(self.s_comp):
+                self.s_comp.wait_event(self.ready[slot])
+                outs = self.run(buf)
+                self.done[slot].record(self.s_comp)
+            with torch.cuda.stream(self.s_out):
+                self.s_out.wait_event(self.done[slot])
+                for k, v in outs.items():
+                    hout[k].copy_(v, non_blocking=True)
+            keep.append(outs)
+        self.s_out.synchronize()
+        del keep
+
+
+def _batch_pieces(host_in, host_out, nslice):
+    """Split pinned host dicts along the batch (outermost) axis into `nslice` pieces."""
+    B = next(iter(host_in.values())).shape[0]
+    step = B // nslice
+    sl = lambda d, j: {k: v[j * step:(j + 1) * step] for k, v in d.items()}
+    return [(sl(host_in, j), sl(host_out, j)) for j in range(nslice)]
+
+
 class Cl6LM:
     """4 layers of the Cl(6,0) LM scan section, forward + backward."""
     name = "cl6_lm_scan_fwd_bwd"
@@ -197,21 +252,20 @@ class Cl6LM:
                      for O in self.outs]
         h2d = sum(v.numel() * v.element_size() for Lh in self.host for v in Lh.values())
         d2h = sum(v.numel() * v.element_size() for Ho in self.hout for v in Ho.values())
+        pieces = [pc for Lh, Ho in zip(self.host, self.hout) for pc in _batch_pieces(Lh, Ho, 2)]
+        self.pipe = E2EPipeline(pieces, self.e2e_run, self.dev)
         return h2d, d2h
 
-    def e2e_step(self):
+    @staticmethod
+    def e2e_run(d):
         from csn_b200 import ops
-        for Lh, Ho in zip(self.host, self.hout):
-            gens = Lh["gens"].to(self.dev, non_blocking=True).requires_grad_(True)
-            dt = Lh["dt"].to(self.dev, non_blocking=True).requires_grad_(True)
-            gamma = Lh["gamma"].to(self.dev, non_blocking=True).requires_grad_(True)
-            S = Lh["S"].to(self.dev, non_blocking=True).requires_grad_(True)
-            dX = Lh["dX"].to(self.dev, non_blocking=True)
-            X = ops.fused_rotor_scan(gens, dt, gamma, S)
-            X.backward(dX)
-            for k, src in (("X", X.detach()), ("dgens", gens.grad), ("ddt", dt.grad),
-                           ("dgamma", gamma.grad), ("dS", S.grad)):
-                Ho[k].copy_(src, non_blocking=True)
+        gens, dt, gamma, S = (d[k].detach().requires_grad_(True) for k in ("gens", "dt", "gamma", "S"))
+        X = ops.fused_rotor_scan(gens, dt, gamma, S)
+        X.backward(d["dX"])
+        return dict(X=X.detach(), dgens=gens.grad, ddt=dt.grad, dgamma=gamma.grad, dS=S.grad)
+
+    def e2e_step(self):
+        self.pipe.step()
 
     def cpu_reference(self, reps, warmup, sample_batch=8):
         import numpy as np
@@ -290,20 +344,20 @@ class Cl3:
         import torch
         self.host = {k: v.cpu().pin_memory() for k, v in self.inp.items()}
         self.hout = {k: torch.empty_like(v, device="cpu").pin_memory() for k, v in self.out.items()}
+        self.pipe = E2EPipeline(_batch_pieces(self.host, self.hout, 8), self.e2e_run, self.dev)
         return (sum(v.numel() * v.element_size() for v in self.host.values()),
                 sum(v.numel() * v.element_size() for v in self.hout.values()))
 
-    def e2e_step(self):
+    @staticmethod
+    def e2e_run(d):
         from csn_b200 import ops
-        H = self.host
-        gens = H["gens"].to(self.dev, non_blocking=True).requires_grad_(True)
-        dt = H["dt"].to(self.dev, non_blocking=True).requires_grad_(True)
-        x = H["x"].to(self.dev, non_blocking=True).requires_grad_(True)
-        dh = H["dh"].to(self.dev, non_blocking=True)
+        gens, dt, x = (d[k].detach().requires_grad_(True) for k in ("gens", "dt", "x"))
         h = ops.ga3_rotor_scan(gens, dt, x)
-        h.backward(dh)
-        for k, src in (("h", h.detach()), ("dx", x.grad), ("dgens", gens.grad), ("ddt", dt.grad)):
-            self.hout[k].copy_(src, non_blocking=True)
+        h.backward(d["dh"])
+        return dict(h=h.detach(), dx=x.grad, dgens=gens.grad, ddt=dt.grad)
+
+    def e2e_step(self):
+        self.pipe.step()
 
     def cpu_reference(self, reps, warmup, sample_batch=4):
         from oracle import oracle as orc
@@ -375,20 +429,20 @@ class Cl8:
         import torch
         self.host = {k: v.cpu().pin_memory() for k, v in self.inp.items()}
         self.hout = {k: torch.empty_like(v, device="cpu").pin_memory() for k, v in self.out.items()}
+        self.pipe = E2EPipeline(_batch_pieces(self.host, self.hout, 4), self.e2e_run, self.dev)
         return (sum(v.numel() * v.element_size() for v in self.host.values()),
                 sum(v.numel() * v.element_size() for v in self.hout.values()))
 
-    def e2e_step(self):
+    @staticmethod
+    def e2e_run(d):
         from csn_b200 import ops
-        H = self.host
-        gens = H["gens"].to(self.dev, non_blocking=True).requires_grad_(True)
-        dt = H["dt"].to(self.dev, non_blocking=True).requires_grad_(True)
-        S = H["S"].to(self.dev, non_blocking=True).requires_grad_(True)
-        dX = H["dX"].to(self.dev, non_blocking=True)
+        gens, dt, S = (d[k].detach().requires_grad_(True) for k in ("gens", "dt", "S"))
         X = ops.fused_rotor_scan(gens, dt, None, S, basis="ga")
-        X.backward(dX)
-        for k, src in (("X", X.detach()), ("dS", S.grad), ("dgens", gens.grad), ("ddt", dt.grad)):
-            self.hout[k].copy_(src, non_blocking=True)
+        X.backward(d["dX"])
+        return dict(X=X.detach(), dS=S.grad, dgens=gens.grad, ddt=dt.grad)
+
+    def e2e_step(self):
+        self.pipe.step()
 
     def cpu_reference(self, reps, warmup, sample_batch=1):
         import numpy as np
@@ -764,7 +818,8 @@ def main():
         e2e = {"value": wl.elems_per_step * ws * args.e2e_steps / el / 1e9, "unit": UNIT,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "timing": "wall clock around K steps (pinned host -> device, op forward + backward, "
-                         "device -> pinned host) ending in a stream synchronize, max over ranks"}
+                         "device -> pinned host, pipelined over pieces on three streams) ending in "
+                         "a stream synchronize, max over ranks"}
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:

@@ -62,17 +62,24 @@ def _workspace(nbytes, device):
 
 
 # --------------------------------------------------------------------- plain scan
-def _scan_fwd(M, C, h0, two_sided):
+SCAN_TWO_SIDED, SCAN_REVERSE = 1, 2  # csn_scan_* flags
+
+
+def _scan_flags(two_sided, reverse=False):
+    return (SCAN_TWO_SIDED if two_sided else 0) | (SCAN_REVERSE if reverse else 0)
+
+
+def _scan_fwd(M, C, h0, two_sided, reverse=False):
     B, T, N, D, _ = M.shape
     X = torch.empty_like(C)
     ws_bytes = _lib.load().csn_scan_workspace_bytes(B, T, N, D)
     ws = _workspace(ws_bytes, M.device)
-    _lib.call("csn_scan_fwd", _ptr(M), _ptr(C), _ptr(h0), _ptr(X), B, T, N, D, int(two_sided),
-              _ptr(ws), ws_bytes, _stream(M.device))
+    _lib.call("csn_scan_fwd", _ptr(M), _ptr(C), _ptr(h0), _ptr(X), B, T, N, D,
+              _scan_flags(two_sided, reverse), _ptr(ws), ws_bytes, _stream(M.device))
     return X
 
 
-def _scan_bwd(M, X, dX, h0, two_sided, need_dh0):
+def _scan_bwd(M, X, dX, h0, two_sided, need_dh0, reverse=False):
     B, T, N, D, _ = M.shape
     dM = torch.empty_like(M)
     dC = torch.empty_like(M)
@@ -80,18 +87,18 @@ def _scan_bwd(M, X, dX, h0, two_sided, need_dh0):
     ws_bytes = _lib.load().csn_scan_workspace_bytes(B, T, N, D)
     ws = _workspace(ws_bytes, M.device)
     _lib.call("csn_scan_bwd", _ptr(M), _ptr(X), _ptr(dX), _ptr(h0), _ptr(dM), _ptr(dC), _ptr(dh0),
-              B, T, N, D, int(two_sided), _ptr(ws), ws_bytes, _stream(M.device))
+              B, T, N, D, _scan_flags(two_sided, reverse), _ptr(ws), ws_bytes, _stream(M.device))
     return dM, dC, dh0
 
 
 class ScanFunction(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, M, C, h0, two_sided):
+    def forward(ctx, M, C, h0, two_sided, reverse=False):
         _require_cuda(M, C, h0)
         Mf, Cf, hf = _f32(M), _f32(C), _f32(h0)
-        X = _scan_fwd(Mf, Cf, hf, two_sided)
+        X = _scan_fwd(Mf, Cf, hf, two_sided, reverse)
         ctx.save_for_backward(Mf, X, hf)
-        ctx.two_sided = two_sided
+        ctx.two_sided, ctx.reverse = two_sided, reverse
         ctx.dtypes = (M.dtype, C.dtype, None if h0 is None else h0.dtype)
         return X.to(C.dtype)
 
@@ -99,38 +106,61 @@ class ScanFunction(torch.autograd.Function):
     def backward(ctx, dX):
         Mf, X, hf = ctx.saved_tensors
         need_dh0 = len(ctx.needs_input_grad) > 2 and ctx.needs_input_grad[2]
-        dM, dC, dh0 = _scan_bwd(Mf, X, _f32(dX), hf, ctx.two_sided, need_dh0)
+        dM, dC, dh0 = _scan_bwd(Mf, X, _f32(dX), hf, ctx.two_sided, need_dh0, ctx.reverse)
         dM = dM.to(ctx.dtypes[0])
         dC = dC.to(ctx.dtypes[1])
         if dh0 is not None:
             dh0 = dh0.to(ctx.dtypes[2])
-        return dM, dC, dh0, None
+        return dM, dC, dh0, None, None
 
 
-def rotor_scan(M, C, two_sided: bool = True, h0=None):
+def rotor_scan(M, C, two_sided: bool = True, h0=None, reverse: bool = False):
     """Inclusive scan X_t = M_t X_{t-1} M_t^T + C_t (two-sided) or M_t X_{t-1} + C_t.
 
     M, C: [B, T, N, D, D] with D in {4, 8, 16}; h0: optional [B, N, D, D] (X_{-1}).
+    reverse=True scans from t = T-1 down to 0 (X_t = M_t X_{t+1} (M_t^T) + C_t, h0 = X_T):
+    the flipped scan, without flipping any tensor.
     """
     if M.dim() != 5 or C.shape != M.shape or M.shape[-1] != M.shape[-2]:
         raise ValueError(f"rotor_scan expects M, C of shape [B, T, N, D, D], got {tuple(M.shape)}, "
                          f"{tuple(C.shape)}")
-    return ScanFunction.apply(M, C, h0, bool(two_sided))
+    return ScanFunction.apply(M, C, h0, bool(two_sided), bool(reverse))
 
 
 # ---------------------------------------------------------------- fused rotor scan
+def _rotor_fwd(g, d, ga, s, hf, basis, two_sided):
+    """Raw fused forward on float32 contiguous CUDA tensors -> X."""
+    B, T, N, D, _ = s.shape
+    X = torch.empty_like(s)
+    ws_bytes = _lib.load().csn_rotor_scan_workspace_bytes(B, T, N, D)
+    ws = _workspace(ws_bytes, s.device)
+    _lib.call("csn_rotor_scan_fwd", _ptr(g), _ptr(d), _ptr(ga), _ptr(s), _ptr(hf), _ptr(X),
+              B, T, N, D, basis, int(two_sided), _ptr(ws), ws_bytes, _stream(s.device))
+    return X
+
+
+def _rotor_bwd(g, d, ga, s, hf, X, dXf, basis, two_sided, need_dh0):
+    """Raw fused adjoint -> (dgens, ddt, dgamma or None, dS, dh0 or None)."""
+    B, T, N, D, _ = s.shape
+    dg = torch.empty_like(g)
+    ddt = torch.empty_like(d)
+    dga = torch.empty_like(ga) if ga is not None else None
+    dS = torch.empty_like(s)
+    dh0 = torch.empty_like(hf) if (hf is not None and need_dh0) else None
+    ws_bytes = _lib.load().csn_rotor_scan_workspace_bytes(B, T, N, D)
+    ws = _workspace(ws_bytes, s.device)
+    _lib.call("csn_rotor_scan_bwd", _ptr(g), _ptr(d), _ptr(ga), _ptr(s), _ptr(hf), _ptr(X),
+              _ptr(dXf), _ptr(dg), _ptr(ddt), _ptr(dga), _ptr(dS), _ptr(dh0), B, T, N, D,
+              basis, int(two_sided), _ptr(ws), ws_bytes, _stream(s.device))
+    return dg, ddt, dga, dS, dh0
+
+
 class RotorScanFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, gens, dt, gamma, S, h0, basis, two_sided):
         _require_cuda(gens, dt, gamma, S, h0)
         g, d, ga, s, hf = _f32(gens), _f32(dt), _f32(gamma), _f32(S), _f32(h0)
-        B, T, N, D, _ = s.shape
-        X = torch.empty_like(s)
-        lib = _lib.load()
-        ws_bytes = lib.csn_rotor_scan_workspace_bytes(B, T, N, D)
-        ws = _workspace(ws_bytes, s.device)
-        _lib.call("csn_rotor_scan_fwd", _ptr(g), _ptr(d), _ptr(ga), _ptr(s), _ptr(hf), _ptr(X),
-                  B, T, N, D, basis, int(two_sided), _ptr(ws), ws_bytes, _stream(s.device))
+        X = _rotor_fwd(g, d, ga, s, hf, basis, two_sided)
         ctx.save_for_backward(g, d, ga, s, hf, X)
         ctx.basis, ctx.two_sided = basis, two_sided
         ctx.dtypes = tuple(None if t is None else t.dtype for t in (gens, dt, gamma, S, h0))
@@ -139,20 +169,7 @@ class RotorScanFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dX):
         g, d, ga, s, hf, X = ctx.saved_tensors
-        B, T, N, D, _ = s.shape
-        dXf = _f32(dX)
-        dg = torch.empty_like(g)
-        ddt = torch.empty_like(d)
-        dga = torch.empty_like(ga) if ga is not None else None
-        dS = torch.empty_like(s)
-        dh0 = torch.empty_like(hf) if (hf is not None and ctx.needs_input_grad[4]) else None
-        lib = _lib.load()
-        ws_bytes = lib.csn_rotor_scan_workspace_bytes(B, T, N, D)
-        ws = _workspace(ws_bytes, s.device)
-        _lib.call("csn_rotor_scan_bwd", _ptr(g), _ptr(d), _ptr(ga), _ptr(s), _ptr(hf), _ptr(X),
-                  _ptr(dXf), _ptr(dg), _ptr(ddt), _ptr(dga), _ptr(dS), _ptr(dh0), B, T, N, D,
-                  ctx.basis, int(ctx.two_sided), _ptr(ws), ws_bytes, _stream(s.device))
-        outs = [dg, ddt, dga, dS, dh0]
+        outs = _rotor_bwd(g, d, ga, s, hf, X, _f32(dX), ctx.basis, ctx.two_sided, ctx.needs_input_grad[4])
         outs = [None if o is None else o.to(dt_) for o, dt_ in zip(outs, ctx.dtypes)]
         return outs[0], outs[1], outs[2], outs[3], outs[4], None, None
 
@@ -177,14 +194,25 @@ def fused_rotor_scan(gens, dt, gamma, S, basis: str = "triu", two_sided: bool = 
 
 
 # ------------------------------------------------------------------------ Cayley
+def _cayley_fwd(O):
+    D = O.shape[-1]
+    Q = torch.empty_like(O)
+    _lib.call("csn_cayley_fwd", _ptr(O), _ptr(Q), O.numel() // (D * D), D, _stream(O.device))
+    return Q
+
+
+def _cayley_bwd(Q, dQf):
+    D = Q.shape[-1]
+    dO = torch.empty_like(Q)
+    _lib.call("csn_cayley_bwd", _ptr(Q), _ptr(dQf), _ptr(dO), Q.numel() // (D * D), D, _stream(Q.device))
+    return dO
+
+
 class CayleyFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, Om):
         _require_cuda(Om)
-        O = _f32(Om)
-        D = O.shape[-1]
-        Q = torch.empty_like(O)
-        _lib.call("csn_cayley_fwd", _ptr(O), _ptr(Q), O.numel() // (D * D), D, _stream(O.device))
+        Q = _cayley_fwd(_f32(Om))
         ctx.save_for_backward(Q)
         ctx.dtype = Om.dtype
         return Q.to(Om.dtype)
@@ -192,11 +220,7 @@ class CayleyFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dQ):
         (Q,) = ctx.saved_tensors
-        D = Q.shape[-1]
-        dO = torch.empty_like(Q)
-        _lib.call("csn_cayley_bwd", _ptr(Q), _ptr(_f32(dQ)), _ptr(dO), Q.numel() // (D * D), D,
-                  _stream(Q.device))
-        return dO.to(ctx.dtype)
+        return _cayley_bwd(Q, _f32(dQ)).to(ctx.dtype)
 
 
 def cayley(Omega):
@@ -205,18 +229,35 @@ def cayley(Omega):
 
 
 # ----------------------------------------------------------------- Clifford cell
+def _cell_fwd(xf, pf, wr, wi, gb, dt):
+    Bt, N, A = pf.shape
+    if A != 16:
+        raise ValueError("the Clifford cell works on 16-component (4 x 4) states")
+    nxt = torch.empty_like(pf)
+    _lib.call("csn_cell_fwd", _ptr(pf), _ptr(xf), _ptr(wr), _ptr(wi), _ptr(gb), float(dt),
+              _ptr(nxt), Bt, N, xf.shape[1], _stream(pf.device))
+    return nxt
+
+
+def _cell_bwd(xf, pf, wr, wi, gb, dt, dnf):
+    """-> (dx, dprev, dW_rec, dW_in, dgamma_bias)"""
+    Bt, N, _ = pf.shape
+    dprev, dx = torch.empty_like(pf), torch.empty_like(xf)
+    dwr, dwi, dgb = torch.empty_like(wr), torch.empty_like(wi), torch.empty_like(gb)
+    nbytes = _lib.load().csn_cell_workspace_bytes(Bt, N)
+    ws = _workspace(nbytes, pf.device)
+    _lib.call("csn_cell_bwd", _ptr(pf), _ptr(xf), _ptr(wr), _ptr(wi), _ptr(gb), float(dt),
+              _ptr(dnf), _ptr(dprev), _ptr(dx), _ptr(dwr), _ptr(dwi), _ptr(dgb),
+              Bt, N, xf.shape[1], _ptr(ws), nbytes, _stream(pf.device))
+    return dx, dprev, dwr, dwi, dgb
+
+
 class CellFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, prev, W_rec, W_in, gamma_bias, dt):
         _require_cuda(x, prev, W_rec, W_in, gamma_bias)
         xf, pf, wr, wi, gb = (_f32(t) for t in (x, prev, W_rec, W_in, gamma_bias))
-        Bt, N, A = pf.shape
-        if A != 16:
-            raise ValueError("the Clifford cell works on 16-component (4 x 4) states")
-        in_dim = xf.shape[1]
-        nxt = torch.empty_like(pf)
-        _lib.call("csn_cell_fwd", _ptr(pf), _ptr(xf), _ptr(wr), _ptr(wi), _ptr(gb), float(dt),
-                  _ptr(nxt), Bt, N, in_dim, _stream(pf.device))
+        nxt = _cell_fwd(xf, pf, wr, wi, gb, dt)
         ctx.save_for_backward(xf, pf, wr, wi, gb)
         ctx.dt = float(dt)
         ctx.dtypes = (x.dtype, prev.dtype, W_rec.dtype, W_in.dtype, gamma_bias.dtype)
@@ -225,19 +266,7 @@ class CellFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dnext):
         xf, pf, wr, wi, gb = ctx.saved_tensors
-        Bt, N, _ = pf.shape
-        in_dim = xf.shape[1]
-        dprev = torch.empty_like(pf)
-        dx = torch.empty_like(xf)
-        dwr = torch.empty_like(wr)
-        dwi = torch.empty_like(wi)
-        dgb = torch.empty_like(gb)
-        nbytes = _lib.load().csn_cell_workspace_bytes(Bt, N)
-        ws = _workspace(nbytes, pf.device)
-        _lib.call("csn_cell_bwd", _ptr(pf), _ptr(xf), _ptr(wr), _ptr(wi), _ptr(gb), ctx.dt,
-                  _ptr(_f32(dnext)), _ptr(dprev), _ptr(dx), _ptr(dwr), _ptr(dwi), _ptr(dgb),
-                  Bt, N, in_dim, _ptr(ws), nbytes, _stream(pf.device))
-        outs = [dx, dprev, dwr, dwi, dgb]
+        outs = _cell_bwd(xf, pf, wr, wi, gb, ctx.dt, _f32(dnext))
         outs = [o.to(d) for o, d in zip(outs, ctx.dtypes)]
         return outs[0], outs[1], outs[2], outs[3], outs[4], None
 
@@ -248,17 +277,34 @@ def cell_step(x, prev, W_rec, W_in, gamma_bias, dt: float = 0.02):
 
 
 # ----------------------------------------------------------- Cl(3,0) blade scan
+def _ga3_fwd(g, d, xf, hf):
+    B, T, N, _ = xf.shape
+    h = torch.empty_like(xf)
+    nbytes = _lib.load().csn_ga3_workspace_bytes(B, T, N)
+    ws = _workspace(nbytes, xf.device)
+    _lib.call("csn_ga3_scan_fwd", _ptr(g), _ptr(d), _ptr(xf), _ptr(hf), _ptr(h), B, T, N,
+              _ptr(ws), nbytes, _stream(xf.device))
+    return h
+
+
+def _ga3_bwd(g, d, hf, h, dhf, need_dh0):
+    """-> (dgens, ddt, dx, dh0 or None)"""
+    B, T, N, _ = h.shape
+    dg, ddt, dx = torch.empty_like(g), torch.empty_like(d), torch.empty_like(h)
+    dh0 = torch.empty_like(hf) if (hf is not None and need_dh0) else None
+    nbytes = _lib.load().csn_ga3_workspace_bytes(B, T, N)
+    ws = _workspace(nbytes, h.device)
+    _lib.call("csn_ga3_scan_bwd", _ptr(g), _ptr(d), _ptr(hf), _ptr(h), _ptr(dhf), _ptr(dg),
+              _ptr(ddt), _ptr(dx), _ptr(dh0), B, T, N, _ptr(ws), nbytes, _stream(h.device))
+    return dg, ddt, dx, dh0
+
+
 class Ga3ScanFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, gens, dt, x, h0):
         _require_cuda(gens, dt, x, h0)
         g, d, xf, hf = _f32(gens), _f32(dt), _f32(x), _f32(h0)
-        B, T, N, _ = xf.shape
-        h = torch.empty_like(xf)
-        nbytes = _lib.load().csn_ga3_workspace_bytes(B, T, N)
-        ws = _workspace(nbytes, xf.device)
-        _lib.call("csn_ga3_scan_fwd", _ptr(g), _ptr(d), _ptr(xf), _ptr(hf), _ptr(h), B, T, N,
-                  _ptr(ws), nbytes, _stream(xf.device))
+        h = _ga3_fwd(g, d, xf, hf)
         ctx.save_for_backward(g, d, hf, h)
         ctx.dtypes = tuple(None if t is None else t.dtype for t in (gens, dt, x, h0))
         return h.to(x.dtype)
@@ -266,14 +312,7 @@ class Ga3ScanFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dh):
         g, d, hf, h = ctx.saved_tensors
-        B, T, N, _ = h.shape
-        dg, ddt, dx = torch.empty_like(g), torch.empty_like(d), torch.empty_like(h)
-        dh0 = torch.empty_like(hf) if (hf is not None and ctx.needs_input_grad[3]) else None
-        nbytes = _lib.load().csn_ga3_workspace_bytes(B, T, N)
-        ws = _workspace(nbytes, h.device)
-        _lib.call("csn_ga3_scan_bwd", _ptr(g), _ptr(d), _ptr(hf), _ptr(h), _ptr(_f32(dh)), _ptr(dg),
-                  _ptr(ddt), _ptr(dx), _ptr(dh0), B, T, N, _ptr(ws), nbytes, _stream(h.device))
-        outs = [dg, ddt, dx, dh0]
+        outs = _ga3_bwd(g, d, hf, h, _f32(dh), ctx.needs_input_grad[3])
         return tuple(None if o is None else o.to(t) for o, t in zip(outs, ctx.dtypes))
 
 
@@ -339,3 +378,7 @@ class RotorStepGraph:
     def replay(self):
         self.graph.replay()
         return self.h
+
+
+# torch.ops.csn.* registrations (needs the helpers above; imported last on purpose)
+from . import library  # noqa: E402,F401

@@ -33,7 +33,7 @@ template <int D, int BASIS, bool DAMPED, int K>
 __device__ __forceinline__ void rotor_transition(const ScanArgs& a, int64_t b, int64_t t,
                                                  int64_t e, Mat<D>& M, RotorStep<D, K>& r) {
   load_gens<K>(r.g, a.gens + e * K);
-  r.dt = __ldg(a.dt + b * a.T + t);
+  r.dt = __ldg(a.dt + b * a.T + tphys(a, t));
   build_I_minus_omega<D, BASIS, K>(M, r.g, 0.5f * r.dt);
   gj_inverse(M);  // M = A^{-1}
   if constexpr (DAMPED) {
@@ -483,9 +483,10 @@ extern "C" size_t csn_rotor_scan_workspace_bytes(int64_t B, int64_t T, int64_t N
 }
 
 extern "C" int csn_scan_fwd(const float* M, const float* C, const float* h0, float* X, int64_t B,
-                            int64_t T, int64_t N, int D, int two_sided, void* workspace,
+                            int64_t T, int64_t N, int D, int flags, void* workspace,
                             size_t workspace_bytes, void* stream) {
   if (int rc = check_shape(B, T, N, D)) return rc;
+  if (flags & ~(CSN_SCAN_TWO_SIDED | CSN_SCAN_REVERSE)) return set_error(CSN_ERR_INVALID, "csn_scan_fwd: unknown flags");
   if (B * T * N == 0) return CSN_OK;
   if (!M || !C || !X) return set_error(CSN_ERR_INVALID, "csn_scan_fwd: M, C and X are required");
   if (!aligned16(M) || !aligned16(C) || !aligned16(X) || (h0 && !aligned16(h0)))
@@ -496,16 +497,19 @@ extern "C" int csn_scan_fwd(const float* M, const float* C, const float* h0, flo
   if (int rc = get_ws(ws, workspace, workspace_bytes, plan_bytes(p), st)) return rc;
   ScanArgs a{};
   a.M = M; a.C = C; a.h0 = h0; a.out = X; a.B = B; a.T = T; a.N = N;
+  a.rev = (flags & CSN_SCAN_REVERSE) != 0;
+  const bool two = (flags & CSN_SCAN_TWO_SIDED) != 0;
   bind_ws(a, p, ws.base, D);
-  if (D == 16) return scan16_dispatch(a, SRC_MC, BASIS_TRIU, false, two_sided != 0, false, st);
-  return dispatch(a, D, SRC_MC, BASIS_TRIU, false, two_sided != 0, false, st);
+  if (D == 16) return scan16_dispatch(a, SRC_MC, BASIS_TRIU, false, two, false, st);
+  return dispatch(a, D, SRC_MC, BASIS_TRIU, false, two, false, st);
 }
 
 extern "C" int csn_scan_bwd(const float* M, const float* X, const float* dX, const float* h0,
                             float* dM, float* dC, float* dh0, int64_t B, int64_t T, int64_t N,
-                            int D, int two_sided, void* workspace, size_t workspace_bytes,
+                            int D, int flags, void* workspace, size_t workspace_bytes,
                             void* stream) {
   if (int rc = check_shape(B, T, N, D)) return rc;
+  if (flags & ~(CSN_SCAN_TWO_SIDED | CSN_SCAN_REVERSE)) return set_error(CSN_ERR_INVALID, "csn_scan_bwd: unknown flags");
   if (B * T * N == 0) return CSN_OK;
   if (!M || !X || !dX || !dM || !dC)
     return set_error(CSN_ERR_INVALID, "csn_scan_bwd: M, X, dX, dM and dC are required");
@@ -520,9 +524,11 @@ extern "C" int csn_scan_bwd(const float* M, const float* X, const float* dX, con
   ScanArgs a{};
   a.M = M; a.X = X; a.dX = dX; a.h0 = h0; a.dM = dM; a.dC = dC; a.dh0 = dh0;
   a.B = B; a.T = T; a.N = N;
+  a.rev = (flags & CSN_SCAN_REVERSE) != 0;
+  const bool two = (flags & CSN_SCAN_TWO_SIDED) != 0;
   bind_ws(a, p, ws.base, D);
-  if (D == 16) return scan16_dispatch(a, SRC_MC, BASIS_TRIU, false, two_sided != 0, true, st);
-  return dispatch(a, D, SRC_MC, BASIS_TRIU, false, two_sided != 0, true, st);
+  if (D == 16) return scan16_dispatch(a, SRC_MC, BASIS_TRIU, false, two, true, st);
+  return dispatch(a, D, SRC_MC, BASIS_TRIU, false, two, true, st);
 }
 
 static int rotor_common_checks(const float* gens, const float* dt, const float* S, int64_t B,

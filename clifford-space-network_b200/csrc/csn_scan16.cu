@@ -417,7 +417,7 @@ __device__ __forceinline__ void step_matrix(const ScanArgs& a, const Warp& w, co
     alpha = sa = 1.0f;
     dtv = gam = 0.0f;
   } else {
-    dtv = __ldg(a.dt + w.b * a.T + t);
+    dtv = __ldg(a.dt + w.b * a.T + tphys(a, t));
     if constexpr (DAMPED) {
       gam = __ldg(a.gamma + e);
       alpha = 1.0f / (1.0f + expf(gam * dtv));
@@ -452,14 +452,14 @@ __global__ void __launch_bounds__(128) fwd16_kernel(ScanArgs a) {
     f_zero(X);
   }
   float gr[KR];
-  if (SRC == SRC_ROTOR && w.t0 < w.t1) fetch_gens<K>(gr, a.gens, (w.b * a.T + w.t0) * a.N + w.n, lane);
+  if (SRC == SRC_ROTOR && w.t0 < w.t1) fetch_gens<K>(gr, a.gens, elem(a, w.b, w.t0, w.n), lane);
   for (int64_t t = w.t0; t < w.t1; ++t) {
-    const int64_t e = (w.b * a.T + t) * a.N + w.n;
+    const int64_t e = elem(a, w.b, t, w.n);
     F16 Cin;
     f_load(Cin, (SRC == SRC_MC ? a.C : a.S) + e * DD, lane);
     if constexpr (SRC == SRC_ROTOR) {
       stage_gens<K>(w.gs, gr, lane);
-      if (t + 1 < w.t1) fetch_gens<K>(gr, a.gens, e + a.N, lane);
+      if (t + 1 < w.t1) fetch_gens<K>(gr, a.gens, elem(a, w.b, t + 1, w.n), lane);
     }
     F16 M;
     float alpha, sa, dtv, gam;
@@ -506,14 +506,14 @@ __global__ void __launch_bounds__(128) bwd16_reduce_kernel(ScanArgs a) {
   f_zero(Gc);
   f_identity(P, lane);
   float gr[KR];
-  if (SRC == SRC_ROTOR && w.t0 < w.t1) fetch_gens<K>(gr, a.gens, (w.b * a.T + w.t1 - 1) * a.N + w.n, lane);
+  if (SRC == SRC_ROTOR && w.t0 < w.t1) fetch_gens<K>(gr, a.gens, elem(a, w.b, w.t1 - 1, w.n), lane);
   for (int64_t t = w.t1 - 1; t >= w.t0; --t) {
-    const int64_t e = (w.b * a.T + t) * a.N + w.n;
+    const int64_t e = elem(a, w.b, t, w.n);
     F16 dX;
     f_load(dX, a.dX + e * DD, lane);
     if constexpr (SRC == SRC_ROTOR) {
       stage_gens<K>(w.gs, gr, lane);
-      if (t - 1 >= w.t0) fetch_gens<K>(gr, a.gens, e - a.N, lane);
+      if (t - 1 >= w.t0) fetch_gens<K>(gr, a.gens, elem(a, w.b, t - 1, w.n), lane);
     }
     F16 M;
     float alpha, sa, dtv, gam;
@@ -574,17 +574,17 @@ __global__ void __launch_bounds__(128, 3) bwd16_apply_kernel(ScanArgs a) {
     }
   }
   float gr[KR];
-  if (SRC == SRC_ROTOR && w.t0 < w.t1) fetch_gens<K>(gr, a.gens, (w.b * a.T + w.t1 - 1) * a.N + w.n, lane);
+  if (SRC == SRC_ROTOR && w.t0 < w.t1) fetch_gens<K>(gr, a.gens, elem(a, w.b, w.t1 - 1, w.n), lane);
   for (int64_t t = w.t1 - 1; t >= w.t0; --t) {
-    const int64_t e = (w.b * a.T + t) * a.N + w.n;
+    const int64_t e = elem(a, w.b, t, w.n);
     F16 dX, Xp, Sx;
     f_load(dX, a.dX + e * DD, lane);
-    const float* xprev = (t > 0) ? (a.X + (e - a.N) * DD) : (a.h0 ? a.h0 + w.s * DD : nullptr);
+    const float* xprev = (t > 0) ? (a.X + elem(a, w.b, t - 1, w.n) * DD) : (a.h0 ? a.h0 + w.s * DD : nullptr);
     if (xprev) f_load(Xp, xprev, lane);
     if (SRC == SRC_ROTOR && DAMPED) f_load(Sx, a.S + e * DD, lane);
     if constexpr (SRC == SRC_ROTOR) {
       stage_gens<K>(w.gs, gr, lane);
-      if (t - 1 >= w.t0) fetch_gens<K>(gr, a.gens, e - a.N, lane);
+      if (t - 1 >= w.t0) fetch_gens<K>(gr, a.gens, elem(a, w.b, t - 1, w.n), lane);
     }
     F16 M;
     float alpha, sa, dtv, gam;

@@ -44,10 +44,15 @@ struct ScanArgs {
   int agg_mode;
   float* P_out;  // [B, N, D, D]
   float* c_out;  // [B, N, D, D]
+  int rev;       // plain scan in reverse time (X_t = M_t X_{t+1} (M_t^T) + C_t, X_T = h0)
 };
 
+// Physical time of scan step t: the plain scan can run in reverse time (rev), i.e. scan
+// step t reads and writes time T - 1 - t, so "the previous step" is the next time index.
+__device__ __forceinline__ int64_t tphys(const ScanArgs& a, int64_t t) { return a.rev ? a.T - 1 - t : t; }
+
 __device__ __forceinline__ int64_t elem(const ScanArgs& a, int64_t b, int64_t t, int64_t n) {
-  return (b * a.T + t) * a.N + n;
+  return (b * a.T + tphys(a, t)) * a.N + n;
 }
 
 // ----------------------------------------------------------------- step sources

@@ -55,23 +55,31 @@ const char* csn_last_error(void);
 /* ------------------------------------------------------------------ plain scan */
 size_t csn_scan_workspace_bytes(int64_t B, int64_t T, int64_t N, int D);
 
-/* X_t = M_t X_{t-1} M_t^T + C_t (two_sided != 0) or M_t X_{t-1} + C_t, X_{-1} = h0 or 0.
+/* Plain-scan flags: bit 0 two-sided (X_t = M_t X_{t-1} M_t^T + C_t, else M_t X_{t-1} + C_t),
+ * bit 1 reverse time (the scan runs from t = T-1 down to 0: X_t = M_t X_{t+1} (M_t^T) + C_t,
+ * X_T = h0 or 0) -- the flipped scan of the reference's bidirectional spatial scan
+ * (csn_toolkit/csn/vision.py:97-107) without flipping any tensor.  flags = 0 / 1 are the
+ * former one-sided / two-sided values. */
+#define CSN_SCAN_TWO_SIDED 1
+#define CSN_SCAN_REVERSE 2
+
+/* X_t = M_t X_{t-1} M_t^T + C_t (two-sided) or M_t X_{t-1} + C_t, X_{-1} = h0 or 0.
  * Replaces python/clifford_scan.py:41 parallel_rotor_scan (two-sided default),
  * csn_toolkit/csn/scan.py:24 CliffordScanFunction.forward, and the pybind entry
  * scan_fwd_cuda_d4(M, C) -> X of csn_toolkit/csn/cuda/scan_cuda.cpp:6 ([S,T,4,4] is
- * B = S, N = 1, D = 4, two_sided = 0).  D in {4, 8, 16}. */
+ * B = S, N = 1, D = 4, flags = 0).  D in {4, 8, 16}. */
 int csn_scan_fwd(const float* M, const float* C, const float* h0, float* X,
-                 int64_t B, int64_t T, int64_t N, int D, int two_sided,
+                 int64_t B, int64_t T, int64_t N, int D, int flags,
                  void* workspace, size_t workspace_bytes, void* stream);
 
 /* Reverse-time adjoint of csn_scan_fwd: dM, dC (and dh0 when h0 and dh0 are given).
  * Replaces csn_toolkit/csn/scan.py:44 CliffordScanFunction.backward, autograd through
  * python/clifford_scan.py:41, and scan_bwd_cuda_d4(M, X, grad_X) -> [grad_M, grad_C]
- * of csn_toolkit/csn/cuda/scan_cuda.cpp:7.  dM_0 = 0 when h0 is NULL, as in the
- * reference. */
+ * of csn_toolkit/csn/cuda/scan_cuda.cpp:7.  dM of the first scanned step is 0 when h0 is
+ * NULL, as in the reference.  Same flags as csn_scan_fwd. */
 int csn_scan_bwd(const float* M, const float* X, const float* dX, const float* h0,
                  float* dM, float* dC, float* dh0,
-                 int64_t B, int64_t T, int64_t N, int D, int two_sided,
+                 int64_t B, int64_t T, int64_t N, int D, int flags,
                  void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------ fused rotor scan */

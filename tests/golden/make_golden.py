@@ -19,6 +19,10 @@ functions called (paths relative to the reference root):
 * python/clifford_cl6.py:150-171 the block's scan section, composed from the calls above
 * python/clifford_layer.py:14 CliffordTENNCell
 * python/clifford_cl6.py:71 CliffordCL6Block, python/clifford_cl8.py:92 CliffordCL8Block
+* csn_toolkit/csn/vision.py:56,113 CliffordSpatialRotorBlockCl4 / Cl8 (use_schulz=False)
+
+    python tests/golden/make_golden.py [group ...]     (groups: scans cayley rotor ga3 cells
+                                                        blocks spatial; default: all)
 """
 from __future__ import annotations
 
@@ -42,6 +46,7 @@ from python.clifford_cl8 import cayley_rotor_16x16, cayley_rotor_4x4, CliffordCL
 from python.clifford_layer import CliffordTENNCell  # noqa: E402
 import csn.scan as ref_csn_scan  # noqa: E402
 import csn.rotors as ref_csn_rotors  # noqa: E402
+import csn.vision as ref_csn_vision  # noqa: E402
 
 import importlib.util  # noqa: E402
 
@@ -232,16 +237,46 @@ def blocks(rng):
         save(name, x=x, W=W, out=out, Omega=Omega, dt=dt, dx=x.grad, **sd, **grads)
 
 
-def main():
+def spatial(rng):
+    """2D bidirectional spatial blocks (eval mode: BatchNorm with its running statistics)."""
+    for name, cls, kw, (B, C, H, W) in (
+        ("spatial_cl4", ref_csn_vision.CliffordSpatialRotorBlockCl4, dict(num_neurons=2), (2, 6, 5, 4)),
+        ("spatial_cl8", ref_csn_vision.CliffordSpatialRotorBlockCl8, dict(num_neurons=1), (1, 4, 3, 4)),
+    ):
+        torch.manual_seed(int(rng.integers(1 << 30)))
+        blk = cls(C, use_schulz=False, **kw).double().eval()
+        with torch.no_grad():  # rotations and decays well away from identity / zero
+            blk.biv_proj.weight.mul_(4.0)
+            blk.gamma_log.copy_(t(rng.standard_normal(kw["num_neurons"]) * 0.5))
+        x = t(rng.standard_normal((B, C, H, W))).requires_grad_(True)
+        Wt = t(rng.standard_normal((B, C, H, W)))
+        out = blk(x)
+        (out * Wt).sum().backward()
+        sd = {f"param.{k}": v for k, v in blk.state_dict().items()}
+        grads = {f"grad.{k}": p.grad for k, p in blk.named_parameters()}
+        save(name, x=x, W=Wt, out=out, dx=x.grad, **sd, **grads)
+
+
+GROUPS = {"scans": (scans, 0), "cayley": (cayleys, 0), "rotor": (rotor_scans, 0), "ga3": (ga3, 0),
+          "cells": (cells, 0), "blocks": (blocks, 0), "spatial": (spatial, 1)}
+
+
+def main(names):
     os.environ.setdefault("PYTHONDONTWRITEBYTECODE", "1")
-    rng = np.random.default_rng(20260101)
-    print("scans");  scans(rng)
-    print("cayley"); cayleys(rng)
-    print("rotor");  rotor_scans(rng)
-    print("ga3");    ga3(rng)
-    print("cells");  cells(rng)
-    print("blocks"); blocks(rng)
+    unknown = set(names) - set(GROUPS)
+    if unknown:
+        raise SystemExit(f"unknown groups {sorted(unknown)}; choose from {list(GROUPS)}")
+    # stream-0 groups share one generator in this order (each fixture depends on the draws
+    # before it), so asking for any of them regenerates all of them; later groups draw from
+    # their own streams, so adding one changes no existing fixture
+    if any(GROUPS[n][1] == 0 for n in names):
+        names = set(names) | {n for n, (_, stream) in GROUPS.items() if stream == 0}
+    rng0 = np.random.default_rng(20260101)
+    for name, (fn, stream) in GROUPS.items():
+        if name in names:
+            print(name)
+            fn(rng0 if stream == 0 else np.random.default_rng(20260101 + stream))
 
 
 if __name__ == "__main__":
-    main()
+    main(sys.argv[1:] or list(GROUPS))

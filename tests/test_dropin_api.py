@@ -50,6 +50,19 @@ def test_block_state_dict_matches_reference(golden, name, ctor):
     blk.load_state_dict({k: torch.as_tensor(g["param." + k]) for k in ref_keys})
 
 
+@pytest.mark.parametrize("name,cls,kw", [("spatial_cl4", "CliffordSpatialRotorBlockCl4", dict(num_neurons=2)),
+                                         ("spatial_cl8", "CliffordSpatialRotorBlockCl8", dict(num_neurons=1))])
+def test_spatial_block_state_dict_matches_reference(golden, name, cls, kw):
+    import csn.vision as vision
+    g = golden(name)
+    ref_keys = {k[len("param."):]: tuple(v.shape) for k, v in g.items() if k.startswith("param.")}
+    blk = getattr(vision, cls)(g["x"].shape[1], **kw)
+    assert {k: tuple(v.shape) for k, v in blk.state_dict().items()} == ref_keys
+    blk.load_state_dict({k: torch.as_tensor(g["param." + k]) for k in ref_keys})
+    # csn_toolkit/csn/vision.py:58, :115
+    assert params(type(blk).__init__) == ["self", "in_channels", "num_neurons", "use_schulz"]
+
+
 def test_cell_parameters_match_reference():
     from python.clifford_layer import CliffordTENNCell
     cell = CliffordTENNCell(num_neurons=5, in_dim=4)

@@ -6,8 +6,11 @@
 //    cp.async into a private shared-memory slot of the thread; each slot is refilled
 //    for the next step right after its last read in the current step, so the copy
 //    overlaps (at least) the rest of the step's arithmetic;
-//  * slot strides are = 4 (mod 32) words apart for every 128-bit access pattern used
-//    here, so the 8 lanes of a quarter warp hit 8 different bank groups;
+//  * slot strides are 4 or 28 (mod 32) words, so the 8 lanes of a quarter warp hit 8
+//    different bank groups in every 128-bit access pattern used here (own-slot rows and
+//    the 4-lanes-per-row cooperative copies);
+//  * rows that whole warps move (S, dX, X_{t-1}, X, dS, generators in the apply passes)
+//    are copied cooperatively, 64 contiguous bytes of 8 rows per warp instruction;
 //  * matrices that would not fit in the 255-register budget next to the live state
 //    (the running product P in the reduce passes, M in the backward apply pass) live in
 //    the slot too, and products with them are written as row-broadcast outer products
@@ -52,11 +55,14 @@ __device__ __forceinline__ void sts_row(float* p, const float (&r)[8]) {
 }
 
 // ------------------------------------------------- warp-cooperative row transfers
-// A lane's per-step rows (S, dX, X, dS: 64 floats = 256 B) are contiguous in memory but
-// 256 B away from its neighbours' rows.  Instead of each lane moving its own row 16 B at
-// a time (every warp instruction then touches 32 rows), 16 lanes move one whole row
-// together: instruction v handles rows 2v and 2v+1 of the warp, one contiguous 256 B
-// run per half warp.  The owner's row index comes from a shuffle.
+// A lane's per-step rows (S, dX, X_{t-1}, X, dS: 64 floats = 256 B; generators 28 floats)
+// are contiguous in memory but far from its neighbours' rows.  Instead of each lane moving
+// its own row 16 B at a time (every warp instruction then touches 32 rows), 4 lanes move
+// one row together: one warp instruction copies 64 contiguous bytes of each of 8 rows, and
+// a lane issues RF / 16 such copies per row, for 4 groups of 8 rows.  The owner's row base
+// comes from a shuffle once per row.  Rows p and p + 4 of a group share each 8-lane phase
+// of a 128-bit shared-memory access: with slot strides of 41 or 55 (mod 8) 16-byte units
+// their 4 + 4 vectors fall in 8 different bank groups.
 struct LaneRows {
   int64_t first;  // element index (b*T + t)*N + n of the lane's first step (forward order)
   int len;        // steps in the lane's chunk (0 for lanes past the end of the grid)
@@ -74,23 +80,31 @@ __device__ __forceinline__ int64_t lane_row(int64_t first, int len, int t0, int 
   return first + (int64_t)(k - back) * row_step;
 }
 
-// g -> smem.  RF floats per row (RF/4 16-byte vectors), 16 lanes per row for RF = 64
-// (two rows per instruction), 8 lanes per row for RF = 28 (four rows per instruction).
+// row handled by this lane inside an 8-row group
+__device__ __forceinline__ int coop_row_in_group(int lane) { return ((lane >> 2) & 1) * 4 + (lane >> 3); }
+
+// g -> smem, RF floats per row (RF % 4 == 0).
 template <int RF, bool REVERSE>
 __device__ __forceinline__ void coop_load_rows(float* warp_slots, int stride, int off,
                                                const float* __restrict__ g, const LaneRows& me,
                                                int step, int64_t row_step, int back = 0) {
-  constexpr int RV = RF / 4, LPR = RV > 8 ? 16 : 8, RPI = 32 / LPR;
-  const int lane = threadIdx.x & 31, c = lane % LPR;
+  constexpr int RV = RF / 4, SUB = (RV + 3) / 4;
+  const int lane = threadIdx.x & 31, c = lane & 3, rg = coop_row_in_group(lane);
 #pragma unroll
-  for (int v = 0; v < 32 / RPI; ++v) {
-    const int r = v * RPI + lane / LPR;
+  for (int v = 0; v < 4; ++v) {
+    const int r = 8 * v + rg;
     const int64_t first = __shfl_sync(FULL, me.first, r);
     const int len = __shfl_sync(FULL, me.len, r);
     const int t0 = __shfl_sync(FULL, me.t0, r);
-    if (c < RV && step < len) {
+    if (step < len) {
       const int64_t row = lane_row<REVERSE>(first, len, t0, step, back, row_step);
-      if (row >= 0) cp_async16(warp_slots + r * stride + off + 4 * c, g + row * RF + 4 * c);
+      if (row >= 0) {
+#pragma unroll
+        for (int u = 0; u < SUB; ++u) {
+          const int vec = 4 * u + c;
+          if (vec < RV) cp_async16(warp_slots + r * stride + off + 4 * vec, g + row * RF + 4 * vec);
+        }
+      }
     }
   }
 }
@@ -100,20 +114,26 @@ template <int RF, bool REVERSE>
 __device__ __forceinline__ void coop_store_rows(const float* warp_slots, int stride, int off,
                                                 float* __restrict__ g, const LaneRows& me,
                                                 int step, int64_t row_step, float scale) {
-  constexpr int RV = RF / 4, LPR = RV > 8 ? 16 : 8, RPI = 32 / LPR;
-  const int lane = threadIdx.x & 31, c = lane % LPR;
+  constexpr int RV = RF / 4, SUB = (RV + 3) / 4;
+  const int lane = threadIdx.x & 31, c = lane & 3, rg = coop_row_in_group(lane);
 #pragma unroll
-  for (int v = 0; v < 32 / RPI; ++v) {
-    const int r = v * RPI + lane / LPR;
+  for (int v = 0; v < 4; ++v) {
+    const int r = 8 * v + rg;
     const int64_t first = __shfl_sync(FULL, me.first, r);
     const int len = __shfl_sync(FULL, me.len, r);
     const int t0 = __shfl_sync(FULL, me.t0, r);
     const float sc = __shfl_sync(FULL, scale, r);
-    if (c < RV && step < len) {
+    if (step < len) {
       const int64_t row = lane_row<REVERSE>(first, len, t0, step, 0, row_step);
-      float4 f = *reinterpret_cast<const float4*>(warp_slots + r * stride + off + 4 * c);
-      f.x *= sc; f.y *= sc; f.z *= sc; f.w *= sc;
-      __stcs(reinterpret_cast<float4*>(g + row * RF + 4 * c), f);
+#pragma unroll
+      for (int u = 0; u < SUB; ++u) {
+        const int vec = 4 * u + c;
+        if (vec < RV) {
+          float4 f = *reinterpret_cast<const float4*>(warp_slots + r * stride + off + 4 * vec);
+          f.x *= sc; f.y *= sc; f.z *= sc; f.w *= sc;
+          __stcs(reinterpret_cast<float4*>(g + row * RF + 4 * vec), f);
+        }
+      }
     }
   }
 }

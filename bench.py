@@ -411,6 +411,7 @@ class Cl8:
         self.inp = {k: v.to(dev) for k, v in self._host(7 + rank, self.B).items()}
         self.out = dict(X=torch.empty_like(self.inp["S"]), dS=torch.empty_like(self.inp["S"]),
                         dgens=torch.empty_like(self.inp["gens"]), ddt=torch.empty_like(self.inp["dt"]))
+        self.Mc = torch.empty_like(self.inp["S"])  # rotor cache
         self.ws_bytes = lib.csn_rotor_scan_workspace_bytes(self.B, self.T, self.N, self.D)
         self.work = torch.empty(self.ws_bytes, dtype=torch.uint8, device=dev)
 
@@ -419,10 +420,11 @@ class Cl8:
         sp = ctypes.c_void_p(stream.cuda_stream)
         I, O = self.inp, self.out
         B, T, N, D = self.B, self.T, self.N, self.D
-        _lib.call("csn_rotor_scan_fwd", _p(I["gens"]), _p(I["dt"]), _p(None), _p(I["S"]), _p(None),
-                  _p(O["X"]), B, T, N, D, 1, 1, _p(self.work), self.ws_bytes, sp)
-        _lib.call("csn_rotor_scan_bwd", _p(I["gens"]), _p(I["dt"]), _p(None), _p(I["S"]), _p(None),
-                  _p(O["X"]), _p(I["dX"]), _p(O["dgens"]), _p(O["ddt"]), _p(None), _p(O["dS"]),
+        # the op's D = 16 path: rotors stored by the forward, reused by the backward
+        _lib.call("csn_rotor_scan_fwd_cached", _p(I["gens"]), _p(I["dt"]), _p(None), _p(I["S"]), _p(None),
+                  _p(O["X"]), _p(self.Mc), B, T, N, D, 1, 1, _p(self.work), self.ws_bytes, sp)
+        _lib.call("csn_rotor_scan_bwd_cached", _p(I["gens"]), _p(I["dt"]), _p(None), _p(I["S"]), _p(None),
+                  _p(O["X"]), _p(I["dX"]), _p(self.Mc), _p(O["dgens"]), _p(O["ddt"]), _p(None), _p(O["dS"]),
                   _p(None), B, T, N, D, 1, 1, _p(self.work), self.ws_bytes, sp)
 
     def e2e_setup(self):

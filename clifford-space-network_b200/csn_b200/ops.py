@@ -128,19 +128,25 @@ def rotor_scan(M, C, two_sided: bool = True, h0=None, reverse: bool = False):
 
 
 # ---------------------------------------------------------------- fused rotor scan
-def _rotor_fwd(g, d, ga, s, hf, basis, two_sided):
-    """Raw fused forward on float32 contiguous CUDA tensors -> X."""
+def _rotor_fwd(g, d, ga, s, hf, basis, two_sided, Mc=None):
+    """Raw fused forward on float32 contiguous CUDA tensors -> X.  With Mc ([B, T, N, 16, 16],
+    D = 16 only) every step's rotor M_t is stored there for the backward."""
     B, T, N, D, _ = s.shape
     X = torch.empty_like(s)
     ws_bytes = _lib.load().csn_rotor_scan_workspace_bytes(B, T, N, D)
     ws = _workspace(ws_bytes, s.device)
+    if Mc is not None:
+        _lib.call("csn_rotor_scan_fwd_cached", _ptr(g), _ptr(d), _ptr(ga), _ptr(s), _ptr(hf), _ptr(X),
+                  _ptr(Mc), B, T, N, D, basis, int(two_sided), _ptr(ws), ws_bytes, _stream(s.device))
+        return X
     _lib.call("csn_rotor_scan_fwd", _ptr(g), _ptr(d), _ptr(ga), _ptr(s), _ptr(hf), _ptr(X),
               B, T, N, D, basis, int(two_sided), _ptr(ws), ws_bytes, _stream(s.device))
     return X
 
 
-def _rotor_bwd(g, d, ga, s, hf, X, dXf, basis, two_sided, need_dh0):
-    """Raw fused adjoint -> (dgens, ddt, dgamma or None, dS, dh0 or None)."""
+def _rotor_bwd(g, d, ga, s, hf, X, dXf, basis, two_sided, need_dh0, Mc=None):
+    """Raw fused adjoint -> (dgens, ddt, dgamma or None, dS, dh0 or None); Mc = the rotors
+    stored by the forward (D = 16) or None to rebuild them."""
     B, T, N, D, _ = s.shape
     dg = torch.empty_like(g)
     ddt = torch.empty_like(d)
@@ -149,6 +155,11 @@ def _rotor_bwd(g, d, ga, s, hf, X, dXf, basis, two_sided, need_dh0):
     dh0 = torch.empty_like(hf) if (hf is not None and need_dh0) else None
     ws_bytes = _lib.load().csn_rotor_scan_workspace_bytes(B, T, N, D)
     ws = _workspace(ws_bytes, s.device)
+    if Mc is not None:
+        _lib.call("csn_rotor_scan_bwd_cached", _ptr(g), _ptr(d), _ptr(ga), _ptr(s), _ptr(hf), _ptr(X),
+                  _ptr(dXf), _ptr(Mc), _ptr(dg), _ptr(ddt), _ptr(dga), _ptr(dS), _ptr(dh0), B, T, N, D,
+                  basis, int(two_sided), _ptr(ws), ws_bytes, _stream(s.device))
+        return dg, ddt, dga, dS, dh0
     _lib.call("csn_rotor_scan_bwd", _ptr(g), _ptr(d), _ptr(ga), _ptr(s), _ptr(hf), _ptr(X),
               _ptr(dXf), _ptr(dg), _ptr(ddt), _ptr(dga), _ptr(dS), _ptr(dh0), B, T, N, D,
               basis, int(two_sided), _ptr(ws), ws_bytes, _stream(s.device))
@@ -160,16 +171,19 @@ class RotorScanFunction(torch.autograd.Function):
     def forward(ctx, gens, dt, gamma, S, h0, basis, two_sided):
         _require_cuda(gens, dt, gamma, S, h0)
         g, d, ga, s, hf = _f32(gens), _f32(dt), _f32(gamma), _f32(S), _f32(h0)
-        X = _rotor_fwd(g, d, ga, s, hf, basis, two_sided)
-        ctx.save_for_backward(g, d, ga, s, hf, X)
+        # D = 16: keep the step rotors for the backward (1 KB per element, like S) instead
+        # of rebuilding them there
+        Mc = torch.empty_like(s) if s.shape[-1] == 16 else None
+        X = _rotor_fwd(g, d, ga, s, hf, basis, two_sided, Mc)
+        ctx.save_for_backward(g, d, ga, s, hf, X, Mc)
         ctx.basis, ctx.two_sided = basis, two_sided
         ctx.dtypes = tuple(None if t is None else t.dtype for t in (gens, dt, gamma, S, h0))
         return X.to(S.dtype)
 
     @staticmethod
     def backward(ctx, dX):
-        g, d, ga, s, hf, X = ctx.saved_tensors
-        outs = _rotor_bwd(g, d, ga, s, hf, X, _f32(dX), ctx.basis, ctx.two_sided, ctx.needs_input_grad[4])
+        g, d, ga, s, hf, X, Mc = ctx.saved_tensors
+        outs = _rotor_bwd(g, d, ga, s, hf, X, _f32(dX), ctx.basis, ctx.two_sided, ctx.needs_input_grad[4], Mc)
         outs = [None if o is None else o.to(dt_) for o, dt_ in zip(outs, ctx.dtypes)]
         return outs[0], outs[1], outs[2], outs[3], outs[4], None, None
 

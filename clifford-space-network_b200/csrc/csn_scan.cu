@@ -599,6 +599,67 @@ extern "C" int csn_rotor_scan_bwd(const float* gens, const float* dt, const floa
   return dispatch(a, D, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, true, st);
 }
 
+// ======================================================= rotor cache (D = 16)
+// The forward stores every step's M_t = sqrt(a_t) Q_t in Mcache ([B, T, N, 16, 16], the
+// layout of S); the backward given the same Mcache loads the rotors instead of rebuilding
+// them, and so does the forward's apply pass.  Three of the four passes then skip the
+// Cayley transform, for 1 KB of extra HBM traffic per element per pass.
+extern "C" int csn_rotor_scan_fwd_cached(const float* gens, const float* dt, const float* gamma,
+                                         const float* S, const float* h0, float* X, float* Mcache,
+                                         int64_t B, int64_t T, int64_t N, int D, int basis,
+                                         int two_sided, void* workspace, size_t workspace_bytes,
+                                         void* stream) {
+  if (int rc = rotor_common_checks(gens, dt, S, B, T, N, D, basis)) return rc;
+  if (D != 16) return set_error(CSN_ERR_UNSUPPORTED, "csn_rotor_scan_fwd_cached: the rotor cache is for D = 16");
+  if (B * T * N == 0) return CSN_OK;
+  if (!X || !aligned16(X) || (h0 && !aligned16(h0)) || !Mcache || !aligned16(Mcache))
+    return set_error(CSN_ERR_INVALID, "csn_rotor_scan_fwd_cached: X or Mcache missing or misaligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Plan p = make_plan(B, T, N, D, false);
+  Workspace ws;
+  if (int rc = get_ws(ws, workspace, workspace_bytes, plan_bytes(p), st)) return rc;
+  ScanArgs a{};
+  a.gens = gens; a.dt = dt; a.gamma = gamma; a.S = S; a.h0 = h0; a.out = X;
+  a.B = B; a.T = T; a.N = N;
+  a.Mc_out = Mcache;
+  bind_ws(a, p, ws.base, D);
+  return scan16_dispatch(a, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, false, st);
+}
+
+extern "C" int csn_rotor_scan_bwd_cached(const float* gens, const float* dt, const float* gamma,
+                                         const float* S, const float* h0, const float* X,
+                                         const float* dX, const float* Mcache, float* dgens,
+                                         float* ddt, float* dgamma, float* dS, float* dh0, int64_t B,
+                                         int64_t T, int64_t N, int D, int basis, int two_sided,
+                                         void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = rotor_common_checks(gens, dt, S, B, T, N, D, basis)) return rc;
+  if (D != 16) return set_error(CSN_ERR_UNSUPPORTED, "csn_rotor_scan_bwd_cached: the rotor cache is for D = 16");
+  if (B * T * N == 0) {
+    if (B * T > 0 && ddt) {
+      cudaError_t e = cudaMemsetAsync(ddt, 0, sizeof(float) * B * T, static_cast<cudaStream_t>(stream));
+      if (e != cudaSuccess) return set_cuda_error(e, "cudaMemsetAsync(ddt)");
+    }
+    return CSN_OK;
+  }
+  if (!X || !dX || !dgens || !ddt || !dS || (gamma && !dgamma) || !Mcache)
+    return set_error(CSN_ERR_INVALID, "csn_rotor_scan_bwd_cached: missing X, dX, Mcache or a gradient output");
+  if (!aligned16(X) || !aligned16(dX) || !aligned16(dS) || !aligned16(Mcache) || (h0 && !aligned16(h0)) ||
+      (dh0 && !aligned16(dh0)))
+    return set_error(CSN_ERR_INVALID, "csn_rotor_scan_bwd_cached: pointers must be 16-byte aligned");
+  if (dh0 && !h0) return set_error(CSN_ERR_INVALID, "csn_rotor_scan_bwd_cached: dh0 needs h0");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Plan p = make_plan(B, T, N, D, true);
+  Workspace ws;
+  if (int rc = get_ws(ws, workspace, workspace_bytes, plan_bytes(p), st)) return rc;
+  ScanArgs a{};
+  a.gens = gens; a.dt = dt; a.gamma = gamma; a.S = S; a.h0 = h0; a.X = X; a.dX = dX;
+  a.dgens = dgens; a.ddt = ddt; a.dgamma = dgamma; a.dC = dS; a.dh0 = dh0;
+  a.B = B; a.T = T; a.N = N;
+  a.Mc_in = Mcache;
+  bind_ws(a, p, ws.base, D);
+  return scan16_dispatch(a, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, true, st);
+}
+
 // ======================================================= no-allocation forward variant
 //
 // csn_rotor_scan_fwd_noalloc is csn_rotor_scan_fwd for callers that must not allocate

@@ -426,8 +426,13 @@ __device__ __forceinline__ void step_matrix(const ScanArgs& a, const Warp& w, co
       gam = 0.0f;
       alpha = sa = 1.0f;
     }
-    build_Om<NTerms<BASIS>::value>(M, w.gs, terms, 0.5f * dtv);
-    cayley(M, sa, w.lane);
+    if (a.Mc_in) {
+      f_load(M, a.Mc_in + e * DD, w.lane);  // cached rotor of this step
+    } else {
+      build_Om<NTerms<BASIS>::value>(M, w.gs, terms, 0.5f * dtv);
+      cayley(M, sa, w.lane);
+      if (a.Mc_out) f_store<false>(a.Mc_out + e * DD, M, w.lane);
+    }
   }
 }
 
@@ -743,16 +748,21 @@ int run16(const ScanArgs& a, bool bwd, cudaStream_t st) {
   }
   if (!bwd) {
     if (total == 0) return CSN_OK;
+    ScanArgs ap = a;  // apply pass: reads the rotors the reduce pass stored
     if (a.nchunks > 1) {
       if (a.agg_mode != 2) {
         KernelTimer kt("fwd_reduce", st);
         fwd16_kernel<true, SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(a);
+        if (a.Mc_out) {
+          ap.Mc_in = a.Mc_out;
+          ap.Mc_out = nullptr;
+        }
       }
       KernelTimer kt("fwd_carry", st);
       launch_grouped_carry<16, TWO, false>(a, st);
     }
     KernelTimer kt("fwd_apply", st);
-    fwd16_kernel<false, SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(a);
+    fwd16_kernel<false, SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(ap);
     return check_launch("scan forward (D=16)");
   }
   if (total > 0) {

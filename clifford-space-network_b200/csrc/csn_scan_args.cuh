@@ -45,6 +45,11 @@ struct ScanArgs {
   float* P_out;  // [B, N, D, D]
   float* c_out;  // [B, N, D, D]
   int rev;       // plain scan in reverse time (X_t = M_t X_{t+1} (M_t^T) + C_t, X_T = h0)
+  // Rotor cache (D = 16 fused scans): the step matrices M_t = sqrt(a_t) Q_t, [B, T, N, D, D].
+  // A pass with Mc_out computes M_t and stores it; a pass with Mc_in loads it instead of
+  // rebuilding the Cayley rotor.
+  const float* Mc_in;
+  float* Mc_out;
 };
 
 // Physical time of scan step t: the plain scan can run in reverse time (rev), i.e. scan

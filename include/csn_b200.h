@@ -106,6 +106,26 @@ int csn_rotor_scan_bwd(const float* gens, const float* dt, const float* gamma, c
                        int64_t B, int64_t T, int64_t N, int D, int basis, int two_sided,
                        void* workspace, size_t workspace_bytes, void* stream);
 
+/* Rotor cache for D = 16 (where building a rotor costs as much as the scan step itself):
+ *   csn_rotor_scan_fwd_cached: csn_rotor_scan_fwd that also stores every step's matrix
+ *                              M_t = sqrt(a_t) Q_t in Mcache ([B,T,N,16,16], the layout of S);
+ *                              its apply pass reuses what its reduce pass stored;
+ *   csn_rotor_scan_bwd_cached: csn_rotor_scan_bwd that loads M_t from that Mcache instead
+ *                              of rebuilding the Cayley rotors (same other inputs as the forward).
+ * Same results as the uncached pair to fp32 rounding.  D != 16 -> CSN_ERR_UNSUPPORTED.  Replaces
+ * the same reference code as csn_rotor_scan_fwd/bwd (python/clifford_cl8.py:160-179, where
+ * autograd keeps the rotors Q between forward and backward). */
+int csn_rotor_scan_fwd_cached(const float* gens, const float* dt, const float* gamma,
+                              const float* S, const float* h0, float* X, float* Mcache,
+                              int64_t B, int64_t T, int64_t N, int D, int basis, int two_sided,
+                              void* workspace, size_t workspace_bytes, void* stream);
+int csn_rotor_scan_bwd_cached(const float* gens, const float* dt, const float* gamma,
+                              const float* S, const float* h0, const float* X, const float* dX,
+                              const float* Mcache, float* dgens, float* ddt, float* dgamma,
+                              float* dS, float* dh0, int64_t B, int64_t T, int64_t N, int D,
+                              int basis, int two_sided, void* workspace, size_t workspace_bytes,
+                              void* stream);
+
 /* Same computation and chunking as csn_rotor_scan_fwd (bit-identical results), for
  * callers that cannot allocate device memory: hosts that hand the whole GPU to their
  * own memory pool, or loops that must not allocate once running.  No counterpart in

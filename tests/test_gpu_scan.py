@@ -233,3 +233,39 @@ def test_undamped_orthogonal_scan_preserves_norm_L8192(ops):
     n0 = S[:, 0].flatten(2).norm(dim=-1)
     nT = X[:, -1].flatten(2).norm(dim=-1)
     assert ((nT - n0).abs() / n0).max().item() < 1e-4
+
+
+@pytest.mark.parametrize("basis", ["triu", "ga"])
+@pytest.mark.parametrize("damped", [True, False], ids=["damped", "undamped"])
+@pytest.mark.parametrize("two", [True, False], ids=["two", "one"])
+@pytest.mark.parametrize("T", [6, 150])  # one chunk (apply stores the rotors) / many chunks
+def test_d16_rotor_cache_matches_uncached_entry_points(ops, basis, damped, two, T):
+    """csn_rotor_scan_{fwd,bwd}_cached (rotors stored once, reused by the other passes) give
+    the results of the entry points that rebuild every rotor, and store M_t = sqrt(a) Q."""
+    from csn_b200 import _lib
+    rng = np.random.default_rng(31 + T + 2 * damped + 4 * two + 8 * (basis == "ga"))
+    B, N = 2, 3
+    from csn_b200 import algebra
+    E = algebra.triu_basis(16) if basis == "triu" else algebra.bivector_basis(algebra.CL8)
+    gens = cuda(rng.standard_normal((B, T, N, E.shape[0])) * np.where(rng.random((B, T, N, 1)) < 0.5, 0.05, 2.0))
+    dt, S, dX = cuda(rng.uniform(0.01, 0.1, (B, T))), cuda(rng.standard_normal((B, T, N, 16, 16))), cuda(rng.standard_normal((B, T, N, 16, 16)))
+    gamma = cuda(np.log1p(np.exp(rng.standard_normal((B, T, N))))) if damped else None
+    h0 = cuda(rng.standard_normal((B, N, 16, 16)))
+    bi = ops.BASIS[basis]
+    X0 = ops._rotor_fwd(gens, dt, gamma, S, h0, bi, two)
+    Mc = torch.empty_like(S)
+    X1 = ops._rotor_fwd(gens, dt, gamma, S, h0, bi, two, Mc)
+    assert rel(X1, X0.cpu().numpy()) < 1e-5
+    # the stored rotors are the transitions of the plain scan
+    C = S if gamma is None else S * (1.0 - torch.sigmoid(-gamma * dt[..., None]))[..., None, None]
+    Xm = ops.rotor_scan(Mc, C, two_sided=two, h0=h0)
+    assert rel(Xm, X0.cpu().numpy()) < 1e-4
+    g0 = ops._rotor_bwd(gens, dt, gamma, S, h0, X0, dX, bi, two, True)
+    g1 = ops._rotor_bwd(gens, dt, gamma, S, h0, X1, dX, bi, two, True, Mc)
+    for a_, b_ in zip(g1, g0):
+        if b_ is not None:
+            assert rel(a_, b_.cpu().numpy()) < 1e-5
+    with pytest.raises(_lib.CsnError, match="UNSUPPORTED"):
+        s8 = cuda(rng.standard_normal((1, 4, 1, 8, 8)))
+        ops._rotor_fwd(cuda(rng.standard_normal((1, 4, 1, 28))), cuda(np.full((1, 4), 0.05)), None, s8,
+                       None, 0, True, torch.empty_like(s8))

@@ -241,7 +241,8 @@ class Cl6LM:
         for L, O in zip(self.inputs, self.outs):
             _lib.call("csn_rotor_scan_fwd", _p(L["gens"]), _p(L["dt"]), _p(L["gamma"]), _p(L["S"]),
                       _p(None), _p(O["X"]), B, T, N, D, 0, 1, _p(self.work), self.ws_bytes, sp)
-            _lib.call("csn_rotor_scan_bwd", _p(L["gens"]), _p(L["dt"]), _p(L["gamma"]), _p(L["S"]),
+            # the op's path: the backward reuses the chunk rotor products its forward left
+            _lib.call("csn_rotor_scan_bwd_reuse", _p(L["gens"]), _p(L["dt"]), _p(L["gamma"]), _p(L["S"]),
                       _p(None), _p(O["X"]), _p(L["dX"]), _p(O["dgens"]), _p(O["ddt"]), _p(O["dgamma"]),
                       _p(O["dS"]), _p(None), B, T, N, D, 0, 1, _p(self.work), self.ws_bytes, sp)
 

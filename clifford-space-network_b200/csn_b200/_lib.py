@@ -33,6 +33,8 @@ SIGNATURES = {
                            _int),
     "csn_rotor_scan_bwd": ([_f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _i64, _i64, _i64, _int,
                             _int, _int, _f, _sz, _f], _int),
+    "csn_rotor_scan_bwd_reuse": ([_f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _i64, _i64, _i64, _int,
+                                  _int, _int, _f, _sz, _f], _int),
     "csn_rotor_scan_fwd_cached": ([_f, _f, _f, _f, _f, _f, _f, _i64, _i64, _i64, _int, _int, _int, _f,
                                    _sz, _f], _int),
     "csn_rotor_scan_bwd_cached": ([_f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _i64, _i64,

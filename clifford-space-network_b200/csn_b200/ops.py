@@ -128,13 +128,15 @@ def rotor_scan(M, C, two_sided: bool = True, h0=None, reverse: bool = False):
 
 
 # ---------------------------------------------------------------- fused rotor scan
-def _rotor_fwd(g, d, ga, s, hf, basis, two_sided, Mc=None):
+def _rotor_fwd(g, d, ga, s, hf, basis, two_sided, Mc=None, ws=None):
     """Raw fused forward on float32 contiguous CUDA tensors -> X.  With Mc ([B, T, N, 16, 16],
-    D = 16 only) every step's rotor M_t is stored there for the backward."""
+    D = 16 only) every step's rotor M_t is stored there for the backward.  `ws`: a workspace
+    of csn_rotor_scan_workspace_bytes to use (and keep for a reusing backward)."""
     B, T, N, D, _ = s.shape
     X = torch.empty_like(s)
     ws_bytes = _lib.load().csn_rotor_scan_workspace_bytes(B, T, N, D)
-    ws = _workspace(ws_bytes, s.device)
+    if ws is None:
+        ws = _workspace(ws_bytes, s.device)
     if Mc is not None:
         _lib.call("csn_rotor_scan_fwd_cached", _ptr(g), _ptr(d), _ptr(ga), _ptr(s), _ptr(hf), _ptr(X),
                   _ptr(Mc), B, T, N, D, basis, int(two_sided), _ptr(ws), ws_bytes, _stream(s.device))
@@ -144,9 +146,10 @@ def _rotor_fwd(g, d, ga, s, hf, basis, two_sided, Mc=None):
     return X
 
 
-def _rotor_bwd(g, d, ga, s, hf, X, dXf, basis, two_sided, need_dh0, Mc=None):
+def _rotor_bwd(g, d, ga, s, hf, X, dXf, basis, two_sided, need_dh0, Mc=None, fwd_ws=None):
     """Raw fused adjoint -> (dgens, ddt, dgamma or None, dS, dh0 or None); Mc = the rotors
-    stored by the forward (D = 16) or None to rebuild them."""
+    stored by the forward (D = 16) or None to rebuild them; fwd_ws = the forward's workspace,
+    whose chunk rotor products the backward then reuses."""
     B, T, N, D, _ = s.shape
     dg = torch.empty_like(g)
     ddt = torch.empty_like(d)
@@ -159,6 +162,11 @@ def _rotor_bwd(g, d, ga, s, hf, X, dXf, basis, two_sided, need_dh0, Mc=None):
         _lib.call("csn_rotor_scan_bwd_cached", _ptr(g), _ptr(d), _ptr(ga), _ptr(s), _ptr(hf), _ptr(X),
                   _ptr(dXf), _ptr(Mc), _ptr(dg), _ptr(ddt), _ptr(dga), _ptr(dS), _ptr(dh0), B, T, N, D,
                   basis, int(two_sided), _ptr(ws), ws_bytes, _stream(s.device))
+        return dg, ddt, dga, dS, dh0
+    if fwd_ws is not None:
+        _lib.call("csn_rotor_scan_bwd_reuse", _ptr(g), _ptr(d), _ptr(ga), _ptr(s), _ptr(hf), _ptr(X),
+                  _ptr(dXf), _ptr(dg), _ptr(ddt), _ptr(dga), _ptr(dS), _ptr(dh0), B, T, N, D,
+                  basis, int(two_sided), _ptr(fwd_ws), ws_bytes, _stream(s.device))
         return dg, ddt, dga, dS, dh0
     _lib.call("csn_rotor_scan_bwd", _ptr(g), _ptr(d), _ptr(ga), _ptr(s), _ptr(hf), _ptr(X),
               _ptr(dXf), _ptr(dg), _ptr(ddt), _ptr(dga), _ptr(dS), _ptr(dh0), B, T, N, D,
@@ -174,8 +182,13 @@ class RotorScanFunction(torch.autograd.Function):
         # D = 16: keep the step rotors for the backward (1 KB per element, like S) instead
         # of rebuilding them there
         Mc = torch.empty_like(s) if s.shape[-1] == 16 else None
-        X = _rotor_fwd(g, d, ga, s, hf, basis, two_sided, Mc)
+        # D = 4, 8: keep the forward's workspace, whose chunk rotor products the backward reuses
+        B, T, N, D, _ = s.shape
+        ws = None if Mc is not None else _workspace(_lib.load().csn_rotor_scan_workspace_bytes(B, T, N, D),
+                                                   s.device)
+        X = _rotor_fwd(g, d, ga, s, hf, basis, two_sided, Mc, ws)
         ctx.save_for_backward(g, d, ga, s, hf, X, Mc)
+        ctx.fwd_ws = ws
         ctx.basis, ctx.two_sided = basis, two_sided
         ctx.dtypes = tuple(None if t is None else t.dtype for t in (gens, dt, gamma, S, h0))
         return X.to(S.dtype)
@@ -183,7 +196,9 @@ class RotorScanFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dX):
         g, d, ga, s, hf, X, Mc = ctx.saved_tensors
-        outs = _rotor_bwd(g, d, ga, s, hf, X, _f32(dX), ctx.basis, ctx.two_sided, ctx.needs_input_grad[4], Mc)
+        outs = _rotor_bwd(g, d, ga, s, hf, X, _f32(dX), ctx.basis, ctx.two_sided, ctx.needs_input_grad[4], Mc,
+                          ctx.fwd_ws if Mc is None else None)
+        ctx.fwd_ws = None
         outs = [None if o is None else o.to(dt_) for o, dt_ in zip(outs, ctx.dtypes)]
         return outs[0], outs[1], outs[2], outs[3], outs[4], None, None
 

@@ -157,10 +157,10 @@ __global__ void __launch_bounds__(128) bwd_reduce_kernel(ScanArgs a) {
     add_scaled_mat(g, a.dX + e * (D * D), 1.0f);
     lmulT(M, g);
     if constexpr (TWO) rmul(g, M);
-    rmul(P, M);
+    if (!a.reuse_P) rmul(P, M);
   }
   const int64_t s = b * a.N + n;
-  store_mat(a.aggP + (s * a.nchunks + j) * (D * D), P);
+  if (!a.reuse_P) store_mat(a.aggP + (s * a.nchunks + j) * (D * D), P);
   store_mat(a.aggC + (s * a.nchunks + j) * (D * D), g);
 }
 
@@ -595,6 +595,46 @@ extern "C" int csn_rotor_scan_bwd(const float* gens, const float* dt, const floa
   a.dgens = dgens; a.ddt = ddt; a.dgamma = dgamma; a.dC = dS; a.dh0 = dh0;
   a.B = B; a.T = T; a.N = N;
   bind_ws(a, p, ws.base, D);
+  if (D == 16) return scan16_dispatch(a, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, true, st);
+  return dispatch(a, D, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, true, st);
+}
+
+// ======================================================= backward after a forward
+// csn_rotor_scan_bwd on the workspace its forward used: the chunk products P_j that the
+// forward's reduce pass left in it are the ones the backward carry needs, so the backward
+// reduce pass computes only the gradient aggregates.
+extern "C" int csn_rotor_scan_bwd_reuse(const float* gens, const float* dt, const float* gamma,
+                                        const float* S, const float* h0, const float* X,
+                                        const float* dX, float* dgens, float* ddt, float* dgamma,
+                                        float* dS, float* dh0, int64_t B, int64_t T, int64_t N,
+                                        int D, int basis, int two_sided, void* workspace,
+                                        size_t workspace_bytes, void* stream) {
+  if (int rc = rotor_common_checks(gens, dt, S, B, T, N, D, basis)) return rc;
+  if (B * T * N == 0) {
+    if (B * T > 0 && ddt) {
+      cudaError_t e = cudaMemsetAsync(ddt, 0, sizeof(float) * B * T, static_cast<cudaStream_t>(stream));
+      if (e != cudaSuccess) return set_cuda_error(e, "cudaMemsetAsync(ddt)");
+    }
+    return CSN_OK;
+  }
+  if (!X || !dX || !dgens || !ddt || !dS || (gamma && !dgamma))
+    return set_error(CSN_ERR_INVALID, "csn_rotor_scan_bwd_reuse: missing X, dX or a gradient output");
+  if (!aligned16(X) || !aligned16(dX) || !aligned16(dS) || (h0 && !aligned16(h0)) ||
+      (dh0 && !aligned16(dh0)))
+    return set_error(CSN_ERR_INVALID, "csn_rotor_scan_bwd_reuse: pointers must be 16-byte aligned");
+  if (dh0 && !h0) return set_error(CSN_ERR_INVALID, "csn_rotor_scan_bwd_reuse: dh0 needs h0");
+  Plan p = make_plan(B, T, N, D, true);
+  const size_t need = plan_bytes(p);
+  if (need > 256 && (!workspace || workspace_bytes < need))
+    return set_error(CSN_ERR_INVALID,
+                     "csn_rotor_scan_bwd_reuse: needs the forward's workspace (csn_rotor_scan_workspace_bytes)");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  ScanArgs a{};
+  a.gens = gens; a.dt = dt; a.gamma = gamma; a.S = S; a.h0 = h0; a.X = X; a.dX = dX;
+  a.dgens = dgens; a.ddt = ddt; a.dgamma = dgamma; a.dC = dS; a.dh0 = dh0;
+  a.B = B; a.T = T; a.N = N;
+  a.reuse_P = 1;
+  bind_ws(a, p, static_cast<float*>(workspace), D);
   if (D == 16) return scan16_dispatch(a, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, true, st);
   return dispatch(a, D, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, true, st);
 }

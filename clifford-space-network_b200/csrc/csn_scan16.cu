@@ -540,12 +540,14 @@ __global__ void __launch_bounds__(128) bwd16_reduce_kernel(ScanArgs a) {
     F16S Ws;
     split(Ws, W);
     nt(Gc, Mts, Ws);  // M^T G M  |  M^T G
-    F16S Ps;
-    split(Ps, P);
-    nt(P, Ps, Mts);  // P M
+    if (!a.reuse_P) {
+      F16S Ps;
+      split(Ps, P);
+      nt(P, Ps, Mts);  // P M
+    }
   }
   f_store<false>(a.aggC + (w.s * a.nchunks + w.j) * DD, Gc, lane);
-  f_store<false>(a.aggP + (w.s * a.nchunks + w.j) * DD, P, lane);
+  if (!a.reuse_P) f_store<false>(a.aggP + (w.s * a.nchunks + w.j) * DD, P, lane);
 }
 
 // -------------------------------------------------------------- backward: apply

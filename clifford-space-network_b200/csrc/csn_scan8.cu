@@ -370,22 +370,25 @@ __global__ void __launch_bounds__(THREADS, 2) bwd8_reduce_kernel(ScanArgs a) {
     lmulT(M, g);
     if constexpr (TWO) rmul(g, M);
     // P <- P M, row by row in place
+    if (!a.reuse_P) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      float v[8], o[8];
-      lds_row(v, slot + BwdRedSlot::P + 8 * i);
+      for (int i = 0; i < 8; ++i) {
+        float v[8], o[8];
+        lds_row(v, slot + BwdRedSlot::P + 8 * i);
 #pragma unroll
-      for (int l = 0; l < 8; ++l) {
-        float acc = 0.0f;
+        for (int l = 0; l < 8; ++l) {
+          float acc = 0.0f;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) acc = fmaf(v[k], M.a[k][l], acc);
-        o[l] = acc;
+          for (int k = 0; k < 8; ++k) acc = fmaf(v[k], M.a[k][l], acc);
+          o[l] = acc;
+        }
+        sts_row(slot + BwdRedSlot::P + 8 * i, o);
       }
-      sts_row(slot + BwdRedSlot::P + 8 * i, o);
     }
   }
   cp_async_wait<0>();
   store_mat(a.aggC + (s * a.nchunks + j) * DD, g);
+  if (a.reuse_P) return;
   Mat<8> P;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {

@@ -50,6 +50,9 @@ struct ScanArgs {
   // rebuilding the Cayley rotor.
   const float* Mc_in;
   float* Mc_out;
+  // Backward: aggP already holds each chunk's product P_j (left there by the forward on the
+  // same generators), so the backward reduce pass computes only the gradient aggregates.
+  int reuse_P;
 };
 
 // Physical time of scan step t: the plain scan can run in reverse time (rev), i.e. scan

@@ -106,6 +106,17 @@ int csn_rotor_scan_bwd(const float* gens, const float* dt, const float* gamma, c
                        int64_t B, int64_t T, int64_t N, int D, int basis, int two_sided,
                        void* workspace, size_t workspace_bytes, void* stream);
 
+/* csn_rotor_scan_bwd for a backward that follows its forward on the same workspace: the
+ * workspace must be the one given to csn_rotor_scan_fwd with the same gens, dt, gamma, B, T,
+ * N, D and basis, unused since; the chunk rotor products that forward left in it are reused,
+ * so the backward's reduce pass skips them.  Same results as csn_rotor_scan_bwd to fp32
+ * rounding.  Replaces the same reference code (autograd keeps the forward's intermediates). */
+int csn_rotor_scan_bwd_reuse(const float* gens, const float* dt, const float* gamma, const float* S,
+                             const float* h0, const float* X, const float* dX,
+                             float* dgens, float* ddt, float* dgamma, float* dS, float* dh0,
+                             int64_t B, int64_t T, int64_t N, int D, int basis, int two_sided,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
 /* Rotor cache for D = 16 (where building a rotor costs as much as the scan step itself):
  *   csn_rotor_scan_fwd_cached: csn_rotor_scan_fwd that also stores every step's matrix
  *                              M_t = sqrt(a_t) Q_t in Mcache ([B,T,N,16,16], the layout of S);

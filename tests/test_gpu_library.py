@@ -42,8 +42,10 @@ def test_scan_and_rotor_ops_match_the_autograd_functions(mods):
     a = ops.fused_rotor_scan(gens, dt, gamma, S, h0=h0)
     b = csn.fused_rotor_scan_fwd(gens, dt, gamma, S, h0, 0, True)
     assert torch.equal(a, b)
+    # the op's backward reuses the chunk rotor products of its forward (products formed as M P);
+    # the functional operator rebuilds them (P M): equal up to fp32 rounding
     for ga, gb in zip(_grads(a, W, [gens, dt, gamma, S, h0]), _grads(b, W, [gens, dt, gamma, S, h0])):
-        assert torch.equal(ga, gb)
+        assert ((ga - gb).abs().max() / gb.abs().max()).item() < 1e-5
 
 
 def test_cayley_cell_ga3_ops_match(mods):

@@ -269,3 +269,27 @@ def test_d16_rotor_cache_matches_uncached_entry_points(ops, basis, damped, two, 
         s8 = cuda(rng.standard_normal((1, 4, 1, 8, 8)))
         ops._rotor_fwd(cuda(rng.standard_normal((1, 4, 1, 28))), cuda(np.full((1, 4), 0.05)), None, s8,
                        None, 0, True, torch.empty_like(s8))
+
+
+@pytest.mark.parametrize("D,basis", [(4, "triu"), (8, "triu"), (16, "ga")])
+@pytest.mark.parametrize("damped", [True, False], ids=["damped", "undamped"])
+@pytest.mark.parametrize("two", [True, False], ids=["two", "one"])
+def test_backward_reusing_forward_workspace_matches(ops, D, basis, damped, two):
+    """csn_rotor_scan_bwd_reuse on the forward's workspace (chunk rotor products taken from
+    it) equals csn_rotor_scan_bwd on a fresh workspace."""
+    from csn_b200 import _lib
+    rng = np.random.default_rng(57 + D + 2 * damped + 4 * two)
+    B, T, N = (2, 300, 3) if D < 16 else (1, 120, 2)
+    E, gens, dt, gamma, S = _rotor_case(rng, B, T, N, D, basis, damped, gscale=2.0)
+    g, d, s = cuda(gens), cuda(dt), cuda(S)
+    ga = cuda(gamma) if damped else None
+    h0, dX = cuda(rng.standard_normal((B, N, D, D))), cuda(rng.standard_normal((B, T, N, D, D)))
+    bi = ops.BASIS[basis]
+    ws = torch.zeros(_lib.load().csn_rotor_scan_workspace_bytes(B, T, N, D), dtype=torch.uint8, device=DEV)
+    X = ops._rotor_fwd(g, d, ga, s, h0, bi, two, None, ws)
+    ref = ops._rotor_bwd(g, d, ga, s, h0, X, dX, bi, two, True)
+    for _ in range(2):  # the reused products survive a backward (aggP is only read)
+        got = ops._rotor_bwd(g, d, ga, s, h0, X, dX, bi, two, True, None, ws)
+        for a_, b_ in zip(got, ref):
+            if b_ is not None:
+                assert rel(a_, b_.cpu().numpy()) < 1e-5

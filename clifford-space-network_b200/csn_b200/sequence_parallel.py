@@ -20,6 +20,9 @@ each exchange the ranks all-gather a small header (shapes, flags) so that a rank
 mismatched shard is reported on every rank instead of deadlocking the collective, and
 the gathered carries are checked for non-finite values on every rank alike.
 
+Per direction the ranks make two collectives and two host synchronisations: the header check
+and one stacked all-gather of the summaries with one finiteness check.
+
 The kernel calls go through a backend object (``CudaBackend`` here); tests substitute a
 CPU backend to exercise the exchange logic with the gloo backend.
 """
@@ -111,27 +114,32 @@ def _world(group):
 
 
 def _check_header(local: torch.Tensor, group, what: str):
-    """All-gather a small int64 header; raise the same error on every rank on mismatch."""
+    """All-gather a small int64 header; raise the same error on every rank on mismatch.
+    One collective and one host synchronisation; it runs before any collective whose sizes
+    depend on the shard, so a mismatched rank cannot leave the others waiting."""
     ws, _ = _world(group)
-    hdr = [torch.empty_like(local) for _ in range(ws)]
-    dist.all_gather(hdr, local, group=group)
-    ref = hdr[0]
-    for r, h in enumerate(hdr):
-        if not torch.equal(h, ref):
-            raise ShardMismatchError(f"{what}: rank {r} shard header {h.tolist()} != rank 0 {ref.tolist()}")
+    hdr = local.new_empty((ws * local.shape[0],))
+    dist.all_gather_into_tensor(hdr, local.contiguous(), group=group)
+    hdr = hdr.view(ws, -1)
+    bad = (hdr != hdr[:1]).any(dim=1)
+    if bool(bad.any()):
+        r = int(bad.nonzero()[0])
+        raise ShardMismatchError(f"{what}: rank {r} shard header {hdr[r].tolist()} != rank 0 {hdr[0].tolist()}")
 
 
-def _gather(t: torch.Tensor, group):
+def _gather_checked(parts, group, what: str):
+    """All-gather the shard summaries of every rank in ONE collective (stacked), check them
+    for non-finite values with ONE host synchronisation (the same result on every rank), and
+    return one [ws, ...] tensor per part."""
     ws, _ = _world(group)
-    out = [torch.empty_like(t) for _ in range(ws)]
-    dist.all_gather(out, t.contiguous(), group=group)
-    return out
-
-
-def _check_finite(ts, what):
-    for r, t in enumerate(ts):
-        if not bool(torch.isfinite(t).all()):
-            raise ShardMismatchError(f"{what}: carry from rank {r} is not finite")
+    local = torch.stack([p.contiguous() for p in parts])  # [n_parts, ...]
+    out = local.new_empty((ws * local.shape[0],) + tuple(local.shape[1:]))
+    dist.all_gather_into_tensor(out, local, group=group)  # rank-major concatenation
+    out = out.view((ws,) + tuple(local.shape))
+    if not bool(torch.isfinite(out).all()):
+        r = int((~torch.isfinite(out.flatten(1))).any(dim=1).nonzero()[0])
+        raise ShardMismatchError(f"{what}: carry from rank {r} is not finite")
+    return [out[:, i] for i in range(len(parts))]
 
 
 def sp_forward(gens, dt, gamma, S, group=None, backend=None, basis="triu", two_sided=True):
@@ -147,12 +155,12 @@ def sp_forward(gens, dt, gamma, S, group=None, backend=None, basis="triu", two_s
     _check_header(torch.tensor([B, T, N, D, gens.shape[-1], flags], dtype=torch.int64, device=dev),
                   group, "sequence-parallel forward")
     P, c, ws_fwd = backend.fwd_aggregate(gens, dt, gamma, S, basis, two_sided)
-    Ps, cs = _gather(P, group), _gather(c, group)
-    _check_finite(Ps + cs, "sequence-parallel forward")
+    Pall, call = _gather_checked([P, c], group, "sequence-parallel forward")  # [ws, B, N, D, D]
+    Ps = list(Pall.unbind(0))
     h_in = None
     if g > 0:
-        Mseq = torch.stack(Ps[:g], dim=1)        # [B, g, N, D, D]
-        Cseq = torch.stack(cs[:g], dim=1)
+        Mseq = Pall[:g].transpose(0, 1).contiguous()  # [B, g, N, D, D]
+        Cseq = call[:g].transpose(0, 1).contiguous()
         h_in = backend.scan_mc(Mseq, Cseq, two_sided)[:, -1].contiguous()
     X = backend.rotor_fwd(gens, dt, gamma, S, h_in, basis, two_sided, ws=ws_fwd)
     return X, h_in, Ps
@@ -167,8 +175,8 @@ def sp_backward(gens, dt, gamma, S, X, dX, h_in, Ps, group=None, backend=None, b
     _check_header(torch.tensor([B, T, N, D, int(dX.shape == S.shape)], dtype=torch.int64,
                                device=S.device), group, "sequence-parallel backward")
     cb, ws_bwd = backend.bwd_aggregate(gens, dt, gamma, dX, basis, two_sided)
-    cbs = _gather(cb, group)
-    _check_finite(cbs, "sequence-parallel backward")
+    (cball,) = _gather_checked([cb], group, "sequence-parallel backward")
+    cbs = list(cball.unbind(0))
     H = None
     if g < ws - 1:
         later = list(range(ws - 1, g, -1))         # r = G-1 .. g+1

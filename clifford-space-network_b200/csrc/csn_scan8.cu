@@ -265,7 +265,8 @@ __global__ void __launch_bounds__(THREADS, 2) fwd8_kernel(ScanArgs a) {
       cp_async_commit();
       if (live) {
         // P <- M P; column j of the new P = M * (column j of P) = M * (row j of P^T)
-#pragma unroll
+        // (jj only addresses shared memory: rolled, 9 % faster than unrolled)
+#pragma unroll 1
         for (int jj = 0; jj < 8; ++jj) {
           float v[8], o[8];
           lds_row(v, slot + FwdSlot::P + 8 * jj);
@@ -369,9 +370,9 @@ __global__ void __launch_bounds__(THREADS, 2) bwd8_reduce_kernel(ScanArgs a) {
     cp_async_commit();
     lmulT(M, g);
     if constexpr (TWO) rmul(g, M);
-    // P <- P M, row by row in place
+    // P <- P M, row by row in place (i only addresses shared memory: rolled)
     if (!a.reuse_P) {
-#pragma unroll
+#pragma unroll 1
       for (int i = 0; i < 8; ++i) {
         float v[8], o[8];
         lds_row(v, slot + BwdRedSlot::P + 8 * i);

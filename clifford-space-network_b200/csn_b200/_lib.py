@@ -39,6 +39,10 @@ SIGNATURES = {
                                    _sz, _f], _int),
     "csn_rotor_scan_bwd_cached": ([_f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _i64, _i64,
                                    _i64, _int, _int, _int, _f, _sz, _f], _int),
+    "csn_rotor_scan_heads_fwd": ([_f, _f, _f, _f, _f, _f, _f, _i64, _i64, _i64, _i64, _int, _int, _int,
+                                  _f, _sz, _f], _int),
+    "csn_rotor_scan_heads_bwd": ([_f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _i64, _i64, _i64,
+                                  _i64, _int, _int, _int, _int, _f, _sz, _f], _int),
     "csn_rotor_scan_fwd_noalloc": ([_f, _f, _f, _f, _f, _f, _i64, _i64, _i64, _int, _int, _int,
                                     _f], _int),
     "csn_rotor_scan_aggregate_workspace_bytes": ([_i64, _i64, _i64, _int], _sz),

@@ -11,6 +11,8 @@ Ops (reference functions they replace, paths relative to the reference root):
                                csn_toolkit/csn/scan.py:16-72 CliffordScanFunction (one-sided)
 * :func:`fused_rotor_scan`  -- python/clifford_cl6.py:150-171 / python/clifford_cl8.py:160-179
                                (Cayley rotor + decay + scan in one pass)
+* :func:`fused_rotor_scan_heads` -- python/clifford_multihead.py:137-170 (per-head dt, heads
+                               read in place instead of folded into the batch)
 * :func:`cayley`            -- python/clifford_cl6.py:57, python/clifford_cl8.py:29,65
 * :func:`cell_step`         -- python/clifford_layer.py:50-115 CliffordTENNCell.forward
 * :func:`ga3_rotor_scan`    -- Cl(3,0) blade-basis form of the two-sided scan
@@ -24,8 +26,8 @@ import torch
 
 from . import _lib
 
-__all__ = ["rotor_scan", "fused_rotor_scan", "cayley", "cell_step", "ga3_rotor_scan", "rotor_step",
-           "RotorStepGraph", "BASIS"]
+__all__ = ["rotor_scan", "fused_rotor_scan", "fused_rotor_scan_heads", "cayley", "cell_step", "ga3_rotor_scan",
+           "rotor_step", "RotorStepGraph", "BASIS"]
 
 BASIS = {"triu": 0, "ga": 1}
 
@@ -128,21 +130,41 @@ def rotor_scan(M, C, two_sided: bool = True, h0=None, reverse: bool = False):
 
 
 # ---------------------------------------------------------------- fused rotor scan
-def _rotor_fwd(g, d, ga, s, hf, basis, two_sided, Mc=None, ws=None):
-    """Raw fused forward on float32 contiguous CUDA tensors -> X.  With Mc ([B, T, N, 16, 16],
-    D = 16 only) every step's rotor M_t is stored there for the backward.  `ws`: a workspace
-    of csn_rotor_scan_workspace_bytes to use (and keep for a reusing backward)."""
+def _rotor_dims(s):
+    """(B, T, H, Nh, D) of S: [B, T, N, D, D] is one dt per step (H = 0), [B, T, H, Nh, D, D]
+    one dt per head."""
+    if s.dim() == 6:
+        B, T, H, Nh, D, _ = s.shape
+        return B, T, H, Nh, D
     B, T, N, D, _ = s.shape
+    return B, T, 0, N, D
+
+
+def _rotor_ws_bytes(s):
+    B, T, H, Nh, D = _rotor_dims(s)
+    return _lib.load().csn_rotor_scan_workspace_bytes(B, T, max(H, 1) * Nh, D)
+
+
+def _rotor_fwd(g, d, ga, s, hf, basis, two_sided, Mc=None, ws=None):
+    """Raw fused forward on float32 contiguous CUDA tensors -> X.  S is [B, T, N, D, D] (dt
+    [B, T]) or the multi-head layout [B, T, H, Nh, D, D] (dt [B, T, H]).  With Mc (the shape
+    of S, D = 16 only) every step's rotor M_t is stored there for the backward.  `ws`: a
+    workspace of csn_rotor_scan_workspace_bytes to use (and keep for a reusing backward)."""
+    B, T, H, Nh, D = _rotor_dims(s)
     X = torch.empty_like(s)
-    ws_bytes = _lib.load().csn_rotor_scan_workspace_bytes(B, T, N, D)
+    ws_bytes = _rotor_ws_bytes(s)
     if ws is None:
         ws = _workspace(ws_bytes, s.device)
+    if H:
+        _lib.call("csn_rotor_scan_heads_fwd", _ptr(g), _ptr(d), _ptr(ga), _ptr(s), _ptr(hf), _ptr(X),
+                  _ptr(Mc), B, T, H, Nh, D, basis, int(two_sided), _ptr(ws), ws_bytes, _stream(s.device))
+        return X
     if Mc is not None:
         _lib.call("csn_rotor_scan_fwd_cached", _ptr(g), _ptr(d), _ptr(ga), _ptr(s), _ptr(hf), _ptr(X),
-                  _ptr(Mc), B, T, N, D, basis, int(two_sided), _ptr(ws), ws_bytes, _stream(s.device))
+                  _ptr(Mc), B, T, Nh, D, basis, int(two_sided), _ptr(ws), ws_bytes, _stream(s.device))
         return X
     _lib.call("csn_rotor_scan_fwd", _ptr(g), _ptr(d), _ptr(ga), _ptr(s), _ptr(hf), _ptr(X),
-              B, T, N, D, basis, int(two_sided), _ptr(ws), ws_bytes, _stream(s.device))
+              B, T, Nh, D, basis, int(two_sided), _ptr(ws), ws_bytes, _stream(s.device))
     return X
 
 
@@ -150,26 +172,32 @@ def _rotor_bwd(g, d, ga, s, hf, X, dXf, basis, two_sided, need_dh0, Mc=None, fwd
     """Raw fused adjoint -> (dgens, ddt, dgamma or None, dS, dh0 or None); Mc = the rotors
     stored by the forward (D = 16) or None to rebuild them; fwd_ws = the forward's workspace,
     whose chunk rotor products the backward then reuses."""
-    B, T, N, D, _ = s.shape
+    B, T, H, Nh, D = _rotor_dims(s)
     dg = torch.empty_like(g)
     ddt = torch.empty_like(d)
     dga = torch.empty_like(ga) if ga is not None else None
     dS = torch.empty_like(s)
     dh0 = torch.empty_like(hf) if (hf is not None and need_dh0) else None
-    ws_bytes = _lib.load().csn_rotor_scan_workspace_bytes(B, T, N, D)
+    ws_bytes = _rotor_ws_bytes(s)
+    if H:
+        ws = fwd_ws if fwd_ws is not None else _workspace(ws_bytes, s.device)
+        _lib.call("csn_rotor_scan_heads_bwd", _ptr(g), _ptr(d), _ptr(ga), _ptr(s), _ptr(hf), _ptr(X),
+                  _ptr(dXf), _ptr(Mc), _ptr(dg), _ptr(ddt), _ptr(dga), _ptr(dS), _ptr(dh0), B, T, H, Nh, D,
+                  basis, int(two_sided), int(fwd_ws is not None), _ptr(ws), ws_bytes, _stream(s.device))
+        return dg, ddt, dga, dS, dh0
+    if fwd_ws is not None and Mc is None:
+        _lib.call("csn_rotor_scan_bwd_reuse", _ptr(g), _ptr(d), _ptr(ga), _ptr(s), _ptr(hf), _ptr(X),
+                  _ptr(dXf), _ptr(dg), _ptr(ddt), _ptr(dga), _ptr(dS), _ptr(dh0), B, T, Nh, D,
+                  basis, int(two_sided), _ptr(fwd_ws), ws_bytes, _stream(s.device))
+        return dg, ddt, dga, dS, dh0
     ws = _workspace(ws_bytes, s.device)
     if Mc is not None:
         _lib.call("csn_rotor_scan_bwd_cached", _ptr(g), _ptr(d), _ptr(ga), _ptr(s), _ptr(hf), _ptr(X),
-                  _ptr(dXf), _ptr(Mc), _ptr(dg), _ptr(ddt), _ptr(dga), _ptr(dS), _ptr(dh0), B, T, N, D,
+                  _ptr(dXf), _ptr(Mc), _ptr(dg), _ptr(ddt), _ptr(dga), _ptr(dS), _ptr(dh0), B, T, Nh, D,
                   basis, int(two_sided), _ptr(ws), ws_bytes, _stream(s.device))
         return dg, ddt, dga, dS, dh0
-    if fwd_ws is not None:
-        _lib.call("csn_rotor_scan_bwd_reuse", _ptr(g), _ptr(d), _ptr(ga), _ptr(s), _ptr(hf), _ptr(X),
-                  _ptr(dXf), _ptr(dg), _ptr(ddt), _ptr(dga), _ptr(dS), _ptr(dh0), B, T, N, D,
-                  basis, int(two_sided), _ptr(fwd_ws), ws_bytes, _stream(s.device))
-        return dg, ddt, dga, dS, dh0
     _lib.call("csn_rotor_scan_bwd", _ptr(g), _ptr(d), _ptr(ga), _ptr(s), _ptr(hf), _ptr(X),
-              _ptr(dXf), _ptr(dg), _ptr(ddt), _ptr(dga), _ptr(dS), _ptr(dh0), B, T, N, D,
+              _ptr(dXf), _ptr(dg), _ptr(ddt), _ptr(dga), _ptr(dS), _ptr(dh0), B, T, Nh, D,
               basis, int(two_sided), _ptr(ws), ws_bytes, _stream(s.device))
     return dg, ddt, dga, dS, dh0
 
@@ -183,9 +211,7 @@ class RotorScanFunction(torch.autograd.Function):
         # of rebuilding them there
         Mc = torch.empty_like(s) if s.shape[-1] == 16 else None
         # D = 4, 8: keep the forward's workspace, whose chunk rotor products the backward reuses
-        B, T, N, D, _ = s.shape
-        ws = None if Mc is not None else _workspace(_lib.load().csn_rotor_scan_workspace_bytes(B, T, N, D),
-                                                   s.device)
+        ws = None if Mc is not None else _workspace(_rotor_ws_bytes(s), s.device)
         X = _rotor_fwd(g, d, ga, s, hf, basis, two_sided, Mc, ws)
         ctx.save_for_backward(g, d, ga, s, hf, X, Mc)
         ctx.fwd_ws = ws
@@ -217,6 +243,27 @@ def fused_rotor_scan(gens, dt, gamma, S, basis: str = "triu", two_sided: bool = 
     dt = dt.reshape(B, T)
     if gamma is not None:
         gamma = gamma.reshape(B, T, N)
+    if basis not in BASIS:
+        raise ValueError(f"basis must be one of {sorted(BASIS)}")
+    return RotorScanFunction.apply(gens, dt, gamma, S, h0, BASIS[basis], bool(two_sided))
+
+
+def fused_rotor_scan_heads(gens, dt, gamma, S, basis: str = "triu", two_sided: bool = True, h0=None):
+    """fused_rotor_scan on the multi-head layout, one dt per head (python/clifford_multihead.py:137-170).
+
+    gens [B, T, H, Nh, K], dt [B, T, H] (or [B, T, H, 1, 1, 1]), gamma [B, T, H, Nh] (or
+    [B, T, H, Nh, 1, 1]; None = undamped), S [B, T, H, Nh, D, D], h0 [B, H, Nh, D, D] ->
+    X [B, T, H, Nh, D, D].  Neuron (h, i) uses dt[b, t, h]; the reference's fold of heads into
+    the batch is read in place, so neither inputs nor X are transposed.
+    """
+    if S.dim() != 6:
+        raise ValueError("S must be [B, T, H, Nh, D, D]")
+    B, T, H, Nh, D, _ = S.shape
+    if H < 1:
+        raise ValueError("fused_rotor_scan_heads needs at least one head")
+    dt = dt.reshape(B, T, H)
+    if gamma is not None:
+        gamma = gamma.reshape(B, T, H, Nh)
     if basis not in BASIS:
         raise ValueError(f"basis must be one of {sorted(BASIS)}")
     return RotorScanFunction.apply(gens, dt, gamma, S, h0, BASIS[basis], bool(two_sided))

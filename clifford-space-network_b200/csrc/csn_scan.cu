@@ -19,6 +19,8 @@
 // The backward pass is the mirror image in reverse time with transitions M^T
 // (G_t = dX_t + M_{t+1}^T G_{t+1} M_{t+1}), chunk aggregates (P_j, c'_j) where
 // H_{j-1} = P_j^T H_j P_j + c'_j, and an apply pass that emits the gradients.
+#include <climits>
+#include <cstdio>
 #include <mutex>
 
 #include "csn_common.cuh"
@@ -33,7 +35,8 @@ template <int D, int BASIS, bool DAMPED, int K>
 __device__ __forceinline__ void rotor_transition(const ScanArgs& a, int64_t b, int64_t t,
                                                  int64_t e, Mat<D>& M, RotorStep<D, K>& r) {
   load_gens<K>(r.g, a.gens + e * K);
-  r.dt = __ldg(a.dt + b * a.T + tphys(a, t));
+  const int64_t tp = tphys(a, t);
+  r.dt = __ldg(a.dt + dt_index(a, b, tp, e - (b * a.T + tp) * a.N));
   build_I_minus_omega<D, BASIS, K>(M, r.g, 0.5f * r.dt);
   gj_inverse(M);  // M = A^{-1}
   if constexpr (DAMPED) {
@@ -426,7 +429,8 @@ int run_bwd(ScanArgs a, cudaStream_t st) {
   if (SRC == SRC_ROTOR && a.B * a.T > 0) {
     const int64_t BT = a.B * a.T;
     KernelTimer kt("reduce_channels", st);
-    reduce_channels_kernel<<<blocks_for(BT, 256), 256, 0, st>>>(a.ddt_part, a.ddt, BT, a.N);
+    const int64_t H = dt_heads(a);
+    reduce_channels_kernel<<<blocks_for(BT * H, 256), 256, 0, st>>>(a.ddt_part, a.ddt, BT * H, a.N / H);
   }
   return check_launch("scan backward");
 }
@@ -546,24 +550,102 @@ static int rotor_common_checks(const float* gens, const float* dt, const float* 
   return CSN_OK;
 }
 
-extern "C" int csn_rotor_scan_fwd(const float* gens, const float* dt, const float* gamma,
-                                  const float* S, const float* h0, float* X, int64_t B, int64_t T,
-                                  int64_t N, int D, int basis, int two_sided, void* workspace,
-                                  size_t workspace_bytes, void* stream) {
+namespace {
+
+int fail(int code, const char* fn, const char* what) {
+  char buf[320];
+  snprintf(buf, sizeof(buf), "%s: %s", fn, what);
+  return set_error(code, buf);
+}
+
+// H heads: the N channels are H groups of N / H neurons and dt holds one value per head,
+// [B, T, H] (H = 1: [B, T]); ddt has the shape of dt.
+int check_heads(const char* fn, int64_t N, int64_t H) {
+  if (H < 0 || (H == 0 && N != 0)) return fail(CSN_ERR_INVALID, fn, "the head count must be >= 1");
+  if (H > 1 && (N % H != 0 || N > INT32_MAX))
+    return fail(CSN_ERR_INVALID, fn, "channels must split evenly into heads (N = H * Nh < 2^31)");
+  return CSN_OK;
+}
+
+int zero_ddt(float* ddt, int64_t n, cudaStream_t st) {
+  if (n <= 0 || !ddt) return CSN_OK;
+  cudaError_t e = cudaMemsetAsync(ddt, 0, sizeof(float) * n, st);
+  return e == cudaSuccess ? CSN_OK : set_cuda_error(e, "cudaMemsetAsync(ddt)");
+}
+
+// Forward of every fused-rotor entry point.  Mc_out (D = 16 only): also store each step's M_t.
+int rotor_fwd_impl(const char* fn, const float* gens, const float* dt, const float* gamma,
+                   const float* S, const float* h0, float* X, float* Mc_out, int64_t B, int64_t T,
+                   int64_t N, int64_t H, int D, int basis, int two_sided, void* workspace,
+                   size_t workspace_bytes, cudaStream_t st) {
   if (int rc = rotor_common_checks(gens, dt, S, B, T, N, D, basis)) return rc;
+  if (int rc = check_heads(fn, N, H)) return rc;
+  if (Mc_out && D != 16) return fail(CSN_ERR_UNSUPPORTED, fn, "the rotor cache is for D = 16");
   if (B * T * N == 0) return CSN_OK;
-  if (!X || !aligned16(X) || (h0 && !aligned16(h0)))
-    return set_error(CSN_ERR_INVALID, "csn_rotor_scan_fwd: X missing or misaligned");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (!X || !aligned16(X) || (h0 && !aligned16(h0)) || (Mc_out && !aligned16(Mc_out)))
+    return fail(CSN_ERR_INVALID, fn, "X missing or X, h0, Mcache misaligned");
   Plan p = make_plan(B, T, N, D, false);
   Workspace ws;
   if (int rc = get_ws(ws, workspace, workspace_bytes, plan_bytes(p), st)) return rc;
   ScanArgs a{};
   a.gens = gens; a.dt = dt; a.gamma = gamma; a.S = S; a.h0 = h0; a.out = X;
   a.B = B; a.T = T; a.N = N;
+  a.dtH = H;
+  a.Mc_out = Mc_out;
   bind_ws(a, p, ws.base, D);
   if (D == 16) return scan16_dispatch(a, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, false, st);
   return dispatch(a, D, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, false, st);
+}
+
+// Adjoint of every fused-rotor entry point.  Mc_in (D = 16 only): the forward's stored
+// rotors; reuse: the workspace is the forward's, whose chunk products P_j are reused.
+int rotor_bwd_impl(const char* fn, const float* gens, const float* dt, const float* gamma,
+                   const float* S, const float* h0, const float* X, const float* dX,
+                   const float* Mc_in, float* dgens, float* ddt, float* dgamma, float* dS, float* dh0,
+                   int64_t B, int64_t T, int64_t N, int64_t H, int D, int basis, int two_sided,
+                   bool reuse, void* workspace, size_t workspace_bytes, cudaStream_t st) {
+  if (int rc = rotor_common_checks(gens, dt, S, B, T, N, D, basis)) return rc;
+  if (int rc = check_heads(fn, N, H)) return rc;
+  if (Mc_in && D != 16) return fail(CSN_ERR_UNSUPPORTED, fn, "the rotor cache is for D = 16");
+  if (B * T * N == 0) return zero_ddt(ddt, B * T * H, st);
+  if (!X || !dX || !dgens || !ddt || !dS || (gamma && !dgamma))
+    return fail(CSN_ERR_INVALID, fn, "missing X, dX or a gradient output");
+  if (!aligned16(X) || !aligned16(dX) || !aligned16(dS) || (h0 && !aligned16(h0)) ||
+      (dh0 && !aligned16(dh0)) || (Mc_in && !aligned16(Mc_in)))
+    return fail(CSN_ERR_INVALID, fn, "pointers must be 16-byte aligned");
+  if (dh0 && !h0) return fail(CSN_ERR_INVALID, fn, "dh0 needs h0");
+  Plan p = make_plan(B, T, N, D, true);
+  Workspace ws;
+  if (reuse) {
+    const size_t need = plan_bytes(p);
+    if (need > 256 && (!workspace || workspace_bytes < need))
+      return fail(CSN_ERR_INVALID, fn, "needs the forward's workspace (csn_rotor_scan_workspace_bytes)");
+    ws.base = static_cast<float*>(workspace);
+  } else if (int rc = get_ws(ws, workspace, workspace_bytes, plan_bytes(p), st)) {
+    return rc;
+  }
+  ScanArgs a{};
+  a.gens = gens; a.dt = dt; a.gamma = gamma; a.S = S; a.h0 = h0; a.X = X; a.dX = dX;
+  a.dgens = dgens; a.ddt = ddt; a.dgamma = dgamma; a.dC = dS; a.dh0 = dh0;
+  a.B = B; a.T = T; a.N = N;
+  a.dtH = H;
+  a.Mc_in = Mc_in;
+  a.reuse_P = reuse ? 1 : 0;
+  bind_ws(a, p, ws.base, D);
+  if (D == 16) return scan16_dispatch(a, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, true, st);
+  return dispatch(a, D, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, true, st);
+}
+
+cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+}  // namespace
+
+extern "C" int csn_rotor_scan_fwd(const float* gens, const float* dt, const float* gamma,
+                                  const float* S, const float* h0, float* X, int64_t B, int64_t T,
+                                  int64_t N, int D, int basis, int two_sided, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  return rotor_fwd_impl("csn_rotor_scan_fwd", gens, dt, gamma, S, h0, X, nullptr, B, T, N, 1, D, basis,
+                        two_sided, workspace, workspace_bytes, as_stream(stream));
 }
 
 extern "C" int csn_rotor_scan_bwd(const float* gens, const float* dt, const float* gamma,
@@ -572,31 +654,9 @@ extern "C" int csn_rotor_scan_bwd(const float* gens, const float* dt, const floa
                                   float* dS, float* dh0, int64_t B, int64_t T, int64_t N, int D,
                                   int basis, int two_sided, void* workspace,
                                   size_t workspace_bytes, void* stream) {
-  if (int rc = rotor_common_checks(gens, dt, S, B, T, N, D, basis)) return rc;
-  if (B * T * N == 0) {
-    if (B * T > 0 && ddt) {
-      cudaError_t e = cudaMemsetAsync(ddt, 0, sizeof(float) * B * T, static_cast<cudaStream_t>(stream));
-      if (e != cudaSuccess) return set_cuda_error(e, "cudaMemsetAsync(ddt)");
-    }
-    return CSN_OK;
-  }
-  if (!X || !dX || !dgens || !ddt || !dS || (gamma && !dgamma))
-    return set_error(CSN_ERR_INVALID, "csn_rotor_scan_bwd: missing X, dX or a gradient output");
-  if (!aligned16(X) || !aligned16(dX) || !aligned16(dS) || (h0 && !aligned16(h0)) ||
-      (dh0 && !aligned16(dh0)))
-    return set_error(CSN_ERR_INVALID, "csn_rotor_scan_bwd: pointers must be 16-byte aligned");
-  if (dh0 && !h0) return set_error(CSN_ERR_INVALID, "csn_rotor_scan_bwd: dh0 needs h0");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  Plan p = make_plan(B, T, N, D, true);
-  Workspace ws;
-  if (int rc = get_ws(ws, workspace, workspace_bytes, plan_bytes(p), st)) return rc;
-  ScanArgs a{};
-  a.gens = gens; a.dt = dt; a.gamma = gamma; a.S = S; a.h0 = h0; a.X = X; a.dX = dX;
-  a.dgens = dgens; a.ddt = ddt; a.dgamma = dgamma; a.dC = dS; a.dh0 = dh0;
-  a.B = B; a.T = T; a.N = N;
-  bind_ws(a, p, ws.base, D);
-  if (D == 16) return scan16_dispatch(a, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, true, st);
-  return dispatch(a, D, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, true, st);
+  return rotor_bwd_impl("csn_rotor_scan_bwd", gens, dt, gamma, S, h0, X, dX, nullptr, dgens, ddt, dgamma,
+                        dS, dh0, B, T, N, 1, D, basis, two_sided, false, workspace, workspace_bytes,
+                        as_stream(stream));
 }
 
 // ======================================================= backward after a forward
@@ -609,34 +669,9 @@ extern "C" int csn_rotor_scan_bwd_reuse(const float* gens, const float* dt, cons
                                         float* dS, float* dh0, int64_t B, int64_t T, int64_t N,
                                         int D, int basis, int two_sided, void* workspace,
                                         size_t workspace_bytes, void* stream) {
-  if (int rc = rotor_common_checks(gens, dt, S, B, T, N, D, basis)) return rc;
-  if (B * T * N == 0) {
-    if (B * T > 0 && ddt) {
-      cudaError_t e = cudaMemsetAsync(ddt, 0, sizeof(float) * B * T, static_cast<cudaStream_t>(stream));
-      if (e != cudaSuccess) return set_cuda_error(e, "cudaMemsetAsync(ddt)");
-    }
-    return CSN_OK;
-  }
-  if (!X || !dX || !dgens || !ddt || !dS || (gamma && !dgamma))
-    return set_error(CSN_ERR_INVALID, "csn_rotor_scan_bwd_reuse: missing X, dX or a gradient output");
-  if (!aligned16(X) || !aligned16(dX) || !aligned16(dS) || (h0 && !aligned16(h0)) ||
-      (dh0 && !aligned16(dh0)))
-    return set_error(CSN_ERR_INVALID, "csn_rotor_scan_bwd_reuse: pointers must be 16-byte aligned");
-  if (dh0 && !h0) return set_error(CSN_ERR_INVALID, "csn_rotor_scan_bwd_reuse: dh0 needs h0");
-  Plan p = make_plan(B, T, N, D, true);
-  const size_t need = plan_bytes(p);
-  if (need > 256 && (!workspace || workspace_bytes < need))
-    return set_error(CSN_ERR_INVALID,
-                     "csn_rotor_scan_bwd_reuse: needs the forward's workspace (csn_rotor_scan_workspace_bytes)");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  ScanArgs a{};
-  a.gens = gens; a.dt = dt; a.gamma = gamma; a.S = S; a.h0 = h0; a.X = X; a.dX = dX;
-  a.dgens = dgens; a.ddt = ddt; a.dgamma = dgamma; a.dC = dS; a.dh0 = dh0;
-  a.B = B; a.T = T; a.N = N;
-  a.reuse_P = 1;
-  bind_ws(a, p, static_cast<float*>(workspace), D);
-  if (D == 16) return scan16_dispatch(a, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, true, st);
-  return dispatch(a, D, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, true, st);
+  return rotor_bwd_impl("csn_rotor_scan_bwd_reuse", gens, dt, gamma, S, h0, X, dX, nullptr, dgens, ddt,
+                        dgamma, dS, dh0, B, T, N, 1, D, basis, two_sided, true, workspace,
+                        workspace_bytes, as_stream(stream));
 }
 
 // ======================================================= rotor cache (D = 16)
@@ -649,21 +684,14 @@ extern "C" int csn_rotor_scan_fwd_cached(const float* gens, const float* dt, con
                                          int64_t B, int64_t T, int64_t N, int D, int basis,
                                          int two_sided, void* workspace, size_t workspace_bytes,
                                          void* stream) {
-  if (int rc = rotor_common_checks(gens, dt, S, B, T, N, D, basis)) return rc;
-  if (D != 16) return set_error(CSN_ERR_UNSUPPORTED, "csn_rotor_scan_fwd_cached: the rotor cache is for D = 16");
-  if (B * T * N == 0) return CSN_OK;
-  if (!X || !aligned16(X) || (h0 && !aligned16(h0)) || !Mcache || !aligned16(Mcache))
-    return set_error(CSN_ERR_INVALID, "csn_rotor_scan_fwd_cached: X or Mcache missing or misaligned");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  Plan p = make_plan(B, T, N, D, false);
-  Workspace ws;
-  if (int rc = get_ws(ws, workspace, workspace_bytes, plan_bytes(p), st)) return rc;
-  ScanArgs a{};
-  a.gens = gens; a.dt = dt; a.gamma = gamma; a.S = S; a.h0 = h0; a.out = X;
-  a.B = B; a.T = T; a.N = N;
-  a.Mc_out = Mcache;
-  bind_ws(a, p, ws.base, D);
-  return scan16_dispatch(a, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, false, st);
+  if (D != 16) {
+    if (int rc = rotor_common_checks(gens, dt, S, B, T, N, D, basis)) return rc;
+    return set_error(CSN_ERR_UNSUPPORTED, "csn_rotor_scan_fwd_cached: the rotor cache is for D = 16");
+  }
+  if (B * T * N > 0 && !Mcache)
+    return set_error(CSN_ERR_INVALID, "csn_rotor_scan_fwd_cached: Mcache is required");
+  return rotor_fwd_impl("csn_rotor_scan_fwd_cached", gens, dt, gamma, S, h0, X, Mcache, B, T, N, 1, D,
+                        basis, two_sided, workspace, workspace_bytes, as_stream(stream));
 }
 
 extern "C" int csn_rotor_scan_bwd_cached(const float* gens, const float* dt, const float* gamma,
@@ -672,32 +700,42 @@ extern "C" int csn_rotor_scan_bwd_cached(const float* gens, const float* dt, con
                                          float* ddt, float* dgamma, float* dS, float* dh0, int64_t B,
                                          int64_t T, int64_t N, int D, int basis, int two_sided,
                                          void* workspace, size_t workspace_bytes, void* stream) {
-  if (int rc = rotor_common_checks(gens, dt, S, B, T, N, D, basis)) return rc;
-  if (D != 16) return set_error(CSN_ERR_UNSUPPORTED, "csn_rotor_scan_bwd_cached: the rotor cache is for D = 16");
-  if (B * T * N == 0) {
-    if (B * T > 0 && ddt) {
-      cudaError_t e = cudaMemsetAsync(ddt, 0, sizeof(float) * B * T, static_cast<cudaStream_t>(stream));
-      if (e != cudaSuccess) return set_cuda_error(e, "cudaMemsetAsync(ddt)");
-    }
-    return CSN_OK;
+  if (D != 16) {
+    if (int rc = rotor_common_checks(gens, dt, S, B, T, N, D, basis)) return rc;
+    return set_error(CSN_ERR_UNSUPPORTED, "csn_rotor_scan_bwd_cached: the rotor cache is for D = 16");
   }
-  if (!X || !dX || !dgens || !ddt || !dS || (gamma && !dgamma) || !Mcache)
-    return set_error(CSN_ERR_INVALID, "csn_rotor_scan_bwd_cached: missing X, dX, Mcache or a gradient output");
-  if (!aligned16(X) || !aligned16(dX) || !aligned16(dS) || !aligned16(Mcache) || (h0 && !aligned16(h0)) ||
-      (dh0 && !aligned16(dh0)))
-    return set_error(CSN_ERR_INVALID, "csn_rotor_scan_bwd_cached: pointers must be 16-byte aligned");
-  if (dh0 && !h0) return set_error(CSN_ERR_INVALID, "csn_rotor_scan_bwd_cached: dh0 needs h0");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  Plan p = make_plan(B, T, N, D, true);
-  Workspace ws;
-  if (int rc = get_ws(ws, workspace, workspace_bytes, plan_bytes(p), st)) return rc;
-  ScanArgs a{};
-  a.gens = gens; a.dt = dt; a.gamma = gamma; a.S = S; a.h0 = h0; a.X = X; a.dX = dX;
-  a.dgens = dgens; a.ddt = ddt; a.dgamma = dgamma; a.dC = dS; a.dh0 = dh0;
-  a.B = B; a.T = T; a.N = N;
-  a.Mc_in = Mcache;
-  bind_ws(a, p, ws.base, D);
-  return scan16_dispatch(a, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, true, st);
+  if (B * T * N > 0 && !Mcache)
+    return set_error(CSN_ERR_INVALID, "csn_rotor_scan_bwd_cached: Mcache is required");
+  return rotor_bwd_impl("csn_rotor_scan_bwd_cached", gens, dt, gamma, S, h0, X, dX, Mcache, dgens, ddt,
+                        dgamma, dS, dh0, B, T, N, 1, D, basis, two_sided, false, workspace,
+                        workspace_bytes, as_stream(stream));
+}
+
+// ======================================================= multi-head layout (per-head dt)
+// The H * Nh channels are H heads of Nh neurons with one dt per (b, t, head): the same
+// recurrence as folding the heads into the batch ([B * H, T, Nh]) and broadcasting each
+// head's dt over its neurons, read in place from the [B, T, H, Nh, ...] layout.
+extern "C" int csn_rotor_scan_heads_fwd(const float* gens, const float* dt, const float* gamma,
+                                        const float* S, const float* h0, float* X, float* Mcache,
+                                        int64_t B, int64_t T, int64_t H, int64_t Nh, int D, int basis,
+                                        int two_sided, void* workspace, size_t workspace_bytes,
+                                        void* stream) {
+  if (H < 0 || Nh < 0) return set_error(CSN_ERR_INVALID, "csn_rotor_scan_heads_fwd: negative dimension");
+  return rotor_fwd_impl("csn_rotor_scan_heads_fwd", gens, dt, gamma, S, h0, X, Mcache, B, T, H * Nh, H, D,
+                        basis, two_sided, workspace, workspace_bytes, as_stream(stream));
+}
+
+extern "C" int csn_rotor_scan_heads_bwd(const float* gens, const float* dt, const float* gamma,
+                                        const float* S, const float* h0, const float* X,
+                                        const float* dX, const float* Mcache, float* dgens,
+                                        float* ddt, float* dgamma, float* dS, float* dh0, int64_t B,
+                                        int64_t T, int64_t H, int64_t Nh, int D, int basis,
+                                        int two_sided, int reuse, void* workspace,
+                                        size_t workspace_bytes, void* stream) {
+  if (H < 0 || Nh < 0) return set_error(CSN_ERR_INVALID, "csn_rotor_scan_heads_bwd: negative dimension");
+  return rotor_bwd_impl("csn_rotor_scan_heads_bwd", gens, dt, gamma, S, h0, X, dX, Mcache, dgens, ddt,
+                        dgamma, dS, dh0, B, T, H * Nh, H, D, basis, two_sided, reuse != 0,
+                        workspace, workspace_bytes, as_stream(stream));
 }
 
 // ======================================================= no-allocation forward variant

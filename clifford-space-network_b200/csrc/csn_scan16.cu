@@ -417,7 +417,7 @@ __device__ __forceinline__ void step_matrix(const ScanArgs& a, const Warp& w, co
     alpha = sa = 1.0f;
     dtv = gam = 0.0f;
   } else {
-    dtv = __ldg(a.dt + w.b * a.T + tphys(a, t));
+    dtv = __ldg(a.dt + dt_index(a, w.b, tphys(a, t), w.n));
     if constexpr (DAMPED) {
       gam = __ldg(a.gamma + e);
       alpha = 1.0f / (1.0f + expf(gam * dtv));
@@ -782,7 +782,9 @@ int run16(const ScanArgs& a, bool bwd, cudaStream_t st) {
   if (SRC == SRC_ROTOR && a.B * a.T > 0) {
     const int64_t BT = a.B * a.T;
     KernelTimer kt("reduce_channels", st);
-    reduce_channels_kernel<<<(unsigned)((BT + 255) / 256), 256, 0, st>>>(a.ddt_part, a.ddt, BT, a.N);
+    const int64_t H = dt_heads(a);
+    reduce_channels_kernel<<<(unsigned)((BT * H + 255) / 256), 256, 0, st>>>(a.ddt_part, a.ddt, BT * H,
+                                                                            a.N / H);
   }
   return check_launch("scan backward (D=16)");
 }

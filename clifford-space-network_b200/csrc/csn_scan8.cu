@@ -195,7 +195,7 @@ __global__ void __launch_bounds__(THREADS, 2) fwd8_kernel(ScanArgs a) {
       const int64_t e = (b * a.T + t) * a.N + n;
       cp_async_floats<K>(slot + FwdSlot::G, a.gens + e * K);
       if (DAMPED) cp_async4(slot + FwdSlot::GAM, a.gamma + e);
-      cp_async4(slot + FwdSlot::DT, a.dt + b * a.T + t);
+      cp_async4(slot + FwdSlot::DT, a.dt + dt_index(a, b, t, n));
     }
   };
 
@@ -331,7 +331,7 @@ __global__ void __launch_bounds__(THREADS, 2) bwd8_reduce_kernel(ScanArgs a) {
     const int64_t e = (b * a.T + t) * a.N + n;
     cp_async_floats<K>(slot + BwdRedSlot::G, a.gens + e * K);
     if (DAMPED) cp_async4(slot + BwdRedSlot::GAM, a.gamma + e);
-    cp_async4(slot + BwdRedSlot::DT, a.dt + b * a.T + t);
+    cp_async4(slot + BwdRedSlot::DT, a.dt + dt_index(a, b, t, n));
   };
   auto issue_b = [&](int64_t t) {
     const int64_t e = (b * a.T + t) * a.N + n;
@@ -466,7 +466,7 @@ __global__ void __launch_bounds__(THREADS, 2) bwd8_apply_kernel(ScanArgs a) {
   if (me.len > 0) {
     const int64_t e = (b * a.T + t1 - 1) * a.N + n;
     if (DAMPED) gam_n = __ldg(a.gamma + e);
-    dt_n = __ldg(a.dt + b * a.T + t1 - 1);
+    dt_n = __ldg(a.dt + dt_index(a, b, t1 - 1, n));
   }
 
   Mat<8> H;
@@ -482,7 +482,7 @@ __global__ void __launch_bounds__(THREADS, 2) bwd8_apply_kernel(ScanArgs a) {
     if (st + 1 < me.len) {  // scalars of the next step, a full step ahead
       const int64_t e1 = (b * a.T + t - 1) * a.N + n;
       if (DAMPED) gam_n = __ldg(a.gamma + e1);
-      dt_n = __ldg(a.dt + b * a.T + t - 1);
+      dt_n = __ldg(a.dt + dt_index(a, b, t - 1, n));
     }
     // ---- 1. Cayley in registers (Xp, gens landed; S, dX may still be in flight)
     cp_async_wait<1>();
@@ -776,7 +776,9 @@ int run8(const ScanArgs& a, bool bwd, cudaStream_t st) {
   if (a.B * a.T > 0) {
     const int64_t BT = a.B * a.T;
     KernelTimer kt("reduce_channels", st);
-    reduce_channels_kernel<<<(unsigned)((BT + 255) / 256), 256, 0, st>>>(a.ddt_part, a.ddt, BT, a.N);
+    const int64_t H = dt_heads(a);
+    reduce_channels_kernel<<<(unsigned)((BT * H + 255) / 256), 256, 0, st>>>(a.ddt_part, a.ddt, BT * H,
+                                                                            a.N / H);
   }
   return check_launch("rotor scan backward (D=8)");
 }

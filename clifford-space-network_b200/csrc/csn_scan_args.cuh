@@ -53,6 +53,9 @@ struct ScanArgs {
   // Backward: aggP already holds each chunk's product P_j (left there by the forward on the
   // same generators), so the backward reduce pass computes only the gradient aggregates.
   int reuse_P;
+  // Per-head dt: with dtH > 1 the N channels are dtH heads of N / dtH neurons and dt (and
+  // ddt) is [B, T, dtH]; channel n reads head n / (N / dtH).  0 or 1: dt is [B, T].
+  int64_t dtH;
 };
 
 // Physical time of scan step t: the plain scan can run in reverse time (rev), i.e. scan
@@ -62,6 +65,16 @@ __device__ __forceinline__ int64_t tphys(const ScanArgs& a, int64_t t) { return 
 __device__ __forceinline__ int64_t elem(const ScanArgs& a, int64_t b, int64_t t, int64_t n) {
   return (b * a.T + tphys(a, t)) * a.N + n;
 }
+
+// Index of dt for batch b, physical time tp and channel n.
+__device__ __forceinline__ int64_t dt_index(const ScanArgs& a, int64_t b, int64_t tp, int64_t n) {
+  if (a.dtH <= 1) return b * a.T + tp;
+  const uint32_t nh = static_cast<uint32_t>(a.N / a.dtH);  // N < 2^31 (checked by the entry points)
+  return (b * a.T + tp) * a.dtH + static_cast<uint32_t>(n) / nh;
+}
+
+// Rows of the ddt reduction: ddt[b, t, h] = sum of the per-channel partials of head h.
+__host__ __device__ __forceinline__ int64_t dt_heads(const ScanArgs& a) { return a.dtH > 1 ? a.dtH : 1; }
 
 // ----------------------------------------------------------------- step sources
 enum Src : int { SRC_MC = 0, SRC_ROTOR = 1 };

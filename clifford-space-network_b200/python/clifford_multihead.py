@@ -1,0 +1,151 @@
+"""Multi-head Cl(6,0) block and LM, drop-in for python/clifford_multihead.py.
+
+Same parameters (state_dict keys and shapes), inputs and outputs as the reference's
+MultiHeadAdaptiveTime, MultiHeadCliffordCL6Block and MultiHeadCliffordLM
+(python/clifford_multihead.py:28-304).  The scan section (:137-173) -- skew generators,
+Omega, exact Cayley rotors, per-head decay, the fold of heads into the batch, M/C and the scan
+over [B*H, T, Nh] -- runs as ONE fused CUDA op (csn_b200.ops.fused_rotor_scan_heads) that reads
+the [B, T, H, Nh, ...] projections in place with one dt per head: nothing is folded, unfolded
+or transposed, and M, C and Q are never materialised.  Omega is still returned for the action
+regulariser of the LM.
+"""
+import math
+from typing import Dict, Optional, Tuple
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from csn_b200 import ops
+from python.clifford_cl6 import cayley_rotor_8x8, skew_from_generators  # noqa: F401 (re-export)
+from python.clifford_model import GeometricGatedLinearUnit, RiemannianGeodesicHead
+from python.clifford_scan import parallel_rotor_scan, surrogate_spike  # noqa: F401 (re-export)
+
+
+class MultiHeadAdaptiveTime(nn.Module):
+    """Per-head dt_t^(h) = softplus(W^(h) x_t + b^(h)) * dt_base, initialised at dt_base
+    (python/clifford_multihead.py:28-53).  Returns [B, T, H]."""
+
+    def __init__(self, d_model: int, num_heads: int, dt_base: float = 0.05):
+        super().__init__()
+        self.num_heads = num_heads
+        self.dt_base = dt_base
+        self.proj = nn.Linear(d_model, num_heads)
+        nn.init.zeros_(self.proj.weight)
+        nn.init.constant_(self.proj.bias, math.log(math.e - 1.0))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return F.softplus(self.proj(x)) * self.dt_base
+
+
+class MultiHeadCliffordCL6Block(nn.Module):
+    def __init__(self, d_model: int, num_heads: int = 3, num_neurons_per_head: int = 2,
+                 kernel_size: int = 4, dt_base: float = 0.05, spike_threshold: float = 0.1,
+                 spike_beta: float = 10.0):
+        super().__init__()
+        self.d_model = d_model
+        self.num_heads = num_heads
+        self.num_neurons_per_head = num_neurons_per_head
+        self.total_neurons = num_heads * num_neurons_per_head
+        self.dt_base = dt_base
+        self.spike_threshold = spike_threshold
+        self.spike_beta = spike_beta
+        self.ln_1 = nn.LayerNorm(d_model)
+        self.conv1d = nn.Conv1d(d_model, d_model, kernel_size=kernel_size, padding=kernel_size - 1,
+                                groups=d_model)
+        self.time_head = MultiHeadAdaptiveTime(d_model, num_heads=num_heads, dt_base=dt_base)
+        self.in_proj = nn.Linear(d_model, self.total_neurons * 64)
+        self.gamma_proj = nn.Linear(d_model, self.total_neurons)
+        self.biv_proj = nn.Linear(d_model, self.total_neurons * 28)
+        self.omega_scale = nn.Parameter(torch.ones(num_heads, num_neurons_per_head, 1) * 10.0)
+        self.W_mix = nn.Parameter(torch.randn(num_heads, num_neurons_per_head, num_neurons_per_head)
+                                  / math.sqrt(num_neurons_per_head))
+        self.out_proj = nn.Linear(self.total_neurons * 64, d_model)
+        self.ln_2 = nn.LayerNorm(d_model)
+        self.gglu = GeometricGatedLinearUnit(d_model, d_ffn=2 * d_model)
+        self.register_buffer("triu_u", torch.triu_indices(8, 8, offset=1)[0], persistent=False)
+        self.register_buffer("triu_v", torch.triu_indices(8, 8, offset=1)[1], persistent=False)
+
+    def forward(self, x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """x [B, T, d_model] -> (out [B, T, d_model], Omega [B, T, H, Nh, 8, 8], dt [B, T, H])."""
+        B, T, _ = x.shape
+        H, Nh = self.num_heads, self.num_neurons_per_head
+        residual = x
+        x_conv = F.silu(self.conv1d(self.ln_1(x).transpose(1, 2))[:, :, :T].transpose(1, 2))
+        dt = self.time_head(x_conv)                                          # [B, T, H]
+        S = self.in_proj(x_conv).view(B, T, H, Nh, 8, 8)
+        gamma = F.softplus(self.gamma_proj(x_conv)).view(B, T, H, Nh)
+        biv = self.biv_proj(x_conv).view(B, T, H, Nh, 28) * self.omega_scale
+        # lines 137-173 fused: per-head dt, heads read in place, X [B, T, H, Nh, 8, 8]
+        X = ops.fused_rotor_scan_heads(biv, dt, gamma, S)
+        Omega = skew_from_generators(biv, 8, self.triu_u, self.triu_v) * (0.5 * dt[..., None, None, None])
+        energy = torch.norm(X, dim=(-1, -2), keepdim=True)
+        X = X * surrogate_spike(energy, threshold=self.spike_threshold, beta=self.spike_beta)
+        X_mixed = torch.einsum("hmn,bthnrc->bthmrc", self.W_mix, X)
+        h = residual + self.out_proj(X_mixed.reshape(B, T, self.total_neurons * 64))
+        out = h + self.gglu(self.ln_2(h))
+        return out, Omega, dt
+
+
+class MultiHeadCliffordLM(nn.Module):
+    """Embedding, MultiHeadCliffordCL6Block stack, final LayerNorm and geodesic head, with the
+    reference's action / smoothness / time regularisers and per-head dt diagnostics
+    (python/clifford_multihead.py:197-304)."""
+
+    def __init__(self, vocab_size: int, d_model: int = 48, num_layers: int = 2, num_heads: int = 3,
+                 num_neurons_per_head: int = 2, dt_base: float = 0.05, kernel_size: int = 4,
+                 spike_threshold: float = 0.1, lambda_kin: float = 0.01, lambda_smooth: float = 0.005,
+                 lambda_time: float = 0.01):
+        super().__init__()
+        self.vocab_size = vocab_size
+        self.d_model = d_model
+        self.num_layers = num_layers
+        self.num_heads = num_heads
+        self.num_neurons_per_head = num_neurons_per_head
+        self.dt_base = dt_base
+        self.lambda_kin = lambda_kin
+        self.lambda_smooth = lambda_smooth
+        self.lambda_time = lambda_time
+        self.tok_emb = nn.Embedding(vocab_size, d_model)
+        self.blocks = nn.ModuleList([
+            MultiHeadCliffordCL6Block(d_model=d_model, num_heads=num_heads,
+                                      num_neurons_per_head=num_neurons_per_head, kernel_size=kernel_size,
+                                      dt_base=dt_base, spike_threshold=spike_threshold)
+            for _ in range(num_layers)])
+        self.ln_f = nn.LayerNorm(d_model)
+        self.head = RiemannianGeodesicHead(vocab_size=vocab_size, d_model=d_model)
+
+    def forward(self, idx: torch.Tensor, targets: Optional[torch.Tensor] = None
+                ) -> Tuple[torch.Tensor, Optional[torch.Tensor], Dict[str, float]]:
+        B, T = idx.shape
+        x = self.tok_emb(idx)
+        e_kin = e_smooth = t_smooth = 0.0
+        dts = []
+        for block in self.blocks:
+            x, Omega, dt = block(x)
+            dts.append(dt)
+            e_kin = e_kin + (Omega ** 2).mean()
+            if T > 1:
+                e_smooth = e_smooth + ((Omega[:, 1:] - Omega[:, :-1]) ** 2).mean()
+                t_smooth = t_smooth + (((dt[:, 1:] - dt[:, :-1]) / self.dt_base) ** 2).mean()
+            else:
+                e_smooth = e_smooth + torch.tensor(0.0, device=idx.device)
+                t_smooth = t_smooth + torch.tensor(0.0, device=idx.device)
+        logits = self.head(self.ln_f(x))
+        diagnostics: Dict[str, float] = {}
+        stacked = torch.stack(dts)  # [L, B, T, H]
+        for h in range(self.num_heads):
+            d = stacked[..., h]
+            diagnostics[f"head_{h}_mean_dt"] = d.mean().item()
+            diagnostics[f"head_{h}_min_dt"] = d.min().item()
+            diagnostics[f"head_{h}_max_dt"] = d.max().item()
+        loss = None
+        if targets is not None:
+            ce = F.cross_entropy(logits.view(-1, self.vocab_size), targets.view(-1))
+            action = self.lambda_kin * e_kin + self.lambda_smooth * e_smooth
+            time_pen = self.lambda_time * t_smooth
+            loss = ce + action + time_pen
+            diagnostics["ce_loss"] = ce.item()
+            diagnostics["action_loss"] = action.item()
+            diagnostics["time_loss"] = time_pen.item()
+        return logits, loss, diagnostics

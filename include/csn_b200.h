@@ -137,6 +137,29 @@ int csn_rotor_scan_bwd_cached(const float* gens, const float* dt, const float* g
                               int basis, int two_sided, void* workspace, size_t workspace_bytes,
                               void* stream);
 
+/* Multi-head layout with one dt per head (python/clifford_multihead.py:137-170): the
+ * N = H * Nh channels are H heads of Nh neurons and
+ *   gens [B,T,H,Nh,K], dt [B,T,H], gamma [B,T,H,Nh] (NULL = undamped), S, X, dX, dS
+ *   [B,T,H,Nh,D,D], h0, dh0 [B,H,Nh,D,D], ddt [B,T,H];
+ * neuron (h, i) uses dt[b,t,h].  The recurrence of every neuron is the one of
+ * csn_rotor_scan_fwd/bwd; the reference gets the same numbers by folding heads into the batch
+ * ([B*H, T, Nh], python/clifford_multihead.py:157-163) with transposed copies of Omega, S and
+ * the decay, which these entry points read in place instead.  ddt is summed over each head's
+ * neurons.  Workspace: csn_rotor_scan_workspace_bytes(B, T, H * Nh, D).
+ *   Mcache: NULL, or (D = 16 only, as csn_rotor_scan_fwd_cached / _bwd_cached) the step
+ *           rotors [B,T,H,Nh,16,16] that the forward stores and the backward loads;
+ *   reuse:  1 = the workspace is the one the forward used (as csn_rotor_scan_bwd_reuse). */
+int csn_rotor_scan_heads_fwd(const float* gens, const float* dt, const float* gamma,
+                             const float* S, const float* h0, float* X, float* Mcache,
+                             int64_t B, int64_t T, int64_t H, int64_t Nh, int D, int basis,
+                             int two_sided, void* workspace, size_t workspace_bytes, void* stream);
+int csn_rotor_scan_heads_bwd(const float* gens, const float* dt, const float* gamma,
+                             const float* S, const float* h0, const float* X, const float* dX,
+                             const float* Mcache, float* dgens, float* ddt, float* dgamma,
+                             float* dS, float* dh0, int64_t B, int64_t T, int64_t H, int64_t Nh,
+                             int D, int basis, int two_sided, int reuse, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
 /* Same computation and chunking as csn_rotor_scan_fwd (bit-identical results), for
  * callers that cannot allocate device memory: hosts that hand the whole GPU to their
  * own memory pool, or loops that must not allocate once running.  No counterpart in

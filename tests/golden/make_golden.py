@@ -20,9 +20,10 @@ functions called (paths relative to the reference root):
 * python/clifford_layer.py:14 CliffordTENNCell
 * python/clifford_cl6.py:71 CliffordCL6Block, python/clifford_cl8.py:92 CliffordCL8Block
 * csn_toolkit/csn/vision.py:56,113 CliffordSpatialRotorBlockCl4 / Cl8 (use_schulz=False)
+* python/clifford_multihead.py:56,197 MultiHeadCliffordCL6Block, MultiHeadCliffordLM
 
     python tests/golden/make_golden.py [group ...]     (groups: scans cayley rotor ga3 cells
-                                                        blocks spatial; default: all)
+                                                        blocks spatial multihead; default: all)
 """
 from __future__ import annotations
 
@@ -44,6 +45,7 @@ from python.clifford_scan import parallel_rotor_scan as ref_tree_scan  # noqa: E
 from python.clifford_cl6 import cayley_rotor_8x8, CliffordCL6Block  # noqa: E402
 from python.clifford_cl8 import cayley_rotor_16x16, cayley_rotor_4x4, CliffordCL8Block  # noqa: E402
 from python.clifford_layer import CliffordTENNCell  # noqa: E402
+from python.clifford_multihead import MultiHeadCliffordCL6Block, MultiHeadCliffordLM  # noqa: E402
 import csn.scan as ref_csn_scan  # noqa: E402
 import csn.rotors as ref_csn_rotors  # noqa: E402
 import csn.vision as ref_csn_vision  # noqa: E402
@@ -257,8 +259,33 @@ def spatial(rng):
         save(name, x=x, W=Wt, out=out, dx=x.grad, **sd, **grads)
 
 
+def multihead(rng):
+    """Multi-head Cl(6) block (per-head dt, head-folded scan) and a 2-layer multi-head LM."""
+    torch.manual_seed(int(rng.integers(1 << 30)))
+    blk = MultiHeadCliffordCL6Block(d_model=16, num_heads=2, num_neurons_per_head=2).double()
+    with torch.no_grad():  # per-head dt that varies per token
+        blk.time_head.proj.weight.normal_(0.0, 0.2)
+    x = t(rng.standard_normal((2, 12, 16))).requires_grad_(True)
+    W = t(rng.standard_normal((2, 12, 16)))
+    out, Omega, dt = blk(x)
+    (out * W).sum().backward()
+    sd = {f"param.{k}": v for k, v in blk.state_dict().items()}
+    grads = {f"grad.{k}": p.grad for k, p in blk.named_parameters()}
+    save("multihead_block", x=x, W=W, out=out, Omega=Omega, dt=dt, dx=x.grad, **sd, **grads)
+    torch.manual_seed(int(rng.integers(1 << 30)))
+    lm = MultiHeadCliffordLM(vocab_size=11, d_model=16, num_layers=2, num_heads=2).double()
+    idx = torch.as_tensor(rng.integers(0, 11, (2, 12)))
+    tgt = torch.as_tensor(rng.integers(0, 11, (2, 12)))
+    logits, loss, _ = lm(idx, tgt)
+    loss.backward()
+    sd = {f"param.{k}": v for k, v in lm.state_dict().items()}
+    grads = {f"grad.{k}": p.grad for k, p in lm.named_parameters()}
+    save("multihead_lm", idx=idx, targets=tgt, logits=logits, loss=loss, **sd, **grads)
+
+
 GROUPS = {"scans": (scans, 0), "cayley": (cayleys, 0), "rotor": (rotor_scans, 0), "ga3": (ga3, 0),
-          "cells": (cells, 0), "blocks": (blocks, 0), "spatial": (spatial, 1)}
+          "cells": (cells, 0), "blocks": (blocks, 0), "spatial": (spatial, 1),
+          "multihead": (multihead, 2)}
 
 
 def main(names):

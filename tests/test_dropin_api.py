@@ -63,6 +63,26 @@ def test_spatial_block_state_dict_matches_reference(golden, name, cls, kw):
     assert params(type(blk).__init__) == ["self", "in_channels", "num_neurons", "use_schulz"]
 
 
+@pytest.mark.parametrize("name,ctor", [
+    ("multihead_block", lambda: __import__("python.clifford_multihead", fromlist=["x"]).MultiHeadCliffordCL6Block(
+        16, num_heads=2, num_neurons_per_head=2)),
+    ("multihead_lm", lambda: __import__("python.clifford_multihead", fromlist=["x"]).MultiHeadCliffordLM(
+        vocab_size=11, d_model=16, num_layers=2, num_heads=2)),
+])
+def test_multihead_state_dict_matches_reference(golden, name, ctor):
+    g = golden(name)
+    ref_keys = {k[len("param."):]: tuple(v.shape) for k, v in g.items() if k.startswith("param.")}
+    m = ctor()
+    assert {k: tuple(v.shape) for k, v in m.state_dict().items()} == ref_keys
+    m.load_state_dict({k: torch.as_tensor(g["param." + k]) for k in ref_keys})
+    from python import clifford_multihead as mh
+    # python/clifford_multihead.py:62-71, :206-219
+    assert params(mh.MultiHeadCliffordCL6Block.__init__) == [
+        "self", "d_model", "num_heads", "num_neurons_per_head", "kernel_size", "dt_base", "spike_threshold",
+        "spike_beta"]
+    assert params(mh.MultiHeadCliffordLM.forward) == ["self", "idx", "targets"]
+
+
 def test_cell_parameters_match_reference():
     from python.clifford_layer import CliffordTENNCell
     cell = CliffordTENNCell(num_neurons=5, in_dim=4)

@@ -42,6 +42,37 @@ def test_block_forward_backward_matches_reference(golden, name):
         assert rel(p.grad, g["grad." + k]) < 1e-3, k
 
 
+def test_multihead_block_matches_reference(golden):
+    """python/clifford_multihead.py:56-194: per-head dt, head-folded fused scan."""
+    from python.clifford_multihead import MultiHeadCliffordCL6Block
+    g = golden("multihead_block")
+    blk = load_block(lambda: MultiHeadCliffordCL6Block(16, num_heads=2, num_neurons_per_head=2), g)
+    x = torch.tensor(g["x"], dtype=torch.float32, device=DEV, requires_grad=True)
+    out, Omega, dt = blk(x)
+    assert rel(out, g["out"]) < 1e-4
+    assert rel(Omega, g["Omega"]) < 1e-4 and rel(dt, g["dt"]) < 1e-5
+    (out * torch.tensor(g["W"], dtype=torch.float32, device=DEV)).sum().backward()
+    assert rel(x.grad, g["dx"]) < 1e-3
+    for k, p in blk.named_parameters():
+        assert rel(p.grad, g["grad." + k]) < 1e-3, k
+
+
+def test_multihead_lm_matches_reference(golden):
+    """python/clifford_multihead.py:197-304: logits, loss with the action / time penalties,
+    every parameter gradient."""
+    from python.clifford_multihead import MultiHeadCliffordLM
+    g = golden("multihead_lm")
+    lm = load_block(lambda: MultiHeadCliffordLM(vocab_size=11, d_model=16, num_layers=2, num_heads=2), g)
+    idx = torch.as_tensor(g["idx"], device=DEV)
+    logits, loss, diag = lm(idx, torch.as_tensor(g["targets"], device=DEV))
+    assert rel(logits, g["logits"]) < 1e-4
+    assert abs(loss.item() - float(g["loss"])) / abs(float(g["loss"])) < 1e-5
+    assert set(diag) >= {"head_0_mean_dt", "head_1_max_dt", "ce_loss", "action_loss", "time_loss"}
+    loss.backward()
+    for k, p in lm.named_parameters():
+        assert rel(p.grad, g["grad." + k]) < 1e-3, k
+
+
 @pytest.mark.parametrize("case", ["cell_a", "cell_b"])
 def test_cell_matches_reference(golden, case):
     from python.clifford_layer import CliffordTENNCell

@@ -271,6 +271,113 @@ def test_d16_rotor_cache_matches_uncached_entry_points(ops, basis, damped, two, 
                        None, 0, True, torch.empty_like(s8))
 
 
+def _heads_case(rng, B, T, H, Nh, D, basis, damped):
+    E, gens, _, gamma, S = _rotor_case(rng, B, T, H * Nh, D, basis, damped, gscale=8.0)
+    gens = gens.reshape(B, T, H, Nh, -1)
+    gamma = gamma.reshape(B, T, H, Nh) if damped else None
+    dt = rng.uniform(0.01, 0.1, (B, T, H))
+    return E, gens, dt, gamma, S.reshape(B, T, H, Nh, D, D)
+
+
+@pytest.mark.parametrize("D,basis", [(4, "triu"), (8, "triu"), (16, "ga")])
+@pytest.mark.parametrize("damped", [True, False], ids=["damped", "undamped"])
+@pytest.mark.parametrize("two", [True, False], ids=["two", "one"])
+def test_heads_layout_matches_oracle_on_folded_heads(ops, oracle, D, basis, damped, two):
+    """fused_rotor_scan_heads (one dt per head, [B, T, H, Nh, ...] read in place) against the
+    oracle on the reference's fold of heads into the batch, [B*H, T, Nh]
+    (python/clifford_multihead.py:157-170)."""
+    rng = np.random.default_rng(hash(("heads", D, basis, damped, two)) % 2**32)
+    B, T, H, Nh = (2, 150, 3, 2) if D < 16 else (1, 70, 2, 2)
+    E, gens, dt, gamma, S = _heads_case(rng, B, T, H, Nh, D, basis, damped)
+    h0 = rng.standard_normal((B, H, Nh, D, D))
+    W = rng.standard_normal((B, T, H, Nh, D, D))
+
+    def fold(a):
+        return np.swapaxes(a, 1, 2).reshape(B * H, T, *a.shape[3:])
+
+    def unfold(a):
+        return np.swapaxes(a.reshape(B, H, T, *a.shape[2:]), 1, 2)
+
+    h0f = h0.reshape(B * H, Nh, D, D)
+    gf = fold(gamma) if damped else None
+    Xr = oracle.rotor_scan_fwd(fold(gens), fold(dt), gf, fold(S), E, h0=h0f, two_sided=two)
+    dg, ddt, dgam, dS, dh0 = oracle.rotor_scan_bwd(fold(gens), fold(dt), gf, fold(S), E, Xr, fold(W),
+                                                   h0=h0f, two_sided=two)
+    tg, tdt, tS, th0 = cuda(gens, True), cuda(dt, True), cuda(S, True), cuda(h0, True)
+    tga = cuda(gamma, True) if damped else None
+    X = ops.fused_rotor_scan_heads(tg, tdt, tga, tS, basis=basis, two_sided=two, h0=th0)
+    assert X.shape == (B, T, H, Nh, D, D)
+    assert rel(X, unfold(Xr)) < FWD_TOL
+    (X * cuda(W)).sum().backward()
+    assert rel(tg.grad, unfold(dg)) < BWD_TOL
+    assert rel(tdt.grad, unfold(ddt)) < BWD_TOL
+    assert rel(tS.grad, unfold(dS)) < BWD_TOL
+    assert rel(th0.grad, dh0.reshape(B, H, Nh, D, D)) < BWD_TOL
+    if damped:
+        assert rel(tga.grad, unfold(dgam)) < BWD_TOL
+
+
+@pytest.mark.parametrize("D,basis", [(4, "triu"), (8, "triu"), (16, "triu")])
+@pytest.mark.parametrize("damped", [True, False], ids=["damped", "undamped"])
+@pytest.mark.parametrize("two", [True, False], ids=["two", "one"])
+def test_heads_layout_is_bit_identical_to_folded_entry_points(ops, D, basis, damped, two):
+    """The multi-head entry points run the same per-sequence arithmetic, chunking and ddt
+    summation order as the plain ones on the folded copies, so every output is bit-identical
+    (forward, reusing backward for D = 4, 8, cached rotors for D = 16)."""
+    rng = np.random.default_rng(hash(("heads-bits", D, damped, two)) % 2**32)
+    B, T, H, Nh = (2, 300, 3, 2) if D < 16 else (1, 120, 2, 2)
+    E, gens, dt, gamma, S = _heads_case(rng, B, T, H, Nh, D, basis, damped)
+    g, d, s = cuda(gens), cuda(dt), cuda(S)
+    ga = cuda(gamma) if damped else None
+    h0 = cuda(rng.standard_normal((B, H, Nh, D, D)))
+    dX = cuda(rng.standard_normal((B, T, H, Nh, D, D)))
+    bi = ops.BASIS[basis]
+
+    def fold(t):
+        return None if t is None else t.transpose(1, 2).reshape(B * H, T, *t.shape[3:]).contiguous()
+
+    def unfold(t):
+        return None if t is None else t.reshape(B, H, T, *t.shape[2:]).transpose(1, 2)
+
+    def state(Mc_like):
+        if D == 16:
+            return torch.empty_like(Mc_like), None
+        return None, torch.zeros(ops._rotor_ws_bytes(Mc_like), dtype=torch.uint8, device=DEV)
+
+    Mc_h, ws_h = state(s)
+    Mc_f, ws_f = state(fold(s))
+    Xh = ops._rotor_fwd(g, d, ga, s, h0, bi, two, Mc_h, ws_h)
+    Xf = ops._rotor_fwd(fold(g), fold(d), fold(ga), fold(s), h0.reshape(B * H, Nh, D, D), bi, two, Mc_f, ws_f)
+    assert torch.equal(Xh, unfold(Xf))
+    if D == 16:
+        assert torch.equal(Mc_h, unfold(Mc_f))
+    gh = ops._rotor_bwd(g, d, ga, s, h0, Xh, dX, bi, two, True, Mc_h, ws_h)
+    gf = ops._rotor_bwd(fold(g), fold(d), fold(ga), fold(s), h0.reshape(B * H, Nh, D, D), Xf, fold(dX), bi, two,
+                        True, Mc_f, ws_f)
+    names = ("dgens", "ddt", "dgamma", "dS")
+    for name, a_, b_ in zip(names, gh[:4], gf[:4]):
+        if b_ is not None:
+            assert torch.equal(a_, unfold(b_)), name
+    assert torch.equal(gh[4], gf[4].reshape(B, H, Nh, D, D))
+
+
+def test_heads_layout_without_neurons_zeroes_ddt(ops):
+    """Nh = 0: nothing to scan, and ddt [B, T, H] (the gradient of an unused dt) is zero."""
+    from csn_b200 import _lib
+    B, T, H, D = 2, 5, 3, 8
+    g = torch.zeros(B, T, H, 0, 28, device=DEV)
+    d = torch.full((B, T, H), 0.05, device=DEV)
+    s = torch.zeros(B, T, H, 0, D, D, device=DEV)
+    X = ops._rotor_fwd(g, d, None, s, None, 0, True)
+    assert X.shape == s.shape
+    ddt = torch.full_like(d, 7.0)
+    _lib.call("csn_rotor_scan_heads_bwd", ops._ptr(g), ops._ptr(d), None, ops._ptr(s), None, ops._ptr(X),
+              ops._ptr(X), None, ops._ptr(g), ops._ptr(ddt), None, ops._ptr(s), None, B, T, H, 0, D, 0, 1, 0,
+              None, 0, ops._stream(d.device))
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(ddt) == 0
+
+
 @pytest.mark.parametrize("D,basis", [(4, "triu"), (8, "triu"), (16, "ga")])
 @pytest.mark.parametrize("damped", [True, False], ids=["damped", "undamped"])
 @pytest.mark.parametrize("two", [True, False], ids=["two", "one"])

@@ -2,7 +2,7 @@
 """Throughput benchmark of the rotor-scan hot path (forward + backward).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload cl6_lm|cl3|cl8|gen|sp]
+                    [--workload cl6_lm|cl3|cl8|gen|sp|lm_train]
 
 Workloads (one "step" = one forward + backward pass over one batch of synthetic input,
 seeded, float32, shaped like the reference's configurations):
@@ -22,6 +22,8 @@ seeded, float32, shaped like the reference's configurations):
   p50 latency of one rotor step (graph-replayed) and tokens/s.
 * ``sp`` -- sequence-parallel long scan, Cl(6,0): B 8, L 2^20, C 64, time axis split over
   the torchrun ranks (strong scaling), forward + backward.
+* ``lm_train`` -- one training step of the whole Cl(6,0) LM around the scan (d_model 128,
+  4 blocks x 8 neurons, B32 L2048, AdamW): tokens/s, with the scan's share of the step.
 
 N > 1 runs under torchrun: every rank owns its own batch (independent sequences, no
 data-path collective: weak scaling); time is the max over ranks.  ``--impl reference``
@@ -712,6 +714,83 @@ def run_generation(args, ws, rank, local, cores):
     return 0
 
 
+def run_lm_train(args, ws, rank, local, cores):
+    """One training step of the Cl(6,0) LM of the Cl(6) LM config (vocab 65 uniform token ids,
+    d_model 128, 4 CliffordCL6Blocks x 8 neurons, B32 L2048, AdamW lr 1e-3): embedding, blocks
+    (ln_1 -> causal depthwise conv -> SiLU -> projections -> fused rotor scan -> spike -> mixed
+    out_proj -> GGLU), geodesic head, cross entropy + action + time penalties, backward, optimizer
+    step, diagnostics read back.  Tokens/s = B * L / step time (CUDA events around K steps)."""
+    config = {"workload": "cl6_lm_train_step", "batch": args.batch or 32, "seq_len": 2048, "d_model": 128,
+              "layers": args.layers or 4, "neurons": 8, "vocab": 65, "optimizer": "AdamW",
+              "l2": "inputs larger than L2 (each block's S is 134 MB)"}
+    metric = "Cl(6) LM training step tokens/s (fwd + bwd + AdamW)"
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "the reference LM is PyTorch source that "
+                              "is not on the GPU box; its scan is timed by the cl6_lm workload"}), flush=True)
+        return 0
+    import torch
+    from csn_b200 import _lib
+    from python.clifford_cl6 import CliffordCL6ForCausalLM
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    _lib.load()
+    torch.manual_seed(0)
+    B, T = config["batch"], config["seq_len"]
+    model = CliffordCL6ForCausalLM(vocab_size=65, d_model=128, num_layers=config["layers"], num_neurons=8).to(dev)
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-3)
+    gen = torch.Generator(device="cpu").manual_seed(0)
+    idx_h = torch.randint(0, 65, (B, T), generator=gen).pin_memory()
+    tgt_h = torch.randint(0, 65, (B, T), generator=gen).pin_memory()
+    idx, tgt = idx_h.to(dev), tgt_h.to(dev)
+
+    def step(i, t):
+        opt.zero_grad(set_to_none=True)
+        _, loss, diag = model(i, t)
+        loss.backward()
+        opt.step()
+        return diag
+
+    for _ in range(max(3, args.warmup)):
+        step(idx, tgt)
+    torch.cuda.synchronize()
+    _lib.timing_reset()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        _lib.timing_enable(True)
+        e0.record()
+        for _ in range(args.steps):
+            step(idx, tgt)
+        e1.record()
+        torch.cuda.synchronize()
+        _lib.timing_enable(False)
+    ms = e0.elapsed_time(e1) / args.steps
+    names = ("fwd_reduce", "fwd_carry", "fwd_apply", "bwd_reduce", "bwd_carry", "bwd_apply", "reduce_channels",
+             "spike_fwd", "spike_bwd", "layer_norm_fwd", "layer_norm_bwd", "layer_norm_param_reduce")
+    kt = {n: _lib.timing_read(n) for n in names}
+    launches = sum(c for _, c in kt.values())
+    _lib.timing_reset()
+    # end to end: token ids from pinned host memory every step, diagnostics (loss terms) back to host
+    t0 = time.perf_counter()
+    K = max(1, args.e2e_steps)
+    for _ in range(K):
+        step(idx_h.to(dev, non_blocking=True), tgt_h.to(dev, non_blocking=True))
+    torch.cuda.synchronize()
+    e2e_ms = (time.perf_counter() - t0) / K * 1e3
+    print(json.dumps({
+        "metric": metric, "value": B * T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
+        "scan_ms_per_step": sum(kt[n][0] for n in names[:7]) / args.steps,
+        "kernel_ms": {n: {"total_ms": t, "launches": c} for n, (t, c) in kt.items()},
+        "gpu_launches": launches, "clocks": clk.summary(),
+        "e2e": {"value": B * T / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": 2 * B * T * 8,
+                "d2h_bytes_per_step": 6 * 4, "timing": "wall clock per step: token ids pinned host -> device, "
+                "train step, diagnostics to host"},
+        "cpu_baseline": None}), flush=True)
+    return 0
+
+
 # ==================================================================================== main
 def main():
     ap = argparse.ArgumentParser()
@@ -719,7 +798,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="cl6_lm", choices=sorted(WORKLOADS) + ["gen", "sp"])
+    ap.add_argument("--workload", default="cl6_lm", choices=sorted(WORKLOADS) + ["gen", "sp", "lm_train"])
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=None, help="per-rank batch (profiling: smaller)")
@@ -731,6 +810,8 @@ def main():
         return run_generation(args, ws, rank, local, cores)
     if args.workload == "sp":
         return run_sequence_parallel(args, ws, rank, local, cores)
+    if args.workload == "lm_train":
+        return run_lm_train(args, ws, rank, local, cores)
     kw = {}
     if args.batch is not None:
         kw["batch"] = args.batch

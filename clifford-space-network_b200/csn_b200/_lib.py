@@ -64,6 +64,11 @@ SIGNATURES = {
     "csn_cell_workspace_bytes": ([_i64, _i64], _sz),
     "csn_cell_bwd": ([_f, _f, _f, _f, _f, ctypes.c_float, _f, _f, _f, _f, _f, _f, _i64, _i64, _i64,
                       _f, _sz, _f], _int),
+    "csn_spike_fwd": ([_f, _f, _i64, _int, ctypes.c_float, _f], _int),
+    "csn_spike_bwd": ([_f, _f, _f, _i64, _int, ctypes.c_float, ctypes.c_float, _f], _int),
+    "csn_layer_norm_fwd": ([_f, _f, _f, _f, _f, _f, _i64, _int, ctypes.c_float, _f], _int),
+    "csn_layer_norm_bwd_workspace_bytes": ([_i64, _int], _sz),
+    "csn_layer_norm_bwd": ([_f, _f, _f, _f, _f, _f, _f, _f, _i64, _int, _f, _sz, _f], _int),
     "csn_timing_enable": ([_int], _int),
     "csn_timing_reset": ([], _int),
     "csn_timing_read": ([ctypes.c_char_p, ctypes.POINTER(ctypes.c_double),

@@ -27,7 +27,7 @@ import torch
 from . import _lib
 
 __all__ = ["rotor_scan", "fused_rotor_scan", "fused_rotor_scan_heads", "cayley", "cell_step", "ga3_rotor_scan",
-           "rotor_step", "RotorStepGraph", "BASIS"]
+           "rotor_step", "RotorStepGraph", "state_spike", "layer_norm", "BASIS"]
 
 BASIS = {"triu": 0, "ga": 1}
 
@@ -454,6 +454,91 @@ class RotorStepGraph:
     def replay(self):
         self.graph.replay()
         return self.h
+
+
+# ------------------------------------------------------------ block kernels
+class StateSpikeFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, X, threshold, beta):
+        _require_cuda(X)
+        x = _f32(X)
+        D = x.shape[-1]
+        Xs = torch.empty_like(x)
+        _lib.call("csn_spike_fwd", _ptr(x), _ptr(Xs), x.numel() // (D * D), D, float(threshold),
+                  _stream(x.device))
+        ctx.save_for_backward(x)
+        ctx.threshold, ctx.beta, ctx.dtype = float(threshold), float(beta), X.dtype
+        return Xs.to(X.dtype)
+
+    @staticmethod
+    def backward(ctx, dXs):
+        (x,) = ctx.saved_tensors
+        g = _f32(dXs)
+        D = x.shape[-1]
+        dX = torch.empty_like(x)
+        _lib.call("csn_spike_bwd", _ptr(x), _ptr(g), _ptr(dX), x.numel() // (D * D), D, ctx.threshold, ctx.beta,
+                  _stream(x.device))
+        return dX.to(ctx.dtype), None, None
+
+
+def state_spike(X, threshold: float = 0.5, beta: float = 10.0):
+    """X * surrogate_spike(||X||_F, threshold, beta) over the last two (D x D) axes, as one CUDA
+    kernel each way (python/clifford_scan.py:90-116 applied as in python/clifford_cl6.py:174-176).
+    D in {4, 8, 16}."""
+    if X.dim() < 2 or X.shape[-1] != X.shape[-2] or X.shape[-1] not in (4, 8, 16):
+        raise ValueError(f"state_spike expects [..., D, D] with D in (4, 8, 16), got {tuple(X.shape)}")
+    return StateSpikeFunction.apply(X, threshold, beta)
+
+
+class LayerNormFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, bias, eps):
+        _require_cuda(x, weight, bias)
+        C = x.shape[-1]
+        xf, w, b = _f32(x), _f32(weight), _f32(bias)
+        R = xf.numel() // C
+        y = torch.empty_like(xf)
+        mean = torch.empty(R, device=xf.device)
+        rstd = torch.empty(R, device=xf.device)
+        _lib.call("csn_layer_norm_fwd", _ptr(xf), _ptr(w), _ptr(b), _ptr(y), _ptr(mean), _ptr(rstd), R, C,
+                  float(eps), _stream(xf.device))
+        ctx.save_for_backward(xf, w, mean, rstd)
+        ctx.dtypes = (x.dtype, weight.dtype, bias.dtype)
+        return y.to(x.dtype)
+
+    @staticmethod
+    def backward(ctx, dy):
+        xf, w, mean, rstd = ctx.saved_tensors
+        C = xf.shape[-1]
+        R = xf.numel() // C
+        g = _f32(dy)
+        dx = torch.empty_like(xf)
+        dw = torch.empty_like(w) if ctx.needs_input_grad[1] else None
+        db = torch.empty_like(w) if ctx.needs_input_grad[2] else None
+        nb = _lib.load().csn_layer_norm_bwd_workspace_bytes(R, C)
+        ws = _workspace(max(nb, 16), xf.device)
+        _lib.call("csn_layer_norm_bwd", _ptr(g), _ptr(xf), _ptr(mean), _ptr(rstd), _ptr(w), _ptr(dx), _ptr(dw),
+                  _ptr(db), R, C, _ptr(ws), nb, _stream(xf.device))
+        out = (dx.to(ctx.dtypes[0]), None if dw is None else dw.to(ctx.dtypes[1]),
+               None if db is None else db.to(ctx.dtypes[2]), None)
+        return out
+
+
+LAYER_NORM_MAX_C = 1024
+
+
+def layer_norm_supported(C: int) -> bool:
+    """Feature counts the CUDA LayerNorm handles (C % 4 == 0, C <= 1024)."""
+    return 0 < C <= LAYER_NORM_MAX_C and C % 4 == 0
+
+
+def layer_norm(x, weight, bias, eps: float = 1e-5):
+    """F.layer_norm(x, (C,), weight, bias, eps) over the last axis as one CUDA kernel each way
+    (the blocks' nn.LayerNorm, python/clifford_cl6.py:94,121,229); layer_norm_supported(C) only."""
+    C = x.shape[-1]
+    if not layer_norm_supported(C) or weight is None or bias is None:
+        raise ValueError(f"layer_norm: needs affine weight and bias and C % 4 == 0, C <= {LAYER_NORM_MAX_C}")
+    return LayerNormFunction.apply(x, weight, bias, eps)
 
 
 # torch.ops.csn.* registrations (needs the helpers above; imported last on purpose)

@@ -1,10 +1,15 @@
 """Cl(6,0) ~ M_8(R) block with adaptive dt, drop-in for python/clifford_cl6.py.
 
 ``CliffordCL6Block.forward`` keeps the reference's parameters, inputs and outputs
-(python/clifford_cl6.py:71-186) but runs lines 150-171 -- skew generator, Omega,
-exact Cayley rotor, decay, M/C construction and the scan -- as ONE fused CUDA op
-(csn_b200.ops.fused_rotor_scan): M and C are never materialised.  Omega is still
-returned for the action regulariser of the LM.
+(python/clifford_cl6.py:71-186) with the block's producer/consumer chain fused:
+  * lines 150-171 -- skew generator, Omega, exact Cayley rotor, decay, M/C construction and the
+    scan -- are ONE fused CUDA op (csn_b200.ops.fused_rotor_scan): M and C are never materialised;
+  * the event spike of lines 174-176 is one CUDA kernel each way (ops.state_spike);
+  * the inter-neuron mixing of line 179 is linear, so it is folded into out_proj's weight
+    (W_out (W_mix (x) I_64), a [d_model, N*64] matrix built per call): X_mixed is never formed;
+  * ln_1 / ln_2 run the CUDA LayerNorm kernels (csn_b200.modules.LayerNorm).
+Omega is still returned by forward(); CliffordCL6ForCausalLM takes its action regulariser from
+the generator coefficients instead (sum Omega^2 = 2 sum (0.5 dt biv)^2), so it never forms Omega.
 """
 import math
 from typing import Dict, Optional, Tuple
@@ -14,6 +19,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from csn_b200 import ops
+from csn_b200.modules import LayerNorm
 from python.clifford_model import GeometricGatedLinearUnit, RiemannianGeodesicHead
 from python.clifford_scan import parallel_rotor_scan, surrogate_spike  # noqa: F401 (re-export)
 
@@ -38,6 +44,33 @@ def cayley_rotor_8x8(Omega: torch.Tensor) -> torch.Tensor:
     return ops.cayley(Omega)
 
 
+def generator_action(biv: torch.Tensor, dt: torch.Tensor, D: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(Omega^2).mean() and ((Omega[:, 1:] - Omega[:, :-1])^2).mean() of the LMs' least-action
+    regulariser (python/clifford_cl6.py:257-262, clifford_cl8.py, clifford_multihead.py) from the
+    K generator coefficients, without forming Omega = skew(biv) * 0.5 dt: each coefficient
+    w = 0.5 dt biv sits at (u, v) and, negated, at (v, u) of a D x D matrix with a zero diagonal,
+    so a mean over Omega's D^2 entries is (2 K / D^2) times the mean over w.  biv [B, T, ..., K];
+    dt broadcasts against biv[..., 0] from the left ([B, T] or [B, T, H]).  The smoothness term is
+    0 for T = 1."""
+    K = biv.shape[-1]
+    ratio = 2.0 * K / float(D * D)
+    dtb = dt.reshape(*dt.shape, *([1] * (biv.dim() - dt.dim())))
+    w = biv * (0.5 * dtb)
+    e_kin = ratio * (w ** 2).mean()
+    if biv.shape[1] > 1:
+        e_smooth = ratio * ((w[:, 1:] - w[:, :-1]) ** 2).mean()
+    else:
+        e_smooth = torch.zeros((), device=biv.device, dtype=biv.dtype)
+    return e_kin, e_smooth
+
+
+def read_diagnostics(named: Dict[str, torch.Tensor]) -> Dict[str, float]:
+    """{name: float} of scalar tensors with one device -> host read for all of them."""
+    vals = torch.stack([torch.as_tensor(v).detach().float().reshape(()).to(next(iter(named.values())).device)
+                        for v in named.values()]).tolist()
+    return dict(zip(named.keys(), vals))
+
+
 def skew_from_generators(biv: torch.Tensor, D: int, triu_u: torch.Tensor, triu_v: torch.Tensor):
     skew = torch.zeros(*biv.shape[:-1], D, D, device=biv.device, dtype=biv.dtype)
     skew[..., triu_u, triu_v] = biv
@@ -54,7 +87,7 @@ class CliffordCL6Block(nn.Module):
         self.dt_base = dt_base
         self.spike_threshold = spike_threshold
         self.spike_beta = spike_beta
-        self.ln_1 = nn.LayerNorm(d_model)
+        self.ln_1 = LayerNorm(d_model)
         self.conv1d = nn.Conv1d(d_model, d_model, kernel_size=kernel_size, padding=kernel_size - 1,
                                 groups=d_model)
         self.time_head = AdaptiveTimeHead(d_model, dt_base=dt_base)
@@ -64,28 +97,39 @@ class CliffordCL6Block(nn.Module):
         self.omega_scale = nn.Parameter(torch.ones(num_neurons, 1) * 10.0)
         self.W_mix = nn.Parameter(torch.randn(num_neurons, num_neurons) / math.sqrt(num_neurons))
         self.out_proj = nn.Linear(num_neurons * 64, d_model)
-        self.ln_2 = nn.LayerNorm(d_model)
+        self.ln_2 = LayerNorm(d_model)
         self.gglu = GeometricGatedLinearUnit(d_model, d_ffn=2 * d_model)
         self.register_buffer("triu_u", torch.triu_indices(8, 8, offset=1)[0], persistent=False)
         self.register_buffer("triu_v", torch.triu_indices(8, 8, offset=1)[1], persistent=False)
 
-    def forward(self, x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    def mixed_out_weight(self) -> torch.Tensor:
+        """out_proj's weight with the mixing folded in: out_proj(mix(X)) = X W^T + b with
+        W[o, j*64 + rc] = sum_i W_out[o, i*64 + rc] W_mix[i, j] (python/clifford_cl6.py:179-184)."""
+        N = self.num_neurons
+        W = self.out_proj.weight.view(self.d_model, N, 64)
+        return torch.einsum("oir,ij->ojr", W, self.W_mix).reshape(self.d_model, N * 64)
+
+    def forward_core(self, x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """forward() without Omega: (out [B, T, d_model], biv [B, T, N, 28] (the scaled generator
+        coefficients, Omega = skew(biv) * 0.5 dt), dt [B, T])."""
         B, T, _ = x.shape
         N = self.num_neurons
         residual = x
         x_conv = F.silu(self.conv1d(self.ln_1(x).transpose(1, 2))[:, :, :T].transpose(1, 2))
-        dt = self.time_head(x_conv)                                   # [B, T, 1, 1, 1]
+        dt = self.time_head(x_conv).view(B, T)
         S = self.in_proj(x_conv).view(B, T, N, 8, 8)
         gamma = F.softplus(self.gamma_proj(x_conv))                   # [B, T, N]
         biv = self.biv_proj(x_conv).view(B, T, N, 28) * self.omega_scale
-        X_all = ops.fused_rotor_scan(biv, dt.view(B, T), gamma, S)     # lines 150-171 fused
-        Omega = skew_from_generators(biv, 8, self.triu_u, self.triu_v) * (0.5 * dt)
-        energy = torch.norm(X_all, dim=(-1, -2), keepdim=True)
-        X_spiked = X_all * surrogate_spike(energy, threshold=self.spike_threshold, beta=self.spike_beta)
-        feat = torch.einsum("ij,btjrc->btirc", self.W_mix, X_spiked).reshape(B, T, N * 64)
-        h = residual + self.out_proj(feat)
+        X_all = ops.fused_rotor_scan(biv, dt, gamma, S)               # lines 150-171 fused
+        X_spiked = ops.state_spike(X_all, self.spike_threshold, self.spike_beta)
+        h = residual + F.linear(X_spiked.view(B, T, N * 64), self.mixed_out_weight(), self.out_proj.bias)
         out = h + self.gglu(self.ln_2(h))
-        return out, Omega, dt.view(B, T)
+        return out, biv, dt
+
+    def forward(self, x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        out, biv, dt = self.forward_core(x)
+        Omega = skew_from_generators(biv, 8, self.triu_u, self.triu_v) * (0.5 * dt)[..., None, None, None]
+        return out, Omega, dt
 
     # ------------------------------------------------ O(1)-state generation (extension)
     def init_state(self, batch_size: int, device=None):
@@ -138,7 +182,7 @@ class CliffordCL6ForCausalLM(nn.Module):
             CliffordCL6Block(d_model=d_model, num_neurons=num_neurons, kernel_size=kernel_size,
                              dt_base=dt_base, spike_threshold=spike_threshold)
             for _ in range(num_layers)])
-        self.ln_f = nn.LayerNorm(d_model)
+        self.ln_f = LayerNorm(d_model)
         self.head = RiemannianGeodesicHead(vocab_size=vocab_size, d_model=d_model)
 
     def forward(self, idx: torch.Tensor, targets: Optional[torch.Tensor] = None):
@@ -149,23 +193,22 @@ class CliffordCL6ForCausalLM(nn.Module):
         t_loss = 0.0
         dts = []
         for block in self.blocks:
-            x, Omega, dt_t = block(x)
+            x, biv, dt_t = block.forward_core(x)
             dts.append(dt_t)
-            e_kin = e_kin + (Omega ** 2).mean()
+            kin, smooth = generator_action(biv, dt_t, 8)
+            e_kin = e_kin + kin
             if T > 1:
-                e_smooth = e_smooth + ((Omega[:, 1:] - Omega[:, :-1]) ** 2).mean()
+                e_smooth = e_smooth + smooth
                 t_loss = t_loss + (((dt_t[:, 1:] - dt_t[:, :-1]) / self.dt_base) ** 2).mean()
         logits = self.head(self.ln_f(x))
         stacked = torch.stack(dts)
-        diagnostics: Dict[str, float] = {"mean_dt": stacked.mean().item(), "min_dt": stacked.min().item(),
-                                         "max_dt": stacked.max().item()}
+        named = {"mean_dt": stacked.mean(), "min_dt": stacked.min(), "max_dt": stacked.max()}
         loss = None
         if targets is not None:
             ce = F.cross_entropy(logits.view(-1, self.vocab_size), targets.view(-1))
             action = self.lambda_kin * e_kin + self.lambda_smooth * e_smooth
             time_pen = self.lambda_time * t_loss
             loss = ce + action + time_pen
-            diagnostics["ce_loss"] = ce.item()
-            diagnostics["action_loss"] = float(action)
-            diagnostics["time_loss"] = float(time_pen)
+            named.update(ce_loss=ce, action_loss=action, time_loss=time_pen)
+        diagnostics: Dict[str, float] = read_diagnostics(named)
         return logits, loss, diagnostics

@@ -14,7 +14,8 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from csn_b200 import ops
-from python.clifford_cl6 import AdaptiveTimeHead, skew_from_generators
+from csn_b200.modules import LayerNorm
+from python.clifford_cl6 import AdaptiveTimeHead, generator_action, read_diagnostics, skew_from_generators
 from python.clifford_model import GeometricGatedLinearUnit, RiemannianGeodesicHead
 from python.clifford_scan import parallel_rotor_scan, surrogate_spike  # noqa: F401 (re-export)
 
@@ -42,7 +43,7 @@ class CliffordCL8Block(nn.Module):
         self.use_schulz = use_schulz
         self.is_spinor_bundle = is_spinor_bundle
         self.num_biv = 120
-        self.ln_1 = nn.LayerNorm(d_model)
+        self.ln_1 = LayerNorm(d_model)
         self.conv1d = nn.Conv1d(d_model, d_model, kernel_size=kernel_size, padding=kernel_size - 1,
                                 groups=d_model)
         self.time_head = AdaptiveTimeHead(d_model, dt_base=dt_base)
@@ -52,29 +53,39 @@ class CliffordCL8Block(nn.Module):
         self.omega_scale = nn.Parameter(torch.ones(num_neurons, 1) * 10.0)
         self.W_mix = nn.Parameter(torch.randn(num_neurons, num_neurons) / math.sqrt(num_neurons))
         self.out_proj = nn.Linear(num_neurons * 256, d_model)
-        self.ln_2 = nn.LayerNorm(d_model)
+        self.ln_2 = LayerNorm(d_model)
         self.gglu = GeometricGatedLinearUnit(d_model, d_ffn=2 * d_model)
         u, v = torch.triu_indices(16, 16, offset=1)
         self.register_buffer("triu_u", u, persistent=False)
         self.register_buffer("triu_v", v, persistent=False)
 
-    def forward(self, x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    def mixed_out_weight(self) -> torch.Tensor:
+        """out_proj's weight with the inter-neuron mixing folded in (python/clifford_cl8.py:189-193):
+        W[o, j*256 + rc] = sum_i W_out[o, i*256 + rc] W_mix[i, j]."""
+        N = self.num_neurons
+        W = self.out_proj.weight.view(self.d_model, N, 256)
+        return torch.einsum("oir,ij->ojr", W, self.W_mix).reshape(self.d_model, N * 256)
+
+    def forward_core(self, x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """forward() without Omega: (out, biv [B, T, N, 120] scaled generators, dt [B, T])."""
         B, T, _ = x.shape
         N = self.num_neurons
         residual = x
         x_conv = F.silu(self.conv1d(self.ln_1(x).transpose(1, 2))[:, :, :T].transpose(1, 2))
-        dt = self.time_head(x_conv)
+        dt = self.time_head(x_conv).view(B, T)
         S = self.in_proj(x_conv).view(B, T, N, 16, 16)
         gamma = F.softplus(self.gamma_proj(x_conv))
         biv = self.biv_proj(x_conv).view(B, T, N, self.num_biv) * self.omega_scale
-        X_all = ops.fused_rotor_scan(biv, dt.view(B, T), gamma, S, two_sided=not self.is_spinor_bundle)
-        Omega = skew_from_generators(biv, 16, self.triu_u, self.triu_v) * (0.5 * dt)
-        energy = torch.norm(X_all, dim=(-1, -2), keepdim=True)
-        X_spiked = X_all * surrogate_spike(energy, threshold=self.spike_threshold, beta=self.spike_beta)
-        feat = torch.einsum("ij,btjrc->btirc", self.W_mix, X_spiked).reshape(B, T, N * 256)
-        h = residual + self.out_proj(feat)
+        X_all = ops.fused_rotor_scan(biv, dt, gamma, S, two_sided=not self.is_spinor_bundle)
+        X_spiked = ops.state_spike(X_all, self.spike_threshold, self.spike_beta)
+        h = residual + F.linear(X_spiked.view(B, T, N * 256), self.mixed_out_weight(), self.out_proj.bias)
         out = h + self.gglu(self.ln_2(h))
-        return out, Omega, dt.view(B, T)
+        return out, biv, dt
+
+    def forward(self, x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        out, biv, dt = self.forward_core(x)
+        Omega = skew_from_generators(biv, 16, self.triu_u, self.triu_v) * (0.5 * dt)[..., None, None, None]
+        return out, Omega, dt
 
 
 class CliffordCL8ForCausalLM(nn.Module):
@@ -98,7 +109,7 @@ class CliffordCL8ForCausalLM(nn.Module):
                              dt_base=dt_base, spike_threshold=spike_threshold, use_schulz=use_schulz,
                              is_spinor_bundle=is_spinor_bundle)
             for _ in range(num_layers)])
-        self.ln_f = nn.LayerNorm(d_model)
+        self.ln_f = LayerNorm(d_model)
         self.head = RiemannianGeodesicHead(vocab_size=vocab_size, d_model=d_model)
 
     def forward(self, idx: torch.Tensor, targets: Optional[torch.Tensor] = None):
@@ -109,23 +120,22 @@ class CliffordCL8ForCausalLM(nn.Module):
         t_loss = 0.0
         dts = []
         for block in self.blocks:
-            x, Omega, dt_t = block(x)
+            x, biv, dt_t = block.forward_core(x)
             dts.append(dt_t)
-            e_kin = e_kin + (Omega ** 2).mean()
+            kin, smooth = generator_action(biv, dt_t, 16)
+            e_kin = e_kin + kin
             if T > 1:
-                e_smooth = e_smooth + ((Omega[:, 1:] - Omega[:, :-1]) ** 2).mean()
+                e_smooth = e_smooth + smooth
                 t_loss = t_loss + (((dt_t[:, 1:] - dt_t[:, :-1]) / self.dt_base) ** 2).mean()
         logits = self.head(self.ln_f(x))
         stacked = torch.stack(dts)
-        diagnostics: Dict[str, float] = {"mean_dt": stacked.mean().item(), "min_dt": stacked.min().item(),
-                                         "max_dt": stacked.max().item()}
+        named = {"mean_dt": stacked.mean(), "min_dt": stacked.min(), "max_dt": stacked.max()}
         loss = None
         if targets is not None:
             ce = F.cross_entropy(logits.view(-1, self.vocab_size), targets.view(-1))
             action = self.lambda_kin * e_kin + self.lambda_smooth * e_smooth
             time_pen = self.lambda_time * t_loss
             loss = ce + action + time_pen
-            diagnostics["ce_loss"] = ce.item()
-            diagnostics["action_loss"] = float(action)
-            diagnostics["time_loss"] = float(time_pen)
+            named.update(ce_loss=ce, action_loss=action, time_loss=time_pen)
+        diagnostics: Dict[str, float] = read_diagnostics(named)
         return logits, loss, diagnostics

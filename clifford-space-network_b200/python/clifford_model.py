@@ -3,7 +3,9 @@
 RiemannianGeodesicHead and GeometricGatedLinearUnit are plain PyTorch modules with the
 reference's parameters (python/clifford_model.py:24-75).  CliffordTENNBlock builds the
 reference's symmetric rational rotor Q = (I + Om)(I - Om) / (1 + |Om|^2/8)
-(python/clifford_model.py:165-180) in PyTorch and runs the scan on the CUDA library.
+(python/clifford_model.py:165-180) in PyTorch and runs the scan on the CUDA library; its
+spike is the CUDA state-spike kernel, its inter-neuron mixing is folded into out_proj's weight
+and its LayerNorms run the CUDA LayerNorm kernels, as in the Cl(6) block.
 """
 import math
 from typing import Optional, Tuple
@@ -12,7 +14,9 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from python.clifford_scan import parallel_rotor_scan, surrogate_spike
+from csn_b200 import ops
+from csn_b200.modules import LayerNorm
+from python.clifford_scan import parallel_rotor_scan, surrogate_spike  # noqa: F401 (re-export)
 
 
 class RiemannianGeodesicHead(nn.Module):
@@ -51,7 +55,7 @@ class CliffordTENNBlock(nn.Module):
         self.num_neurons = num_neurons
         self.spike_threshold = spike_threshold
         self.spike_beta = spike_beta
-        self.ln_1 = nn.LayerNorm(d_model)
+        self.ln_1 = LayerNorm(d_model)
         self.conv1d = nn.Conv1d(d_model, d_model, kernel_size=kernel_size, padding=kernel_size - 1,
                                 groups=d_model)
         self.in_proj = nn.Linear(d_model, num_neurons * 16)
@@ -60,7 +64,7 @@ class CliffordTENNBlock(nn.Module):
         self.omega_scale = nn.Parameter(torch.ones(num_neurons, 1) * 10.0)
         self.W_mix = nn.Parameter(torch.randn(num_neurons, num_neurons) * (1.0 / math.sqrt(num_neurons)))
         self.out_proj = nn.Linear(num_neurons * 16, d_model)
-        self.ln_2 = nn.LayerNorm(d_model)
+        self.ln_2 = LayerNorm(d_model)
         self.gglu = GeometricGatedLinearUnit(d_model, d_ffn=2 * d_model)
         u, v = torch.triu_indices(4, 4, offset=1)
         self.register_buffer("_triu_u", u, persistent=False)
@@ -82,10 +86,11 @@ class CliffordTENNBlock(nn.Module):
         denom = 1.0 + 0.25 * (0.5 * torch.sum(Omega ** 2, dim=(-1, -2), keepdim=True))
         Q = torch.matmul(eye + Omega, eye - Omega) / denom
         X_all = parallel_rotor_scan(torch.sqrt(decay) * Q, (1.0 - decay) * S)
-        energy = torch.norm(X_all, dim=(-1, -2), keepdim=True)
-        X_spiked = X_all * surrogate_spike(energy, threshold=self.spike_threshold, beta=self.spike_beta)
-        feat = torch.einsum("ij,btjrc->btirc", self.W_mix, X_spiked).reshape(B, T, self.num_neurons * 16)
-        h = residual + self.out_proj(feat)
+        X_spiked = ops.state_spike(X_all, self.spike_threshold, self.spike_beta)
+        N = self.num_neurons
+        # mixing folded into out_proj: W[o, j*16 + rc] = sum_i W_out[o, i*16 + rc] W_mix[i, j]
+        W = torch.einsum("oir,ij->ojr", self.out_proj.weight.view(self.d_model, N, 16), self.W_mix)
+        h = residual + F.linear(X_spiked.reshape(B, T, N * 16), W.reshape(self.d_model, N * 16), self.out_proj.bias)
         return h + self.gglu(self.ln_2(h)), Omega
 
 
@@ -102,7 +107,7 @@ class CliffordTENNForCausalLM(nn.Module):
         self.tok_emb = nn.Embedding(vocab_size, d_model)
         self.blocks = nn.ModuleList([CliffordTENNBlock(d_model, num_neurons, kernel_size, spike_threshold)
                                      for _ in range(num_layers)])
-        self.ln_f = nn.LayerNorm(d_model)
+        self.ln_f = LayerNorm(d_model)
         self.head = RiemannianGeodesicHead(vocab_size=vocab_size, d_model=d_model)
 
     def forward(self, idx: torch.Tensor, dt: float = 0.05, targets: Optional[torch.Tensor] = None):

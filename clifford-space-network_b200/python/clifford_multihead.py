@@ -6,8 +6,10 @@ MultiHeadAdaptiveTime, MultiHeadCliffordCL6Block and MultiHeadCliffordLM
 Omega, exact Cayley rotors, per-head decay, the fold of heads into the batch, M/C and the scan
 over [B*H, T, Nh] -- runs as ONE fused CUDA op (csn_b200.ops.fused_rotor_scan_heads) that reads
 the [B, T, H, Nh, ...] projections in place with one dt per head: nothing is folded, unfolded
-or transposed, and M, C and Q are never materialised.  Omega is still returned for the action
-regulariser of the LM.
+or transposed, and M, C and Q are never materialised.  The spike is one CUDA kernel each way,
+the per-head mixing is folded into out_proj's weight and the LayerNorms run the CUDA kernels,
+as in the Cl(6) block.  Omega is still returned by forward(); the LM takes its action
+regulariser from the generator coefficients instead.
 """
 import math
 from typing import Dict, Optional, Tuple
@@ -17,7 +19,9 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from csn_b200 import ops
-from python.clifford_cl6 import cayley_rotor_8x8, skew_from_generators  # noqa: F401 (re-export)
+from csn_b200.modules import LayerNorm
+from python.clifford_cl6 import (cayley_rotor_8x8, generator_action, read_diagnostics,  # noqa: F401
+                                 skew_from_generators)
 from python.clifford_model import GeometricGatedLinearUnit, RiemannianGeodesicHead
 from python.clifford_scan import parallel_rotor_scan, surrogate_spike  # noqa: F401 (re-export)
 
@@ -50,7 +54,7 @@ class MultiHeadCliffordCL6Block(nn.Module):
         self.dt_base = dt_base
         self.spike_threshold = spike_threshold
         self.spike_beta = spike_beta
-        self.ln_1 = nn.LayerNorm(d_model)
+        self.ln_1 = LayerNorm(d_model)
         self.conv1d = nn.Conv1d(d_model, d_model, kernel_size=kernel_size, padding=kernel_size - 1,
                                 groups=d_model)
         self.time_head = MultiHeadAdaptiveTime(d_model, num_heads=num_heads, dt_base=dt_base)
@@ -61,13 +65,20 @@ class MultiHeadCliffordCL6Block(nn.Module):
         self.W_mix = nn.Parameter(torch.randn(num_heads, num_neurons_per_head, num_neurons_per_head)
                                   / math.sqrt(num_neurons_per_head))
         self.out_proj = nn.Linear(self.total_neurons * 64, d_model)
-        self.ln_2 = nn.LayerNorm(d_model)
+        self.ln_2 = LayerNorm(d_model)
         self.gglu = GeometricGatedLinearUnit(d_model, d_ffn=2 * d_model)
         self.register_buffer("triu_u", torch.triu_indices(8, 8, offset=1)[0], persistent=False)
         self.register_buffer("triu_v", torch.triu_indices(8, 8, offset=1)[1], persistent=False)
 
-    def forward(self, x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-        """x [B, T, d_model] -> (out [B, T, d_model], Omega [B, T, H, Nh, 8, 8], dt [B, T, H])."""
+    def mixed_out_weight(self) -> torch.Tensor:
+        """out_proj's weight with the block-diagonal head mixing folded in
+        (python/clifford_multihead.py:184-191): W[o, (h, n, rc)] = sum_m W_out[o, (h, m, rc)] W_mix[h, m, n]."""
+        H, Nh = self.num_heads, self.num_neurons_per_head
+        W = self.out_proj.weight.view(self.d_model, H, Nh, 64)
+        return torch.einsum("ohmr,hmn->ohnr", W, self.W_mix).reshape(self.d_model, H * Nh * 64)
+
+    def forward_core(self, x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """forward() without Omega: (out, biv [B, T, H, Nh, 28] scaled generators, dt [B, T, H])."""
         B, T, _ = x.shape
         H, Nh = self.num_heads, self.num_neurons_per_head
         residual = x
@@ -78,12 +89,15 @@ class MultiHeadCliffordCL6Block(nn.Module):
         biv = self.biv_proj(x_conv).view(B, T, H, Nh, 28) * self.omega_scale
         # lines 137-173 fused: per-head dt, heads read in place, X [B, T, H, Nh, 8, 8]
         X = ops.fused_rotor_scan_heads(biv, dt, gamma, S)
-        Omega = skew_from_generators(biv, 8, self.triu_u, self.triu_v) * (0.5 * dt[..., None, None, None])
-        energy = torch.norm(X, dim=(-1, -2), keepdim=True)
-        X = X * surrogate_spike(energy, threshold=self.spike_threshold, beta=self.spike_beta)
-        X_mixed = torch.einsum("hmn,bthnrc->bthmrc", self.W_mix, X)
-        h = residual + self.out_proj(X_mixed.reshape(B, T, self.total_neurons * 64))
+        X = ops.state_spike(X, self.spike_threshold, self.spike_beta)
+        h = residual + F.linear(X.view(B, T, self.total_neurons * 64), self.mixed_out_weight(), self.out_proj.bias)
         out = h + self.gglu(self.ln_2(h))
+        return out, biv, dt
+
+    def forward(self, x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """x [B, T, d_model] -> (out [B, T, d_model], Omega [B, T, H, Nh, 8, 8], dt [B, T, H])."""
+        out, biv, dt = self.forward_core(x)
+        Omega = skew_from_generators(biv, 8, self.triu_u, self.triu_v) * (0.5 * dt[..., None, None, None])
         return out, Omega, dt
 
 
@@ -112,7 +126,7 @@ class MultiHeadCliffordLM(nn.Module):
                                       num_neurons_per_head=num_neurons_per_head, kernel_size=kernel_size,
                                       dt_base=dt_base, spike_threshold=spike_threshold)
             for _ in range(num_layers)])
-        self.ln_f = nn.LayerNorm(d_model)
+        self.ln_f = LayerNorm(d_model)
         self.head = RiemannianGeodesicHead(vocab_size=vocab_size, d_model=d_model)
 
     def forward(self, idx: torch.Tensor, targets: Optional[torch.Tensor] = None
@@ -122,30 +136,29 @@ class MultiHeadCliffordLM(nn.Module):
         e_kin = e_smooth = t_smooth = 0.0
         dts = []
         for block in self.blocks:
-            x, Omega, dt = block(x)
+            x, biv, dt = block.forward_core(x)
             dts.append(dt)
-            e_kin = e_kin + (Omega ** 2).mean()
+            kin, smooth = generator_action(biv, dt, 8)
+            e_kin = e_kin + kin
+            e_smooth = e_smooth + smooth
             if T > 1:
-                e_smooth = e_smooth + ((Omega[:, 1:] - Omega[:, :-1]) ** 2).mean()
                 t_smooth = t_smooth + (((dt[:, 1:] - dt[:, :-1]) / self.dt_base) ** 2).mean()
             else:
-                e_smooth = e_smooth + torch.tensor(0.0, device=idx.device)
                 t_smooth = t_smooth + torch.tensor(0.0, device=idx.device)
         logits = self.head(self.ln_f(x))
-        diagnostics: Dict[str, float] = {}
         stacked = torch.stack(dts)  # [L, B, T, H]
+        named = {}
         for h in range(self.num_heads):
             d = stacked[..., h]
-            diagnostics[f"head_{h}_mean_dt"] = d.mean().item()
-            diagnostics[f"head_{h}_min_dt"] = d.min().item()
-            diagnostics[f"head_{h}_max_dt"] = d.max().item()
+            named[f"head_{h}_mean_dt"] = d.mean()
+            named[f"head_{h}_min_dt"] = d.min()
+            named[f"head_{h}_max_dt"] = d.max()
         loss = None
         if targets is not None:
             ce = F.cross_entropy(logits.view(-1, self.vocab_size), targets.view(-1))
             action = self.lambda_kin * e_kin + self.lambda_smooth * e_smooth
             time_pen = self.lambda_time * t_smooth
             loss = ce + action + time_pen
-            diagnostics["ce_loss"] = ce.item()
-            diagnostics["action_loss"] = action.item()
-            diagnostics["time_loss"] = time_pen.item()
+            named.update(ce_loss=ce, action_loss=action, time_loss=time_pen)
+        diagnostics: Dict[str, float] = read_diagnostics(named)
         return logits, loss, diagnostics

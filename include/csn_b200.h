@@ -274,6 +274,31 @@ int csn_cell_bwd(const float* prev, const float* x, const float* W_rec, const fl
                  float* dW_rec, float* dW_in, float* dgamma_bias, int64_t Bt, int64_t N,
                  int64_t in_dim, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------- block kernels around the scan */
+/* Event spike of the scan output (python/clifford_scan.py:90-116 surrogate_spike on the
+ * Frobenius energy, python/clifford_cl6.py:174-176, clifford_cl8.py:184-186,
+ * clifford_multihead.py:176-178, clifford_model.py:190-192): for each of the n D x D states,
+ *   Xs = X * [||X||_F - threshold >= 0]
+ * and the surrogate adjoint (fast sigmoid 1 / (1 + beta |e - threshold|)^2 on the energy e):
+ *   dX = [e >= threshold] dXs + (<dXs, X> / (1 + beta |e - threshold|)^2 / e) X   (0 at e = 0).
+ * D in {4, 8, 16}; pointers 16-byte aligned. */
+int csn_spike_fwd(const float* X, float* Xs, int64_t n, int D, float threshold, void* stream);
+int csn_spike_bwd(const float* X, const float* dXs, float* dX, int64_t n, int D, float threshold,
+                  float beta, void* stream);
+
+/* LayerNorm over rows of C features (nn.LayerNorm(C, eps) of the blocks' ln_1 / ln_2 and the
+ * LM's ln_f, python/clifford_cl6.py:94,121,229 applied at :140,184,272): y = (x - mean) * rstd * weight + bias,
+ * rstd = 1 / sqrt(biased var + eps); mean and rstd [R] are kept for the backward.
+ * 0 < C <= 1024, C % 4 == 0 (CSN_ERR_UNSUPPORTED otherwise); x, y, dy, dx, weight 16-byte
+ * aligned.  The backward writes dx [R, C] and, when given, dweight and dbias [C]; its
+ * workspace holds per-CTA partial sums (csn_layer_norm_bwd_workspace_bytes). */
+int csn_layer_norm_fwd(const float* x, const float* weight, const float* bias, float* y, float* mean,
+                       float* rstd, int64_t R, int C, float eps, void* stream);
+size_t csn_layer_norm_bwd_workspace_bytes(int64_t R, int C);
+int csn_layer_norm_bwd(const float* dy, const float* x, const float* mean, const float* rstd,
+                       const float* weight, float* dx, float* dweight, float* dbias, int64_t R, int C,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
 /* -------------------------------------------------------------- kernel timing */
 /* Measurement hook with no counterpart in the reference (which times with wall clock,
  * tests/profile_performance.py:41-71).  While enabled, every kernel the library

@@ -69,6 +69,15 @@ SIGNATURES = {
     "csn_layer_norm_fwd": ([_f, _f, _f, _f, _f, _f, _i64, _int, ctypes.c_float, _f], _int),
     "csn_layer_norm_bwd_workspace_bytes": ([_i64, _int], _sz),
     "csn_layer_norm_bwd": ([_f, _f, _f, _f, _f, _f, _f, _f, _i64, _int, _f, _sz, _f], _int),
+    "csn_ln_conv_silu_fwd": ([_f, _f, _f, _f, _f, _f, _f, _f, _i64, _i64, _int, _int, ctypes.c_float, _f], _int),
+    "csn_ln_conv_silu_bwd_workspace_bytes": ([_i64, _i64, _int, _int], _sz),
+    "csn_ln_conv_silu_bwd": ([_f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _i64, _i64, _int, _int, _f,
+                              _sz, _f], _int),
+    "csn_generator_action_workspace_bytes": ([_i64, _i64], _sz),
+    "csn_generator_action_fwd": ([_f, _f, _i64, _i64, _int, _int, ctypes.c_float, ctypes.c_float, _f, _f, _sz, _f],
+                                 _int),
+    "csn_generator_action_bwd": ([_f, _f, _f, _f, _i64, _i64, _int, _int, ctypes.c_float, ctypes.c_float, _f, _f,
+                                  _f], _int),
     "csn_timing_enable": ([_int], _int),
     "csn_timing_reset": ([], _int),
     "csn_timing_read": ([ctypes.c_char_p, ctypes.POINTER(ctypes.c_double),

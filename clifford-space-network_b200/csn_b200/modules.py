@@ -19,3 +19,19 @@ class LayerNorm(nn.LayerNorm):
                 and ops.layer_norm_supported(C)):
             return ops.layer_norm(x, self.weight, self.bias, self.eps)
         return F.layer_norm(x, self.normalized_shape, self.weight, self.bias, self.eps)
+
+
+def causal_conv_input(ln: nn.LayerNorm, conv: nn.Conv1d, x: torch.Tensor) -> torch.Tensor:
+    """x_conv = silu(conv(ln(x).transpose(1, 2))[:, :, :T].transpose(1, 2)) of the blocks
+    (python/clifford_cl6.py:140-142), as the fused CUDA kernels when the layers have the blocks'
+    form (affine LayerNorm over C; depthwise, bias, stride 1, dilation 1, left padding K - 1
+    conv) and the sizes fit them; otherwise the same chain of library layers."""
+    T = x.shape[1]
+    C = x.shape[-1]
+    K = conv.kernel_size[0]
+    if (x.dim() == 3 and len(ln.normalized_shape) == 1 and ln.weight is not None and ln.bias is not None
+            and conv.groups == C == conv.in_channels == conv.out_channels and conv.bias is not None
+            and conv.stride == (1,) and conv.dilation == (1,) and conv.padding == (K - 1,)
+            and conv.padding_mode == "zeros" and ops.ln_conv_silu_supported(C, K)):
+        return ops.ln_conv_silu(x, ln.weight, ln.bias, ln.eps, conv.weight, conv.bias)
+    return F.silu(conv(ln(x).transpose(1, 2))[:, :, :T].transpose(1, 2))

@@ -21,13 +21,15 @@ Ops (reference functions they replace, paths relative to the reference root):
 from __future__ import annotations
 
 import ctypes
+import math
 
 import torch
 
 from . import _lib
 
 __all__ = ["rotor_scan", "fused_rotor_scan", "fused_rotor_scan_heads", "cayley", "cell_step", "ga3_rotor_scan",
-           "rotor_step", "RotorStepGraph", "state_spike", "layer_norm", "BASIS"]
+           "rotor_step", "RotorStepGraph", "state_spike", "layer_norm", "ln_conv_silu",
+           "generator_action", "BASIS"]
 
 BASIS = {"triu": 0, "ga": 1}
 
@@ -539,6 +541,104 @@ def layer_norm(x, weight, bias, eps: float = 1e-5):
     if not layer_norm_supported(C) or weight is None or bias is None:
         raise ValueError(f"layer_norm: needs affine weight and bias and C % 4 == 0, C <= {LAYER_NORM_MAX_C}")
     return LayerNormFunction.apply(x, weight, bias, eps)
+
+
+class LnConvSiluFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, ln_w, ln_b, eps, conv_w, conv_b):
+        _require_cuda(x, ln_w, ln_b, conv_w, conv_b)
+        B, T, C = x.shape
+        K = conv_w.shape[-1]
+        xf, lw, lb, cw, cb = _f32(x), _f32(ln_w), _f32(ln_b), _f32(conv_w), _f32(conv_b)
+        y = torch.empty_like(xf)
+        mean = torch.empty(B * T, device=xf.device)
+        rstd = torch.empty(B * T, device=xf.device)
+        _lib.call("csn_ln_conv_silu_fwd", _ptr(xf), _ptr(lw), _ptr(lb), _ptr(cw), _ptr(cb), _ptr(y), _ptr(mean),
+                  _ptr(rstd), B, T, C, K, float(eps), _stream(xf.device))
+        ctx.save_for_backward(xf, lw, lb, cw, cb, mean, rstd)
+        ctx.dtypes = (x.dtype, ln_w.dtype, ln_b.dtype, conv_w.dtype, conv_b.dtype)
+        return y.to(x.dtype)
+
+    @staticmethod
+    def backward(ctx, dy):
+        xf, lw, lb, cw, cb, mean, rstd = ctx.saved_tensors
+        B, T, C = xf.shape
+        K = cw.shape[-1]
+        g = _f32(dy)
+        dx = torch.empty_like(xf)
+        need = ctx.needs_input_grad
+        dlw = torch.empty_like(lw) if need[1] else None
+        dlb = torch.empty_like(lb) if need[2] else None
+        dcw = torch.empty_like(cw) if need[4] else None
+        dcb = torch.empty_like(cb) if need[5] else None
+        nb = _lib.load().csn_ln_conv_silu_bwd_workspace_bytes(B, T, C, K)
+        ws = _workspace(max(nb, 16), xf.device)
+        _lib.call("csn_ln_conv_silu_bwd", _ptr(g), _ptr(xf), _ptr(mean), _ptr(rstd), _ptr(lw), _ptr(lb), _ptr(cw),
+                  _ptr(cb), _ptr(dx), _ptr(dlw), _ptr(dlb), _ptr(dcw), _ptr(dcb), B, T, C, K, _ptr(ws), nb,
+                  _stream(xf.device))
+        outs = (dx, dlw, dlb, None, dcw, dcb)
+        dts = (ctx.dtypes[0], ctx.dtypes[1], ctx.dtypes[2], None, ctx.dtypes[3], ctx.dtypes[4])
+        return tuple(None if o is None else o.to(d) for o, d in zip(outs, dts))
+
+
+def ln_conv_silu_supported(C: int, K: int) -> bool:
+    """Shapes the fused ln -> causal conv -> SiLU kernels handle (C % 4 == 0, C <= 256, K <= 4)."""
+    return 0 < C <= 256 and C % 4 == 0 and 1 <= K <= 4
+
+
+def ln_conv_silu(x, ln_weight, ln_bias, eps, conv_weight, conv_bias):
+    """silu(causal_depthwise_conv1d(layer_norm(x))) over x [B, T, C] as one CUDA kernel each way:
+    the blocks' python/clifford_cl6.py:140-142 (LayerNorm(C, eps), Conv1d(C, C, K, padding=K-1,
+    groups=C) keeping the first T outputs, SiLU).  conv_weight [C, 1, K]."""
+    B, T, C = x.shape
+    K = conv_weight.shape[-1]
+    if not ln_conv_silu_supported(C, K) or tuple(conv_weight.shape) != (C, 1, K) or conv_bias is None:
+        raise ValueError("ln_conv_silu: needs C % 4 == 0, C <= 256, K <= 4, a [C, 1, K] depthwise weight and a bias")
+    return LnConvSiluFunction.apply(x, ln_weight, ln_bias, eps, conv_weight, conv_bias)
+
+
+class GeneratorActionFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, biv, dt, D):
+        _require_cuda(biv, dt)
+        B, T = biv.shape[:2]
+        H = dt.shape[2] if dt.dim() == 3 else 1
+        bf, df = _f32(biv), _f32(dt)
+        R = math.prod(biv.shape[2:])
+        K = biv.shape[-1]
+        ratio = 2.0 * K / float(D * D)
+        ck = ratio / max(1, B * T * R)
+        cs = ratio / max(1, B * (T - 1) * R) if T > 1 else 0.0
+        out = torch.empty(2, device=bf.device)
+        nb = _lib.load().csn_generator_action_workspace_bytes(B, T)
+        ws = _workspace(max(nb, 16), bf.device)
+        _lib.call("csn_generator_action_fwd", _ptr(bf), _ptr(df), B, T, R, H, ck, cs, _ptr(out), _ptr(ws), nb,
+                  _stream(bf.device))
+        ctx.save_for_backward(bf, df)
+        ctx.meta = (B, T, R, H, ck, cs, biv.dtype, dt.dtype)
+        return out[0].to(biv.dtype), out[1].to(biv.dtype)
+
+    @staticmethod
+    def backward(ctx, g_kin, g_smooth):
+        bf, df = ctx.saved_tensors
+        B, T, R, H, ck, cs, bdt, ddt_type = ctx.meta
+        gk = None if g_kin is None else _f32(g_kin.reshape(1))
+        gs = None if g_smooth is None else _f32(g_smooth.reshape(1))
+        dbiv = torch.empty_like(bf) if ctx.needs_input_grad[0] else None
+        ddt = torch.empty_like(df) if ctx.needs_input_grad[1] else None
+        _lib.call("csn_generator_action_bwd", _ptr(bf), _ptr(df), _ptr(gk), _ptr(gs), B, T, R, H, ck, cs, _ptr(dbiv),
+                  _ptr(ddt), _stream(bf.device))
+        return (None if dbiv is None else dbiv.to(bdt), None if ddt is None else ddt.to(ddt_type), None)
+
+
+def generator_action(biv, dt, D: int):
+    """(Omega^2).mean() and ((Omega[:, 1:] - Omega[:, :-1])^2).mean() for Omega = skew(biv) * 0.5 dt
+    (D x D, K = biv.shape[-1] generators) without forming Omega -- the LMs' least-action terms
+    (python/clifford_cl6.py:257-262) as one CUDA kernel each way.  biv [B, T, ..., K]; dt [B, T]
+    (one dt per step) or [B, T, H] (one per head: biv [B, T, H, ..., K])."""
+    if biv.dim() < 3 or dt.shape[:2] != biv.shape[:2] or dt.dim() > 3:
+        raise ValueError("generator_action: biv [B, T, ..., K] and dt [B, T] or [B, T, H]")
+    return GeneratorActionFunction.apply(biv, dt, int(D))
 
 
 # torch.ops.csn.* registrations (needs the helpers above; imported last on purpose)

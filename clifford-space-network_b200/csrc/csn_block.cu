@@ -13,6 +13,24 @@
 //   dx = rstd (g dy - mean(g dy) - xhat mean(g dy xhat)),  dg = sum_rows dy xhat,  db = sum_rows dy
 // One warp per row, the row in registers (C <= 1024, C % 4 == 0); the parameter gradients
 // are summed per CTA and then over CTAs by a second kernel.
+//
+// The blocks' input chain ln_1 -> causal depthwise conv1d (kernel K, left zero padding) -> SiLU
+// (python/clifford_cl6.py:140-142), fused:
+//   y[b, t, c] = silu(cb[c] + sum_{j<K} cw[c, j] ln[b, t - K + 1 + j, c]),  ln rows t < 0 are 0
+// One warp walks a chunk of time steps of one sequence with the last K LayerNorm rows in a
+// register ring, so x is read once and neither the transposed, padded nor pre-activation
+// tensors exist.  The backward walks the same chunk (plus K - 1 rows of look-ahead) with rings
+// of LayerNorm rows and conv-output gradients:
+//   du_t = dy_t silu'(u_t),  dln_s = sum_j cw[:, j] du_{s + K - 1 - j},  then the LayerNorm adjoint;
+// conv weight / bias and LayerNorm weight / bias gradients are summed per CTA, then over CTAs.
+//
+// Least-action terms of the LMs (python/clifford_cl6.py:257-262) on the generator coefficients
+// w[b, t, j] = 0.5 dt[b, t, head(j)] biv[b, t, j] (row of R = N * K coefficients, H heads of R / H):
+//   S_kin = sum w^2,  S_smooth = sum_{t >= 1} (w_t - w_{t-1})^2
+// and the adjoint for dL/de_kin, dL/de_smooth with e = c S (c given by the caller):
+//   dw_t = 2 c_k g_k w_t + 2 c_s g_s ((w_t - w_{t-1}) [t >= 1] - (w_{t+1} - w_t) [t <= T - 2])
+//   dbiv = 0.5 dt dw,  ddt[b, t, h] = sum_{j in head h} 0.5 biv dw
+// The gradient scalars are read on the device, so no host synchronisation is needed.
 #include <cstdio>
 
 #include "csn_common.cuh"
@@ -284,6 +302,465 @@ int ln_check(const char* fn, int64_t R, int C) {
   return CSN_OK;
 }
 
+// ------------------------------------------------------- ln -> causal conv -> SiLU
+// C <= 128 * NV, K <= 4.
+template <int NV>
+__device__ __forceinline__ void load_row_params(const float* __restrict__ p, int C4, int lane, float4 (&out)[NV]) {
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int j = lane + 32 * k;
+    out[k] = j < C4 ? __ldg(reinterpret_cast<const float4*>(p) + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
+// cw [C, 1, K]: tap j of the 4 channels of float4 column jc
+template <int NV, int K>
+__device__ __forceinline__ void load_conv_taps(const float* __restrict__ cw, int C4, int lane, float4 (&w)[K][NV]) {
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int jc = lane + 32 * k;
+#pragma unroll
+    for (int j = 0; j < K; ++j)
+      w[j][k] = jc < C4 ? make_float4(__ldg(cw + (4 * jc + 0) * K + j), __ldg(cw + (4 * jc + 1) * K + j),
+                                      __ldg(cw + (4 * jc + 2) * K + j), __ldg(cw + (4 * jc + 3) * K + j))
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
+// LayerNorm of one row (warp-collective): out = (x - mu) rs g + b
+template <int NV>
+__device__ __forceinline__ void ln_row(const float* __restrict__ xr, int C4, int lane, float inv_c, float eps,
+                                       const float4 (&g)[NV], const float4 (&b)[NV], float4 (&out)[NV],
+                                       float& mu, float& rs) {
+  float4 v[NV];
+  float s = 0.0f;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int j = lane + 32 * k;
+    v[k] = j < C4 ? __ldg(reinterpret_cast<const float4*>(xr) + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+    s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+  }
+  mu = group_sum<32>(s) * inv_c;
+  float q = 0.0f;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    if (lane + 32 * k < C4) {
+      const float a = v[k].x - mu, bb = v[k].y - mu, c = v[k].z - mu, d = v[k].w - mu;
+      q += (a * a + bb * bb) + (c * c + d * d);
+    }
+  }
+  rs = rsqrtf(group_sum<32>(q) * inv_c + eps);
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    if (lane + 32 * k < C4)
+      out[k] = make_float4((v[k].x - mu) * rs * g[k].x + b[k].x, (v[k].y - mu) * rs * g[k].y + b[k].y,
+                           (v[k].z - mu) * rs * g[k].z + b[k].z, (v[k].w - mu) * rs * g[k].w + b[k].w);
+    else
+      out[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
+__device__ __forceinline__ float silu_f(float u) { return u / (1.0f + expf(-u)); }
+// d silu / du = s (1 + u (1 - s)), s = sigmoid(u)
+__device__ __forceinline__ float silu_grad(float u) {
+  const float s = 1.0f / (1.0f + expf(-u));
+  return s * (1.0f + u * (1.0f - s));
+}
+
+__device__ __forceinline__ float4 fma4(const float4& a, const float4& b, const float4& c) {
+  return make_float4(fmaf(a.x, b.x, c.x), fmaf(a.y, b.y, c.y), fmaf(a.z, b.z, c.z), fmaf(a.w, b.w, c.w));
+}
+
+template <int NV, int K>
+__global__ void __launch_bounds__(256) lnconv_fwd_kernel(const float* __restrict__ x, const float* __restrict__ lg,
+                                                         const float* __restrict__ lb, const float* __restrict__ cw,
+                                                         const float* __restrict__ cb, float* __restrict__ y,
+                                                         float* __restrict__ mean_out, float* __restrict__ rstd_out,
+                                                         int64_t B, int64_t T, int C, int TCH, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int C4 = C >> 2;
+  const float inv_c = 1.0f / (float)C;
+  float4 g[NV], lbv[NV], bias[NV], w[K][NV];
+  load_row_params<NV>(lg, C4, lane, g);
+  load_row_params<NV>(lb, C4, lane, lbv);
+  load_row_params<NV>(cb, C4, lane, bias);
+  load_conv_taps<NV, K>(cw, C4, lane, w);
+  const int64_t nch = (T + TCH - 1) / TCH;
+  const int64_t items = B * nch;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t it = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); it < items; it += warps) {
+    const int64_t b = it / nch;
+    const int64_t t0 = (it % nch) * TCH;
+    const int64_t t1 = min(T, t0 + (int64_t)TCH);
+    float4 ring[K][NV];  // ring[K - 1] = newest row
+#pragma unroll
+    for (int q = 0; q < K; ++q)
+#pragma unroll
+      for (int k = 0; k < NV; ++k) ring[q][k] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int q = 0; q + 1 < K; ++q) {  // rows t0 - K + 1 .. t0 - 1 into ring[1 .. K - 1]
+      const int64_t tau = t0 - (K - 1) + q;
+      if (tau >= 0) {
+        float mu, rs;
+        ln_row<NV>(x + (b * T + tau) * C, C4, lane, inv_c, eps, g, lbv, ring[q + 1], mu, rs);
+      }
+    }
+    for (int64_t t = t0; t < t1; ++t) {
+#pragma unroll
+      for (int q = 0; q + 1 < K; ++q)
+#pragma unroll
+        for (int k = 0; k < NV; ++k) ring[q][k] = ring[q + 1][k];
+      float mu, rs;
+      const int64_t row = b * T + t;
+      ln_row<NV>(x + row * C, C4, lane, inv_c, eps, g, lbv, ring[K - 1], mu, rs);
+      if (lane == 0) {
+        mean_out[row] = mu;
+        rstd_out[row] = rs;
+      }
+      float4* yr = reinterpret_cast<float4*>(y + row * C);
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+        const int jc = lane + 32 * k;
+        if (jc < C4) {
+          float4 u = bias[k];
+#pragma unroll
+          for (int j = 0; j < K; ++j) u = fma4(w[j][k], ring[j][k], u);
+          yr[jc] = make_float4(silu_f(u.x), silu_f(u.y), silu_f(u.z), silu_f(u.w));
+        }
+      }
+    }
+  }
+}
+
+template <int NV, int K>
+__global__ void __launch_bounds__(256) lnconv_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x,
+                                                         const float* __restrict__ mean, const float* __restrict__ rstd,
+                                                         const float* __restrict__ lg, const float* __restrict__ lb,
+                                                         const float* __restrict__ cw, const float* __restrict__ cb,
+                                                         float* __restrict__ dx, float* __restrict__ part,
+                                                         int64_t B, int64_t T, int C, int TCH) {
+  __shared__ __align__(16) float red[8][256 + 4];  // rows of 1040 B: float4 stores stay aligned
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int C4 = C >> 2;
+  const float inv_c = 1.0f / (float)C;
+  float4 g[NV], lbv[NV], bias[NV], w[K][NV];
+  load_row_params<NV>(lg, C4, lane, g);
+  load_row_params<NV>(lb, C4, lane, lbv);
+  load_row_params<NV>(cb, C4, lane, bias);
+  load_conv_taps<NV, K>(cw, C4, lane, w);
+  const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 aw[K][NV], acb[NV], ag[NV], ab[NV];
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    acb[k] = ag[k] = ab[k] = z4;
+#pragma unroll
+    for (int j = 0; j < K; ++j) aw[j][k] = z4;
+  }
+  const int64_t nch = (T + TCH - 1) / TCH;
+  const int64_t items = B * nch;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t it = blockIdx.x * (int64_t)(blockDim.x >> 5) + wid; it < items; it += warps) {
+    const int64_t b = it / nch;
+    const int64_t t0 = (it % nch) * TCH;
+    const int64_t t1 = min(T, t0 + (int64_t)TCH);
+    float4 lr[K][NV], dr[K][NV];  // LayerNorm rows and conv-output gradients, [K - 1] = row tau
+#pragma unroll
+    for (int q = 0; q < K; ++q)
+#pragma unroll
+      for (int k = 0; k < NV; ++k) lr[q][k] = dr[q][k] = z4;
+    auto ln_of = [&](int64_t tau, float4 (&out)[NV]) {  // LayerNorm row from the saved statistics
+      const float mu = __ldg(mean + b * T + tau), rs = __ldg(rstd + b * T + tau);
+      const float4* xr = reinterpret_cast<const float4*>(x + (b * T + tau) * C);
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+        const int jc = lane + 32 * k;
+        if (jc < C4) {
+          const float4 v = __ldg(xr + jc);
+          out[k] = make_float4((v.x - mu) * rs * g[k].x + lbv[k].x, (v.y - mu) * rs * g[k].y + lbv[k].y,
+                               (v.z - mu) * rs * g[k].z + lbv[k].z, (v.w - mu) * rs * g[k].w + lbv[k].w);
+        } else {
+          out[k] = z4;
+        }
+      }
+    };
+#pragma unroll
+    for (int q = 0; q + 1 < K; ++q) {
+      const int64_t tau = t0 - (K - 1) + q;
+      if (tau >= 0) ln_of(tau, lr[q + 1]);
+    }
+    for (int64_t tau = t0; tau < t1 + (K - 1); ++tau) {
+#pragma unroll
+      for (int q = 0; q + 1 < K; ++q)
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+          lr[q][k] = lr[q + 1][k];
+          dr[q][k] = dr[q + 1][k];
+        }
+      if (tau < T) {
+        ln_of(tau, lr[K - 1]);
+        const float4* dyr = reinterpret_cast<const float4*>(dy + (b * T + tau) * C);
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+          const int jc = lane + 32 * k;
+          float4 du = z4;
+          if (jc < C4) {
+            float4 u = bias[k];
+#pragma unroll
+            for (int j = 0; j < K; ++j) u = fma4(w[j][k], lr[j][k], u);
+            const float4 d = __ldg(dyr + jc);
+            du = make_float4(d.x * silu_grad(u.x), d.y * silu_grad(u.y), d.z * silu_grad(u.z), d.w * silu_grad(u.w));
+          }
+          dr[K - 1][k] = du;
+          if (tau < t1) {  // this chunk's outputs: conv parameter gradients
+            acb[k] = make_float4(acb[k].x + du.x, acb[k].y + du.y, acb[k].z + du.z, acb[k].w + du.w);
+#pragma unroll
+            for (int j = 0; j < K; ++j) aw[j][k] = fma4(du, lr[j][k], aw[j][k]);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < NV; ++k) lr[K - 1][k] = dr[K - 1][k] = z4;
+      }
+      const int64_t s = tau - (K - 1);  // every du that reaches LayerNorm row s is known now
+      if (s >= t0) {
+        const int64_t row = b * T + s;
+        const float mu = __ldg(mean + row), rs = __ldg(rstd + row);
+        const float4* xr = reinterpret_cast<const float4*>(x + row * C);
+        float4 xh[NV], wd[NV], dl[NV];
+        float s1 = 0.0f, s2 = 0.0f;
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+          const int jc = lane + 32 * k;
+          float4 d = z4;
+#pragma unroll
+          for (int j = 0; j < K; ++j) d = fma4(w[j][k], dr[K - 1 - j][k], d);
+          dl[k] = d;
+          if (jc < C4) {
+            const float4 v = __ldg(xr + jc);
+            xh[k] = make_float4((v.x - mu) * rs, (v.y - mu) * rs, (v.z - mu) * rs, (v.w - mu) * rs);
+          } else {
+            xh[k] = z4;
+          }
+          wd[k] = make_float4(d.x * g[k].x, d.y * g[k].y, d.z * g[k].z, d.w * g[k].w);
+          s1 += dot4(wd[k], xh[k]);
+          s2 += (wd[k].x + wd[k].y) + (wd[k].z + wd[k].w);
+        }
+        s1 = group_sum<32>(s1) * inv_c;
+        s2 = group_sum<32>(s2) * inv_c;
+        float4* o = reinterpret_cast<float4*>(dx + row * C);
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+          const int jc = lane + 32 * k;
+          if (jc < C4) {
+            o[jc] = make_float4((wd[k].x - xh[k].x * s1 - s2) * rs, (wd[k].y - xh[k].y * s1 - s2) * rs,
+                                (wd[k].z - xh[k].z * s1 - s2) * rs, (wd[k].w - xh[k].w * s1 - s2) * rs);
+            ag[k] = fma4(dl[k], xh[k], ag[k]);
+            ab[k] = make_float4(ab[k].x + dl[k].x, ab[k].y + dl[k].y, ab[k].z + dl[k].z, ab[k].w + dl[k].w);
+          }
+        }
+      }
+    }
+  }
+  // per-CTA sums: part[blockIdx.x, q * C + c], q = conv taps 0..K-1, conv bias, ln weight, ln bias
+  const int64_t base = (int64_t)blockIdx.x * (K + 3) * C;
+#pragma unroll
+  for (int q = 0; q < K + 3; ++q) {
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int jc = lane + 32 * k;
+      if (jc < C4) {
+        const float4 v = q < K ? aw[q < K ? q : 0][k] : (q == K ? acb[k] : (q == K + 1 ? ag[k] : ab[k]));
+        *reinterpret_cast<float4*>(&red[wid][4 * jc]) = v;
+      }
+    }
+    __syncthreads();
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+      float t = 0.0f;
+#pragma unroll
+      for (int v = 0; v < 8; ++v) t += red[v][c];
+      part[base + (int64_t)q * C + c] = t;
+    }
+    __syncthreads();
+  }
+}
+
+// Sum the per-CTA partials: 32 columns per CTA (deterministic order), scattered to the
+// parameter layouts (conv weight [C, 1, K]).
+__global__ void __launch_bounds__(256) lnconv_param_reduce_kernel(const float* __restrict__ part, int P, int C, int K,
+                                                                  float* __restrict__ dcw, float* __restrict__ dcb,
+                                                                  float* __restrict__ dlg, float* __restrict__ dlb) {
+  __shared__ float acc[8][33];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int Q = (K + 3) * C;
+  const int col = blockIdx.x * 32 + lane;
+  float t = 0.0f;
+  if (col < Q)
+    for (int p = wid; p < P; p += 8) t += part[(int64_t)p * Q + col];
+  acc[wid][lane] = t;
+  __syncthreads();
+  if (wid == 0 && col < Q) {
+    float u = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) u += acc[w][lane];
+    const int q = col / C, c = col % C;
+    if (q < K) {
+      if (dcw) dcw[c * K + q] = u;
+    } else if (q == K) {
+      if (dcb) dcb[c] = u;
+    } else if (q == K + 1) {
+      if (dlg) dlg[c] = u;
+    } else if (dlb) {
+      dlb[c] = u;
+    }
+  }
+}
+
+int lnconv_chunk(int64_t B, int64_t T) {
+  // ~148 SMs x 32 warps of work items, 8..64 steps per warp
+  const int64_t target = 148 * 32;
+  int64_t tc = (B * T + target - 1) / target;
+  tc = tc < 8 ? 8 : (tc > 64 ? 64 : tc);
+  return (int)tc;
+}
+
+unsigned lnconv_grid(int64_t B, int64_t T, int tc) {
+  const int64_t items = B * ((T + tc - 1) / tc);
+  const int64_t blocks = (items + 7) / 8;
+  const int64_t cap = 148 * 4;
+  return (unsigned)(blocks < cap ? (blocks > 0 ? blocks : 1) : cap);
+}
+
+int lnconv_check(const char* fn, int64_t B, int64_t T, int C, int K) {
+  if (B < 0 || T < 0 || C <= 0 || C % 4 != 0 || C > 256 || K < 1 || K > 4) {
+    char buf[200];
+    snprintf(buf, sizeof(buf), "%s: needs B, T >= 0, 0 < C <= 256 with C %% 4 == 0 and 1 <= K <= 4", fn);
+    return set_error(CSN_ERR_UNSUPPORTED, buf);
+  }
+  return CSN_OK;
+}
+
+template <int NV>
+void lnconv_fwd_launch(int K, unsigned grid, cudaStream_t st, const float* x, const float* lg, const float* lb,
+                       const float* cw, const float* cb, float* y, float* mean, float* rstd, int64_t B, int64_t T,
+                       int C, int tc, float eps) {
+  switch (K) {
+    case 1: lnconv_fwd_kernel<NV, 1><<<grid, 256, 0, st>>>(x, lg, lb, cw, cb, y, mean, rstd, B, T, C, tc, eps); break;
+    case 2: lnconv_fwd_kernel<NV, 2><<<grid, 256, 0, st>>>(x, lg, lb, cw, cb, y, mean, rstd, B, T, C, tc, eps); break;
+    case 3: lnconv_fwd_kernel<NV, 3><<<grid, 256, 0, st>>>(x, lg, lb, cw, cb, y, mean, rstd, B, T, C, tc, eps); break;
+    default: lnconv_fwd_kernel<NV, 4><<<grid, 256, 0, st>>>(x, lg, lb, cw, cb, y, mean, rstd, B, T, C, tc, eps); break;
+  }
+}
+
+template <int NV>
+void lnconv_bwd_launch(int K, unsigned grid, cudaStream_t st, const float* dy, const float* x, const float* mean,
+                       const float* rstd, const float* lg, const float* lb, const float* cw, const float* cb,
+                       float* dx, float* part, int64_t B, int64_t T, int C, int tc) {
+  switch (K) {
+    case 1: lnconv_bwd_kernel<NV, 1><<<grid, 256, 0, st>>>(dy, x, mean, rstd, lg, lb, cw, cb, dx, part, B, T, C, tc); break;
+    case 2: lnconv_bwd_kernel<NV, 2><<<grid, 256, 0, st>>>(dy, x, mean, rstd, lg, lb, cw, cb, dx, part, B, T, C, tc); break;
+    case 3: lnconv_bwd_kernel<NV, 3><<<grid, 256, 0, st>>>(dy, x, mean, rstd, lg, lb, cw, cb, dx, part, B, T, C, tc); break;
+    default: lnconv_bwd_kernel<NV, 4><<<grid, 256, 0, st>>>(dy, x, mean, rstd, lg, lb, cw, cb, dx, part, B, T, C, tc); break;
+  }
+}
+
+// ------------------------------------------------------------ least-action terms
+__global__ void __launch_bounds__(256) gen_action_fwd_kernel(const float* __restrict__ biv, const float* __restrict__ dt,
+                                                             int64_t B, int64_t T, int R, int H,
+                                                             float* __restrict__ part) {
+  __shared__ float red[8][2];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int seg = R / H;
+  float ak = 0.0f, as = 0.0f;
+  const int64_t rows = B * T;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t row = blockIdx.x * (int64_t)(blockDim.x >> 5) + wid; row < rows; row += warps) {
+    const bool has_prev = (row % T) != 0;
+    for (int j = lane; j < R; j += 32) {
+      const int h = j / seg;
+      const float w = 0.5f * __ldg(dt + row * H + h) * __ldg(biv + row * R + j);
+      ak = fmaf(w, w, ak);
+      if (has_prev) {
+        const float d = w - 0.5f * __ldg(dt + (row - 1) * H + h) * __ldg(biv + (row - 1) * R + j);
+        as = fmaf(d, d, as);
+      }
+    }
+  }
+  ak = group_sum<32>(ak);
+  as = group_sum<32>(as);
+  if (lane == 0) {
+    red[wid][0] = ak;
+    red[wid][1] = as;
+  }
+  __syncthreads();
+  if (threadIdx.x < 2) {
+    float t = 0.0f;
+#pragma unroll
+    for (int v = 0; v < 8; ++v) t += red[v][threadIdx.x];
+    part[2 * (int64_t)blockIdx.x + threadIdx.x] = t;
+  }
+}
+
+// out[q] = c[q] * sum_p part[p, q]   (one CTA, fixed order)
+__global__ void __launch_bounds__(256) gen_action_finish_kernel(const float* __restrict__ part, int P, float ck,
+                                                                float cs, float* __restrict__ out) {
+  __shared__ float red[2][256];
+  for (int q = 0; q < 2; ++q) {
+    float t = 0.0f;
+    for (int p = threadIdx.x; p < P; p += blockDim.x) t += part[2 * p + q];
+    red[q][threadIdx.x] = t;
+  }
+  __syncthreads();
+  for (int o = 128; o > 0; o >>= 1) {
+    if (threadIdx.x < o) {
+      red[0][threadIdx.x] += red[0][threadIdx.x + o];
+      red[1][threadIdx.x] += red[1][threadIdx.x + o];
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    out[0] = ck * red[0][0];
+    out[1] = cs * red[1][0];
+  }
+}
+
+__global__ void __launch_bounds__(256) gen_action_bwd_kernel(const float* __restrict__ biv, const float* __restrict__ dt,
+                                                             const float* __restrict__ gk, const float* __restrict__ gs,
+                                                             float ck, float cs, int64_t B, int64_t T, int R, int H,
+                                                             float* __restrict__ dbiv, float* __restrict__ ddt) {
+  const int lane = threadIdx.x & 31;
+  const int seg = R / H;
+  const float a = 2.0f * ck * (gk ? __ldg(gk) : 0.0f);
+  const float c = 2.0f * cs * (gs ? __ldg(gs) : 0.0f);
+  const int64_t rows = B * T;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t row = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); row < rows; row += warps) {
+    const int64_t t = row % T;
+    for (int h = 0; h < H; ++h) {
+      const float hdt = 0.5f * __ldg(dt + row * H + h);
+      const float hdp = t > 0 ? 0.5f * __ldg(dt + (row - 1) * H + h) : 0.0f;
+      const float hdn = t + 1 < T ? 0.5f * __ldg(dt + (row + 1) * H + h) : 0.0f;
+      float acc = 0.0f;
+      for (int j = h * seg + lane; j < (h + 1) * seg; j += 32) {
+        const float bv = __ldg(biv + row * R + j);
+        const float w = hdt * bv;
+        float dw = a * w;
+        if (t > 0) dw = fmaf(c, w - hdp * __ldg(biv + (row - 1) * R + j), dw);
+        if (t + 1 < T) dw = fmaf(-c, hdn * __ldg(biv + (row + 1) * R + j) - w, dw);
+        if (dbiv) dbiv[row * R + j] = dw * hdt;
+        acc = fmaf(dw, 0.5f * bv, acc);
+      }
+      acc = group_sum<32>(acc);
+      if (lane == 0 && ddt) ddt[row * H + h] = acc;
+    }
+  }
+}
+
+unsigned action_grid(int64_t rows) {
+  const int64_t blocks = (rows + 7) / 8;
+  const int64_t cap = 148 * 8;
+  return (unsigned)(blocks < cap ? (blocks > 0 ? blocks : 1) : cap);
+}
+
 }  // namespace
 }  // namespace csn
 
@@ -376,4 +853,115 @@ extern "C" int csn_layer_norm_bwd(const float* dy, const float* x, const float* 
     ln_param_reduce_kernel<<<(unsigned)((2 * C + 31) / 32), 256, 0, st>>>(part, dweight, dbias, (int)grid, C);
   }
   return check_launch("csn_layer_norm_bwd");
+}
+
+extern "C" int csn_ln_conv_silu_fwd(const float* x, const float* ln_weight, const float* ln_bias,
+                                    const float* conv_weight, const float* conv_bias, float* y, float* mean,
+                                    float* rstd, int64_t B, int64_t T, int C, int K, float eps, void* stream) {
+  if (int rc = lnconv_check("csn_ln_conv_silu_fwd", B, T, C, K)) return rc;
+  if (B * T == 0) return CSN_OK;
+  if (!x || !ln_weight || !ln_bias || !conv_weight || !conv_bias || !y || !mean || !rstd || !al16(x) || !al16(y) ||
+      !al16(ln_weight) || !al16(ln_bias) || !al16(conv_bias))
+    return set_error(CSN_ERR_INVALID, "csn_ln_conv_silu_fwd: missing or misaligned pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int tc = lnconv_chunk(B, T);
+  const unsigned grid = lnconv_grid(B, T, tc);
+  KernelTimer kt("ln_conv_silu_fwd", st);
+  if (C <= 128)
+    lnconv_fwd_launch<1>(K, grid, st, x, ln_weight, ln_bias, conv_weight, conv_bias, y, mean, rstd, B, T, C, tc, eps);
+  else
+    lnconv_fwd_launch<2>(K, grid, st, x, ln_weight, ln_bias, conv_weight, conv_bias, y, mean, rstd, B, T, C, tc, eps);
+  return check_launch("csn_ln_conv_silu_fwd");
+}
+
+extern "C" size_t csn_ln_conv_silu_bwd_workspace_bytes(int64_t B, int64_t T, int C, int K) {
+  if (B <= 0 || T <= 0 || C <= 0 || K <= 0) return 0;
+  return (size_t)lnconv_grid(B, T, lnconv_chunk(B, T)) * (size_t)(K + 3) * (size_t)C * sizeof(float);
+}
+
+extern "C" int csn_ln_conv_silu_bwd(const float* dy, const float* x, const float* mean, const float* rstd,
+                                    const float* ln_weight, const float* ln_bias, const float* conv_weight,
+                                    const float* conv_bias, float* dx, float* dln_weight, float* dln_bias,
+                                    float* dconv_weight, float* dconv_bias, int64_t B, int64_t T, int C, int K,
+                                    void* workspace, size_t workspace_bytes, void* stream) {
+  if (int rc = lnconv_check("csn_ln_conv_silu_bwd", B, T, C, K)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (B * T == 0) {
+    float* outs[4] = {dln_weight, dln_bias, dconv_weight, dconv_bias};
+    const size_t n[4] = {(size_t)C, (size_t)C, (size_t)C * K, (size_t)C};
+    for (int i = 0; i < 4; ++i)
+      if (outs[i] && cudaMemsetAsync(outs[i], 0, n[i] * sizeof(float), st) != cudaSuccess)
+        return set_error(CSN_ERR_CUDA, "csn_ln_conv_silu_bwd: cudaMemsetAsync");
+    return CSN_OK;
+  }
+  if (!dy || !x || !mean || !rstd || !ln_weight || !ln_bias || !conv_weight || !conv_bias || !dx || !al16(dy) ||
+      !al16(x) || !al16(dx) || !al16(ln_weight) || !al16(ln_bias) || !al16(conv_bias))
+    return set_error(CSN_ERR_INVALID, "csn_ln_conv_silu_bwd: missing or misaligned pointer");
+  const int tc = lnconv_chunk(B, T);
+  const unsigned grid = lnconv_grid(B, T, tc);
+  if (!workspace || workspace_bytes < csn_ln_conv_silu_bwd_workspace_bytes(B, T, C, K))
+    return set_error(CSN_ERR_INVALID,
+                     "csn_ln_conv_silu_bwd: workspace smaller than csn_ln_conv_silu_bwd_workspace_bytes");
+  float* part = static_cast<float*>(workspace);
+  {
+    KernelTimer kt("ln_conv_silu_bwd", st);
+    if (C <= 128)
+      lnconv_bwd_launch<1>(K, grid, st, dy, x, mean, rstd, ln_weight, ln_bias, conv_weight, conv_bias, dx, part, B,
+                           T, C, tc);
+    else
+      lnconv_bwd_launch<2>(K, grid, st, dy, x, mean, rstd, ln_weight, ln_bias, conv_weight, conv_bias, dx, part, B,
+                           T, C, tc);
+  }
+  {
+    KernelTimer kt("ln_conv_silu_param_reduce", st);
+    lnconv_param_reduce_kernel<<<(unsigned)(((K + 3) * C + 31) / 32), 256, 0, st>>>(
+        part, (int)grid, C, K, dconv_weight, dconv_bias, dln_weight, dln_bias);
+  }
+  return check_launch("csn_ln_conv_silu_bwd");
+}
+
+extern "C" size_t csn_generator_action_workspace_bytes(int64_t B, int64_t T) {
+  return (size_t)action_grid(B * T) * 2 * sizeof(float);
+}
+
+extern "C" int csn_generator_action_fwd(const float* biv, const float* dt, int64_t B, int64_t T, int R, int H,
+                                        float c_kin, float c_smooth, float* out, void* workspace,
+                                        size_t workspace_bytes, void* stream) {
+  if (B < 0 || T < 0 || R < 0 || H < 1 || (R % H) != 0)
+    return set_error(CSN_ERR_INVALID, "csn_generator_action_fwd: needs B, T, R >= 0, H >= 1 and R % H == 0");
+  if (!out) return set_error(CSN_ERR_INVALID, "csn_generator_action_fwd: out is required");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (B * T * R == 0) {
+    if (cudaMemsetAsync(out, 0, 2 * sizeof(float), st) != cudaSuccess)
+      return set_error(CSN_ERR_CUDA, "csn_generator_action_fwd: cudaMemsetAsync");
+    return CSN_OK;
+  }
+  if (!biv || !dt) return set_error(CSN_ERR_INVALID, "csn_generator_action_fwd: biv and dt are required");
+  const unsigned grid = action_grid(B * T);
+  if (!workspace || workspace_bytes < csn_generator_action_workspace_bytes(B, T))
+    return set_error(CSN_ERR_INVALID, "csn_generator_action_fwd: workspace smaller than csn_generator_action_workspace_bytes");
+  float* part = static_cast<float*>(workspace);
+  KernelTimer kt("generator_action_fwd", st);
+  gen_action_fwd_kernel<<<grid, 256, 0, st>>>(biv, dt, B, T, R, H, part);
+  gen_action_finish_kernel<<<1, 256, 0, st>>>(part, (int)grid, c_kin, c_smooth, out);
+  return check_launch("csn_generator_action_fwd");
+}
+
+extern "C" int csn_generator_action_bwd(const float* biv, const float* dt, const float* g_kin, const float* g_smooth,
+                                        int64_t B, int64_t T, int R, int H, float c_kin, float c_smooth,
+                                        float* dbiv, float* ddt, void* stream) {
+  if (B < 0 || T < 0 || R < 0 || H < 1 || (R % H) != 0)
+    return set_error(CSN_ERR_INVALID, "csn_generator_action_bwd: needs B, T, R >= 0, H >= 1 and R % H == 0");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (B * T == 0) return CSN_OK;
+  if (R == 0) {
+    if (ddt && cudaMemsetAsync(ddt, 0, sizeof(float) * B * T * H, st) != cudaSuccess)
+      return set_error(CSN_ERR_CUDA, "csn_generator_action_bwd: cudaMemsetAsync");
+    return CSN_OK;
+  }
+  if (!biv || !dt) return set_error(CSN_ERR_INVALID, "csn_generator_action_bwd: biv and dt are required");
+  KernelTimer kt("generator_action_bwd", st);
+  gen_action_bwd_kernel<<<action_grid(B * T), 256, 0, st>>>(biv, dt, g_kin, g_smooth, c_kin, c_smooth, B, T, R, H,
+                                                             dbiv, ddt);
+  return check_launch("csn_generator_action_bwd");
 }

@@ -7,7 +7,8 @@
   * the event spike of lines 174-176 is one CUDA kernel each way (ops.state_spike);
   * the inter-neuron mixing of line 179 is linear, so it is folded into out_proj's weight
     (W_out (W_mix (x) I_64), a [d_model, N*64] matrix built per call): X_mixed is never formed;
-  * ln_1 / ln_2 run the CUDA LayerNorm kernels (csn_b200.modules.LayerNorm).
+  * ln_1 -> causal depthwise conv -> SiLU (lines 140-142) is one CUDA kernel each way
+    (csn_b200.modules.causal_conv_input), and ln_2 runs the CUDA LayerNorm kernels.
 Omega is still returned by forward(); CliffordCL6ForCausalLM takes its action regulariser from
 the generator coefficients instead (sum Omega^2 = 2 sum (0.5 dt biv)^2), so it never forms Omega.
 """
@@ -19,7 +20,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from csn_b200 import ops
-from csn_b200.modules import LayerNorm
+from csn_b200.modules import LayerNorm, causal_conv_input
 from python.clifford_model import GeometricGatedLinearUnit, RiemannianGeodesicHead
 from python.clifford_scan import parallel_rotor_scan, surrogate_spike  # noqa: F401 (re-export)
 
@@ -49,19 +50,10 @@ def generator_action(biv: torch.Tensor, dt: torch.Tensor, D: int) -> Tuple[torch
     regulariser (python/clifford_cl6.py:257-262, clifford_cl8.py, clifford_multihead.py) from the
     K generator coefficients, without forming Omega = skew(biv) * 0.5 dt: each coefficient
     w = 0.5 dt biv sits at (u, v) and, negated, at (v, u) of a D x D matrix with a zero diagonal,
-    so a mean over Omega's D^2 entries is (2 K / D^2) times the mean over w.  biv [B, T, ..., K];
-    dt broadcasts against biv[..., 0] from the left ([B, T] or [B, T, H]).  The smoothness term is
-    0 for T = 1."""
-    K = biv.shape[-1]
-    ratio = 2.0 * K / float(D * D)
-    dtb = dt.reshape(*dt.shape, *([1] * (biv.dim() - dt.dim())))
-    w = biv * (0.5 * dtb)
-    e_kin = ratio * (w ** 2).mean()
-    if biv.shape[1] > 1:
-        e_smooth = ratio * ((w[:, 1:] - w[:, :-1]) ** 2).mean()
-    else:
-        e_smooth = torch.zeros((), device=biv.device, dtype=biv.dtype)
-    return e_kin, e_smooth
+    so a mean over Omega's D^2 entries is (2 K / D^2) times the mean over w.  One CUDA kernel
+    each way (ops.generator_action).  biv [B, T, ..., K]; dt [B, T] or [B, T, H] (per head).
+    The smoothness term is 0 for T = 1."""
+    return ops.generator_action(biv, dt, D)
 
 
 def read_diagnostics(named: Dict[str, torch.Tensor]) -> Dict[str, float]:
@@ -115,7 +107,7 @@ class CliffordCL6Block(nn.Module):
         B, T, _ = x.shape
         N = self.num_neurons
         residual = x
-        x_conv = F.silu(self.conv1d(self.ln_1(x).transpose(1, 2))[:, :, :T].transpose(1, 2))
+        x_conv = causal_conv_input(self.ln_1, self.conv1d, x)      # ln_1 -> causal conv -> SiLU, fused
         dt = self.time_head(x_conv).view(B, T)
         S = self.in_proj(x_conv).view(B, T, N, 8, 8)
         gamma = F.softplus(self.gamma_proj(x_conv))                   # [B, T, N]

@@ -14,7 +14,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from csn_b200 import ops
-from csn_b200.modules import LayerNorm
+from csn_b200.modules import LayerNorm, causal_conv_input
 from python.clifford_cl6 import AdaptiveTimeHead, generator_action, read_diagnostics, skew_from_generators
 from python.clifford_model import GeometricGatedLinearUnit, RiemannianGeodesicHead
 from python.clifford_scan import parallel_rotor_scan, surrogate_spike  # noqa: F401 (re-export)
@@ -71,7 +71,7 @@ class CliffordCL8Block(nn.Module):
         B, T, _ = x.shape
         N = self.num_neurons
         residual = x
-        x_conv = F.silu(self.conv1d(self.ln_1(x).transpose(1, 2))[:, :, :T].transpose(1, 2))
+        x_conv = causal_conv_input(self.ln_1, self.conv1d, x)      # ln_1 -> causal conv -> SiLU, fused
         dt = self.time_head(x_conv).view(B, T)
         S = self.in_proj(x_conv).view(B, T, N, 16, 16)
         gamma = F.softplus(self.gamma_proj(x_conv))

@@ -15,7 +15,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from csn_b200 import ops
-from csn_b200.modules import LayerNorm
+from csn_b200.modules import LayerNorm, causal_conv_input
 from python.clifford_scan import parallel_rotor_scan, surrogate_spike  # noqa: F401 (re-export)
 
 
@@ -73,7 +73,7 @@ class CliffordTENNBlock(nn.Module):
     def forward(self, x: torch.Tensor, dt: float = 0.05) -> Tuple[torch.Tensor, torch.Tensor]:
         B, T, _ = x.shape
         residual = x
-        x_conv = F.silu(self.conv1d(self.ln_1(x).transpose(1, 2))[:, :, :T].transpose(1, 2))
+        x_conv = causal_conv_input(self.ln_1, self.conv1d, x)      # ln_1 -> causal conv -> SiLU, fused
         S = self.in_proj(x_conv).view(B, T, self.num_neurons, 4, 4)
         gamma = F.softplus(self.gamma_proj(x_conv))
         decay = torch.sigmoid(-gamma * dt).unsqueeze(-1).unsqueeze(-1)

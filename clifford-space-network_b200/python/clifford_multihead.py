@@ -19,7 +19,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from csn_b200 import ops
-from csn_b200.modules import LayerNorm
+from csn_b200.modules import LayerNorm, causal_conv_input
 from python.clifford_cl6 import (cayley_rotor_8x8, generator_action, read_diagnostics,  # noqa: F401
                                  skew_from_generators)
 from python.clifford_model import GeometricGatedLinearUnit, RiemannianGeodesicHead
@@ -82,7 +82,7 @@ class MultiHeadCliffordCL6Block(nn.Module):
         B, T, _ = x.shape
         H, Nh = self.num_heads, self.num_neurons_per_head
         residual = x
-        x_conv = F.silu(self.conv1d(self.ln_1(x).transpose(1, 2))[:, :, :T].transpose(1, 2))
+        x_conv = causal_conv_input(self.ln_1, self.conv1d, x)      # ln_1 -> causal conv -> SiLU, fused
         dt = self.time_head(x_conv)                                          # [B, T, H]
         S = self.in_proj(x_conv).view(B, T, H, Nh, 8, 8)
         gamma = F.softplus(self.gamma_proj(x_conv)).view(B, T, H, Nh)

@@ -299,6 +299,43 @@ int csn_layer_norm_bwd(const float* dy, const float* x, const float* mean, const
                        const float* weight, float* dx, float* dweight, float* dbias, int64_t R, int C,
                        void* workspace, size_t workspace_bytes, void* stream);
 
+/* The blocks' input chain ln_1 -> causal depthwise conv1d -> SiLU (python/clifford_cl6.py:140-142,
+ * clifford_cl8.py, clifford_multihead.py, clifford_model.py: nn.LayerNorm(C), then
+ * nn.Conv1d(C, C, K, padding=K-1, groups=C) on the transposed sequence keeping the first T
+ * outputs, then F.silu), fused:
+ *   y[b,t,c] = silu(conv_bias[c] + sum_{j<K} conv_weight[c,0,j] * ln(x)[b, t-K+1+j, c])
+ * with ln rows before t = 0 taken as 0.  x, y [B, T, C]; conv_weight [C, 1, K]; mean, rstd
+ * [B*T] are the LayerNorm statistics the backward reuses.  The backward writes dx and, when
+ * given, the four parameter gradients (its workspace holds per-CTA partial sums).
+ * 0 < C <= 256, C % 4 == 0, 1 <= K <= 4 (CSN_ERR_UNSUPPORTED otherwise); x, y, dy, dx,
+ * ln_weight, ln_bias, conv_bias 16-byte aligned. */
+int csn_ln_conv_silu_fwd(const float* x, const float* ln_weight, const float* ln_bias,
+                         const float* conv_weight, const float* conv_bias, float* y, float* mean,
+                         float* rstd, int64_t B, int64_t T, int C, int K, float eps, void* stream);
+size_t csn_ln_conv_silu_bwd_workspace_bytes(int64_t B, int64_t T, int C, int K);
+int csn_ln_conv_silu_bwd(const float* dy, const float* x, const float* mean, const float* rstd,
+                         const float* ln_weight, const float* ln_bias, const float* conv_weight,
+                         const float* conv_bias, float* dx, float* dln_weight, float* dln_bias,
+                         float* dconv_weight, float* dconv_bias, int64_t B, int64_t T, int C, int K,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
+/* Least-action regulariser of the LMs (python/clifford_cl6.py:257-262, the same lines of
+ * clifford_cl8.py and clifford_multihead.py) on the generator coefficients instead of Omega:
+ * rows (b, t) of R = N * K coefficients biv [B, T, R] in H heads of R / H, dt [B, T, H];
+ * w = 0.5 dt biv;  out[0] = c_kin * sum w^2,  out[1] = c_smooth * sum_{t >= 1} (w_t - w_{t-1})^2
+ * (device scalars; the sums are reduced in a fixed order).  With c_kin = 2K / (D^2 * B*T*R) and
+ * c_smooth = 2K / (D^2 * B*(T-1)*R) these are (Omega^2).mean() and
+ * ((Omega[:, 1:] - Omega[:, :-1])^2).mean() of Omega = skew(biv) * 0.5 dt (D x D, K generators).
+ * The backward takes dL/dout[0], dL/dout[1] as device pointers (NULL = 0) and writes dbiv
+ * [B, T, R] and ddt [B, T, H] (either may be NULL). */
+size_t csn_generator_action_workspace_bytes(int64_t B, int64_t T);
+int csn_generator_action_fwd(const float* biv, const float* dt, int64_t B, int64_t T, int R, int H,
+                             float c_kin, float c_smooth, float* out, void* workspace,
+                             size_t workspace_bytes, void* stream);
+int csn_generator_action_bwd(const float* biv, const float* dt, const float* g_kin,
+                             const float* g_smooth, int64_t B, int64_t T, int R, int H, float c_kin,
+                             float c_smooth, float* dbiv, float* ddt, void* stream);
+
 /* -------------------------------------------------------------- kernel timing */
 /* Measurement hook with no counterpart in the reference (which times with wall clock,
  * tests/profile_performance.py:41-71).  While enabled, every kernel the library

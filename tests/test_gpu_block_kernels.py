@@ -109,3 +109,96 @@ def test_layer_norm_rejects_unsupported_sizes(ops):
         x = torch.zeros(2, 2048, device=DEV)
         _lib.call("csn_layer_norm_fwd", ops._ptr(x), ops._ptr(x), ops._ptr(x), ops._ptr(x), ops._ptr(x),
                   ops._ptr(x), 2, 2048, 1e-5, ops._stream(x.device))
+
+
+def reference_conv_input(x, lw, lb, cw, cb, eps):
+    T = x.shape[1]
+    ln = torch.nn.functional.layer_norm(x, (x.shape[-1],), lw, lb, eps)
+    u = torch.nn.functional.conv1d(ln.transpose(1, 2), cw, cb, padding=cw.shape[-1] - 1, groups=x.shape[-1])
+    return torch.nn.functional.silu(u[:, :, :T].transpose(1, 2))
+
+
+@pytest.mark.parametrize("C", [4, 48, 128, 256])
+@pytest.mark.parametrize("K", [1, 2, 3, 4])
+@pytest.mark.parametrize("BT", [(1, 1), (2, 3), (3, 100), (2, 2048)], ids=lambda s: f"B{s[0]}T{s[1]}")
+def test_ln_conv_silu_matches_torch_chain(ops, C, K, BT):
+    """ln -> causal depthwise conv (left padding K - 1, first T outputs) -> SiLU of the blocks
+    (python/clifford_cl6.py:140-142): output and the gradients of x, both LayerNorm parameters
+    and both conv parameters, against the float64 torch chain."""
+    B, T = BT
+    rng = np.random.default_rng(C * 100 + K * 10 + T)
+    arrs = [rng.standard_normal((B, T, C)) * 2.0 + 0.5, rng.standard_normal(C), rng.standard_normal(C),
+            rng.standard_normal((C, 1, K)) * 0.5, rng.standard_normal(C) * 0.3]
+    dy = rng.standard_normal((B, T, C))
+    t64 = [torch.tensor(a, dtype=torch.float64, device=DEV, requires_grad=True) for a in arrs]
+    ref = reference_conv_input(*t64, 1e-5)
+    (ref * torch.tensor(dy, dtype=torch.float64, device=DEV)).sum().backward()
+    t32 = [torch.tensor(a, dtype=torch.float32, device=DEV, requires_grad=True) for a in arrs]
+    got = ops.ln_conv_silu(t32[0], t32[1], t32[2], 1e-5, t32[3], t32[4])
+    (got * torch.tensor(dy, dtype=torch.float32, device=DEV)).sum().backward()
+    assert got.shape == (B, T, C)
+    assert rel(got, ref) < 1e-5
+    for name, a, r in zip(("x", "ln_w", "ln_b", "conv_w", "conv_b"), t32, t64):
+        assert rel(a.grad, r.grad) < 1e-4, name
+
+
+def test_causal_conv_input_module_path(ops):
+    """The blocks' helper takes the fused kernels for the block layers and the library chain for
+    layers outside the kernels' range, with the same result."""
+    from csn_b200.modules import LayerNorm, causal_conv_input
+    torch.manual_seed(0)
+    for C, K in ((64, 4), (6, 4), (320, 4), (64, 5)):
+        ln = LayerNorm(C).to(DEV)
+        conv = torch.nn.Conv1d(C, C, K, padding=K - 1, groups=C).to(DEV)
+        x = torch.randn(2, 17, C, device=DEV)
+        ref = reference_conv_input(x.double(), ln.weight.double(), ln.bias.double(), conv.weight.double(),
+                                   conv.bias.double(), ln.eps)
+        assert rel(causal_conv_input(ln, conv, x), ref) < 1e-5
+
+
+def reference_action(biv, dt, D):
+    """The reference's terms on the explicit Omega (python/clifford_cl6.py:257-262)."""
+    from python.clifford_cl6 import skew_from_generators
+    u, v = torch.triu_indices(D, D, offset=1, device=biv.device)
+    dtb = dt.reshape(*dt.shape, *([1] * (biv.dim() - dt.dim())))
+    Omega = skew_from_generators(biv, D, u, v) * (0.5 * dtb)[..., None]
+    kin = (Omega ** 2).mean()
+    smooth = ((Omega[:, 1:] - Omega[:, :-1]) ** 2).mean() if biv.shape[1] > 1 else torch.zeros((), device=biv.device,
+                                                                                                 dtype=biv.dtype)
+    return kin, smooth
+
+
+@pytest.mark.parametrize("case", ["cl6", "cl8", "heads", "T1", "cl6_long"])
+def test_generator_action_matches_omega_form(ops, case):
+    rng = np.random.default_rng(len(case) * 31 + ord(case[-1]))
+    if case == "cl6":
+        biv, dt, D = rng.standard_normal((3, 17, 8, 28)) * 5, rng.uniform(0.02, 0.08, (3, 17)), 8
+    elif case == "cl6_long":
+        biv, dt, D = rng.standard_normal((4, 2048, 8, 28)) * 5, rng.uniform(0.02, 0.08, (4, 2048)), 8
+    elif case == "cl8":
+        biv, dt, D = rng.standard_normal((2, 9, 2, 120)) * 5, rng.uniform(0.02, 0.08, (2, 9)), 16
+    elif case == "heads":
+        biv, dt, D = rng.standard_normal((2, 11, 3, 2, 28)) * 5, rng.uniform(0.02, 0.08, (2, 11, 3)), 8
+    else:
+        biv, dt, D = rng.standard_normal((2, 1, 4, 28)) * 5, rng.uniform(0.02, 0.08, (2, 1)), 8
+    wk, ws = 0.7, -1.3
+    b64 = torch.tensor(biv, dtype=torch.float64, device=DEV, requires_grad=True)
+    d64 = torch.tensor(dt, dtype=torch.float64, device=DEV, requires_grad=True)
+    rk, rs = reference_action(b64, d64, D)
+    (wk * rk + ws * rs).backward()
+    b32 = torch.tensor(biv, dtype=torch.float32, device=DEV, requires_grad=True)
+    d32 = torch.tensor(dt, dtype=torch.float32, device=DEV, requires_grad=True)
+    gk, gs = ops.generator_action(b32, d32, D)
+    (wk * gk + ws * gs).backward()
+    assert abs(gk.item() - rk.item()) <= 1e-5 * abs(rk.item())
+    assert abs(gs.item() - rs.item()) <= 1e-5 * max(abs(rs.item()), 1e-30)
+    assert rel(b32.grad, b64.grad) < 1e-5
+    assert rel(d32.grad, d64.grad) < 1e-5
+    # only one of the two terms in the loss
+    b32.grad = None
+    d32.grad = None
+    ops.generator_action(b32, d32, D)[0].backward()
+    b64.grad = None
+    d64.grad = None
+    reference_action(b64, d64, D)[0].backward()
+    assert rel(b32.grad, b64.grad) < 1e-5 and rel(d32.grad, d64.grad) < 1e-5

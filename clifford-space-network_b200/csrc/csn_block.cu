@@ -266,10 +266,18 @@ __global__ void __launch_bounds__(256) ln_param_reduce_kernel(const float* __res
   __shared__ float acc[8][33];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int c = blockIdx.x * 32 + lane;
-  float t = 0.0f;
-  if (c < 2 * C)
-    for (int p = wid; p < P; p += 8) t += part[(int64_t)p * 2 * C + c];
-  acc[wid][lane] = t;
+  float t0 = 0.0f, t1 = 0.0f, t2 = 0.0f, t3 = 0.0f;  // four independent chains
+  if (c < 2 * C) {
+    int p = wid;
+    for (; p + 24 < P; p += 32) {
+      t0 += part[(int64_t)p * 2 * C + c];
+      t1 += part[(int64_t)(p + 8) * 2 * C + c];
+      t2 += part[(int64_t)(p + 16) * 2 * C + c];
+      t3 += part[(int64_t)(p + 24) * 2 * C + c];
+    }
+    for (; p < P; p += 8) t0 += part[(int64_t)p * 2 * C + c];
+  }
+  acc[wid][lane] = (t0 + t1) + (t2 + t3);
   __syncthreads();
   if (wid == 0 && c < 2 * C) {
     float u = 0.0f;
@@ -327,19 +335,23 @@ __device__ __forceinline__ void load_conv_taps(const float* __restrict__ cw, int
   }
 }
 
-// LayerNorm of one row (warp-collective): out = (x - mu) rs g + b
 template <int NV>
-__device__ __forceinline__ void ln_row(const float* __restrict__ xr, int C4, int lane, float inv_c, float eps,
-                                       const float4 (&g)[NV], const float4 (&b)[NV], float4 (&out)[NV],
-                                       float& mu, float& rs) {
-  float4 v[NV];
-  float s = 0.0f;
+__device__ __forceinline__ void load_row(const float* __restrict__ xr, int C4, int lane, float4 (&v)[NV]) {
 #pragma unroll
   for (int k = 0; k < NV; ++k) {
     const int j = lane + 32 * k;
     v[k] = j < C4 ? __ldg(reinterpret_cast<const float4*>(xr) + j) : make_float4(0.f, 0.f, 0.f, 0.f);
-    s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
   }
+}
+
+// LayerNorm of one row held as v (warp-collective): out = (x - mu) rs g + b
+template <int NV>
+__device__ __forceinline__ void ln_vals(const float4 (&v)[NV], int C4, int lane, float inv_c, float eps,
+                                        const float4 (&g)[NV], const float4 (&b)[NV], float4 (&out)[NV],
+                                        float& mu, float& rs) {
+  float s = 0.0f;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
   mu = group_sum<32>(s) * inv_c;
   float q = 0.0f;
 #pragma unroll
@@ -358,6 +370,15 @@ __device__ __forceinline__ void ln_row(const float* __restrict__ xr, int C4, int
     else
       out[k] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
+}
+
+template <int NV>
+__device__ __forceinline__ void ln_row(const float* __restrict__ xr, int C4, int lane, float inv_c, float eps,
+                                       const float4 (&g)[NV], const float4 (&b)[NV], float4 (&out)[NV],
+                                       float& mu, float& rs) {
+  float4 v[NV];
+  load_row<NV>(xr, C4, lane, v);
+  ln_vals<NV>(v, C4, lane, inv_c, eps, g, b, out, mu, rs);
 }
 
 __device__ __forceinline__ float silu_f(float u) { return u / (1.0f + expf(-u)); }
@@ -405,14 +426,25 @@ __global__ void __launch_bounds__(256) lnconv_fwd_kernel(const float* __restrict
         ln_row<NV>(x + (b * T + tau) * C, C4, lane, inv_c, eps, g, lbv, ring[q + 1], mu, rs);
       }
     }
+    float4 cur[NV];
+    load_row<NV>(x + (b * T + t0) * C, C4, lane, cur);
     for (int64_t t = t0; t < t1; ++t) {
+      float4 nxt[NV];  // the next row is in flight while this one is normalised
+      if (t + 1 < t1) {
+        load_row<NV>(x + (b * T + t + 1) * C, C4, lane, nxt);
+      } else {
+#pragma unroll
+        for (int k = 0; k < NV; ++k) nxt[k] = cur[k];
+      }
 #pragma unroll
       for (int q = 0; q + 1 < K; ++q)
 #pragma unroll
         for (int k = 0; k < NV; ++k) ring[q][k] = ring[q + 1][k];
       float mu, rs;
       const int64_t row = b * T + t;
-      ln_row<NV>(x + row * C, C4, lane, inv_c, eps, g, lbv, ring[K - 1], mu, rs);
+      ln_vals<NV>(cur, C4, lane, inv_c, eps, g, lbv, ring[K - 1], mu, rs);
+#pragma unroll
+      for (int k = 0; k < NV; ++k) cur[k] = nxt[k];
       if (lane == 0) {
         mean_out[row] = mu;
         rstd_out[row] = rs;
@@ -433,7 +465,7 @@ __global__ void __launch_bounds__(256) lnconv_fwd_kernel(const float* __restrict
 }
 
 template <int NV, int K>
-__global__ void __launch_bounds__(256) lnconv_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x,
+__global__ void __launch_bounds__(256, NV == 1 ? 2 : 1) lnconv_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x,
                                                          const float* __restrict__ mean, const float* __restrict__ rstd,
                                                          const float* __restrict__ lg, const float* __restrict__ lb,
                                                          const float* __restrict__ cw, const float* __restrict__ cb,
@@ -488,7 +520,25 @@ __global__ void __launch_bounds__(256) lnconv_bwd_kernel(const float* __restrict
       const int64_t tau = t0 - (K - 1) + q;
       if (tau >= 0) ln_of(tau, lr[q + 1]);
     }
+    // row tau's x, dy and statistics are loaded one iteration ahead
+    float4 cx[NV], cdy[NV];
+    float cm = 0.0f, cr = 0.0f;
+    auto fetch = [&](int64_t tau, float4 (&xv)[NV], float4 (&dv)[NV], float& m, float& r) {
+      load_row<NV>(x + (b * T + tau) * C, C4, lane, xv);
+      load_row<NV>(dy + (b * T + tau) * C, C4, lane, dv);
+      m = __ldg(mean + b * T + tau);
+      r = __ldg(rstd + b * T + tau);
+    };
+    fetch(t0, cx, cdy, cm, cr);
     for (int64_t tau = t0; tau < t1 + (K - 1); ++tau) {
+      float4 nx[NV], ndy[NV];
+      float nm = 0.0f, nr = 0.0f;
+      if (tau + 1 < T && tau + 1 < t1 + (K - 1)) {
+        fetch(tau + 1, nx, ndy, nm, nr);
+      } else {
+#pragma unroll
+        for (int k = 0; k < NV; ++k) nx[k] = ndy[k] = z4;
+      }
 #pragma unroll
       for (int q = 0; q + 1 < K; ++q)
 #pragma unroll
@@ -497,8 +547,14 @@ __global__ void __launch_bounds__(256) lnconv_bwd_kernel(const float* __restrict
           dr[q][k] = dr[q + 1][k];
         }
       if (tau < T) {
-        ln_of(tau, lr[K - 1]);
-        const float4* dyr = reinterpret_cast<const float4*>(dy + (b * T + tau) * C);
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+          const float4 v = cx[k];
+          lr[K - 1][k] = lane + 32 * k < C4
+                             ? make_float4((v.x - cm) * cr * g[k].x + lbv[k].x, (v.y - cm) * cr * g[k].y + lbv[k].y,
+                                           (v.z - cm) * cr * g[k].z + lbv[k].z, (v.w - cm) * cr * g[k].w + lbv[k].w)
+                             : z4;
+        }
 #pragma unroll
         for (int k = 0; k < NV; ++k) {
           const int jc = lane + 32 * k;
@@ -507,7 +563,7 @@ __global__ void __launch_bounds__(256) lnconv_bwd_kernel(const float* __restrict
             float4 u = bias[k];
 #pragma unroll
             for (int j = 0; j < K; ++j) u = fma4(w[j][k], lr[j][k], u);
-            const float4 d = __ldg(dyr + jc);
+            const float4 d = cdy[k];
             du = make_float4(d.x * silu_grad(u.x), d.y * silu_grad(u.y), d.z * silu_grad(u.z), d.w * silu_grad(u.w));
           }
           dr[K - 1][k] = du;
@@ -559,6 +615,13 @@ __global__ void __launch_bounds__(256) lnconv_bwd_kernel(const float* __restrict
           }
         }
       }
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+        cx[k] = nx[k];
+        cdy[k] = ndy[k];
+      }
+      cm = nm;
+      cr = nr;
     }
   }
   // per-CTA sums: part[blockIdx.x, q * C + c], q = conv taps 0..K-1, conv bias, ln weight, ln bias
@@ -593,10 +656,18 @@ __global__ void __launch_bounds__(256) lnconv_param_reduce_kernel(const float* _
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int Q = (K + 3) * C;
   const int col = blockIdx.x * 32 + lane;
-  float t = 0.0f;
-  if (col < Q)
-    for (int p = wid; p < P; p += 8) t += part[(int64_t)p * Q + col];
-  acc[wid][lane] = t;
+  float t0 = 0.0f, t1 = 0.0f, t2 = 0.0f, t3 = 0.0f;  // four independent chains
+  if (col < Q) {
+    int p = wid;
+    for (; p + 24 < P; p += 32) {
+      t0 += part[(int64_t)p * Q + col];
+      t1 += part[(int64_t)(p + 8) * Q + col];
+      t2 += part[(int64_t)(p + 16) * Q + col];
+      t3 += part[(int64_t)(p + 24) * Q + col];
+    }
+    for (; p < P; p += 8) t0 += part[(int64_t)p * Q + col];
+  }
+  acc[wid][lane] = (t0 + t1) + (t2 + t3);
   __syncthreads();
   if (wid == 0 && col < Q) {
     float u = 0.0f;
@@ -664,6 +735,19 @@ void lnconv_bwd_launch(int K, unsigned grid, cudaStream_t st, const float* dy, c
 }
 
 // ------------------------------------------------------------ least-action terms
+// V = 4: float4 accesses (R and the head width R / H multiples of 4, 16-byte aligned rows);
+// V = 1: scalar.
+template <int V>
+__device__ __forceinline__ void ldv(const float* p, float (&v)[V]) {
+  if constexpr (V == 4) {
+    const float4 f = __ldg(reinterpret_cast<const float4*>(p));
+    v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+  } else {
+    v[0] = __ldg(p);
+  }
+}
+
+template <int V>
 __global__ void __launch_bounds__(256) gen_action_fwd_kernel(const float* __restrict__ biv, const float* __restrict__ dt,
                                                              int64_t B, int64_t T, int R, int H,
                                                              float* __restrict__ part) {
@@ -675,13 +759,25 @@ __global__ void __launch_bounds__(256) gen_action_fwd_kernel(const float* __rest
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   for (int64_t row = blockIdx.x * (int64_t)(blockDim.x >> 5) + wid; row < rows; row += warps) {
     const bool has_prev = (row % T) != 0;
-    for (int j = lane; j < R; j += 32) {
-      const int h = j / seg;
-      const float w = 0.5f * __ldg(dt + row * H + h) * __ldg(biv + row * R + j);
-      ak = fmaf(w, w, ak);
+    for (int j = V * lane; j < R; j += 32 * V) {
+      const int h = H == 1 ? 0 : j / seg;
+      const float hd = 0.5f * __ldg(dt + row * H + h);
+      float bv[V];
+      ldv<V>(biv + row * R + j, bv);
+      float bp[V];
+      float hp = 0.0f;
       if (has_prev) {
-        const float d = w - 0.5f * __ldg(dt + (row - 1) * H + h) * __ldg(biv + (row - 1) * R + j);
-        as = fmaf(d, d, as);
+        hp = 0.5f * __ldg(dt + (row - 1) * H + h);
+        ldv<V>(biv + (row - 1) * R + j, bp);
+      }
+#pragma unroll
+      for (int u = 0; u < V; ++u) {
+        const float w = hd * bv[u];
+        ak = fmaf(w, w, ak);
+        if (has_prev) {
+          const float d = w - hp * bp[u];
+          as = fmaf(d, d, as);
+        }
       }
     }
   }
@@ -723,6 +819,7 @@ __global__ void __launch_bounds__(256) gen_action_finish_kernel(const float* __r
   }
 }
 
+template <int V>
 __global__ void __launch_bounds__(256) gen_action_bwd_kernel(const float* __restrict__ biv, const float* __restrict__ dt,
                                                              const float* __restrict__ gk, const float* __restrict__ gs,
                                                              float ck, float cs, int64_t B, int64_t T, int R, int H,
@@ -735,24 +832,39 @@ __global__ void __launch_bounds__(256) gen_action_bwd_kernel(const float* __rest
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   for (int64_t row = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); row < rows; row += warps) {
     const int64_t t = row % T;
+    const bool prev = t > 0, next = t + 1 < T;
     for (int h = 0; h < H; ++h) {
       const float hdt = 0.5f * __ldg(dt + row * H + h);
-      const float hdp = t > 0 ? 0.5f * __ldg(dt + (row - 1) * H + h) : 0.0f;
-      const float hdn = t + 1 < T ? 0.5f * __ldg(dt + (row + 1) * H + h) : 0.0f;
+      const float hdp = prev ? 0.5f * __ldg(dt + (row - 1) * H + h) : 0.0f;
+      const float hdn = next ? 0.5f * __ldg(dt + (row + 1) * H + h) : 0.0f;
       float acc = 0.0f;
-      for (int j = h * seg + lane; j < (h + 1) * seg; j += 32) {
-        const float bv = __ldg(biv + row * R + j);
-        const float w = hdt * bv;
-        float dw = a * w;
-        if (t > 0) dw = fmaf(c, w - hdp * __ldg(biv + (row - 1) * R + j), dw);
-        if (t + 1 < T) dw = fmaf(-c, hdn * __ldg(biv + (row + 1) * R + j) - w, dw);
-        if (dbiv) dbiv[row * R + j] = dw * hdt;
-        acc = fmaf(dw, 0.5f * bv, acc);
+      for (int j = h * seg + V * lane; j < (h + 1) * seg; j += 32 * V) {
+        float bv[V], bp[V], bn[V], out[V];
+        ldv<V>(biv + row * R + j, bv);
+        if (prev) ldv<V>(biv + (row - 1) * R + j, bp);
+        if (next) ldv<V>(biv + (row + 1) * R + j, bn);
+#pragma unroll
+        for (int u = 0; u < V; ++u) {
+          const float w = hdt * bv[u];
+          float dw = a * w;
+          if (prev) dw = fmaf(c, w - hdp * bp[u], dw);
+          if (next) dw = fmaf(-c, hdn * bn[u] - w, dw);
+          out[u] = dw * hdt;
+          acc = fmaf(dw, 0.5f * bv[u], acc);
+        }
+        if (dbiv) {
+          if constexpr (V == 4) *reinterpret_cast<float4*>(dbiv + row * R + j) = make_float4(out[0], out[1], out[2], out[3]);
+          else dbiv[row * R + j] = out[0];
+        }
       }
       acc = group_sum<32>(acc);
       if (lane == 0 && ddt) ddt[row * H + h] = acc;
     }
   }
+}
+
+bool action_vec4(const float* biv, int R, int H) {
+  return R % 4 == 0 && (R / H) % 4 == 0 && (reinterpret_cast<uintptr_t>(biv) & 15u) == 0;
 }
 
 unsigned action_grid(int64_t rows) {
@@ -942,7 +1054,8 @@ extern "C" int csn_generator_action_fwd(const float* biv, const float* dt, int64
     return set_error(CSN_ERR_INVALID, "csn_generator_action_fwd: workspace smaller than csn_generator_action_workspace_bytes");
   float* part = static_cast<float*>(workspace);
   KernelTimer kt("generator_action_fwd", st);
-  gen_action_fwd_kernel<<<grid, 256, 0, st>>>(biv, dt, B, T, R, H, part);
+  if (action_vec4(biv, R, H)) gen_action_fwd_kernel<4><<<grid, 256, 0, st>>>(biv, dt, B, T, R, H, part);
+  else gen_action_fwd_kernel<1><<<grid, 256, 0, st>>>(biv, dt, B, T, R, H, part);
   gen_action_finish_kernel<<<1, 256, 0, st>>>(part, (int)grid, c_kin, c_smooth, out);
   return check_launch("csn_generator_action_fwd");
 }
@@ -961,7 +1074,11 @@ extern "C" int csn_generator_action_bwd(const float* biv, const float* dt, const
   }
   if (!biv || !dt) return set_error(CSN_ERR_INVALID, "csn_generator_action_bwd: biv and dt are required");
   KernelTimer kt("generator_action_bwd", st);
-  gen_action_bwd_kernel<<<action_grid(B * T), 256, 0, st>>>(biv, dt, g_kin, g_smooth, c_kin, c_smooth, B, T, R, H,
-                                                             dbiv, ddt);
+  if (action_vec4(biv, R, H) && (!dbiv || al16(dbiv)))
+    gen_action_bwd_kernel<4><<<action_grid(B * T), 256, 0, st>>>(biv, dt, g_kin, g_smooth, c_kin, c_smooth, B, T, R,
+                                                                 H, dbiv, ddt);
+  else
+    gen_action_bwd_kernel<1><<<action_grid(B * T), 256, 0, st>>>(biv, dt, g_kin, g_smooth, c_kin, c_smooth, B, T, R,
+                                                                 H, dbiv, ddt);
   return check_launch("csn_generator_action_bwd");
 }

@@ -251,3 +251,78 @@ def rotor_step(gens: Tensor, dt: Tensor, gamma: Optional[Tensor], S: Tensor, h: 
 @rotor_step.register_fake
 def _(gens, dt, gamma, S, h, basis, two_sided):
     return None
+
+
+# ------------------------------------------------------- sequence-parallel scan
+def _resolve_group(group_name: str):
+    """The process group registered under `group_name` ("" = the default group)."""
+    if not group_name:
+        return None
+    import torch.distributed.distributed_c10d as c10d
+    return c10d._resolve_process_group(group_name)
+
+
+def _basis_name(basis: int) -> str:
+    return {v: k for k, v in ops.BASIS.items()}[basis]
+
+
+@torch.library.custom_op("csn::sp_scan", mutates_args=())
+def sp_scan(gens: Tensor, dt: Tensor, gamma: Optional[Tensor], S: Tensor, group_name: str, basis: int,
+            two_sided: bool) -> Tuple[Tensor, Tensor, Tensor]:
+    """Sequence-parallel fused rotor scan of this rank's time shard over the group named
+    `group_name` (csn_b200.sequence_parallel): returns (X, h_in, Ps) -- the shard's trajectory,
+    its carry-in (zeros on the first rank) and the gathered shard products [ranks, B, N, D, D],
+    the last two kept for the backward.  Every rank of the group calls it with its shard."""
+    from .sequence_parallel import sp_forward
+    B, T, N, D, _ = S.shape
+    g, d, ga, sf = _f(gens), _f(dt).reshape(B, T), _f(gamma), _f(S)
+    X, h_in, Ps = sp_forward(g, d, None if ga is None else ga.reshape(B, T, N), sf, _resolve_group(group_name),
+                             None, _basis_name(basis), two_sided)
+    h = h_in if h_in is not None else torch.zeros(B, N, D, D, device=S.device)
+    return X, h, torch.stack(Ps)
+
+
+@sp_scan.register_fake
+def _(gens, dt, gamma, S, group_name, basis, two_sided):
+    import torch.distributed as dist
+    ws = dist.get_world_size(_resolve_group(group_name)) if dist.is_initialized() else 1
+    B, T, N, D, _ = S.shape
+    return (torch.empty_like(S, dtype=torch.float32), S.new_empty((B, N, D, D), dtype=torch.float32),
+            S.new_empty((ws, B, N, D, D), dtype=torch.float32))
+
+
+@torch.library.custom_op("csn::sp_scan_bwd", mutates_args=())
+def sp_scan_bwd(gens: Tensor, dt: Tensor, gamma: Optional[Tensor], S: Tensor, X: Tensor, dX: Tensor,
+                h_in: Tensor, Ps: Tensor, group_name: str, basis: int,
+                two_sided: bool) -> Tuple[Tensor, Tensor, Tensor, Tensor]:
+    """Adjoint of csn::sp_scan on this rank's shard: (dgens, ddt, dgamma or [0], dS)."""
+    from .sequence_parallel import sp_backward
+    B, T, N, D, _ = S.shape
+    ga = _f(gamma)
+    dg, ddt, dga, dS = sp_backward(_f(gens), _f(dt).reshape(B, T), None if ga is None else ga.reshape(B, T, N),
+                                   _f(S), _f(X), _f(dX), _f(h_in), list(_f(Ps).unbind(0)),
+                                   _resolve_group(group_name), None, _basis_name(basis), two_sided)
+    return (dg, ddt.reshape(dt.shape), dga.reshape(gamma.shape) if dga is not None else dS.new_empty((0,)), dS)
+
+
+@sp_scan_bwd.register_fake
+def _(gens, dt, gamma, S, X, dX, h_in, Ps, group_name, basis, two_sided):
+    return (torch.empty_like(gens, dtype=torch.float32), torch.empty_like(dt, dtype=torch.float32),
+            torch.empty_like(gamma, dtype=torch.float32) if gamma is not None else S.new_empty((0,)),
+            torch.empty_like(S, dtype=torch.float32))
+
+
+def _sp_setup(ctx, inputs, output):
+    gens, dt, gamma, S, group_name, basis, two_sided = inputs
+    X, h, Ps = output
+    ctx.save_for_backward(gens, dt, gamma, S, X, h, Ps)
+    ctx.args = (group_name, basis, two_sided)
+
+
+def _sp_backward(ctx, dX, dh, dPs):
+    gens, dt, gamma, S, X, h, Ps = ctx.saved_tensors
+    dg, ddt, dga, dS = torch.ops.csn.sp_scan_bwd(gens, dt, gamma, S, X, dX, h, Ps, *ctx.args)
+    return dg, ddt, (dga if gamma is not None else None), dS, None, None, None
+
+
+sp_scan.register_autograd(_sp_backward, setup_context=_sp_setup)

@@ -95,7 +95,7 @@ def _port():
     return p
 
 
-def _nccl_worker(rank, ws, port, q):
+def _nccl_worker(rank, ws, port, q, use_op=False):
     try:
         for p in (str(REPO / "clifford-space-network_b200"), str(REPO)):
             if p not in sys.path:
@@ -115,7 +115,10 @@ def _nccl_worker(rank, ws, port, q):
         lg = gens[:, sl].contiguous().requires_grad_(True)
         ldt = dt[:, sl].contiguous().requires_grad_(True)
         lS = S[:, sl].contiguous().requires_grad_(True)
-        X = sequence_parallel_rotor_scan(lg, ldt, None, lS)
+        if use_op:  # the torch.library operator, group by name
+            X = torch.ops.csn.sp_scan(lg, ldt, None, lS, dist.group.WORLD.group_name, 0, True)[0]
+        else:
+            X = sequence_parallel_rotor_scan(lg, ldt, None, lS)
         X.backward(dX[:, sl].contiguous())
         tg, tdt, tS = gens.clone().requires_grad_(True), dt.clone().requires_grad_(True), S.clone().requires_grad_(True)
         Xf = ops.fused_rotor_scan(tg, tdt, None, tS)
@@ -130,19 +133,33 @@ def _nccl_worker(rank, ws, port, q):
         q.put((rank, "error", repr(e), traceback.format_exc()))
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_sequence_parallel_over_nccl_ranks():
+def _run_nccl(ws, use_op):
     import torch.multiprocessing as mp
-    ws = min(torch.cuda.device_count(), 4)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_nccl_worker, args=(r, ws, port, q)) for r in range(ws)]
+    procs = [ctx.Process(target=_nccl_worker, args=(r, ws, port, q, use_op)) for r in range(ws)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in range(ws)]
     for p in procs:
         p.join(timeout=60)
-    for r in res:
+    return res
+
+
+def test_sp_scan_operator_on_one_rank():
+    """torch.ops.csn.sp_scan (forward + registered autograd) on a one-rank NCCL group equals
+    the fused scan."""
+    for r in _run_nccl(1, True):
         assert r[1] == "ok", r
         assert max(r[2]) < 1e-4, r
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("use_op", [False, True], ids=["function", "operator"])
+def test_sequence_parallel_over_nccl_ranks(use_op):
+    ws = min(torch.cuda.device_count(), 4)
+    for r in _run_nccl(ws, use_op):
+        assert r[1] == "ok", r
+        assert max(r[2]) < 1e-4, r
+

@@ -11,7 +11,8 @@ def csn_ops():
 
 
 NAMES = ["scan_fwd", "scan_bwd", "fused_rotor_scan_fwd", "fused_rotor_scan_bwd", "cayley_fwd",
-         "cayley_bwd", "cell_fwd", "cell_bwd", "ga3_scan_fwd", "ga3_scan_bwd", "rotor_step"]
+         "cayley_bwd", "cell_fwd", "cell_bwd", "ga3_scan_fwd", "ga3_scan_bwd", "rotor_step", "sp_scan",
+         "sp_scan_bwd"]
 
 
 @pytest.mark.parametrize("name", NAMES)
@@ -34,6 +35,10 @@ def test_fake_shapes_on_meta(csn_ops):
     assert csn_ops.cayley_fwd(m(7, 16, 16)).shape == (7, 16, 16)
     assert csn_ops.cell_fwd(m(4, 3), m(4, 5, 16), m(5, 5, 16), m(5, 3, 16), m(5), 0.02).shape == (4, 5, 16)
     assert csn_ops.ga3_scan_fwd(m(B, T, N, 3), m(B, T), m(B, T, N, 8), None).shape == (B, T, N, 8)
+    X, h, Ps = csn_ops.sp_scan(m(B, T, N, K), m(B, T), None, M, "", 0, True)  # no process group: 1 rank
+    assert X.shape == M.shape and h.shape == (B, N, D, D) and Ps.shape == (1, B, N, D, D)
+    g = csn_ops.sp_scan_bwd(m(B, T, N, K), m(B, T), None, M, X, X, h, Ps, "", 0, True)
+    assert [tuple(t.shape) for t in g] == [(B, T, N, K), (B, T), (0,), (B, T, N, D, D)]
 
 
 def test_schema_arguments_follow_the_ops_api(csn_ops):
@@ -41,3 +46,8 @@ def test_schema_arguments_follow_the_ops_api(csn_ops):
     assert args == ["gens", "dt", "gamma", "S", "h0", "basis", "two_sided"]
     args = [a.name for a in csn_ops.scan_fwd.default._schema.arguments]
     assert args == ["M", "C", "h0", "two_sided", "reverse"]
+
+
+def test_sp_scan_schema(csn_ops):
+    args = [a.name for a in csn_ops.sp_scan.default._schema.arguments]
+    assert args == ["gens", "dt", "gamma", "S", "group_name", "basis", "two_sided"]

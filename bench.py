@@ -768,7 +768,8 @@ def run_lm_train(args, ws, rank, local, cores):
     names = ("fwd_reduce", "fwd_carry", "fwd_apply", "bwd_reduce", "bwd_carry", "bwd_apply", "reduce_channels",
              "spike_fwd", "spike_bwd", "layer_norm_fwd", "layer_norm_bwd", "layer_norm_param_reduce",
              "ln_conv_silu_fwd", "ln_conv_silu_bwd", "ln_conv_silu_param_reduce", "generator_action_fwd",
-             "generator_action_bwd")
+             "generator_action_bwd", "projection_epilogue_fwd", "projection_epilogue_bwd", "column_sum",
+             "silu_gate_fwd", "silu_gate_bwd")
     kt = {n: _lib.timing_read(n) for n in names}
     launches = sum(c for _, c in kt.values())
     _lib.timing_reset()

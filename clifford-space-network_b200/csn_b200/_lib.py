@@ -78,6 +78,13 @@ SIGNATURES = {
                                  _int),
     "csn_generator_action_bwd": ([_f, _f, _f, _f, _i64, _i64, _int, _int, ctypes.c_float, ctypes.c_float, _f, _f,
                                   _f], _int),
+    "csn_projection_epilogue_fwd": ([_f, _i64, _int, _int, _int, _f, ctypes.c_float, _f, _f, _f, _f], _int),
+    "csn_projection_epilogue_bwd": ([_f, _i64, _int, _int, _int, _f, ctypes.c_float, _f, _f, _f, _f, _f, _f],
+                                    _int),
+    "csn_column_sum_workspace_bytes": ([_i64, _int], _sz),
+    "csn_column_sum": ([_f, _i64, _int, _f, _f, _sz, _f], _int),
+    "csn_silu_gate_fwd": ([_f, _i64, _int, _f, _f], _int),
+    "csn_silu_gate_bwd": ([_f, _f, _i64, _int, _f, _f], _int),
     "csn_timing_enable": ([_int], _int),
     "csn_timing_reset": ([], _int),
     "csn_timing_read": ([ctypes.c_char_p, ctypes.POINTER(ctypes.c_double),

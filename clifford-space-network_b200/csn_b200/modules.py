@@ -35,3 +35,18 @@ def causal_conv_input(ln: nn.LayerNorm, conv: nn.Conv1d, x: torch.Tensor) -> tor
             and conv.padding_mode == "zeros" and ops.ln_conv_silu_supported(C, K)):
         return ops.ln_conv_silu(x, ln.weight, ln.bias, ln.eps, conv.weight, conv.bias)
     return F.silu(conv(ln(x).transpose(1, 2))[:, :, :T].transpose(1, 2))
+
+
+def generator_inputs(x: torch.Tensor, biv_proj: nn.Linear, gamma_proj: nn.Linear, time_proj: nn.Linear,
+                     omega_scale: torch.Tensor, dt_base: float):
+    """(biv [..., N*K], gamma [..., N], dt [..., HT]) of the blocks' projections
+    (python/clifford_cl6.py:144-155: biv_proj(x) * omega_scale, softplus(gamma_proj(x)),
+    softplus(time_head.proj(x)) * dt_base) as ONE GEMM over the concatenated weights and the
+    CUDA projection epilogue; the parameters stay the three nn.Linear layers'."""
+    N = gamma_proj.out_features
+    HT = time_proj.out_features
+    K = biv_proj.out_features // N
+    W = torch.cat([biv_proj.weight, gamma_proj.weight, time_proj.weight], 0)
+    b = torch.cat([biv_proj.bias, gamma_proj.bias, time_proj.bias], 0)
+    raw = ops.linear(x, W, b)
+    return ops.projection_epilogue(raw, omega_scale, dt_base, N, K, HT)

@@ -29,7 +29,7 @@ from . import _lib
 
 __all__ = ["rotor_scan", "fused_rotor_scan", "fused_rotor_scan_heads", "cayley", "cell_step", "ga3_rotor_scan",
            "rotor_step", "RotorStepGraph", "state_spike", "layer_norm", "ln_conv_silu",
-           "generator_action", "BASIS"]
+           "generator_action", "linear", "projection_epilogue", "silu_gate", "column_sum", "BASIS"]
 
 BASIS = {"triu": 0, "ga": 1}
 
@@ -639,6 +639,116 @@ def generator_action(biv, dt, D: int):
     if biv.dim() < 3 or dt.shape[:2] != biv.shape[:2] or dt.dim() > 3:
         raise ValueError("generator_action: biv [B, T, ..., K] and dt [B, T] or [B, T, H]")
     return GeneratorActionFunction.apply(biv, dt, int(D))
+
+
+def column_sum(x2d):
+    """Deterministic column sums of a float32 [R, C] CUDA matrix (csn_column_sum)."""
+    _require_cuda(x2d)
+    xf = _f32(x2d)
+    R, C = xf.shape
+    out = torch.empty(C, device=xf.device)
+    nb = _lib.load().csn_column_sum_workspace_bytes(R, C)
+    ws = _workspace(max(nb, 16), xf.device)
+    _lib.call("csn_column_sum", _ptr(xf), R, C, _ptr(out), _ptr(ws), nb, _stream(xf.device))
+    return out
+
+
+class LinearFunction(torch.autograd.Function):
+    """y = x W^T + b with cuBLAS GEMMs both ways and the bias gradient by csn_column_sum."""
+
+    @staticmethod
+    def forward(ctx, x, W, b):
+        _require_cuda(x, W, b)
+        x2 = x.reshape(-1, x.shape[-1])
+        y = torch.addmm(b, x2, W.t()) if b is not None else x2 @ W.t()
+        ctx.save_for_backward(x2, W)
+        ctx.has_b = b is not None
+        ctx.xshape = x.shape
+        return y.view(*x.shape[:-1], W.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, W = ctx.saved_tensors
+        d2 = dy.reshape(-1, dy.shape[-1])
+        dx = (d2 @ W).view(ctx.xshape) if ctx.needs_input_grad[0] else None
+        dW = d2.t() @ x2 if ctx.needs_input_grad[1] else None
+        db = column_sum(d2).to(dy.dtype) if (ctx.has_b and ctx.needs_input_grad[2]) else None
+        return dx, dW, db
+
+
+def linear(x, W, b=None):
+    """F.linear(x, W, b) whose bias gradient is a deterministic CUDA column sum."""
+    return LinearFunction.apply(x, W, b)
+
+
+class ProjectionEpilogueFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, raw, scale, dt_base, N, K, HT):
+        _require_cuda(raw, scale)
+        rf, sf = _f32(raw), _f32(scale)
+        lead = raw.shape[:-1]
+        R = rf.numel() // rf.shape[-1]
+        biv = torch.empty(*lead, N * K, device=rf.device)
+        gamma = torch.empty(*lead, N, device=rf.device)
+        dt = torch.empty(*lead, HT, device=rf.device)
+        _lib.call("csn_projection_epilogue_fwd", _ptr(rf), R, N, K, HT, _ptr(sf), float(dt_base), _ptr(biv),
+                  _ptr(gamma), _ptr(dt), _stream(rf.device))
+        ctx.save_for_backward(rf, sf)
+        ctx.meta = (float(dt_base), N, K, HT, raw.dtype, scale.dtype)
+        return biv, gamma, dt
+
+    @staticmethod
+    def backward(ctx, dbiv, dgamma, ddt):
+        rf, sf = ctx.saved_tensors
+        dt_base, N, K, HT, rdt, sdt = ctx.meta
+        R = rf.numel() // rf.shape[-1]
+        draw = torch.empty_like(rf)
+        part = torch.empty(R, N, device=rf.device)
+        _lib.call("csn_projection_epilogue_bwd", _ptr(rf), R, N, K, HT, _ptr(sf), dt_base,
+                  _ptr(None if dbiv is None else _f32(dbiv)), _ptr(None if dgamma is None else _f32(dgamma)),
+                  _ptr(None if ddt is None else _f32(ddt)), _ptr(draw), _ptr(part), _stream(rf.device))
+        dscale = column_sum(part).to(sdt) if ctx.needs_input_grad[1] else None
+        return draw.to(rdt), dscale, None, None, None, None
+
+
+def projection_epilogue(raw, omega_scale, dt_base: float, N: int, K: int, HT: int):
+    """(biv [..., N*K], gamma [..., N], dt [..., HT]) from the fused projection output raw
+    [..., N*K + N + HT]: biv = raw * omega_scale[n], gamma = softplus, dt = softplus * dt_base
+    (python/clifford_cl6.py:144-155), one CUDA kernel each way."""
+    if raw.shape[-1] != N * K + N + HT or omega_scale.numel() != N:
+        raise ValueError("projection_epilogue: raw must have N*K + N + HT columns and omega_scale N entries")
+    return ProjectionEpilogueFunction.apply(raw, omega_scale.reshape(N), dt_base, N, K, HT)
+
+
+class SiluGateFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, gu):
+        _require_cuda(gu)
+        gf = _f32(gu)
+        F2 = gf.shape[-1]
+        R = gf.numel() // F2
+        y = torch.empty(*gf.shape[:-1], F2 // 2, device=gf.device)
+        _lib.call("csn_silu_gate_fwd", _ptr(gf), R, F2 // 2, _ptr(y), _stream(gf.device))
+        ctx.save_for_backward(gf)
+        ctx.dtype = gu.dtype
+        return y.to(gu.dtype)
+
+    @staticmethod
+    def backward(ctx, dy):
+        (gf,) = ctx.saved_tensors
+        F2 = gf.shape[-1]
+        R = gf.numel() // F2
+        dgu = torch.empty_like(gf)
+        _lib.call("csn_silu_gate_bwd", _ptr(gf), _ptr(_f32(dy)), R, F2 // 2, _ptr(dgu), _stream(gf.device))
+        return dgu.to(ctx.dtype)
+
+
+def silu_gate(gu):
+    """silu(g) * u for gu = [g | u] on the last axis (GeometricGatedLinearUnit's gate,
+    python/clifford_model.py:42-43), one CUDA kernel each way."""
+    if gu.shape[-1] % 2:
+        raise ValueError("silu_gate: the last axis must hold [g | u]")
+    return SiluGateFunction.apply(gu)
 
 
 # torch.ops.csn.* registrations (needs the helpers above; imported last on purpose)

@@ -31,6 +31,16 @@
 //   dw_t = 2 c_k g_k w_t + 2 c_s g_s ((w_t - w_{t-1}) [t >= 1] - (w_{t+1} - w_t) [t <= T - 2])
 //   dbiv = 0.5 dt dw,  ddt[b, t, h] = sum_{j in head h} 0.5 biv dw
 // The gradient scalars are read on the device, so no host synchronisation is needed.
+//
+// Projection epilogue (python/clifford_cl6.py:144-155): the generator, decay and time
+// projections run as ONE GEMM whose rows hold Q = N*K + N + HT columns
+// [generators | gamma | time]; the epilogue writes the scan's inputs
+//   biv = raw * omega_scale[n],  gamma = softplus(raw),  dt = softplus(raw) * dt_base
+// (softplus(x) = x above 20, as torch) and its adjoint writes the GEMM output's gradient in
+// the same layout plus per-row partials of d omega_scale (summed by the column sum).
+// Column sum: deterministic sums of the rows of a [R, C] matrix (bias gradients).
+// Gate of the GGLU: y = silu(g) * u on one [R, 2F] GEMM output [g | u], and its adjoint into
+// one [R, 2F] gradient (python/clifford_model.py:42-43).
 #include <cstdio>
 
 #include "csn_common.cuh"
@@ -873,6 +883,147 @@ unsigned action_grid(int64_t rows) {
   return (unsigned)(blocks < cap ? (blocks > 0 ? blocks : 1) : cap);
 }
 
+// --------------------------------------------------------------- projection epilogue
+__device__ __forceinline__ float softplus_f(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
+__device__ __forceinline__ float softplus_grad(float x) {
+  if (x > 20.0f) return 1.0f;
+  const float z = expf(x);
+  return z / (z + 1.0f);
+}
+
+__global__ void __launch_bounds__(256) proj_epilogue_fwd_kernel(const float* __restrict__ raw, int64_t R, int N, int K,
+                                                                int HT, const float* __restrict__ scale, float dt_base,
+                                                                float* __restrict__ biv, float* __restrict__ gamma,
+                                                                float* __restrict__ dt) {
+  const int NK = N * K, Q = NK + N + HT;
+  const int64_t total = R * Q;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / Q;
+    const int c = (int)(i - r * Q);
+    const float v = __ldg(raw + i);
+    if (c < NK) biv[r * NK + c] = v * __ldg(scale + c / K);
+    else if (c < NK + N) gamma[r * N + (c - NK)] = softplus_f(v);
+    else dt[r * HT + (c - NK - N)] = softplus_f(v) * dt_base;
+  }
+}
+
+// thread per (row, j): j < N writes the K generator gradients and the gamma gradient of
+// neuron j and part[r, j] = sum_k dbiv raw; j >= N writes the gradient of time column j - N.
+__global__ void __launch_bounds__(256) proj_epilogue_bwd_kernel(const float* __restrict__ raw, int64_t R, int N, int K,
+                                                                int HT, const float* __restrict__ scale, float dt_base,
+                                                                const float* __restrict__ dbiv,
+                                                                const float* __restrict__ dgamma,
+                                                                const float* __restrict__ ddt, float* __restrict__ draw,
+                                                                float* __restrict__ part) {
+  const int NK = N * K, Q = NK + N + HT, J = N + HT;
+  const int64_t total = R * J;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / J;
+    const int j = (int)(i - r * J);
+    const float* rr = raw + r * Q;
+    float* dr = draw + r * Q;
+    if (j < N) {
+      const float sc = __ldg(scale + j);
+      float acc = 0.0f;
+      for (int k = 0; k < K; ++k) {
+        const float g = dbiv ? __ldg(dbiv + r * NK + j * K + k) : 0.0f;
+        dr[j * K + k] = g * sc;
+        acc = fmaf(g, __ldg(rr + j * K + k), acc);
+      }
+      part[r * N + j] = acc;
+      const float gg = dgamma ? __ldg(dgamma + r * N + j) : 0.0f;
+      dr[NK + j] = gg * softplus_grad(__ldg(rr + NK + j));
+    } else {
+      const int h = j - N;
+      const float gd = ddt ? __ldg(ddt + r * HT + h) : 0.0f;
+      dr[NK + N + h] = gd * dt_base * softplus_grad(__ldg(rr + NK + N + h));
+    }
+  }
+}
+
+// ------------------------------------------------------------------- column sum
+// part[cta, c] = sum over this CTA's rows (contiguous row range); 256 threads over columns.
+__global__ void __launch_bounds__(256) colsum_partial_kernel(const float* __restrict__ x, int64_t R, int C, int64_t rows_per,
+                                                             float* __restrict__ part) {
+  const int64_t r0 = blockIdx.x * rows_per;
+  const int64_t r1 = min(R, r0 + rows_per);
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    float t0 = 0.0f, t1 = 0.0f, t2 = 0.0f, t3 = 0.0f;
+    int64_t r = r0;
+    for (; r + 3 < r1; r += 4) {
+      t0 += __ldg(x + r * C + c);
+      t1 += __ldg(x + (r + 1) * C + c);
+      t2 += __ldg(x + (r + 2) * C + c);
+      t3 += __ldg(x + (r + 3) * C + c);
+    }
+    for (; r < r1; ++r) t0 += __ldg(x + r * C + c);
+    part[(int64_t)blockIdx.x * C + c] = (t0 + t1) + (t2 + t3);
+  }
+}
+
+// out[c] = sum_p part[p, c]: 32 columns per CTA, 8 warps over interleaved rows, fixed order.
+__global__ void __launch_bounds__(256) colsum_finish_kernel(const float* __restrict__ part, int P, int C,
+                                                            float* __restrict__ out) {
+  __shared__ float acc[8][33];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + lane;
+  float t0 = 0.0f, t1 = 0.0f;
+  if (c < C) {
+    int p = wid;
+    for (; p + 8 < P; p += 16) {
+      t0 += part[(int64_t)p * C + c];
+      t1 += part[(int64_t)(p + 8) * C + c];
+    }
+    for (; p < P; p += 8) t0 += part[(int64_t)p * C + c];
+  }
+  acc[wid][lane] = t0 + t1;
+  __syncthreads();
+  if (wid == 0 && c < C) {
+    float u = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) u += acc[w][lane];
+    out[c] = u;
+  }
+}
+
+void colsum_plan(int64_t R, int64_t& ctas, int64_t& rows_per) {
+  const int64_t target = 148 * 4;
+  rows_per = (R + target - 1) / target;
+  if (rows_per < 16) rows_per = 16;
+  ctas = (R + rows_per - 1) / rows_per;
+  if (ctas < 1) ctas = 1;
+}
+
+// ------------------------------------------------------------------------ gate
+__global__ void __launch_bounds__(256) silu_gate_fwd_kernel(const float* __restrict__ gu, int64_t R, int F,
+                                                            float* __restrict__ y) {
+  const int64_t total = R * F;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / F;
+    const int f = (int)(i - r * F);
+    const float g = __ldg(gu + r * 2 * F + f), u = __ldg(gu + r * 2 * F + F + f);
+    y[i] = silu_f(g) * u;
+  }
+}
+
+__global__ void __launch_bounds__(256) silu_gate_bwd_kernel(const float* __restrict__ gu, const float* __restrict__ dy,
+                                                            int64_t R, int F, float* __restrict__ dgu) {
+  const int64_t total = R * F;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / F;
+    const int f = (int)(i - r * F);
+    const float g = __ldg(gu + r * 2 * F + f), u = __ldg(gu + r * 2 * F + F + f), d = __ldg(dy + i);
+    dgu[r * 2 * F + f] = d * u * silu_grad(g);
+    dgu[r * 2 * F + F + f] = d * silu_f(g);
+  }
+}
+
+unsigned elem_grid(int64_t n) {
+  const int64_t blocks = (n + 255) / 256;
+  const int64_t cap = 148 * 16;
+  return (unsigned)(blocks < cap ? (blocks > 0 ? blocks : 1) : cap);
+}
+
 }  // namespace
 }  // namespace csn
 
@@ -1081,4 +1232,84 @@ extern "C" int csn_generator_action_bwd(const float* biv, const float* dt, const
     gen_action_bwd_kernel<1><<<action_grid(B * T), 256, 0, st>>>(biv, dt, g_kin, g_smooth, c_kin, c_smooth, B, T, R,
                                                                  H, dbiv, ddt);
   return check_launch("csn_generator_action_bwd");
+}
+
+extern "C" int csn_projection_epilogue_fwd(const float* raw, int64_t R, int N, int K, int HT,
+                                           const float* omega_scale, float dt_base, float* biv, float* gamma,
+                                           float* dt, void* stream) {
+  if (R < 0 || N < 0 || K < 0 || HT < 0) return set_error(CSN_ERR_INVALID, "csn_projection_epilogue_fwd: negative size");
+  const int64_t Q = (int64_t)N * K + N + HT;
+  if (R * Q == 0) return CSN_OK;
+  if (!raw || (N * K > 0 && (!omega_scale || !biv)) || (N > 0 && !gamma) || (HT > 0 && !dt))
+    return set_error(CSN_ERR_INVALID, "csn_projection_epilogue_fwd: missing pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  KernelTimer kt("projection_epilogue_fwd", st);
+  proj_epilogue_fwd_kernel<<<elem_grid(R * Q), 256, 0, st>>>(raw, R, N, K, HT, omega_scale, dt_base, biv, gamma, dt);
+  return check_launch("csn_projection_epilogue_fwd");
+}
+
+extern "C" int csn_projection_epilogue_bwd(const float* raw, int64_t R, int N, int K, int HT,
+                                           const float* omega_scale, float dt_base, const float* dbiv,
+                                           const float* dgamma, const float* ddt, float* draw, float* scale_part,
+                                           void* stream) {
+  if (R < 0 || N < 0 || K < 0 || HT < 0) return set_error(CSN_ERR_INVALID, "csn_projection_epilogue_bwd: negative size");
+  const int64_t J = (int64_t)N + HT;
+  if (R * J == 0) return CSN_OK;
+  if (!raw || !draw || (N > 0 && (!omega_scale || !scale_part)))
+    return set_error(CSN_ERR_INVALID, "csn_projection_epilogue_bwd: missing pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  KernelTimer kt("projection_epilogue_bwd", st);
+  proj_epilogue_bwd_kernel<<<elem_grid(R * J), 256, 0, st>>>(raw, R, N, K, HT, omega_scale, dt_base, dbiv, dgamma,
+                                                               ddt, draw, scale_part);
+  return check_launch("csn_projection_epilogue_bwd");
+}
+
+extern "C" size_t csn_column_sum_workspace_bytes(int64_t R, int C) {
+  if (R <= 0 || C <= 0) return 0;
+  int64_t ctas, rows_per;
+  colsum_plan(R, ctas, rows_per);
+  return (size_t)ctas * (size_t)C * sizeof(float);
+}
+
+extern "C" int csn_column_sum(const float* x, int64_t R, int C, float* out, void* workspace, size_t workspace_bytes,
+                              void* stream) {
+  if (R < 0 || C < 0) return set_error(CSN_ERR_INVALID, "csn_column_sum: negative size");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (C == 0) return CSN_OK;
+  if (!out) return set_error(CSN_ERR_INVALID, "csn_column_sum: out is required");
+  if (R == 0) {
+    if (cudaMemsetAsync(out, 0, sizeof(float) * C, st) != cudaSuccess)
+      return set_error(CSN_ERR_CUDA, "csn_column_sum: cudaMemsetAsync");
+    return CSN_OK;
+  }
+  if (!x) return set_error(CSN_ERR_INVALID, "csn_column_sum: x is required");
+  int64_t ctas, rows_per;
+  colsum_plan(R, ctas, rows_per);
+  if (!workspace || workspace_bytes < csn_column_sum_workspace_bytes(R, C))
+    return set_error(CSN_ERR_INVALID, "csn_column_sum: workspace smaller than csn_column_sum_workspace_bytes");
+  float* part = static_cast<float*>(workspace);
+  KernelTimer kt("column_sum", st);
+  colsum_partial_kernel<<<(unsigned)ctas, 256, 0, st>>>(x, R, C, rows_per, part);
+  colsum_finish_kernel<<<(unsigned)((C + 31) / 32), 256, 0, st>>>(part, (int)ctas, C, out);
+  return check_launch("csn_column_sum");
+}
+
+extern "C" int csn_silu_gate_fwd(const float* gu, int64_t R, int F, float* y, void* stream) {
+  if (R < 0 || F < 0) return set_error(CSN_ERR_INVALID, "csn_silu_gate_fwd: negative size");
+  if (R * F == 0) return CSN_OK;
+  if (!gu || !y) return set_error(CSN_ERR_INVALID, "csn_silu_gate_fwd: missing pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  KernelTimer kt("silu_gate_fwd", st);
+  silu_gate_fwd_kernel<<<elem_grid(R * F), 256, 0, st>>>(gu, R, F, y);
+  return check_launch("csn_silu_gate_fwd");
+}
+
+extern "C" int csn_silu_gate_bwd(const float* gu, const float* dy, int64_t R, int F, float* dgu, void* stream) {
+  if (R < 0 || F < 0) return set_error(CSN_ERR_INVALID, "csn_silu_gate_bwd: negative size");
+  if (R * F == 0) return CSN_OK;
+  if (!gu || !dy || !dgu) return set_error(CSN_ERR_INVALID, "csn_silu_gate_bwd: missing pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  KernelTimer kt("silu_gate_bwd", st);
+  silu_gate_bwd_kernel<<<elem_grid(R * F), 256, 0, st>>>(gu, dy, R, F, dgu);
+  return check_launch("csn_silu_gate_bwd");
 }

@@ -8,7 +8,10 @@
   * the inter-neuron mixing of line 179 is linear, so it is folded into out_proj's weight
     (W_out (W_mix (x) I_64), a [d_model, N*64] matrix built per call): X_mixed is never formed;
   * ln_1 -> causal depthwise conv -> SiLU (lines 140-142) is one CUDA kernel each way
-    (csn_b200.modules.causal_conv_input), and ln_2 runs the CUDA LayerNorm kernels.
+    (csn_b200.modules.causal_conv_input), and ln_2 runs the CUDA LayerNorm kernels;
+  * the generator, decay and time projections (lines 144-155) are one GEMM whose output
+    the CUDA projection epilogue turns into the scan's inputs (omega_scale, softplus, dt_base);
+    bias gradients are deterministic CUDA column sums (csn_b200.ops.linear).
 Omega is still returned by forward(); CliffordCL6ForCausalLM takes its action regulariser from
 the generator coefficients instead (sum Omega^2 = 2 sum (0.5 dt biv)^2), so it never forms Omega.
 """
@@ -20,7 +23,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from csn_b200 import ops
-from csn_b200.modules import LayerNorm, causal_conv_input
+from csn_b200.modules import LayerNorm, causal_conv_input, generator_inputs
 from python.clifford_model import GeometricGatedLinearUnit, RiemannianGeodesicHead
 from python.clifford_scan import parallel_rotor_scan, surrogate_spike  # noqa: F401 (re-export)
 
@@ -108,13 +111,14 @@ class CliffordCL6Block(nn.Module):
         N = self.num_neurons
         residual = x
         x_conv = causal_conv_input(self.ln_1, self.conv1d, x)      # ln_1 -> causal conv -> SiLU, fused
-        dt = self.time_head(x_conv).view(B, T)
-        S = self.in_proj(x_conv).view(B, T, N, 8, 8)
-        gamma = F.softplus(self.gamma_proj(x_conv))                   # [B, T, N]
-        biv = self.biv_proj(x_conv).view(B, T, N, 28) * self.omega_scale
+        S = ops.linear(x_conv, self.in_proj.weight, self.in_proj.bias).view(B, T, N, 8, 8)
+        # lines 144-155: generator, decay and time projections as one GEMM + CUDA epilogue
+        biv, gamma, dt = generator_inputs(x_conv, self.biv_proj, self.gamma_proj, self.time_head.proj,
+                                          self.omega_scale, self.time_head.dt_base)
+        biv, dt = biv.view(B, T, N, 28), dt.view(B, T)
         X_all = ops.fused_rotor_scan(biv, dt, gamma, S)               # lines 150-171 fused
         X_spiked = ops.state_spike(X_all, self.spike_threshold, self.spike_beta)
-        h = residual + F.linear(X_spiked.view(B, T, N * 64), self.mixed_out_weight(), self.out_proj.bias)
+        h = residual + ops.linear(X_spiked.view(B, T, N * 64), self.mixed_out_weight(), self.out_proj.bias)
         out = h + self.gglu(self.ln_2(h))
         return out, biv, dt
 

@@ -14,7 +14,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from csn_b200 import ops
-from csn_b200.modules import LayerNorm, causal_conv_input
+from csn_b200.modules import LayerNorm, causal_conv_input, generator_inputs
 from python.clifford_cl6 import AdaptiveTimeHead, generator_action, read_diagnostics, skew_from_generators
 from python.clifford_model import GeometricGatedLinearUnit, RiemannianGeodesicHead
 from python.clifford_scan import parallel_rotor_scan, surrogate_spike  # noqa: F401 (re-export)
@@ -72,13 +72,13 @@ class CliffordCL8Block(nn.Module):
         N = self.num_neurons
         residual = x
         x_conv = causal_conv_input(self.ln_1, self.conv1d, x)      # ln_1 -> causal conv -> SiLU, fused
-        dt = self.time_head(x_conv).view(B, T)
-        S = self.in_proj(x_conv).view(B, T, N, 16, 16)
-        gamma = F.softplus(self.gamma_proj(x_conv))
-        biv = self.biv_proj(x_conv).view(B, T, N, self.num_biv) * self.omega_scale
+        S = ops.linear(x_conv, self.in_proj.weight, self.in_proj.bias).view(B, T, N, 16, 16)
+        biv, gamma, dt = generator_inputs(x_conv, self.biv_proj, self.gamma_proj, self.time_head.proj,
+                                          self.omega_scale, self.time_head.dt_base)
+        biv, dt = biv.view(B, T, N, self.num_biv), dt.view(B, T)
         X_all = ops.fused_rotor_scan(biv, dt, gamma, S, two_sided=not self.is_spinor_bundle)
         X_spiked = ops.state_spike(X_all, self.spike_threshold, self.spike_beta)
-        h = residual + F.linear(X_spiked.view(B, T, N * 256), self.mixed_out_weight(), self.out_proj.bias)
+        h = residual + ops.linear(X_spiked.view(B, T, N * 256), self.mixed_out_weight(), self.out_proj.bias)
         out = h + self.gglu(self.ln_2(h))
         return out, biv, dt
 

@@ -19,7 +19,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from csn_b200 import ops
-from csn_b200.modules import LayerNorm, causal_conv_input
+from csn_b200.modules import LayerNorm, causal_conv_input, generator_inputs
 from python.clifford_cl6 import (cayley_rotor_8x8, generator_action, read_diagnostics,  # noqa: F401
                                  skew_from_generators)
 from python.clifford_model import GeometricGatedLinearUnit, RiemannianGeodesicHead
@@ -83,14 +83,14 @@ class MultiHeadCliffordCL6Block(nn.Module):
         H, Nh = self.num_heads, self.num_neurons_per_head
         residual = x
         x_conv = causal_conv_input(self.ln_1, self.conv1d, x)      # ln_1 -> causal conv -> SiLU, fused
-        dt = self.time_head(x_conv)                                          # [B, T, H]
-        S = self.in_proj(x_conv).view(B, T, H, Nh, 8, 8)
-        gamma = F.softplus(self.gamma_proj(x_conv)).view(B, T, H, Nh)
-        biv = self.biv_proj(x_conv).view(B, T, H, Nh, 28) * self.omega_scale
+        S = ops.linear(x_conv, self.in_proj.weight, self.in_proj.bias).view(B, T, H, Nh, 8, 8)
+        biv, gamma, dt = generator_inputs(x_conv, self.biv_proj, self.gamma_proj, self.time_head.proj,
+                                          self.omega_scale, self.time_head.dt_base)       # dt [B, T, H]
+        biv, gamma = biv.view(B, T, H, Nh, 28), gamma.view(B, T, H, Nh)
         # lines 137-173 fused: per-head dt, heads read in place, X [B, T, H, Nh, 8, 8]
         X = ops.fused_rotor_scan_heads(biv, dt, gamma, S)
         X = ops.state_spike(X, self.spike_threshold, self.spike_beta)
-        h = residual + F.linear(X.view(B, T, self.total_neurons * 64), self.mixed_out_weight(), self.out_proj.bias)
+        h = residual + ops.linear(X.view(B, T, self.total_neurons * 64), self.mixed_out_weight(), self.out_proj.bias)
         out = h + self.gglu(self.ln_2(h))
         return out, biv, dt
 

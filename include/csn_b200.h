@@ -336,6 +336,33 @@ int csn_generator_action_bwd(const float* biv, const float* dt, const float* g_k
                              const float* g_smooth, int64_t B, int64_t T, int R, int H, float c_kin,
                              float c_smooth, float* dbiv, float* ddt, void* stream);
 
+/* Projection epilogue of the blocks (python/clifford_cl6.py:144-155; clifford_cl8.py,
+ * clifford_multihead.py likewise): the generator, decay and time projections computed as one
+ * GEMM give raw [R, Q] with Q = N*K + N + HT columns [generators | gamma | time]; the forward
+ * writes the scan's inputs
+ *   biv[r, n, k] = raw[r, n*K + k] * omega_scale[n],   gamma[r, n] = softplus(raw[r, N*K + n]),
+ *   dt[r, h] = softplus(raw[r, N*K + N + h]) * dt_base          (softplus(x) = x for x > 20);
+ * the backward writes draw [R, Q] from dbiv, dgamma, ddt (each may be NULL = 0) and
+ * scale_part[r, n] = sum_k dbiv[r, n, k] raw[r, n*K + k], whose column sum is d omega_scale. */
+int csn_projection_epilogue_fwd(const float* raw, int64_t R, int N, int K, int HT,
+                                const float* omega_scale, float dt_base, float* biv, float* gamma,
+                                float* dt, void* stream);
+int csn_projection_epilogue_bwd(const float* raw, int64_t R, int N, int K, int HT,
+                                const float* omega_scale, float dt_base, const float* dbiv,
+                                const float* dgamma, const float* ddt, float* draw,
+                                float* scale_part, void* stream);
+
+/* out[c] = sum_r x[r, c] for x [R, C] row-major, summed in a fixed order (deterministic): the
+ * bias gradients of the blocks' projections.  Workspace: csn_column_sum_workspace_bytes. */
+size_t csn_column_sum_workspace_bytes(int64_t R, int C);
+int csn_column_sum(const float* x, int64_t R, int C, float* out, void* workspace,
+                   size_t workspace_bytes, void* stream);
+
+/* Gate of GeometricGatedLinearUnit (python/clifford_model.py:42-43) on one GEMM output
+ * gu [R, 2F] = [x W_gate^T | x W_up^T]:  y = silu(g) * u  [R, F];  backward dgu [R, 2F]. */
+int csn_silu_gate_fwd(const float* gu, int64_t R, int F, float* y, void* stream);
+int csn_silu_gate_bwd(const float* gu, const float* dy, int64_t R, int F, float* dgu, void* stream);
+
 /* -------------------------------------------------------------- kernel timing */
 /* Measurement hook with no counterpart in the reference (which times with wall clock,
  * tests/profile_performance.py:41-71).  While enabled, every kernel the library

@@ -202,3 +202,73 @@ def test_generator_action_matches_omega_form(ops, case):
     d64.grad = None
     reference_action(b64, d64, D)[0].backward()
     assert rel(b32.grad, b64.grad) < 1e-5 and rel(d32.grad, d64.grad) < 1e-5
+
+
+@pytest.mark.parametrize("N,K,HT", [(8, 28, 1), (2, 120, 1), (6, 28, 3)])
+def test_projection_epilogue_matches_torch(ops, N, K, HT):
+    """biv * omega_scale, softplus(gamma), softplus(time) * dt_base on the fused projection output
+    (python/clifford_cl6.py:144-155), forward and gradients, including raw values above
+    softplus's threshold of 20."""
+    rng = np.random.default_rng(N * 7 + K + HT)
+    R = 333
+    raw = rng.standard_normal((3, R, N * K + N + HT)) * 4.0
+    raw[0, :5] = 25.0
+    scale = rng.standard_normal((N, 1)) * 3.0
+    gb, gg, gd = (rng.standard_normal(s) for s in ((3, R, N * K), (3, R, N), (3, R, HT)))
+    F = torch.nn.functional
+    r64 = torch.tensor(raw, dtype=torch.float64, device=DEV, requires_grad=True)
+    s64 = torch.tensor(scale, dtype=torch.float64, device=DEV, requires_grad=True)
+    biv = (r64[..., :N * K].reshape(3, R, N, K) * s64).reshape(3, R, N * K)
+    gam = F.softplus(r64[..., N * K:N * K + N])
+    dt = F.softplus(r64[..., N * K + N:]) * 0.05
+    loss = sum((a * torch.tensor(g, dtype=torch.float64, device=DEV)).sum() for a, g in ((biv, gb), (gam, gg), (dt, gd)))
+    loss.backward()
+    r32 = torch.tensor(raw, dtype=torch.float32, device=DEV, requires_grad=True)
+    s32 = torch.tensor(scale, dtype=torch.float32, device=DEV, requires_grad=True)
+    ob, og, od = ops.projection_epilogue(r32, s32, 0.05, N, K, HT)
+    loss32 = sum((a * torch.tensor(g, dtype=torch.float32, device=DEV)).sum() for a, g in ((ob, gb), (og, gg), (od, gd)))
+    loss32.backward()
+    for a, r in ((ob, biv), (og, gam), (od, dt)):
+        assert rel(a, r) < 1e-6
+    assert rel(r32.grad, r64.grad) < 1e-5
+    assert rel(s32.grad, s64.grad) < 1e-5
+
+
+@pytest.mark.parametrize("R,C", [(1, 1), (7, 3), (65536, 224), (1000, 512)])
+def test_column_sum_is_deterministic_and_exact(ops, R, C):
+    rng = np.random.default_rng(R + C)
+    x = rng.standard_normal((R, C))
+    got = ops.column_sum(torch.tensor(x, dtype=torch.float32, device=DEV))
+    assert rel(got, torch.tensor(x.sum(0))) < 1e-5
+    assert torch.equal(got, ops.column_sum(torch.tensor(x, dtype=torch.float32, device=DEV)))
+
+
+def test_linear_matches_torch_linear(ops):
+    torch.manual_seed(0)
+    x = torch.randn(4, 50, 128, device=DEV, dtype=torch.float64)
+    W = torch.randn(233, 128, device=DEV, dtype=torch.float64)
+    b = torch.randn(233, device=DEV, dtype=torch.float64)
+    dy = torch.randn(4, 50, 233, device=DEV, dtype=torch.float64)
+    ts = [t.clone().requires_grad_(True) for t in (x, W, b)]
+    (torch.nn.functional.linear(*ts) * dy).sum().backward()
+    us = [t.float().clone().requires_grad_(True) for t in (x, W, b)]
+    y = ops.linear(*us)
+    (y * dy.float()).sum().backward()
+    assert rel(y, torch.nn.functional.linear(x, W, b)) < 1e-5
+    for a, r in zip(us, ts):
+        assert rel(a.grad, r.grad) < 1e-5
+
+
+@pytest.mark.parametrize("F_", [1, 256, 100])
+def test_silu_gate_matches_torch(ops, F_):
+    rng = np.random.default_rng(F_)
+    gu = rng.standard_normal((3, 77, 2 * F_)) * 3
+    dy = rng.standard_normal((3, 77, F_))
+    g64 = torch.tensor(gu, dtype=torch.float64, device=DEV, requires_grad=True)
+    ref = torch.nn.functional.silu(g64[..., :F_]) * g64[..., F_:]
+    (ref * torch.tensor(dy, dtype=torch.float64, device=DEV)).sum().backward()
+    g32 = torch.tensor(gu, dtype=torch.float32, device=DEV, requires_grad=True)
+    got = ops.silu_gate(g32)
+    (got * torch.tensor(dy, dtype=torch.float32, device=DEV)).sum().backward()
+    assert rel(got, ref) < 1e-6
+    assert rel(g32.grad, g64.grad) < 1e-5

@@ -891,52 +891,46 @@ __device__ __forceinline__ float softplus_grad(float x) {
   return z / (z + 1.0f);
 }
 
+// One warp per row: lanes walk the row's columns (coalesced).
 __global__ void __launch_bounds__(256) proj_epilogue_fwd_kernel(const float* __restrict__ raw, int64_t R, int N, int K,
                                                                 int HT, const float* __restrict__ scale, float dt_base,
                                                                 float* __restrict__ biv, float* __restrict__ gamma,
                                                                 float* __restrict__ dt) {
+  const int lane = threadIdx.x & 31;
   const int NK = N * K, Q = NK + N + HT;
-  const int64_t total = R * Q;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / Q;
-    const int c = (int)(i - r * Q);
-    const float v = __ldg(raw + i);
-    if (c < NK) biv[r * NK + c] = v * __ldg(scale + c / K);
-    else if (c < NK + N) gamma[r * N + (c - NK)] = softplus_f(v);
-    else dt[r * HT + (c - NK - N)] = softplus_f(v) * dt_base;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < R; r += warps) {
+    const float* rr = raw + r * Q;
+    for (int c = lane; c < NK; c += 32) biv[r * NK + c] = __ldg(rr + c) * __ldg(scale + c / K);
+    for (int c = lane; c < N; c += 32) gamma[r * N + c] = softplus_f(__ldg(rr + NK + c));
+    for (int c = lane; c < HT; c += 32) dt[r * HT + c] = softplus_f(__ldg(rr + NK + N + c)) * dt_base;
   }
 }
 
-// thread per (row, j): j < N writes the K generator gradients and the gamma gradient of
-// neuron j and part[r, j] = sum_k dbiv raw; j >= N writes the gradient of time column j - N.
+// One warp per row: the gradient row elementwise (coalesced), then lane n sums neuron n's
+// K products for part[r, n] (the row is in L1 by then).
 __global__ void __launch_bounds__(256) proj_epilogue_bwd_kernel(const float* __restrict__ raw, int64_t R, int N, int K,
                                                                 int HT, const float* __restrict__ scale, float dt_base,
                                                                 const float* __restrict__ dbiv,
                                                                 const float* __restrict__ dgamma,
                                                                 const float* __restrict__ ddt, float* __restrict__ draw,
                                                                 float* __restrict__ part) {
-  const int NK = N * K, Q = NK + N + HT, J = N + HT;
-  const int64_t total = R * J;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / J;
-    const int j = (int)(i - r * J);
+  const int lane = threadIdx.x & 31;
+  const int NK = N * K, Q = NK + N + HT;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < R; r += warps) {
     const float* rr = raw + r * Q;
     float* dr = draw + r * Q;
-    if (j < N) {
-      const float sc = __ldg(scale + j);
+    for (int c = lane; c < NK; c += 32) dr[c] = (dbiv ? __ldg(dbiv + r * NK + c) : 0.0f) * __ldg(scale + c / K);
+    for (int c = lane; c < N; c += 32)
+      dr[NK + c] = (dgamma ? __ldg(dgamma + r * N + c) : 0.0f) * softplus_grad(__ldg(rr + NK + c));
+    for (int c = lane; c < HT; c += 32)
+      dr[NK + N + c] = (ddt ? __ldg(ddt + r * HT + c) : 0.0f) * dt_base * softplus_grad(__ldg(rr + NK + N + c));
+    for (int n = lane; n < N; n += 32) {
       float acc = 0.0f;
-      for (int k = 0; k < K; ++k) {
-        const float g = dbiv ? __ldg(dbiv + r * NK + j * K + k) : 0.0f;
-        dr[j * K + k] = g * sc;
-        acc = fmaf(g, __ldg(rr + j * K + k), acc);
-      }
-      part[r * N + j] = acc;
-      const float gg = dgamma ? __ldg(dgamma + r * N + j) : 0.0f;
-      dr[NK + j] = gg * softplus_grad(__ldg(rr + NK + j));
-    } else {
-      const int h = j - N;
-      const float gd = ddt ? __ldg(ddt + r * HT + h) : 0.0f;
-      dr[NK + N + h] = gd * dt_base * softplus_grad(__ldg(rr + NK + N + h));
+      if (dbiv)
+        for (int k = 0; k < K; ++k) acc = fmaf(__ldg(dbiv + r * NK + n * K + k), __ldg(rr + n * K + k), acc);
+      part[r * N + n] = acc;
     }
   }
 }
@@ -995,31 +989,72 @@ void colsum_plan(int64_t R, int64_t& ctas, int64_t& rows_per) {
 }
 
 // ------------------------------------------------------------------------ gate
+// One warp per row; V = 4: float4 columns (F % 4 == 0, 16-byte aligned rows).
+template <int V>
+__device__ __forceinline__ void ld_v(const float* p, float (&v)[V]) {
+  if constexpr (V == 4) {
+    const float4 f = __ldg(reinterpret_cast<const float4*>(p));
+    v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+  } else {
+    v[0] = __ldg(p);
+  }
+}
+template <int V>
+__device__ __forceinline__ void st_v(float* p, const float (&v)[V]) {
+  if constexpr (V == 4) *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  else p[0] = v[0];
+}
+
+template <int V>
 __global__ void __launch_bounds__(256) silu_gate_fwd_kernel(const float* __restrict__ gu, int64_t R, int F,
                                                             float* __restrict__ y) {
-  const int64_t total = R * F;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / F;
-    const int f = (int)(i - r * F);
-    const float g = __ldg(gu + r * 2 * F + f), u = __ldg(gu + r * 2 * F + F + f);
-    y[i] = silu_f(g) * u;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < R; r += warps) {
+    const float* g0 = gu + r * 2 * F;
+    for (int f = V * lane; f < F; f += 32 * V) {
+      float g[V], u[V], o[V];
+      ld_v<V>(g0 + f, g);
+      ld_v<V>(g0 + F + f, u);
+#pragma unroll
+      for (int q = 0; q < V; ++q) o[q] = silu_f(g[q]) * u[q];
+      st_v<V>(y + r * F + f, o);
+    }
   }
 }
 
+template <int V>
 __global__ void __launch_bounds__(256) silu_gate_bwd_kernel(const float* __restrict__ gu, const float* __restrict__ dy,
                                                             int64_t R, int F, float* __restrict__ dgu) {
-  const int64_t total = R * F;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / F;
-    const int f = (int)(i - r * F);
-    const float g = __ldg(gu + r * 2 * F + f), u = __ldg(gu + r * 2 * F + F + f), d = __ldg(dy + i);
-    dgu[r * 2 * F + f] = d * u * silu_grad(g);
-    dgu[r * 2 * F + F + f] = d * silu_f(g);
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < R; r += warps) {
+    const float* g0 = gu + r * 2 * F;
+    float* d0 = dgu + r * 2 * F;
+    for (int f = V * lane; f < F; f += 32 * V) {
+      float g[V], u[V], d[V], dg[V], du[V];
+      ld_v<V>(g0 + f, g);
+      ld_v<V>(g0 + F + f, u);
+      ld_v<V>(dy + r * F + f, d);
+#pragma unroll
+      for (int q = 0; q < V; ++q) {
+        dg[q] = d[q] * u[q] * silu_grad(g[q]);
+        du[q] = d[q] * silu_f(g[q]);
+      }
+      st_v<V>(d0 + f, dg);
+      st_v<V>(d0 + F + f, du);
+    }
   }
 }
 
-unsigned elem_grid(int64_t n) {
-  const int64_t blocks = (n + 255) / 256;
+bool gate_vec4(const void* a, const void* b, const void* c, int F) {
+  const uintptr_t m = reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+                      reinterpret_cast<uintptr_t>(c);
+  return F % 4 == 0 && (m & 15u) == 0;
+}
+
+unsigned row_grid(int64_t rows) {  // warp per row, 8 warps per CTA
+  const int64_t blocks = (rows + 7) / 8;
   const int64_t cap = 148 * 16;
   return (unsigned)(blocks < cap ? (blocks > 0 ? blocks : 1) : cap);
 }
@@ -1244,7 +1279,7 @@ extern "C" int csn_projection_epilogue_fwd(const float* raw, int64_t R, int N, i
     return set_error(CSN_ERR_INVALID, "csn_projection_epilogue_fwd: missing pointer");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   KernelTimer kt("projection_epilogue_fwd", st);
-  proj_epilogue_fwd_kernel<<<elem_grid(R * Q), 256, 0, st>>>(raw, R, N, K, HT, omega_scale, dt_base, biv, gamma, dt);
+  proj_epilogue_fwd_kernel<<<row_grid(R), 256, 0, st>>>(raw, R, N, K, HT, omega_scale, dt_base, biv, gamma, dt);
   return check_launch("csn_projection_epilogue_fwd");
 }
 
@@ -1259,8 +1294,8 @@ extern "C" int csn_projection_epilogue_bwd(const float* raw, int64_t R, int N, i
     return set_error(CSN_ERR_INVALID, "csn_projection_epilogue_bwd: missing pointer");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   KernelTimer kt("projection_epilogue_bwd", st);
-  proj_epilogue_bwd_kernel<<<elem_grid(R * J), 256, 0, st>>>(raw, R, N, K, HT, omega_scale, dt_base, dbiv, dgamma,
-                                                               ddt, draw, scale_part);
+  proj_epilogue_bwd_kernel<<<row_grid(R), 256, 0, st>>>(raw, R, N, K, HT, omega_scale, dt_base, dbiv, dgamma, ddt,
+                                                          draw, scale_part);
   return check_launch("csn_projection_epilogue_bwd");
 }
 
@@ -1300,7 +1335,8 @@ extern "C" int csn_silu_gate_fwd(const float* gu, int64_t R, int F, float* y, vo
   if (!gu || !y) return set_error(CSN_ERR_INVALID, "csn_silu_gate_fwd: missing pointer");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   KernelTimer kt("silu_gate_fwd", st);
-  silu_gate_fwd_kernel<<<elem_grid(R * F), 256, 0, st>>>(gu, R, F, y);
+  if (gate_vec4(gu, y, y, F)) silu_gate_fwd_kernel<4><<<row_grid(R), 256, 0, st>>>(gu, R, F, y);
+  else silu_gate_fwd_kernel<1><<<row_grid(R), 256, 0, st>>>(gu, R, F, y);
   return check_launch("csn_silu_gate_fwd");
 }
 
@@ -1310,6 +1346,7 @@ extern "C" int csn_silu_gate_bwd(const float* gu, const float* dy, int64_t R, in
   if (!gu || !dy || !dgu) return set_error(CSN_ERR_INVALID, "csn_silu_gate_bwd: missing pointer");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   KernelTimer kt("silu_gate_bwd", st);
-  silu_gate_bwd_kernel<<<elem_grid(R * F), 256, 0, st>>>(gu, dy, R, F, dgu);
+  if (gate_vec4(gu, dy, dgu, F)) silu_gate_bwd_kernel<4><<<row_grid(R), 256, 0, st>>>(gu, dy, R, F, dgu);
+  else silu_gate_bwd_kernel<1><<<row_grid(R), 256, 0, st>>>(gu, dy, R, F, dgu);
   return check_launch("csn_silu_gate_bwd");
 }

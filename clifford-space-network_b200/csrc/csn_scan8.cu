@@ -521,43 +521,37 @@ __global__ void __launch_bounds__(THREADS, 2) bwd8_apply_kernel(ScanArgs a) {
     // ---- 3. dM, with G read back from the dX buffer
     Mat<8> dM;
     if constexpr (TWO) {
+      // dM = (G M) Xp^T + (G^T M) Xp.  First the G^T M part, which reads every column of G;
+      // then G M by halves of rows: half h reads only rows 4h..4h+3 of G, so its rows of G M
+      // replace them in the dX buffer, where the state update H = M^T (G M) reads them.
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         // keeps the scheduler from overlapping the two halves (which would hold both
         // halves' temporaries at once and spill)
         __syncwarp();
-        float W[4][8], U[4][8];
+        float U[4][8];
 #pragma unroll
         for (int r = 0; r < 4; ++r)
 #pragma unroll
-          for (int l = 0; l < 8; ++l) W[r][l] = U[r][l] = 0.0f;
-        // k only addresses shared memory here, so the loop stays rolled: a shorter step
-        // body for the instruction cache (measured 4 % faster than unrolled)
+          for (int l = 0; l < 8; ++l) U[r][l] = 0.0f;
+        // k only addresses shared memory here, so the loop stays rolled (smaller step body)
 #pragma unroll 1
-        for (int k = 0; k < 8; ++k) {  // W = G[rows] M,  U = (G^T)[rows] M
+        for (int k = 0; k < 8; ++k) {  // U = (G^T)[rows] M
           float mr[8];
           lds_row(mr, sM + 8 * k);
           const float4 gu4 = *reinterpret_cast<const float4*>(sDX + 8 * k + 4 * h);  // G[k][rows]
           const float guv[4] = {gu4.x, gu4.y, gu4.z, gu4.w};
 #pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            const float gw = sDX[8 * (4 * h + r) + k], gu = guv[r];
+          for (int r = 0; r < 4; ++r)
 #pragma unroll
-            for (int l = 0; l < 8; ++l) {
-              W[r][l] = fmaf(gw, mr[l], W[r][l]);
-              U[r][l] = fmaf(gu, mr[l], U[r][l]);
-            }
-          }
+            for (int l = 0; l < 8; ++l) U[r][l] = fmaf(guv[r], mr[l], U[r][l]);
         }
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {  // dM[rows] = W Xp^T + U Xp
+        for (int k = 0; k < 8; ++k) {  // dM[rows] = U Xp
           float xr[8];
           lds_row(xr, sXp + 8 * k);
 #pragma unroll
           for (int r = 0; r < 4; ++r) {
-            float acc = 0.0f;
-#pragma unroll
-            for (int c = 0; c < 8; ++c) acc = fmaf(W[r][c], xr[c], acc);
             if (k == 0) {
 #pragma unroll
               for (int l = 0; l < 8; ++l) dM.a[4 * h + r][l] = U[r][0] * xr[l];
@@ -565,9 +559,42 @@ __global__ void __launch_bounds__(THREADS, 2) bwd8_apply_kernel(ScanArgs a) {
 #pragma unroll
               for (int l = 0; l < 8; ++l) dM.a[4 * h + r][l] = fmaf(U[r][k], xr[l], dM.a[4 * h + r][l]);
             }
+          }
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        __syncwarp();
+        float W[4][8];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+          for (int l = 0; l < 8; ++l) W[r][l] = 0.0f;
+#pragma unroll 1
+        for (int k = 0; k < 8; ++k) {  // W = G[rows] M
+          float mr[8];
+          lds_row(mr, sM + 8 * k);
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const float gw = sDX[8 * (4 * h + r) + k];
+#pragma unroll
+            for (int l = 0; l < 8; ++l) W[r][l] = fmaf(gw, mr[l], W[r][l]);
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {  // dM[rows][k] += W[rows] . Xp[k]
+          float xr[8];
+          lds_row(xr, sXp + 8 * k);
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            float acc = 0.0f;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) acc = fmaf(W[r][c], xr[c], acc);
             dM.a[4 * h + r][k] += acc;
           }
         }
+#pragma unroll
+        for (int r = 0; r < 4; ++r) sts_row(sDX + 8 * (4 * h + r), W[r]);  // rows of G M over rows of G
       }
     } else {
 #pragma unroll
@@ -671,10 +698,10 @@ __global__ void __launch_bounds__(THREADS, 2) bwd8_apply_kernel(ScanArgs a) {
     __syncwarp();
     issue_gens(st + 1);
     cp_async_commit();
-    // ---- 6. H <- M^T G M (one-sided: M^T G), G read back by rows from the dX buffer
+    // ---- 6. H <- M^T (G M) (one-sided: M^T G): rows of G M (two-sided) or of G (one-sided)
+    // are read back from the dX buffer
     {
-      Mat<8> Tm;  // M^T G
-      mat_zero(Tm);
+      mat_zero(H);
 #pragma unroll 1  // k only addresses shared memory (rolled, as above)
       for (int k = 0; k < 8; ++k) {
         float mr[8], gr[8];
@@ -683,21 +710,7 @@ __global__ void __launch_bounds__(THREADS, 2) bwd8_apply_kernel(ScanArgs a) {
 #pragma unroll
         for (int i = 0; i < 8; ++i)
 #pragma unroll
-          for (int l = 0; l < 8; ++l) Tm.a[i][l] = fmaf(mr[i], gr[l], Tm.a[i][l]);
-      }
-      if constexpr (TWO) {
-        mat_zero(H);
-#pragma unroll
-        for (int jj = 0; jj < 8; ++jj) {
-          float mr[8];
-          lds_row(mr, sM + 8 * jj);
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-#pragma unroll
-            for (int l = 0; l < 8; ++l) H.a[i][l] = fmaf(Tm.a[i][jj], mr[l], H.a[i][l]);
-        }
-      } else {
-        H = Tm;
+          for (int l = 0; l < 8; ++l) H.a[i][l] = fmaf(mr[i], gr[l], H.a[i][l]);
       }
     }
     __syncwarp();  // M and G buffers are free

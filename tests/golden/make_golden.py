@@ -21,9 +21,11 @@ functions called (paths relative to the reference root):
 * python/clifford_cl6.py:71 CliffordCL6Block, python/clifford_cl8.py:92 CliffordCL8Block
 * csn_toolkit/csn/vision.py:56,113 CliffordSpatialRotorBlockCl4 / Cl8 (use_schulz=False)
 * python/clifford_multihead.py:56,197 MultiHeadCliffordCL6Block, MultiHeadCliffordLM
+* python/clifford_cl6.py:189 CliffordCL6ForCausalLM, python/clifford_cl8.py:199 CliffordCL8ForCausalLM,
+  python/clifford_model.py:78,207 CliffordTENNBlock, CliffordTENNForCausalLM
 
     python tests/golden/make_golden.py [group ...]     (groups: scans cayley rotor ga3 cells
-                                                        blocks spatial multihead; default: all)
+                                                        blocks spatial multihead lms; default: all)
 """
 from __future__ import annotations
 
@@ -283,9 +285,46 @@ def multihead(rng):
     save("multihead_lm", idx=idx, targets=tgt, logits=logits, loss=loss, **sd, **grads)
 
 
+def lms(rng):
+    """Whole LMs around the scan (python/clifford_cl6.py:189-297, clifford_cl8.py:199-298,
+    clifford_model.py:207-295) and the Cl(4) TENN block (clifford_model.py:78-205): logits, the
+    loss with its regularisers, every parameter gradient.  Time heads get weights that make dt
+    vary per token; the Cl(8) LM uses the exact Cayley rotor (use_schulz=False)."""
+    from python.clifford_cl6 import CliffordCL6ForCausalLM
+    from python.clifford_cl8 import CliffordCL8ForCausalLM
+    from python.clifford_model import CliffordTENNBlock, CliffordTENNForCausalLM
+    cases = [("cl6_lm", CliffordCL6ForCausalLM, dict(vocab_size=11, d_model=16, num_layers=2, num_neurons=2)),
+             ("cl8_lm", CliffordCL8ForCausalLM, dict(vocab_size=11, d_model=16, num_layers=1, num_neurons=1,
+                                                     use_schulz=False)),
+             ("tenn_lm", CliffordTENNForCausalLM, dict(vocab_size=11, d_model=16, num_layers=2, num_neurons=2))]
+    for name, cls, kw in cases:
+        torch.manual_seed(int(rng.integers(1 << 30)))
+        lm = cls(**kw).double()
+        with torch.no_grad():
+            for blk in lm.blocks:
+                if hasattr(blk, "time_head"):
+                    blk.time_head.proj.weight.normal_(0.0, 0.2)
+        idx = torch.as_tensor(rng.integers(0, 11, (2, 12)))
+        tgt = torch.as_tensor(rng.integers(0, 11, (2, 12)))
+        logits, loss, _ = lm(idx, targets=tgt)
+        loss.backward()
+        sd = {f"param.{k}": v for k, v in lm.state_dict().items()}
+        grads = {f"grad.{k}": p.grad for k, p in lm.named_parameters()}
+        save(name, idx=idx, targets=tgt, logits=logits, loss=loss, **sd, **grads)
+    torch.manual_seed(int(rng.integers(1 << 30)))
+    blk = CliffordTENNBlock(d_model=16, num_neurons=2).double()
+    x = t(rng.standard_normal((2, 12, 16))).requires_grad_(True)
+    W = t(rng.standard_normal((2, 12, 16)))
+    out, Omega = blk(x, dt=0.07)
+    (out * W).sum().backward()
+    sd = {f"param.{k}": v for k, v in blk.state_dict().items()}
+    grads = {f"grad.{k}": p.grad for k, p in blk.named_parameters()}
+    save("tenn_block", x=x, W=W, out=out, Omega=Omega, dx=x.grad, **sd, **grads)
+
+
 GROUPS = {"scans": (scans, 0), "cayley": (cayleys, 0), "rotor": (rotor_scans, 0), "ga3": (ga3, 0),
           "cells": (cells, 0), "blocks": (blocks, 0), "spatial": (spatial, 1),
-          "multihead": (multihead, 2)}
+          "multihead": (multihead, 2), "lms": (lms, 3)}
 
 
 def main(names):

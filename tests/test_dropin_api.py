@@ -103,3 +103,23 @@ def test_dropin_modules_refuse_cpu_tensors():
     M = torch.zeros(1, 3, 1, 4, 4)
     with pytest.raises(RuntimeError, match="CUDA"):
         parallel_rotor_scan(M, M)
+
+
+@pytest.mark.parametrize("name,mod,cls,kw", [
+    ("cl6_lm", "python.clifford_cl6", "CliffordCL6ForCausalLM", dict(vocab_size=11, d_model=16, num_layers=2,
+                                                                    num_neurons=2)),
+    ("cl8_lm", "python.clifford_cl8", "CliffordCL8ForCausalLM", dict(vocab_size=11, d_model=16, num_layers=1,
+                                                                    num_neurons=1, use_schulz=False)),
+    ("tenn_lm", "python.clifford_model", "CliffordTENNForCausalLM", dict(vocab_size=11, d_model=16, num_layers=2,
+                                                                         num_neurons=2)),
+    ("tenn_block", "python.clifford_model", "CliffordTENNBlock", dict(d_model=16, num_neurons=2)),
+])
+def test_lm_state_dict_matches_reference(golden, name, mod, cls, kw):
+    """Checkpoint compatibility of the whole LMs and the TENN block: the reference's state_dict
+    keys and shapes load unchanged."""
+    import importlib
+    g = golden(name)
+    ref_keys = {k[len("param."):]: tuple(v.shape) for k, v in g.items() if k.startswith("param.")}
+    m = getattr(importlib.import_module(mod), cls)(**kw)
+    assert {k: tuple(v.shape) for k, v in m.state_dict().items()} == ref_keys
+    m.load_state_dict({k: torch.as_tensor(g["param." + k]) for k in ref_keys})

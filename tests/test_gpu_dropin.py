@@ -211,3 +211,46 @@ def test_fused_cuda_d4_port(oracle):
     Xf = fused_cuda_clifford_scan(M.detach().permute(0, 2, 1, 3, 4).reshape(B * N, T, 4, 4),
                                   C.detach().permute(0, 2, 1, 3, 4).reshape(B * N, T, 4, 4))
     assert rel(Xf.view(B, N, T, 4, 4).permute(0, 2, 1, 3, 4), Xr) < 1e-4
+
+
+LM_CTORS = {
+    "cl6_lm": ("python.clifford_cl6", "CliffordCL6ForCausalLM", dict(vocab_size=11, d_model=16, num_layers=2,
+                                                                    num_neurons=2)),
+    "cl8_lm": ("python.clifford_cl8", "CliffordCL8ForCausalLM", dict(vocab_size=11, d_model=16, num_layers=1,
+                                                                    num_neurons=1, use_schulz=False)),
+    "tenn_lm": ("python.clifford_model", "CliffordTENNForCausalLM", dict(vocab_size=11, d_model=16, num_layers=2,
+                                                                         num_neurons=2)),
+}
+
+
+@pytest.mark.parametrize("name", sorted(LM_CTORS))
+def test_lm_matches_reference(golden, name):
+    """Whole LMs on the fused block path (python/clifford_cl6.py:189-297, clifford_cl8.py:199-298,
+    clifford_model.py:207-295): logits, the loss with its least-action (and time) penalties, and
+    every parameter gradient against the reference's float64 run."""
+    import importlib
+    mod, cls, kw = LM_CTORS[name]
+    ctor = getattr(importlib.import_module(mod), cls)
+    g = golden(name)
+    lm = load_block(lambda: ctor(**kw), g)
+    idx = torch.as_tensor(g["idx"], device=DEV)
+    logits, loss, _ = lm(idx, targets=torch.as_tensor(g["targets"], device=DEV))
+    assert rel(logits, g["logits"]) < 1e-4
+    assert abs(loss.item() - float(g["loss"])) / abs(float(g["loss"])) < 1e-5
+    loss.backward()
+    for k, p in lm.named_parameters():
+        assert rel(p.grad, g["grad." + k]) < 1e-3, k
+
+
+def test_tenn_block_matches_reference(golden):
+    """python/clifford_model.py:78-205 CliffordTENNBlock: output, Omega and every gradient."""
+    from python.clifford_model import CliffordTENNBlock
+    g = golden("tenn_block")
+    blk = load_block(lambda: CliffordTENNBlock(16, num_neurons=2), g)
+    x = torch.tensor(g["x"], dtype=torch.float32, device=DEV, requires_grad=True)
+    out, Omega = blk(x, dt=0.07)
+    assert rel(out, g["out"]) < 1e-4 and rel(Omega, g["Omega"]) < 1e-5
+    (out * torch.tensor(g["W"], dtype=torch.float32, device=DEV)).sum().backward()
+    assert rel(x.grad, g["dx"]) < 1e-3
+    for k, p in blk.named_parameters():
+        assert rel(p.grad, g["grad." + k]) < 1e-3, k

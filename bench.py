@@ -2,7 +2,7 @@
 """Throughput benchmark of the rotor-scan hot path (forward + backward).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload cl6_lm|cl3|cl8|gen|sp|lm_train]
+                    [--workload cl6_lm|cl3|cl8|gen|sp|lm_train|spatial]
 
 Workloads (one "step" = one forward + backward pass over one batch of synthetic input,
 seeded, float32, shaped like the reference's configurations):
@@ -24,6 +24,8 @@ seeded, float32, shaped like the reference's configurations):
   the torchrun ranks (strong scaling), forward + backward.
 * ``lm_train`` -- one training step of the whole Cl(6,0) LM around the scan (d_model 128,
   4 blocks x 8 neurons, B32 L2048, AdamW): tokens/s, with the scan's share of the step.
+* ``spatial`` -- the detector's three spatial rotor blocks (Cl(4) 80 x 80, Cl(8) 40 x 40 and
+  20 x 20 feature maps of a 640 x 640 image), batch 16, forward + backward.
 
 N > 1 runs under torchrun: every rank owns its own batch (independent sequences, no
 data-path collective: weak scaling); time is the max over ranks.  ``--impl reference``
@@ -794,6 +796,149 @@ def run_lm_train(args, ws, rank, local, cores):
     return 0
 
 
+SPATIAL_BLOCKS = (("Cl4", 128, 2, 80), ("Cl8", 256, 1, 40), ("Cl8", 256, 1, 20))  # (algebra, C, N, H = W)
+
+
+def _spatial_cpu(reps, warmup, cores):
+    """The spatial scan section on the host cores: the four one-sided direction scans of the
+    three blocks (rows left->right and right->left, then columns down and up of that result),
+    forward and backward, one image, float64 C oracle (reversed scans by flipped arrays)."""
+    import numpy as np
+    from oracle import oracle as orc
+    rng = np.random.default_rng(0)
+    cases = []
+    for alg, C, N, H in SPATIAL_BLOCKS:
+        D = 4 if alg == "Cl4" else 16
+        M = rng.uniform(0.3, 0.9, (1, H * H, N, 1, 1)) * np.eye(D) + 0.05 * rng.standard_normal((1, H * H, N, D, D))
+        Cm = rng.standard_normal((1, H * H, N, D, D))
+        cases.append((H, N, D, M, Cm))
+
+    def bidir(M, C):
+        f = orc.scan_fwd(M, C, two_sided=False)
+        b = orc.scan_fwd(M[:, ::-1], C[:, ::-1], two_sided=False)[:, ::-1]
+        orc.scan_bwd(M, f, np.ones_like(f), two_sided=False)
+        orc.scan_bwd(M[:, ::-1], b[:, ::-1], np.ones_like(b), two_sided=False)
+        return 0.5 * (f + b)
+
+    def one():
+        for H, N, D, M, Cm in cases:
+            ph = bidir(M.reshape(H, H, N, D, D), Cm.reshape(H, H, N, D, D))
+            bidir(M.reshape(1, H, H * N, D, D), ph.reshape(1, H, H * N, D, D))
+
+    el = _time_cpu(one, reps, warmup)
+    elems = sum(H * H * N for H, N, _, _, _ in cases) * reps
+    return elems, el, "one image of the three blocks' scan sections (4 direction scans each), fwd+bwd, float64 C oracle"
+
+
+def run_spatial(args, ws, rank, local, cores):
+    """The three spatial rotor blocks of the reference detector (csn_toolkit/csn/vision.py:223-246,
+    CSN-Large at 640 x 640: C3 Cl(4) 128 channels 80 x 80 with 2 neurons, C4 / C5 Cl(8) 256
+    channels 40 x 40 / 20 x 20 with 1 neuron), forward + backward of each block (projections,
+    Cayley, the four-direction spatial scan, out_proj, BatchNorm, SiLU) at batch 16.  Elements =
+    B * H * W * N summed over the blocks; one step = one fwd + bwd of all three."""
+    B = args.batch or 16
+    config = {"workload": "spatial_rotor_blocks_fwd_bwd", "batch": B,
+              "blocks": [f"{a} C{c} N{n} {h}x{h}" for a, c, n, h in SPATIAL_BLOCKS],
+              "l2": "inputs larger than L2 (the Cl(4) block's M and C are 105 MB each)"}
+    metric = "spatial rotor blocks fwd+bwd Gelem/s (B*H*W*N)"
+    elems = B * sum(h * h * n for _, _, n, h in SPATIAL_BLOCKS)
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+        e, el, sample = _spatial_cpu(max(1, args.steps), min(args.warmup, 1), cores)
+        v = e / el / 1e9
+        print(json.dumps({"metric": metric, "value": v, "unit": "Gelem/s", "n_gpus": args.gpus, "steps": args.steps,
+                          "warmup": args.warmup, "ms_per_step": el / max(1, args.steps) * 1e3,
+                          "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+                          "data": "synthetic", "config": config, "impl": "reference",
+                          "cpu_baseline": {"value": v, "unit": "Gelem/s", "cores": cores, "kind": "port",
+                                           "sample": sample},
+                          "e2e": {"value": v, "unit": "Gelem/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+              flush=True)
+        return 0
+    import torch
+    from csn_b200 import _lib
+    from csn.vision import CliffordSpatialRotorBlockCl4, CliffordSpatialRotorBlockCl8
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    _lib.load()
+    torch.manual_seed(0)
+    blocks, xs, ws_ = [], [], []
+    gen = torch.Generator(device="cpu").manual_seed(0)
+    for alg, C, N, H in SPATIAL_BLOCKS:
+        cls = CliffordSpatialRotorBlockCl4 if alg == "Cl4" else CliffordSpatialRotorBlockCl8
+        blocks.append(cls(C, num_neurons=N, use_schulz=False).to(dev))
+        xs.append(torch.randn(B, C, H, H, generator=gen).to(dev))
+        ws_.append(torch.randn(B, C, H, H, generator=gen).to(dev))
+
+    def step(inputs):
+        outs = []
+        for blk, x, w in zip(blocks, inputs, ws_):
+            x = x.requires_grad_(True)
+            y = blk(x)
+            (y * w).sum().backward()
+            outs.append(y.detach())
+        return outs
+
+    for _ in range(max(3, args.warmup)):
+        step(xs)
+    torch.cuda.synchronize()
+    _lib.timing_reset()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        _lib.timing_enable(True)
+        e0.record()
+        for _ in range(args.steps):
+            step(xs)
+        e1.record()
+        torch.cuda.synchronize()
+        _lib.timing_enable(False)
+    ms = e0.elapsed_time(e1) / args.steps
+    names = ("fwd_reduce", "fwd_carry", "fwd_apply", "bwd_reduce", "bwd_carry", "bwd_apply", "cayley_fwd",
+             "cayley_bwd")
+    kt = {n: _lib.timing_read(n) for n in names}
+    launches = sum(c for _, c in kt.values())
+    _lib.timing_reset()
+    # end to end: the three feature maps from pinned host memory, outputs back, every step
+    hx = [x.cpu().pin_memory() for x in xs]
+    hy = [torch.empty(x.shape).pin_memory() for x in xs]
+    K = max(1, args.e2e_steps)
+
+    def e2e_step():  # the host maps into the blocks' device input buffers, outputs back
+        with torch.no_grad():
+            for x, h in zip(xs, hx):
+                x.copy_(h, non_blocking=True)
+        outs = step(xs)
+        for h, o in zip(hy, outs):
+            h.copy_(o, non_blocking=True)
+        torch.cuda.synchronize()
+
+    e2e_step()  # untimed: the first run from host buffers
+    t0 = time.perf_counter()
+    for _ in range(K):
+        e2e_step()
+    e2e_ms = (time.perf_counter() - t0) / K * 1e3
+    nbytes = sum(h.numel() * 4 for h in hx)
+    cpu = None
+    if not args.no_cpu_baseline:
+        os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+        e, el, sample = _spatial_cpu(2, 0, cores)
+        cpu = {"value": e / el / 1e9, "unit": "Gelem/s", "cores": cores, "kind": "port", "sample": sample}
+    print(json.dumps({
+        "metric": metric, "value": elems / (ms * 1e-3) / 1e9, "unit": "Gelem/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
+        "scan_ms_per_step": sum(kt[n][0] for n in names) / args.steps,
+        "kernel_ms": {n: {"total_ms": t, "launches": c} for n, (t, c) in kt.items()},
+        "gpu_launches": launches, "clocks": clk.summary(),
+        "e2e": {"value": elems / (e2e_ms * 1e-3) / 1e9, "unit": "Gelem/s", "h2d_bytes_per_step": nbytes,
+                "d2h_bytes_per_step": nbytes, "timing": "wall clock per step: feature maps pinned host -> device, "
+                "three blocks fwd + bwd, outputs to host"},
+        "cpu_baseline": cpu}), flush=True)
+    return 0
+
+
 # ==================================================================================== main
 def main():
     ap = argparse.ArgumentParser()
@@ -801,7 +946,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="cl6_lm", choices=sorted(WORKLOADS) + ["gen", "sp", "lm_train"])
+    ap.add_argument("--workload", default="cl6_lm", choices=sorted(WORKLOADS) + ["gen", "sp", "lm_train", "spatial"])
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=None, help="per-rank batch (profiling: smaller)")
@@ -815,6 +960,8 @@ def main():
         return run_sequence_parallel(args, ws, rank, local, cores)
     if args.workload == "lm_train":
         return run_lm_train(args, ws, rank, local, cores)
+    if args.workload == "spatial":
+        return run_spatial(args, ws, rank, local, cores)
     kw = {}
     if args.batch is not None:
         kw["batch"] = args.batch

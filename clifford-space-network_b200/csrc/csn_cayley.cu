@@ -146,7 +146,9 @@ extern "C" int csn_cayley_fwd(const float* Omega, float* Q, int64_t count, int D
   if (!Omega || !Q || !a16(Omega) || !a16(Q))
     return set_error(CSN_ERR_INVALID, "csn_cayley_fwd: pointers missing or not 16-byte aligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (D != 4 && D != 8 && D != 16) return set_error(CSN_ERR_UNSUPPORTED, "csn_cayley_fwd: D must be 4, 8 or 16");
   const unsigned g1 = (unsigned)((count + 127) / 128), g4 = (unsigned)((count + 3) / 4);
+  KernelTimer kt("cayley_fwd", st);
   switch (D) {
     case 4: cayley_fwd_reg<4><<<g1, 128, 0, st>>>(Omega, Q, count); break;
     case 8: cayley_fwd_reg<8><<<g1, 128, 0, st>>>(Omega, Q, count); break;
@@ -163,7 +165,9 @@ extern "C" int csn_cayley_bwd(const float* Q, const float* dQ, float* dOmega, in
   if (!Q || !dQ || !dOmega || !a16(Q) || !a16(dQ) || !a16(dOmega))
     return set_error(CSN_ERR_INVALID, "csn_cayley_bwd: pointers missing or not 16-byte aligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (D != 4 && D != 8 && D != 16) return set_error(CSN_ERR_UNSUPPORTED, "csn_cayley_bwd: D must be 4, 8 or 16");
   const unsigned g1 = (unsigned)((count + 127) / 128), g4 = (unsigned)((count + 3) / 4);
+  KernelTimer kt("cayley_bwd", st);
   switch (D) {
     case 4: cayley_bwd_reg<4><<<g1, 128, 0, st>>>(Q, dQ, dOmega, count); break;
     case 8: cayley_bwd_reg<8><<<g1, 128, 0, st>>>(Q, dQ, dOmega, count); break;

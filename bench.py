@@ -433,9 +433,11 @@ class Cl8:
         # the op's D = 16 path: rotors stored by the forward, reused by the backward
         _lib.call("csn_rotor_scan_fwd_cached", _p(I["gens"]), _p(I["dt"]), _p(None), _p(I["S"]), _p(None),
                   _p(O["X"]), _p(self.Mc), B, T, N, D, 1, 1, _p(self.work), self.ws_bytes, sp)
-        _lib.call("csn_rotor_scan_bwd_cached", _p(I["gens"]), _p(I["dt"]), _p(None), _p(I["S"]), _p(None),
+        # the op's path: the backward loads the cached rotors and reuses the chunk products the
+        # forward left in the workspace (one head: the [B, T, N] layout)
+        _lib.call("csn_rotor_scan_heads_bwd", _p(I["gens"]), _p(I["dt"]), _p(None), _p(I["S"]), _p(None),
                   _p(O["X"]), _p(I["dX"]), _p(self.Mc), _p(O["dgens"]), _p(O["ddt"]), _p(None), _p(O["dS"]),
-                  _p(None), B, T, N, D, 1, 1, _p(self.work), self.ws_bytes, sp)
+                  _p(None), B, T, 1, N, D, 1, 1, 1, _p(self.work), self.ws_bytes, sp)
 
     def e2e_setup(self):
         import torch

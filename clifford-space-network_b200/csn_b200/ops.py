@@ -181,11 +181,13 @@ def _rotor_bwd(g, d, ga, s, hf, X, dXf, basis, two_sided, need_dh0, Mc=None, fwd
     dS = torch.empty_like(s)
     dh0 = torch.empty_like(hf) if (hf is not None and need_dh0) else None
     ws_bytes = _rotor_ws_bytes(s)
-    if H:
+    if H or (Mc is not None and fwd_ws is not None):
+        # the multi-head entry point (H = 1 is the [B, T, N] layout) takes the rotor cache and
+        # the forward's workspace together
         ws = fwd_ws if fwd_ws is not None else _workspace(ws_bytes, s.device)
         _lib.call("csn_rotor_scan_heads_bwd", _ptr(g), _ptr(d), _ptr(ga), _ptr(s), _ptr(hf), _ptr(X),
-                  _ptr(dXf), _ptr(Mc), _ptr(dg), _ptr(ddt), _ptr(dga), _ptr(dS), _ptr(dh0), B, T, H, Nh, D,
-                  basis, int(two_sided), int(fwd_ws is not None), _ptr(ws), ws_bytes, _stream(s.device))
+                  _ptr(dXf), _ptr(Mc), _ptr(dg), _ptr(ddt), _ptr(dga), _ptr(dS), _ptr(dh0), B, T, max(H, 1), Nh,
+                  D, basis, int(two_sided), int(fwd_ws is not None), _ptr(ws), ws_bytes, _stream(s.device))
         return dg, ddt, dga, dS, dh0
     if fwd_ws is not None and Mc is None:
         _lib.call("csn_rotor_scan_bwd_reuse", _ptr(g), _ptr(d), _ptr(ga), _ptr(s), _ptr(hf), _ptr(X),
@@ -212,8 +214,8 @@ class RotorScanFunction(torch.autograd.Function):
         # D = 16: keep the step rotors for the backward (1 KB per element, like S) instead
         # of rebuilding them there
         Mc = torch.empty_like(s) if s.shape[-1] == 16 else None
-        # D = 4, 8: keep the forward's workspace, whose chunk rotor products the backward reuses
-        ws = None if Mc is not None else _workspace(_rotor_ws_bytes(s), s.device)
+        # keep the forward's workspace, whose chunk rotor products the backward reuses
+        ws = _workspace(_rotor_ws_bytes(s), s.device)
         X = _rotor_fwd(g, d, ga, s, hf, basis, two_sided, Mc, ws)
         ctx.save_for_backward(g, d, ga, s, hf, X, Mc)
         ctx.fwd_ws = ws
@@ -225,7 +227,7 @@ class RotorScanFunction(torch.autograd.Function):
     def backward(ctx, dX):
         g, d, ga, s, hf, X, Mc = ctx.saved_tensors
         outs = _rotor_bwd(g, d, ga, s, hf, X, _f32(dX), ctx.basis, ctx.two_sided, ctx.needs_input_grad[4], Mc,
-                          ctx.fwd_ws if Mc is None else None)
+                          ctx.fwd_ws)
         ctx.fwd_ws = None
         outs = [None if o is None else o.to(dt_) for o, dt_ in zip(outs, ctx.dtypes)]
         return outs[0], outs[1], outs[2], outs[3], outs[4], None, None

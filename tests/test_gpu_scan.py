@@ -265,6 +265,14 @@ def test_d16_rotor_cache_matches_uncached_entry_points(ops, basis, damped, two, 
     for a_, b_ in zip(g1, g0):
         if b_ is not None:
             assert rel(a_, b_.cpu().numpy()) < 1e-5
+    # cached rotors together with the forward's chunk products (the autograd op's path)
+    ws = torch.zeros(_lib.load().csn_rotor_scan_workspace_bytes(B, T, N, 16), dtype=torch.uint8, device=DEV)
+    Mc2 = torch.empty_like(S)
+    X2 = ops._rotor_fwd(gens, dt, gamma, S, h0, bi, two, Mc2, ws)
+    g2 = ops._rotor_bwd(gens, dt, gamma, S, h0, X2, dX, bi, two, True, Mc2, ws)
+    for a_, b_ in zip(g2, g0):
+        if b_ is not None:
+            assert rel(a_, b_.cpu().numpy()) < 1e-5
     with pytest.raises(_lib.CsnError, match="UNSUPPORTED"):
         s8 = cuda(rng.standard_normal((1, 4, 1, 8, 8)))
         ops._rotor_fwd(cuda(rng.standard_normal((1, 4, 1, 28))), cuda(np.full((1, 4), 0.05)), None, s8,

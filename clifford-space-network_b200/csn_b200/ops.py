@@ -655,8 +655,25 @@ def column_sum(x2d):
     return out
 
 
+WGRAD_SPLIT = 32
+
+
+def _weight_grad(d2, x2):
+    """dW = d2^T x2 over R rows.  For the LM's R = B*T (tens of thousands of rows) and narrow
+    W, one GEMM has too few output tiles to fill the GPU; the sum over rows is split into
+    WGRAD_SPLIT batched GEMMs whose partial products are then added (deterministic; measured
+    1.7x faster on [65536, 512] x [65536, 128])."""
+    R = d2.shape[0]
+    s = WGRAD_SPLIT
+    if R % s == 0 and R >= s * 1024:
+        return torch.bmm(d2.reshape(s, R // s, d2.shape[1]).transpose(1, 2),
+                         x2.reshape(s, R // s, x2.shape[1])).sum(0)
+    return d2.t() @ x2
+
+
 class LinearFunction(torch.autograd.Function):
-    """y = x W^T + b with cuBLAS GEMMs both ways and the bias gradient by csn_column_sum."""
+    """y = x W^T + b with cuBLAS GEMMs both ways (the weight gradient split over rows) and the
+    bias gradient by csn_column_sum."""
 
     @staticmethod
     def forward(ctx, x, W, b):
@@ -673,7 +690,7 @@ class LinearFunction(torch.autograd.Function):
         x2, W = ctx.saved_tensors
         d2 = dy.reshape(-1, dy.shape[-1])
         dx = (d2 @ W).view(ctx.xshape) if ctx.needs_input_grad[0] else None
-        dW = d2.t() @ x2 if ctx.needs_input_grad[1] else None
+        dW = _weight_grad(d2, x2) if ctx.needs_input_grad[1] else None
         db = column_sum(d2).to(dy.dtype) if (ctx.has_b and ctx.needs_input_grad[2]) else None
         return dx, dW, db
 

@@ -45,8 +45,8 @@ class GeometricGatedLinearUnit(nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         # w_gate and w_up as one GEMM, silu(g) * u as one CUDA kernel each way
-        gu = F.linear(x, torch.cat([self.w_gate.weight, self.w_up.weight], 0))
-        return self.w_down(ops.silu_gate(gu))
+        gu = ops.linear(x, torch.cat([self.w_gate.weight, self.w_up.weight], 0))
+        return ops.linear(ops.silu_gate(gu), self.w_down.weight)
 
 
 class CliffordTENNBlock(nn.Module):

@@ -300,6 +300,8 @@ int scan16_dispatch(const ScanArgs& a, int src, int basis, bool damped, bool two
                     cudaStream_t st);
 // Implemented in csn_scan8.cu (staged D = 8 fused rotor kernels).
 int scan8_rotor_dispatch(const ScanArgs& a, bool damped, bool two, bool bwd, cudaStream_t st);
+int scan8_rotor_step(const float* gens, const float* dt, const float* gamma, const float* S, float* h,
+                     int64_t B, int64_t N, bool two, cudaStream_t st);
 
 namespace {
 
@@ -822,6 +824,7 @@ extern "C" int csn_rotor_step(const float* gens, const float* dt, const float* g
   if (B * N == 0) return CSN_OK;
   if (!h || !aligned16(h)) return set_error(CSN_ERR_INVALID, "csn_rotor_step: h missing or misaligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (D == 8 && basis == BASIS_TRIU) return scan8_rotor_step(gens, dt, gamma, S, h, B, N, two_sided != 0, st);
   Plan p = make_plan(B, 1, N, D, false);
   ScanArgs a{};
   a.gens = gens; a.dt = dt; a.gamma = gamma; a.S = S; a.h0 = h; a.out = h;

@@ -796,12 +796,140 @@ int run8(const ScanArgs& a, bool bwd, cudaStream_t st) {
   return check_launch("rotor scan backward (D=8)");
 }
 
+// ------------------------------------------------------------- single step (generation)
+// One step X <- M X M^T + (1 - alpha) S (one-sided: M X) of B x N independent states,
+// row-parallel: eight lanes per state, lane r owns row r of A = I - Omega, of M and of X.
+// The Gauss-Jordan pivot row is broadcast within the 8-lane group by shuffles; the rows of
+// X and M that the products need go through shared memory.  The arithmetic per entry is
+// the same sequence as the sequential scan (build_I_minus_omega, gj_inverse, lmul, rmulT),
+// so a step equals the scan's step.
+constexpr int STEP_THREADS = 128;
+
+template <bool DAMPED, bool TWO>
+__global__ void __launch_bounds__(STEP_THREADS) step8_kernel(const float* __restrict__ gens,
+                                                             const float* __restrict__ dt,
+                                                             const float* __restrict__ gamma,
+                                                             const float* __restrict__ S,
+                                                             float* h, int64_t B, int64_t N) {
+  __shared__ __align__(16) float sX[STEP_THREADS / 8][DD];
+  __shared__ __align__(16) float sM[STEP_THREADS / 8][DD];
+  const int r = threadIdx.x & 7;
+  const int grp = threadIdx.x >> 3;
+  const int64_t e = blockIdx.x * (int64_t)(STEP_THREADS / 8) + grp;  // state index b * N + n
+  const bool active = e < B * N;  // uniform over the 8-lane group
+  const int64_t b = active ? e / N : 0;
+
+  // row r of A = I - (dt / 2) Omega; generator k of the pair (u, v), u < v, row-major
+  const float dtv = active ? __ldg(dt + b) : 0.0f;
+  const float hdt = 0.5f * dtv;
+  float row[8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    if (c == r) {
+      row[c] = 1.0f;
+    } else {
+      const int u = c < r ? c : r, v = c < r ? r : c;
+      const int k = u * 8 - u * (u + 1) / 2 + (v - u - 1);
+      const float w = active ? hdt * __ldg(gens + e * K + k) : 0.0f;
+      row[c] = c < r ? w : -w;
+    }
+  }
+  // Gauss-Jordan without pivoting (every pivot of I - Omega is >= 1)
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    float p[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) p[c] = __shfl_sync(FULL, row[c], k, 8);
+    const float inv = 1.0f / p[k];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) p[c] = (c == k) ? inv : p[c] * inv;
+    if (r == k) {
+#pragma unroll
+      for (int c = 0; c < 8; ++c) row[c] = p[c];
+    } else {
+      const float f = row[k];
+      row[k] = 0.0f;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) row[c] = fmaf(-f, p[c], row[c]);
+    }
+  }
+  float alpha = 1.0f, sa = 1.0f;
+  if constexpr (DAMPED) {
+    if (active) {
+      alpha = 1.0f / (1.0f + expf(__ldg(gamma + e) * dtv));
+      sa = sqrtf(alpha);
+    }
+  }
+  float xr[8];
+  if (active) lds_row(xr, h + e * DD + 8 * r);  // generic load: h is read and written here
+  else
+#pragma unroll
+    for (int c = 0; c < 8; ++c) xr[c] = 0.0f;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) row[c] = sa * (2.0f * row[c] - ((c == r) ? 1.0f : 0.0f));
+  sts_row(&sX[grp][8 * r], xr);
+  sts_row(&sM[grp][8 * r], row);
+  __syncwarp();
+  // Y = M X: row r of Y = sum_k M[r][k] X[k][:]
+  float y[8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) y[c] = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    float xk[8];
+    lds_row(xk, &sX[grp][8 * k]);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) y[c] = fmaf(row[k], xk[c], y[c]);
+  }
+  if constexpr (TWO) {  // Z = Y M^T: Z[r][l] = sum_j Y[r][j] M[l][j]
+    float z[8];
+#pragma unroll
+    for (int l = 0; l < 8; ++l) {
+      float ml[8];
+      lds_row(ml, &sM[grp][8 * l]);
+      float acc = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc = fmaf(y[j], ml[j], acc);
+      z[l] = acc;
+    }
+#pragma unroll
+    for (int c = 0; c < 8; ++c) y[c] = z[c];
+  }
+  if (!active) return;
+  const float cs = DAMPED ? (1.0f - alpha) : 1.0f;
+  const float4* sp = reinterpret_cast<const float4*>(S + e * DD + 8 * r);
+  const float4 s0 = __ldg(sp), s1 = __ldg(sp + 1);
+  const float sr[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+  for (int c = 0; c < 8; ++c) y[c] = fmaf(cs, sr[c], y[c]);
+  sts_row(h + e * DD + 8 * r, y);
+}
+
+template <bool DAMPED, bool TWO>
+int run_step8(const float* gens, const float* dt, const float* gamma, const float* S, float* h,
+              int64_t B, int64_t N, cudaStream_t st) {
+  const int64_t states = B * N;
+  const unsigned grid = (unsigned)((states + STEP_THREADS / 8 - 1) / (STEP_THREADS / 8));
+  KernelTimer kt("rotor_step", st);
+  step8_kernel<DAMPED, TWO><<<grid, STEP_THREADS, 0, st>>>(gens, dt, gamma, S, h, B, N);
+  return check_launch("rotor step (D=8)");
+}
+
 }  // namespace s8
 
 int scan8_rotor_dispatch(const ScanArgs& a, bool damped, bool two, bool bwd, cudaStream_t st) {
   using namespace s8;
   if (damped) return two ? run8<true, true>(a, bwd, st) : run8<true, false>(a, bwd, st);
   return two ? run8<false, true>(a, bwd, st) : run8<false, false>(a, bwd, st);
+}
+
+int scan8_rotor_step(const float* gens, const float* dt, const float* gamma, const float* S, float* h,
+                     int64_t B, int64_t N, bool two, cudaStream_t st) {
+  using namespace s8;
+  if (gamma) return two ? run_step8<true, true>(gens, dt, gamma, S, h, B, N, st)
+                        : run_step8<true, false>(gens, dt, gamma, S, h, B, N, st);
+  return two ? run_step8<false, true>(gens, dt, gamma, S, h, B, N, st)
+             : run_step8<false, false>(gens, dt, gamma, S, h, B, N, st);
 }
 
 }  // namespace csn

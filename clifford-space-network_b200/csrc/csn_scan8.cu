@@ -820,6 +820,19 @@ __global__ void __launch_bounds__(STEP_THREADS) step8_kernel(const float* __rest
   const int64_t b = active ? e / N : 0;
 
   // row r of A = I - (dt / 2) Omega; generator k of the pair (u, v), u < v, row-major
+  // the state and S rows do not depend on the rotor: issue their loads first so that their
+  // latency overlaps the Cayley inverse
+  float xr[8], sr[8];
+  if (active) {
+    lds_row(xr, h + e * DD + 8 * r);  // generic load: h is read and written here
+    const float4* sp = reinterpret_cast<const float4*>(S + e * DD + 8 * r);
+    const float4 s0 = __ldg(sp), s1 = __ldg(sp + 1);
+    sr[0] = s0.x; sr[1] = s0.y; sr[2] = s0.z; sr[3] = s0.w;
+    sr[4] = s1.x; sr[5] = s1.y; sr[6] = s1.z; sr[7] = s1.w;
+  } else {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) xr[c] = sr[c] = 0.0f;
+  }
   const float dtv = active ? __ldg(dt + b) : 0.0f;
   const float hdt = 0.5f * dtv;
   float row[8];
@@ -860,11 +873,6 @@ __global__ void __launch_bounds__(STEP_THREADS) step8_kernel(const float* __rest
       sa = sqrtf(alpha);
     }
   }
-  float xr[8];
-  if (active) lds_row(xr, h + e * DD + 8 * r);  // generic load: h is read and written here
-  else
-#pragma unroll
-    for (int c = 0; c < 8; ++c) xr[c] = 0.0f;
 #pragma unroll
   for (int c = 0; c < 8; ++c) row[c] = sa * (2.0f * row[c] - ((c == r) ? 1.0f : 0.0f));
   sts_row(&sX[grp][8 * r], xr);
@@ -897,9 +905,6 @@ __global__ void __launch_bounds__(STEP_THREADS) step8_kernel(const float* __rest
   }
   if (!active) return;
   const float cs = DAMPED ? (1.0f - alpha) : 1.0f;
-  const float4* sp = reinterpret_cast<const float4*>(S + e * DD + 8 * r);
-  const float4 s0 = __ldg(sp), s1 = __ldg(sp + 1);
-  const float sr[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
 #pragma unroll
   for (int c = 0; c < 8; ++c) y[c] = fmaf(cs, sr[c], y[c]);
   sts_row(h + e * DD + 8 * r, y);

@@ -52,6 +52,37 @@ def test_stepping_equals_scan_and_oracle(ops, oracle, D, basis, damped):
         assert rel(traj[-1][1][:16], Xr[:, -1]) < 1e-4
 
 
+@pytest.mark.parametrize("B,N", [(1, 1), (3, 5), (7, 3), (33, 9)])  # partial 8-lane groups / CTAs
+@pytest.mark.parametrize("damped", [True, False], ids=["damped", "undamped"])
+@pytest.mark.parametrize("two", [True, False], ids=["two", "one"])
+def test_d8_step_ragged_state_counts_match_oracle_and_scan(ops, oracle, B, N, damped, two):
+    """The D = 8 step kernel runs 16 states per CTA, 8 lanes per state: state counts that
+    leave part of a warp or a CTA idle, from a random initial state, against one oracle step
+    and against the scan's T = 1 path with the same h0 (no state outside [B, N] written)."""
+    from csn_b200 import algebra
+    D = 8
+    E = algebra.triu_basis(D)
+    rng = np.random.default_rng(100 * B + N + 2 * damped + two)
+    gens = rng.standard_normal((B, 1, N, 28)) * 0.3
+    dt = rng.uniform(0.01, 0.1, (B, 1))
+    gamma = np.log1p(np.exp(rng.standard_normal((B, 1, N)))) if damped else None
+    S = rng.standard_normal((B, 1, N, D, D))
+    h0 = rng.standard_normal((B, N, D, D))
+    t = lambda a: torch.tensor(a, dtype=torch.float32, device=DEV)
+    # the state sits inside a larger buffer: the guard entries after it must stay untouched
+    buf = torch.full((B * N * D * D + 64,), 7.0, device=DEV)
+    h = buf[:B * N * D * D].view(B, N, D, D)
+    h.copy_(t(h0))
+    ops.rotor_step(t(gens[:, 0]), t(dt[:, 0]), None if gamma is None else t(gamma[:, 0]), t(S[:, 0]), h,
+                   two_sided=two)
+    assert torch.all(buf[B * N * D * D:] == 7.0)
+    Xr = oracle.rotor_scan_fwd(gens, dt, gamma, S, E, h0=h0, two_sided=two)[:, 0]
+    assert rel(h, Xr) < 1e-5
+    X = ops.fused_rotor_scan(t(gens), t(dt), None if gamma is None else t(gamma), t(S), h0=t(h0),
+                             two_sided=two)
+    assert rel(h, X[:, 0]) < 1e-6
+
+
 def test_step_graph_matches_step_loop(ops):
     B, N, D, steps = 256, 8, 8, 64
     g = ops.RotorStepGraph(B, N, D, steps=steps, damped=True)

@@ -22,7 +22,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from csn_b200 import ops
+from csn_b200 import graphs, ops
 from csn_b200.modules import LayerNorm, causal_conv_input, generator_inputs
 from python.clifford_model import GeometricGatedLinearUnit, RiemannianGeodesicHead
 from python.clifford_scan import parallel_rotor_scan, surrogate_spike  # noqa: F401 (re-export)
@@ -60,7 +60,11 @@ def generator_action(biv: torch.Tensor, dt: torch.Tensor, D: int) -> Tuple[torch
 
 
 def read_diagnostics(named: Dict[str, torch.Tensor]) -> Dict[str, float]:
-    """{name: float} of scalar tensors with one device -> host read for all of them."""
+    """{name: float} of scalar tensors with one device -> host read for all of them.  Inside
+    csn_b200.graphs.deferred_diagnostics() (a captured training step) the scalars stay on the
+    device, unread: {name: 0-d tensor}."""
+    if graphs.diagnostics_deferred():
+        return {k: v.detach().float().reshape(()) if torch.is_tensor(v) else float(v) for k, v in named.items()}
     vals = torch.stack([torch.as_tensor(v).detach().float().reshape(()).to(next(iter(named.values())).device)
                         for v in named.values()]).tolist()
     return dict(zip(named.keys(), vals))

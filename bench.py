@@ -723,7 +723,9 @@ def run_lm_train(args, ws, rank, local, cores):
     d_model 128, 4 CliffordCL6Blocks x 8 neurons, B32 L2048, AdamW lr 1e-3): embedding, blocks
     (ln_1 -> causal depthwise conv -> SiLU -> projections -> fused rotor scan -> spike -> mixed
     out_proj -> GGLU), geodesic head, cross entropy + action + time penalties, backward, optimizer
-    step, diagnostics read back.  Tokens/s = B * L / step time (CUDA events around K steps)."""
+    step, diagnostics read back.  The step is captured once as a CUDA graph (TrainStepGraph) and
+    replayed; tokens/s = B * L / step time (CUDA events around K replays).  The eager step time
+    is reported beside it."""
     config = {"workload": "cl6_lm_train_step", "batch": args.batch or 32, "seq_len": 2048, "d_model": 128,
               "layers": args.layers or 4, "neurons": 8, "vocab": 65, "optimizer": "AdamW",
               "l2": "inputs larger than L2 (each block's S is 134 MB)"}

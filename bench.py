@@ -855,7 +855,9 @@ def run_spatial(args, ws, rank, local, cores):
     CSN-Large at 640 x 640: C3 Cl(4) 128 channels 80 x 80 with 2 neurons, C4 / C5 Cl(8) 256
     channels 40 x 40 / 20 x 20 with 1 neuron), forward + backward of each block (projections,
     Cayley, the four-direction spatial scan, out_proj, BatchNorm, SiLU) at batch 16.  Elements =
-    B * H * W * N summed over the blocks; one step = one fwd + bwd of all three."""
+    B * H * W * N summed over the blocks; one step = one fwd + bwd of all three (parameter and
+    input-map gradients), captured once as a CUDA graph and replayed; the eager step time is
+    reported beside it."""
     B = args.batch or 16
     config = {"workload": "spatial_rotor_blocks_fwd_bwd", "batch": B,
               "blocks": [f"{a} C{c} N{n} {h}x{h}" for a, c, n, h in SPATIAL_BLOCKS],
@@ -878,7 +880,7 @@ def run_spatial(args, ws, rank, local, cores):
               flush=True)
         return 0
     import torch
-    from csn_b200 import _lib
+    from csn_b200 import _lib, graphs
     from csn.vision import CliffordSpatialRotorBlockCl4, CliffordSpatialRotorBlockCl8
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
@@ -892,28 +894,52 @@ def run_spatial(args, ws, rank, local, cores):
         xs.append(torch.randn(B, C, H, H, generator=gen).to(dev))
         ws_.append(torch.randn(B, C, H, H, generator=gen).to(dev))
 
-    def step(inputs):
-        outs = []
-        for blk, x, w in zip(blocks, inputs, ws_):
-            x = x.requires_grad_(True)
-            y = blk(x)
-            (y * w).sum().backward()
-            outs.append(y.detach())
+    class Blocks(torch.nn.Module):  # the three blocks; loss = sum over blocks of sum(y * w)
+        def __init__(self):
+            super().__init__()
+            self.blocks = torch.nn.ModuleList(blocks)
+
+        def forward(self, *inputs):
+            outs = [blk(x) for blk, x in zip(self.blocks, inputs)]
+            return outs, sum((y * w).sum() for y, w in zip(outs, ws_))
+
+    net = Blocks()
+    for x in xs:
+        x.requires_grad_(True)
+
+    def step(inputs):  # gradients of the parameters and of the input maps, not accumulated
+        net.zero_grad(set_to_none=True)
+        for x in inputs:
+            x.grad = None
+        outs, loss = net(*inputs)
+        loss.backward()
         return outs
 
+    # eager steps first: per-step launch count and kernel times of this package's kernels
     for _ in range(max(3, args.warmup)):
         step(xs)
     torch.cuda.synchronize()
     _lib.timing_reset()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _lib.timing_enable(True)
+    e0.record()
+    for _ in range(args.steps):
+        step(xs)
+    e1.record()
+    torch.cuda.synchronize()
+    _lib.timing_enable(False)
+    eager_ms = e0.elapsed_time(e1) / args.steps
+    # the timed step: forward + backward of the three blocks captured once as a CUDA graph
+    g = graphs.TrainStepGraph(net, None, xs, warmup=3, inputs_require_grad=True)
+    for _ in range(max(3, args.warmup)):
+        g(*g.inputs)
+    torch.cuda.synchronize()
     with ClockSampler(local) as clk:
-        _lib.timing_enable(True)
         e0.record()
         for _ in range(args.steps):
-            step(xs)
+            g(*g.inputs)
         e1.record()
         torch.cuda.synchronize()
-        _lib.timing_enable(False)
     ms = e0.elapsed_time(e1) / args.steps
     names = ("fwd_reduce", "fwd_carry", "fwd_apply", "bwd_reduce", "bwd_carry", "bwd_apply", "cayley_fwd",
              "cayley_bwd")
@@ -921,17 +947,14 @@ def run_spatial(args, ws, rank, local, cores):
     launches = sum(c for _, c in kt.values())
     _lib.timing_reset()
     # end to end: the three feature maps from pinned host memory, outputs back, every step
-    hx = [x.cpu().pin_memory() for x in xs]
+    hx = [x.detach().cpu().pin_memory() for x in xs]
     hy = [torch.empty(x.shape).pin_memory() for x in xs]
     K = max(1, args.e2e_steps)
 
-    def e2e_step():  # the host maps into the blocks' device input buffers, outputs back
-        with torch.no_grad():
-            for x, h in zip(xs, hx):
-                x.copy_(h, non_blocking=True)
-        outs = step(xs)
+    def e2e_step():  # the host maps into the captured step's input buffers, outputs back
+        outs, _ = g(*hx)
         for h, o in zip(hy, outs):
-            h.copy_(o, non_blocking=True)
+            h.copy_(o.detach(), non_blocking=True)
         torch.cuda.synchronize()
 
     e2e_step()  # untimed: the first run from host buffers
@@ -949,12 +972,13 @@ def run_spatial(args, ws, rank, local, cores):
         "metric": metric, "value": elems / (ms * 1e-3) / 1e9, "unit": "Gelem/s", "n_gpus": 1, "steps": args.steps,
         "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
+        "eager_ms_per_step": eager_ms, "step": "CUDA graph of the three blocks' forward + backward",
         "scan_ms_per_step": sum(kt[n][0] for n in names) / args.steps,
         "kernel_ms": {n: {"total_ms": t, "launches": c} for n, (t, c) in kt.items()},
         "gpu_launches": launches, "clocks": clk.summary(),
         "e2e": {"value": elems / (e2e_ms * 1e-3) / 1e9, "unit": "Gelem/s", "h2d_bytes_per_step": nbytes,
                 "d2h_bytes_per_step": nbytes, "timing": "wall clock per step: feature maps pinned host -> device, "
-                "three blocks fwd + bwd, outputs to host"},
+                "three blocks fwd + bwd (captured step), outputs to host"},
         "cpu_baseline": cpu}), flush=True)
     return 0
 

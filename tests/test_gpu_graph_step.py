@@ -55,3 +55,39 @@ def test_graphed_train_step_equals_eager_steps(lm):
     torch.cuda.synchronize()
     for (n, pe), pg in zip(eager.named_parameters(), graphed.parameters()):
         assert rel(pg.detach(), pe.detach()) < 1e-5, n
+
+
+def test_graphed_forward_backward_without_optimizer_equals_eager():
+    """TrainStepGraph without an optimizer (the spatial blocks' fwd + bwd): outputs, parameter
+    gradients and input-map gradients of a replay equal one eager step."""
+    from csn_b200 import graphs
+    from csn.vision import CliffordSpatialRotorBlockCl4, CliffordSpatialRotorBlockCl8
+    torch.manual_seed(0)
+
+    class Blocks(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.blocks = torch.nn.ModuleList([CliffordSpatialRotorBlockCl4(16, num_neurons=2, use_schulz=False),
+                                               CliffordSpatialRotorBlockCl8(32, num_neurons=1, use_schulz=False)])
+            self.w = [torch.randn(2, 16, 8, 8, device=DEV), torch.randn(2, 32, 6, 6, device=DEV)]
+
+        def forward(self, *xs):
+            outs = [blk(x) for blk, x in zip(self.blocks, xs)]
+            return outs, sum((y * w).sum() for y, w in zip(outs, self.w))
+
+    eager = Blocks().to(DEV)
+    graphed = copy.deepcopy(eager)
+    xs = [torch.randn(2, 16, 8, 8, device=DEV), torch.randn(2, 32, 6, 6, device=DEV)]
+    step = graphs.TrainStepGraph(graphed, None, xs, warmup=2, inputs_require_grad=True)
+    new = [torch.randn_like(x) for x in xs]
+    outs_g, _ = step(*new)
+    xe = [x.clone().requires_grad_(True) for x in new]
+    outs_e, loss = eager(*xe)
+    loss.backward()
+    torch.cuda.synchronize()
+    for a, b in zip(outs_g, outs_e):
+        assert rel(a.detach(), b.detach()) < 1e-5
+    for a, b in zip(step.inputs, xe):
+        assert rel(a.grad, b.grad) < 1e-5
+    for (n, pe), pg in zip(eager.named_parameters(), graphed.parameters()):
+        assert rel(pg.grad, pe.grad) < 1e-5, n

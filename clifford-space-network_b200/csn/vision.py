@@ -4,7 +4,9 @@ of csn_toolkit/csn/vision.py:56-167.
 Same parameters and buffers (state_dict-compatible: in_proj, biv_proj, metric_proj, gamma_log,
 lambda_sw, out_proj, norm, triu_u, triu_v) and the same forward: 1x1 / 3x3 convolutions give
 the per-pixel step size, injection and generators; Omega = (skew(gens) + tanh(lambda) J_sw)
-* ds / 2 clamped to [-3, 3]; M = sigmoid(-softplus(gamma) ds) Q with the toolkit Cayley
+* ds / 2 clamped to [-3, 3] and the decay sigmoid(-softplus(gamma) ds), both in one CUDA
+kernel from the convolutions' NCHW outputs (csn_b200.ops.spatial_generators; the skew uses the
+row-major triu order of the triu_u / triu_v buffers); M = decay Q with the toolkit Cayley
 rotor; then the 2D bidirectional one-sided scan, here csn_b200.spatial.spatial_scan_2d --
 four scans on views of one buffer with the reverse-time mode instead of the reference's
 permute / contiguous copies and flips.  Rotors are exact whatever ``use_schulz`` says
@@ -13,9 +15,9 @@ EMA) are callers of these blocks and are not part of this package.
 """
 import torch
 import torch.nn as nn
-import torch.nn.functional as F
 
 from csn.rotors import cayley_rotor_4x4, cayley_rotor_16x16
+from csn_b200 import ops
 from csn_b200.spatial import spatial_scan_2d
 
 
@@ -46,20 +48,13 @@ class _SpatialRotorBlock(nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         B, _, H, W = x.shape
-        N, D, K = self.num_neurons, self.D, self.K
-        pix = lambda t, *shape: t.permute(0, 2, 3, 1).reshape(B, H * W, *shape)
-        ds = pix(F.softplus(self.metric_proj(x)), N)
-        C_inj = pix(self.in_proj(x), N, D, D)
-        biv = pix(self.biv_proj(x), N, K)
-        skew = biv.new_zeros(B, H * W, N, D, D)
-        skew[..., self.triu_u, self.triu_v] = biv
-        skew[..., self.triu_v, self.triu_u] = -biv
-        J_sw = 0.5 * (C_inj - C_inj.transpose(-1, -2))
-        half_ds = 0.5 * ds[..., None, None]
-        Omega = ((skew + torch.tanh(self.lambda_sw) * J_sw) * half_ds).clamp(min=-3.0, max=3.0)
+        N, D = self.num_neurons, self.D
+        # softplus step size, triu skew scatter, tanh-gated antisymmetric injection, scale,
+        # clamp, decay and the pixel-major layout: one CUDA kernel each way
+        Omega, C_inj, decay = ops.spatial_generators(self.in_proj(x), self.biv_proj(x), self.metric_proj(x),
+                                                     self.lambda_sw, self.gamma_log, D)
         Q = self._cayley(Omega)
-        decay = torch.sigmoid(-F.softplus(self.gamma_log).view(1, 1, N, 1, 1) * ds[..., None, None])
-        psi = spatial_scan_2d(decay * Q, C_inj, H, W, two_sided=False)
+        psi = spatial_scan_2d(decay[..., None, None] * Q, C_inj, H, W, two_sided=False)
         out = psi.reshape(B, H, W, N * D * D).permute(0, 3, 1, 2)
         return self.act(self.norm(x + self.out_proj(out)))
 

@@ -770,5 +770,60 @@ def silu_gate(gu):
     return SiluGateFunction.apply(gu)
 
 
+class SpatialGeneratorsFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, in_proj, biv_proj, metric, lambda_sw, gamma_log, D: int):
+        _require_cuda(in_proj, biv_proj, metric, lambda_sw, gamma_log)
+        B, NDD, H, W = in_proj.shape
+        N = NDD // (D * D)
+        cf, bf, mf = _f32(in_proj), _f32(biv_proj), _f32(metric)
+        lf, gf = _f32(lambda_sw).reshape(1), _f32(gamma_log).reshape(N)
+        omega = torch.empty(B, H * W, N, D, D, device=cf.device)
+        c = torch.empty_like(omega)
+        decay = torch.empty(B, H * W, N, device=cf.device)
+        _lib.call("csn_spatial_generators_fwd", _ptr(cf), _ptr(bf), _ptr(mf), _ptr(lf), _ptr(gf), _ptr(omega),
+                  _ptr(c), _ptr(decay), B, H * W, N, D, _stream(cf.device))
+        ctx.save_for_backward(cf, bf, mf, lf, gf)
+        ctx.D, ctx.dtypes = D, (in_proj.dtype, biv_proj.dtype, metric.dtype, lambda_sw.dtype, gamma_log.dtype)
+        ctx.shapes = (lambda_sw.shape, gamma_log.shape)
+        return omega, c, decay
+
+    @staticmethod
+    def backward(ctx, d_omega, d_c, d_decay):
+        cf, bf, mf, lf, gf = ctx.saved_tensors
+        D = ctx.D
+        B, NDD, H, W = cf.shape
+        N, HW = NDD // (D * D), H * W
+        zeros = lambda shape: torch.zeros(shape, device=cf.device)
+        dom = _f32(d_omega) if d_omega is not None else zeros((B, HW, N, D, D))
+        dc = _f32(d_c) if d_c is not None else zeros((B, HW, N, D, D))
+        ddec = _f32(d_decay) if d_decay is not None else zeros((B, HW, N))
+        dcraw, dbraw, dmraw = torch.empty_like(cf), torch.empty_like(bf), torch.empty_like(mf)
+        P = _lib.load().csn_spatial_generators_partials(B, HW)
+        dlam, dgam = torch.empty(P, device=cf.device), torch.empty(P, N, device=cf.device)
+        _lib.call("csn_spatial_generators_bwd", _ptr(cf), _ptr(bf), _ptr(mf), _ptr(lf), _ptr(gf), _ptr(dom),
+                  _ptr(dc), _ptr(ddec), _ptr(dcraw), _ptr(dbraw), _ptr(dmraw), _ptr(dlam), _ptr(dgam),
+                  B, HW, N, D, _stream(cf.device))
+        t = ctx.dtypes
+        return (dcraw.to(t[0]), dbraw.to(t[1]), dmraw.to(t[2]), dlam.sum().reshape(ctx.shapes[0]).to(t[3]),
+                dgam.sum(0).reshape(ctx.shapes[1]).to(t[4]), None)
+
+
+def spatial_generators(in_proj, biv_proj, metric, lambda_sw, gamma_log, D: int):
+    """(Omega, C, decay) of the spatial rotor blocks from their NCHW convolution outputs
+    (csn_toolkit/csn/vision.py:81-93, :138-150): ds = softplus(metric), Omega = clamp((skew(biv)
+    + tanh(lambda) (C - C^T) / 2) ds / 2, -3, 3), decay = sigmoid(-softplus(gamma_log) ds).
+    in_proj [B, N*D*D, H, W], biv_proj [B, N*K, H, W], metric [B, N, H, W] -> Omega, C
+    [B, H*W, N, D, D] and decay [B, H*W, N], pixel-major; one CUDA kernel each way."""
+    B, NDD, H, W = in_proj.shape
+    K = D * (D - 1) // 2
+    if NDD % (D * D) or biv_proj.shape != (B, NDD // (D * D) * K, H, W) or metric.shape != (B, NDD // (D * D), H, W):
+        raise ValueError("spatial_generators: in_proj [B, N*D*D, H, W], biv_proj [B, N*K, H, W], "
+                         "metric [B, N, H, W] expected")
+    if lambda_sw.numel() != 1 or gamma_log.numel() != NDD // (D * D):
+        raise ValueError("spatial_generators: lambda_sw has 1 value and gamma_log N")
+    return SpatialGeneratorsFunction.apply(in_proj, biv_proj, metric, lambda_sw, gamma_log, D)
+
+
 # torch.ops.csn.* registrations (needs the helpers above; imported last on purpose)
 from . import library  # noqa: E402,F401

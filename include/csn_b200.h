@@ -363,6 +363,27 @@ int csn_column_sum(const float* x, int64_t R, int C, float* out, void* workspace
 int csn_silu_gate_fwd(const float* gu, int64_t R, int F, float* y, void* stream);
 int csn_silu_gate_bwd(const float* gu, const float* dy, int64_t R, int F, float* dgu, void* stream);
 
+/* ------------------------------------------------- spatial blocks' generator chain */
+/* The per-pixel chain of CliffordSpatialRotorBlockCl4 / Cl8 between their convolutions and
+ * the Cayley rotor (csn_toolkit/csn/vision.py:81-93, :138-150), fused: from the NCHW outputs
+ * in_proj [B, N*D*D, H, W], biv_proj [B, N*K, H, W] (K = D(D-1)/2, row-major triu) and
+ * metric [B, N, H, W], with the parameters lambda_sw (1 value) and gamma_log [N] on the device,
+ *   ds = softplus(metric), Omega = clamp((skew(biv) + tanh(lambda) (C - C^T) / 2) ds / 2, -3, 3),
+ *   decay = sigmoid(-softplus(gamma_log) ds),
+ * written pixel-major: omega, c [B, H*W, N, D, D], decay [B, H*W, N].  D in {4, 8, 16}.
+ * The backward takes d_omega, d_c, d_decay in those layouts, writes the three NCHW input
+ * gradients and per-CTA partial sums of dlambda [P] and dgamma [P, N], P =
+ * csn_spatial_generators_partials(B, H*W); the caller sums the partials over P. */
+int64_t csn_spatial_generators_partials(int64_t B, int64_t HW);
+int csn_spatial_generators_fwd(const float* in_proj, const float* biv_proj, const float* metric,
+                               const float* lambda_sw, const float* gamma_log, float* omega, float* c,
+                               float* decay, int64_t B, int64_t HW, int64_t N, int D, void* stream);
+int csn_spatial_generators_bwd(const float* in_proj, const float* biv_proj, const float* metric,
+                               const float* lambda_sw, const float* gamma_log, const float* d_omega,
+                               const float* d_c, const float* d_decay, float* d_in_proj, float* d_biv_proj,
+                               float* d_metric, float* dlambda_part, float* dgamma_part, int64_t B,
+                               int64_t HW, int64_t N, int D, void* stream);
+
 /* -------------------------------------------------------------- kernel timing */
 /* Measurement hook with no counterpart in the reference (which times with wall clock,
  * tests/profile_performance.py:41-71).  While enabled, every kernel the library

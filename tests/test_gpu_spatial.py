@@ -122,3 +122,50 @@ def test_spatial_block_matches_reference_golden(golden, name, cls, monkeypatch):
     assert rel(x.grad, g["dx"]) < BWD_TOL
     for k, p in blk.named_parameters():
         assert rel(p.grad, g[f"grad.{k}"]) < BWD_TOL, k
+
+
+def _generator_chain64(craw, braw, mraw, lam, gam, D):
+    """The spatial blocks' torch chain between the convolutions and the Cayley rotor
+    (csn_toolkit/csn/vision.py:81-93), float64 on the CPU."""
+    import torch.nn.functional as F
+    B, _, H, W = craw.shape
+    N, K = gam.shape[0], D * (D - 1) // 2
+    pix = lambda t, *shape: t.permute(0, 2, 3, 1).reshape(B, H * W, *shape)
+    ds = pix(F.softplus(mraw), N)
+    C = pix(craw, N, D, D)
+    biv = pix(braw, N, K)
+    iu = torch.triu_indices(D, D, 1)
+    skew = biv.new_zeros(B, H * W, N, D, D)
+    skew[..., iu[0], iu[1]] = biv
+    skew[..., iu[1], iu[0]] = -biv
+    J = 0.5 * (C - C.transpose(-1, -2))
+    Omega = ((skew + torch.tanh(lam) * J) * (0.5 * ds[..., None, None])).clamp(min=-3.0, max=3.0)
+    decay = torch.sigmoid(-F.softplus(gam).view(1, 1, N) * ds)
+    return Omega, C, decay
+
+
+@pytest.mark.parametrize("D,N,shape", [(4, 2, (2, 5, 7)), (4, 3, (1, 16, 16)), (8, 1, (2, 3, 11)),
+                                       (16, 1, (2, 6, 5)), (16, 2, (1, 4, 9))])
+def test_spatial_generators_match_torch_chain(ops, D, N, shape):
+    """Fused generator chain vs the torch chain in float64: Omega (clamped entries included),
+    pixel-major C, decay and every input gradient, on pixel counts that leave a partial tile."""
+    B, H, W = shape
+    K = D * (D - 1) // 2
+    g = torch.Generator().manual_seed(D * 100 + N)
+    ins = [torch.randn(B, N * D * D, H, W, generator=g, dtype=torch.float64) * 3,
+           torch.randn(B, N * K, H, W, generator=g, dtype=torch.float64) * 3,
+           torch.randn(B, N, H, W, generator=g, dtype=torch.float64),
+           torch.tensor(0.3, dtype=torch.float64), torch.randn(N, generator=g, dtype=torch.float64)]
+    ref_in = [t.clone().requires_grad_(True) for t in ins]
+    outs64 = _generator_chain64(*ref_in, D)
+    assert (outs64[0].abs() == 3.0).any()  # the clamp is exercised
+    grads = [torch.randn(o.shape, generator=g, dtype=torch.float64) for o in outs64]
+    sum((o * w).sum() for o, w in zip(outs64, grads)).backward()
+    gpu_in = [t.float().to(DEV).requires_grad_(True) for t in ins]
+    outs = ops.spatial_generators(*gpu_in, D)
+    for o, r in zip(outs, outs64):
+        assert o.shape == r.shape
+        assert rel(o, r) < 1e-5
+    sum((o * w.float().to(DEV)).sum() for o, w in zip(outs, grads)).backward()
+    for name, t, r in zip(("in_proj", "biv_proj", "metric", "lambda_sw", "gamma_log"), gpu_in, ref_in):
+        assert rel(t.grad, r.grad) < 1e-4, name

@@ -811,7 +811,7 @@ class SpatialGeneratorsFunction(torch.autograd.Function):
 
 def spatial_generators(in_proj, biv_proj, metric, lambda_sw, gamma_log, D: int):
     """(Omega, C, decay) of the spatial rotor blocks from their NCHW convolution outputs
-    (csn_toolkit/csn/vision.py:81-93, :138-150): ds = softplus(metric), Omega = clamp((skew(biv)
+    (csn_toolkit/csn/vision.py:79-94, :136-151): ds = softplus(metric), Omega = clamp((skew(biv)
     + tanh(lambda) (C - C^T) / 2) ds / 2, -3, 3), decay = sigmoid(-softplus(gamma_log) ds).
     in_proj [B, N*D*D, H, W], biv_proj [B, N*K, H, W], metric [B, N, H, W] -> Omega, C
     [B, H*W, N, D, D] and decay [B, H*W, N], pixel-major; one CUDA kernel each way."""

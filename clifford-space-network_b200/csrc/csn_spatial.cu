@@ -1,7 +1,7 @@
 // csn_spatial.cu -- the spatial rotor blocks' generator chain, fused (forward and adjoint).
 //
 // Per pixel p = (h, w) of image b and neuron n, from the three convolution outputs in NCHW
-// (csn_toolkit/csn/vision.py:81-93 for Cl(4), :138-150 for Cl(8)):
+// (csn_toolkit/csn/vision.py:79-94 for Cl(4), :136-151 for Cl(8)):
 //   ds     = softplus(metric[b, n, p])
 //   C      = in_proj[b, n*D*D + (i, j), p]                       (D x D injection)
 //   skew   = triu scatter of biv_proj[b, n*K + k, p], k row-major over u < v, minus its transpose

@@ -365,7 +365,7 @@ int csn_silu_gate_bwd(const float* gu, const float* dy, int64_t R, int F, float*
 
 /* ------------------------------------------------- spatial blocks' generator chain */
 /* The per-pixel chain of CliffordSpatialRotorBlockCl4 / Cl8 between their convolutions and
- * the Cayley rotor (csn_toolkit/csn/vision.py:81-93, :138-150), fused: from the NCHW outputs
+ * the Cayley rotor (csn_toolkit/csn/vision.py:79-94, :136-151), fused: from the NCHW outputs
  * in_proj [B, N*D*D, H, W], biv_proj [B, N*K, H, W] (K = D(D-1)/2, row-major triu) and
  * metric [B, N, H, W], with the parameters lambda_sw (1 value) and gamma_log [N] on the device,
  *   ds = softplus(metric), Omega = clamp((skew(biv) + tanh(lambda) (C - C^T) / 2) ds / 2, -3, 3),

@@ -126,7 +126,7 @@ def test_spatial_block_matches_reference_golden(golden, name, cls, monkeypatch):
 
 def _generator_chain64(craw, braw, mraw, lam, gam, D):
     """The spatial blocks' torch chain between the convolutions and the Cayley rotor
-    (csn_toolkit/csn/vision.py:81-93), float64 on the CPU."""
+    (csn_toolkit/csn/vision.py:79-94), float64 on the CPU."""
     import torch.nn.functional as F
     B, _, H, W = craw.shape
     N, K = gam.shape[0], D * (D - 1) // 2

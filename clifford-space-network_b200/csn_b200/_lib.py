@@ -85,7 +85,7 @@ SIGNATURES = {
     "csn_column_sum": ([_f, _i64, _int, _f, _f, _sz, _f], _int),
     "csn_silu_gate_fwd": ([_f, _i64, _int, _f, _f], _int),
     "csn_silu_gate_bwd": ([_f, _f, _i64, _int, _f, _f], _int),
-    "csn_spatial_generators_partials": ([_i64, _i64], _i64),
+    "csn_spatial_generators_partials": ([_i64, _i64, _int], _i64),
     "csn_spatial_generators_fwd": ([_f, _f, _f, _f, _f, _f, _f, _f, _i64, _i64, _i64, _int, _f], _int),
     "csn_spatial_generators_bwd": ([_f] * 13 + [_i64, _i64, _i64, _int, _f], _int),
     "csn_timing_enable": ([_int], _int),

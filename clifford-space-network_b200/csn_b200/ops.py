@@ -799,7 +799,7 @@ class SpatialGeneratorsFunction(torch.autograd.Function):
         dc = _f32(d_c) if d_c is not None else zeros((B, HW, N, D, D))
         ddec = _f32(d_decay) if d_decay is not None else zeros((B, HW, N))
         dcraw, dbraw, dmraw = torch.empty_like(cf), torch.empty_like(bf), torch.empty_like(mf)
-        P = _lib.load().csn_spatial_generators_partials(B, HW)
+        P = _lib.load().csn_spatial_generators_partials(B, HW, D)
         dlam, dgam = torch.empty(P, device=cf.device), torch.empty(P, N, device=cf.device)
         _lib.call("csn_spatial_generators_bwd", _ptr(cf), _ptr(bf), _ptr(mf), _ptr(lf), _ptr(gf), _ptr(dom),
                   _ptr(dc), _ptr(ddec), _ptr(dcraw), _ptr(dbraw), _ptr(dmraw), _ptr(dlam), _ptr(dgam),

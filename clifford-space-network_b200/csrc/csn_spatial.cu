@@ -33,7 +33,6 @@
 namespace csn {
 namespace {
 
-constexpr int SP_TP = 16;        // pixels per CTA
 constexpr int SP_THREADS = 256;
 constexpr unsigned SP_FULL = 0xffffffffu;
 
@@ -56,20 +55,25 @@ __device__ __forceinline__ void sp_triu_pair(int k, int& u, int& v) {
   v = u + 1 + k;
 }
 
+// pixels per CTA: about 4 K matrix entries per CTA of 256 threads (64 for D = 4, 16 for D = 16)
+__host__ __device__ constexpr int sp_tp(int D) { return D == 4 ? 64 : (D == 8 ? 32 : 16); }
+
 // Shared-memory tile of one CTA: the NCHW inputs of TP pixels, columns padded to TP + 1.
 template <int D>
 struct SpTile {
   static constexpr int DD = D * D;
   static constexpr int K = D * (D - 1) / 2;
-  static constexpr int LD = SP_TP + 1;
+  static constexpr int TP = sp_tp(D);
+  static constexpr int LD = TP + 1;
 };
 
 // stage rows [0, rows) of a [B, rows, HW] tensor's TP pixel columns starting at p0
+template <int TP>
 __device__ __forceinline__ void sp_stage(float* dst, const float* __restrict__ src, int rows, int64_t HW,
                                          int64_t b, int64_t p0, int np) {
-  for (int t = threadIdx.x; t < rows * SP_TP; t += SP_THREADS) {
-    const int r = t / SP_TP, pl = t % SP_TP;
-    dst[r * (SP_TP + 1) + pl] = pl < np ? __ldg(src + (b * rows + r) * HW + p0 + pl) : 0.0f;
+  for (int t = threadIdx.x; t < rows * TP; t += SP_THREADS) {
+    const int r = t / TP, pl = t % TP;
+    dst[r * (TP + 1) + pl] = pl < np ? __ldg(src + (b * rows + r) * HW + p0 + pl) : 0.0f;
   }
 }
 
@@ -99,14 +103,14 @@ __global__ void __launch_bounds__(SP_THREADS) spatial_gen_fwd_kernel(
   float* sB = sC + N * T::DD * T::LD;           // [N*K][LD]
   float* sM = sB + N * T::K * T::LD;            // [N][LD]  ds
   const int64_t b = blockIdx.y;
-  const int64_t p0 = (int64_t)blockIdx.x * SP_TP;
-  const int np = HW - p0 < SP_TP ? (int)(HW - p0) : SP_TP;
-  sp_stage(sC, craw, N * T::DD, HW, b, p0, np);
-  sp_stage(sB, braw, N * T::K, HW, b, p0, np);
-  sp_stage(sM, mraw, N, HW, b, p0, np);
+  const int64_t p0 = (int64_t)blockIdx.x * T::TP;
+  const int np = HW - p0 < T::TP ? (int)(HW - p0) : T::TP;
+  sp_stage<T::TP>(sC, craw, N * T::DD, HW, b, p0, np);
+  sp_stage<T::TP>(sB, braw, N * T::K, HW, b, p0, np);
+  sp_stage<T::TP>(sM, mraw, N, HW, b, p0, np);
   __syncthreads();
-  for (int t = threadIdx.x; t < N * SP_TP; t += SP_THREADS) {  // ds = softplus(metric)
-    const int n = t / SP_TP, pl = t % SP_TP;
+  for (int t = threadIdx.x; t < N * T::TP; t += SP_THREADS) {  // ds = softplus(metric)
+    const int n = t / T::TP, pl = t % T::TP;
     sM[n * T::LD + pl] = sp_softplus(sM[n * T::LD + pl]);
   }
   __syncthreads();
@@ -145,18 +149,18 @@ __global__ void __launch_bounds__(SP_THREADS) spatial_gen_bwd_kernel(
   float* sDs = sRaw + N * T::LD;                // [N][LD]  ds
   float* sDm = sDs + N * T::LD;                 // [N][LD]  dmetric
   float* sG = sDm + N * T::LD;                  // [TP][LG] masked dOmega
-  float* sTl = sG + SP_TP * LG;                 // [TP*N]
-  float* sGam = sTl + SP_TP * N;                // [TP*N]
+  float* sTl = sG + T::TP * LG;                 // [TP*N]
+  float* sGam = sTl + T::TP * N;                // [TP*N]
   const int64_t b = blockIdx.y;
-  const int64_t p0 = (int64_t)blockIdx.x * SP_TP;
-  const int np = HW - p0 < SP_TP ? (int)(HW - p0) : SP_TP;
+  const int64_t p0 = (int64_t)blockIdx.x * T::TP;
+  const int np = HW - p0 < T::TP ? (int)(HW - p0) : T::TP;
   const int64_t cta = (int64_t)blockIdx.y * gridDim.x + blockIdx.x;
-  sp_stage(sC, craw, N * T::DD, HW, b, p0, np);
-  sp_stage(sB, braw, N * T::K, HW, b, p0, np);
-  sp_stage(sRaw, mraw, N, HW, b, p0, np);
+  sp_stage<T::TP>(sC, craw, N * T::DD, HW, b, p0, np);
+  sp_stage<T::TP>(sB, braw, N * T::K, HW, b, p0, np);
+  sp_stage<T::TP>(sRaw, mraw, N, HW, b, p0, np);
   __syncthreads();
-  for (int t = threadIdx.x; t < N * SP_TP; t += SP_THREADS) {
-    const int n = t / SP_TP, pl = t % SP_TP;
+  for (int t = threadIdx.x; t < N * T::TP; t += SP_THREADS) {
+    const int n = t / T::TP, pl = t % T::TP;
     sDs[n * T::LD + pl] = sp_softplus(sRaw[n * T::LD + pl]);
   }
   __syncthreads();
@@ -212,8 +216,8 @@ __global__ void __launch_bounds__(SP_THREADS) spatial_gen_bwd_kernel(
     for (int pl = 0; pl < np; ++pl) s += sGam[pl * N + n];
     dgam_part[cta * N + n] = s;
   }
-  for (int t = threadIdx.x; t < N * SP_TP; t += SP_THREADS) {
-    const int n = t / SP_TP, pl = t % SP_TP;
+  for (int t = threadIdx.x; t < N * T::TP; t += SP_THREADS) {
+    const int n = t / T::TP, pl = t % T::TP;
     if (pl < np) dmraw[(b * N + n) * HW + p0 + pl] = sDm[n * T::LD + pl];
   }
   // 4. dC_in = dC + 0.5 tl (dpre - dpre^T), transposed into the C tile (read last in step 2)
@@ -226,12 +230,12 @@ __global__ void __launch_bounds__(SP_THREADS) spatial_gen_bwd_kernel(
   }
   __syncthreads();
   // 5. NCHW gradients of the injection and generator convolutions (coalesced along pixels)
-  for (int t = threadIdx.x; t < per_px * SP_TP; t += SP_THREADS) {
-    const int r = t / SP_TP, pl = t % SP_TP;
+  for (int t = threadIdx.x; t < per_px * T::TP; t += SP_THREADS) {
+    const int r = t / T::TP, pl = t % T::TP;
     if (pl < np) dcraw[(b * per_px + r) * HW + p0 + pl] = sC[r * T::LD + pl];
   }
-  for (int t = threadIdx.x; t < N * T::K * SP_TP; t += SP_THREADS) {
-    const int r = t / SP_TP, pl = t % SP_TP;
+  for (int t = threadIdx.x; t < N * T::K * T::TP; t += SP_THREADS) {
+    const int r = t / T::TP, pl = t % T::TP;
     if (pl >= np) continue;
     const int n = r / T::K, k = r % T::K;
     int u, v;
@@ -252,13 +256,13 @@ using namespace csn;
 constexpr size_t SP_SMEM_MAX = 227 * 1024;
 
 size_t sp_fwd_smem(int64_t N, int D) {
-  const int64_t DD = D * D, K = D * (D - 1) / 2;
-  return (size_t)((N * DD + N * K + N) * (SP_TP + 1)) * sizeof(float);
+  const int64_t DD = D * D, K = D * (D - 1) / 2, TP = sp_tp(D);
+  return (size_t)((N * DD + N * K + N) * (TP + 1)) * sizeof(float);
 }
 
 size_t sp_bwd_smem(int64_t N, int D) {
-  const int64_t DD = D * D, K = D * (D - 1) / 2;
-  return (size_t)((N * DD + N * K + 3 * N) * (SP_TP + 1) + SP_TP * (N * DD + 1) + 2 * SP_TP * N) * sizeof(float);
+  const int64_t DD = D * D, K = D * (D - 1) / 2, TP = sp_tp(D);
+  return (size_t)((N * DD + N * K + 3 * N) * (TP + 1) + TP * (N * DD + 1) + 2 * TP * N) * sizeof(float);
 }
 
 int sp_check(const char* fn, int64_t B, int64_t HW, int64_t N, int D) {
@@ -267,7 +271,7 @@ int sp_check(const char* fn, int64_t B, int64_t HW, int64_t N, int D) {
     snprintf(msg, sizeof msg, "%s: D = %d, expected 4, 8 or 16", fn, D);
     return set_error(CSN_ERR_UNSUPPORTED, msg);
   }
-  if (B < 0 || HW < 0 || N < 0 || B > 65535 || (HW + SP_TP - 1) / SP_TP > 0x7fffffff) {
+  if (B < 0 || HW < 0 || N < 0 || B > 65535 || HW > ((int64_t)1 << 35)) {
     snprintf(msg, sizeof msg, "%s: B in [0, 65535], H*W >= 0, N >= 0 required", fn);
     return set_error(CSN_ERR_INVALID, msg);
   }
@@ -290,7 +294,7 @@ int sp_fwd(const float* craw, const float* braw, const float* mraw, const float*
            float* c, float* dec, int64_t B, int64_t HW, int N, cudaStream_t st) {
   const size_t smem = sp_fwd_smem(N, D);
   if (int rc = sp_smem_attr(spatial_gen_fwd_kernel<D>, smem, "csn_spatial_generators_fwd")) return rc;
-  const dim3 grid((unsigned)((HW + SP_TP - 1) / SP_TP), (unsigned)B);
+  const dim3 grid((unsigned)((HW + sp_tp(D) - 1) / sp_tp(D)), (unsigned)B);
   KernelTimer kt("spatial_generators_fwd", st);
   spatial_gen_fwd_kernel<D><<<grid, SP_THREADS, smem, st>>>(craw, braw, mraw, lam, gam, om, c, dec, HW, N);
   return check_launch("csn_spatial_generators_fwd");
@@ -302,7 +306,7 @@ int sp_bwd(const float* craw, const float* braw, const float* mraw, const float*
            float* dlam, float* dgam, int64_t B, int64_t HW, int N, cudaStream_t st) {
   const size_t smem = sp_bwd_smem(N, D);
   if (int rc = sp_smem_attr(spatial_gen_bwd_kernel<D>, smem, "csn_spatial_generators_bwd")) return rc;
-  const dim3 grid((unsigned)((HW + SP_TP - 1) / SP_TP), (unsigned)B);
+  const dim3 grid((unsigned)((HW + sp_tp(D) - 1) / sp_tp(D)), (unsigned)B);
   KernelTimer kt("spatial_generators_bwd", st);
   spatial_gen_bwd_kernel<D><<<grid, SP_THREADS, smem, st>>>(craw, braw, mraw, lam, gam, dom, dc, ddec, dcraw,
                                                              dbraw, dmraw, dlam, dgam, HW, N);
@@ -311,9 +315,9 @@ int sp_bwd(const float* craw, const float* braw, const float* mraw, const float*
 
 }  // namespace
 
-extern "C" int64_t csn_spatial_generators_partials(int64_t B, int64_t HW) {
-  if (B < 0 || HW < 0) return 0;
-  return B * ((HW + SP_TP - 1) / SP_TP);
+extern "C" int64_t csn_spatial_generators_partials(int64_t B, int64_t HW, int D) {
+  if (B < 0 || HW < 0 || (D != 4 && D != 8 && D != 16)) return 0;
+  return B * ((HW + sp_tp(D) - 1) / sp_tp(D));
 }
 
 extern "C" int csn_spatial_generators_fwd(const float* in_proj, const float* biv_proj, const float* metric,

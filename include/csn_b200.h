@@ -373,8 +373,9 @@ int csn_silu_gate_bwd(const float* gu, const float* dy, int64_t R, int F, float*
  * written pixel-major: omega, c [B, H*W, N, D, D], decay [B, H*W, N].  D in {4, 8, 16}.
  * The backward takes d_omega, d_c, d_decay in those layouts, writes the three NCHW input
  * gradients and per-CTA partial sums of dlambda [P] and dgamma [P, N], P =
- * csn_spatial_generators_partials(B, H*W); the caller sums the partials over P. */
-int64_t csn_spatial_generators_partials(int64_t B, int64_t HW);
+ * csn_spatial_generators_partials(B, H*W, D) (0 for an unsupported D); the caller sums the
+ * partials over P. */
+int64_t csn_spatial_generators_partials(int64_t B, int64_t HW, int D);
 int csn_spatial_generators_fwd(const float* in_proj, const float* biv_proj, const float* metric,
                                const float* lambda_sw, const float* gamma_log, float* omega, float* c,
                                float* decay, int64_t B, int64_t HW, int64_t N, int D, void* stream);

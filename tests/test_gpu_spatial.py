@@ -144,7 +144,7 @@ def _generator_chain64(craw, braw, mraw, lam, gam, D):
     return Omega, C, decay
 
 
-@pytest.mark.parametrize("D,N,shape", [(4, 2, (2, 5, 7)), (4, 3, (1, 16, 16)), (8, 1, (2, 3, 11)),
+@pytest.mark.parametrize("D,N,shape", [(4, 2, (2, 5, 7)), (4, 2, (2, 9, 9)), (4, 3, (1, 16, 16)), (8, 1, (2, 3, 11)),
                                        (16, 1, (2, 6, 5)), (16, 2, (1, 4, 9))])
 def test_spatial_generators_match_torch_chain(ops, D, N, shape):
     """Fused generator chain vs the torch chain in float64: Omega (clamped entries included),

@@ -58,6 +58,26 @@ __device__ __forceinline__ void sp_triu_pair(int k, int& u, int& v) {
 // pixels per CTA: about 4 K matrix entries per CTA of 256 threads (64 for D = 4, 16 for D = 16)
 __host__ __device__ constexpr int sp_tp(int D) { return D == 4 ? 64 : (D == 8 ? 32 : 16); }
 
+// The entries e = threadIdx.x + SP_THREADS m of a CTA's tile as (pixel, entry) = divmod(e, per),
+// advanced without dividing (one division per thread at the start)
+struct SpIter {
+  int pl, r, dq, dr, per;
+  __device__ explicit SpIter(int per_) : per(per_) {
+    pl = threadIdx.x / per;
+    r = threadIdx.x % per;
+    dq = SP_THREADS / per;
+    dr = SP_THREADS % per;
+  }
+  __device__ void next() {
+    pl += dq;
+    r += dr;
+    if (r >= per) {
+      r -= per;
+      ++pl;
+    }
+  }
+};
+
 // Shared-memory tile of one CTA: the NCHW inputs of TP pixels, columns padded to TP + 1.
 template <int D>
 struct SpTile {
@@ -117,8 +137,8 @@ __global__ void __launch_bounds__(SP_THREADS) spatial_gen_fwd_kernel(
   const float tl = tanhf(__ldg(lambda_sw));
   const int per_px = N * T::DD;
   const int64_t base = (b * HW + p0) * per_px;  // first output entry of this CTA
-  for (int e = threadIdx.x; e < np * per_px; e += SP_THREADS) {
-    const int pl = e / per_px, r = e % per_px;
+  for (SpIter it(per_px); it.pl < np; it.next()) {
+    const int pl = it.pl, r = it.r, e = pl * per_px + r;
     const int n = r / T::DD, ij = r % T::DD, i = ij / D, j = ij % D;
     const float ds = sM[n * T::LD + pl];
     float J;
@@ -155,6 +175,13 @@ __global__ void __launch_bounds__(SP_THREADS) spatial_gen_bwd_kernel(
   const int64_t p0 = (int64_t)blockIdx.x * T::TP;
   const int np = HW - p0 < T::TP ? (int)(HW - p0) : T::TP;
   const int64_t cta = (int64_t)blockIdx.y * gridDim.x + blockIdx.x;
+  __shared__ unsigned char sPair[2][T::K];  // (u, v) of generator k
+  for (int k = threadIdx.x; k < T::K; k += SP_THREADS) {
+    int u, v;
+    sp_triu_pair<D>(k, u, v);
+    sPair[0][k] = (unsigned char)u;
+    sPair[1][k] = (unsigned char)v;
+  }
   sp_stage<T::TP>(sC, craw, N * T::DD, HW, b, p0, np);
   sp_stage<T::TP>(sB, braw, N * T::K, HW, b, p0, np);
   sp_stage<T::TP>(sRaw, mraw, N, HW, b, p0, np);
@@ -167,8 +194,8 @@ __global__ void __launch_bounds__(SP_THREADS) spatial_gen_bwd_kernel(
   const float tl = tanhf(__ldg(lambda_sw));
   const int64_t base = (b * HW + p0) * per_px;
   // 1. g = dOmega where the clamp passed Omega through
-  for (int e = threadIdx.x; e < np * per_px; e += SP_THREADS) {
-    const int pl = e / per_px, r = e % per_px;
+  for (SpIter it(per_px); it.pl < np; it.next()) {
+    const int pl = it.pl, r = it.r, e = pl * per_px + r;
     const int n = r / T::DD, ij = r % T::DD, i = ij / D, j = ij % D;
     float J;
     const float om = sp_pre<D>(sC, sB, n, i, j, pl, tl, J) * (0.5f * sDs[n * T::LD + pl]);
@@ -221,8 +248,8 @@ __global__ void __launch_bounds__(SP_THREADS) spatial_gen_bwd_kernel(
     if (pl < np) dmraw[(b * N + n) * HW + p0 + pl] = sDm[n * T::LD + pl];
   }
   // 4. dC_in = dC + 0.5 tl (dpre - dpre^T), transposed into the C tile (read last in step 2)
-  for (int e = threadIdx.x; e < np * per_px; e += SP_THREADS) {
-    const int pl = e / per_px, r = e % per_px;
+  for (SpIter it(per_px); it.pl < np; it.next()) {
+    const int pl = it.pl, r = it.r, e = pl * per_px + r;
     const int n = r / T::DD, ij = r % T::DD, i = ij / D, j = ij % D;
     const float h = 0.5f * sDs[n * T::LD + pl];
     const float dij = sG[pl * LG + r] * h, dji = sG[pl * LG + n * T::DD + j * D + i] * h;
@@ -238,8 +265,7 @@ __global__ void __launch_bounds__(SP_THREADS) spatial_gen_bwd_kernel(
     const int r = t / T::TP, pl = t % T::TP;
     if (pl >= np) continue;
     const int n = r / T::K, k = r % T::K;
-    int u, v;
-    sp_triu_pair<D>(k, u, v);
+    const int u = sPair[0][k], v = sPair[1][k];
     const float h = 0.5f * sDs[n * T::LD + pl];
     const float* g = sG + pl * LG + n * T::DD;
     dbraw[(b * N * T::K + r) * HW + p0 + pl] = (g[u * D + v] - g[v * D + u]) * h;
@@ -253,7 +279,7 @@ namespace {
 
 using namespace csn;
 
-constexpr size_t SP_SMEM_MAX = 227 * 1024;
+constexpr size_t SP_SMEM_MAX = 227 * 1024 - 256;  // the backward also holds a static pair table
 
 size_t sp_fwd_smem(int64_t N, int D) {
   const int64_t DD = D * D, K = D * (D - 1) / 2, TP = sp_tp(D);

@@ -57,6 +57,24 @@ def test_invalid_arguments_are_rejected_without_a_gpu(lib):
     assert lib.csn_scan_fwd(null, null, null, null, 0, 4, 2, 8, 1, null, 0, null) == 0
 
 
+def test_spatial_generator_arguments_are_checked_without_a_gpu(lib):
+    null = ctypes.c_void_p(0)
+    fwd = lambda B, HW, N, D: lib.csn_spatial_generators_fwd(null, null, null, null, null, null, null, null,
+                                                             B, HW, N, D, null)
+    bwd = lambda B, HW, N, D: lib.csn_spatial_generators_bwd(*([null] * 13), B, HW, N, D, null)
+    assert fwd(2, 64, 1, 5) == 2 and b"4, 8 or 16" in lib.csn_last_error()
+    assert bwd(-1, 64, 1, 4) == 1
+    assert fwd(2, 64, 1, 16) == 1 and b"missing pointer" in lib.csn_last_error()
+    assert bwd(2, 64, 2, 8) == 1 and b"missing pointer" in lib.csn_last_error()
+    assert bwd(1, 64, 6, 16) == 2 and b"shared memory" in lib.csn_last_error()  # 6 neurons of 16 x 16
+    assert fwd(0, 64, 1, 4) == 0 and bwd(2, 0, 1, 16) == 0  # empty problems are a no-op
+    # one partial row per CTA: 64 / 32 / 16 pixels per CTA for D = 4 / 8 / 16
+    assert lib.csn_spatial_generators_partials(16, 6400, 4) == 1600
+    assert lib.csn_spatial_generators_partials(16, 1600, 16) == 1600
+    assert lib.csn_spatial_generators_partials(2, 33, 8) == 4
+    assert lib.csn_spatial_generators_partials(2, 33, 5) == 0
+
+
 def test_workspace_query_is_pure(lib):
     n1 = lib.csn_scan_workspace_bytes(32, 2048, 8, 8)
     n2 = lib.csn_rotor_scan_workspace_bytes(32, 2048, 8, 8)

@@ -87,6 +87,24 @@ struct SpTile {
   static constexpr int LD = TP + 1;
 };
 
+// Tile row of the injection entry (i, j): for D = 16, j is XOR-swizzled by i >> 1, so that a
+// warp reading entries (j, i) over j (the transposed read) touches 16 banks instead of 2
+// (rows 16 x LD floats apart share a bank pair); D = 4, 8 keep i D + j
+template <int D>
+__host__ __device__ __forceinline__ int sp_crow(int i, int j) { return D == 16 ? i * D + (j ^ (i >> 1)) : i * D + j; }
+
+// stage the NCHW injection columns into the swizzled tile rows of sp_crow
+template <int D, int TP>
+__device__ __forceinline__ void sp_stage_c(float* dst, const float* __restrict__ src, int rows, int64_t HW,
+                                           int64_t b, int64_t p0, int np) {
+  constexpr int DD = D * D;
+  for (int t = threadIdx.x; t < rows * TP; t += SP_THREADS) {
+    const int r = t / TP, pl = t % TP;
+    const int ij = r % DD, row = r - ij + sp_crow<D>(ij / D, ij % D);
+    dst[row * (TP + 1) + pl] = pl < np ? __ldg(src + (b * rows + r) * HW + p0 + pl) : 0.0f;
+  }
+}
+
 // stage rows [0, rows) of a [B, rows, HW] tensor's TP pixel columns starting at p0
 template <int TP>
 __device__ __forceinline__ void sp_stage(float* dst, const float* __restrict__ src, int rows, int64_t HW,
@@ -103,8 +121,8 @@ template <int D>
 __device__ __forceinline__ float sp_pre(const float* sC, const float* sB, int n, int i, int j, int pl, float tl,
                                         float& J) {
   using T = SpTile<D>;
-  const float cij = sC[(n * T::DD + i * D + j) * T::LD + pl];
-  const float cji = sC[(n * T::DD + j * D + i) * T::LD + pl];
+  const float cij = sC[(n * T::DD + sp_crow<D>(i, j)) * T::LD + pl];
+  const float cji = sC[(n * T::DD + sp_crow<D>(j, i)) * T::LD + pl];
   J = 0.5f * (cij - cji);
   float skew = 0.0f;
   if (i < j) skew = sB[(n * T::K + sp_triu_index<D>(i, j)) * T::LD + pl];
@@ -125,7 +143,7 @@ __global__ void __launch_bounds__(SP_THREADS) spatial_gen_fwd_kernel(
   const int64_t b = blockIdx.y;
   const int64_t p0 = (int64_t)blockIdx.x * T::TP;
   const int np = HW - p0 < T::TP ? (int)(HW - p0) : T::TP;
-  sp_stage<T::TP>(sC, craw, N * T::DD, HW, b, p0, np);
+  sp_stage_c<D, T::TP>(sC, craw, N * T::DD, HW, b, p0, np);
   sp_stage<T::TP>(sB, braw, N * T::K, HW, b, p0, np);
   sp_stage<T::TP>(sM, mraw, N, HW, b, p0, np);
   __syncthreads();
@@ -144,7 +162,7 @@ __global__ void __launch_bounds__(SP_THREADS) spatial_gen_fwd_kernel(
     float J;
     const float pre = sp_pre<D>(sC, sB, n, i, j, pl, tl, J);
     omega[base + e] = fminf(fmaxf(pre * (0.5f * ds), -3.0f), 3.0f);
-    cout[base + e] = sC[(n * T::DD + ij) * T::LD + pl];
+    cout[base + e] = sC[(n * T::DD + sp_crow<D>(i, j)) * T::LD + pl];
     if (ij == 0) {
       const float sg = sp_softplus(__ldg(gamma_log + n));
       decay[(b * HW + p0 + pl) * N + n] = sp_sigmoid(-sg * ds);
@@ -182,7 +200,7 @@ __global__ void __launch_bounds__(SP_THREADS) spatial_gen_bwd_kernel(
     sPair[0][k] = (unsigned char)u;
     sPair[1][k] = (unsigned char)v;
   }
-  sp_stage<T::TP>(sC, craw, N * T::DD, HW, b, p0, np);
+  sp_stage_c<D, T::TP>(sC, craw, N * T::DD, HW, b, p0, np);
   sp_stage<T::TP>(sB, braw, N * T::K, HW, b, p0, np);
   sp_stage<T::TP>(sRaw, mraw, N, HW, b, p0, np);
   __syncthreads();

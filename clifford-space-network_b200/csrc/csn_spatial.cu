@@ -35,6 +35,7 @@ namespace {
 
 constexpr int SP_THREADS = 256;
 constexpr unsigned SP_FULL = 0xffffffffu;
+constexpr int SP_BATCH = 4;      // global loads in flight per thread in the backward's entry loops
 
 // torch.nn.functional.softplus (beta 1, threshold 20) and its derivative
 __device__ __forceinline__ float sp_softplus(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
@@ -93,26 +94,43 @@ struct SpTile {
 template <int D>
 __host__ __device__ __forceinline__ int sp_crow(int i, int j) { return D == 16 ? i * D + (j ^ (i >> 1)) : i * D + j; }
 
-// stage the NCHW injection columns into the swizzled tile rows of sp_crow
-template <int D, int TP>
-__device__ __forceinline__ void sp_stage_c(float* dst, const float* __restrict__ src, int rows, int64_t HW,
-                                           int64_t b, int64_t p0, int np) {
-  constexpr int DD = D * D;
-  for (int t = threadIdx.x; t < rows * TP; t += SP_THREADS) {
-    const int r = t / TP, pl = t % TP;
-    const int ij = r % DD, row = r - ij + sp_crow<D>(ij / D, ij % D);
-    dst[row * (TP + 1) + pl] = pl < np ? __ldg(src + (b * rows + r) * HW + p0 + pl) : 0.0f;
+// Stage rows [0, rows) of a [B, rows, HW] tensor's TP pixel columns starting at p0 into tile
+// rows row_of(r): SP_STAGE loads in flight per thread before their shared-memory stores
+constexpr int SP_STAGE = 8;
+
+template <int TP, typename RowOf>
+__device__ __forceinline__ void sp_stage_rows(float* dst, const float* __restrict__ src, int rows, int64_t HW,
+                                              int64_t b, int64_t p0, int np, RowOf row_of) {
+  const int total = rows * TP;
+  for (int t0 = threadIdx.x; t0 < total; t0 += SP_THREADS * SP_STAGE) {
+    float v[SP_STAGE];
+#pragma unroll
+    for (int u = 0; u < SP_STAGE; ++u) {
+      const int t = t0 + u * SP_THREADS, r = t / TP, pl = t % TP;
+      v[u] = (t < total && pl < np) ? __ldg(src + (b * rows + r) * HW + p0 + pl) : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < SP_STAGE; ++u) {
+      const int t = t0 + u * SP_THREADS;
+      if (t < total) dst[row_of(t / TP) * (TP + 1) + t % TP] = v[u];
+    }
   }
 }
 
-// stage rows [0, rows) of a [B, rows, HW] tensor's TP pixel columns starting at p0
+// the NCHW injection columns, into the swizzled tile rows of sp_crow
+template <int D, int TP>
+__device__ __forceinline__ void sp_stage_c(float* dst, const float* __restrict__ src, int rows, int64_t HW,
+                                           int64_t b, int64_t p0, int np) {
+  sp_stage_rows<TP>(dst, src, rows, HW, b, p0, np, [](int r) {
+    const int ij = r % (D * D);
+    return r - ij + sp_crow<D>(ij / D, ij % D);
+  });
+}
+
 template <int TP>
 __device__ __forceinline__ void sp_stage(float* dst, const float* __restrict__ src, int rows, int64_t HW,
                                          int64_t b, int64_t p0, int np) {
-  for (int t = threadIdx.x; t < rows * TP; t += SP_THREADS) {
-    const int r = t / TP, pl = t % TP;
-    dst[r * (TP + 1) + pl] = pl < np ? __ldg(src + (b * rows + r) * HW + p0 + pl) : 0.0f;
-  }
+  sp_stage_rows<TP>(dst, src, rows, HW, b, p0, np, [](int r) { return r; });
 }
 
 // skew + tl 0.5 (C - C^T) at entry (i, j) of neuron n, pixel pl (Omega before the 0.5 ds
@@ -211,14 +229,27 @@ __global__ void __launch_bounds__(SP_THREADS) spatial_gen_bwd_kernel(
   __syncthreads();
   const float tl = tanhf(__ldg(lambda_sw));
   const int64_t base = (b * HW + p0) * per_px;
-  // 1. g = dOmega where the clamp passed Omega through
-  for (SpIter it(per_px); it.pl < np; it.next()) {
-    const int pl = it.pl, r = it.r, e = pl * per_px + r;
-    const int n = r / T::DD, ij = r % T::DD, i = ij / D, j = ij % D;
-    float J;
-    const float om = sp_pre<D>(sC, sB, n, i, j, pl, tl, J) * (0.5f * sDs[n * T::LD + pl]);
-    const bool pass = om >= -3.0f && om <= 3.0f;
-    sG[pl * LG + r] = pass ? __ldg(d_omega + base + e) : 0.0f;
+  // 1. g = dOmega where the clamp passed Omega through (SP_BATCH loads in flight per thread)
+  for (SpIter it(per_px); it.pl < np;) {
+    int pls[SP_BATCH], rs[SP_BATCH];
+    float dv[SP_BATCH];
+#pragma unroll
+    for (int u = 0; u < SP_BATCH; ++u) {
+      pls[u] = it.pl;
+      rs[u] = it.r;
+      dv[u] = it.pl < np ? __ldg(d_omega + base + it.pl * per_px + it.r) : 0.0f;
+      it.next();
+    }
+#pragma unroll
+    for (int u = 0; u < SP_BATCH; ++u) {
+      const int pl = pls[u], r = rs[u];
+      if (pl >= np) break;
+      const int n = r / T::DD, ij = r % T::DD, i = ij / D, j = ij % D;
+      float J;
+      const float om = sp_pre<D>(sC, sB, n, i, j, pl, tl, J) * (0.5f * sDs[n * T::LD + pl]);
+      const bool pass = om >= -3.0f && om <= 3.0f;
+      sG[pl * LG + r] = pass ? dv[u] : 0.0f;
+    }
   }
   __syncthreads();
   // 2. per (pixel, neuron): dds, dmetric and the lambda / gamma contributions (warp sums)
@@ -266,12 +297,25 @@ __global__ void __launch_bounds__(SP_THREADS) spatial_gen_bwd_kernel(
     if (pl < np) dmraw[(b * N + n) * HW + p0 + pl] = sDm[n * T::LD + pl];
   }
   // 4. dC_in = dC + 0.5 tl (dpre - dpre^T), transposed into the C tile (read last in step 2)
-  for (SpIter it(per_px); it.pl < np; it.next()) {
-    const int pl = it.pl, r = it.r, e = pl * per_px + r;
-    const int n = r / T::DD, ij = r % T::DD, i = ij / D, j = ij % D;
-    const float h = 0.5f * sDs[n * T::LD + pl];
-    const float dij = sG[pl * LG + r] * h, dji = sG[pl * LG + n * T::DD + j * D + i] * h;
-    sC[r * T::LD + pl] = __ldg(d_c + base + e) + 0.5f * tl * (dij - dji);
+  for (SpIter it(per_px); it.pl < np;) {
+    int pls[SP_BATCH], rs[SP_BATCH];
+    float dv[SP_BATCH];
+#pragma unroll
+    for (int u = 0; u < SP_BATCH; ++u) {
+      pls[u] = it.pl;
+      rs[u] = it.r;
+      dv[u] = it.pl < np ? __ldg(d_c + base + it.pl * per_px + it.r) : 0.0f;
+      it.next();
+    }
+#pragma unroll
+    for (int u = 0; u < SP_BATCH; ++u) {
+      const int pl = pls[u], r = rs[u];
+      if (pl >= np) break;
+      const int n = r / T::DD, ij = r % T::DD, i = ij / D, j = ij % D;
+      const float h = 0.5f * sDs[n * T::LD + pl];
+      const float dij = sG[pl * LG + r] * h, dji = sG[pl * LG + n * T::DD + j * D + i] * h;
+      sC[r * T::LD + pl] = dv[u] + 0.5f * tl * (dij - dji);
+    }
   }
   __syncthreads();
   // 5. NCHW gradients of the injection and generator convolutions (coalesced along pixels)

@@ -126,6 +126,15 @@ def _p(t):
     return ctypes.c_void_p(0 if t is None else t.data_ptr())
 
 
+def _cpu_threads(cores):
+    """Give the float64 CPU oracle every host core: set OMP_NUM_THREADS for this process
+    (torchrun starts ranks with OMP_NUM_THREADS=1) and set the oracle's OpenMP thread count
+    directly, which also holds when its library is already loaded.  Returns the count used."""
+    os.environ["OMP_NUM_THREADS"] = str(cores)
+    from oracle import oracle as orc
+    return orc.set_threads(cores)
+
+
 def _time_cpu(one, reps, warmup):
     for _ in range(warmup):
         one()
@@ -508,6 +517,7 @@ def run_sequence_parallel(args, ws, rank, local, cores):
             return 0
         from csn_b200 import algebra
         from oracle import oracle as orc
+        cores = _cpu_threads(cores)
         E = algebra.triu_basis(D)
         rng = np.random.default_rng(0)
         Ts, Cs = 8192, 4
@@ -619,6 +629,7 @@ def run_generation(args, ws, rank, local, cores):
             return 0
         from csn_b200 import algebra
         from oracle import oracle as orc
+        cores = _cpu_threads(cores)
         E = algebra.triu_basis(D)
         rng = np.random.default_rng(0)
         h = np.zeros((B, N, D, D))
@@ -693,6 +704,7 @@ def run_generation(args, ws, rank, local, cores):
     if not args.no_cpu_baseline:
         from csn_b200 import algebra
         from oracle import oracle as orc
+        cores = _cpu_threads(cores)
         E = algebra.triu_basis(D)
         rng = np.random.default_rng(0)
         hh = np.zeros((B, N, D, D))
@@ -867,7 +879,7 @@ def run_spatial(args, ws, rank, local, cores):
     if args.impl == "reference":
         if rank != 0:
             return 0
-        os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+        cores = _cpu_threads(cores)
         e, el, sample = _spatial_cpu(max(1, args.steps), min(args.warmup, 1), cores)
         v = e / el / 1e9
         print(json.dumps({"metric": metric, "value": v, "unit": "Gelem/s", "n_gpus": args.gpus, "steps": args.steps,
@@ -965,7 +977,7 @@ def run_spatial(args, ws, rank, local, cores):
     nbytes = sum(h.numel() * 4 for h in hx)
     cpu = None
     if not args.no_cpu_baseline:
-        os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+        cores = _cpu_threads(cores)
         e, el, sample = _spatial_cpu(2, 0, cores)
         cpu = {"value": e / el / 1e9, "unit": "Gelem/s", "cores": cores, "kind": "port", "sample": sample}
     print(json.dumps({
@@ -1016,7 +1028,7 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return 0
-        os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+        cores = _cpu_threads(cores)
         elems, el, sample = wl.cpu_reference(reps=max(1, args.steps), warmup=min(args.warmup, 1))
         v = elems / el / 1e9
         line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
@@ -1106,7 +1118,7 @@ def main():
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        os.environ.setdefault("OMP_NUM_THREADS", str(cores))
+        cores = _cpu_threads(cores)
         elems, el, sample = wl.cpu_reference(reps=2, warmup=0)
         cpu = {"value": elems / el / 1e9, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
 

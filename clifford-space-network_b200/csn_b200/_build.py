@@ -5,10 +5,16 @@
 Each ``csrc/*.cu`` is compiled to an object in ``csrc/_build/`` (in parallel) and the
 objects are linked into ``csn_b200/libcsn_b200.so`` with the CUDA runtime linked
 statically, so the library depends only on the driver.
+
+The build is content-addressed: a SHA-256 over every source, header and the build flags is
+compiled into the library (``csn_version()`` ends in ``src <hash>``) and recorded beside it,
+so a library whose sources changed since it was linked is rebuilt whatever the file times
+say, and a caller can check that the library it loaded is the one these sources make.
 """
 from __future__ import annotations
 
 import concurrent.futures as cf
+import hashlib
 import os
 import shutil
 import subprocess
@@ -35,25 +41,43 @@ def sources() -> list:
     return sorted(CSRC.glob("*.cu"))
 
 
-def _stale() -> bool:
-    if not LIB.exists():
-        return True
-    t = LIB.stat().st_mtime
-    deps = list(CSRC.glob("*.cu")) + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h"))
+HASH_FILE = LIB.with_name(LIB.name + ".srchash")
+# what the last build() call did: "built" or "reused"
+last_action = None
+
+
+def source_hash() -> str:
+    """SHA-256 (first 16 hex digits) over the build flags and every source and header."""
+    deps = sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h"))
     deps.append(ROOT.parent / "include" / "csn_b200.h")
-    return any(p.stat().st_mtime > t for p in deps if p.exists())
+    h = hashlib.sha256(" ".join(ARCH + FLAGS).encode())
+    for p in deps:
+        if p.exists():
+            h.update(p.name.encode())
+            h.update(p.read_bytes())
+    return h.hexdigest()[:16]
+
+
+def _stale(digest: str) -> bool:
+    if not LIB.exists() or not HASH_FILE.exists():
+        return True
+    return HASH_FILE.read_text().strip() != digest
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:
-    """Compile every CUDA source and link the shared library (skips when up to date)."""
-    if not force and not _stale():
+    """Compile every CUDA source and link the shared library (skipped when the library was
+    built from exactly these sources)."""
+    global last_action
+    digest = source_hash()
+    if not force and not _stale(digest):
+        last_action = "reused"
         return LIB
     nvcc = _nvcc()
     OBJ.mkdir(parents=True, exist_ok=True)
 
     def compile_one(src: Path) -> Path:
         obj = OBJ / (src.stem + ".o")
-        cmd = [nvcc, *ARCH, *FLAGS, "-c", str(src), "-o", str(obj)]
+        cmd = [nvcc, *ARCH, *FLAGS, f"-DCSN_SOURCE_HASH=\"{digest}\"", "-c", str(src), "-o", str(obj)]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"nvcc failed on {src.name}:\n{r.stdout}\n{r.stderr}")
@@ -69,6 +93,8 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
     os.replace(tmp, LIB)
+    HASH_FILE.write_text(digest + "\n")
+    last_action = "built"
     return LIB
 
 

@@ -778,9 +778,9 @@ class SpatialGeneratorsFunction(torch.autograd.Function):
         N = NDD // (D * D)
         cf, bf, mf = _f32(in_proj), _f32(biv_proj), _f32(metric)
         lf, gf = _f32(lambda_sw).reshape(1), _f32(gamma_log).reshape(N)
-        omega = torch.empty(B, H * W, N, D, D, device=cf.device)
+        omega = torch.empty(B, H * W, N, D, D, device=cf.device, dtype=torch.float32)
         c = torch.empty_like(omega)
-        decay = torch.empty(B, H * W, N, device=cf.device)
+        decay = torch.empty(B, H * W, N, device=cf.device, dtype=torch.float32)
         _lib.call("csn_spatial_generators_fwd", _ptr(cf), _ptr(bf), _ptr(mf), _ptr(lf), _ptr(gf), _ptr(omega),
                   _ptr(c), _ptr(decay), B, H * W, N, D, _stream(cf.device))
         ctx.save_for_backward(cf, bf, mf, lf, gf)
@@ -794,13 +794,14 @@ class SpatialGeneratorsFunction(torch.autograd.Function):
         D = ctx.D
         B, NDD, H, W = cf.shape
         N, HW = NDD // (D * D), H * W
-        zeros = lambda shape: torch.zeros(shape, device=cf.device)
+        zeros = lambda shape: torch.zeros(shape, device=cf.device, dtype=torch.float32)
         dom = _f32(d_omega) if d_omega is not None else zeros((B, HW, N, D, D))
         dc = _f32(d_c) if d_c is not None else zeros((B, HW, N, D, D))
         ddec = _f32(d_decay) if d_decay is not None else zeros((B, HW, N))
         dcraw, dbraw, dmraw = torch.empty_like(cf), torch.empty_like(bf), torch.empty_like(mf)
         P = _lib.load().csn_spatial_generators_partials(B, HW, D)
-        dlam, dgam = torch.empty(P, device=cf.device), torch.empty(P, N, device=cf.device)
+        dlam = torch.zeros(P, device=cf.device, dtype=torch.float32)
+        dgam = torch.zeros(P, N, device=cf.device, dtype=torch.float32)
         _lib.call("csn_spatial_generators_bwd", _ptr(cf), _ptr(bf), _ptr(mf), _ptr(lf), _ptr(gf), _ptr(dom),
                   _ptr(dc), _ptr(ddec), _ptr(dcraw), _ptr(dbraw), _ptr(dmraw), _ptr(dlam), _ptr(dgam),
                   B, HW, N, D, _stream(cf.device))

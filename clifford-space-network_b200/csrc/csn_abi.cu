@@ -86,6 +86,11 @@ extern "C" int csn_timing_read(const char* name, double* total_ms, int64_t* coun
   return CSN_OK;
 }
 
-extern "C" const char* csn_version(void) { return "csn_b200 0.1.0 (sm_100a)"; }
+#ifndef CSN_SOURCE_HASH
+#define CSN_SOURCE_HASH "unknown"
+#endif
+// "csn_b200 <version> (sm_100a) src <hash>": the hash of the sources the library was built
+// from (computed by the build script), so a caller can check which build it loaded
+extern "C" const char* csn_version(void) { return "csn_b200 0.2.0 (sm_100a) src " CSN_SOURCE_HASH; }
 
 extern "C" const char* csn_last_error(void) { return csn::g_last_error; }

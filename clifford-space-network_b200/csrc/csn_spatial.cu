@@ -359,8 +359,9 @@ int sp_check(const char* fn, int64_t B, int64_t HW, int64_t N, int D) {
     snprintf(msg, sizeof msg, "%s: D = %d, expected 4, 8 or 16", fn, D);
     return set_error(CSN_ERR_UNSUPPORTED, msg);
   }
-  if (B < 0 || HW < 0 || N < 0 || B > 65535 || HW > ((int64_t)1 << 35)) {
-    snprintf(msg, sizeof msg, "%s: B in [0, 65535], H*W >= 0, N >= 0 required", fn);
+  // grid.x = ceil(HW / TP) with TP >= 16 must stay below 2^31: H*W <= 2^34
+  if (B < 0 || HW < 0 || N < 0 || B > 65535 || HW > ((int64_t)1 << 34)) {
+    snprintf(msg, sizeof msg, "%s: B in [0, 65535], H*W in [0, 2^34], N >= 0 required", fn);
     return set_error(CSN_ERR_INVALID, msg);
   }
   if (sp_bwd_smem(N, D) > SP_SMEM_MAX) {
@@ -429,7 +430,15 @@ extern "C" int csn_spatial_generators_bwd(const float* in_proj, const float* biv
                                           float* dgamma_part, int64_t B, int64_t HW, int64_t N, int D,
                                           void* stream) {
   if (int rc = sp_check("csn_spatial_generators_bwd", B, HW, N, D)) return rc;
-  if (B * HW * N == 0) return CSN_OK;
+  if (B * HW * N == 0) {
+    // no neurons: the lambda partials (one per CTA tile) are still summed by the caller
+    const int64_t P = csn_spatial_generators_partials(B, HW, D);
+    if (P > 0 && dlambda_part) {
+      cudaError_t e = cudaMemsetAsync(dlambda_part, 0, sizeof(float) * P, static_cast<cudaStream_t>(stream));
+      if (e != cudaSuccess) return set_cuda_error(e, "csn_spatial_generators_bwd: cudaMemsetAsync");
+    }
+    return CSN_OK;
+  }
   if (!in_proj || !biv_proj || !metric || !lambda_sw || !gamma_log || !d_omega || !d_c || !d_decay || !d_in_proj ||
       !d_biv_proj || !d_metric || !dlambda_part || !dgamma_part)
     return set_error(CSN_ERR_INVALID, "csn_spatial_generators_bwd: missing pointer");

@@ -169,7 +169,10 @@ int csn_rotor_scan_heads_bwd(const float* gens, const float* dt, const float* ga
  * that loads it, until process exit; problems whose csn_scan_workspace_bytes(B, T, N, D)
  * exceeds 33554432 bytes are rejected with CSN_ERR_INVALID.  The first call on a device
  * looks up that array's device address (cudaGetSymbolAddress), so make it before any
- * stream capture.  All calls share the one array: calls that overlap on the GPU (other
+ * stream capture.  The address is cached per device ordinal for the life of the process:
+ * after cudaDeviceReset (or anything else that destroys the device's primary context and
+ * so reloads the module) the cached address is stale, and the entry point must not be
+ * called again on that device.  All calls share the one array: calls that overlap on the GPU (other
  * streams, other threads) race and must be serialised by the caller.  No scratch word
  * needs to start at zero: every word a call reads is written earlier in that call. */
 int csn_rotor_scan_fwd_noalloc(const float* gens, const float* dt, const float* gamma,

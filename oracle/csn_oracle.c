@@ -19,8 +19,24 @@
 #include <math.h>
 #include <stdlib.h>
 #include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
 
 #define ORC_MAXD 16
+
+/* Number of OpenMP threads for the calls that follow (a launcher may have set
+ * OMP_NUM_THREADS=1 for the whole process before the library was loaded).
+ * Returns the count in effect. */
+int orc_set_threads(int n) {
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+  return omp_get_max_threads();
+#else
+  (void)n;
+  return 1;
+#endif
+}
 
 /* ------------------------------------------------------------------------ */
 /* small dense helpers                                                       */

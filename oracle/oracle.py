@@ -72,6 +72,7 @@ def _load():
         "orc_ga3_scan_fwd": [_D, _D, _D, _D, _D, _L, _L, _L],
         "orc_ga3_scan_bwd": [_D, _D, _D, _D, _D, _D, _D, _D, _D, _L, _L, _L],
         "orc_cell_fwd": [_D, _D, _D, _D, _D, ctypes.c_double, _D, _L, _L, _L],
+        "orc_set_threads": [ctypes.c_int],
     }
     for name, args in sig.items():
         fn = getattr(lib, name)
@@ -81,9 +82,11 @@ def _load():
     return lib
 
 
-def set_threads(n: int) -> None:
-    """Number of OpenMP threads the oracle uses (must be set before first call)."""
+def set_threads(n: int) -> int:
+    """Number of OpenMP threads the oracle uses from now on, whatever OMP_NUM_THREADS the
+    process was started with (torchrun sets it to 1).  Returns the count in effect."""
     os.environ["OMP_NUM_THREADS"] = str(int(n))
+    return int(_load().orc_set_threads(int(n)))
 
 
 def _c(a):

@@ -24,8 +24,9 @@ functions called (paths relative to the reference root):
 * python/clifford_cl6.py:189 CliffordCL6ForCausalLM, python/clifford_cl8.py:199 CliffordCL8ForCausalLM,
   python/clifford_model.py:78,207 CliffordTENNBlock, CliffordTENNForCausalLM
 
-    python tests/golden/make_golden.py [group ...]     (groups: scans cayley rotor ga3 cells
-                                                        blocks spatial multihead lms; default: all)
+    [CSN_REFERENCE_ROOT=<reference root>] python tests/golden/make_golden.py [group ...]
+        (groups: scans cayley rotor ga3 cells blocks spatial multihead lms; default: all;
+         CSN_REFERENCE_ROOT defaults to /root/reference)
 """
 from __future__ import annotations
 
@@ -36,7 +37,9 @@ from pathlib import Path
 import numpy as np
 import torch
 
-REF = Path("/root/reference")
+# The reference tree to import and run: CSN_REFERENCE_ROOT, default /root/reference (the
+# read-only copy of the reference project on the machine that generated the fixtures).
+REF = Path(os.environ.get("CSN_REFERENCE_ROOT", "/root/reference"))
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
 sys.path.insert(0, str(REF))

@@ -4,9 +4,11 @@ Some hosts cannot let a library allocate device memory: they reserve the whole G
 for their own pool, or forbid allocation once their serving loop is running.  For
 them the library offers a forward rotor scan whose scratch lives in a static device
 array.  This test checks that entry point against the ordinary, workspace-taking
-csn_rotor_scan_fwd on two calls in a row with different inputs (the second call must
-not be disturbed by what the first left in the shared scratch), and that a problem
-too large for the static scratch is refused with a clear error.
+csn_rotor_scan_fwd for every matrix size (D = 4, 8, 16), on calls in a row with
+different inputs and shapes (a call must not be disturbed by what the one before it
+left in the shared scratch).  Both entry points run the same chunk plan and kernels, so
+their outputs are compared bit for bit.  A problem too large for the static scratch
+must be refused with a clear error.
 
 The file name sorts last so that a run stopping at the first failure has already run
 every other test; it is also self-contained, so it passes run alone in a fresh process.
@@ -20,7 +22,6 @@ import torch
 pytestmark = pytest.mark.gpu
 
 DEV = "cuda:0"
-TOL = 1e-4  # same forward tolerance as the other GPU parity tests
 
 
 def _case(seed, B, T, N, D):
@@ -61,14 +62,19 @@ def _run_both(lib, seed, B, T, N, D):
     return X, X_ref
 
 
-def test_noalloc_matches_workspace_entry_point_on_two_calls(lib):
-    # first call: 8 x 8 rotors over several chunks; second call: a different shape and
-    # seed, so stale scratch from the first call would show up as a mismatch
-    for seed, shape in ((11, (4, 777, 8, 8)), (12, (3, 1500, 5, 8))):
+# (seed, (B, T, N, D)): every case runs several chunks per sequence; consecutive cases
+# differ in shape and seed, so stale scratch from the call before would show up
+CASES = ((11, (4, 777, 8, 8)), (12, (3, 1500, 5, 8)), (13, (4, 2000, 8, 4)), (14, (2, 500, 3, 16)),
+         (15, (3, 911, 2, 4)), (16, (1, 300, 5, 16)))
+
+
+def test_noalloc_is_bit_identical_to_workspace_entry_point_on_calls_in_a_row(lib):
+    for seed, shape in CASES:
+        B, T, N, D = shape
+        assert 256 < lib.csn_scan_workspace_bytes(B, T, N, D) <= (32 << 20)  # chunked, fits
         X, X_ref = _run_both(lib, seed, *shape)
         assert torch.isfinite(X).all()
-        err = ((X - X_ref).abs().max() / X_ref.abs().max()).item()
-        assert err <= TOL, f"no-alloc vs workspace entry point: max-rel {err:.3e}"
+        assert torch.equal(X, X_ref), f"no-alloc differs from the workspace entry point at {shape}"
 
 
 def test_noalloc_refuses_problems_above_its_static_scratch(lib):

@@ -247,6 +247,27 @@ def _fmt_poly(entries, rv="r"):
     return s[2:] if s.startswith("+ ") else s
 
 
+def _fmt_unit_poly(entries, rv="r"):
+    """L[i][j] for a unit rotor.  An entry with an r0^2 term is a number near 1 for the rotors
+    of small steps; with r0^2 = 1 - r1^2 - r2^2 - r3^2 it is written as 1 + (small terms), the
+    small part summed first, so the entry is rounded once, unbiased.  Summing the squares
+    directly rounds quantities near 1 again and again, which leaves the map slightly
+    contracting or expanding in the same direction every step."""
+    c00 = sum(c for a, b, c in entries if a == 0 and b == 0)
+    if c00 == 0:
+        return _fmt_poly(entries, rv)
+    rest = {}
+    for a, b, c in entries:
+        if a == 0 and b == 0:
+            continue
+        rest[(a, b)] = rest.get((a, b), 0) + c
+    for m in (1, 2, 3):  # c00 r0^2 = c00 (1 - r1^2 - r2^2 - r3^2)
+        rest[(m, m)] = rest.get((m, m), 0) - c00
+    small = [(a, b, c) for (a, b), c in sorted(rest.items()) if c != 0]
+    one = f"{float(c00)}f" if c00 != 1 else "1.0f"
+    return f"{one} + ({_fmt_poly(small, rv)})" if small else one
+
+
 def emit_header(path: Path) -> str:
     """Write csrc/ga_tables.h and return its text."""
     lines = [
@@ -273,7 +294,7 @@ def emit_header(path: Path) -> str:
     ]
     nz = []
     for (i, j), ent in sorted(poly.items()):
-        lines.append(f"  L.m[{i}][{j}] = {_fmt_poly(ent)};")
+        lines.append(f"  L.m[{i}][{j}] = {_fmt_unit_poly(ent)};")
         nz.append((i, j))
     lines += ["}", ""]
     # vector-Jacobian product of (R h R~) with respect to the rotor components:

@@ -20,12 +20,9 @@ __global__ void __launch_bounds__(128) cayley_fwd_reg(const float* __restrict__ 
 #pragma unroll
   for (int i = 0; i < D; ++i)
 #pragma unroll
-    for (int j = 0; j < D; ++j) A.a[i][j] = ((i == j) ? 1.0f : 0.0f) - A.a[i][j];
-  gj_inverse(A);
-#pragma unroll
-  for (int i = 0; i < D; ++i)
-#pragma unroll
-    for (int j = 0; j < D; ++j) A.a[i][j] = 2.0f * A.a[i][j] - ((i == j) ? 1.0f : 0.0f);
+    for (int j = 0; j < D; ++j) A.a[i][j] = -A.a[i][j];  // (I - Om) - I
+  gj_inverse_dev(A);  // (I - Om)^{-1} - I
+  rotor_from_dev(A, 1.0f);
   store_mat(Q + e * D * D, A);
 }
 
@@ -67,17 +64,18 @@ __global__ void __launch_bounds__(128) cayley_fwd_16(const float* __restrict__ O
 #pragma unroll
   for (int q = 0; q < 8; ++q) {
     const int idx = lane + 32 * q;
-    A[idx] = ((idx / 16 == idx % 16) ? 1.0f : 0.0f) - Om[e * 256 + idx];
+    A[idx] = -Om[e * 256 + idx];  // deviation form: (I - Om) - I (see gj_inverse_dev)
   }
   __syncwarp();
   for (int k = 0; k < 16; ++k) {
-    const float inv = 1.0f / A[k * 16 + k];
+    const float ekk = A[k * 16 + k];
+    const float inv = 1.0f / (1.0f + ekk);
     float nv[8];
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       const int idx = lane + 32 * q, i = idx / 16, j = idx % 16;
       const float aij = A[idx];
-      if (i == k && j == k) nv[q] = inv;
+      if (i == k && j == k) nv[q] = -ekk * inv;
       else if (i == k) nv[q] = aij * inv;
       else if (j == k) nv[q] = -aij * inv;
       else nv[q] = aij - A[i * 16 + k] * A[k * 16 + j] * inv;
@@ -90,7 +88,7 @@ __global__ void __launch_bounds__(128) cayley_fwd_16(const float* __restrict__ O
 #pragma unroll
   for (int q = 0; q < 8; ++q) {
     const int idx = lane + 32 * q;
-    Q[e * 256 + idx] = 2.0f * A[idx] - ((idx / 16 == idx % 16) ? 1.0f : 0.0f);
+    Q[e * 256 + idx] = fmaf(2.0f, A[idx], (idx / 16 == idx % 16) ? 1.0f : 0.0f);
   }
 }
 

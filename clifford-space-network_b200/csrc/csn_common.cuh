@@ -107,26 +107,44 @@ __device__ __forceinline__ void rmul(Mat<D>& X, const Mat<D>& M) {
   }
 }
 
-// In-place Gauss-Jordan inverse without pivoting.  Only used on A = I - Omega with
-// Omega skew: the symmetric part of A and of every Schur complement of A is the
-// identity or larger, so every pivot is >= 1 and no pivoting is needed.
+// Gauss-Jordan inverse of A = I + E without pivoting, in deviation form: on entry E = A - I,
+// on exit E = A^{-1} - I.  Only used on A = I - Omega with Omega skew: the symmetric part of
+// A and of every Schur complement of A is the identity or larger, so every pivot is >= 1 and
+// no pivoting is needed.  The elimination is the plain in-place one (pivot 1 / d, row k / d,
+// column k -A_ik / d, the rest A_ij - A_ik A_kj / d), written for the deviations: the
+// diagonal keeps E_ii = A_ii - 1 instead of A_ii.  For the small generators of long scans the
+// entries of A^{-1} near 1 then never get rounded as numbers near 1 -- their deviations are
+// carried to full relative precision -- and the rotor built from them is orthogonal to
+// rounding level with no bias.  Rounding those entries themselves leaves every rotor short
+// of orthogonal in the same direction, which an undamped scan compounds step after step
+// (8e-4 of the state after 16384 steps of so(8) generators of size 1e-4).
 template <int D>
-__device__ __forceinline__ void gj_inverse(Mat<D>& A) {
+__device__ __forceinline__ void gj_inverse_dev(Mat<D>& E) {
 #pragma unroll
   for (int k = 0; k < D; ++k) {
-    const float inv = 1.0f / A.a[k][k];
-    A.a[k][k] = 1.0f;
+    const float ekk = E.a[k][k];
+    const float inv = 1.0f / (1.0f + ekk);
 #pragma unroll
-    for (int j = 0; j < D; ++j) A.a[k][j] *= inv;
+    for (int j = 0; j < D; ++j) E.a[k][j] = (j == k) ? -ekk * inv : E.a[k][j] * inv;
 #pragma unroll
     for (int i = 0; i < D; ++i) {
       if (i == k) continue;
-      const float f = A.a[i][k];
-      A.a[i][k] = 0.0f;
+      const float f = E.a[i][k];
 #pragma unroll
-      for (int j = 0; j < D; ++j) A.a[i][j] = fmaf(-f, A.a[k][j], A.a[i][j]);
+      for (int j = 0; j < D; ++j)
+        if (j != k) E.a[i][j] = fmaf(-f, E.a[k][j], E.a[i][j]);
+      E.a[i][k] = -f * inv;
     }
   }
+}
+
+// Cayley rotor M = sa (2 (I - Omega)^{-1} - I) = sa (I + 2 E) from E = (I - Omega)^{-1} - I.
+template <int D>
+__device__ __forceinline__ void rotor_from_dev(Mat<D>& E, float sa) {
+#pragma unroll
+  for (int i = 0; i < D; ++i)
+#pragma unroll
+    for (int j = 0; j < D; ++j) E.a[i][j] = sa * fmaf(2.0f, E.a[i][j], (i == j) ? 1.0f : 0.0f);
 }
 
 // ---------------------------------------------------------------- global loads
@@ -282,24 +300,25 @@ __host__ __device__ constexpr auto rho_biv_tab() {
   else return cl8_biv_tab();
 }
 
-// A <- I - h * sum_k g_k E_k  (h = dt / 2), for the generator layout BASIS.
+// E <- -h * sum_k g_k E_k  (h = dt / 2) = (I - Omega) - I, the deviation of A = I - Omega
+// from the identity (the input of gj_inverse_dev), for the generator layout BASIS.
 template <int D, int BASIS, int K>
-__device__ __forceinline__ void build_I_minus_omega(Mat<D>& A, const float (&g)[K], float h) {
+__device__ __forceinline__ void build_neg_omega(Mat<D>& E, const float (&g)[K], float h) {
   if constexpr (BASIS == BASIS_TRIU) {
     int k = 0;
 #pragma unroll
     for (int u = 0; u < D; ++u) {
-      A.a[u][u] = 1.0f;
+      E.a[u][u] = 0.0f;
 #pragma unroll
       for (int v = u + 1; v < D; ++v) {
         const float w = h * g[k];
-        A.a[u][v] = -w;
-        A.a[v][u] = w;
+        E.a[u][v] = -w;
+        E.a[v][u] = w;
         ++k;
       }
     }
   } else {
-    mat_identity(A);
+    mat_zero(E);
     constexpr auto tab = rho_biv_tab<D>();
 #pragma unroll
     for (int k = 0; k < K; ++k) {
@@ -308,7 +327,7 @@ __device__ __forceinline__ void build_I_minus_omega(Mat<D>& A, const float (&g)[
       for (int u = 0; u < D; ++u) {
         const int col = tab.col[k][u];
         const float sg = tab.sgn[k][u];
-        A.a[u][col] = fmaf(-sg, w, A.a[u][col]);
+        E.a[u][col] = fmaf(-sg, w, E.a[u][col]);
       }
     }
   }

@@ -58,7 +58,7 @@ __device__ __forceinline__ void rotor(const float* __restrict__ g, float dtv, fl
   om[2] = hh * __ldg(g + 2);
   w = om[0] * om[0] + om[1] * om[1] + om[2] * om[2];
   const float inv = 1.0f / (1.0f + w);
-  r[0] = (1.0f - w) * inv;
+  r[0] = 1.0f - 2.0f * w * inv;  // (1 - w) / (1 + w), rounded once near 1
   r[1] = 2.0f * om[0] * inv;
   r[2] = 2.0f * om[1] * inv;
   r[3] = 2.0f * om[2] * inv;

@@ -37,8 +37,8 @@ __device__ __forceinline__ void rotor_transition(const ScanArgs& a, int64_t b, i
   load_gens<K>(r.g, a.gens + e * K);
   const int64_t tp = tphys(a, t);
   r.dt = __ldg(a.dt + dt_index(a, b, tp, e - (b * a.T + tp) * a.N));
-  build_I_minus_omega<D, BASIS, K>(M, r.g, 0.5f * r.dt);
-  gj_inverse(M);  // M = A^{-1}
+  build_neg_omega<D, BASIS, K>(M, r.g, 0.5f * r.dt);
+  gj_inverse_dev(M);  // M = A^{-1} - I
   if constexpr (DAMPED) {
     r.gamma = __ldg(a.gamma + e);
     r.alpha = 1.0f / (1.0f + expf(r.gamma * r.dt));
@@ -48,11 +48,7 @@ __device__ __forceinline__ void rotor_transition(const ScanArgs& a, int64_t b, i
     r.alpha = 1.0f;
     r.sa = 1.0f;
   }
-  // M = sa * (2 A^{-1} - I)
-#pragma unroll
-  for (int i = 0; i < D; ++i)
-#pragma unroll
-    for (int j = 0; j < D; ++j) M.a[i][j] = r.sa * (2.0f * M.a[i][j] - ((i == j) ? 1.0f : 0.0f));
+  rotor_from_dev(M, r.sa);  // M = sa (2 A^{-1} - I)
 }
 
 // Load/build the transition M_t; returns the scale applied to the injected matrix

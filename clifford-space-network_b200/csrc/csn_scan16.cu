@@ -12,12 +12,22 @@
 //   forward      X' = M (M X^T)^T + C            (two products)
 //   chunk product P^T <- P^T M^T
 //   adjoint      H' = M^T (M^T G^T)^T,  dM = (G M) Xp^T + G^T (Xp^T M^T)^T, ...
-// Transposes are products with the identity.  Products run as 3xTF32: each fp32 operand
-// is split into a TF32 head and a TF32 tail and hi*hi + hi*lo + lo*hi is accumulated in
-// fp32, which keeps fp32-level accuracy.  The Cayley inverse (I - Omega)^{-1} is a short
-// matrix series when |h Omega|_F <= 0.1 (three or four products, accurate to 2e-8) and
-// otherwise a Gauss-Jordan elimination on the fragment, whose pivot rows and columns
-// reach the lanes that need them by shuffles; either way the step stays in registers.
+// Two tensor-core precisions, chosen by where a product's rounding error goes:
+//  * the recurrent products -- the state X, the chunk product P, the gradient carry H
+//    and g -- feed the next step, so their rounding errors accumulate over the whole
+//    sequence.  The tf32 MMA's fp32 accumulation truncates toward zero (about -0.3 ulp
+//    per MMA, -1 ulp with a chained C, measured on sm_100a), which shrinks an undamped
+//    state by a few ulps per step: 5e-4 off the float64 recurrence after 8192 steps at
+//    the Cl(8,0) benchmark shape.  These products therefore run on the FP64 tensor
+//    cores (mma.m8n8k4.f64 on f64 copies of the same fragments, "F16D"): exact fp32
+//    inputs, fp64 accumulation, one round-to-nearest when a value goes back to fp32;
+//  * the per-step adjoint products (dM, dOmega) and the transposes do not feed the
+//    recurrence and run as 3xTF32: each fp32 operand is split into a TF32 head and a
+//    TF32 tail and hi*hi + hi*lo + lo*hi is accumulated in fp32 (fp32-level error, no
+//    accumulation over time).  Transposes are products with the identity (exact).
+// The Cayley inverse (I - Omega)^{-1} is a Gauss-Jordan elimination on the fragment in
+// fp32 (round-to-nearest FMAs), whose pivot rows and columns reach the lanes that need
+// them by shuffles; the step stays in registers.
 #include <stdint.h>
 
 #include "csn_common.cuh"
@@ -190,13 +200,89 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-// In-place Gauss-Jordan inverse of the fragment (no pivoting: the matrices inverted
-// here are I - Omega with Omega skew, whose pivots are >= 1).  Pivot k: row k lives in
-// the quad g = k % 8, column k in the lanes t = (k % 8) / 2.  With d = a_kk, u = column k
-// except u_k = d - 1, and v = row k except v_k = d + 1, the whole in-place step
-//   a_ij - a_ik a_kj / d,  a_kj / d (row k),  -a_ik / d (column k),  1 / d (pivot)
-// is the single rank-1 update A <- A - u v^T / d.
-__device__ __forceinline__ void gj_inverse(F16& A, int lane) {
+// --------------------------------------------- fp64 fragments (recurrent products)
+// F16D holds the same matrix entries as F16 (same lane and slot), in fp64.
+struct F16D {
+  double v[2][4];
+};
+
+// d (8 x 8) += A (8 x 4) * B (4 x 8), fp64 in and out.  Lane (g, t): a = A[g][t],
+// b = B[t][g], d = D[g][2 t], D[g][2 t + 1].
+__device__ __forceinline__ void dmma(double (&d)[2], double a, double b) {
+  asm("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};\n"
+      : "+d"(d[0]), "+d"(d[1])
+      : "d"(a), "d"(b));
+}
+
+// A B^T on fp64 fragments.  Output tile (h, nz) = rows 8 h.., columns 8 nz..; its four
+// k-steps of 4 take, in slot t, the column 8 nt + 2 t + c (k-step 2 nt + c) of the rows
+// of A and of B that the lane holds -- the same column permutation on both sides.
+__device__ __forceinline__ F16D nt64(const F16D& A, const F16D& B) {
+  F16D z;
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int nz = 0; nz < 2; ++nz) {
+      double d[2] = {0.0, 0.0};
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) dmma(d, A.v[nt][2 * h + c], B.v[nt][2 * nz + c]);
+      z.v[nz][2 * h] = d[0];
+      z.v[nz][2 * h + 1] = d[1];
+    }
+  return z;
+}
+
+__device__ __forceinline__ F16D to_d(const F16& x) {
+  F16D y;
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) y.v[nt][e] = (double)x.v[nt][e];
+  return y;
+}
+__device__ __forceinline__ F16 to_f(const F16D& x) {
+  F16 y;
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) y.v[nt][e] = __double2float_rn(x.v[nt][e]);
+  return y;
+}
+__device__ __forceinline__ void d_zero(F16D& x) {
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) x.v[nt][e] = 0.0;
+}
+__device__ __forceinline__ F16D d_identity(int lane) {
+  F16D x;
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) x.v[nt][e] = (frow(lane, e) == fcol(lane, nt, e)) ? 1.0 : 0.0;
+  return x;
+}
+// y += a x (x fp32)
+__device__ __forceinline__ void d_axpy(F16D& y, float a, const F16& x) {
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) y.v[nt][e] = fma((double)a, (double)x.v[nt][e], y.v[nt][e]);
+}
+// X^T as the product I X^T (exact)
+__device__ __forceinline__ F16D transpose64(const F16D& X, int lane) { return nt64(d_identity(lane), X); }
+
+// In-place Gauss-Jordan inverse of the fragment in deviation form (as gj_inverse_dev in
+// csn_common.cuh): on entry E = A - I for A = I - Omega (no pivoting: Omega skew, pivots
+// >= 1), on exit E = A^{-1} - I, so entries near 1 are carried as their deviations.
+// Pivot k: row k lives in the quad g = k % 8, column k in the lanes t = (k % 8) / 2.  With
+// d = 1 + E_kk, u = column k of E and v = row k of E except v_k = E_kk + 2, the whole
+// in-place step
+//   E_ij - E_ik E_kj / d,  E_kj / d (row k),  -E_ik / d (column k),  -E_kk / d (pivot)
+// is the single rank-1 update E <- E - u v^T / d.
+__device__ __forceinline__ void gj_inverse_dev(F16& A, int lane) {
   const int g = lane >> 2, t = lane & 3;
 #pragma unroll
   for (int k = 0; k < 16; ++k) {
@@ -210,9 +296,8 @@ __device__ __forceinline__ void gj_inverse(F16& A, int lane) {
 #pragma unroll
     for (int h = 0; h < 2; ++h) u[h] = __shfl_sync(FULL, A.v[kn][2 * h + ke], 4 * g + kt);
     const float piv = __shfl_sync(FULL, A.v[kn][2 * kh + ke], 4 * kg + kt);
-    const float inv = __frcp_rn(piv);
-    if (g == kg) u[kh] -= 1.0f;   // this lane holds row k
-    if (t == kt) v[kn][ke] += 1.0f;  // this lane holds column k
+    const float inv = __frcp_rn(1.0f + piv);
+    if (t == kt) v[kn][ke] += 2.0f;  // this lane holds column k
     const float p0 = u[0] * inv, p1 = u[1] * inv;
 #pragma unroll
     for (int n2 = 0; n2 < 2; ++n2)
@@ -280,76 +365,23 @@ __device__ __forceinline__ void build_Om(F16& Om, const float* gs, const uint32_
     }
 }
 
-// |Om|_F^2 at or below these takes a series inverse (|Om|_2 <= |Om|_F <= 0.1 or 0.05).
-constexpr float kSeriesFro2 = 0.01f;
-constexpr float kShortSeriesFro2 = 0.0025f;
-
-// M = sa (2 (I - Om)^{-1} - I), in place on Om.
-// (I - Om)^{-1} = (I + Om) (I - W)^{-1} with W = Om^2 (Om skew, so W is symmetric and
-// |W|_2 <= |Om|_F^2 = eps^2), and (I - W)^{-1} = sum_k W^k:
-//   eps <= 0.05:  (I + Om) (I + W + W^2)       truncation <= eps^6 / (1 - eps^2) <= 1.6e-8
-//   eps <= 0.1:   (I + Om) (I + W) (I + W^2)   truncation <= eps^8 / (1 - eps^2) <= 1.01e-8
-// -- three or four products whose operands are symmetric or skew, so each is a plain
-// A B^T with no transposes; larger Om takes the Gauss-Jordan elimination.  The choice is
-// uniform across the warp (one matrix per warp).
+// M = sa (2 (I - Om)^{-1} - I) = sa (I + 2 E), E = (I - Om)^{-1} - I, in place on Om, by
+// Gauss-Jordan elimination in fp32 in deviation form (round-to-nearest FMAs on entries that
+// stay small).  A matrix series for the inverse in tf32 MMAs would be cheaper, but it rounds
+// the entries near 1 of (I - Om)^{-1} itself, with the MMA's truncating accumulation on top,
+// which leaves every rotor short of orthogonal in the same direction; an undamped scan
+// compounds that over the whole sequence.
 __device__ __forceinline__ void cayley(F16& M, float sa, int lane) {
-  const float fro2 = warp_sum(f_dot(M, M));
-  if (fro2 <= kSeriesFro2) {
-    F16S Os;
-    split(Os, M);
-    F16 W;
-    nt(W, Os, Os);  // Om Om^T = -Om^2
-    F16 U;          // I + Om
 #pragma unroll
-    for (int n2 = 0; n2 < 2; ++n2)
+  for (int n2 = 0; n2 < 2; ++n2)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        W.v[n2][e] = -W.v[n2][e];
-        U.v[n2][e] = ((frow(lane, e) == fcol(lane, n2, e)) ? 1.0f : 0.0f) + M.v[n2][e];
-      }
-    F16S Ws;
-    split(Ws, W);
-    F16 Q;
-    nt(Q, Ws, Ws);  // W W^T = W^2
-    F16 E;          // symmetric
-    if (fro2 <= kShortSeriesFro2) {
-#pragma unroll
-      for (int n2 = 0; n2 < 2; ++n2)
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          E.v[n2][e] = ((frow(lane, e) == fcol(lane, n2, e)) ? 1.0f : 0.0f) + W.v[n2][e] + Q.v[n2][e];
-    } else {
-      F16 P;
-#pragma unroll
-      for (int n2 = 0; n2 < 2; ++n2)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float id = (frow(lane, e) == fcol(lane, n2, e)) ? 1.0f : 0.0f;
-          P.v[n2][e] = id + W.v[n2][e];
-          Q.v[n2][e] += id;
-        }
-      F16S Ps, Qs;
-      split(Ps, P);
-      split(Qs, Q);
-      nt(E, Ps, Qs);  // (I + W) (I + W^2)
-    }
-    F16S Us, Es;
-    split(Us, U);
-    split(Es, E);
-    nt(M, Us, Es);  // (I + Om) E
-  } else {
-#pragma unroll
-    for (int n2 = 0; n2 < 2; ++n2)
-#pragma unroll
-      for (int e = 0; e < 4; ++e)
-        M.v[n2][e] = ((frow(lane, e) == fcol(lane, n2, e)) ? 1.0f : 0.0f) - M.v[n2][e];
-    gj_inverse(M, lane);
-  }
+    for (int e = 0; e < 4; ++e) M.v[n2][e] = -M.v[n2][e];  // E = (I - Om) - I
+  gj_inverse_dev(M, lane);
 #pragma unroll
   for (int n2 = 0; n2 < 2; ++n2)
 #pragma unroll
     for (int e = 0; e < 4; ++e)
-      M.v[n2][e] = sa * (2.0f * M.v[n2][e] - ((frow(lane, e) == fcol(lane, n2, e)) ? 1.0f : 0.0f));
+      M.v[n2][e] = sa * fmaf(2.0f, M.v[n2][e], (frow(lane, e) == fcol(lane, n2, e)) ? 1.0f : 0.0f);
 }
 
 __device__ const Cl8BivTab g_cl8_tab = cl8_biv_tab();
@@ -453,16 +485,20 @@ __global__ void __launch_bounds__(128) fwd16_kernel(ScanArgs a) {
   constexpr int KR = (K + 31) / 32;
   S16_PROLOGUE(BASIS, K);
   const int lane = w.lane;
-  F16 X, Pt;
+  F16D X, Pt;  // recurrent: fp64 fragments
   if (REDUCE) {
-    f_zero(X);
-    f_identity(Pt, lane);
+    d_zero(X);
+    Pt = d_identity(lane);
   } else if (a.nchunks > 1) {
-    f_load_plain(X, a.carry + (w.s * a.nchunks + w.j) * DD, lane);
+    F16 x;
+    f_load_plain(x, a.carry + (w.s * a.nchunks + w.j) * DD, lane);
+    X = to_d(x);
   } else if (a.h0) {
-    f_load(X, a.h0 + w.s * DD, lane);
+    F16 x;
+    f_load(x, a.h0 + w.s * DD, lane);
+    X = to_d(x);
   } else {
-    f_zero(X);
+    d_zero(X);
   }
   float gr[KR];
   if (SRC == SRC_ROTOR && w.t0 < w.t1) fetch_gens<K>(gr, a.gens, elem(a, w.b, w.t0, w.n), lane);
@@ -478,30 +514,24 @@ __global__ void __launch_bounds__(128) fwd16_kernel(ScanArgs a) {
     float alpha, sa, dtv, gam;
     step_matrix<SRC, BASIS, DAMPED, K>(a, w, terms, e, t, M, alpha, sa, dtv, gam);
     const float cs = (SRC == SRC_ROTOR && DAMPED) ? (1.0f - alpha) : 1.0f;
-    F16S Ms, Xs;
-    split(Ms, M);
-    split(Xs, X);
-    F16 V;
+    const F16D Md = to_d(M);
+    F16D V;
     if constexpr (TWO) {
-      nt(V, Ms, Xs);  // M X^T
+      V = nt64(Md, X);  // M X^T
     } else {
-      transpose(V, Xs, lane);  // X^T
+      V = transpose64(X, lane);  // X^T
     }
-    F16S Vs;
-    split(Vs, V);
-    nt(X, Ms, Vs);  // M V^T:  M X M^T  |  M X
-    f_axpy(X, cs, Cin);
+    X = nt64(Md, V);  // M V^T:  M X M^T  |  M X
+    d_axpy(X, cs, Cin);
     if constexpr (REDUCE) {
-      F16S Ps;
-      split(Ps, Pt);
-      nt(Pt, Ps, Ms);  // P^T M^T = (M P)^T
+      Pt = nt64(Pt, Md);  // P^T M^T = (M P)^T
     } else {
-      f_store<true>(a.out + e * DD, X, lane);
+      f_store<true>(a.out + e * DD, to_f(X), lane);
     }
   }
   if constexpr (REDUCE) {
-    f_store<false>(a.aggC + (w.s * a.nchunks + w.j) * DD, X, lane);
-    f_store_t(a.aggP + (w.s * a.nchunks + w.j) * DD, Pt, lane);
+    f_store<false>(a.aggC + (w.s * a.nchunks + w.j) * DD, to_f(X), lane);
+    f_store_t(a.aggP + (w.s * a.nchunks + w.j) * DD, to_f(Pt), lane);
   }
 }
 
@@ -515,9 +545,9 @@ __global__ void __launch_bounds__(128, 4) bwd16_reduce_kernel(ScanArgs a) {
   S16_PROLOGUE(BASIS, K);
   if (w.j == 0 && !a.agg_mode) return;  // chunk 0's aggregate is only used by shard aggregates
   const int lane = w.lane;
-  F16 Gc, P;
-  f_zero(Gc);
-  f_identity(P, lane);
+  F16D Gc, P;  // recurrent: fp64 fragments
+  d_zero(Gc);
+  P = d_identity(lane);
   float gr[KR];
   if (SRC == SRC_ROTOR && w.t0 < w.t1) fetch_gens<K>(gr, a.gens, elem(a, w.b, w.t1 - 1, w.n), lane);
   for (int64_t t = w.t1 - 1; t >= w.t0; --t) {
@@ -531,34 +561,29 @@ __global__ void __launch_bounds__(128, 4) bwd16_reduce_kernel(ScanArgs a) {
     F16 M;
     float alpha, sa, dtv, gam;
     step_matrix<SRC, BASIS, DAMPED, K>(a, w, terms, e, t, M, alpha, sa, dtv, gam);
-    F16S Ms, Mts;
-    split(Ms, M);
     F16 Mt;
     // M in memory (a given M, or the cached rotor): read it transposed instead of a product
     const float* mem_m = (SRC == SRC_MC) ? a.M : a.Mc_in;
-    if (mem_m) f_load_t(Mt, mem_m + e * DD, lane);
-    else transpose(Mt, Ms, lane);
-    split(Mts, Mt);
-    f_axpy(Gc, 1.0f, dX);  // G = g + dX
-    F16S Gs;
-    split(Gs, Gc);
-    F16 W;
-    if constexpr (TWO) {
-      nt(W, Mts, Gs);  // M^T G^T
+    if (mem_m) {
+      f_load_t(Mt, mem_m + e * DD, lane);
     } else {
-      transpose(W, Gs, lane);  // G^T
+      F16S Ms;
+      split(Ms, M);
+      transpose(Mt, Ms, lane);
     }
-    F16S Ws;
-    split(Ws, W);
-    nt(Gc, Mts, Ws);  // M^T G M  |  M^T G
-    if (!a.reuse_P) {
-      F16S Ps;
-      split(Ps, P);
-      nt(P, Ps, Mts);  // P M
+    const F16D Mtd = to_d(Mt);
+    d_axpy(Gc, 1.0f, dX);  // G = g + dX
+    F16D W;
+    if constexpr (TWO) {
+      W = nt64(Mtd, Gc);  // M^T G^T
+    } else {
+      W = transpose64(Gc, lane);  // G^T
     }
+    Gc = nt64(Mtd, W);  // M^T G M  |  M^T G
+    if (!a.reuse_P) P = nt64(P, Mtd);  // P M
   }
-  f_store<false>(a.aggC + (w.s * a.nchunks + w.j) * DD, Gc, lane);
-  if (!a.reuse_P) f_store<false>(a.aggP + (w.s * a.nchunks + w.j) * DD, P, lane);
+  f_store<false>(a.aggC + (w.s * a.nchunks + w.j) * DD, to_f(Gc), lane);
+  if (!a.reuse_P) f_store<false>(a.aggP + (w.s * a.nchunks + w.j) * DD, to_f(P), lane);
 }
 
 // -------------------------------------------------------------- backward: apply
@@ -573,10 +598,14 @@ __global__ void __launch_bounds__(128, 3) bwd16_apply_kernel(ScanArgs a) {
   constexpr int KR = (K + 31) / 32;
   S16_PROLOGUE(BASIS, K);
   const int lane = w.lane;
-  F16 H;
-  if (a.nchunks > 1) f_load_plain(H, a.carry + (w.s * a.nchunks + w.j) * DD, lane);
-  else if (a.hT) f_load(H, a.hT + w.s * DD, lane);
-  else f_zero(H);
+  F16D H;  // recurrent gradient carry: fp64 fragment
+  {
+    F16 h;
+    if (a.nchunks > 1) f_load_plain(h, a.carry + (w.s * a.nchunks + w.j) * DD, lane);
+    else if (a.hT) f_load(h, a.hT + w.s * DD, lane);
+    else f_zero(h);
+    H = to_d(h);
+  }
   // triu generator k = lane + 32 m  ->  (i, j) packed as i * 16 + j
   int kpair[KR];
   if constexpr (SRC == SRC_ROTOR && BASIS == BASIS_TRIU) {
@@ -612,8 +641,20 @@ __global__ void __launch_bounds__(128, 3) bwd16_apply_kernel(ScanArgs a) {
     F16 Mt;
     transpose(Mt, Ms, lane);  // (reading M^T from memory measured 0.6 % slower here)
     split(Mts, Mt);
-    F16 G = H;
-    f_axpy(G, 1.0f, dX);
+    // G = H + dX in fp64; the carry to the previous step, M^T G M (one-sided M^T G), is
+    // formed from it right away, and the step's gradients use G rounded to fp32
+    F16 G;
+    {
+      F16D Gd = H;
+      d_axpy(Gd, 1.0f, dX);
+      G = to_f(Gd);
+      const F16D Mtd = to_d(Mt);
+      if constexpr (TWO) {
+        H = nt64(Mtd, nt64(Mtd, Gd));  // M^T (M^T G^T)^T = M^T G M
+      } else {
+        H = nt64(Mtd, transpose64(Gd, lane));  // M^T G
+      }
+    }
     F16S Gs;
     split(Gs, G);
     const float cs = (SRC == SRC_ROTOR && DAMPED) ? (1.0f - alpha) : 1.0f;
@@ -720,18 +761,8 @@ __global__ void __launch_bounds__(128, 3) bwd16_apply_kernel(ScanArgs a) {
         a.ddt_part[e] = ddt;
       }
     }
-    // ---- H <- M^T G M  |  M^T G
-    if constexpr (TWO) {
-      F16 W;
-      nt(W, Mts, Gs);  // M^T G^T
-      F16S Ws;
-      split(Ws, W);
-      nt(H, Mts, Ws);  // M^T G M
-    } else {
-      nt(H, Mts, Gts);  // M^T G
-    }
   }
-  if (w.j == 0 && a.dh0) f_store<false>(a.dh0 + w.s * DD, H, lane);
+  if (w.j == 0 && a.dh0) f_store<false>(a.dh0 + w.s * DD, to_f(H), lane);
 }
 
 unsigned nblk(int64_t warps) { return (unsigned)((warps + WARPS - 1) / WARPS); }

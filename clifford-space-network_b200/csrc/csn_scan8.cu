@@ -148,8 +148,8 @@ __device__ __forceinline__ void cayley_from_slot(const float* gslot, float dtv, 
     const float4 f = *reinterpret_cast<const float4*>(gslot + 4 * v);
     g[4 * v] = f.x; g[4 * v + 1] = f.y; g[4 * v + 2] = f.z; g[4 * v + 3] = f.w;
   }
-  build_I_minus_omega<8, BASIS_TRIU, K>(M, g, 0.5f * dtv);
-  gj_inverse(M);
+  build_neg_omega<8, BASIS_TRIU, K>(M, g, 0.5f * dtv);
+  gj_inverse_dev(M);  // (I - Omega)^{-1} - I
   if constexpr (DAMPED) {
     alpha = 1.0f / (1.0f + expf(gam * dtv));
     sa = sqrtf(alpha);
@@ -157,10 +157,7 @@ __device__ __forceinline__ void cayley_from_slot(const float* gslot, float dtv, 
     alpha = 1.0f;
     sa = 1.0f;
   }
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) M.a[i][j] = sa * (2.0f * M.a[i][j] - ((i == j) ? 1.0f : 0.0f));
+  rotor_from_dev(M, sa);
 }
 
 __device__ __forceinline__ void thread_coords(const ScanArgs& a, int64_t tid, int64_t& b, int64_t& n,
@@ -801,7 +798,7 @@ int run8(const ScanArgs& a, bool bwd, cudaStream_t st) {
 // row-parallel: eight lanes per state, lane r owns row r of A = I - Omega, of M and of X.
 // The Gauss-Jordan pivot row is broadcast within the 8-lane group by shuffles; the rows of
 // X and M that the products need go through shared memory.  The arithmetic per entry is
-// the same sequence as the sequential scan (build_I_minus_omega, gj_inverse, lmul, rmulT),
+// the same sequence as the sequential scan (build_neg_omega, gj_inverse_dev, lmul, rmulT),
 // so a step equals the scan's step.
 constexpr int STEP_THREADS = 128;
 
@@ -835,11 +832,11 @@ __global__ void __launch_bounds__(STEP_THREADS) step8_kernel(const float* __rest
   }
   const float dtv = active ? __ldg(dt + b) : 0.0f;
   const float hdt = 0.5f * dtv;
-  float row[8];
+  float row[8];  // row r of E = A - I (the deviation form of gj_inverse_dev)
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
     if (c == r) {
-      row[c] = 1.0f;
+      row[c] = 0.0f;
     } else {
       const int u = c < r ? c : r, v = c < r ? r : c;
       const int k = u * 8 - u * (u + 1) / 2 + (v - u - 1);
@@ -847,23 +844,25 @@ __global__ void __launch_bounds__(STEP_THREADS) step8_kernel(const float* __rest
       row[c] = c < r ? w : -w;
     }
   }
-  // Gauss-Jordan without pivoting (every pivot of I - Omega is >= 1)
+  // Gauss-Jordan without pivoting (every pivot of I - Omega is >= 1), in the deviation
+  // form of gj_inverse_dev: rows end as those of (I - Omega)^{-1} - I
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
     float p[8];
 #pragma unroll
     for (int c = 0; c < 8; ++c) p[c] = __shfl_sync(FULL, row[c], k, 8);
-    const float inv = 1.0f / p[k];
+    const float inv = 1.0f / (1.0f + p[k]);
 #pragma unroll
-    for (int c = 0; c < 8; ++c) p[c] = (c == k) ? inv : p[c] * inv;
+    for (int c = 0; c < 8; ++c) p[c] = (c == k) ? -p[k] * inv : p[c] * inv;
     if (r == k) {
 #pragma unroll
       for (int c = 0; c < 8; ++c) row[c] = p[c];
     } else {
       const float f = row[k];
-      row[k] = 0.0f;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) row[c] = fmaf(-f, p[c], row[c]);
+      for (int c = 0; c < 8; ++c)
+        if (c != k) row[c] = fmaf(-f, p[c], row[c]);
+      row[k] = -f * inv;
     }
   }
   float alpha = 1.0f, sa = 1.0f;
@@ -874,7 +873,7 @@ __global__ void __launch_bounds__(STEP_THREADS) step8_kernel(const float* __rest
     }
   }
 #pragma unroll
-  for (int c = 0; c < 8; ++c) row[c] = sa * (2.0f * row[c] - ((c == r) ? 1.0f : 0.0f));
+  for (int c = 0; c < 8; ++c) row[c] = sa * fmaf(2.0f, row[c], (c == r) ? 1.0f : 0.0f);
   sts_row(&sX[grp][8 * r], xr);
   sts_row(&sM[grp][8 * r], row);
   __syncwarp();

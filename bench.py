@@ -27,10 +27,14 @@ seeded, float32, shaped like the reference's configurations):
 * ``spatial`` -- the detector's three spatial rotor blocks (Cl(4) 80 x 80, Cl(8) 40 x 40 and
   20 x 20 feature maps of a 640 x 640 image), batch 16, forward + backward.
 
-N > 1 runs under torchrun: every rank owns its own batch (independent sequences, no
-data-path collective: weak scaling); time is the max over ranks.  ``--impl reference``
-times the float64 CPU restatement of the reference algorithm (the oracle) on the host
-cores instead, on a bounded sample of the same workload.
+Without ``--workload``, a run started by torch.distributed.run (at any world size, 1
+included) is the ``sp`` workload -- the long-sequence configuration that is split over
+GPUs, strong scaling, with one NCCL all-gather per direction -- and a plain run is
+``cl6_lm``.  The other workloads under torchrun run one replica per rank (independent
+sequences, no data-path collective: weak scaling); time is the max over ranks.
+``--impl reference`` times the float64 CPU restatement of the reference algorithm (the
+oracle) on the host cores instead, on a bounded sample of the same workload; under torchrun
+rank 0 alone runs it.
 """
 from __future__ import annotations
 
@@ -52,6 +56,12 @@ sys.path.insert(0, str(REPO))
 
 METRIC = "rotor-scan fwd+bwd Gelem/s (B*L*C)"
 UNIT = "Gelem/s"
+
+
+def launched_by_torchrun():
+    """True when torch.distributed.run started this process (it sets these for every world
+    size, 1 included)."""
+    return any(k in os.environ for k in ("TORCHELASTIC_RUN_ID", "LOCAL_WORLD_SIZE", "GROUP_RANK"))
 
 
 def dist_env():
@@ -142,6 +152,81 @@ def _time_cpu(one, reps, warmup):
     for _ in range(reps):
         one()
     return time.perf_counter() - t0
+
+
+# ================================================= the reference's own fp32 CPU path
+# Runs in a child process whose import path holds only the reference toolkit installed in
+# baseline/_ref (its `csn` package would otherwise meet this repository's drop-in `csn`).
+_REF_CPU_SCRIPT = r"""
+import json, sys, time
+sys.path.insert(0, sys.argv[1])
+import torch
+from csn import rotors as rr, scan as rs
+threads = int(sys.argv[2])
+torch.set_num_threads(threads)
+B, T, N, D = map(int, sys.argv[3:7])
+K = D * (D - 1) // 2
+g = torch.Generator().manual_seed(0)
+gens = torch.randn(B, T, N, K, generator=g)
+dt = torch.rand(B, T, generator=g) * 0.02 + 0.04
+gamma = torch.nn.functional.softplus(torch.randn(B, T, N, generator=g) * 0.5)
+S = torch.randn(B, T, N, D, D, generator=g)
+dX = torch.randn(B, T, N, D, D, generator=g)
+iu = torch.triu_indices(D, D, 1)
+
+def step(scan):
+    gg, dd, ga, SS = (t.clone().requires_grad_(True) for t in (gens, dt, gamma, S))
+    skew = torch.zeros(B, T, N, D, D)
+    skew[..., iu[0], iu[1]] = gg
+    skew[..., iu[1], iu[0]] = -gg
+    h = (0.5 * dd)[:, :, None, None, None]
+    Q = rr.cayley_rotor_8x8(skew * h, use_schulz=False)
+    a = torch.sigmoid(-ga * dd[:, :, None])[..., None, None]
+    X = scan(torch.sqrt(a) * Q, (1 - a) * SS)
+    X.backward(dX)
+
+out = {}
+for name, scan in (("tree_two_sided", lambda M, C: rs._parallel_tree_scan(M, C, is_spinor_bundle=False)),
+                   ("sequential_one_sided", lambda M, C: rs.CliffordScanFunction.apply(M, C))):
+    step(scan)  # warm-up
+    t0 = time.perf_counter()
+    step(scan)
+    out[name] = B * T * N / (time.perf_counter() - t0) / 1e9
+model = ""
+try:
+    for line in open("/proc/cpuinfo"):
+        if line.startswith("model name"):
+            model = line.split(":", 1)[1].strip()
+            break
+except OSError:
+    pass
+print(json.dumps({"gelem_s": out, "threads": threads, "cpu": model}))
+"""
+
+
+def reference_fp32_cpu(cores, B=4, T=2048, N=8, D=8, timeout=600):
+    """The reference toolkit's own CPU scan path (baseline/_ref: csn.rotors.cayley_rotor_8x8 with
+    use_schulz=False, decay, then csn.scan's two-sided tree _parallel_tree_scan and the one-sided
+    sequential CliffordScanFunction), fp32, forward + backward by autograd, on a slice of the
+    Cl(6) LM configuration with all host threads.  None-free: on any failure the reason."""
+    import subprocess
+    ref = REPO / "baseline" / "_ref"
+    if not (ref / "csn" / "scan.py").exists():
+        return {"unavailable": "the reference toolkit is not installed in baseline/_ref"}
+    env = dict(os.environ, PYTHONDONTWRITEBYTECODE="1", OMP_NUM_THREADS=str(cores), PYTHONPATH=str(ref))
+    try:
+        r = subprocess.run([sys.executable, "-c", _REF_CPU_SCRIPT, str(ref), str(cores), str(B), str(T), str(N),
+                            str(D)], capture_output=True, text=True, timeout=timeout, cwd=str(ref), env=env)
+        if r.returncode != 0:
+            return {"unavailable": (r.stderr.strip().splitlines() or ["failed"])[-1][:200]}
+        d = json.loads(r.stdout.strip().splitlines()[-1])
+    except Exception as e:  # noqa: BLE001 -- a baseline that cannot run must not fail the bench
+        return {"unavailable": repr(e)[:200]}
+    return {"unit": UNIT, "value_tree_two_sided": d["gelem_s"]["tree_two_sided"],
+            "value_sequential_one_sided": d["gelem_s"]["sequential_one_sided"], "cores": d["threads"],
+            "cpu": d["cpu"], "kind": "reference", "dtype": "f32",
+            "sample": f"B{B} L{T} C{N} D{D} slice, Cayley + decay + scan, forward + backward (autograd), one timed "
+                      "step after one warm-up, the reference toolkit's torch code"}
 
 
 # =============================================================================== workloads
@@ -520,7 +605,8 @@ def run_sequence_parallel(args, ws, rank, local, cores):
         cores = _cpu_threads(cores)
         E = algebra.triu_basis(D)
         rng = np.random.default_rng(0)
-        Ts, Cs = 8192, 4
+        Ts, Cs = 8192, min(C, max(4, cores))  # one full-length-8192 sequence per host thread
+        cores = min(cores, Cs)
         gs, dts, Ss = (rng.standard_normal((1, Ts, Cs, K)) * 0.02, rng.uniform(0.001, 0.01, (1, Ts)),
                        rng.standard_normal((1, Ts, Cs, D, D)))
         dXs = rng.standard_normal((1, Ts, Cs, D, D))
@@ -542,7 +628,8 @@ def run_sequence_parallel(args, ws, rank, local, cores):
                                   "d2h_bytes_per_step": 0}}), flush=True)
         return 0
     import torch
-    from csn_b200 import _lib
+    from csn_b200 import _lib, ops
+    from csn_b200 import sequence_parallel as spm
     from csn_b200.sequence_parallel import CudaBackend, sp_backward, sp_forward
     if ws > 1:
         import torch.distributed as dist
@@ -558,7 +645,6 @@ def run_sequence_parallel(args, ws, rank, local, cores):
     S = torch.randn(B, Tl, cs, D, D, device=dev, generator=g)
     dX = torch.randn(B, Tl, cs, D, D, device=dev, generator=g)
     be = CudaBackend()
-    launches = [0]
 
     def step():
         for _ in range(nslab):
@@ -589,6 +675,8 @@ def run_sequence_parallel(args, ws, rank, local, cores):
         e1.record()
         torch.cuda.synchronize()
     _lib.timing_enable(False)
+    if ws > 1:
+        spm.check()  # the last exchange's finiteness verdict
     kt = {k: _lib.timing_read(k) for k in SP_KERNELS}
     barrier()
     ms = e0.elapsed_time(e1)
@@ -599,17 +687,108 @@ def run_sequence_parallel(args, ws, rank, local, cores):
     ms_step = ms / steps
     value = elems / (ms_step * 1e-3) / 1e9
     hbm, peak_kind = peaks()
+    # dominant kernel's roofline: algorithmic bytes per element of each pass (undamped:
+    # no gamma), elements of one launch = this rank's slab
+    kbytes = {"agg_fwd_reduce": 4.0 * (K + n + 1.0 / cs), "fwd_reduce": 4.0 * (K + n + 1.0 / cs),
+              "fwd_apply": 4.0 * (K + 2 * n + 1.0 / cs), "agg_bwd_reduce": 4.0 * (n + K + 1.0 / cs),
+              "bwd_reduce": 4.0 * (n + K + 1.0 / cs), "bwd_apply": 4.0 * (3 * n + 2 * K + 1 + 1.0 / cs)}
+    dom = max((k for k in kbytes if kt[k][1]), key=lambda k: kt[k][0])
+    dom_ms = kt[dom][0] / kt[dom][1]
+    dom_ach = kbytes[dom] * (B * Tl * cs) / (dom_ms * 1e-3) / 1e9
+    roofline = {"bound": "hbm", "kernel": dom, "achieved": dom_ach, "peak": hbm, "unit": "GB/s",
+                "frac": dom_ach / hbm, "traffic": None, "peak_kind": peak_kind,
+                "bytes_per_elem": kbytes[dom], "avg_launch_ms": dom_ms}
+    _lib.timing_reset()
+    # end to end through the public ops: every step, every slab's inputs (gens, dt, S, dX)
+    # copied from pinned host memory and its outputs (X, dgens, ddt, dS) copied back.  The
+    # host side is a 1 GiB pinned staging buffer per direction that the copies cycle through
+    # (the bytes moved per step are those of the full tensors).
+    e2e = None
+    if args.e2e_steps > 0:
+        stage_in = torch.randn(1 << 28).pin_memory()
+        stage_out = torch.empty(1 << 28).pin_memory()
+
+        def h2d(t):
+            f = t.view(-1)
+            for o in range(0, f.numel(), stage_in.numel()):
+                m = min(stage_in.numel(), f.numel() - o)
+                f[o:o + m].copy_(stage_in[:m], non_blocking=True)
+            return t.numel() * 4
+
+        def d2h(t):
+            f = t.reshape(-1)
+            for o in range(0, f.numel(), stage_out.numel()):
+                m = min(stage_out.numel(), f.numel() - o)
+                stage_out[:m].copy_(f[o:o + m], non_blocking=True)
+            return t.numel() * 4
+
+        def e2e_step():
+            hb = db = 0
+            for _ in range(nslab):
+                for t in (gens, dt, S, dX):
+                    hb += h2d(t)
+                gd, dd, Sd = (t.detach().requires_grad_(True) for t in (gens, dt, S))
+                if ws > 1:
+                    X = spm.sequence_parallel_rotor_scan(gd, dd, None, Sd)
+                else:
+                    X = ops.fused_rotor_scan(gd, dd, None, Sd)
+                X.backward(dX)
+                for t in (X.detach(), gd.grad, dd.grad, Sd.grad):
+                    db += d2h(t)
+                del X, gd, dd, Sd
+            torch.cuda.current_stream(dev).synchronize()
+            return hb, db
+
+        k_e2e = min(args.e2e_steps, 1)  # one step moves the whole problem over PCIe (~80 GB per GPU)
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(k_e2e):
+            h2d_b, d2h_b = e2e_step()
+        el = time.perf_counter() - t0
+        if ws > 1:
+            spm.check()
+            t = torch.tensor([el], device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            el = t.item()
+        e2e = {"value": elems * k_e2e / el / 1e9, "unit": UNIT, "h2d_bytes_per_step": h2d_b,
+               "d2h_bytes_per_step": d2h_b,
+               "timing": "wall clock around K steps: every slab's inputs pinned host -> device, the "
+                         "sequence-parallel autograd op forward + backward, outputs -> pinned host, one "
+                         "stream synchronize per step, max over ranks"}
+        del stage_in, stage_out
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        from csn_b200 import algebra
+        from oracle import oracle as orc
+        cores = _cpu_threads(cores)
+        E = algebra.triu_basis(D)
+        rng = np.random.default_rng(0)
+        Ts, Cs = 8192, min(C, max(4, cores))
+        cores = min(cores, Cs)
+        a = (rng.standard_normal((1, Ts, Cs, K)) * 0.02, rng.uniform(0.001, 0.01, (1, Ts)),
+             rng.standard_normal((1, Ts, Cs, D, D)))
+        dXs = rng.standard_normal((1, Ts, Cs, D, D))
+
+        def ref_step():
+            Xr = orc.rotor_scan_fwd(a[0], a[1], None, a[2], E)
+            orc.rotor_scan_bwd(a[0], a[1], None, a[2], E, Xr, dXs)
+
+        cel = _time_cpu(ref_step, 2, 0)
+        cpu = {"value": Ts * Cs * 2 / cel / 1e9, "unit": UNIT, "cores": cores, "kind": "port",
+               "sample": f"B1 L{Ts} C{Cs} slice per sample, fwd+bwd, float64 C oracle, OpenMP"}
     if rank == 0:
         ach = op_bytes * elems / ws / (ms_step * 1e-3) / 1e9
         print(json.dumps({"metric": METRIC, "value": value, "unit": UNIT,
                           "n_gpus": ws, "steps": steps, "warmup": max(3, args.warmup),
                           "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
-                          "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
+                          "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                          "config": dict(config, parallelism=f"sequence{ws}"),
+                          "roofline": roofline,
                           "op_roofline": {"achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
                                           "bytes_per_elem": op_bytes, "note": "per rank"},
                           "kernel_ms_per_step": {k: v[0] / steps for k, v in kt.items() if v[1]},
                           "gpu_launches": sum(v[1] for v in kt.values()),
-                          "clocks": clk.summary()}), flush=True)
+                          "clocks": clk.summary(), "e2e": e2e, "cpu_baseline": cpu}), flush=True)
     if ws > 1:
         torch.distributed.destroy_process_group()
     return 0
@@ -995,6 +1174,106 @@ def run_spatial(args, ws, rank, local, cores):
     return 0
 
 
+# ===================================================== the other configurations, same run
+def _device_inputs(wl, dev, seed):
+    """wl's inputs drawn on the device (same distributions as its host inputs)."""
+    import torch
+    g = torch.Generator(device=dev).manual_seed(seed)
+    r = lambda *shape: torch.randn(*shape, device=dev, generator=g)
+    u = lambda *shape: torch.rand(*shape, device=dev, generator=g)
+    B, T, N = wl.B, wl.T, wl.N
+    if isinstance(wl, Cl8):
+        return dict(gens=r(B, T, N, wl.K) * 0.05, dt=u(B, T) * 0.045 + 0.005, S=r(B, T, N, 16, 16),
+                    dX=r(B, T, N, 16, 16))
+    return dict(gens=r(B, T, N, 3) * 0.1, dt=u(B, T) * 0.09 + 0.01, x=r(B, T, N, 8), dh=r(B, T, N, 8))
+
+
+def measure_config(wl, dev, lib, steps=10, warmup=3):
+    """Device-timed value, dominant-kernel and whole-op roofline of workload wl (inputs on the
+    device, no host copies); a summary of the figures the main line gives for its workload."""
+    import torch
+    from csn_b200 import _lib
+    wl.dev = dev
+    if isinstance(wl, Cl8):
+        wl.inp = _device_inputs(wl, dev, 7)
+        wl.out = dict(X=torch.empty_like(wl.inp["S"]), dS=torch.empty_like(wl.inp["S"]),
+                      dgens=torch.empty_like(wl.inp["gens"]), ddt=torch.empty_like(wl.inp["dt"]))
+        wl.Mc = torch.empty_like(wl.inp["S"])
+        wl.ws_bytes = lib.csn_rotor_scan_workspace_bytes(wl.B, wl.T, wl.N, wl.D)
+    else:
+        wl.inp = _device_inputs(wl, dev, 99)
+        wl.out = dict(h=torch.empty_like(wl.inp["x"]), dx=torch.empty_like(wl.inp["x"]),
+                      dgens=torch.empty_like(wl.inp["gens"]), ddt=torch.empty_like(wl.inp["dt"]))
+        wl.ws_bytes = lib.csn_ga3_workspace_bytes(wl.B, wl.T, wl.N)
+    wl.work = torch.empty(wl.ws_bytes, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(warmup):
+        wl.step(stream)
+    torch.cuda.synchronize()
+    _lib.timing_reset()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _lib.timing_enable(True)
+    e0.record(stream)
+    for _ in range(steps):
+        wl.step(stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    _lib.timing_enable(False)
+    ms = e0.elapsed_time(e1) / steps
+    kt = {n: _lib.timing_read(n) for n in wl.kernel_names}
+    _lib.timing_reset()
+    hbm, peak_kind = peaks()
+    dom = max(wl.kernel_bytes, key=lambda n: kt[n][0])
+    dom_ms = kt[dom][0] / max(1, kt[dom][1])
+    per_launch = wl.elems_per_step * steps / max(1, kt[dom][1])
+    ach = wl.kernel_bytes[dom] * per_launch / (dom_ms * 1e-3) / 1e9
+    op = wl.op_bytes * wl.elems_per_step / (ms * 1e-3) / 1e9
+    res = {"metric": METRIC, "value": wl.elems_per_step / (ms * 1e-3) / 1e9, "unit": UNIT,
+           "ms_per_step": ms, "steps": steps, "warmup": warmup, "config": wl.config,
+           "roofline": {"bound": "hbm", "kernel": dom, "achieved": ach, "peak": hbm, "unit": "GB/s",
+                        "frac": ach / hbm, "peak_kind": peak_kind, "avg_launch_ms": dom_ms},
+           "op_roofline": {"achieved": op, "peak": hbm, "unit": "GB/s", "frac": op / hbm,
+                           "bytes_per_elem": wl.op_bytes},
+           "kernel_ms_per_step": {n: t / steps for n, (t, c) in kt.items() if c},
+           "gpu_launches": sum(c for _, c in kt.values())}
+    del wl.inp, wl.out, wl.work
+    if hasattr(wl, "Mc"):
+        del wl.Mc
+    torch.cuda.empty_cache()
+    return res
+
+
+def measure_generation(dev, steps=2048, chunk=128):
+    """p50 latency of one graph-replayed rotor step of the Cl(6,0) generation configuration
+    (256 streams x 8 channels) and tokens/s."""
+    import numpy as np
+    import torch
+    from csn_b200 import ops
+    B, N, D = 256, 8, 8
+    g = ops.RotorStepGraph(B, N, D, steps=chunk, damped=True, device=dev)
+    gen = torch.Generator(device="cpu").manual_seed(0)
+    g.gens.copy_(torch.randn(chunk, B, N, 28, generator=gen) * 0.1)
+    g.dt.copy_(torch.rand(chunk, B, generator=gen) * 0.09 + 0.01)
+    g.gamma.copy_(torch.nn.functional.softplus(torch.randn(chunk, B, N, generator=gen)))
+    g.S.copy_(torch.randn(chunk, B, N, D, D, generator=gen))
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    lat = []
+    for _ in range(steps // chunk):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        g.replay()
+        e1.record()
+        e1.synchronize()
+        lat.append(e0.elapsed_time(e1) * 1e3 / chunk)
+    p50 = float(np.median(lat))
+    return {"metric": "rotor-step p50 latency (us), 256 streams x 8 channels Cl(6,0)", "value": p50,
+            "unit": "us", "tok_per_s": B / (p50 * 1e-6), "steps": steps, "higher_is_better": False,
+            "config": {"workload": "cl6_generation_step", "streams": B, "channels": N, "matrix_dim": D,
+                       "graph_steps": chunk, "damped": True}}
+
+
 # ==================================================================================== main
 def main():
     ap = argparse.ArgumentParser()
@@ -1002,13 +1281,18 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="cl6_lm", choices=sorted(WORKLOADS) + ["gen", "sp", "lm_train", "spatial"])
+    ap.add_argument("--workload", default=None, choices=sorted(WORKLOADS) + ["gen", "sp", "lm_train", "spatial"],
+                    help="default: sp when launched by torch.distributed.run (any world size), else cl6_lm")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-other-configs", action="store_true",
+                    help="cl6_lm at N = 1: skip the Cl(3), Cl(8) and generation figures of the same run")
     ap.add_argument("--batch", type=int, default=None, help="per-rank batch (profiling: smaller)")
     ap.add_argument("--layers", type=int, default=None, help="layers per step (cl6_lm; profiling: 1)")
     args = ap.parse_args()
     ws, rank, local = dist_env()
+    if args.workload is None:
+        args.workload = "sp" if launched_by_torchrun() else "cl6_lm"
     cores = os.cpu_count() or 1
     if args.workload == "gen":
         return run_generation(args, ws, rank, local, cores)
@@ -1037,6 +1321,8 @@ def main():
                 "data": "synthetic", "config": wl.config, "impl": "reference",
                 "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
                 "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        if args.workload == "cl6_lm":  # beside the port: the reference's own fp32 torch code
+            line["cpu_baseline"]["reference_fp32"] = reference_fp32_cpu(cores)
         print(json.dumps(line), flush=True)
         return 0
 
@@ -1121,6 +1407,19 @@ def main():
         cores = _cpu_threads(cores)
         elems, el, sample = wl.cpu_reference(reps=2, warmup=0)
         cpu = {"value": elems / el / 1e9, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+        if args.workload == "cl6_lm":
+            cpu["reference_fp32"] = reference_fp32_cpu(cores)
+
+    # the Cl(3) bandwidth, Cl(8) and generation configurations, measured in the same run
+    # (device-timed, inputs on the device) so that their figures travel with this line
+    others = None
+    if ws == 1 and args.workload == "cl6_lm" and not args.no_other_configs:
+        del wl.inputs, wl.outs, wl.work
+        if hasattr(wl, "pipe"):
+            del wl.pipe, wl.host, wl.hout
+        torch.cuda.empty_cache()
+        others = {"cl3": measure_config(Cl3(), dev, lib), "cl8": measure_config(Cl8(), dev, lib),
+                  "gen": measure_generation(dev)}
 
     if rank == 0:
         op_ach = wl.op_bytes * wl.elems_per_step / (ms_per_step * 1e-3) / 1e9
@@ -1138,6 +1437,8 @@ def main():
                                 "bytes_per_elem": wl.op_bytes},
                 "kernel_ms": {n: {"total_ms": t, "launches": c} for n, (t, c) in ktimes.items()},
                 "gpu_launches": launches, "clocks": clk.summary(), "e2e": e2e, "cpu_baseline": cpu}
+        if others is not None:
+            line["other_configs"] = others
         print(json.dumps(line), flush=True)
     if ws > 1:
         torch.distributed.destroy_process_group()

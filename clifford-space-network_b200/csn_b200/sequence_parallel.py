@@ -15,13 +15,19 @@ backward (mirror image in reverse time)
   3. H_g = reverse scan of (P_r^T, c'_r), r > g           (gradient entering from the right)
   4. resume the local adjoint with h0 = h_g and H_g entering after the last step
 
-The cross-shard compositions run on the same CUDA kernels as everything else.  Before
-each exchange the ranks all-gather a small header (shapes, flags) so that a rank with a
-mismatched shard is reported on every rank instead of deadlocking the collective, and
-the gathered carries are checked for non-finite values on every rank alike.
+The cross-shard compositions run on the same CUDA kernels as everything else.
 
-Per direction the ranks make two collectives and two host synchronisations: the header check
-and one stacked all-gather of the summaries with one finiteness check.
+Per direction the ranks make ONE collective and no host synchronisation: the shard
+summaries are packed into one buffer together with a finiteness flag of this rank's
+summaries, and all-gathered.  The gathered flags are reduced on the device and copied to
+pinned host memory asynchronously; the next sequence-parallel call (or ``check()``) reads
+that copy, long finished by then, and raises ``ShardMismatchError`` on every rank alike when
+a carry was not finite.  The layout (shapes, flags) is validated once: the first call with a
+given layout all-gathers a small header first, with a host check, so that a rank with a
+mismatched shard is reported on every rank instead of deadlocking the collective; later
+calls with a layout that every rank has validated skip it (ranks that keep calling with
+the same shapes make the same decision).  A rank that changes its shapes alone after that
+first call runs into the process group's timeout instead.
 
 The kernel calls go through a backend object (``CudaBackend`` here); tests substitute a
 CPU backend to exercise the exchange logic with the gloo backend.
@@ -127,19 +133,85 @@ def _check_header(local: torch.Tensor, group, what: str):
         raise ShardMismatchError(f"{what}: rank {r} shard header {hdr[r].tolist()} != rank 0 {hdr[0].tolist()}")
 
 
-def _gather_checked(parts, group, what: str):
-    """All-gather the shard summaries of every rank in ONE collective (stacked), check them
-    for non-finite values with ONE host synchronisation (the same result on every rank), and
-    return one [ws, ...] tensor per part."""
+# layouts every rank of a group has validated: (group key, direction, header) -> True
+_VALIDATED: dict = {}
+
+
+def _group_key(group):
+    return "default" if group is None else id(group)
+
+
+def _validate_layout_once(header: tuple, group, direction: str, device, what: str):
+    """The header exchange of `_check_header`, made only the first time this rank uses this
+    layout on this group."""
+    key = (_group_key(group), direction, header)
+    if key in _VALIDATED:
+        return
+    _check_header(torch.tensor(header, dtype=torch.int64, device=device), group, what)
+    _VALIDATED[key] = True
+
+
+class _PendingCheck:
+    """Finiteness of the last exchange: a device flag copied asynchronously to pinned host
+    memory, read at the next call or by check()."""
+
+    def __init__(self):
+        self.item = None  # (host tensor [2], event or None, what)
+
+    def set(self, bad_any, first_bad, what):
+        flags = torch.stack([bad_any.to(torch.int64), first_bad.to(torch.int64)])
+        if flags.is_cuda:
+            host = torch.empty(2, dtype=torch.int64, pin_memory=True)
+            host.copy_(flags, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream(flags.device))
+        else:
+            host, ev = flags.clone(), None
+        self.item = (host, ev, what)
+
+    def raise_if_bad(self):
+        if self.item is None:
+            return
+        host, ev, what = self.item
+        self.item = None
+        if ev is not None:
+            ev.synchronize()  # recorded one exchange ago: normally long complete
+        if int(host[0]):
+            raise ShardMismatchError(f"{what}: carry from rank {int(host[1])} is not finite")
+
+
+_PENDING = _PendingCheck()
+
+
+def check() -> None:
+    """Raise ShardMismatchError if the last exchange gathered a non-finite carry (every rank
+    reaches the same verdict).  Calls of sp_forward / sp_backward do this themselves for the
+    exchange before them."""
+    _PENDING.raise_if_bad()
+
+
+def _gather_packed(parts, group, what: str):
+    """All-gather the shard summaries of every rank and this rank's finiteness flag in ONE
+    collective (one packed buffer), with no host synchronisation; returns one [ws, ...]
+    tensor per part.  The verdict on finiteness is left in _PENDING."""
     ws, _ = _world(group)
-    local = torch.stack([p.contiguous() for p in parts])  # [n_parts, ...]
-    out = local.new_empty((ws * local.shape[0],) + tuple(local.shape[1:]))
+    shapes = [tuple(p.shape) for p in parts]
+    flat = [p.reshape(-1) for p in parts]
+    ok = torch.stack([torch.isfinite(f).all() for f in flat]).all().to(flat[0].dtype).reshape(1)
+    local = torch.cat(flat + [ok])
+    out = local.new_empty((ws * local.numel(),))
     dist.all_gather_into_tensor(out, local, group=group)  # rank-major concatenation
-    out = out.view((ws,) + tuple(local.shape))
-    if not bool(torch.isfinite(out).all()):
-        r = int((~torch.isfinite(out.flatten(1))).any(dim=1).nonzero()[0])
-        raise ShardMismatchError(f"{what}: carry from rank {r} is not finite")
-    return [out[:, i] for i in range(len(parts))]
+    out = out.view(ws, -1)
+    bad = out[:, -1] == 0
+    _PENDING.set(bad.any(), torch.argmax(bad.to(torch.int32)), what)
+    res, o = [], 0
+    for shp in shapes:
+        n = 1
+        for d in shp:
+            n *= d
+        res.append(out[:, o:o + n].reshape((ws,) + shp))
+        o += n
+    return res
 
 
 def sp_forward(gens, dt, gamma, S, group=None, backend=None, basis="triu", two_sided=True):
@@ -148,14 +220,14 @@ def sp_forward(gens, dt, gamma, S, group=None, backend=None, basis="triu", two_s
     Returns (X_local, h_in, Ps): the shard trajectory, the carry-in (None on rank 0) and the
     gathered shard products (kept for the backward pass)."""
     backend = backend or CudaBackend()
+    _PENDING.raise_if_bad()
     ws, g = _world(group)
     B, T, N, D, _ = S.shape
     dev = S.device
     flags = int(gamma is not None) * 1 + int(two_sided) * 2 + (BASIS[basis] << 2)
-    _check_header(torch.tensor([B, T, N, D, gens.shape[-1], flags], dtype=torch.int64, device=dev),
-                  group, "sequence-parallel forward")
+    _validate_layout_once((B, T, N, D, gens.shape[-1], flags), group, "fwd", dev, "sequence-parallel forward")
     P, c, ws_fwd = backend.fwd_aggregate(gens, dt, gamma, S, basis, two_sided)
-    Pall, call = _gather_checked([P, c], group, "sequence-parallel forward")  # [ws, B, N, D, D]
+    Pall, call = _gather_packed([P, c], group, "sequence-parallel forward")  # [ws, B, N, D, D]
     Ps = list(Pall.unbind(0))
     h_in = None
     if g > 0:
@@ -170,12 +242,13 @@ def sp_backward(gens, dt, gamma, S, X, dX, h_in, Ps, group=None, backend=None, b
                 two_sided=True):
     """Backward of the sequence-parallel scan: (dgens, ddt, dgamma, dS) of this shard."""
     backend = backend or CudaBackend()
+    _PENDING.raise_if_bad()
     ws, g = _world(group)
     B, T, N, D, _ = S.shape
-    _check_header(torch.tensor([B, T, N, D, int(dX.shape == S.shape)], dtype=torch.int64,
-                               device=S.device), group, "sequence-parallel backward")
+    _validate_layout_once((B, T, N, D, int(dX.shape == S.shape)), group, "bwd", S.device,
+                          "sequence-parallel backward")
     cb, ws_bwd = backend.bwd_aggregate(gens, dt, gamma, dX, basis, two_sided)
-    (cball,) = _gather_checked([cb], group, "sequence-parallel backward")
+    (cball,) = _gather_packed([cb], group, "sequence-parallel backward")
     cbs = list(cball.unbind(0))
     H = None
     if g < ws - 1:

@@ -165,18 +165,19 @@ from csn import rotors as rr, scan as rs
 threads = int(sys.argv[2])
 torch.set_num_threads(threads)
 B, T, N, D = map(int, sys.argv[3:7])
+dev = torch.device(sys.argv[7])
 K = D * (D - 1) // 2
 g = torch.Generator().manual_seed(0)
-gens = torch.randn(B, T, N, K, generator=g)
-dt = torch.rand(B, T, generator=g) * 0.02 + 0.04
-gamma = torch.nn.functional.softplus(torch.randn(B, T, N, generator=g) * 0.5)
-S = torch.randn(B, T, N, D, D, generator=g)
-dX = torch.randn(B, T, N, D, D, generator=g)
-iu = torch.triu_indices(D, D, 1)
+gens = torch.randn(B, T, N, K, generator=g).to(dev)
+dt = (torch.rand(B, T, generator=g) * 0.02 + 0.04).to(dev)
+gamma = torch.nn.functional.softplus(torch.randn(B, T, N, generator=g) * 0.5).to(dev)
+S = torch.randn(B, T, N, D, D, generator=g).to(dev)
+dX = torch.randn(B, T, N, D, D, generator=g).to(dev)
+iu = torch.triu_indices(D, D, 1).to(dev)
 
 def step(scan):
     gg, dd, ga, SS = (t.clone().requires_grad_(True) for t in (gens, dt, gamma, S))
-    skew = torch.zeros(B, T, N, D, D)
+    skew = torch.zeros(B, T, N, D, D, device=dev)
     skew[..., iu[0], iu[1]] = gg
     skew[..., iu[1], iu[0]] = -gg
     h = (0.5 * dd)[:, :, None, None, None]
@@ -185,13 +186,18 @@ def step(scan):
     X = scan(torch.sqrt(a) * Q, (1 - a) * SS)
     X.backward(dX)
 
+def clock():
+    if dev.type == "cuda":
+        torch.cuda.synchronize(dev)
+    return time.perf_counter()
+
 out = {}
 for name, scan in (("tree_two_sided", lambda M, C: rs._parallel_tree_scan(M, C, is_spinor_bundle=False)),
                    ("sequential_one_sided", lambda M, C: rs.CliffordScanFunction.apply(M, C))):
     step(scan)  # warm-up
-    t0 = time.perf_counter()
+    t0 = clock()
     step(scan)
-    out[name] = B * T * N / (time.perf_counter() - t0) / 1e9
+    out[name] = B * T * N / (clock() - t0) / 1e9
 model = ""
 try:
     for line in open("/proc/cpuinfo"):
@@ -204,11 +210,12 @@ print(json.dumps({"gelem_s": out, "threads": threads, "cpu": model}))
 """
 
 
-def reference_fp32_cpu(cores, B=4, T=2048, N=8, D=8, timeout=600):
-    """The reference toolkit's own CPU scan path (baseline/_ref: csn.rotors.cayley_rotor_8x8 with
+def reference_fp32_cpu(cores, B=4, T=2048, N=8, D=8, timeout=600, device="cpu"):
+    """The reference toolkit's own scan path (baseline/_ref: csn.rotors.cayley_rotor_8x8 with
     use_schulz=False, decay, then csn.scan's two-sided tree _parallel_tree_scan and the one-sided
-    sequential CliffordScanFunction), fp32, forward + backward by autograd, on a slice of the
-    Cl(6) LM configuration with all host threads.  None-free: on any failure the reason."""
+    sequential CliffordScanFunction), fp32, forward + backward by autograd, on the Cl(6) LM
+    configuration (a slice of it on the host) with all host threads, or on `device` (its torch
+    code on the GPU).  On any failure: the reason."""
     import subprocess
     ref = REPO / "baseline" / "_ref"
     if not (ref / "csn" / "scan.py").exists():
@@ -216,17 +223,19 @@ def reference_fp32_cpu(cores, B=4, T=2048, N=8, D=8, timeout=600):
     env = dict(os.environ, PYTHONDONTWRITEBYTECODE="1", OMP_NUM_THREADS=str(cores), PYTHONPATH=str(ref))
     try:
         r = subprocess.run([sys.executable, "-c", _REF_CPU_SCRIPT, str(ref), str(cores), str(B), str(T), str(N),
-                            str(D)], capture_output=True, text=True, timeout=timeout, cwd=str(ref), env=env)
+                            str(D), device], capture_output=True, text=True, timeout=timeout, cwd=str(ref), env=env)
         if r.returncode != 0:
             return {"unavailable": (r.stderr.strip().splitlines() or ["failed"])[-1][:200]}
         d = json.loads(r.stdout.strip().splitlines()[-1])
     except Exception as e:  # noqa: BLE001 -- a baseline that cannot run must not fail the bench
         return {"unavailable": repr(e)[:200]}
-    return {"unit": UNIT, "value_tree_two_sided": d["gelem_s"]["tree_two_sided"],
-            "value_sequential_one_sided": d["gelem_s"]["sequential_one_sided"], "cores": d["threads"],
-            "cpu": d["cpu"], "kind": "reference", "dtype": "f32",
-            "sample": f"B{B} L{T} C{N} D{D} slice, Cayley + decay + scan, forward + backward (autograd), one timed "
-                      "step after one warm-up, the reference toolkit's torch code"}
+    res = {"unit": UNIT, "value_tree_two_sided": d["gelem_s"]["tree_two_sided"],
+           "value_sequential_one_sided": d["gelem_s"]["sequential_one_sided"], "kind": "reference", "dtype": "f32",
+           "sample": f"B{B} L{T} C{N} D{D}, Cayley + decay + scan, forward + backward (autograd), one timed "
+                     f"step after one warm-up, the reference toolkit's torch code on {device}"}
+    if device == "cpu":
+        res.update(cores=d["threads"], cpu=d["cpu"])
+    return res
 
 
 # =============================================================================== workloads
@@ -975,6 +984,23 @@ def run_lm_train(args, ws, rank, local, cores):
         e1.record()
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
+    # The GEMM that materialises S ([B*T, d_model] x [d_model, N*64]) once per block, timed alone:
+    # building S inside the scan instead would redo this work in each of the three scan passes
+    # that read S (forward reduce, forward apply, backward apply), to save S's HBM round trips.
+    from csn_b200 import ops as _ops
+    blk = model.blocks[0]
+    xs = torch.randn(B * T, blk.d_model, device=dev)
+    for _ in range(3):
+        _ops.linear(xs, blk.in_proj.weight, blk.in_proj.bias)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(10):
+        _ops.linear(xs, blk.in_proj.weight, blk.in_proj.bias)
+    e1.record()
+    torch.cuda.synchronize()
+    in_proj_ms = e0.elapsed_time(e1) / 10
+    s_bytes = B * T * blk.num_neurons * 64 * 4
+    del xs
     names = ("fwd_reduce", "fwd_carry", "fwd_apply", "bwd_reduce", "bwd_carry", "bwd_apply", "reduce_channels",
              "spike_fwd", "spike_bwd", "layer_norm_fwd", "layer_norm_bwd", "layer_norm_param_reduce",
              "ln_conv_silu_fwd", "ln_conv_silu_bwd", "ln_conv_silu_param_reduce", "generator_action_fwd",
@@ -999,6 +1025,8 @@ def run_lm_train(args, ws, rank, local, cores):
         "eager_ms_per_step": eager_ms, "step": "CUDA graph of forward + backward + AdamW (capturable)",
         "scan_ms_per_step": sum(kt[n][0] for n in names[:7]) / args.steps,
         "kernel_ms": {n: {"total_ms": t, "launches": c} for n, (t, c) in kt.items()},
+        "s_materialisation": {"in_proj_gemm_ms": in_proj_ms, "s_bytes_per_block": s_bytes,
+                              "s_round_trips_per_block": "1 write (the GEMM) + 3 reads (scan passes)"},
         "gpu_launches": launches, "clocks": clk.summary(),
         "e2e": {"value": B * T / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": 2 * B * T * 8,
                 "d2h_bytes_per_step": 6 * 4, "timing": "wall clock per step: token ids pinned host -> device, "
@@ -1409,6 +1437,10 @@ def main():
         cpu = {"value": elems / el / 1e9, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
         if args.workload == "cl6_lm":
             cpu["reference_fp32"] = reference_fp32_cpu(cores)
+    ref_gpu = None
+    if rank == 0 and ws == 1 and args.workload == "cl6_lm" and not args.no_cpu_baseline:
+        # the reference toolkit's torch code on this GPU, at this workload's shape (one layer)
+        ref_gpu = reference_fp32_cpu(cores, B=wl.B, T=wl.T, N=wl.N, D=wl.D, device=f"cuda:{local}")
 
     # the Cl(3) bandwidth, Cl(8) and generation configurations, measured in the same run
     # (device-timed, inputs on the device) so that their figures travel with this line
@@ -1439,6 +1471,8 @@ def main():
                 "gpu_launches": launches, "clocks": clk.summary(), "e2e": e2e, "cpu_baseline": cpu}
         if others is not None:
             line["other_configs"] = others
+        if ref_gpu is not None:
+            line["reference_fp32_gpu"] = ref_gpu
         print(json.dumps(line), flush=True)
     if ws > 1:
         torch.distributed.destroy_process_group()

@@ -55,8 +55,6 @@ SIGNATURES = {
     "csn_rotor_scan_bwd_resume": ([_f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _i64, _i64,
                                    _i64, _int, _int, _int, _f, _sz, _f], _int),
     "csn_rotor_step": ([_f, _f, _f, _f, _f, _i64, _i64, _int, _int, _int, _f], _int),
-    "csn_device_status": ([ctypes.POINTER(ctypes.c_uint), _int, _f], _int),
-    "csn_selftest_bounded_wait": ([_int, _f], _int),
     "csn_cayley_fwd": ([_f, _f, _i64, _int, _f], _int),
     "csn_cayley_bwd": ([_f, _f, _f, _i64, _int, _f], _int),
     "csn_ga3_workspace_bytes": ([_i64, _i64, _i64], _sz),
@@ -156,14 +154,6 @@ def timing_read(name: str | None = None):
     cnt = ctypes.c_int64(0)
     call("csn_timing_read", name.encode() if name else None, ctypes.byref(tot), ctypes.byref(cnt))
     return tot.value, cnt.value
-
-
-def device_status(reset: bool = True, stream=None) -> int:
-    """Bits of bounded device-side waits that gave up (CSN_STATUS_WAIT_TIMEOUT = 1); 0 = none.
-    Synchronises the stream."""
-    v = ctypes.c_uint(0)
-    call("csn_device_status", ctypes.byref(v), int(reset), stream)
-    return v.value
 
 
 def version() -> str:

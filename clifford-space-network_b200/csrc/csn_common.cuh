@@ -251,52 +251,6 @@ __device__ __forceinline__ void cp_async_floats(float* smem, const float* gmem) 
   for (int v = 0; v < NF / 4; ++v) cp_async16(smem + 4 * v, gmem + 4 * v);
 }
 
-// ------------------------------------------------------------ bulk (TMA) staging
-// One-dimensional bulk copies global -> this CTA's shared memory, completed on an mbarrier
-// (the copy engine moves a whole row; the issuing lane spends one instruction on it).  Only
-// this GPU's own memory is read and no multicast form is used.
-__device__ __forceinline__ unsigned smem_u32(const void* p) {
-  return static_cast<unsigned>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-// make the initialised barriers visible to the copy engine
-__device__ __forceinline__ void mbar_init_fence() {
-  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-}
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, unsigned bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
-  unsigned ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait for the phase of `parity`: false after `limit` polls (each poll may suspend
-// the thread for a hardware-chosen interval first).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, int limit) {
-  for (int i = 0; i < limit; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
-  return false;
-}
-// order this thread's earlier generic shared-memory accesses before later bulk copies into them
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-}
-// bytes % 16 == 0, both addresses 16-byte aligned
-__device__ __forceinline__ void bulk_g2s(void* smem, const void* gmem, unsigned bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
-                   smem_u32(smem)),
-               "l"(gmem), "r"(bytes), "r"(smem_u32(bar))
-               : "memory");
-}
-
 // Generator layouts accepted by the fused rotor kernels.
 enum Basis : int {
   BASIS_TRIU = 0,  // reference layout: g_k at torch.triu_indices(D, D, 1)[:, k]

@@ -298,8 +298,6 @@ int scan16_dispatch(const ScanArgs& a, int src, int basis, bool damped, bool two
 int scan8_rotor_dispatch(const ScanArgs& a, bool damped, bool two, bool bwd, cudaStream_t st);
 int scan8_rotor_step(const float* gens, const float* dt, const float* gamma, const float* S, float* h,
                      int64_t B, int64_t N, bool two, cudaStream_t st);
-int device_status8(unsigned* flags, int reset, cudaStream_t st);
-int selftest_wait8(int polls, cudaStream_t st);
 
 namespace {
 
@@ -808,20 +806,6 @@ extern "C" int csn_rotor_scan_fwd_noalloc(const float* gens, const float* dt, co
   bind_ws(a, p, scratch, D);
   if (D == 16) return scan16_dispatch(a, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, false, st);
   return dispatch(a, D, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, false, st);
-}
-
-// ================================================================ device status
-// Bounded device-side waits that gave up since the last read (CSN_STATUS_* bits); reading
-// synchronises `stream`.
-extern "C" int csn_device_status(unsigned* flags, int reset, void* stream) {
-  if (!flags) return set_error(CSN_ERR_INVALID, "csn_device_status: flags is required");
-  return device_status8(flags, reset, static_cast<cudaStream_t>(stream));
-}
-
-// A bounded wait that must give up (see csn_b200.h); for tests of the status path.
-extern "C" int csn_selftest_bounded_wait(int polls, void* stream) {
-  if (polls < 1 || polls > (1 << 20)) return set_error(CSN_ERR_INVALID, "csn_selftest_bounded_wait: 1 <= polls <= 2^20");
-  return selftest_wait8(polls, static_cast<cudaStream_t>(stream));
 }
 
 // ================================================================ O(1) state step

@@ -25,9 +25,10 @@
 //    recurrence and run as 3xTF32: each fp32 operand is split into a TF32 head and a
 //    TF32 tail and hi*hi + hi*lo + lo*hi is accumulated in fp32 (fp32-level error, no
 //    accumulation over time).  Transposes are products with the identity (exact).
-// The Cayley inverse (I - Omega)^{-1} is a Gauss-Jordan elimination on the fragment in
-// fp32 (round-to-nearest FMAs), whose pivot rows and columns reach the lanes that need
-// them by shuffles; the step stays in registers.
+// The Cayley rotor is built from E = (I - Omega)^{-1} - I: a matrix series of small
+// products when |h Omega|_F <= 0.05, else a Gauss-Jordan elimination on the fragment in
+// deviation form (round-to-nearest FMAs), whose pivot rows and columns reach the lanes that
+// need them by shuffles; the step stays in registers.
 #include <stdint.h>
 
 #include "csn_common.cuh"
@@ -365,18 +366,62 @@ __device__ __forceinline__ void build_Om(F16& Om, const float* gs, const uint32_
     }
 }
 
-// M = sa (2 (I - Om)^{-1} - I) = sa (I + 2 E), E = (I - Om)^{-1} - I, in place on Om, by
-// Gauss-Jordan elimination in fp32 in deviation form (round-to-nearest FMAs on entries that
-// stay small).  A matrix series for the inverse in tf32 MMAs would be cheaper, but it rounds
-// the entries near 1 of (I - Om)^{-1} itself, with the MMA's truncating accumulation on top,
-// which leaves every rotor short of orthogonal in the same direction; an undamped scan
-// compounds that over the whole sequence.
+// |Om|_F^2 at or below this takes the series (|Om|_2 <= |Om|_F <= 0.05).
+constexpr float kSeriesFro2 = 0.0025f;
+
+// M = sa (2 (I - Om)^{-1} - I) = sa (I + 2 E) with E = (I - Om)^{-1} - I, in place on Om.
+// Both ways keep E small until M is formed, so no entry near 1 of (I - Om)^{-1} is rounded
+// on its own (that rounding leaves every rotor short of orthogonal in the same direction,
+// which an undamped scan compounds over the whole sequence):
+//  * |Om|_F <= 0.05: E = Om (I - Om)^{-1} = A + A P' with A = Om + W, W = Om^2 (symmetric),
+//    P' = W + W^2 + W W^2 -- the series of (I - W)^{-1} to W^3 (truncation eps^8 / (1 - eps^2)
+//    <= 4e-11) -- four NT products (tf32 MMAs) of matrices of size eps^2 or less, so their
+//    truncating accumulation is far below fp32 rounding of E;
+//  * larger Om: Gauss-Jordan elimination in deviation form (round-to-nearest FMAs).
+// The choice is uniform across the warp (one matrix per warp).
 __device__ __forceinline__ void cayley(F16& M, float sa, int lane) {
+  const float fro2 = warp_sum(f_dot(M, M));
+  if (fro2 <= kSeriesFro2) {
+    F16S Os;
+    split(Os, M);
+    F16 W;
+    nt(W, Os, Os);  // Om Om^T = -Om^2
 #pragma unroll
-  for (int n2 = 0; n2 < 2; ++n2)
+    for (int n2 = 0; n2 < 2; ++n2)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) M.v[n2][e] = -M.v[n2][e];  // E = (I - Om) - I
-  gj_inverse_dev(M, lane);
+      for (int e = 0; e < 4; ++e) W.v[n2][e] = -W.v[n2][e];
+    F16S Ws;
+    split(Ws, W);
+    F16 W2;
+    nt(W2, Ws, Ws);  // W W^T = W^2
+    F16S W2s;
+    split(W2s, W2);
+    F16 W3;
+    nt(W3, Ws, W2s);  // W (W^2)^T = W^3
+    F16 A, Pp;
+#pragma unroll
+    for (int n2 = 0; n2 < 2; ++n2)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        A.v[n2][e] = M.v[n2][e] + W.v[n2][e];
+        Pp.v[n2][e] = (W.v[n2][e] + W2.v[n2][e]) + W3.v[n2][e];
+      }
+    F16S As, Ps;
+    split(As, A);
+    split(Ps, Pp);
+    F16 AP;
+    nt(AP, As, Ps);  // A P'^T = A P' (P' symmetric)
+#pragma unroll
+    for (int n2 = 0; n2 < 2; ++n2)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) M.v[n2][e] = A.v[n2][e] + AP.v[n2][e];
+  } else {
+#pragma unroll
+    for (int n2 = 0; n2 < 2; ++n2)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) M.v[n2][e] = -M.v[n2][e];  // E = (I - Om) - I
+    gj_inverse_dev(M, lane);
+  }
 #pragma unroll
   for (int n2 = 0; n2 < 2; ++n2)
 #pragma unroll
@@ -448,7 +493,9 @@ __device__ __forceinline__ void stage_gens(float* gs, const float (&gr)[(K + 31)
 }
 
 // The step matrix M (Cayley rotor or a given M) of element e at time t.
-template <int SRC, int BASIS, bool DAMPED, int K>
+// CIN: the rotors come from the cache a.Mc_in (a compile-time choice, so the kernels that
+// load them carry none of the registers of the rotor build).
+template <int SRC, int BASIS, bool DAMPED, int K, bool CIN>
 __device__ __forceinline__ void step_matrix(const ScanArgs& a, const Warp& w, const uint32_t (&terms)[2][4],
                                             int64_t e, int64_t t, F16& M, float& alpha, float& sa,
                                             float& dtv, float& gam) {
@@ -466,7 +513,7 @@ __device__ __forceinline__ void step_matrix(const ScanArgs& a, const Warp& w, co
       gam = 0.0f;
       alpha = sa = 1.0f;
     }
-    if (a.Mc_in) {
+    if constexpr (CIN) {
       f_load(M, a.Mc_in + e * DD, w.lane);  // cached rotor of this step
     } else {
       build_Om<NTerms<BASIS>::value>(M, w.gs, terms, 0.5f * dtv);
@@ -479,7 +526,7 @@ __device__ __forceinline__ void step_matrix(const ScanArgs& a, const Warp& w, co
 // ---------------------------------------------------------------------- forward
 // REDUCE: chunk aggregate (P = M_last ... M_first, c = chunk scanned from zero);
 // otherwise the apply pass from the chunk's carry.
-template <bool REDUCE, int SRC, int BASIS, bool DAMPED, bool TWO>
+template <bool REDUCE, int SRC, int BASIS, bool DAMPED, bool TWO, bool CIN>
 __global__ void __launch_bounds__(128) fwd16_kernel(ScanArgs a) {
   constexpr int K = GenCount<16, BASIS>::K;
   constexpr int KR = (K + 31) / 32;
@@ -512,7 +559,7 @@ __global__ void __launch_bounds__(128) fwd16_kernel(ScanArgs a) {
     }
     F16 M;
     float alpha, sa, dtv, gam;
-    step_matrix<SRC, BASIS, DAMPED, K>(a, w, terms, e, t, M, alpha, sa, dtv, gam);
+    step_matrix<SRC, BASIS, DAMPED, K, CIN>(a, w, terms, e, t, M, alpha, sa, dtv, gam);
     const float cs = (SRC == SRC_ROTOR && DAMPED) ? (1.0f - alpha) : 1.0f;
     const F16D Md = to_d(M);
     F16D V;
@@ -538,7 +585,7 @@ __global__ void __launch_bounds__(128) fwd16_kernel(ScanArgs a) {
 // ------------------------------------------------------------- backward: reduce
 // c' = gradient leaving the chunk at its first step with zero gradient from the right,
 // P = M_last ... M_first (built as P <- P M walking backwards).
-template <int SRC, int BASIS, bool DAMPED, bool TWO>
+template <int SRC, int BASIS, bool DAMPED, bool TWO, bool CIN>
 __global__ void __launch_bounds__(128, 4) bwd16_reduce_kernel(ScanArgs a) {
   constexpr int K = GenCount<16, BASIS>::K;
   constexpr int KR = (K + 31) / 32;
@@ -560,7 +607,7 @@ __global__ void __launch_bounds__(128, 4) bwd16_reduce_kernel(ScanArgs a) {
     }
     F16 M;
     float alpha, sa, dtv, gam;
-    step_matrix<SRC, BASIS, DAMPED, K>(a, w, terms, e, t, M, alpha, sa, dtv, gam);
+    step_matrix<SRC, BASIS, DAMPED, K, CIN>(a, w, terms, e, t, M, alpha, sa, dtv, gam);
     F16 Mt;
     // M in memory (a given M, or the cached rotor): read it transposed instead of a product
     const float* mem_m = (SRC == SRC_MC) ? a.M : a.Mc_in;
@@ -592,7 +639,7 @@ __global__ void __launch_bounds__(128, 4) bwd16_reduce_kernel(ScanArgs a) {
 //   rotor: da = -<G, S> + <dM, M> / (2 a);  dOmega = 0.5 sa B dM B with B = I + M^T / sa;
 //          dg_k = <dOmega, E_k> dt / 2
 //   H <- M^T G M  (one-sided: M^T G)
-template <int SRC, int BASIS, bool DAMPED, bool TWO>
+template <int SRC, int BASIS, bool DAMPED, bool TWO, bool CIN>
 __global__ void __launch_bounds__(128, 3) bwd16_apply_kernel(ScanArgs a) {
   constexpr int K = GenCount<16, BASIS>::K;
   constexpr int KR = (K + 31) / 32;
@@ -635,7 +682,7 @@ __global__ void __launch_bounds__(128, 3) bwd16_apply_kernel(ScanArgs a) {
     }
     F16 M;
     float alpha, sa, dtv, gam;
-    step_matrix<SRC, BASIS, DAMPED, K>(a, w, terms, e, t, M, alpha, sa, dtv, gam);
+    step_matrix<SRC, BASIS, DAMPED, K, CIN>(a, w, terms, e, t, M, alpha, sa, dtv, gam);
     F16S Ms, Mts;
     split(Ms, M);
     F16 Mt;
@@ -767,6 +814,38 @@ __global__ void __launch_bounds__(128, 3) bwd16_apply_kernel(ScanArgs a) {
 
 unsigned nblk(int64_t warps) { return (unsigned)((warps + WARPS - 1) / WARPS); }
 
+// Launch a pass in its rotor-cache-loading form when a.Mc_in is set (rotor sources only).
+template <bool REDUCE, int SRC, int BASIS, bool DAMPED, bool TWO>
+void launch_fwd16(const ScanArgs& a, unsigned grid, cudaStream_t st) {
+  if constexpr (SRC == SRC_ROTOR) {
+    if (a.Mc_in) {
+      fwd16_kernel<REDUCE, SRC, BASIS, DAMPED, TWO, true><<<grid, 128, 0, st>>>(a);
+      return;
+    }
+  }
+  fwd16_kernel<REDUCE, SRC, BASIS, DAMPED, TWO, false><<<grid, 128, 0, st>>>(a);
+}
+template <int SRC, int BASIS, bool DAMPED, bool TWO>
+void launch_bwd16_reduce(const ScanArgs& a, unsigned grid, cudaStream_t st) {
+  if constexpr (SRC == SRC_ROTOR) {
+    if (a.Mc_in) {
+      bwd16_reduce_kernel<SRC, BASIS, DAMPED, TWO, true><<<grid, 128, 0, st>>>(a);
+      return;
+    }
+  }
+  bwd16_reduce_kernel<SRC, BASIS, DAMPED, TWO, false><<<grid, 128, 0, st>>>(a);
+}
+template <int SRC, int BASIS, bool DAMPED, bool TWO>
+void launch_bwd16_apply(const ScanArgs& a, unsigned grid, cudaStream_t st) {
+  if constexpr (SRC == SRC_ROTOR) {
+    if (a.Mc_in) {
+      bwd16_apply_kernel<SRC, BASIS, DAMPED, TWO, true><<<grid, 128, 0, st>>>(a);
+      return;
+    }
+  }
+  bwd16_apply_kernel<SRC, BASIS, DAMPED, TWO, false><<<grid, 128, 0, st>>>(a);
+}
+
 template <int SRC, int BASIS, bool DAMPED, bool TWO>
 int run16(const ScanArgs& a, bool bwd, cudaStream_t st) {
   const int64_t S = a.B * a.N;
@@ -776,14 +855,14 @@ int run16(const ScanArgs& a, bool bwd, cudaStream_t st) {
     if (!bwd) {
       {
         KernelTimer kt("agg_fwd_reduce", st);
-        fwd16_kernel<true, SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(a);
+        launch_fwd16<true, SRC, BASIS, DAMPED, TWO>(a, nblk(total), st);
       }
       KernelTimer kt("agg_compose", st);
       compose_kernel<16, TWO, false><<<nblk(S), 128, 0, st>>>(a);
     } else {
       {
         KernelTimer kt("agg_bwd_reduce", st);
-        bwd16_reduce_kernel<SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(a);
+        launch_bwd16_reduce<SRC, BASIS, DAMPED, TWO>(a, nblk(total), st);
       }
       KernelTimer kt("agg_compose", st);
       compose_kernel<16, TWO, true><<<nblk(S), 128, 0, st>>>(a);
@@ -796,7 +875,7 @@ int run16(const ScanArgs& a, bool bwd, cudaStream_t st) {
     if (a.nchunks > 1) {
       if (a.agg_mode != 2) {
         KernelTimer kt("fwd_reduce", st);
-        fwd16_kernel<true, SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(a);
+        launch_fwd16<true, SRC, BASIS, DAMPED, TWO>(a, nblk(total), st);
         if (a.Mc_out) {
           ap.Mc_in = a.Mc_out;
           ap.Mc_out = nullptr;
@@ -806,20 +885,20 @@ int run16(const ScanArgs& a, bool bwd, cudaStream_t st) {
       launch_grouped_carry<16, TWO, false>(a, st);
     }
     KernelTimer kt("fwd_apply", st);
-    fwd16_kernel<false, SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(ap);
+    launch_fwd16<false, SRC, BASIS, DAMPED, TWO>(ap, nblk(total), st);
     return check_launch("scan forward (D=16)");
   }
   if (total > 0) {
     if (a.nchunks > 1) {
       if (a.agg_mode != 2) {
         KernelTimer kt("bwd_reduce", st);
-        bwd16_reduce_kernel<SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(a);
+        launch_bwd16_reduce<SRC, BASIS, DAMPED, TWO>(a, nblk(total), st);
       }
       KernelTimer kt("bwd_carry", st);
       launch_grouped_carry<16, TWO, true>(a, st);
     }
     KernelTimer kt("bwd_apply", st);
-    bwd16_apply_kernel<SRC, BASIS, DAMPED, TWO><<<nblk(total), 128, 0, st>>>(a);
+    launch_bwd16_apply<SRC, BASIS, DAMPED, TWO>(a, nblk(total), st);
   }
   if (SRC == SRC_ROTOR && a.B * a.T > 0) {
     const int64_t BT = a.B * a.T;

@@ -44,12 +44,6 @@ static_assert(BwdAppSlot::STRIDE % 32 == 28, "bank spread");
 
 extern __shared__ __align__(16) float s8_smem[];
 
-// Device status of the kernels in this file: bit 0 = a bounded mbarrier wait gave up
-// (read and cleared by csn_device_status).
-__device__ unsigned g_s8_status;
-constexpr unsigned kStatusWaitTimeout = 1u;
-constexpr int kWaitPolls = 1 << 20;  // bulk-copy waits give up after this many polls
-
 __device__ __forceinline__ void lds_row(float (&r)[8], const float* p) {
   const float4 a = *reinterpret_cast<const float4*>(p);
   const float4 b = *reinterpret_cast<const float4*>(p + 4);
@@ -433,33 +427,10 @@ __global__ void __launch_bounds__(THREADS, 2) bwd8_apply_kernel(ScanArgs a) {
   float* sXp = slot + BwdAppSlot::XP;
   float* sDX = slot + BwdAppSlot::DX;
   float* sG = slot + BwdAppSlot::G;
-  // Inputs arrive by bulk copies (one per row, issued by the row's own lane) on three
-  // barriers per warp: 0 = X_{t-1}, 1 = generators, 2 = S and dX.  Each lane arrives once per
-  // phase with the bytes it issued (0 when it has no row), so a phase completes when all 32
-  // lanes have arrived and their rows have landed.
-  uint64_t* bars = reinterpret_cast<uint64_t*>(s8_smem + THREADS * ST) + 3 * (threadIdx.x >> 5);
-  if ((threadIdx.x & 31) == 0) {
-#pragma unroll
-    for (int i = 0; i < 3; ++i) mbar_init(&bars[i], 32);
-    mbar_init_fence();
-  }
-  __syncwarp();
-  unsigned par[3] = {0u, 0u, 0u};
-  bool waits_ok = true;
-  auto wait_bar = [&](int i) {  // bounded: a wait that gives up is reported, and no later one runs
-    if (waits_ok && !mbar_wait(&bars[i], par[i], kWaitPolls)) {
-      waits_ok = false;
-      atomicOr(&g_s8_status, kStatusWaitTimeout);
-    }
-    par[i] ^= 1u;
-  };
 
   // step st of this lane is time t = t1 - 1 - st
   auto issue_xp = [&](int st) {  // X_{t-1}; rows before t = 0 come from h0 (or zeros) below
-    const int64_t row = (st < me.len) ? lane_row<true>(me.first, me.len, me.t0, st, 1, a.N) : -1;
-    fence_proxy_async_smem();
-    mbar_arrive_expect_tx(&bars[0], row >= 0 ? DD * 4 : 0);
-    if (row >= 0) bulk_g2s(sXp, a.X + row * DD, DD * 4, &bars[0]);
+    coop_load_rows<DD, true>(warp_slots, ST, BwdAppSlot::XP, a.X, me, st, a.N, 1);
   };
   auto fix_xp = [&](int st) {  // own lane: X_{-1} = h0 or 0 when this step is t = 0
     if (st < me.len && t1 - 1 - st == 0) {
@@ -475,23 +446,18 @@ __global__ void __launch_bounds__(THREADS, 2) bwd8_apply_kernel(ScanArgs a) {
     }
   };
   auto issue_gens = [&](int st) {
-    const int64_t row = (st < me.len) ? lane_row<true>(me.first, me.len, me.t0, st, 0, a.N) : -1;
-    fence_proxy_async_smem();
-    mbar_arrive_expect_tx(&bars[1], row >= 0 ? K * 4 : 0);
-    if (row >= 0) bulk_g2s(sG, a.gens + row * K, K * 4, &bars[1]);
+    coop_load_rows<K, true>(warp_slots, ST, BwdAppSlot::G, a.gens, me, st, a.N);
   };
   auto issue_sdx = [&](int st) {
-    const int64_t row = (st < me.len) ? lane_row<true>(me.first, me.len, me.t0, st, 0, a.N) : -1;
-    fence_proxy_async_smem();
-    mbar_arrive_expect_tx(&bars[2], row >= 0 ? (DAMPED ? 2 : 1) * DD * 4 : 0);
-    if (row >= 0) {
-      if (DAMPED) bulk_g2s(sM, a.S + row * DD, DD * 4, &bars[2]);
-      bulk_g2s(sDX, a.dX + row * DD, DD * 4, &bars[2]);
-    }
+    if (DAMPED) coop_load_rows<DD, true>(warp_slots, ST, BwdAppSlot::MS, a.S, me, st, a.N);
+    coop_load_rows<DD, true>(warp_slots, ST, BwdAppSlot::DX, a.dX, me, st, a.N);
   };
   issue_xp(0);
+  cp_async_commit();
   issue_gens(0);
+  cp_async_commit();
   issue_sdx(0);
+  cp_async_commit();
   fix_xp(0);
   float gam_n = 0.0f, dt_n = 0.0f;
   if (me.len > 0) {
@@ -516,13 +482,14 @@ __global__ void __launch_bounds__(THREADS, 2) bwd8_apply_kernel(ScanArgs a) {
       dt_n = __ldg(a.dt + dt_index(a, b, t - 1, n));
     }
     // ---- 1. Cayley in registers (Xp, gens landed; S, dX may still be in flight)
-    wait_bar(0);
-    wait_bar(1);
+    cp_async_wait<1>();
+    __syncwarp();
     Mat<8> Mr;
     float alpha = 1.0f, sa = 1.0f;
     if (live) cayley_from_slot<DAMPED>(sG, dtv, gam, Mr, alpha, sa);
     // ---- 2. G = H + dX;  <G, S>;  G parks in the dX buffer;  M into its buffer
-    wait_bar(2);
+    cp_async_wait<0>();
+    __syncwarp();
     float gS = 0.0f;
     const float cs = DAMPED ? (1.0f - alpha) : 1.0f;
 #pragma unroll
@@ -644,6 +611,7 @@ __global__ void __launch_bounds__(THREADS, 2) bwd8_apply_kernel(ScanArgs a) {
     }
     __syncwarp();  // every lane is done with its Xp
     issue_xp(st + 1);
+    cp_async_commit();
     fix_xp(st + 1);
     // ---- 4. decay gradient
     float da = 0.0f;
@@ -726,6 +694,7 @@ __global__ void __launch_bounds__(THREADS, 2) bwd8_apply_kernel(ScanArgs a) {
     coop_store_rows<K, true>(warp_slots, ST, BwdAppSlot::G, a.dgens, me, st, a.N, 1.0f);
     __syncwarp();
     issue_gens(st + 1);
+    cp_async_commit();
     // ---- 6. H <- M^T (G M) (one-sided: M^T G): rows of G M (two-sided) or of G (one-sided)
     // are read back from the dX buffer
     {
@@ -743,13 +712,9 @@ __global__ void __launch_bounds__(THREADS, 2) bwd8_apply_kernel(ScanArgs a) {
     }
     __syncwarp();  // M and G buffers are free
     issue_sdx(st + 1);
+    cp_async_commit();
   }
-  // every phase armed above has been waited for (the last ones carry no rows) unless a wait
-  // gave up: then drain, bounded, whatever this lane's barriers may still be completing
-  if (!waits_ok) {
-#pragma unroll
-    for (int i = 0; i < 3; ++i) mbar_wait(&bars[i], par[i], kWaitPolls);
-  }
+  cp_async_wait<0>();
   if (active && j == 0 && a.dh0) store_mat(a.dh0 + s * DD, H);
 }
 
@@ -766,7 +731,7 @@ int run8(const ScanArgs& a, bool bwd, cudaStream_t st) {
   const int64_t total = S * a.nchunks;
   const int fwd_bytes = THREADS * FwdSlot::STRIDE * 4;
   const int red_bytes = THREADS * BwdRedSlot::STRIDE * 4;
-  const int app_bytes = THREADS * BwdAppSlot::STRIDE * 4 + (THREADS / 32) * 3 * 8;  // + mbarriers
+  const int app_bytes = THREADS * BwdAppSlot::STRIDE * 4;
   if (a.agg_mode == 1) {
     if (total == 0) return CSN_OK;
     if (!bwd) {
@@ -955,39 +920,6 @@ int run_step8(const float* gens, const float* dt, const float* gamma, const floa
 }
 
 }  // namespace s8
-
-// Self-test of the bounded wait: one thread arms a barrier phase with 16 bytes that no copy
-// delivers, so the phase never completes and the wait must give up after `polls` polls and
-// set the status bit.  Nothing is in flight when the kernel returns.
-__global__ void selftest_wait_kernel(int polls) {
-  __shared__ __align__(8) uint64_t bar;
-  if (threadIdx.x == 0) {
-    mbar_init(&bar, 1);
-    mbar_init_fence();
-    mbar_arrive_expect_tx(&bar, 16);
-    if (!mbar_wait(&bar, 0, polls)) atomicOr(&s8::g_s8_status, s8::kStatusWaitTimeout);
-  }
-}
-
-int selftest_wait8(int polls, cudaStream_t st) {
-  selftest_wait_kernel<<<1, 32, 0, st>>>(polls);
-  return check_launch("csn_selftest_bounded_wait");
-}
-
-// Status word of the kernels above, read on `stream` (a synchronisation), cleared if asked.
-int device_status8(unsigned* flags, int reset, cudaStream_t st) {
-  unsigned v = 0;
-  cudaError_t e = cudaMemcpyFromSymbolAsync(&v, s8::g_s8_status, sizeof(v), 0, cudaMemcpyDeviceToHost, st);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
-  if (e == cudaSuccess && reset) {
-    const unsigned zero = 0;
-    e = cudaMemcpyToSymbolAsync(s8::g_s8_status, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, st);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
-  }
-  if (e != cudaSuccess) return set_cuda_error(e, "csn_device_status");
-  *flags = v;
-  return CSN_OK;
-}
 
 int scan8_rotor_dispatch(const ScanArgs& a, bool damped, bool two, bool bwd, cudaStream_t st) {
   using namespace s8;

@@ -180,20 +180,6 @@ int csn_rotor_scan_fwd_noalloc(const float* gens, const float* dt, const float* 
                                int64_t B, int64_t T, int64_t N, int D, int basis, int two_sided,
                                void* stream);
 
-/* ------------------------------------------------ device status */
-/* The kernels that stage rows with bulk copies wait on mbarriers with a bounded number of
- * polls; a wait that gives up sets a bit here instead of hanging, and the kernel finishes with
- * the step's inputs possibly incomplete.  No reference counterpart (the reference has no
- * device-side waits).  Reads (and with reset != 0 clears) the bits on `stream`, synchronising
- * it; CSN_STATUS_WAIT_TIMEOUT = 1. */
-#define CSN_STATUS_WAIT_TIMEOUT 1u
-int csn_device_status(unsigned* flags, int reset, void* stream);
-
-/* Self-test of that path: launches one thread that waits (at most `polls` polls, 1..2^20) on
- * a barrier phase no copy will complete, so the wait gives up and sets
- * CSN_STATUS_WAIT_TIMEOUT; the kernel then returns normally and the context stays usable. */
-int csn_selftest_bounded_wait(int polls, void* stream);
-
 /* ------------------------------------------------ sequence-parallel shard aggregates */
 /* Summaries of one time shard (the local [B, T, N, ...] slice of a longer sequence) for the
  * cross-GPU carry exchange of the sequence-parallel scan.  The reference has no distributed

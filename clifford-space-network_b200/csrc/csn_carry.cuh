@@ -155,7 +155,7 @@ __global__ void __launch_bounds__(128) compose_kernel(ScanArgs a) {
 }
 
 
-// ------------------------------------------------------------ grouped carry (D = 8, 16)
+// ------------------------------------------------------------ grouped carry (D = 16)
 // The carry is a chain of links h <- L_k h L_k^T + c_k (one-sided: L_k h + c_k), one per
 // chunk boundary: forward L_k = P_k, c_k = aggC_k, k = 0 .. nchunks-2, h_0 = h0; backward
 // L_k = P_j^T, c_k = aggC_j with j = nchunks-1-k, h = hT at the last chunk.  One warp per
@@ -403,6 +403,180 @@ __global__ void __launch_bounds__(32 * carry_max_warps<D>()) carry_grouped_kerne
   walk(std::integral_constant<bool, false>{});
 }
 
+// ------------------------------------------------ grouped carry on fp64 MMA (D = 8)
+// The same three phases as carry_grouped_kernel, with every 8 x 8 product on the FP64 tensor
+// cores (mma.sync m8n8k4 f64) instead of shared-memory round trips: a warp holds a matrix as
+// the m8n8k4 accumulator fragment, lane 4 r + c owning X[r][2c] and X[r][2c+1].  Read with
+// the k-steps taking the even columns, then the odd ones, the same fragment is also the A
+// operand of X and the B operand of X^T, so nt(A, Y, C) = A Y^T + C needs no data movement.
+//   link (two-sided):  w = nt(L, m, 0) = L m^T,  m' = nt(L, w, c) = L m L^T + c
+//   link (one-sided):  the state is held transposed, m'^T = nt(m^T, L, c^T) = (L m + c)^T
+//   group operator:    G^T <- nt(G^T, L, 0) = (L G)^T
+// Links and states are carried in fp64 (the chunk aggregates are read as float); each carry
+// is written as the float nearest to it.
+namespace carry8 {
+
+struct Frag {
+  double x0, x1;
+};
+
+__device__ __forceinline__ void dmma(double& d0, double& d1, double a, double b) {
+  asm("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};\n"
+      : "+d"(d0), "+d"(d1)
+      : "d"(a), "d"(b));
+}
+
+__device__ __forceinline__ Frag nt(const Frag& A, const Frag& Y, Frag C) {
+  dmma(C.x0, C.x1, A.x0, Y.x0);
+  dmma(C.x0, C.x1, A.x1, Y.x1);
+  return C;
+}
+
+__device__ __forceinline__ Frag zero() { return Frag{0.0, 0.0}; }
+__device__ __forceinline__ Frag identity(int r, int c) {
+  return Frag{(r == 2 * c) ? 1.0 : 0.0, (r == 2 * c + 1) ? 1.0 : 0.0};
+}
+
+// fragment of X (T = false) or of X^T (T = true) from a row-major 8 x 8 array
+template <bool T, typename F>
+__device__ __forceinline__ Frag load(const F* p, int r, int c) {
+  if constexpr (T) return Frag{(double)p[(2 * c) * 8 + r], (double)p[(2 * c + 1) * 8 + r]};
+  else return Frag{(double)p[r * 8 + 2 * c], (double)p[r * 8 + 2 * c + 1]};
+}
+template <bool T, typename F>
+__device__ __forceinline__ void store(F* p, const Frag& X, int r, int c) {
+  if constexpr (T) {
+    p[(2 * c) * 8 + r] = (F)X.x0;
+    p[(2 * c + 1) * 8 + r] = (F)X.x1;
+  } else {
+    p[r * 8 + 2 * c] = (F)X.x0;
+    p[r * 8 + 2 * c + 1] = (F)X.x1;
+  }
+}
+
+// one link on the state: two-sided m <- L m L^T + c, one-sided (state transposed) m^T <- m^T L^T + c^T
+template <bool TWO>
+__device__ __forceinline__ Frag link(const Frag& L, const Frag& m, const Frag& c) {
+  if constexpr (TWO) return nt(L, nt(L, m, zero()), c);
+  else return nt(m, L, c);
+}
+
+}  // namespace carry8
+
+// Most warps per sequence and links per warp of the fp64-MMA carry.
+constexpr int CARRY8_MAX_WARPS = 16;
+constexpr int CARRY8_LINKS_PER_WARP = 16;
+
+template <bool TWO, bool REVERSE>
+__global__ void __launch_bounds__(32 * CARRY8_MAX_WARPS) carry8_mma_kernel(ScanArgs a) {
+  using namespace carry8;
+  constexpr int DD = 64;
+  // the operator and the offset of every warp's group, in fp64: [nw][DD] each
+  extern __shared__ __align__(16) double c8_smem[];
+  const int nw = blockDim.x >> 5, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = lane >> 2, c = lane & 3;
+  const int64_t s = blockIdx.x;
+  const int64_t nch = a.nchunks, nl = nch - 1;
+  const int64_t base = s * nch;
+  double* gG = c8_smem;                      // group operators G_w, row-major
+  double* gC = c8_smem + (size_t)nw * DD;    // group offsets (the state's own orientation)
+  const int64_t per = (nl + nw - 1) / nw;
+  const int64_t k0 = min(nl, (int64_t)w * per), k1 = min(nl, k0 + per);
+  // link k: forward L = P_k, c = aggC_k, writes carry k + 1;  backward (chunk j = nch-1-k)
+  // L = P_j^T, c = aggC_j, writes carry j - 1.  One-sided states are held transposed.
+  auto chunk_of = [&](int64_t k) { return REVERSE ? nch - 1 - k : k; };
+  auto out_of = [&](int64_t k) { return REVERSE ? nch - 2 - k : k + 1; };
+  // the lane's two entries of a link's L and c fragments, as stored (float)
+  auto load_link = [&](int64_t k, float (&v)[4]) {
+    const float* P = a.aggP + (base + chunk_of(k)) * DD;
+    const float* C = a.aggC + (base + chunk_of(k)) * DD;
+    const int lo = REVERSE ? (2 * c) * 8 + r : r * 8 + 2 * c, lstep = REVERSE ? 8 : 1;
+    const int co = TWO ? r * 8 + 2 * c : (2 * c) * 8 + r, cstep = TWO ? 1 : 8;
+    v[0] = __ldg(P + lo);
+    v[1] = __ldg(P + lo + lstep);
+    v[2] = __ldg(C + co);
+    v[3] = __ldg(C + co + cstep);
+  };
+
+  // Walk links [k0, k1), composing G^T when COMPOSE and writing every carry otherwise; the
+  // next PF links' operands are in flight meanwhile (a ring of register slots, unrolled so
+  // that slot indices are compile-time).
+  constexpr int PF = 4;
+  auto walk = [&](auto compose_tag, Frag& m, Frag& T) {
+    constexpr bool COMPOSE = decltype(compose_tag)::value;
+    float ring[PF][4];
+#pragma unroll
+    for (int u = 0; u < PF; ++u)
+      if (k0 + u < k1) load_link(k0 + u, ring[u]);
+    for (int64_t kk = k0; kk < k1; kk += PF) {
+#pragma unroll
+      for (int u = 0; u < PF; ++u) {
+        const int64_t k = kk + u;
+        if (k >= k1) break;
+        const Frag L{(double)ring[u][0], (double)ring[u][1]};
+        const Frag cf{(double)ring[u][2], (double)ring[u][3]};
+        if (k + PF < k1) load_link(k + PF, ring[u]);
+        m = link<TWO>(L, m, cf);
+        if constexpr (COMPOSE) T = nt(T, L, zero());
+        else store<!TWO>(a.carry + (base + out_of(k)) * DD, m, r, c);
+      }
+    }
+  };
+
+  // 1. group links: (G_w, c_w) composed from the identity and a zero state
+  {
+    Frag m = zero(), T = identity(r, c);
+    walk(std::integral_constant<bool, true>{}, m, T);
+    store<true>(gG + (size_t)w * DD, T, r, c);  // G_w from G_w^T
+    store<!TWO>(gC + (size_t)w * DD, m, r, c);
+  }
+  __syncthreads();
+  // 2. inclusive scan of the group links (Hillis-Steele): at distance d, warp w >= d puts the
+  //    prefix of group w - d before its own: c <- G_w c_p G_w^T + c_w (one-sided G_w c_p +
+  //    c_w), G <- G_w G_p.  Reads and writes are separated by block barriers.
+  for (int d = 1; d < nw; d <<= 1) {
+    const bool act = w >= d;
+    Frag mn, Tn;
+    if (act) {
+      const Frag L = load<false>(gG + (size_t)w * DD, r, c);
+      const Frag Tp = load<true>(gG + (size_t)(w - d) * DD, r, c);
+      const Frag mp = load<!TWO>(gC + (size_t)(w - d) * DD, r, c);
+      const Frag cw = load<!TWO>(gC + (size_t)w * DD, r, c);
+      mn = link<TWO>(L, mp, cw);
+      Tn = nt(Tp, L, zero());
+    }
+    __syncthreads();
+    if (act) {
+      store<true>(gG + (size_t)w * DD, Tn, r, c);
+      store<!TWO>(gC + (size_t)w * DD, mn, r, c);
+    }
+    __syncthreads();
+  }
+  // 3. carry-in of group w: the initial state carried through groups 0 .. w-1; then replay
+  const float* init = REVERSE ? a.hT : a.h0;
+  Frag m = init ? load<!TWO>(init + s * DD, r, c) : zero();
+  if (w == 0) store<!TWO>(a.carry + (base + (REVERSE ? nch - 1 : 0)) * DD, m, r, c);
+  if (w > 0) {
+    const Frag cp = load<!TWO>(gC + (size_t)(w - 1) * DD, r, c);
+    if (init) m = link<TWO>(load<false>(gG + (size_t)(w - 1) * DD, r, c), m, cp);
+    else m = cp;
+  }
+  Frag unused = zero();
+  walk(std::integral_constant<bool, false>{}, m, unused);
+}
+
+template <bool TWO, bool REVERSE>
+inline void launch_carry8_mma(const ScanArgs& a, cudaStream_t st) {
+  const int64_t nl = a.nchunks - 1;
+  int64_t w = (nl + CARRY8_LINKS_PER_WARP - 1) / CARRY8_LINKS_PER_WARP;
+  w = w < 1 ? 1 : w > CARRY8_MAX_WARPS ? CARRY8_MAX_WARPS : w;
+  const size_t smem = (size_t)2 * w * 64 * sizeof(double);
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(carry8_mma_kernel<TWO, REVERSE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+  carry8_mma_kernel<TWO, REVERSE><<<(unsigned)(a.B * a.N), 32 * (unsigned)w, smem, st>>>(a);
+}
+
 // Warps per sequence for the grouped carry: about 16 links per warp.
 template <int D>
 inline int carry_warps(int64_t nchunks) {
@@ -414,9 +588,14 @@ inline int carry_warps(int64_t nchunks) {
 template <int D>
 inline size_t carry_smem_bytes(int warps) { return (size_t)7 * warps * D * D * sizeof(float); }
 
-// Launch the carry pass of a chunked scan (nchunks > 1): grouped for D = 8, 16.
+// Launch the carry pass of a chunked scan (nchunks > 1): fp64 MMA for D = 8, grouped on
+// shared memory for D = 16.
 template <int D, bool TWO, bool REVERSE>
 inline void launch_grouped_carry(const ScanArgs& a, cudaStream_t st) {
+  if constexpr (D == 8) {
+    launch_carry8_mma<TWO, REVERSE>(a, st);
+    return;
+  }
   const int w = carry_warps<D>(a.nchunks);
   const size_t smem = carry_smem_bytes<D>(w);
   if (smem > 48 * 1024)

@@ -14,8 +14,13 @@
 //  * matrices that would not fit in the 255-register budget next to the live state
 //    (the running product P in the reduce passes, M in the backward apply pass) live in
 //    the slot too, and products with them are written as row-broadcast outer products
-//    (one 128-bit load of a row feeds 32 FMAs), so they cost no register spills.
-// Chunks, carries and results are identical to the generic kernels.
+//    (one 128-bit load of a row feeds 32 FMAs), so they cost no register spills;
+//  * the 8 x 8 products run on packed fp32 (fma.rn.f32x2: two adjacent entries of a row or
+//    column per instruction, the other factor broadcast), which halves the FP32
+//    instructions of the products without changing a single rounding: within a chunk the
+//    forward state, the chunk aggregates and the gradient carry are bit-identical to the
+//    scalar form.
+// Chunks and the order of every accumulation in the forward pass match the generic kernels.
 #include "csn_common.cuh"
 #include "csn_internal.h"
 #include "csn_scan_args.cuh"
@@ -52,6 +57,141 @@ __device__ __forceinline__ void lds_row(float (&r)[8], const float* p) {
 __device__ __forceinline__ void sts_row(float* p, const float (&r)[8]) {
   *reinterpret_cast<float4*>(p) = make_float4(r[0], r[1], r[2], r[3]);
   *reinterpret_cast<float4*>(p + 4) = make_float4(r[4], r[5], r[6], r[7]);
+}
+__device__ __forceinline__ void lds_row2(uint64_t (&r)[4], const float* p) {
+  const ulonglong2 a = *reinterpret_cast<const ulonglong2*>(p);
+  const ulonglong2 b = *reinterpret_cast<const ulonglong2*>(p + 4);
+  r[0] = a.x; r[1] = a.y; r[2] = b.x; r[3] = b.y;
+}
+__device__ __forceinline__ void sts_row2(float* p, const uint64_t (&r)[4]) {
+  *reinterpret_cast<ulonglong2*>(p) = make_ulonglong2(r[0], r[1]);
+  *reinterpret_cast<ulonglong2*>(p + 4) = make_ulonglong2(r[2], r[3]);
+}
+__device__ __forceinline__ float f2lo(uint64_t v) { return f2unpack(v).x; }
+__device__ __forceinline__ float f2hi(uint64_t v) { return f2unpack(v).y; }
+
+// ------------------------------------------------------ packed 8 x 8 products
+// The products below are the scalar lmul / rmulT / lmulT / rmul of csn_common.cuh with two
+// adjacent outputs per fma.rn.f32x2: every output entry sees the same fmaf chain in the same
+// order (k = 0 first, as a product, then accumulated), so the results are bit-identical to
+// the scalar forms, with half the FP32 instructions.  The paired operand is a pair of
+// adjacent entries of M (down a column for lmul8p / rmulT8p, along a row for lmulT8p /
+// rmul8p), the other factor one entry broadcast to both halves.
+
+// X <- M X, columns 2q and 2q+1 at a time (in place: they depend only on themselves)
+__device__ __forceinline__ void lmul8p(const Mat<8>& M, Mat<8>& X) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint64_t z0[4], z1[4];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const uint64_t s0 = f2splat(X.a[k][2 * q]), s1 = f2splat(X.a[k][2 * q + 1]);
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const uint64_t m = f2pack(M.a[2 * p][k], M.a[2 * p + 1][k]);
+        z0[p] = k ? f2fma(m, s0, z0[p]) : f2mul(m, s0);
+        z1[p] = k ? f2fma(m, s1, z1[p]) : f2mul(m, s1);
+      }
+    }
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      X.a[2 * p][2 * q] = f2lo(z0[p]);
+      X.a[2 * p + 1][2 * q] = f2hi(z0[p]);
+      X.a[2 * p][2 * q + 1] = f2lo(z1[p]);
+      X.a[2 * p + 1][2 * q + 1] = f2hi(z1[p]);
+    }
+  }
+}
+
+// X <- X M^T, rows 2u and 2u+1 at a time
+__device__ __forceinline__ void rmulT8p(Mat<8>& X, const Mat<8>& M) {
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    uint64_t y0[4], y1[4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint64_t s0 = f2splat(X.a[2 * u][j]), s1 = f2splat(X.a[2 * u + 1][j]);
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const uint64_t m = f2pack(M.a[2 * p][j], M.a[2 * p + 1][j]);
+        y0[p] = j ? f2fma(s0, m, y0[p]) : f2mul(s0, m);
+        y1[p] = j ? f2fma(s1, m, y1[p]) : f2mul(s1, m);
+      }
+    }
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      X.a[2 * u][2 * p] = f2lo(y0[p]);
+      X.a[2 * u][2 * p + 1] = f2hi(y0[p]);
+      X.a[2 * u + 1][2 * p] = f2lo(y1[p]);
+      X.a[2 * u + 1][2 * p + 1] = f2hi(y1[p]);
+    }
+  }
+}
+
+// X <- M^T X, columns 2q and 2q+1 at a time
+__device__ __forceinline__ void lmulT8p(const Mat<8>& M, Mat<8>& X) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint64_t z0[4], z1[4];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const uint64_t s0 = f2splat(X.a[k][2 * q]), s1 = f2splat(X.a[k][2 * q + 1]);
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const uint64_t m = f2pack(M.a[k][2 * p], M.a[k][2 * p + 1]);
+        z0[p] = k ? f2fma(m, s0, z0[p]) : f2mul(m, s0);
+        z1[p] = k ? f2fma(m, s1, z1[p]) : f2mul(m, s1);
+      }
+    }
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      X.a[2 * p][2 * q] = f2lo(z0[p]);
+      X.a[2 * p + 1][2 * q] = f2hi(z0[p]);
+      X.a[2 * p][2 * q + 1] = f2lo(z1[p]);
+      X.a[2 * p + 1][2 * q + 1] = f2hi(z1[p]);
+    }
+  }
+}
+
+// X <- X M, rows 2u and 2u+1 at a time
+__device__ __forceinline__ void rmul8p(Mat<8>& X, const Mat<8>& M) {
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    uint64_t y0[4], y1[4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint64_t s0 = f2splat(X.a[2 * u][j]), s1 = f2splat(X.a[2 * u + 1][j]);
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const uint64_t m = f2pack(M.a[j][2 * p], M.a[j][2 * p + 1]);
+        y0[p] = j ? f2fma(s0, m, y0[p]) : f2mul(s0, m);
+        y1[p] = j ? f2fma(s1, m, y1[p]) : f2mul(s1, m);
+      }
+    }
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      X.a[2 * u][2 * p] = f2lo(y0[p]);
+      X.a[2 * u][2 * p + 1] = f2hi(y0[p]);
+      X.a[2 * u + 1][2 * p] = f2lo(y1[p]);
+      X.a[2 * u + 1][2 * p + 1] = f2hi(y1[p]);
+    }
+  }
+}
+
+// X += c R for 8 rows R read from shared memory (row stride 8), pairs along the rows
+__device__ __forceinline__ void add_rows8p(Mat<8>& X, const float* rows, float c) {
+  const uint64_t c2 = f2splat(c);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    uint64_t r2[4];
+    lds_row2(r2, rows + 8 * i);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint64_t x = f2fma(c2, r2[q], f2pack(X.a[i][2 * q], X.a[i][2 * q + 1]));
+      X.a[i][2 * q] = f2lo(x);
+      X.a[i][2 * q + 1] = f2hi(x);
+    }
+  }
 }
 
 // ------------------------------------------------- warp-cooperative row transfers
@@ -242,19 +382,23 @@ __global__ void __launch_bounds__(THREADS, 2) fwd8_kernel(ScanArgs a) {
     issue_a(st + 1);
     cp_async_commit();
     if (live) {
-      lmul(M, X);
-      if constexpr (TWO) rmulT(X, M);
+      lmul8p(M, X);
+      if constexpr (TWO) rmulT8p(X, M);
     }
     cp_async_wait<1>();  // S rows of this step
     if constexpr (!REDUCE) __syncwarp();  // rows were copied by other lanes
     const float cs = DAMPED ? (1.0f - alpha) : 1.0f;
     if (live) {
+      if constexpr (TWO) {
+        add_rows8p(X, slot + FwdSlot::S, cs);
+      } else {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        float r[8];
-        lds_row(r, slot + FwdSlot::S + 8 * i);
+        for (int i = 0; i < 8; ++i) {
+          float r[8];
+          lds_row(r, slot + FwdSlot::S + 8 * i);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) X.a[i][c] = fmaf(cs, r[c], X.a[i][c]);
+          for (int c = 0; c < 8; ++c) X.a[i][c] = fmaf(cs, r[c], X.a[i][c]);
+        }
       }
     }
     if constexpr (REDUCE) {
@@ -265,16 +409,19 @@ __global__ void __launch_bounds__(THREADS, 2) fwd8_kernel(ScanArgs a) {
         // (jj only addresses shared memory: rolled, 9 % faster than unrolled)
 #pragma unroll 1
         for (int jj = 0; jj < 8; ++jj) {
-          float v[8], o[8];
+          float v[8];
+          uint64_t o2[4];
           lds_row(v, slot + FwdSlot::P + 8 * jj);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            float acc = 0.0f;
+          for (int k = 0; k < 8; ++k) {
+            const uint64_t sv = f2splat(v[k]);
 #pragma unroll
-            for (int k = 0; k < 8; ++k) acc = fmaf(M.a[i][k], v[k], acc);
-            o[i] = acc;
+            for (int p = 0; p < 4; ++p) {
+              const uint64_t m = f2pack(M.a[2 * p][k], M.a[2 * p + 1][k]);
+              o2[p] = k ? f2fma(m, sv, o2[p]) : f2mul(m, sv);
+            }
           }
-          sts_row(slot + FwdSlot::P + 8 * jj, o);
+          sts_row2(slot + FwdSlot::P + 8 * jj, o2);
         }
       }
     } else {
@@ -356,31 +503,38 @@ __global__ void __launch_bounds__(THREADS, 2) bwd8_reduce_kernel(ScanArgs a) {
     if (t - 1 >= t0) issue_a(t - 1);
     cp_async_commit();
     cp_async_wait<1>();
+    if constexpr (TWO) {
+      add_rows8p(g, slot + BwdRedSlot::DX, 1.0f);
+    } else {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      float r[8];
-      lds_row(r, slot + BwdRedSlot::DX + 8 * i);
+      for (int i = 0; i < 8; ++i) {
+        float r[8];
+        lds_row(r, slot + BwdRedSlot::DX + 8 * i);
 #pragma unroll
-      for (int c = 0; c < 8; ++c) g.a[i][c] += r[c];
+        for (int c = 0; c < 8; ++c) g.a[i][c] += r[c];
+      }
     }
     if (t - 1 >= t0) issue_b(t - 1);
     cp_async_commit();
-    lmulT(M, g);
-    if constexpr (TWO) rmul(g, M);
+    lmulT8p(M, g);
+    if constexpr (TWO) rmul8p(g, M);
     // P <- P M, row by row in place (i only addresses shared memory: rolled)
     if (!a.reuse_P) {
 #pragma unroll 1
       for (int i = 0; i < 8; ++i) {
-        float v[8], o[8];
+        float v[8];
+        uint64_t o2[4];
         lds_row(v, slot + BwdRedSlot::P + 8 * i);
 #pragma unroll
-        for (int l = 0; l < 8; ++l) {
-          float acc = 0.0f;
+        for (int k = 0; k < 8; ++k) {
+          const uint64_t sv = f2splat(v[k]);
 #pragma unroll
-          for (int k = 0; k < 8; ++k) acc = fmaf(v[k], M.a[k][l], acc);
-          o[l] = acc;
+          for (int p = 0; p < 4; ++p) {
+            const uint64_t m = f2pack(M.a[k][2 * p], M.a[k][2 * p + 1]);
+            o2[p] = k ? f2fma(sv, m, o2[p]) : f2mul(sv, m);
+          }
         }
-        sts_row(slot + BwdRedSlot::P + 8 * i, o);
+        sts_row2(slot + BwdRedSlot::P + 8 * i, o2);
       }
     }
   }
@@ -466,10 +620,18 @@ __global__ void __launch_bounds__(THREADS, 2) bwd8_apply_kernel(ScanArgs a) {
     dt_n = __ldg(a.dt + dt_index(a, b, t1 - 1, n));
   }
 
-  Mat<8> H;
-  if (active && a.nchunks > 1) load_mat(H, a.carry + (s * a.nchunks + j) * DD);
-  else if (active && a.hT) load_mat(H, a.hT + s * DD);
-  else mat_zero(H);
+  // packed state and gradients: entry pairs (c, c+1) of a row in one 64-bit register pair
+  uint64_t H2[8][4];
+  {
+    Mat<8> H;
+    if (active && a.nchunks > 1) load_mat(H, a.carry + (s * a.nchunks + j) * DD);
+    else if (active && a.hT) load_mat(H, a.hT + s * DD);
+    else mat_zero(H);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) H2[i][q] = f2pack(H.a[i][2 * q], H.a[i][2 * q + 1]);
+  }
 
   for (int st = 0; st < nsteps; ++st) {
     const bool live = st < me.len;
@@ -490,33 +652,27 @@ __global__ void __launch_bounds__(THREADS, 2) bwd8_apply_kernel(ScanArgs a) {
     // ---- 2. G = H + dX;  <G, S>;  G parks in the dX buffer;  M into its buffer
     cp_async_wait<0>();
     __syncwarp();
-    float gS = 0.0f;
+    uint64_t gS2 = 0;
     const float cs = DAMPED ? (1.0f - alpha) : 1.0f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      float r[8], sr[8];
-      lds_row(r, sDX + 8 * i);
-      if (DAMPED) lds_row(sr, sM + 8 * i);
+      uint64_t r2[4], s2[4];
+      lds_row2(r2, sDX + 8 * i);
+      if (DAMPED) lds_row2(s2, sM + 8 * i);
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        H.a[i][c] += r[c];
-        if (DAMPED) gS = fmaf(H.a[i][c], sr[c], gS);
+      for (int q = 0; q < 4; ++q) {
+        H2[i][q] = f2add(H2[i][q], r2[q]);
+        if (DAMPED) gS2 = f2fma(H2[i][q], s2[q], gS2);
       }
-#pragma unroll
-      for (int c = 0; c < 8; ++c) r[c] = H.a[i][c];
-      sts_row(sDX + 8 * i, r);
+      sts_row2(sDX + 8 * i, H2[i]);
     }
+    const float gS = f2sum(gS2);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      float r[8];
-#pragma unroll
-      for (int c = 0; c < 8; ++c) r[c] = Mr.a[i][c];
-      sts_row(sM + 8 * i, r);
-    }
+    for (int i = 0; i < 8; ++i) sts_row(sM + 8 * i, Mr.a[i]);
     __syncwarp();
     coop_store_rows<DD, true>(warp_slots, ST, BwdAppSlot::DX, a.dC, me, st, a.N, cs);  // dS = (1-a) G
     // ---- 3. dM, with G read back from the dX buffer
-    Mat<8> dM;
+    uint64_t dM2[8][4];
     if constexpr (TWO) {
       // dM = (G M) Xp^T + (G^T M) Xp.  First the G^T M part, which reads every column of G;
       // then G M by halves of rows: half h reads only rows 4h..4h+3 of G, so its rows of G M
@@ -526,77 +682,81 @@ __global__ void __launch_bounds__(THREADS, 2) bwd8_apply_kernel(ScanArgs a) {
         // keeps the scheduler from overlapping the two halves (which would hold both
         // halves' temporaries at once and spill)
         __syncwarp();
-        float U[4][8];
+        uint64_t U2[4][4];
 #pragma unroll
         for (int r = 0; r < 4; ++r)
 #pragma unroll
-          for (int l = 0; l < 8; ++l) U[r][l] = 0.0f;
+          for (int q = 0; q < 4; ++q) U2[r][q] = 0;
         // k only addresses shared memory here, so the loop stays rolled (smaller step body)
 #pragma unroll 1
         for (int k = 0; k < 8; ++k) {  // U = (G^T)[rows] M
-          float mr[8];
-          lds_row(mr, sM + 8 * k);
+          uint64_t mr2[4];
+          lds_row2(mr2, sM + 8 * k);
           const float4 gu4 = *reinterpret_cast<const float4*>(sDX + 8 * k + 4 * h);  // G[k][rows]
           const float guv[4] = {gu4.x, gu4.y, gu4.z, gu4.w};
 #pragma unroll
-          for (int r = 0; r < 4; ++r)
+          for (int r = 0; r < 4; ++r) {
+            const uint64_t gg = f2splat(guv[r]);
 #pragma unroll
-            for (int l = 0; l < 8; ++l) U[r][l] = fmaf(guv[r], mr[l], U[r][l]);
+            for (int q = 0; q < 4; ++q) U2[r][q] = f2fma(gg, mr2[q], U2[r][q]);
+          }
         }
 #pragma unroll
         for (int k = 0; k < 8; ++k) {  // dM[rows] = U Xp
-          float xr[8];
-          lds_row(xr, sXp + 8 * k);
+          uint64_t xr2[4];
+          lds_row2(xr2, sXp + 8 * k);
 #pragma unroll
           for (int r = 0; r < 4; ++r) {
-            if (k == 0) {
+            const float2 up = f2unpack(U2[r][k >> 1]);
+            const uint64_t uu = f2splat((k & 1) ? up.y : up.x);
 #pragma unroll
-              for (int l = 0; l < 8; ++l) dM.a[4 * h + r][l] = U[r][0] * xr[l];
-            } else {
-#pragma unroll
-              for (int l = 0; l < 8; ++l) dM.a[4 * h + r][l] = fmaf(U[r][k], xr[l], dM.a[4 * h + r][l]);
-            }
+            for (int q = 0; q < 4; ++q)
+              dM2[4 * h + r][q] = (k == 0) ? f2mul(uu, xr2[q]) : f2fma(uu, xr2[q], dM2[4 * h + r][q]);
           }
         }
       }
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         __syncwarp();
-        float W[4][8];
+        uint64_t W2[4][4];
 #pragma unroll
         for (int r = 0; r < 4; ++r)
 #pragma unroll
-          for (int l = 0; l < 8; ++l) W[r][l] = 0.0f;
+          for (int q = 0; q < 4; ++q) W2[r][q] = 0;
 #pragma unroll 1
         for (int k = 0; k < 8; ++k) {  // W = G[rows] M
-          float mr[8];
-          lds_row(mr, sM + 8 * k);
+          uint64_t mr2[4];
+          lds_row2(mr2, sM + 8 * k);
 #pragma unroll
           for (int r = 0; r < 4; ++r) {
-            const float gw = sDX[8 * (4 * h + r) + k];
+            const uint64_t gg = f2splat(sDX[8 * (4 * h + r) + k]);
 #pragma unroll
-            for (int l = 0; l < 8; ++l) W[r][l] = fmaf(gw, mr[l], W[r][l]);
+            for (int q = 0; q < 4; ++q) W2[r][q] = f2fma(gg, mr2[q], W2[r][q]);
           }
         }
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {  // dM[rows][k] += W[rows] . Xp[k]
-          float xr[8];
-          lds_row(xr, sXp + 8 * k);
+        for (int kk = 0; kk < 4; ++kk) {  // dM[rows][k] += W[rows] . Xp[k], k = 2kk, 2kk+1
+          uint64_t xa[4], xb[4];
+          lds_row2(xa, sXp + 16 * kk);
+          lds_row2(xb, sXp + 16 * kk + 8);
 #pragma unroll
           for (int r = 0; r < 4; ++r) {
-            float acc = 0.0f;
+            uint64_t pa = f2mul(W2[r][0], xa[0]), pb = f2mul(W2[r][0], xb[0]);
 #pragma unroll
-            for (int c = 0; c < 8; ++c) acc = fmaf(W[r][c], xr[c], acc);
-            dM.a[4 * h + r][k] += acc;
+            for (int q = 1; q < 4; ++q) {
+              pa = f2fma(W2[r][q], xa[q], pa);
+              pb = f2fma(W2[r][q], xb[q], pb);
+            }
+            dM2[4 * h + r][kk] = f2add(dM2[4 * h + r][kk], f2pack(f2sum(pa), f2sum(pb)));
           }
         }
 #pragma unroll
-        for (int r = 0; r < 4; ++r) sts_row(sDX + 8 * (4 * h + r), W[r]);  // rows of G M over rows of G
+        for (int r = 0; r < 4; ++r) sts_row2(sDX + 8 * (4 * h + r), W2[r]);  // rows of G M over rows of G
       }
     } else {
 #pragma unroll
       for (int i = 0; i < 8; ++i) {  // dM = G Xp^T, row i from row i of G
-        float gr[8];
+        float gr[8], d[8];
         lds_row(gr, sDX + 8 * i);
 #pragma unroll
         for (int l = 0; l < 8; ++l) {
@@ -605,8 +765,10 @@ __global__ void __launch_bounds__(THREADS, 2) bwd8_apply_kernel(ScanArgs a) {
           float acc = 0.0f;
 #pragma unroll
           for (int k = 0; k < 8; ++k) acc = fmaf(gr[k], xr[k], acc);
-          dM.a[i][l] = acc;
+          d[l] = acc;
         }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) dM2[i][q] = f2pack(d[2 * q], d[2 * q + 1]);
       }
     }
     __syncwarp();  // every lane is done with its Xp
@@ -616,15 +778,15 @@ __global__ void __launch_bounds__(THREADS, 2) bwd8_apply_kernel(ScanArgs a) {
     // ---- 4. decay gradient
     float da = 0.0f;
     if constexpr (DAMPED) {
-      float dmm = 0.0f;
+      uint64_t dmm2 = 0;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        float mr[8];
-        lds_row(mr, sM + 8 * i);
+        uint64_t mr2[4];
+        lds_row2(mr2, sM + 8 * i);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) dmm = fmaf(dM.a[i][c], mr[c], dmm);
+        for (int q = 0; q < 4; ++q) dmm2 = f2fma(dM2[i][q], mr2[q], dmm2);
       }
-      da = -gS + dmm / (2.0f * alpha);
+      da = -gS + f2sum(dmm2) / (2.0f * alpha);
     }
     // ---- 5. generator gradient: V = (M^T dM + sa dM)/2, dOm = V M^T / sa + V
     float proj[K];
@@ -632,35 +794,43 @@ __global__ void __launch_bounds__(THREADS, 2) bwd8_apply_kernel(ScanArgs a) {
     for (int k = 0; k < K; ++k) proj[k] = 0.0f;
     {
       const float inv_sa = 1.0f / sa;
+      const uint64_t sa2 = f2splat(sa), half2 = f2splat(0.5f);
 #pragma unroll
       for (int h = 0; h < 2; ++h) {  // rows 4h .. 4h+3 of V and dOm
         __syncwarp();
-        float V[4][8];
+        uint64_t V2[4][4];
 #pragma unroll
         for (int r = 0; r < 4; ++r)
 #pragma unroll
-          for (int l = 0; l < 8; ++l) V[r][l] = 0.5f * sa * dM.a[4 * h + r][l];
+          for (int q = 0; q < 4; ++q) V2[r][q] = f2mul(sa2, dM2[4 * h + r][q]);
 #pragma unroll
-        for (int jj = 0; jj < 8; ++jj) {  // V += (M^T dM)[rows] / 2
-          float mr[8];
-          lds_row(mr, sM + 8 * jj);
+        for (int jj = 0; jj < 8; ++jj) {  // V += (M^T dM)[rows]
+          const float4 m4 = *reinterpret_cast<const float4*>(sM + 8 * jj + 4 * h);
+          const float mv[4] = {m4.x, m4.y, m4.z, m4.w};
 #pragma unroll
-          for (int r = 0; r < 4; ++r)
+          for (int r = 0; r < 4; ++r) {
+            const uint64_t mm = f2splat(mv[r]);
 #pragma unroll
-            for (int l = 0; l < 8; ++l) V[r][l] = fmaf(0.5f * mr[4 * h + r], dM.a[jj][l], V[r][l]);
+            for (int q = 0; q < 4; ++q) V2[r][q] = f2fma(mm, dM2[jj][q], V2[r][q]);
+          }
         }
 #pragma unroll
+        for (int r = 0; r < 4; ++r)  // V /= 2 (exact)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) V2[r][q] = f2mul(half2, V2[r][q]);
+#pragma unroll
         for (int l = 0; l < 8; ++l) {  // dOm[rows][l] = (V M^T)[rows][l] / sa + V[rows][l]
-          float mr[8];
-          lds_row(mr, sM + 8 * l);
+          uint64_t mr2[4];
+          lds_row2(mr2, sM + 8 * l);
 #pragma unroll
           for (int r = 0; r < 4; ++r) {
             const int i = 4 * h + r;
             if (i == l) continue;
-            float acc = 0.0f;
+            uint64_t acc2 = f2mul(V2[r][0], mr2[0]);
 #pragma unroll
-            for (int k = 0; k < 8; ++k) acc = fmaf(V[r][k], mr[k], acc);
-            const float dom = fmaf(acc, inv_sa, V[r][l]);
+            for (int q = 1; q < 4; ++q) acc2 = f2fma(V2[r][q], mr2[q], acc2);
+            const float2 vp = f2unpack(V2[r][l >> 1]);
+            const float dom = fmaf(f2sum(acc2), inv_sa, (l & 1) ? vp.y : vp.x);
             if (i < l) proj[i * (15 - i) / 2 + (l - i - 1)] += dom;
             else proj[l * (15 - l) / 2 + (i - l - 1)] -= dom;
           }
@@ -698,16 +868,22 @@ __global__ void __launch_bounds__(THREADS, 2) bwd8_apply_kernel(ScanArgs a) {
     // ---- 6. H <- M^T (G M) (one-sided: M^T G): rows of G M (two-sided) or of G (one-sided)
     // are read back from the dX buffer
     {
-      mat_zero(H);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) H2[i][q] = 0;
 #pragma unroll 1  // k only addresses shared memory (rolled, as above)
       for (int k = 0; k < 8; ++k) {
-        float mr[8], gr[8];
+        float mr[8];
+        uint64_t gr2[4];
         lds_row(mr, sM + 8 * k);
-        lds_row(gr, sDX + 8 * k);
+        lds_row2(gr2, sDX + 8 * k);
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
+        for (int i = 0; i < 8; ++i) {
+          const uint64_t mm = f2splat(mr[i]);
 #pragma unroll
-          for (int l = 0; l < 8; ++l) H.a[i][l] = fmaf(mr[i], gr[l], H.a[i][l]);
+          for (int q = 0; q < 4; ++q) H2[i][q] = f2fma(mm, gr2[q], H2[i][q]);
+        }
       }
     }
     __syncwarp();  // M and G buffers are free
@@ -715,7 +891,18 @@ __global__ void __launch_bounds__(THREADS, 2) bwd8_apply_kernel(ScanArgs a) {
     cp_async_commit();
   }
   cp_async_wait<0>();
-  if (active && j == 0 && a.dh0) store_mat(a.dh0 + s * DD, H);
+  if (active && j == 0 && a.dh0) {
+    Mat<8> H;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 p = f2unpack(H2[i][q]);
+        H.a[i][2 * q] = p.x;
+        H.a[i][2 * q + 1] = p.y;
+      }
+    store_mat(a.dh0 + s * DD, H);
+  }
 }
 
 template <typename Kern>

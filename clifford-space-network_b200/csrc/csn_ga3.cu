@@ -118,30 +118,140 @@ __global__ void __launch_bounds__(256) fwd_reduce(Args a) {
   store8(a.aggC + (s * a.nchunks + j) * 8, c);
 }
 
-// h_{j+1} = P_j h_j P_j~ + c_j  (one thread per sequence)
-__global__ void __launch_bounds__(128) fwd_carry(Args a) {
-  const int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (s >= a.B * a.N) return;
-  float h[8];
-  if (a.h0) load8(h, a.h0 + s * 8);
-  else {
+// ------------------------------------------------------- carries, warp per sequence
+// The carry is a chain of links over the chunks of a sequence: forward h <- L(P_j) h + c_j
+// (j = 0 .. nchunks-2, from h0), backward H <- L(P_j)^T H + c'_j (j = nchunks-1 .. 1, from
+// zero).  A warp walks it in three phases instead of one thread walking every link:
+//   1. lane l composes its contiguous range of ~(nchunks-1)/32 links into one link
+//   2. an inclusive shuffle scan over the 32 lanes (5 levels) composes each lane's link
+//      after those of the lanes before it
+//   3. lane l takes its carry-in from lane l-1's prefix and replays its range, writing
+//      every carry
+// Forward composition, A then B: (P_B P_A, L(P_B) c_A + c_B).  Backward, with the map
+// H -> L(Q)^T H + c: A then B gives (Q_A Q_B, L(Q_B)^T c_A + c_B).  Each lane's aggregates
+// are read through a ring of CARRY_PF links in flight.
+constexpr int CARRY_PF = 4;
+
+template <bool REV>
+__device__ __forceinline__ void link_apply(const float (&q)[4], const float (&v)[8], float (&y)[8]) {
+  Ga3Map L;
+  ga3_sandwich_matrix(q[0], q[1], q[2], q[3], L);
+  if constexpr (REV) apply_LT(L, v, y);
+  else apply_L(L, v, y);
+}
+
+// (q, c) <- (q, c) after (p, cp): forward (q p, L(q) cp + c), backward (p q, L(q)^T cp + c)
+template <bool REV>
+__device__ __forceinline__ void compose_after(float (&q)[4], float (&c)[8], const float (&p)[4],
+                                              const float (&cp)[8]) {
+  float y[8], qn[4];
+  link_apply<REV>(q, cp, y);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) h[i] = 0.0f;
+  for (int i = 0; i < 8; ++i) c[i] += y[i];
+  if constexpr (REV) ga3_even_mul(p, q, qn);
+  else ga3_even_mul(q, p, qn);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) q[i] = qn[i];
+}
+
+template <bool REV>
+__global__ void __launch_bounds__(128) carry_warp(Args a) {
+  const int64_t s = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (s >= a.B * a.N) return;  // s is the same for the whole warp
+  const int64_t nch = a.nchunks, nl = nch - 1;
+  const int64_t per = (nl + 31) / 32;
+  const int64_t k0 = min(nl, lane * per), k1 = min(nl, k0 + per);
+  const float4* aggP = reinterpret_cast<const float4*>(a.aggP) + s * nch;
+  const float* aggC = a.aggC + s * nch * 8;
+  float* carry = a.carry + s * nch * 8;
+  // link k: forward chunk k -> carry k + 1; backward chunk nch-1-k -> carry nch-2-k
+  auto chunk_of = [&](int64_t k) { return REV ? nch - 1 - k : k; };
+  auto out_of = [&](int64_t k) { return REV ? nch - 2 - k : k + 1; };
+  float rp[CARRY_PF][4], rc[CARRY_PF][8];
+  auto fetch = [&](int64_t k, int u) {
+    const float4 q = aggP[chunk_of(k)];
+    rp[u][0] = q.x; rp[u][1] = q.y; rp[u][2] = q.z; rp[u][3] = q.w;
+    load8(rc[u], aggC + chunk_of(k) * 8);
+  };
+  auto prefetch = [&]() {
+#pragma unroll
+    for (int u = 0; u < CARRY_PF; ++u)
+      if (k0 + u < k1) fetch(k0 + u, u);
+  };
+  // 1. the lane's range as one link, from the identity
+  float q[4] = {1.0f, 0.0f, 0.0f, 0.0f}, c[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  prefetch();
+  for (int64_t kk = k0; kk < k1; kk += CARRY_PF) {
+#pragma unroll
+    for (int u = 0; u < CARRY_PF; ++u) {
+      const int64_t k = kk + u;
+      if (k >= k1) break;
+      float p[4], cp[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) p[i] = rp[u][i];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) cp[i] = rc[u][i];
+      if (k + CARRY_PF < k1) fetch(k + CARRY_PF, u);
+      // this link after the range so far: (p, c_k) after (q, c)
+      float y[8], qn[4];
+      link_apply<REV>(p, c, y);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) c[i] = y[i] + cp[i];
+      if constexpr (REV) ga3_even_mul(q, p, qn);
+      else ga3_even_mul(p, q, qn);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) q[i] = qn[i];
+    }
   }
-  store8(a.carry + (s * a.nchunks) * 8, h);
-  float4 Pn = a.nchunks > 1 ? reinterpret_cast<const float4*>(a.aggP)[s * a.nchunks] : make_float4(1, 0, 0, 0);
-  for (int64_t j = 0; j + 1 < a.nchunks; ++j) {
-    const float4 P = Pn;
-    float cv[8];
-    load8(cv, a.aggC + (s * a.nchunks + j) * 8);
-    if (j + 2 < a.nchunks) Pn = reinterpret_cast<const float4*>(a.aggP)[s * a.nchunks + j + 1];
-    Ga3Map L;
-    ga3_sandwich_matrix(P.x, P.y, P.z, P.w, L);
-    float y[8];
-    apply_L(L, h, y);
+  prefetch();  // the replay's first links are in flight during the scan
+  // 2. inclusive scan over the lanes
 #pragma unroll
-    for (int i = 0; i < 8; ++i) h[i] = y[i] + cv[i];
-    store8(a.carry + (s * a.nchunks + j + 1) * 8, h);
+  for (int d = 1; d < 32; d <<= 1) {
+    float pp[4], cp[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) pp[i] = __shfl_up_sync(0xffffffffu, q[i], d);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) cp[i] = __shfl_up_sync(0xffffffffu, c[i], d);
+    if (lane >= d) compose_after<REV>(q, c, pp, cp);
+  }
+  // 3. carry-in: the initial state through the links of lanes 0 .. l-1
+  float pe[4], ce[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) pe[i] = __shfl_up_sync(0xffffffffu, q[i], 1);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ce[i] = __shfl_up_sync(0xffffffffu, c[i], 1);
+  float h[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  const float* init = REV ? nullptr : a.h0;
+  if (init) load8(h, init + s * 8);
+  if (lane == 0) store8(carry + (REV ? nch - 1 : 0) * 8, h);
+  if (lane > 0) {
+    float y[8];
+    if (init) link_apply<REV>(pe, h, y);
+    else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) y[i] = 0.0f;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) h[i] = y[i] + ce[i];
+  }
+  for (int64_t kk = k0; kk < k1; kk += CARRY_PF) {
+#pragma unroll
+    for (int u = 0; u < CARRY_PF; ++u) {
+      const int64_t k = kk + u;
+      if (k >= k1) break;
+      float p[4], cp[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) p[i] = rp[u][i];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) cp[i] = rc[u][i];
+      if (k + CARRY_PF < k1) fetch(k + CARRY_PF, u);
+      float y[8];
+      link_apply<REV>(p, h, y);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) h[i] = y[i] + cp[i];
+      store8(carry + out_of(k) * 8, h);
+    }
   }
 }
 
@@ -202,25 +312,6 @@ __global__ void __launch_bounds__(256) bwd_reduce(Args a) {
   const int64_t s = b * a.N + n;
   reinterpret_cast<float4*>(a.aggP)[s * a.nchunks + j] = make_float4(P[0], P[1], P[2], P[3]);
   store8(a.aggC + (s * a.nchunks + j) * 8, g);
-}
-
-// H_{j-1} = L_{P_j}^T H_j + c'_j
-__global__ void __launch_bounds__(128) bwd_carry(Args a) {
-  const int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (s >= a.B * a.N) return;
-  float H[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  store8(a.carry + (s * a.nchunks + a.nchunks - 1) * 8, H);
-  for (int64_t j = a.nchunks - 1; j >= 1; --j) {
-    const float4 P = reinterpret_cast<const float4*>(a.aggP)[s * a.nchunks + j];
-    float cv[8], y[8];
-    load8(cv, a.aggC + (s * a.nchunks + j) * 8);
-    Ga3Map L;
-    ga3_sandwich_matrix(P.x, P.y, P.z, P.w, L);
-    apply_LT(L, H, y);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) H[i] = y[i] + cv[i];
-    store8(a.carry + (s * a.nchunks + j - 1) * 8, H);
-  }
 }
 
 __global__ void __launch_bounds__(256) bwd_apply(Args a) {
@@ -368,7 +459,7 @@ extern "C" int csn_ga3_scan_fwd(const float* gens, const float* dt, const float*
       ga3::fwd_reduce<<<ga3::blocks(total, 256), 256, 0, st>>>(a);
     }
     KernelTimer kt("ga3_fwd_carry", st);
-    ga3::fwd_carry<<<ga3::blocks(S, 128), 128, 0, st>>>(a);
+    ga3::carry_warp<false><<<ga3::blocks(S * 32, 128), 128, 0, st>>>(a);
   }
   {
     KernelTimer kt("ga3_fwd_apply", st);
@@ -412,7 +503,7 @@ extern "C" int csn_ga3_scan_bwd(const float* gens, const float* dt, const float*
       ga3::bwd_reduce<<<ga3::blocks(total, 256), 256, 0, st>>>(a);
     }
     KernelTimer kt("ga3_bwd_carry", st);
-    ga3::bwd_carry<<<ga3::blocks(S, 128), 128, 0, st>>>(a);
+    ga3::carry_warp<true><<<ga3::blocks(S * 32, 128), 128, 0, st>>>(a);
   }
   {
     KernelTimer kt("ga3_bwd_apply", st);

@@ -304,8 +304,12 @@ namespace {
 int64_t pick_chunk(int64_t S, int64_t T, int D) {
   // Enough (sequence, chunk) work items to fill 148 SMs at the residency each
   // family allows: D = 4 ~1024 threads / SM, D = 8 ~256 threads / SM (register
-  // bound), D = 16 ~16 warps / SM (one warp per chunk, shared-memory bound).
-  const int64_t target = (D == 16) ? 148 * 16 : (D == 8) ? 148 * 256 : 148 * 1024;
+  // bound, one wave).  D = 16 (one warp per chunk): the rotor-building reduce and the
+  // backward apply hold 12 warps / SM (registers), the other passes 16 to 28, so the
+  // plan asks for about 8 waves of 12 warps / SM: the last wave's tail then idles the SMs
+  // for ~1/8 of a pass instead of up to half of it (B16 L8192 C32: 5 chunks per sequence
+  // took 23.7 ms per step, 24-64 chunks 19.3-19.6 ms).
+  const int64_t target = (D == 16) ? 148 * 12 * 8 : (D == 8) ? 148 * 256 : 148 * 1024;
   int64_t chunk = (S * T + target - 1) / target;
   if (chunk < 8) chunk = 8;
   if (chunk > T) chunk = T > 0 ? T : 1;

@@ -845,25 +845,24 @@ def run_generation(args, ws, rank, local, cores):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     _lib.load()
-    g = ops.RotorStepGraph(B, N, D, steps=chunk, damped=True, device=dev)
-    gen = torch.Generator(device="cpu").manual_seed(0)
-    g.gens.copy_(torch.randn(chunk, B, N, 28, generator=gen) * 0.1)
-    g.dt.copy_(torch.rand(chunk, B, generator=gen) * 0.09 + 0.01)
-    g.gamma.copy_(torch.nn.functional.softplus(torch.randn(chunk, B, N, generator=gen)))
-    g.S.copy_(torch.randn(chunk, B, N, D, D, generator=gen))
-    for _ in range(max(3, args.warmup)):
-        g.replay()
-    torch.cuda.synchronize()
     reps = total // chunk
-    lat = []
+    # value: steps launched as an autoregressive loop must (each waits for the previous step);
+    # chained: the same graph with the next step's rotor built during the previous step, valid
+    # when the step inputs are staged ahead (RotorStepGraph's default)
+    lat, lat_chained = [], []
     with ClockSampler(local) as clk:
-        for _ in range(max(reps, args.steps)):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            g.replay()
-            e1.record()
-            e1.synchronize()
-            lat.append(e0.elapsed_time(e1) * 1e3 / chunk)
+        for chained, out in ((False, lat), (True, lat_chained)):
+            g = _gen_graph(B, N, D, chunk, dev, chained)
+            for _ in range(max(3, args.warmup)):
+                g.replay()
+            torch.cuda.synchronize()
+            for _ in range(max(reps, args.steps)):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                g.replay()
+                e1.record()
+                e1.synchronize()
+                out.append(e0.elapsed_time(e1) * 1e3 / chunk)
     p50 = float(np.median(lat))
     # eager: one launch per step from the host (includes the host launch path)
     eager = []
@@ -910,7 +909,10 @@ def run_generation(args, ws, rank, local, cores):
         "warmup": max(3, args.warmup), "ms_per_step": p50 / 1e3, "higher_is_better": False,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
         "tok_per_s": B / (p50 * 1e-6), "p50_eager_us": float(np.median(eager)),
-        "gpu_launches": len(lat) * chunk, "clocks": clk.summary(),
+        "p50_chained_us": float(np.median(lat_chained)),
+        "chained": "steps captured with csn_rotor_step_chained: each step's rotor is built while "
+                   "the previous step runs; valid when the step inputs are staged ahead",
+        "gpu_launches": (len(lat) + len(lat_chained)) * chunk, "clocks": clk.summary(),
         "e2e": {"value": float(np.median(e2e_lat)), "unit": "us", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": hout.numel() * 4,
                 "timing": "wall clock per token: pinned inputs to device, step, state to host"},
@@ -1271,6 +1273,19 @@ def measure_config(wl, dev, lib, steps=10, warmup=3):
     return res
 
 
+def _gen_graph(B, N, D, chunk, dev, chained):
+    """RotorStepGraph of the generation configuration with seeded inputs staged."""
+    import torch
+    from csn_b200 import ops
+    g = ops.RotorStepGraph(B, N, D, steps=chunk, damped=True, device=dev, chained=chained)
+    gen = torch.Generator(device="cpu").manual_seed(0)
+    g.gens.copy_(torch.randn(chunk, B, N, 28, generator=gen) * 0.1)
+    g.dt.copy_(torch.rand(chunk, B, generator=gen) * 0.09 + 0.01)
+    g.gamma.copy_(torch.nn.functional.softplus(torch.randn(chunk, B, N, generator=gen)))
+    g.S.copy_(torch.randn(chunk, B, N, D, D, generator=gen))
+    return g
+
+
 def measure_generation(dev, steps=2048, chunk=128):
     """p50 latency of one graph-replayed rotor step of the Cl(6,0) generation configuration
     (256 streams x 8 channels) and tokens/s."""
@@ -1278,26 +1293,25 @@ def measure_generation(dev, steps=2048, chunk=128):
     import torch
     from csn_b200 import ops
     B, N, D = 256, 8, 8
-    g = ops.RotorStepGraph(B, N, D, steps=chunk, damped=True, device=dev)
-    gen = torch.Generator(device="cpu").manual_seed(0)
-    g.gens.copy_(torch.randn(chunk, B, N, 28, generator=gen) * 0.1)
-    g.dt.copy_(torch.rand(chunk, B, generator=gen) * 0.09 + 0.01)
-    g.gamma.copy_(torch.nn.functional.softplus(torch.randn(chunk, B, N, generator=gen)))
-    g.S.copy_(torch.randn(chunk, B, N, D, D, generator=gen))
-    for _ in range(3):
-        g.replay()
-    torch.cuda.synchronize()
-    lat = []
-    for _ in range(steps // chunk):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        g.replay()
-        e1.record()
-        e1.synchronize()
-        lat.append(e0.elapsed_time(e1) * 1e3 / chunk)
-    p50 = float(np.median(lat))
+    p = {}
+    for chained in (False, True):
+        g = _gen_graph(B, N, D, chunk, dev, chained)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        lat = []
+        for _ in range(steps // chunk):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            g.replay()
+            e1.record()
+            e1.synchronize()
+            lat.append(e0.elapsed_time(e1) * 1e3 / chunk)
+        p[chained] = float(np.median(lat))
+    p50 = p[False]
     return {"metric": "rotor-step p50 latency (us), 256 streams x 8 channels Cl(6,0)", "value": p50,
-            "unit": "us", "tok_per_s": B / (p50 * 1e-6), "steps": steps, "higher_is_better": False,
+            "unit": "us", "tok_per_s": B / (p50 * 1e-6), "p50_chained_us": p[True], "steps": steps,
+            "higher_is_better": False,
             "config": {"workload": "cl6_generation_step", "streams": B, "channels": N, "matrix_dim": D,
                        "graph_steps": chunk, "damped": True}}
 

@@ -55,6 +55,7 @@ SIGNATURES = {
     "csn_rotor_scan_bwd_resume": ([_f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _f, _i64, _i64,
                                    _i64, _int, _int, _int, _f, _sz, _f], _int),
     "csn_rotor_step": ([_f, _f, _f, _f, _f, _i64, _i64, _int, _int, _int, _f], _int),
+    "csn_rotor_step_chained": ([_f, _f, _f, _f, _f, _i64, _i64, _int, _int, _int, _f], _int),
     "csn_cayley_fwd": ([_f, _f, _i64, _int, _f], _int),
     "csn_cayley_bwd": ([_f, _f, _f, _i64, _int, _f], _int),
     "csn_ga3_workspace_bytes": ([_i64, _i64, _i64], _sz),

@@ -429,9 +429,16 @@ class RotorStepGraph:
     Fill ``gens[t], dt[t], gamma[t], S[t]`` (leading step axis) and call ``replay()``: the
     state ``h`` advances `steps` tokens with one graph launch, i.e. without a host round
     trip per token.  Capture happens once, at construction.
+
+    ``chained`` (default): the steps are captured with csn_rotor_step_chained, so each step
+    builds its rotor while the previous step finishes (valid because every step input is in
+    place before replay()).  ``chained=False`` captures ordinary csn_rotor_step launches, each
+    waiting for the previous step to complete, as a decode loop whose inputs are produced
+    between steps must.
     """
 
-    def __init__(self, B, N, D, steps=1, damped=True, basis="triu", two_sided=True, device="cuda"):
+    def __init__(self, B, N, D, steps=1, damped=True, basis="triu", two_sided=True, device="cuda",
+                 chained=True):
         K = D * (D - 1) // 2 if basis == "triu" else (3 if D == 4 else 28)
         dev = torch.device(device)
         self.h = torch.zeros(B, N, D, D, device=dev)
@@ -449,9 +456,12 @@ class RotorStepGraph:
         torch.cuda.current_stream(dev).wait_stream(s)
         self.h.zero_()
         self.graph = torch.cuda.CUDAGraph()
+        # the step inputs are filled before replay() and no kernel in the graph writes them,
+        # so the steps may chain: each builds its rotor while the previous one finishes
+        entry = "csn_rotor_step_chained" if chained else "csn_rotor_step"
         with torch.cuda.graph(self.graph, stream=s):
             for t in range(steps):
-                _lib.call("csn_rotor_step", _ptr(self.gens[t]), _ptr(self.dt[t]),
+                _lib.call(entry, _ptr(self.gens[t]), _ptr(self.dt[t]),
                           _ptr(None if self.gamma is None else self.gamma[t]), _ptr(self.S[t]),
                           _ptr(self.h), B, N, D, *args, ctypes.c_void_p(s.cuda_stream))
 

@@ -297,7 +297,7 @@ int scan16_dispatch(const ScanArgs& a, int src, int basis, bool damped, bool two
 // Implemented in csn_scan8.cu (staged D = 8 fused rotor kernels).
 int scan8_rotor_dispatch(const ScanArgs& a, bool damped, bool two, bool bwd, cudaStream_t st);
 int scan8_rotor_step(const float* gens, const float* dt, const float* gamma, const float* S, float* h,
-                     int64_t B, int64_t N, bool two, cudaStream_t st);
+                     int64_t B, int64_t N, bool two, bool chained, cudaStream_t st);
 
 namespace {
 
@@ -817,14 +817,15 @@ extern "C" int csn_rotor_scan_fwd_noalloc(const float* gens, const float* dt, co
 // (one-sided: M h + C), with (M, C) built from this step's generators, dt, gamma and S.
 // This is the T = 1 case of the fused scan with h0 = h; a single-chunk plan needs no
 // scratch, so the call allocates nothing and launches one kernel.
-extern "C" int csn_rotor_step(const float* gens, const float* dt, const float* gamma,
-                              const float* S, float* h, int64_t B, int64_t N, int D, int basis,
-                              int two_sided, void* stream) {
+static int rotor_step_impl(const float* gens, const float* dt, const float* gamma, const float* S,
+                           float* h, int64_t B, int64_t N, int D, int basis, int two_sided,
+                           bool chained, void* stream) {
   if (int rc = rotor_common_checks(gens, dt, S, B, 1, N, D, basis)) return rc;
   if (B * N == 0) return CSN_OK;
   if (!h || !aligned16(h)) return set_error(CSN_ERR_INVALID, "csn_rotor_step: h missing or misaligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (D == 8 && basis == BASIS_TRIU) return scan8_rotor_step(gens, dt, gamma, S, h, B, N, two_sided != 0, st);
+  if (D == 8 && basis == BASIS_TRIU)
+    return scan8_rotor_step(gens, dt, gamma, S, h, B, N, two_sided != 0, chained, st);
   Plan p = make_plan(B, 1, N, D, false);
   ScanArgs a{};
   a.gens = gens; a.dt = dt; a.gamma = gamma; a.S = S; a.h0 = h; a.out = h;
@@ -832,6 +833,23 @@ extern "C" int csn_rotor_step(const float* gens, const float* dt, const float* g
   bind_ws(a, p, nullptr, D);
   if (D == 16) return scan16_dispatch(a, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, false, st);
   return dispatch(a, D, SRC_ROTOR, basis, gamma != nullptr, two_sided != 0, false, st);
+}
+
+extern "C" int csn_rotor_step(const float* gens, const float* dt, const float* gamma,
+                              const float* S, float* h, int64_t B, int64_t N, int D, int basis,
+                              int two_sided, void* stream) {
+  return rotor_step_impl(gens, dt, gamma, S, h, B, N, D, basis, two_sided, false, stream);
+}
+
+// The same step for a chain of steps on one stream whose inputs are all in place before the
+// chain starts (a captured decode loop): D = 8 with the triu basis launches with programmatic
+// stream serialization, so each step builds its rotor while the previous step finishes and
+// reads the state only once that step has completed.  Other D and bases launch as
+// csn_rotor_step does.
+extern "C" int csn_rotor_step_chained(const float* gens, const float* dt, const float* gamma,
+                                      const float* S, float* h, int64_t B, int64_t N, int D,
+                                      int basis, int two_sided, void* stream) {
+  return rotor_step_impl(gens, dt, gamma, S, h, B, N, D, basis, two_sided, true, stream);
 }
 
 // ======================================================= sequence-parallel shard aggregates

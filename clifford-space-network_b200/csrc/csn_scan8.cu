@@ -989,12 +989,18 @@ int run8(const ScanArgs& a, bool bwd, cudaStream_t st) {
 // so a step equals the scan's step.
 constexpr int STEP_THREADS = 128;
 
-template <bool DAMPED, bool TWO>
+// CHAINED: launched with programmatic stream serialization after another step: the kernel
+// lets the next step launch at once, builds its rotor (which reads only this step's
+// generators, dt, gamma and S) while the previous step is still running, and reads the state
+// only after griddepcontrol.wait, i.e. after the previous grid has completed and its writes
+// are visible.  The inputs must therefore not be written by the kernel launched before it.
+template <bool DAMPED, bool TWO, bool CHAINED>
 __global__ void __launch_bounds__(STEP_THREADS) step8_kernel(const float* __restrict__ gens,
                                                              const float* __restrict__ dt,
                                                              const float* __restrict__ gamma,
                                                              const float* __restrict__ S,
                                                              float* h, int64_t B, int64_t N) {
+  if constexpr (CHAINED) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __shared__ __align__(16) float sX[STEP_THREADS / 8][DD];
   __shared__ __align__(16) float sM[STEP_THREADS / 8][DD];
   const int r = threadIdx.x & 7;
@@ -1008,7 +1014,7 @@ __global__ void __launch_bounds__(STEP_THREADS) step8_kernel(const float* __rest
   // latency overlaps the Cayley inverse
   float xr[8], sr[8];
   if (active) {
-    lds_row(xr, h + e * DD + 8 * r);  // generic load: h is read and written here
+    if constexpr (!CHAINED) lds_row(xr, h + e * DD + 8 * r);  // generic load: h is read and written here
     const float4* sp = reinterpret_cast<const float4*>(S + e * DD + 8 * r);
     const float4 s0 = __ldg(sp), s1 = __ldg(sp + 1);
     sr[0] = s0.x; sr[1] = s0.y; sr[2] = s0.z; sr[3] = s0.w;
@@ -1061,6 +1067,10 @@ __global__ void __launch_bounds__(STEP_THREADS) step8_kernel(const float* __rest
   }
 #pragma unroll
   for (int c = 0; c < 8; ++c) row[c] = sa * fmaf(2.0f, row[c], (c == r) ? 1.0f : 0.0f);
+  if constexpr (CHAINED) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // the previous step's state is complete
+    if (active) lds_row(xr, h + e * DD + 8 * r);
+  }
   sts_row(&sX[grp][8 * r], xr);
   sts_row(&sM[grp][8 * r], row);
   __syncwarp();
@@ -1098,12 +1108,27 @@ __global__ void __launch_bounds__(STEP_THREADS) step8_kernel(const float* __rest
 
 template <bool DAMPED, bool TWO>
 int run_step8(const float* gens, const float* dt, const float* gamma, const float* S, float* h,
-              int64_t B, int64_t N, cudaStream_t st) {
+              int64_t B, int64_t N, bool chained, cudaStream_t st) {
   const int64_t states = B * N;
   const unsigned grid = (unsigned)((states + STEP_THREADS / 8 - 1) / (STEP_THREADS / 8));
   KernelTimer kt("rotor_step", st);
-  step8_kernel<DAMPED, TWO><<<grid, STEP_THREADS, 0, st>>>(gens, dt, gamma, S, h, B, N);
-  return check_launch("rotor step (D=8)");
+  if (!chained) {
+    step8_kernel<DAMPED, TWO, false><<<grid, STEP_THREADS, 0, st>>>(gens, dt, gamma, S, h, B, N);
+    return check_launch("rotor step (D=8)");
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(STEP_THREADS);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t err = cudaLaunchKernelEx(&cfg, step8_kernel<DAMPED, TWO, true>, gens, dt, gamma, S, h, B, N);
+  if (err != cudaSuccess) return set_cuda_error(err, "rotor step (D=8, chained): cudaLaunchKernelEx");
+  return check_launch("rotor step (D=8, chained)");
 }
 
 }  // namespace s8
@@ -1115,12 +1140,12 @@ int scan8_rotor_dispatch(const ScanArgs& a, bool damped, bool two, bool bwd, cud
 }
 
 int scan8_rotor_step(const float* gens, const float* dt, const float* gamma, const float* S, float* h,
-                     int64_t B, int64_t N, bool two, cudaStream_t st) {
+                     int64_t B, int64_t N, bool two, bool chained, cudaStream_t st) {
   using namespace s8;
-  if (gamma) return two ? run_step8<true, true>(gens, dt, gamma, S, h, B, N, st)
-                        : run_step8<true, false>(gens, dt, gamma, S, h, B, N, st);
-  return two ? run_step8<false, true>(gens, dt, gamma, S, h, B, N, st)
-             : run_step8<false, false>(gens, dt, gamma, S, h, B, N, st);
+  if (gamma) return two ? run_step8<true, true>(gens, dt, gamma, S, h, B, N, chained, st)
+                        : run_step8<true, false>(gens, dt, gamma, S, h, B, N, chained, st);
+  return two ? run_step8<false, true>(gens, dt, gamma, S, h, B, N, chained, st)
+             : run_step8<false, false>(gens, dt, gamma, S, h, B, N, chained, st);
 }
 
 }  // namespace csn

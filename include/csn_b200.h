@@ -227,6 +227,16 @@ int csn_rotor_scan_bwd_resume(const float* gens, const float* dt, const float* g
 int csn_rotor_step(const float* gens, const float* dt, const float* gamma, const float* S, float* h,
                    int64_t B, int64_t N, int D, int basis, int two_sided, void* stream);
 
+/* csn_rotor_step for a chain of steps on one stream (a captured decode loop), same arguments
+ * and result.  For D = 8, triu basis, the kernel is launched with programmatic stream
+ * serialization: it builds its rotor while the kernel before it on the stream is still running
+ * and reads h only after that kernel has completed.  Contract: gens, dt, gamma and S of the
+ * step must not be written by the kernel launched just before it on the stream (they are in
+ * place before the chain starts); h may be.  Other D and bases launch as csn_rotor_step. */
+int csn_rotor_step_chained(const float* gens, const float* dt, const float* gamma, const float* S,
+                           float* h, int64_t B, int64_t N, int D, int basis, int two_sided,
+                           void* stream);
+
 /* -------------------------------------------------------------------- Cayley */
 /* Q = (I - Omega)^{-1} (I + Omega) for `count` skew D x D matrices.
  * Replaces cayley_rotor_8x8 (python/clifford_cl6.py:57) and cayley_rotor_16x16 /

@@ -83,9 +83,12 @@ def test_d8_step_ragged_state_counts_match_oracle_and_scan(ops, oracle, B, N, da
     assert rel(h, X[:, 0]) < 1e-6
 
 
-def test_step_graph_matches_step_loop(ops):
+@pytest.mark.parametrize("chained", [True, False])
+def test_step_graph_matches_step_loop(ops, chained):
+    """A captured chain of steps (chained: each step's rotor built while the previous step
+    runs, the state read after it completes) equals the same steps launched one by one."""
     B, N, D, steps = 256, 8, 8, 64
-    g = ops.RotorStepGraph(B, N, D, steps=steps, damped=True)
+    g = ops.RotorStepGraph(B, N, D, steps=steps, damped=True, chained=chained)
     gen = torch.Generator(device="cpu").manual_seed(0)
     g.gens.copy_(torch.randn(steps, B, N, 28, generator=gen) * 0.1)
     g.dt.copy_(torch.rand(steps, B, generator=gen) * 0.09 + 0.01)

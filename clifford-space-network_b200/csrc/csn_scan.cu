@@ -19,6 +19,7 @@
 // The backward pass is the mirror image in reverse time with transitions M^T
 // (G_t = dX_t + M_{t+1}^T G_{t+1} M_{t+1}), chunk aggregates (P_j, c'_j) where
 // H_{j-1} = P_j^T H_j P_j + c'_j, and an apply pass that emits the gradients.
+#include <algorithm>
 #include <climits>
 #include <cstdio>
 #include <mutex>
@@ -301,15 +302,37 @@ int scan8_rotor_step(const float* gens, const float* dt, const float* gamma, con
 
 namespace {
 
+// D = 16 (one warp per chunk): the rotor-building reduce and the backward apply hold 12 warps
+// per SM (registers), so a pass over S sequences cut into n chunks takes about
+// ceil(S n / (148 * 12)) waves of one chunk each; more than one chunk adds the reduce pass
+// (about as long as the apply pass) and the carry.  The chunk count minimises
+//   waves(n) * (chunk(n) + 4) * (n > 1 ? 2 : 1) + (n > 1 ? 32 : 0)
+// (4 steps' worth of per-chunk set-up, 32 for the extra launches): long sequences get
+// enough chunks that the last wave's tail idles the SMs for a small part of a pass (B16
+// L8192 C32: 38 chunks; 5 chunks took 23.7 ms per step, 24 - 64 chunks 19.3 - 19.6 ms),
+// while many short sequences that already fill the SMs stay in one chunk (no reduce pass).
+static int64_t pick_chunk16(int64_t S, int64_t T) {
+  const int64_t slots = 148 * 12;
+  const int64_t n_max = std::max<int64_t>(1, std::min<int64_t>(T / 8, (16 * slots + S - 1) / std::max<int64_t>(S, 1)));
+  int64_t best_chunk = T, best_cost = -1;
+  for (int64_t n = 1; n <= n_max; ++n) {
+    const int64_t chunk = std::max<int64_t>(8, (T + n - 1) / n);
+    const int64_t nn = (T + chunk - 1) / chunk;
+    const int64_t waves = (S * nn + slots - 1) / slots;
+    const int64_t cost = waves * (chunk + 4) * (nn > 1 ? 2 : 1) + (nn > 1 ? 32 : 0);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best_chunk = chunk;
+    }
+  }
+  return std::min<int64_t>(best_chunk, T);
+}
+
 int64_t pick_chunk(int64_t S, int64_t T, int D) {
-  // Enough (sequence, chunk) work items to fill 148 SMs at the residency each
-  // family allows: D = 4 ~1024 threads / SM, D = 8 ~256 threads / SM (register
-  // bound, one wave).  D = 16 (one warp per chunk): the rotor-building reduce and the
-  // backward apply hold 12 warps / SM (registers), the other passes 16 to 28, so the
-  // plan asks for about 8 waves of 12 warps / SM: the last wave's tail then idles the SMs
-  // for ~1/8 of a pass instead of up to half of it (B16 L8192 C32: 5 chunks per sequence
-  // took 23.7 ms per step, 24-64 chunks 19.3-19.6 ms).
-  const int64_t target = (D == 16) ? 148 * 12 * 8 : (D == 8) ? 148 * 256 : 148 * 1024;
+  if (D == 16) return T > 0 ? pick_chunk16(S, T) : 1;
+  // Enough (sequence, chunk) work items to fill 148 SMs at the residency each family
+  // allows: D = 4 ~1024 threads / SM, D = 8 ~256 threads / SM (register bound, one wave).
+  const int64_t target = (D == 8) ? 148 * 256 : 148 * 1024;
   int64_t chunk = (S * T + target - 1) / target;
   if (chunk < 8) chunk = 8;
   if (chunk > T) chunk = T > 0 ? T : 1;

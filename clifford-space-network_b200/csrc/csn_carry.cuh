@@ -54,8 +54,20 @@ static __global__ void reduce_channels_kernel(const float* __restrict__ part, fl
                                        int64_t BT, int64_t N) {
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (i >= BT) return;
+  const float* p = part + i * N;
   float s = 0.0f;
-  for (int64_t n = 0; n < N; ++n) s += part[i * N + n];
+  if ((N & 3) == 0 && (reinterpret_cast<uintptr_t>(p) & 15u) == 0) {
+    // the same left-to-right sum from 16-byte loads
+    for (int64_t n = 0; n < N; n += 4) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(p + n));
+      s += v.x;
+      s += v.y;
+      s += v.z;
+      s += v.w;
+    }
+  } else {
+    for (int64_t n = 0; n < N; ++n) s += p[n];
+  }
   out[i] = s;
 }
 

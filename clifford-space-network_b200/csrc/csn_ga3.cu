@@ -49,19 +49,26 @@ __device__ __forceinline__ void store8_cs(float* __restrict__ p, const float (&v
   __stcs(reinterpret_cast<float4*>(p) + 1, make_float4(v[4], v[5], v[6], v[7]));
 }
 
-// Rotor of step (g, dt); also returns Om and w = |Om|^2 for the backward pass.
-__device__ __forceinline__ void rotor(const float* __restrict__ g, float dtv, float (&r)[4],
-                                      float (&om)[3], float& w) {
+// Rotor of step (g, dt) from the generator values; also returns Om and w = |Om|^2 for the
+// backward pass.
+__device__ __forceinline__ void rotor_vals(const float (&g)[3], float dtv, float (&r)[4], float (&om)[3],
+                                           float& w) {
   const float hh = 0.5f * dtv;
-  om[0] = hh * __ldg(g);
-  om[1] = hh * __ldg(g + 1);
-  om[2] = hh * __ldg(g + 2);
+  om[0] = hh * g[0];
+  om[1] = hh * g[1];
+  om[2] = hh * g[2];
   w = om[0] * om[0] + om[1] * om[1] + om[2] * om[2];
   const float inv = 1.0f / (1.0f + w);
   r[0] = 1.0f - 2.0f * w * inv;  // (1 - w) / (1 + w), rounded once near 1
   r[1] = 2.0f * om[0] * inv;
   r[2] = 2.0f * om[1] * inv;
   r[3] = 2.0f * om[2] * inv;
+}
+// the same from the generators in memory
+__device__ __forceinline__ void rotor(const float* __restrict__ g, float dtv, float (&r)[4],
+                                      float (&om)[3], float& w) {
+  const float gv[3] = {__ldg(g), __ldg(g + 1), __ldg(g + 2)};
+  rotor_vals(gv, dtv, r, om, w);
 }
 
 // y = L x   and   y = L^T x   for the sandwich map L
@@ -98,14 +105,27 @@ __global__ void __launch_bounds__(256) fwd_reduce(Args a) {
   coords(a, tid, b, n, j);
   const int64_t t0 = j * a.chunk, t1 = min(a.T, t0 + a.chunk);
   float P[4] = {1.0f, 0.0f, 0.0f, 0.0f}, c[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  for (int64_t t = t0; t < t1; ++t) {
+  // the next step's inputs are loaded while this step is computed (the pass reads 44 bytes per
+  // step and does little arithmetic on them: without the overlap it waits on every load)
+  float gn[3], dn = 0.0f, xn[8];
+  auto fetch = [&](int64_t t) {
     const int64_t e = (b * a.T + t) * a.N + n;
-    float r[4], om[3], w, y[8], xv[8];
-    rotor(a.gens + e * 3, __ldg(a.dt + b * a.T + t), r, om, w);
+    gn[0] = __ldg(a.gens + e * 3); gn[1] = __ldg(a.gens + e * 3 + 1); gn[2] = __ldg(a.gens + e * 3 + 2);
+    dn = __ldg(a.dt + b * a.T + t);
+    load8(xn, a.x + e * 8);
+  };
+  if (t0 < t1) fetch(t0);
+  for (int64_t t = t0; t < t1; ++t) {
+    float g[3] = {gn[0], gn[1], gn[2]}, xv[8];
+    const float dtv = dn;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) xv[i] = xn[i];
+    if (t + 1 < t1) fetch(t + 1);
+    float r[4], om[3], w, y[8];
+    rotor_vals(g, dtv, r, om, w);
     Ga3Map L;
     ga3_sandwich_matrix(r[0], r[1], r[2], r[3], L);
     apply_L(L, c, y);
-    load8(xv, a.x + e * 8);
 #pragma unroll
     for (int i = 0; i < 8; ++i) c[i] = y[i] + xv[i];
     float Pn[4];
@@ -292,13 +312,24 @@ __global__ void __launch_bounds__(256) bwd_reduce(Args a) {
   if (j == 0) return;
   const int64_t t0 = j * a.chunk, t1 = min(a.T, t0 + a.chunk);
   float P[4] = {1.0f, 0.0f, 0.0f, 0.0f}, g[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  for (int64_t t = t1 - 1; t >= t0; --t) {
+  float gn[3], dn = 0.0f, vn[8];  // next step's inputs, loaded a step ahead
+  auto fetch = [&](int64_t t) {
     const int64_t e = (b * a.T + t) * a.N + n;
-    float r[4], om[3], w, dv[8], y[8];
-    rotor(a.gens + e * 3, __ldg(a.dt + b * a.T + t), r, om, w);
+    gn[0] = __ldg(a.gens + e * 3); gn[1] = __ldg(a.gens + e * 3 + 1); gn[2] = __ldg(a.gens + e * 3 + 2);
+    dn = __ldg(a.dt + b * a.T + t);
+    load8(vn, a.dh + e * 8);
+  };
+  if (t0 < t1) fetch(t1 - 1);
+  for (int64_t t = t1 - 1; t >= t0; --t) {
+    float gg[3] = {gn[0], gn[1], gn[2]}, dv[8];
+    const float dtv = dn;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) dv[i] = vn[i];
+    if (t - 1 >= t0) fetch(t - 1);
+    float r[4], om[3], w, y[8];
+    rotor_vals(gg, dtv, r, om, w);
     Ga3Map L;
     ga3_sandwich_matrix(r[0], r[1], r[2], r[3], L);
-    load8(dv, a.dh + e * 8);
 #pragma unroll
     for (int i = 0; i < 8; ++i) dv[i] += g[i];
     apply_LT(L, dv, y);

@@ -492,6 +492,21 @@ __device__ __forceinline__ void stage_gens(float* gs, const float (&gr)[(K + 31)
   __syncwarp();
 }
 
+// dt, gamma and the decay scalars of element e at time t (the rotor itself comes from the cache).
+template <bool DAMPED>
+__device__ __forceinline__ void rotor_scalars(const ScanArgs& a, const Warp& w, int64_t e, int64_t t,
+                                              float& alpha, float& sa, float& dtv, float& gam) {
+  dtv = __ldg(a.dt + dt_index(a, w.b, tphys(a, t), w.n));
+  if constexpr (DAMPED) {
+    gam = __ldg(a.gamma + e);
+    alpha = 1.0f / (1.0f + expf(gam * dtv));
+    sa = sqrtf(alpha);
+  } else {
+    gam = 0.0f;
+    alpha = sa = 1.0f;
+  }
+}
+
 // The step matrix M (Cayley rotor or a given M) of element e at time t.
 // CIN: the rotors come from the cache a.Mc_in (a compile-time choice, so the kernels that
 // load them carry none of the registers of the rotor build).
@@ -548,18 +563,37 @@ __global__ void __launch_bounds__(128) fwd16_kernel(ScanArgs a) {
     d_zero(X);
   }
   float gr[KR];
-  if (SRC == SRC_ROTOR && w.t0 < w.t1) fetch_gens<K>(gr, a.gens, elem(a, w.b, w.t0, w.n), lane);
+  if (SRC == SRC_ROTOR && !CIN && w.t0 < w.t1) fetch_gens<K>(gr, a.gens, elem(a, w.b, w.t0, w.n), lane);
+  // cached rotors: the next step's rotor and injection are loaded a step ahead
+  F16 Mn, Cn;
+  if constexpr (CIN) {
+    if (w.t0 < w.t1) {
+      const int64_t e0 = elem(a, w.b, w.t0, w.n);
+      f_load(Mn, a.Mc_in + e0 * DD, lane);
+      f_load(Cn, a.S + e0 * DD, lane);
+    }
+  }
   for (int64_t t = w.t0; t < w.t1; ++t) {
     const int64_t e = elem(a, w.b, t, w.n);
-    F16 Cin;
-    f_load(Cin, (SRC == SRC_MC ? a.C : a.S) + e * DD, lane);
-    if constexpr (SRC == SRC_ROTOR) {
-      stage_gens<K>(w.gs, gr, lane);
-      if (t + 1 < w.t1) fetch_gens<K>(gr, a.gens, elem(a, w.b, t + 1, w.n), lane);
-    }
-    F16 M;
+    F16 Cin, M;
     float alpha, sa, dtv, gam;
-    step_matrix<SRC, BASIS, DAMPED, K, CIN>(a, w, terms, e, t, M, alpha, sa, dtv, gam);
+    if constexpr (CIN) {
+      Cin = Cn;
+      M = Mn;
+      if (t + 1 < w.t1) {
+        const int64_t e1 = elem(a, w.b, t + 1, w.n);
+        f_load(Mn, a.Mc_in + e1 * DD, lane);
+        f_load(Cn, a.S + e1 * DD, lane);
+      }
+      rotor_scalars<DAMPED>(a, w, e, t, alpha, sa, dtv, gam);
+    } else {
+      f_load(Cin, (SRC == SRC_MC ? a.C : a.S) + e * DD, lane);
+      if constexpr (SRC == SRC_ROTOR) {
+        stage_gens<K>(w.gs, gr, lane);
+        if (t + 1 < w.t1) fetch_gens<K>(gr, a.gens, elem(a, w.b, t + 1, w.n), lane);
+      }
+      step_matrix<SRC, BASIS, DAMPED, K, CIN>(a, w, terms, e, t, M, alpha, sa, dtv, gam);
+    }
     const float cs = (SRC == SRC_ROTOR && DAMPED) ? (1.0f - alpha) : 1.0f;
     const F16D Md = to_d(M);
     F16D V;
@@ -596,27 +630,44 @@ __global__ void __launch_bounds__(128, 4) bwd16_reduce_kernel(ScanArgs a) {
   d_zero(Gc);
   P = d_identity(lane);
   float gr[KR];
-  if (SRC == SRC_ROTOR && w.t0 < w.t1) fetch_gens<K>(gr, a.gens, elem(a, w.b, w.t1 - 1, w.n), lane);
+  if (SRC == SRC_ROTOR && !CIN && w.t0 < w.t1) fetch_gens<K>(gr, a.gens, elem(a, w.b, w.t1 - 1, w.n), lane);
+  // cached rotors: the next step's M^T (read transposed from the cache) and dX a step ahead
+  F16 Mtn, dXn;
+  if constexpr (CIN) {
+    if (w.t0 < w.t1) {
+      const int64_t e0 = elem(a, w.b, w.t1 - 1, w.n);
+      f_load_t(Mtn, a.Mc_in + e0 * DD, lane);
+      f_load(dXn, a.dX + e0 * DD, lane);
+    }
+  }
   for (int64_t t = w.t1 - 1; t >= w.t0; --t) {
     const int64_t e = elem(a, w.b, t, w.n);
-    F16 dX;
-    f_load(dX, a.dX + e * DD, lane);
-    if constexpr (SRC == SRC_ROTOR) {
-      stage_gens<K>(w.gs, gr, lane);
-      if (t - 1 >= w.t0) fetch_gens<K>(gr, a.gens, elem(a, w.b, t - 1, w.n), lane);
-    }
-    F16 M;
-    float alpha, sa, dtv, gam;
-    step_matrix<SRC, BASIS, DAMPED, K, CIN>(a, w, terms, e, t, M, alpha, sa, dtv, gam);
-    F16 Mt;
-    // M in memory (a given M, or the cached rotor): read it transposed instead of a product
-    const float* mem_m = (SRC == SRC_MC) ? a.M : a.Mc_in;
-    if (mem_m) {
-      f_load_t(Mt, mem_m + e * DD, lane);
+    F16 dX, Mt;
+    if constexpr (CIN) {
+      dX = dXn;
+      Mt = Mtn;
+      if (t - 1 >= w.t0) {
+        const int64_t e1 = elem(a, w.b, t - 1, w.n);
+        f_load_t(Mtn, a.Mc_in + e1 * DD, lane);
+        f_load(dXn, a.dX + e1 * DD, lane);
+      }
     } else {
-      F16S Ms;
-      split(Ms, M);
-      transpose(Mt, Ms, lane);
+      f_load(dX, a.dX + e * DD, lane);
+      if constexpr (SRC == SRC_ROTOR) {
+        stage_gens<K>(w.gs, gr, lane);
+        if (t - 1 >= w.t0) fetch_gens<K>(gr, a.gens, elem(a, w.b, t - 1, w.n), lane);
+      }
+      F16 M;
+      float alpha, sa, dtv, gam;
+      step_matrix<SRC, BASIS, DAMPED, K, CIN>(a, w, terms, e, t, M, alpha, sa, dtv, gam);
+      // M in memory (a given M): read it transposed instead of a product
+      if (SRC == SRC_MC) {
+        f_load_t(Mt, a.M + e * DD, lane);
+      } else {
+        F16S Ms;
+        split(Ms, M);
+        transpose(Mt, Ms, lane);
+      }
     }
     const F16D Mtd = to_d(Mt);
     d_axpy(Gc, 1.0f, dX);  // G = g + dX

@@ -83,14 +83,17 @@ def test_d8_step_ragged_state_counts_match_oracle_and_scan(ops, oracle, B, N, da
     assert rel(h, X[:, 0]) < 1e-6
 
 
+@pytest.mark.parametrize("D", [4, 8, 16])
 @pytest.mark.parametrize("chained", [True, False])
-def test_step_graph_matches_step_loop(ops, chained):
+def test_step_graph_matches_step_loop(ops, chained, D):
     """A captured chain of steps (chained: each step's rotor built while the previous step
-    runs, the state read after it completes) equals the same steps launched one by one."""
-    B, N, D, steps = 256, 8, 8, 64
+    runs, the state read after it completes; for D = 4 and 16 the chained entry point launches
+    as the plain one) equals the same steps launched one by one."""
+    B, N, steps = (256, 8, 64) if D == 8 else (16, 4, 16)
+    K = D * (D - 1) // 2
     g = ops.RotorStepGraph(B, N, D, steps=steps, damped=True, chained=chained)
     gen = torch.Generator(device="cpu").manual_seed(0)
-    g.gens.copy_(torch.randn(steps, B, N, 28, generator=gen) * 0.1)
+    g.gens.copy_(torch.randn(steps, B, N, K, generator=gen) * 0.1)
     g.dt.copy_(torch.rand(steps, B, generator=gen) * 0.09 + 0.01)
     g.gamma.copy_(torch.rand(steps, B, N, generator=gen))
     g.S.copy_(torch.randn(steps, B, N, D, D, generator=gen))

@@ -935,7 +935,8 @@ def run_lm_train(args, ws, rank, local, cores):
     if args.impl == "reference":
         if rank == 0:
             print(json.dumps({"impl": "reference", "unavailable": "the reference LM is PyTorch source that "
-                              "is not on the GPU box; its scan is timed by the cl6_lm workload"}), flush=True)
+                              "is not installed where the bench runs; its scan is timed by the cl6_lm "
+                              "workload"}), flush=True)
         return 0
     import torch
     from csn_b200 import _lib, graphs

@@ -419,6 +419,9 @@ class Cl3:
             "ga3_bwd_reduce": 4.0 * (8 + 3 + 1.0 / N),
             "ga3_bwd_apply": 4.0 * (8 + 8 + 3 + 1.0 / N + 8 + 3 + 1),
         }
+        # DRAM bytes per element of the backward apply, measured with ncu (dram__bytes.sum.per_second
+        # x gpu__time_duration.sum) on this kernel at B4 L65536 C16: 494.0 MB for 4,194,304 elements
+        self.kernel_traffic = {"ga3_bwd_apply": 494.0e6 / 4194304}
         self.kernel_names = ["ga3_fwd_reduce", "ga3_fwd_carry", "ga3_fwd_apply", "ga3_bwd_reduce",
                              "ga3_bwd_carry", "ga3_bwd_apply", "ga3_reduce_channels"]
         self.elems_per_step = self.B * self.T * N
@@ -502,6 +505,10 @@ class Cl8:
             "bwd_reduce": 4.0 * (n + k + 1.0 / N),
             "bwd_apply": 4.0 * (3 * n + 2 * k + 2.0 / N + 1),
         }
+        # DRAM bytes per element of the backward apply, measured with ncu (dram__bytes_read.sum +
+        # dram__bytes_write.sum) at B2 L8192 C32: 1684.2 MB + 575.9 MB for 524,288 elements (the
+        # cached rotor, 1 KB per element, is the part above the algorithmic bytes)
+        self.kernel_traffic = {"bwd_apply": 2260.1e6 / 524288}
         self.kernel_names = ["fwd_reduce", "fwd_carry", "fwd_apply", "bwd_reduce", "bwd_carry",
                              "bwd_apply", "reduce_channels"]
         self.elems_per_step = self.B * self.T * N
@@ -1262,7 +1269,9 @@ def measure_config(wl, dev, lib, steps=10, warmup=3):
     res = {"metric": METRIC, "value": wl.elems_per_step / (ms * 1e-3) / 1e9, "unit": UNIT,
            "ms_per_step": ms, "steps": steps, "warmup": warmup, "config": wl.config,
            "roofline": {"bound": "hbm", "kernel": dom, "achieved": ach, "peak": hbm, "unit": "GB/s",
-                        "frac": ach / hbm, "peak_kind": peak_kind, "avg_launch_ms": dom_ms},
+                        "frac": ach / hbm, "peak_kind": peak_kind, "avg_launch_ms": dom_ms,
+                        "traffic": (wl.kernel_traffic[dom] * per_launch
+                                    if dom in getattr(wl, "kernel_traffic", {}) else None)},
            "op_roofline": {"achieved": op, "peak": hbm, "unit": "GB/s", "frac": op / hbm,
                            "bytes_per_elem": wl.op_bytes},
            "kernel_ms_per_step": {n: t / steps for n, (t, c) in kt.items() if c},

@@ -29,7 +29,6 @@
 namespace csn {
 namespace s8 {
 
-constexpr int D = 8;
 constexpr int DD = 64;
 constexpr int K = 28;  // so(8) generators, reference triu layout
 constexpr int THREADS = 128;

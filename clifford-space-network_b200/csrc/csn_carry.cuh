@@ -577,6 +577,71 @@ __global__ void __launch_bounds__(32 * CARRY8_MAX_WARPS) carry8_mma_kernel(ScanA
   walk(std::integral_constant<bool, false>{}, m, unused);
 }
 
+// Shard aggregate of one sequence from its chunk aggregates (the compose_kernel contract):
+// forward (P, c) <- (P_j P, P_j c P_j^T + c_j) over j = 0 .. nchunks-1 from (I, 0), written to
+// P_out (if set) and c_out; backward H <- P_j^T H P_j + c'_j over j = nchunks-1 .. 0 from 0,
+// written to c_out.  Phases 1 and 2 of carry8_mma_kernel over all nchunks links; the last
+// warp's inclusive prefix is the whole composition.
+template <bool TWO, bool REVERSE>
+__global__ void __launch_bounds__(32 * CARRY8_MAX_WARPS) compose8_mma_kernel(ScanArgs a) {
+  using namespace carry8;
+  constexpr int DD = 64;
+  extern __shared__ __align__(16) double c8_smem[];
+  const int nw = blockDim.x >> 5, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = lane >> 2, c = lane & 3;
+  const int64_t s = blockIdx.x;
+  const int64_t nch = a.nchunks, nl = nch;
+  const int64_t base = s * nch;
+  double* gG = c8_smem;
+  double* gC = c8_smem + (size_t)nw * DD;
+  const int64_t per = (nl + nw - 1) / nw;
+  const int64_t k0 = min(nl, (int64_t)w * per), k1 = min(nl, k0 + per);
+  Frag m = zero(), T = identity(r, c);
+  for (int64_t k = k0; k < k1; ++k) {
+    const int64_t j = REVERSE ? nch - 1 - k : k;
+    const Frag L = load<REVERSE>(a.aggP + (base + j) * DD, r, c);
+    const Frag cf = load<!TWO>(a.aggC + (base + j) * DD, r, c);
+    m = link<TWO>(L, m, cf);
+    T = nt(T, L, zero());
+  }
+  store<true>(gG + (size_t)w * DD, T, r, c);
+  store<!TWO>(gC + (size_t)w * DD, m, r, c);
+  __syncthreads();
+  for (int d = 1; d < nw; d <<= 1) {
+    const bool act = w >= d;
+    Frag mn, Tn;
+    if (act) {
+      const Frag L = load<false>(gG + (size_t)w * DD, r, c);
+      const Frag Tp = load<true>(gG + (size_t)(w - d) * DD, r, c);
+      const Frag mp = load<!TWO>(gC + (size_t)(w - d) * DD, r, c);
+      const Frag cw = load<!TWO>(gC + (size_t)w * DD, r, c);
+      mn = link<TWO>(L, mp, cw);
+      Tn = nt(Tp, L, zero());
+    }
+    __syncthreads();
+    if (act) {
+      store<true>(gG + (size_t)w * DD, Tn, r, c);
+      store<!TWO>(gC + (size_t)w * DD, mn, r, c);
+    }
+    __syncthreads();
+  }
+  if (w == nw - 1) {
+    store<!TWO>(a.c_out + s * DD, load<!TWO>(gC + (size_t)w * DD, r, c), r, c);
+    if (!REVERSE && a.P_out) store<false>(a.P_out + s * DD, load<false>(gG + (size_t)w * DD, r, c), r, c);
+  }
+}
+
+template <bool TWO, bool REVERSE>
+inline void launch_compose8_mma(const ScanArgs& a, cudaStream_t st) {
+  int64_t w = (a.nchunks + CARRY8_LINKS_PER_WARP - 1) / CARRY8_LINKS_PER_WARP;
+  w = w < 1 ? 1 : w > CARRY8_MAX_WARPS ? CARRY8_MAX_WARPS : w;
+  const size_t smem = (size_t)2 * w * 64 * sizeof(double);
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(compose8_mma_kernel<TWO, REVERSE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+  compose8_mma_kernel<TWO, REVERSE><<<(unsigned)(a.B * a.N), 32 * (unsigned)w, smem, st>>>(a);
+}
+
 template <bool TWO, bool REVERSE>
 inline void launch_carry8_mma(const ScanArgs& a, cudaStream_t st) {
   const int64_t nl = a.nchunks - 1;

@@ -927,7 +927,7 @@ int run8(const ScanArgs& a, bool bwd, cudaStream_t st) {
         fwd8_kernel<true, DAMPED, TWO><<<nblk(total), THREADS, fwd_bytes, st>>>(a);
       }
       KernelTimer kt("agg_compose", st);
-      compose_kernel<8, TWO, false><<<(unsigned)((S + 3) / 4), 128, 0, st>>>(a);
+      launch_compose8_mma<TWO, false>(a, st);
     } else {
       {
         KernelTimer kt("agg_bwd_reduce", st);
@@ -935,7 +935,7 @@ int run8(const ScanArgs& a, bool bwd, cudaStream_t st) {
         bwd8_reduce_kernel<DAMPED, TWO><<<nblk(total), THREADS, red_bytes, st>>>(a);
       }
       KernelTimer kt("agg_compose", st);
-      compose_kernel<8, TWO, true><<<(unsigned)((S + 3) / 4), 128, 0, st>>>(a);
+      launch_compose8_mma<TWO, true>(a, st);
     }
     return check_launch("shard aggregate (D=8)");
   }

@@ -927,6 +927,163 @@ def run_generation(args, ws, rank, local, cores):
     return 0
 
 
+# The reference's one published scan figure: its fused CUDA one-sided D = 4 scan, forward +
+# backward, 5.34 ms per step in csn_toolkit/examples/benchmark_cuda_kernels.py:79-118
+# (csn_toolkit/README.md:194, :331; hardware unspecified).
+D4_PUBLISHED_MS = 5.34
+
+# The same harness through the reference toolkit's own PyTorch path (its "sequential loop"
+# arm, csn_toolkit/examples/benchmark_cuda_kernels.py:96-109), run from baseline/_ref.
+_REF_D4_SCRIPT = r"""
+import json, sys, time
+sys.path.insert(0, sys.argv[1])
+import torch
+from csn.scan import parallel_rotor_scan
+dev = torch.device(sys.argv[3])
+torch.set_num_threads(int(sys.argv[4]))
+torch.manual_seed(42)
+B, T, N, D = 2, 80, 1, 4
+M = (0.5 * torch.randn(B, T, N, D, D, device=dev)).contiguous().detach().requires_grad_(True)
+C = torch.randn(B, T, N, D, D, device=dev).contiguous().detach().requires_grad_(True)
+def one():
+    M.grad = None
+    C.grad = None
+    loss = (parallel_rotor_scan(M, C, backend="pytorch") ** 2).sum()
+    loss.backward()
+def sync():
+    if dev.type == "cuda":
+        torch.cuda.synchronize(dev)
+for _ in range(10):
+    one()
+sync()
+n = int(sys.argv[2])
+t = time.perf_counter()
+for _ in range(n):
+    one()
+sync()
+print(json.dumps({"ms": (time.perf_counter() - t) / n * 1e3}))
+"""
+
+
+def reference_d4_ms(runs, device, cores, timeout=900):
+    """Per-step ms of the reference harness's PyTorch arm (baseline/_ref) on `device`."""
+    import subprocess
+    ref = REPO / "baseline" / "_ref"
+    if not (ref / "csn").is_dir():
+        return {"unavailable": "the reference toolkit is not installed in baseline/_ref"}
+    try:
+        r = subprocess.run([sys.executable, "-c", _REF_D4_SCRIPT, str(ref), str(runs), device, str(cores)],
+                           capture_output=True, text=True, timeout=timeout, env=dict(os.environ, PYTHONPATH=str(ref)))
+        return json.loads(r.stdout.strip().splitlines()[-1])
+    except Exception as e:  # noqa: BLE001 -- a baseline that cannot run must not fail the bench
+        return {"unavailable": f"reference harness failed: {type(e).__name__}"}
+
+
+def run_d4_harness(args, ws, rank, local, cores):
+    """The reference's published scan benchmark (csn_toolkit/examples/benchmark_cuda_kernels.py:
+    30-118) through this build's drop-in `csn.scan.parallel_rotor_scan(..., backend="cuda")`:
+    M, C [B2, T80, N1, 4, 4] (M ~ 0.5 N(0, 1), seed 42), one step = forward, loss = sum(X^2),
+    backward; 10 warm-up steps, then the wall-clock mean over the timed steps, as the harness
+    times it (it is launch-bound at this size).  vs_baseline = value / the published 5.34 ms."""
+    metric = "fused D=4 one-sided scan fwd+bwd ms/step, reference harness B2 T80 N1"
+    config = {"workload": "d4_harness", "batch": 2, "seq_len": 80, "channels": 1, "matrix_dim": 4,
+              "sided": "one", "harness": "csn_toolkit/examples/benchmark_cuda_kernels.py:30-118",
+              "l2": "inputs far below L2 (the harness's own shape; latency-bound)"}
+    runs = max(100, args.steps)
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        cores = _cpu_threads(cores)
+        r = reference_d4_ms(max(3, args.steps), "cpu", cores)
+        if "ms" not in r:
+            print(json.dumps({"impl": "reference", "unavailable": r.get("unavailable", "failed")}), flush=True)
+            return 0
+        v = r["ms"]
+        print(json.dumps({"metric": metric, "value": v, "unit": "ms", "n_gpus": 1, "steps": max(3, args.steps),
+                          "warmup": 10, "ms_per_step": v, "higher_is_better": False, "scaling": "weak",
+                          "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
+                          "impl": "reference",
+                          "cpu_baseline": {"value": v, "unit": "ms", "cores": cores, "kind": "reference",
+                                           "sample": "the harness's PyTorch arm (parallel_rotor_scan, "
+                                                     "backend='pytorch') on the host cores"},
+                          "e2e": {"value": v, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+              flush=True)
+        return 0
+    if rank != 0:
+        return 0
+    import torch
+    from csn_b200 import _lib
+    from csn.scan import parallel_rotor_scan
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    _lib.load()
+    torch.manual_seed(42)
+    B, T, N, D = 2, 80, 1, 4
+    M = (0.5 * torch.randn(B, T, N, D, D, device=dev)).contiguous().detach().requires_grad_(True)
+    C = torch.randn(B, T, N, D, D, device=dev).contiguous().detach().requires_grad_(True)
+
+    def one(m, c):
+        m.grad = None
+        c.grad = None
+        loss = (parallel_rotor_scan(m, c, backend="cuda") ** 2).sum()
+        loss.backward()
+        return loss
+
+    for _ in range(max(10, args.warmup)):
+        one(M, C)
+    torch.cuda.synchronize()
+    _lib.timing_reset()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        _lib.timing_enable(True)
+        t0 = time.perf_counter()
+        e0.record()
+        for _ in range(runs):
+            one(M, C)
+        e1.record()
+        torch.cuda.synchronize()
+        wall_ms = (time.perf_counter() - t0) / runs * 1e3
+        _lib.timing_enable(False)
+    dev_ms = e0.elapsed_time(e1) / runs
+    names = ("fwd_reduce", "fwd_carry", "fwd_apply", "bwd_reduce", "bwd_carry", "bwd_apply")
+    kt = {n: _lib.timing_read(n) for n in names}
+    launches = sum(c for _, c in kt.values())
+    _lib.timing_reset()
+    # end to end: M, C from pinned host memory every step, the loss back to the host
+    Mh, Ch = M.detach().cpu().pin_memory(), C.detach().cpu().pin_memory()
+    e2e = []
+    for _ in range(max(20, args.e2e_steps)):
+        t0 = time.perf_counter()
+        m = Mh.to(dev, non_blocking=True).requires_grad_(True)
+        c = Ch.to(dev, non_blocking=True).requires_grad_(True)
+        float(one(m, c))
+        torch.cuda.synchronize()
+        e2e.append((time.perf_counter() - t0) * 1e3)
+    ref_gpu = reference_d4_ms(runs, f"cuda:{local}", 1)
+    cpu = None
+    if not args.no_cpu_baseline:
+        ccores = _cpu_threads(cores)
+        r = reference_d4_ms(10, "cpu", ccores)
+        if "ms" in r:
+            cpu = {"value": r["ms"], "unit": "ms", "cores": ccores, "kind": "reference",
+                   "sample": "the harness's PyTorch arm (parallel_rotor_scan, backend='pytorch') on the "
+                             "host cores, 10 steps after 10 warm-up steps"}
+    print(json.dumps({
+        "metric": metric, "value": wall_ms, "unit": "ms", "n_gpus": 1, "steps": runs,
+        "warmup": max(10, args.warmup), "ms_per_step": wall_ms, "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": wall_ms / D4_PUBLISHED_MS, "dtype": "f32", "data": "synthetic",
+        "config": config, "device_ms_per_step": dev_ms,
+        "kernel_ms_per_step": {n: t / runs for n, (t, c) in kt.items()},
+        "published_ms": D4_PUBLISHED_MS, "reference_pytorch_gpu": ref_gpu,
+        "gpu_launches": launches, "clocks": clk.summary(),
+        "e2e": {"value": float(np.median(e2e)), "unit": "ms", "h2d_bytes_per_step": 2 * M.numel() * 4,
+                "d2h_bytes_per_step": 4,
+                "timing": "wall clock per step: M and C from pinned host memory, forward, loss, backward, "
+                          "loss to the host"},
+        "cpu_baseline": cpu}), flush=True)
+    return 0
+
+
 def run_lm_train(args, ws, rank, local, cores):
     """One training step of the Cl(6,0) LM of the Cl(6) LM config (vocab 65 uniform token ids,
     d_model 128, 4 CliffordCL6Blocks x 8 neurons, B32 L2048, AdamW lr 1e-3): embedding, blocks
@@ -1333,7 +1490,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default=None, choices=sorted(WORKLOADS) + ["gen", "sp", "lm_train", "spatial"],
+    ap.add_argument("--workload", default=None,
+                    choices=sorted(WORKLOADS) + ["gen", "sp", "lm_train", "spatial", "d4_harness"],
                     help="default: sp when launched by torch.distributed.run (any world size), else cl6_lm")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -1354,6 +1512,8 @@ def main():
         return run_lm_train(args, ws, rank, local, cores)
     if args.workload == "spatial":
         return run_spatial(args, ws, rank, local, cores)
+    if args.workload == "d4_harness":
+        return run_d4_harness(args, ws, rank, local, cores)
     kw = {}
     if args.batch is not None:
         kw["batch"] = args.batch

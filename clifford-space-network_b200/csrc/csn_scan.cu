@@ -332,6 +332,10 @@ int64_t pick_chunk(int64_t S, int64_t T, int D) {
   if (D == 16) return T > 0 ? pick_chunk16(S, T) : 1;
   // Enough (sequence, chunk) work items to fill 148 SMs at the residency each family
   // allows: D = 4 ~1024 threads / SM, D = 8 ~256 threads / SM (register bound, one wave).
+  // A problem of at most 1024 elements cannot fill the GPU either way and is bound by its
+  // launches: one chunk per sequence runs the apply pass alone, without the reduce and
+  // carry passes (the reference's D = 4 benchmark, B2 T80: 0.37 -> 0.23 ms per fwd + bwd step).
+  if (S * T <= 1024) return T > 0 ? T : 1;
   const int64_t target = (D == 8) ? 148 * 256 : 148 * 1024;
   int64_t chunk = (S * T + target - 1) / target;
   if (chunk < 8) chunk = 8;

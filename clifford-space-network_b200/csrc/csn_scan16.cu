@@ -21,10 +21,11 @@
 //    the Cl(8,0) benchmark shape.  These products therefore run on the FP64 tensor
 //    cores (mma.m8n8k4.f64 on f64 copies of the same fragments, "F16D"): exact fp32
 //    inputs, fp64 accumulation, one round-to-nearest when a value goes back to fp32;
-//  * the per-step adjoint products (dM, dOmega) and the transposes do not feed the
-//    recurrence and run as 3xTF32: each fp32 operand is split into a TF32 head and a
-//    TF32 tail and hi*hi + hi*lo + lo*hi is accumulated in fp32 (fp32-level error, no
-//    accumulation over time).  Transposes are products with the identity (exact).
+//  * the per-step adjoint products (dM, dOmega) do not feed the recurrence and run as
+//    3xTF32: each fp32 operand is split into a TF32 head and a TF32 tail and
+//    hi*hi + hi*lo + lo*hi is accumulated in fp32 (fp32-level error, no accumulation over
+//    time).  Transposes are data movement (two shuffle rounds per 8 x 8 tile), not
+//    products: exact, and off the tensor pipes.
 // The Cayley rotor is built from E = (I - Omega)^{-1} - I: a matrix series of small
 // products when |h Omega|_F <= 0.05, else a Gauss-Jordan elimination on the fragment in
 // deviation form (round-to-nearest FMAs), whose pivot rows and columns reach the lanes that
@@ -98,25 +99,28 @@ __device__ __forceinline__ void nt(F16& z, const F16S& A, const F16S& B) {
   }
 }
 
-// z = X^T, as the product I X^T (the identity is exact in TF32: head and tail of X only).
-__device__ __forceinline__ void transpose(F16& z, const F16S& X, int lane) {
+// z = X^T by data movement.  Tile (I, J) of z is tile (J, I) of X transposed; an 8 x 8
+// tile, of which lane (g, t) holds row g at columns 2t and 2t + 1, turns in two shuffle
+// rounds: lanes g and g ^ 1 swap one entry each so that lane (g, t) holds column
+// 2t + (g & 1) at rows g & ~1 and (g & ~1) + 1, and the lane that needs column g' at rows
+// 2t', 2t' + 1 reads both from lane 4 (2t' + (g' & 1)) + g' / 2.
+template <typename V>
+__device__ __forceinline__ void transpose_tiles(V (&z)[2][4], const V (&x)[2][4], int lane) {
   const int g = lane >> 2, t = lane & 3;
-  constexpr uint32_t ONE = 0x3f800000u;
+  const bool odd = g & 1;
+  const int src = 4 * (2 * t + (g & 1)) + (g >> 1);
 #pragma unroll
-  for (int nz = 0; nz < 2; ++nz) {
-    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  for (int I = 0; I < 2; ++I)
 #pragma unroll
-    for (int ks = 0; ks < 2; ++ks) {
-      const int c = 8 * ks + 2 * t;  // k columns of slots t and t + 4: c and c + 1
-      const uint32_t a0 = (g == c) ? ONE : 0u, a1 = (g + 8 == c) ? ONE : 0u;
-      const uint32_t a2 = (g == c + 1) ? ONE : 0u, a3 = (g + 8 == c + 1) ? ONE : 0u;
-      mma_tf32(d, a0, a1, a2, a3, X.hi[ks][2 * nz], X.hi[ks][2 * nz + 1]);
-      mma_tf32(d, a0, a1, a2, a3, X.lo[ks][2 * nz], X.lo[ks][2 * nz + 1]);
+    for (int J = 0; J < 2; ++J) {
+      const V a0 = x[I][2 * J], a1 = x[I][2 * J + 1];  // tile (J, I) of X
+      const V r = __shfl_xor_sync(FULL, odd ? a0 : a1, 4);
+      const V b0 = odd ? r : a0, b1 = odd ? a1 : r;
+      z[J][2 * I] = __shfl_sync(FULL, b0, src);
+      z[J][2 * I + 1] = __shfl_sync(FULL, b1, src);
     }
-#pragma unroll
-    for (int e = 0; e < 4; ++e) z.v[nz][e] = d[e];
-  }
 }
+__device__ __forceinline__ void transpose(F16& z, const F16& x, int lane) { transpose_tiles(z.v, x.v, lane); }
 
 __device__ __forceinline__ void f_zero(F16& x) {
 #pragma unroll
@@ -272,8 +276,11 @@ __device__ __forceinline__ void d_axpy(F16D& y, float a, const F16& x) {
 #pragma unroll
     for (int e = 0; e < 4; ++e) y.v[nt][e] = fma((double)a, (double)x.v[nt][e], y.v[nt][e]);
 }
-// X^T as the product I X^T (exact)
-__device__ __forceinline__ F16D transpose64(const F16D& X, int lane) { return nt64(d_identity(lane), X); }
+__device__ __forceinline__ F16D transpose64(const F16D& X, int lane) {
+  F16D z;
+  transpose_tiles(z.v, X.v, lane);
+  return z;
+}
 
 // In-place Gauss-Jordan inverse of the fragment in deviation form (as gj_inverse_dev in
 // csn_common.cuh): on entry E = A - I for A = I - Omega (no pivoting: Omega skew, pivots
@@ -664,9 +671,7 @@ __global__ void __launch_bounds__(128, 4) bwd16_reduce_kernel(ScanArgs a) {
       if (SRC == SRC_MC) {
         f_load_t(Mt, a.M + e * DD, lane);
       } else {
-        F16S Ms;
-        split(Ms, M);
-        transpose(Mt, Ms, lane);
+        transpose(Mt, M, lane);
       }
     }
     const F16D Mtd = to_d(Mt);
@@ -737,7 +742,7 @@ __global__ void __launch_bounds__(128, 3) bwd16_apply_kernel(ScanArgs a) {
     F16S Ms, Mts;
     split(Ms, M);
     F16 Mt;
-    transpose(Mt, Ms, lane);  // (reading M^T from memory measured 0.6 % slower here)
+    transpose(Mt, M, lane);
     split(Mts, Mt);
     // G = H + dX in fp64; the carry to the previous step, M^T G M (one-sided M^T G), is
     // formed from it right away, and the step's gradients use G rounded to fp32
@@ -760,7 +765,7 @@ __global__ void __launch_bounds__(128, 3) bwd16_apply_kernel(ScanArgs a) {
     // ---- dM
     F16 dM;
     F16 Gt;  // G^T (two-sided dM, one-sided carry)
-    transpose(Gt, Gs, lane);
+    transpose(Gt, G, lane);
     F16S Gts;
     split(Gts, Gt);
     if (xprev) {

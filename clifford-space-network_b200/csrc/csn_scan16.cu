@@ -358,10 +358,14 @@ __device__ __forceinline__ void make_terms(uint32_t (&terms)[2][4], const BlockT
         if (r < c) packed = (packed & ~0xffu) | (uint32_t)triu_index(r, c);
         else if (r > c) packed = (packed & ~0xffu) | (uint32_t)triu_index(c, r) | 0x80u;
       } else {
+        // GA: byte offsets into the signed staging gs[0, 2K] = (g, 0, -g), so a term is one
+        // load and one add; 4 (2K) < 256 for K = 28
+        static_assert(4 * (2 * K) < 256, "GA term offsets must fit a byte");
+        packed = (uint32_t)(4 * K) * 0x010101u;
         int m = 0;
         for (int k = 0; k < K; ++k) {
           if (tab.col[k][r] == c && m < 3) {
-            const uint32_t byte = (uint32_t)k | (tab.sgn[k][r] < 0 ? 0x80u : 0u);
+            const uint32_t byte = 4u * (uint32_t)(tab.sgn[k][r] < 0 ? K + 1 + k : k);
             packed = (packed & ~(0xffu << (8 * m))) | (byte << (8 * m));
             ++m;
           }
@@ -371,19 +375,24 @@ __device__ __forceinline__ void make_terms(uint32_t (&terms)[2][4], const BlockT
     }
 }
 
-// Om = h Omega from the generators in shared memory (gs[K] == 0).
-template <int NTERM>
+// Om = h Omega from the generators in shared memory (gs[K] == 0; for the GA basis also
+// gs[K + 1 + k] = -g_k, and the terms are byte offsets).
+template <int BASIS>
 __device__ __forceinline__ void build_Om(F16& Om, const float* gs, const uint32_t (&terms)[2][4], float h) {
 #pragma unroll
   for (int n2 = 0; n2 < 2; ++n2)
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       float om = 0.0f;
-#pragma unroll
-      for (int m = 0; m < NTERM; ++m) {
-        const uint32_t byte = (terms[n2][e] >> (8 * m)) & 0xffu;
+      if constexpr (BASIS == BASIS_TRIU) {
+        const uint32_t byte = terms[n2][e] & 0xffu;
         const float v = gs[byte & 0x7fu];
-        om += (byte & 0x80u) ? -v : v;
+        om = (byte & 0x80u) ? -v : v;
+      } else {
+        const char* gb = reinterpret_cast<const char*>(gs);
+#pragma unroll
+        for (int m = 0; m < NTerms<BASIS>::value; ++m)
+          om += *reinterpret_cast<const float*>(gb + ((terms[n2][e] >> (8 * m)) & 0xffu));
       }
       Om.v[n2][e] = h * om;
     }
@@ -465,7 +474,7 @@ __device__ __forceinline__ void load_tab(BlockTab& tab) {
 struct Warp {
   int lane;
   int64_t b, n, j, s, t0, t1;
-  float* gs;  // K + 1 floats of this warp (gs[K] = 0)
+  float* gs;  // K + 1 floats of this warp (gs[K] = 0), 2K + 1 for the GA basis (then -g)
   float* zs;  // 16 x ZST dOmega scratch (backward apply)
 };
 
@@ -504,13 +513,17 @@ __device__ __forceinline__ void fetch_gens(float (&gr)[(K + 31) / 32], const flo
     gr[m] = (k < K) ? __ldg(gens + e * K + k) : 0.0f;
   }
 }
-template <int K>
+// NEG: also -g at gs[K + 1 + k], for the GA-basis Omega of a pass that builds rotors.
+template <int K, bool NEG>
 __device__ __forceinline__ void stage_gens(float* gs, const float (&gr)[(K + 31) / 32], int lane) {
   __syncwarp();  // previous step's readers are done
 #pragma unroll
   for (int m = 0; m < (K + 31) / 32; ++m) {
     const int k = lane + 32 * m;
-    if (k < K) gs[k] = gr[m];
+    if (k < K) {
+      gs[k] = gr[m];
+      if constexpr (NEG) gs[K + 1 + k] = -gr[m];
+    }
   }
   __syncwarp();
 }
@@ -554,7 +567,7 @@ __device__ __forceinline__ void step_matrix(const ScanArgs& a, const Warp& w, co
     if constexpr (CIN) {
       f_load(M, a.Mc_in + e * DD, w.lane);  // cached rotor of this step
     } else {
-      build_Om<NTerms<BASIS>::value>(M, w.gs, terms, 0.5f * dtv);
+      build_Om<BASIS>(M, w.gs, terms, 0.5f * dtv);
       cayley(M, sa, w.lane);
       if (a.Mc_out) f_store<false>(a.Mc_out + e * DD, M, w.lane);
     }
@@ -612,7 +625,7 @@ __global__ void __launch_bounds__(128) fwd16_kernel(ScanArgs a) {
     } else {
       f_load(Cin, (SRC == SRC_MC ? a.C : a.S) + e * DD, lane);
       if constexpr (SRC == SRC_ROTOR) {
-        stage_gens<K>(w.gs, gr, lane);
+        stage_gens<K, BASIS == BASIS_GA && !CIN>(w.gs, gr, lane);
         if (t + 1 < w.t1) fetch_gens<K>(gr, a.gens, elem(a, w.b, t + 1, w.n), lane);
       }
       step_matrix<SRC, BASIS, DAMPED, K, CIN>(a, w, terms, e, t, M, alpha, sa, dtv, gam);
@@ -677,7 +690,7 @@ __global__ void __launch_bounds__(128, 4) bwd16_reduce_kernel(ScanArgs a) {
     } else {
       f_load(dX, a.dX + e * DD, lane);
       if constexpr (SRC == SRC_ROTOR) {
-        stage_gens<K>(w.gs, gr, lane);
+        stage_gens<K, BASIS == BASIS_GA && !CIN>(w.gs, gr, lane);
         if (t - 1 >= w.t0) fetch_gens<K>(gr, a.gens, elem(a, w.b, t - 1, w.n), lane);
       }
       F16 M;
@@ -749,7 +762,7 @@ __global__ void __launch_bounds__(128, 3) bwd16_apply_kernel(ScanArgs a) {
     if (xprev) f_load(Xp, xprev, lane);
     if (SRC == SRC_ROTOR && DAMPED) f_load(Sx, a.S + e * DD, lane);
     if constexpr (SRC == SRC_ROTOR) {
-      stage_gens<K>(w.gs, gr, lane);
+      stage_gens<K, BASIS == BASIS_GA && !CIN>(w.gs, gr, lane);
       if (t - 1 >= w.t0) fetch_gens<K>(gr, a.gens, elem(a, w.b, t - 1, w.n), lane);
     }
     F16 M;

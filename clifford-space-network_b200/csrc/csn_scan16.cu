@@ -578,7 +578,7 @@ __device__ __forceinline__ void step_matrix(const ScanArgs& a, const Warp& w, co
 // REDUCE: chunk aggregate (P = M_last ... M_first, c = chunk scanned from zero);
 // otherwise the apply pass from the chunk's carry.
 template <bool REDUCE, int SRC, int BASIS, bool DAMPED, bool TWO, bool CIN>
-__global__ void __launch_bounds__(128) fwd16_kernel(ScanArgs a) {
+__global__ void __launch_bounds__(128, 3) fwd16_kernel(ScanArgs a) {
   constexpr int K = GenCount<16, BASIS>::K;
   constexpr int KR = (K + 31) / 32;
   S16_PROLOGUE(BASIS, K);

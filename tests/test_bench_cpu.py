@@ -1,0 +1,50 @@
+"""bench.py's reference arm on the CPU: the JSON line it prints and its rank handling.
+
+The arm times the float64 CPU oracle on the host cores (no GPU), so its contract -- one line
+with the metric, the workload's config, `impl`, `cpu_baseline` and a copy-free `e2e` -- can
+be checked here; under torchrun only rank 0 works and prints.
+"""
+import json
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parents[1]
+
+
+def _run(args, env_extra=None, timeout=600):
+    env = dict(os.environ, PYTHONDONTWRITEBYTECODE="1")
+    for k in ("RANK", "WORLD_SIZE", "LOCAL_RANK", "TORCHELASTIC_RUN_ID", "LOCAL_WORLD_SIZE", "GROUP_RANK"):
+        env.pop(k, None)
+    env.update(env_extra or {})
+    return subprocess.run([sys.executable, str(REPO / "bench.py"), *args], cwd=REPO, env=env,
+                          capture_output=True, text=True, timeout=timeout)
+
+
+def test_reference_arm_prints_one_contract_line():
+    r = _run(["--impl", "reference", "--steps", "1", "--warmup", "0"])
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.strip()]
+    assert len(lines) == 1, r.stdout
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference"
+    assert d["metric"] == "rotor-scan fwd+bwd Gelem/s (B*L*C)" and d["unit"] == "Gelem/s"
+    assert d["higher_is_better"] is True and d["n_gpus"] == 1 and d["steps"] == 1
+    assert d["value"] > 0 and d["ms_per_step"] > 0
+    assert d["config"]["workload"] == "cl6_lm_scan_fwd_bwd"
+    assert (d["config"]["batch"], d["config"]["seq_len"], d["config"]["channels"]) == (32, 2048, 8)
+    cb = d["cpu_baseline"]
+    assert cb["value"] == d["value"] and cb["unit"] == d["unit"]
+    assert cb["kind"] in ("port", "reference") and cb["cores"] >= 1 and cb["sample"]
+    e2e = d["e2e"]
+    assert e2e["value"] == d["value"] and e2e["unit"] == d["unit"]
+    assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
+
+
+def test_reference_arm_other_ranks_exit_quietly():
+    r = _run(["--impl", "reference", "--gpus", "2", "--steps", "1", "--warmup", "0"],
+             {"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1", "LOCAL_WORLD_SIZE": "2",
+              "TORCHELASTIC_RUN_ID": "cpu-test"})
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert r.stdout.strip() == ""

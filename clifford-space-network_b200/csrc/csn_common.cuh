@@ -125,28 +125,6 @@ __device__ __forceinline__ float f2sum(uint64_t v) {
   const float2 p = f2unpack(v);
   return p.x + p.y;
 }
-// sum_k a[k] b[k] over 8 entries: the even and the odd partial sums in one packed
-// accumulator, added at the end
-__device__ __forceinline__ float dot8(const float (&a)[8], const float (&b)[8]) {
-  uint64_t acc = f2mul(f2pack(a[0], a[1]), f2pack(b[0], b[1]));
-  acc = f2fma(f2pack(a[2], a[3]), f2pack(b[2], b[3]), acc);
-  acc = f2fma(f2pack(a[4], a[5]), f2pack(b[4], b[5]), acc);
-  acc = f2fma(f2pack(a[6], a[7]), f2pack(b[6], b[7]), acc);
-  const float2 p = f2unpack(acc);
-  return p.x + p.y;
-}
-
-// X <- X M^T for D = 8 with packed dot products (rows of X against rows of M)
-__device__ __forceinline__ void rmulT_dot8(Mat<8>& X, const Mat<8>& M) {
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    float row[8];
-#pragma unroll
-    for (int l = 0; l < 8; ++l) row[l] = dot8(X.a[i], M.a[l]);
-#pragma unroll
-    for (int l = 0; l < 8; ++l) X.a[i][l] = row[l];
-  }
-}
 
 // X <- X M
 template <int D>
